@@ -1,0 +1,426 @@
+"""bench.py - decode throughput of one DeepSeek-V4-Flash MoE layer (BASELINE
+config 2) on B200, through libdsv4_cuda.so.
+
+A step is one decode token (M=1 by default) through one MoE layer: router
+(BF16 gate [256x7168], sqrt-softplus, top-8), 8 routed FP4 experts
+(gate/up 7168->2048, down 2048->7168, E8M0 per-32 scales) and the FP8 shared
+expert, ordered combine. Weights are random-init with the config's
+distributions and resident in HBM; successive steps cycle through --layers
+independent layer weight sets and a pool of tokens, so a step never finds
+the previous step's weights in L2 (126 MB) - each layer's step reads
+~235 MB.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+--impl reference times the reference engine's own CPU implementation of the
+same step (oracle/_ref, built from the reference sources; the C restatement
+when that library is absent) on the host cores. Under torchrun (N>1) the
+MoE layer is expert-parallel: each rank owns E/N routed experts, the router
+and shared expert are replicated, and one NCCL all-reduce of the zero-padded
+[M][topk][H] expert outputs precedes the ordered combine.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+PKG = os.path.join(ROOT, "deepseek-v4-flash-0731-in-c_b200")
+sys.path.insert(0, PKG)
+sys.path.insert(0, os.path.join(ROOT, "oracle"))
+
+H, I, E, TOPK = 7168, 2048, 256, 8
+ROUTE_SCALE, LIMIT = 1.5, 10
+EXPERT_BYTES = 2 * (I * H // 2 + I * H // 32) + (H * I // 2 + H * I // 32)  # 23,396,352
+SHARED_FP8_BYTES = 2 * (I * H + (I // 128) * (H // 128)) + (H * I + (H // 128) * (I // 128))
+ROUTER_BYTES = E * H * 2
+METRIC = "decode tok/s through one MoE layer (config 2: H7168, I2048, 256+1 experts, top-8)"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--tokens", type=int, default=1, help="tokens per step (M)")
+    ap.add_argument("--layers", type=int, default=4, help="independent layer weight sets")
+    ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    return ap.parse_args()
+
+
+# ---------------------------------------------------------------- weights --
+def make_device_layer(torch, seed, dev):
+    """Random-init config-2 layer in the reference layouts, on the GPU."""
+    g = torch.Generator(device=dev)
+    g.manual_seed(seed)
+
+    def u8(*shape):
+        return torch.randint(0, 256, shape, dtype=torch.uint8, device=dev, generator=g)
+
+    def e8m0(*shape):
+        # lognormal(0, 0.5) scale rounded to a power of two: 127 + round(log2 s)
+        z = torch.randn(shape, device=dev, generator=g) * (0.5 / np.log(2.0))
+        return (127 + torch.round(z)).clamp(0, 254).to(torch.uint8)
+
+    def fp8(*shape):
+        c = torch.randint(0, 254, shape, dtype=torch.int32, device=dev, generator=g)
+        c = torch.where((c & 0x7F) == 0x7F, c - 1, c)
+        return c.to(torch.uint8)
+
+    gate = (torch.randn(E, H, device=dev, generator=g) * 0.02).to(torch.bfloat16).view(torch.uint16)
+    return dict(hidden=H, moe_inter=I, n_experts=E, topk=TOPK, route_scale=ROUTE_SCALE,
+                swiglu_limit=LIMIT, gate_w=gate, bias=None, tid2eid=None,
+                w1=u8(E, I, H // 2), s1=e8m0(E, I, H // 32),
+                w3=u8(E, I, H // 2), s3=e8m0(E, I, H // 32),
+                w2=u8(E, H, I // 2), s2=e8m0(E, H, I // 32),
+                shared=dict(fp8=True, w1=fp8(I, H), s1=e8m0(I // 128, H // 128),
+                            w3=fp8(I, H), s3=e8m0(I // 128, H // 128),
+                            w2=fp8(H, I), s2=e8m0(H // 128, I // 128)))
+
+
+def bf16_tokens(rng, n, m):
+    x = rng.normal(size=(n, m, H)).astype(np.float32)
+    u = x.view(np.uint32).astype(np.uint64)
+    return (((u + 0x7FFF + ((u >> 16) & 1)) >> 16) << 16).astype(np.uint32).view(np.float32)
+
+
+# ------------------------------------------------------------- clocks ----
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except OSError:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if not self.proc:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            p = [v.strip() for v in ln.split(",")]
+            if len(p) < 9:
+                continue
+            try:
+                sm.append(float(p[1]))
+                mx = float(p[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, p[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ------------------------------------------------------------ CPU side ----
+def host_layer_for_reference(rng):
+    """Config-2 layer in host memory, routed experts already in the
+    reference's cache-slot layout (scale run then weight run per expert)."""
+    s13, s2 = I * (H // 32), H * (I // 32)
+    w13, w2 = I * (H // 2), H * (I // 2)
+
+    def e8m0(n):
+        return (127 + np.round(rng.normal(0, 0.5 / np.log(2.0), size=n))).clip(0, 254).astype(np.uint8)
+
+    def fp8(shape):
+        c = rng.integers(0, 254, size=shape, dtype=np.int32)
+        return np.where((c & 0x7F) == 0x7F, c - 1, c).astype(np.uint8)
+
+    gate = (rng.normal(0, 0.02, size=(E, H)).astype(np.float32))
+    u = gate.view(np.uint32).astype(np.uint64)
+    gate = ((u + 0x7FFF + ((u >> 16) & 1)) >> 16).astype(np.uint16)
+    scales = e8m0(E * (2 * s13 + s2)).reshape(E, -1)
+    weights = rng.integers(0, 256, size=(E, 2 * w13 + w2), dtype=np.uint8)
+    shared = dict(fp8=True, w1=fp8((I, H)), s1=e8m0((I // 128) * (H // 128)).reshape(I // 128, -1),
+                  w3=fp8((I, H)), s3=e8m0((I // 128) * (H // 128)).reshape(I // 128, -1),
+                  w2=fp8((H, I)), s2=e8m0((H // 128) * (I // 128)).reshape(H // 128, -1))
+    return dict(hidden=H, moe_inter=I, n_experts=E, topk=TOPK, route_scale=ROUTE_SCALE,
+                swiglu_limit=LIMIT, gate_w=gate, bias=None, tid2eid=None, shared=shared), \
+        (scales, weights)
+
+
+def cpu_reference_run(seconds, steps_cap=None, warmup=1):
+    """Times the reference's own MoE-layer step on the host cores. Returns
+    (tok/s, cores, kind, sample description)."""
+    from oracle import REF_SO
+    ncpu = os.cpu_count() or 1
+    rng = np.random.default_rng(99)
+    layer, slots = host_layer_for_reference(rng)
+    toks = bf16_tokens(rng, 64, 1)[:, 0]
+    if os.path.exists(REF_SO):
+        from oracle import Ref
+        r = Ref()
+        kind = "reference"
+        cores = r.lib.ref_omp_max_threads()
+        run = lambda x: r.moe_forward(layer, x, slots=slots)  # noqa: E731
+    else:
+        from oracle import Oracle
+        o = Oracle()
+        kind = "port"
+        cores = 1
+        s13, w13 = I * (H // 32), I * (H // 2)
+        lay = dict(layer)
+        sc, wt = slots
+        lay["w1"], lay["w2"], lay["w3"] = (wt[:, :w13].reshape(E, I, H // 2),
+                                           wt[:, w13:w13 + H * I // 2].reshape(E, H, I // 2),
+                                           wt[:, w13 + H * I // 2:].reshape(E, I, H // 2))
+        lay["s1"], lay["s2"], lay["s3"] = (sc[:, :s13].reshape(E, I, H // 32),
+                                           sc[:, s13:s13 + H * I // 32].reshape(E, H, I // 32),
+                                           sc[:, s13 + H * I // 32:].reshape(E, I, H // 32))
+        lay = {k: (np.ascontiguousarray(v) if isinstance(v, np.ndarray) else v) for k, v in lay.items()}
+        run = lambda x: o.moe_forward(lay, x)  # noqa: E731
+    for i in range(warmup):
+        run(toks[i % len(toks)])
+    n, t0 = 0, time.perf_counter()
+    while True:
+        run(toks[n % len(toks)])
+        n += 1
+        el = time.perf_counter() - t0
+        if el >= seconds or (steps_cap and n >= steps_cap):
+            break
+    return n / el, cores, kind, f"{n} decode steps (M=1) through one config-2 MoE layer, " \
+        f"256 experts resident in host RAM, {el:.1f} s on {cores} thread(s) of {ncpu} cores"
+
+
+def run_reference_arm(args, rank, world):
+    if rank != 0:
+        return
+    ncpu = os.cpu_count() or 1
+    os.environ.setdefault("OMP_NUM_THREADS", str(ncpu))
+    per_step_cap = max(args.steps, 1)
+    # warm-up, then K timed steps, each step one decode token (bounded run)
+    tps, cores, kind, sample = cpu_reference_run(seconds=max(args.cpu_seconds * 5, 60.0),
+                                                 steps_cap=per_step_cap, warmup=args.warmup)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": tps, "unit": "tok/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": 1e3 / tps, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "fp4e2m1*e4m3->f32", "data": "synthetic",
+        "config": {"workload": "config 2 MoE layer op, decode M=1", "hidden": H,
+                   "moe_inter": I, "experts": E, "topk": TOPK, "shared": "fp8",
+                   "tokens_per_step": 1},
+        "cpu_baseline": {"value": tps, "unit": "tok/s", "cores": cores, "kind": kind,
+                         "sample": sample},
+        "e2e": {"value": tps, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# -------------------------------------------------------------- GPU side --
+def main():
+    args = parse()
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        run_reference_arm(args, rank, world)
+        return
+
+    import torch
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=dev)
+    import dsv4cuda
+    dsv4cuda.set_abort_on_error(False)
+    dsv4cuda.init(local)
+
+    M = args.tokens
+    layers = []
+    for li in range(args.layers):
+        lay = make_device_layer(torch, 1000 + li, dev)
+        layers.append((lay, dsv4cuda.MoeLayer(lay, max_tokens=M, device=True)))
+    torch.cuda.synchronize()
+    rng = np.random.default_rng(7)
+    pool = 32
+    x_host = bf16_tokens(rng, pool, M)
+    x_dev = torch.from_numpy(x_host).to(dev)
+    out_dev = torch.empty((M, H), dtype=torch.float32, device=dev)
+
+    # one CUDA graph per layer (launch overhead amortised; same kernels)
+    stream = torch.cuda.Stream(device=dev)
+    graphs = []
+    xin = torch.empty((M, H), dtype=torch.float32, device=dev)
+    with torch.cuda.stream(stream):
+        for _, L in layers:  # warm the kernels once outside capture
+            xin.copy_(x_dev[0])
+            L.forward(xin, out_dev, stream=stream.cuda_stream)
+    stream.synchronize()
+    for _, L in layers:
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            L.forward(xin, out_dev, stream=torch.cuda.current_stream().cuda_stream)
+        graphs.append(g)
+
+    def step(i):
+        xin.copy_(x_dev[i % pool], non_blocking=True)
+        graphs[i % len(graphs)].replay()
+
+    with torch.cuda.stream(stream):
+        for i in range(args.warmup):
+            step(i)
+    torch.cuda.synchronize()
+
+    clocks = ClockSampler(local)
+    clocks.start()
+    time.sleep(0.3)
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    ev0 = torch.cuda.Event(enable_timing=True)
+    ev1 = torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        ev0.record(stream)
+        for i in range(args.steps):
+            step(args.warmup + i)
+        ev1.record(stream)
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    ms = ev0.elapsed_time(ev1)
+    clk = clocks.stop()
+    if dist:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    ms_per_step = ms / args.steps
+    value = M * args.steps / (ms / 1e3)
+
+    # ---- expert-GEMV roofline: the same forward, ungraphed, with events
+    # around the routed gate/up and down launches on the forward stream
+    U_total, n_fw = 0, 0
+    lib = dsv4cuda.lib
+    for li, (_, L) in enumerate(layers):
+        lib.dsv4cuda_moe_timing_begin(L.handle)
+    gu_ms = dn_ms = 0.0
+    n_timed = 0
+    with torch.cuda.stream(stream):
+        for i in range(max(8, args.steps // 4)):
+            _, L = layers[i % len(layers)]
+            xin.copy_(x_dev[i % pool])
+            L.forward(xin, out_dev, stream=stream.cuda_stream)
+            idx, _, _ = L.last_routes(M)
+            U_total += len(np.unique(idx))
+            n_fw += 1
+    torch.cuda.synchronize()
+    import ctypes as C
+    for _, L in layers:
+        n = C.c_int()
+        a = C.c_float()
+        b = C.c_float()
+        lib.dsv4cuda_moe_timing_end(L.handle, C.byref(n), C.byref(a), C.byref(b))
+        gu_ms += a.value
+        dn_ms += b.value
+        n_timed += n.value
+    U_avg = U_total / max(n_fw, 1)
+    alg_bytes = U_avg * EXPERT_BYTES
+    kern_ms = (gu_ms + dn_ms) / max(n_timed, 1)
+    achieved = alg_bytes / (kern_ms * 1e-3) / 1e9
+    peaks_path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    peak, peak_src = 6650.0, "fallback"
+    if os.path.exists(peaks_path):
+        peak = float(json.load(open(peaks_path))["hbm_gbs"])
+        peak_src = "measured"
+
+    # ---- end to end through the public C API with host buffers
+    pin_x = torch.from_numpy(x_host).pin_memory()
+    pin_out = torch.empty((M, H), dtype=torch.float32).pin_memory()
+    L0 = layers[0][1]
+    xs = pin_x.numpy()
+    outs = pin_out.numpy()
+    for i in range(3):
+        L0.forward_host(xs[i % pool])
+    ptr_out = outs.ctypes.data_as(C.POINTER(C.c_float))
+    t0 = time.perf_counter()
+    e2e_steps = max(20, args.steps // 2)
+    for i in range(e2e_steps):
+        _, Li = layers[i % len(layers)]
+        xi = xs[i % pool]
+        rc = lib.dsv4cuda_moe_forward_host(Li.handle, xi.ctypes.data_as(C.POINTER(C.c_float)),
+                                           None, M, ptr_out)
+        if rc != 0:
+            raise RuntimeError(dsv4cuda.last_error())
+    e2e_s = time.perf_counter() - t0
+    e2e_val = M * e2e_steps / e2e_s
+
+    line = None
+    if rank == 0:
+        cpu = None
+        if world == 1:
+            try:
+                tps, cores, kind, sample = cpu_reference_run(args.cpu_seconds)
+                cpu = {"value": tps, "unit": "tok/s", "cores": cores, "kind": kind,
+                       "sample": sample}
+            except Exception as exc:  # report, do not hide
+                cpu = {"value": None, "unit": "tok/s", "cores": 0, "kind": "reference",
+                       "sample": f"failed: {exc}"}
+        line = {
+            "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "fp4e2m1*e4m3->f32", "data": "synthetic",
+            "config": {"workload": "config 2 MoE layer op, decode M=%d" % M, "hidden": H,
+                       "moe_inter": I, "experts": E, "topk": TOPK, "shared": "fp8",
+                       "tokens_per_step": M, "layers_cycled": args.layers,
+                       "l2": "inputs larger than L2: each step reads a different layer's "
+                             "~235 MB of weights", "parallelism": f"ep{world}"},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "traffic": None,
+                         "kernel": "fp4_gemv_kernel (routed gate/up pair + down)",
+                         "alg_bytes_per_step": alg_bytes, "peak_source": peak_src,
+                         "kernel_ms_per_step": kern_ms},
+            "cpu_baseline": cpu,
+            "e2e": {"value": e2e_val, "unit": "tok/s", "h2d_bytes_per_step": M * H * 4,
+                    "d2h_bytes_per_step": M * H * 4},
+            "gpu_launches": 12 * args.steps,
+            "clocks": clk,
+        }
+        print(json.dumps(line), flush=True)
+    for _, L in layers:
+        L.close()
+    del graphs
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

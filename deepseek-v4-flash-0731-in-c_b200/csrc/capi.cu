@@ -1,0 +1,759 @@
+// capi.cu - the C ABI of libdsv4_cuda.so (declared in include/dsv4_cuda.h).
+//
+// Drop-in kernel symbols stage host operands through per-thread device
+// buffers on a per-thread stream (the reference may call its kernels from
+// several OpenMP threads, src/dsv4/dsv4_model.c:6703-6725), run the exact
+// kernels and copy the results back before returning, like the reference's
+// synchronous kernels.
+#include <cstdarg>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <string>
+#include <vector>
+#include <atomic>
+
+#include <cuda_fp16.h>
+
+#include "dsv4_common.cuh"
+#include "gemv.cuh"
+#include "moe.cuh"
+#include "../../include/dsv4_cuda.h"
+
+#define DSV4_API extern "C" __attribute__((visibility("default")))
+
+namespace {
+
+std::atomic<int> g_abort{1};
+thread_local std::string t_last_error;
+
+struct ThreadState {
+  int device = -1;
+  cudaStream_t stream = nullptr;
+  char* dbuf = nullptr;
+  size_t dcap = 0;
+  int* counter = nullptr;  // device int used as "n_items" for host-built lists
+};
+thread_local ThreadState t_state;
+
+void record_error(const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  t_last_error = buf;
+}
+
+// Drop-in fatal path: the reference exits on its own fatal errors.
+void fatal_or_record(const char* what, cudaError_t e) {
+  record_error("%s: %s", what, cudaGetErrorString(e));
+  if (g_abort.load()) {
+    fprintf(stderr, "dsv4_cuda: %s\n", t_last_error.c_str());
+    exit(1);
+  }
+}
+
+int ensure_thread_state() {
+  if (t_state.stream) return 0;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) { record_error("cudaGetDevice: %s", cudaGetErrorString(e)); return -1; }
+  e = cudaStreamCreateWithFlags(&t_state.stream, cudaStreamNonBlocking);
+  if (e != cudaSuccess) { record_error("stream: %s", cudaGetErrorString(e)); return -1; }
+  e = cudaMalloc(&t_state.counter, sizeof(int) * 4);
+  if (e != cudaSuccess) { record_error("cudaMalloc: %s", cudaGetErrorString(e)); return -1; }
+  t_state.device = dev;
+  return 0;
+}
+
+// Grow-only per-thread device staging buffer.
+char* staging(size_t bytes) {
+  if (bytes > t_state.dcap) {
+    if (t_state.dbuf) cudaFree(t_state.dbuf);
+    t_state.dbuf = nullptr;
+    t_state.dcap = 0;
+    const size_t cap = bytes + bytes / 4 + 4096;
+    if (cudaMalloc(&t_state.dbuf, cap) != cudaSuccess) return nullptr;
+    t_state.dcap = cap;
+  }
+  return t_state.dbuf;
+}
+
+size_t al(size_t b) { return (b + 255) & ~static_cast<size_t>(255); }
+
+// Carves 256-byte aligned pieces out of the staging buffer.
+struct Carver {
+  char* base;
+  size_t off = 0;
+  template <class T>
+  T* take(size_t count) {
+    T* p = reinterpret_cast<T*>(base + off);
+    off += al(count * sizeof(T));
+    return p;
+  }
+};
+
+bool f16_exact(float v) {
+  const __half h = __float2half_rn(v);
+  const float back = __half2float(h);
+  return back == v || (v != v && back != back);
+}
+
+// Host item list for a batch of `batch` tokens against one matrix.
+std::vector<dsv4::GemvItem> batch_items(int batch) {
+  std::vector<dsv4::GemvItem> items((batch + dsv4::kItemTok - 1) / dsv4::kItemTok);
+  for (size_t j = 0; j < items.size(); ++j) {
+    dsv4::GemvItem& it = items[j];
+    it.mat = 0;
+    it.ntok = std::min<int>(dsv4::kItemTok, batch - static_cast<int>(j) * dsv4::kItemTok);
+    for (int i = 0; i < dsv4::kItemTok; ++i) {
+      const int t = std::min<int>(static_cast<int>(j) * dsv4::kItemTok + i, batch - 1);
+      it.tok[i].x = t;
+      it.tok[i].y = t;
+    }
+  }
+  return items;
+}
+
+int nt_bucket(int n) { return n <= 1 ? 1 : n <= 2 ? 2 : n <= 4 ? 4 : 8; }
+
+void batch_limit(const char* kind, int batch) {
+  if (batch > dsv4::kMaxBatch) {
+    // src/dsv4/dsv4_model.c:316-320 / :689-693 / :1094-1098
+    fprintf(stderr, "dsv4: %s batch %d exceeds %d\n", kind, batch, dsv4::kMaxBatch);
+    exit(1);
+  }
+}
+
+#define STAGE_CHECK(expr, what)                      \
+  do {                                               \
+    cudaError_t e__ = (expr);                        \
+    if (e__ != cudaSuccess) {                        \
+      fatal_or_record(what, e__);                    \
+      return;                                        \
+    }                                                \
+  } while (0)
+
+// Upload activations for `batch` tokens: f16 copy (plus an fp32 copy when any
+// value is not exactly representable in f16) and scales.
+struct StagedAct {
+  dsv4::QAct act;
+};
+
+void fp4_or_fp8_gemv(bool fp4, float* const* y0, float* const* y1, const float* const* qx,
+                     const float* const* qscale, int batch, const uint8_t* W0, const uint8_t* S0,
+                     const uint8_t* W1, const uint8_t* S1, int in, int rows, int round_out) {
+  if (batch <= 0 || rows <= 0) return;
+  if (ensure_thread_state() != 0) { fatal_or_record("init", cudaErrorInitializationError); return; }
+  cudaStream_t st = t_state.stream;
+  const bool pair = W1 != nullptr;
+  const size_t wbytes = fp4 ? static_cast<size_t>(rows) * ((in + 1) / 2)
+                            : static_cast<size_t>(rows) * in;
+  const size_t sbytes = fp4 ? static_cast<size_t>(rows) * ((in + 31) / 32)
+                            : static_cast<size_t>((rows + 127) / 128) * ((in + 127) / 128);
+  const int ld = (in + 127) / 128 * 128;
+  const int nsc = ld / 128;
+  bool exact16 = true;
+  for (int t = 0; t < batch && exact16; ++t)
+    for (int c = 0; c < in; ++c)
+      if (!f16_exact(qx[t][c])) { exact16 = false; break; }
+  const std::vector<dsv4::GemvItem> items = batch_items(batch);
+  const size_t need = al(wbytes) * (pair ? 2 : 1) + al(sbytes) * (pair ? 2 : 1) +
+                      al(sizeof(float) * batch * ld) * 2 + al(sizeof(__half) * batch * ld) +
+                      al(sizeof(float) * batch * nsc) + al(sizeof(float) * batch * rows) * 2 +
+                      al(sizeof(dsv4::GemvItem) * items.size()) + 1024;
+  char* base = staging(need);
+  if (!base) { fatal_or_record("staging cudaMalloc", cudaErrorMemoryAllocation); return; }
+  Carver cv{base};
+  uint8_t* dW0 = cv.take<uint8_t>(wbytes);
+  uint8_t* dS0 = cv.take<uint8_t>(sbytes);
+  uint8_t* dW1 = pair ? cv.take<uint8_t>(wbytes) : nullptr;
+  uint8_t* dS1 = pair ? cv.take<uint8_t>(sbytes) : nullptr;
+  float* dx32 = cv.take<float>(static_cast<size_t>(batch) * ld);
+  __half* dx16 = cv.take<__half>(static_cast<size_t>(batch) * ld);
+  float* dqs = cv.take<float>(static_cast<size_t>(batch) * nsc);
+  float* dy0 = cv.take<float>(static_cast<size_t>(batch) * rows);
+  float* dy1 = cv.take<float>(static_cast<size_t>(batch) * rows);
+  dsv4::GemvItem* ditems = cv.take<dsv4::GemvItem>(items.size());
+
+  STAGE_CHECK(cudaMemcpyAsync(dW0, W0, wbytes, cudaMemcpyHostToDevice, st), "copy W");
+  STAGE_CHECK(cudaMemcpyAsync(dS0, S0, sbytes, cudaMemcpyHostToDevice, st), "copy S");
+  if (pair) {
+    STAGE_CHECK(cudaMemcpyAsync(dW1, W1, wbytes, cudaMemcpyHostToDevice, st), "copy W1");
+    STAGE_CHECK(cudaMemcpyAsync(dS1, S1, sbytes, cudaMemcpyHostToDevice, st), "copy S1");
+  }
+  STAGE_CHECK(cudaMemsetAsync(dx32, 0, sizeof(float) * batch * ld, st), "memset");
+  for (int t = 0; t < batch; ++t) {
+    STAGE_CHECK(cudaMemcpyAsync(dx32 + static_cast<size_t>(t) * ld, qx[t], sizeof(float) * in,
+                                cudaMemcpyHostToDevice, st), "copy qx");
+    STAGE_CHECK(cudaMemcpyAsync(dqs + static_cast<size_t>(t) * nsc, qscale[t],
+                                sizeof(float) * ((in + 127) / 128), cudaMemcpyHostToDevice, st),
+                "copy qscale");
+  }
+  STAGE_CHECK(cudaMemcpyAsync(ditems, items.data(), sizeof(dsv4::GemvItem) * items.size(),
+                              cudaMemcpyHostToDevice, st), "copy items");
+  const int nitems = static_cast<int>(items.size());
+  STAGE_CHECK(cudaMemcpyAsync(t_state.counter, &nitems, sizeof(int), cudaMemcpyHostToDevice, st),
+              "copy count");
+  STAGE_CHECK(dsv4::launch_f32_to_f16(dx32, dx16, static_cast<size_t>(batch) * ld, st), "cvt");
+  const dsv4::QAct act{dx16, dqs, ld, exact16 ? nullptr : dx32};
+  const int nt = nt_bucket(std::min(batch, dsv4::kItemTok));
+  if (fp4) {
+    dsv4::Fp4GemvArgs a{};
+    a.W[0] = dW0; a.S[0] = dS0; a.W[1] = dW1; a.S[1] = dS1;
+    a.in = in; a.rows = rows; a.act = act;
+    a.Y[0] = dy0; a.Y[1] = dy1;
+    a.items = ditems; a.n_items = t_state.counter; a.max_items = nitems;
+    STAGE_CHECK(dsv4::launch_fp4_gemv(a, pair, nt, st), "fp4 gemv");
+  } else {
+    dsv4::Fp8GemvArgs a{};
+    a.W[0] = dW0; a.S[0] = dS0; a.W[1] = dW1; a.S[1] = dS1;
+    a.in = in; a.rows = rows; a.round_out = round_out; a.act = act;
+    a.Y[0] = dy0; a.Y[1] = dy1;
+    a.items = ditems; a.n_items = t_state.counter; a.max_items = nitems;
+    STAGE_CHECK(dsv4::launch_fp8_gemv(a, pair, nt, st), "fp8 gemv");
+  }
+  for (int t = 0; t < batch; ++t) {
+    STAGE_CHECK(cudaMemcpyAsync(y0[t], dy0 + static_cast<size_t>(t) * rows, sizeof(float) * rows,
+                                cudaMemcpyDeviceToHost, st), "copy y");
+    if (pair)
+      STAGE_CHECK(cudaMemcpyAsync(y1[t], dy1 + static_cast<size_t>(t) * rows,
+                                  sizeof(float) * rows, cudaMemcpyDeviceToHost, st), "copy y1");
+  }
+  STAGE_CHECK(cudaStreamSynchronize(st), "sync");
+}
+
+void bf16_gemv(float* const* y, const float* const* x, int batch, const uint16_t* W, int in,
+               int out, int round_out) {
+  if (batch <= 0 || out <= 0) return;
+  if (ensure_thread_state() != 0) { fatal_or_record("init", cudaErrorInitializationError); return; }
+  cudaStream_t st = t_state.stream;
+  const size_t wbytes = static_cast<size_t>(out) * in * sizeof(uint16_t);
+  const int ld = (in + 7) / 8 * 8;
+  const std::vector<dsv4::GemvItem> items = batch_items(batch);
+  const size_t need = al(wbytes) + al(sizeof(float) * batch * ld) +
+                      al(sizeof(float) * batch * out) + al(sizeof(dsv4::GemvItem) * items.size()) +
+                      1024;
+  char* base = staging(need);
+  if (!base) { fatal_or_record("staging cudaMalloc", cudaErrorMemoryAllocation); return; }
+  Carver cv{base};
+  uint16_t* dW = cv.take<uint16_t>(static_cast<size_t>(out) * in);
+  float* dx = cv.take<float>(static_cast<size_t>(batch) * ld);
+  float* dy = cv.take<float>(static_cast<size_t>(batch) * out);
+  dsv4::GemvItem* ditems = cv.take<dsv4::GemvItem>(items.size());
+  STAGE_CHECK(cudaMemcpyAsync(dW, W, wbytes, cudaMemcpyHostToDevice, st), "copy W");
+  for (int t = 0; t < batch; ++t)
+    STAGE_CHECK(cudaMemcpyAsync(dx + static_cast<size_t>(t) * ld, x[t], sizeof(float) * in,
+                                cudaMemcpyHostToDevice, st), "copy x");
+  STAGE_CHECK(cudaMemcpyAsync(ditems, items.data(), sizeof(dsv4::GemvItem) * items.size(),
+                              cudaMemcpyHostToDevice, st), "copy items");
+  const int nitems = static_cast<int>(items.size());
+  STAGE_CHECK(cudaMemcpyAsync(t_state.counter, &nitems, sizeof(int), cudaMemcpyHostToDevice, st),
+              "copy count");
+  dsv4::Bf16GemvArgs a{};
+  a.W = dW; a.in = in; a.rows = out; a.round_out = round_out;
+  a.x = dx; a.ldx = ld; a.Y = dy;
+  a.items = ditems; a.n_items = t_state.counter; a.max_items = nitems;
+  STAGE_CHECK(dsv4::launch_bf16_gemv(a, nt_bucket(std::min(batch, dsv4::kItemTok)), st),
+              "bf16 gemv");
+  for (int t = 0; t < batch; ++t)
+    STAGE_CHECK(cudaMemcpyAsync(y[t], dy + static_cast<size_t>(t) * out, sizeof(float) * out,
+                                cudaMemcpyDeviceToHost, st), "copy y");
+  STAGE_CHECK(cudaStreamSynchronize(st), "sync");
+}
+
+void quant_codes(float* qx, float* qscale, const float* x, int n) {
+  if (n <= 0) return;
+  if (ensure_thread_state() != 0) { fatal_or_record("init", cudaErrorInitializationError); return; }
+  cudaStream_t st = t_state.stream;
+  const int nb = (n + 127) / 128;
+  char* base = staging(al(sizeof(float) * n) * 2 + al(sizeof(float) * nb) + 1024);
+  if (!base) { fatal_or_record("staging cudaMalloc", cudaErrorMemoryAllocation); return; }
+  Carver cv{base};
+  float* dx = cv.take<float>(n);
+  float* dq = cv.take<float>(n);
+  float* ds = cv.take<float>(nb);
+  STAGE_CHECK(cudaMemcpyAsync(dx, x, sizeof(float) * n, cudaMemcpyHostToDevice, st), "copy x");
+  STAGE_CHECK(dsv4::launch_quant_fp8_f32(dx, n, dq, ds, st), "quant");
+  STAGE_CHECK(cudaMemcpyAsync(qx, dq, sizeof(float) * n, cudaMemcpyDeviceToHost, st), "copy qx");
+  STAGE_CHECK(cudaMemcpyAsync(qscale, ds, sizeof(float) * nb, cudaMemcpyDeviceToHost, st),
+              "copy qs");
+  STAGE_CHECK(cudaStreamSynchronize(st), "sync");
+}
+
+}  // namespace
+
+// ---------------------------------------------------------------- layer --
+struct dsv4cuda_moe_layer {
+  dsv4::MoeConfig cfg{};
+  dsv4::MoeWeights w{};
+  dsv4::MoeWorkspace ws{};
+  void* owned = nullptr;      // weights copied in by dsv4cuda_moe_create
+  size_t owned_bytes = 0;
+  void* ws_mem = nullptr;
+  size_t ws_bytes = 0;
+  float* d_x = nullptr;       // host-path staging
+  float* d_out = nullptr;
+  int* d_tok = nullptr;
+  int max_tokens = 0;
+  // expert-GEMV timing (dsv4cuda_moe_timing_*): event quadruples per forward
+  std::vector<cudaEvent_t> events;
+  int timed = 0;
+  bool timing = false;
+};
+
+namespace {
+
+struct LayerSizes {
+  size_t gate, bias, tid, w13, s13, w2, s2, sh13, sh13s, sh2, sh2s;
+};
+
+LayerSizes layer_sizes(const dsv4::MoeConfig& c) {
+  const size_t H = c.hidden, I = c.moe_inter, E = c.n_experts, K = c.topk;
+  LayerSizes s{};
+  s.gate = E * H * 2;
+  s.bias = E * 4;
+  s.tid = static_cast<size_t>(c.hash_vocab) * K * 8;
+  s.w13 = E * I * (H / 2);
+  s.s13 = E * I * (H / 32);
+  s.w2 = E * H * (I / 2);
+  s.s2 = E * H * (I / 32);
+  if (c.shared_kind == dsv4::kSharedFp8) {
+    s.sh13 = I * H;
+    s.sh13s = ((I + 127) / 128) * ((H + 127) / 128);
+    s.sh2 = H * I;
+    s.sh2s = ((H + 127) / 128) * ((I + 127) / 128);
+  } else if (c.shared_kind == dsv4::kSharedFp4) {
+    s.sh13 = I * (H / 2);
+    s.sh13s = I * (H / 32);
+    s.sh2 = H * (I / 2);
+    s.sh2s = H * (I / 32);
+  }
+  return s;
+}
+
+int validate_cfg(const dsv4cuda_moe_config* c) {
+  if (!c || c->hidden <= 0 || c->moe_inter <= 0 || c->n_experts <= 0 || c->topk <= 0 ||
+      c->topk > dsv4::kMaxTopk || c->topk > c->n_experts || c->hidden % 32 != 0 ||
+      c->moe_inter % 32 != 0 || c->shared_kind < 0 || c->shared_kind > 2 || c->hash_vocab < 0) {
+    record_error("invalid dsv4cuda_moe_config");
+    return -1;
+  }
+  return 0;
+}
+
+int layer_finish(dsv4cuda_moe_layer* L, int max_tokens) {
+  L->max_tokens = max_tokens;
+  L->ws_bytes = dsv4::moe_workspace_bytes(L->cfg, max_tokens) +
+                al(sizeof(float) * max_tokens * L->cfg.hidden) * 2 + al(sizeof(int) * max_tokens);
+  cudaError_t e = cudaMalloc(&L->ws_mem, L->ws_bytes);
+  if (e != cudaSuccess) { record_error("workspace cudaMalloc: %s", cudaGetErrorString(e)); return -1; }
+  cudaMemset(L->ws_mem, 0, L->ws_bytes);
+  dsv4::moe_workspace_carve(&L->ws, L->cfg, max_tokens, L->ws_mem);
+  char* p = static_cast<char*>(L->ws_mem) + L->ws.bytes;
+  L->d_x = reinterpret_cast<float*>(p);
+  p += al(sizeof(float) * max_tokens * L->cfg.hidden);
+  L->d_out = reinterpret_cast<float*>(p);
+  p += al(sizeof(float) * max_tokens * L->cfg.hidden);
+  L->d_tok = reinterpret_cast<int*>(p);
+  return 0;
+}
+
+dsv4::MoeConfig to_cfg(const dsv4cuda_moe_config* c) {
+  dsv4::MoeConfig m{};
+  m.hidden = c->hidden;
+  m.moe_inter = c->moe_inter;
+  m.n_experts = c->n_experts;
+  m.topk = c->topk;
+  m.swiglu_limit = c->swiglu_limit;
+  m.route_scale = c->route_scale;
+  m.shared_kind = c->shared_kind;
+  m.hash_vocab = c->hash_vocab;
+  return m;
+}
+
+}  // namespace
+
+// ================================================================ exports ==
+
+DSV4_API void dsv4cuda_shutdown(void) {
+  if (t_state.dbuf) cudaFree(t_state.dbuf);
+  if (t_state.counter) cudaFree(t_state.counter);
+  if (t_state.stream) cudaStreamDestroy(t_state.stream);
+  t_state = ThreadState();
+}
+
+DSV4_API int dsv4cuda_init(int device) {
+  if (t_state.stream && t_state.device != device) dsv4cuda_shutdown();
+  cudaError_t e = cudaSetDevice(device);
+  if (e != cudaSuccess) { record_error("cudaSetDevice(%d): %s", device, cudaGetErrorString(e)); return -1; }
+  return ensure_thread_state();
+}
+
+DSV4_API const char* dsv4cuda_last_error(void) { return t_last_error.c_str(); }
+
+DSV4_API int dsv4cuda_set_abort_on_error(int abort_on_error) {
+  return g_abort.exchange(abort_on_error ? 1 : 0);
+}
+
+
+// ---- drop-in kernels
+DSV4_API void dsv4cuda_gemv_fp4_q(float* y, const float* qx, const float* qscale, const uint8_t* W,
+                                  const uint8_t* wscale_code, int in, int rows) {
+  float* ys[1] = {y};
+  const float* xs[1] = {qx};
+  const float* ss[1] = {qscale};
+  fp4_or_fp8_gemv(true, ys, nullptr, xs, ss, 1, W, wscale_code, nullptr, nullptr, in, rows, 1);
+}
+DSV4_API void dsv4cuda_gemv_fp4_batch_q(float* const* y, const float* const* qx,
+                                        const float* const* qscale, int batch, const uint8_t* W,
+                                        const uint8_t* wscale_code, int in, int rows) {
+  if (batch <= 0) return;
+  batch_limit("FP4", batch);
+  fp4_or_fp8_gemv(true, y, nullptr, qx, qscale, batch, W, wscale_code, nullptr, nullptr, in, rows,
+                  1);
+}
+DSV4_API void dsv4cuda_gemv_fp4_pair_q(float* y0, float* y1, const float* qx, const float* qscale,
+                                       const uint8_t* W0, const uint8_t* S0, const uint8_t* W1,
+                                       const uint8_t* S1, int in, int rows) {
+  float* a[1] = {y0};
+  float* b[1] = {y1};
+  const float* xs[1] = {qx};
+  const float* ss[1] = {qscale};
+  fp4_or_fp8_gemv(true, a, b, xs, ss, 1, W0, S0, W1, S1, in, rows, 1);
+}
+DSV4_API void dsv4cuda_gemv_fp8_q(float* y, const float* qx, const float* qscale, const uint8_t* W,
+                                  const uint8_t* wscale_code, int in, int out, int round_out) {
+  float* ys[1] = {y};
+  const float* xs[1] = {qx};
+  const float* ss[1] = {qscale};
+  fp4_or_fp8_gemv(false, ys, nullptr, xs, ss, 1, W, wscale_code, nullptr, nullptr, in, out,
+                  round_out);
+}
+DSV4_API void dsv4cuda_gemv_fp8_batch_q(float* const* y, const float* const* qx,
+                                        const float* const* qscale, int batch, const uint8_t* W,
+                                        const uint8_t* wscale_code, int in, int out,
+                                        int round_out) {
+  if (batch <= 0) return;
+  batch_limit("FP8", batch);
+  fp4_or_fp8_gemv(false, y, nullptr, qx, qscale, batch, W, wscale_code, nullptr, nullptr, in, out,
+                  round_out);
+}
+DSV4_API void dsv4cuda_gemv_fp8_pair_q(float* y0, float* y1, const float* qx, const float* qscale,
+                                       const uint8_t* W0, const uint8_t* S0, const uint8_t* W1,
+                                       const uint8_t* S1, int in, int out) {
+  float* a[1] = {y0};
+  float* b[1] = {y1};
+  const float* xs[1] = {qx};
+  const float* ss[1] = {qscale};
+  fp4_or_fp8_gemv(false, a, b, xs, ss, 1, W0, S0, W1, S1, in, out, 1);
+}
+DSV4_API void dsv4cuda_gemv_bf16(float* y, const float* x, const uint16_t* W, int in, int out,
+                                 int round_out) {
+  float* ys[1] = {y};
+  const float* xs[1] = {x};
+  bf16_gemv(ys, xs, 1, W, in, out, round_out);
+}
+DSV4_API void dsv4cuda_gemv_bf16_batch(float* const* y, const float* const* x, int batch,
+                                       const uint16_t* W, int in, int out, int round_out) {
+  if (batch <= 0) return;
+  batch_limit("BF16", batch);
+  bf16_gemv(y, x, batch, W, in, out, round_out);
+}
+DSV4_API void dsv4cuda_quant_fp8_codes(float* qx, float* qscale, const float* x, int n) {
+  quant_codes(qx, qscale, x, n);
+}
+
+// Unprefixed drop-in names: identical signatures to the reference.
+DSV4_API void dsv4_gemv_fp4_q(float* y, const float* qx, const float* qscale, const uint8_t* W,
+                              const uint8_t* s, int in, int rows) {
+  dsv4cuda_gemv_fp4_q(y, qx, qscale, W, s, in, rows);
+}
+DSV4_API void dsv4_gemv_fp4_batch_q(float* const* y, const float* const* qx,
+                                    const float* const* qscale, int batch, const uint8_t* W,
+                                    const uint8_t* s, int in, int rows) {
+  dsv4cuda_gemv_fp4_batch_q(y, qx, qscale, batch, W, s, in, rows);
+}
+DSV4_API void dsv4_gemv_fp4_pair_q(float* y0, float* y1, const float* qx, const float* qscale,
+                                   const uint8_t* W0, const uint8_t* S0, const uint8_t* W1,
+                                   const uint8_t* S1, int in, int rows) {
+  dsv4cuda_gemv_fp4_pair_q(y0, y1, qx, qscale, W0, S0, W1, S1, in, rows);
+}
+DSV4_API void dsv4_gemv_fp8_q(float* y, const float* qx, const float* qscale, const uint8_t* W,
+                              const uint8_t* s, int in, int out, int round_out) {
+  dsv4cuda_gemv_fp8_q(y, qx, qscale, W, s, in, out, round_out);
+}
+DSV4_API void dsv4_gemv_fp8_batch_q(float* const* y, const float* const* qx,
+                                    const float* const* qscale, int batch, const uint8_t* W,
+                                    const uint8_t* s, int in, int out, int round_out) {
+  dsv4cuda_gemv_fp8_batch_q(y, qx, qscale, batch, W, s, in, out, round_out);
+}
+DSV4_API void dsv4_gemv_fp8_pair_q(float* y0, float* y1, const float* qx, const float* qscale,
+                                   const uint8_t* W0, const uint8_t* S0, const uint8_t* W1,
+                                   const uint8_t* S1, int in, int out) {
+  dsv4cuda_gemv_fp8_pair_q(y0, y1, qx, qscale, W0, S0, W1, S1, in, out);
+}
+DSV4_API void dsv4_gemv_bf16(float* y, const float* x, const uint16_t* W, int in, int out,
+                             int round_out) {
+  dsv4cuda_gemv_bf16(y, x, W, in, out, round_out);
+}
+DSV4_API void dsv4_gemv_bf16_batch(float* const* y, const float* const* x, int batch,
+                                   const uint16_t* W, int in, int out, int round_out) {
+  dsv4cuda_gemv_bf16_batch(y, x, batch, W, in, out, round_out);
+}
+DSV4_API void dsv4_quant_fp8_codes(float* qx, float* qscale, const float* x, int n) {
+  quant_codes(qx, qscale, x, n);
+}
+DSV4_API void dsv4_quant_fp8_act(float* out, float* scales, const float* x, int n) {
+  quant_codes(out, scales, x, n);
+}
+
+// Public dsv4_router (src/dsv4/dsv4_ops.c:473): stages the BF16 gate, runs
+// the device router with the public numerics (separate multiply and add,
+// 1/sum weights) for one token.
+DSV4_API void dsv4_router(int* idx, float* wt, const float* x, const float* gate,
+                          const float* bias, const int64_t* tid2eid, int token_id, int hidden,
+                          int n_experts, int topk, int hash_layer, float route_scale,
+                          float rms_eps) {
+  (void)rms_eps;
+  if (topk <= 0) return;
+  if (ensure_thread_state() != 0) { fatal_or_record("init", cudaErrorInitializationError); return; }
+  cudaStream_t st = t_state.stream;
+  dsv4::MoeConfig c{};
+  c.hidden = hidden;
+  c.moe_inter = 128;
+  c.n_experts = n_experts;
+  c.topk = topk;
+  c.route_scale = route_scale;
+  c.hash_vocab = hash_layer ? 1 : 0;
+  // router-only workspace pieces: zd, zb, idx, wt, counters
+  const size_t gbytes = static_cast<size_t>(n_experts) * hidden * 2;
+  const size_t need = al(gbytes) + al(sizeof(float) * n_experts) + al(sizeof(float) * hidden) +
+                      al(8 * topk) + 2 * al(sizeof(double) * n_experts) + al(sizeof(int) * topk) +
+                      al(sizeof(float) * topk) + al(8 * sizeof(int)) + al(sizeof(int)) + 1024;
+  char* base = staging(need);
+  if (!base) { fatal_or_record("staging cudaMalloc", cudaErrorMemoryAllocation); return; }
+  Carver cv{base};
+  uint16_t* dg = cv.take<uint16_t>(static_cast<size_t>(n_experts) * hidden);
+  float* db = cv.take<float>(n_experts);
+  float* dx = cv.take<float>(hidden);
+  int64_t* dt = cv.take<int64_t>(topk);
+  dsv4::MoeWorkspace ws{};
+  ws.max_tokens = 1;
+  ws.zd = cv.take<double>(n_experts);
+  ws.zb = cv.take<double>(n_experts);
+  ws.idx = cv.take<int>(topk);
+  ws.wt = cv.take<float>(topk);
+  ws.counters = cv.take<int>(8);
+  int* dtok = cv.take<int>(1);
+  STAGE_CHECK(cudaMemcpyAsync(dg, gate, gbytes, cudaMemcpyHostToDevice, st), "copy gate");
+  if (bias)
+    STAGE_CHECK(cudaMemcpyAsync(db, bias, sizeof(float) * n_experts, cudaMemcpyHostToDevice, st),
+                "copy bias");
+  STAGE_CHECK(cudaMemcpyAsync(dx, x, sizeof(float) * hidden, cudaMemcpyHostToDevice, st), "copy x");
+  const int zero = 0;
+  if (hash_layer)
+    STAGE_CHECK(cudaMemcpyAsync(dt, tid2eid + static_cast<size_t>(token_id) * topk,
+                                sizeof(int64_t) * topk, cudaMemcpyHostToDevice, st), "copy tid2eid");
+  STAGE_CHECK(cudaMemcpyAsync(dtok, &zero, sizeof(int), cudaMemcpyHostToDevice, st), "copy tok");
+  STAGE_CHECK(cudaMemsetAsync(ws.counters, 0, 8 * sizeof(int), st), "memset");
+  dsv4::MoeWeights w{};
+  w.gate_w = dg;
+  w.bias = bias ? db : nullptr;
+  w.tid2eid = hash_layer ? dt : nullptr;
+  STAGE_CHECK(dsv4::moe_route(c, w, ws, dx, dtok, 1, 1, st), "router");
+  STAGE_CHECK(cudaMemcpyAsync(idx, ws.idx, sizeof(int) * topk, cudaMemcpyDeviceToHost, st), "copy idx");
+  STAGE_CHECK(cudaMemcpyAsync(wt, ws.wt, sizeof(float) * topk, cudaMemcpyDeviceToHost, st), "copy wt");
+  STAGE_CHECK(cudaStreamSynchronize(st), "sync");
+}
+
+// ---- MoE layer
+DSV4_API int dsv4cuda_moe_create(dsv4cuda_moe_layer** out, const dsv4cuda_moe_config* cfg,
+                                 const dsv4cuda_moe_weights* hw, int max_tokens) {
+  if (!out || !hw || max_tokens <= 0) { record_error("dsv4cuda_moe_create: bad arguments"); return -1; }
+  *out = nullptr;
+  if (validate_cfg(cfg) != 0) return -1;
+  if (!hw->gate_w || !hw->w1 || !hw->s1 || !hw->w3 || !hw->s3 || !hw->w2 || !hw->s2 ||
+      (cfg->shared_kind != 0 && (!hw->sh1 || !hw->sh1s || !hw->sh3 || !hw->sh3s || !hw->sh2 ||
+                                 !hw->sh2s)) ||
+      (cfg->hash_vocab > 0 && !hw->tid2eid)) {
+    record_error("dsv4cuda_moe_create: missing weight pointer");
+    return -1;
+  }
+  dsv4cuda_moe_layer* L = new dsv4cuda_moe_layer();
+  L->cfg = to_cfg(cfg);
+  const LayerSizes s = layer_sizes(L->cfg);
+  const size_t total = al(s.gate) + al(s.bias) + al(s.tid) + 2 * al(s.w13) + 2 * al(s.s13) +
+                       al(s.w2) + al(s.s2) + 2 * al(s.sh13) + 2 * al(s.sh13s) + al(s.sh2) +
+                       al(s.sh2s);
+  cudaError_t e = cudaMalloc(&L->owned, total);
+  if (e != cudaSuccess) {
+    record_error("weights cudaMalloc(%zu): %s", total, cudaGetErrorString(e));
+    delete L;
+    return -1;
+  }
+  L->owned_bytes = total;
+  char* p = static_cast<char*>(L->owned);
+  auto put = [&](const void* src, size_t bytes) -> const void* {
+    if (!src || bytes == 0) return nullptr;
+    void* dst = p;
+    p += al(bytes);
+    if (cudaMemcpy(dst, src, bytes, cudaMemcpyHostToDevice) != cudaSuccess) e = cudaErrorUnknown;
+    return dst;
+  };
+  L->w.gate_w = static_cast<const uint16_t*>(put(hw->gate_w, s.gate));
+  L->w.bias = static_cast<const float*>(put(hw->bias, s.bias));
+  L->w.tid2eid = cfg->hash_vocab > 0 ? static_cast<const int64_t*>(put(hw->tid2eid, s.tid)) : nullptr;
+  L->w.w1 = static_cast<const uint8_t*>(put(hw->w1, s.w13));
+  L->w.s1 = static_cast<const uint8_t*>(put(hw->s1, s.s13));
+  L->w.w3 = static_cast<const uint8_t*>(put(hw->w3, s.w13));
+  L->w.s3 = static_cast<const uint8_t*>(put(hw->s3, s.s13));
+  L->w.w2 = static_cast<const uint8_t*>(put(hw->w2, s.w2));
+  L->w.s2 = static_cast<const uint8_t*>(put(hw->s2, s.s2));
+  if (cfg->shared_kind != 0) {
+    L->w.sh1 = static_cast<const uint8_t*>(put(hw->sh1, s.sh13));
+    L->w.sh1s = static_cast<const uint8_t*>(put(hw->sh1s, s.sh13s));
+    L->w.sh3 = static_cast<const uint8_t*>(put(hw->sh3, s.sh13));
+    L->w.sh3s = static_cast<const uint8_t*>(put(hw->sh3s, s.sh13s));
+    L->w.sh2 = static_cast<const uint8_t*>(put(hw->sh2, s.sh2));
+    L->w.sh2s = static_cast<const uint8_t*>(put(hw->sh2s, s.sh2s));
+  }
+  if (e != cudaSuccess || layer_finish(L, max_tokens) != 0) {
+    if (e != cudaSuccess) record_error("weight upload failed");
+    dsv4cuda_moe_destroy(L);
+    return -1;
+  }
+  *out = L;
+  return 0;
+}
+
+DSV4_API int dsv4cuda_moe_create_device(dsv4cuda_moe_layer** out, const dsv4cuda_moe_config* cfg,
+                                        const dsv4cuda_moe_weights* dw, int max_tokens) {
+  if (!out || !dw || max_tokens <= 0) { record_error("dsv4cuda_moe_create_device: bad arguments"); return -1; }
+  *out = nullptr;
+  if (validate_cfg(cfg) != 0) return -1;
+  dsv4cuda_moe_layer* L = new dsv4cuda_moe_layer();
+  L->cfg = to_cfg(cfg);
+  L->w.gate_w = dw->gate_w;
+  L->w.bias = dw->bias;
+  L->w.tid2eid = dw->tid2eid;
+  L->w.w1 = dw->w1; L->w.s1 = dw->s1; L->w.w3 = dw->w3; L->w.s3 = dw->s3;
+  L->w.w2 = dw->w2; L->w.s2 = dw->s2;
+  L->w.sh1 = dw->sh1; L->w.sh1s = dw->sh1s; L->w.sh3 = dw->sh3; L->w.sh3s = dw->sh3s;
+  L->w.sh2 = dw->sh2; L->w.sh2s = dw->sh2s;
+  if (layer_finish(L, max_tokens) != 0) {
+    dsv4cuda_moe_destroy(L);
+    return -1;
+  }
+  *out = L;
+  return 0;
+}
+
+DSV4_API void dsv4cuda_moe_destroy(dsv4cuda_moe_layer* L) {
+  if (!L) return;
+  for (cudaEvent_t e : L->events) cudaEventDestroy(e);
+  if (L->owned) cudaFree(L->owned);
+  if (L->ws_mem) cudaFree(L->ws_mem);
+  delete L;
+}
+
+DSV4_API size_t dsv4cuda_moe_device_bytes(const dsv4cuda_moe_layer* L) {
+  return L ? L->owned_bytes + L->ws_bytes : 0;
+}
+
+DSV4_API int dsv4cuda_moe_forward(dsv4cuda_moe_layer* L, const float* x, const int* token_ids,
+                                  int n_tokens, float* out, void* stream) {
+  if (!L || !x || !out || n_tokens < 0) { record_error("dsv4cuda_moe_forward: bad arguments"); return -1; }
+  if (n_tokens > L->max_tokens) {
+    record_error("dsv4cuda_moe_forward: %d tokens exceed max_tokens %d", n_tokens, L->max_tokens);
+    return -1;
+  }
+  if (L->cfg.hash_vocab > 0 && !token_ids) { record_error("hash layer needs token_ids"); return -1; }
+  dsv4::MoeWorkspace ws = L->ws;
+  if (L->timing) {
+    const size_t need = static_cast<size_t>(L->timed + 1) * 4;
+    while (L->events.size() < need) {
+      cudaEvent_t ev;
+      if (cudaEventCreate(&ev) != cudaSuccess) { record_error("cudaEventCreate"); return -1; }
+      L->events.push_back(ev);
+    }
+    ws.timing = &L->events[static_cast<size_t>(L->timed) * 4];
+    L->timed++;
+  }
+  cudaError_t e = dsv4::moe_forward(L->cfg, L->w, ws, x, token_ids, n_tokens, out,
+                                    static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) { record_error("moe_forward: %s", cudaGetErrorString(e)); return -1; }
+  return 0;
+}
+
+DSV4_API int dsv4cuda_moe_timing_begin(dsv4cuda_moe_layer* L) {
+  if (!L) return -1;
+  L->timing = true;
+  L->timed = 0;
+  return 0;
+}
+
+DSV4_API int dsv4cuda_moe_timing_end(dsv4cuda_moe_layer* L, int* n_forwards, float* gateup_ms,
+                                     float* down_ms) {
+  if (!L) return -1;
+  L->timing = false;
+  float gu = 0.f, dn = 0.f;
+  for (int i = 0; i < L->timed; ++i) {
+    float a = 0.f, b = 0.f;
+    if (cudaEventSynchronize(L->events[i * 4 + 3]) != cudaSuccess ||
+        cudaEventElapsedTime(&a, L->events[i * 4 + 0], L->events[i * 4 + 1]) != cudaSuccess ||
+        cudaEventElapsedTime(&b, L->events[i * 4 + 2], L->events[i * 4 + 3]) != cudaSuccess) {
+      record_error("timing events failed");
+      return -1;
+    }
+    gu += a;
+    dn += b;
+  }
+  if (n_forwards) *n_forwards = L->timed;
+  if (gateup_ms) *gateup_ms = gu;
+  if (down_ms) *down_ms = dn;
+  L->timed = 0;
+  return 0;
+}
+
+DSV4_API int dsv4cuda_moe_forward_host(dsv4cuda_moe_layer* L, const float* x, const int* token_ids,
+                                       int n_tokens, float* out) {
+  if (!L || !x || !out || n_tokens < 0 || n_tokens > L->max_tokens) {
+    record_error("dsv4cuda_moe_forward_host: bad arguments");
+    return -1;
+  }
+  if (ensure_thread_state() != 0) return -1;
+  cudaStream_t st = t_state.stream;
+  const size_t bytes = sizeof(float) * n_tokens * L->cfg.hidden;
+  cudaError_t e = cudaMemcpyAsync(L->d_x, x, bytes, cudaMemcpyHostToDevice, st);
+  if (e == cudaSuccess && token_ids)
+    e = cudaMemcpyAsync(L->d_tok, token_ids, sizeof(int) * n_tokens, cudaMemcpyHostToDevice, st);
+  if (e != cudaSuccess) { record_error("H2D: %s", cudaGetErrorString(e)); return -1; }
+  if (dsv4cuda_moe_forward(L, L->d_x, token_ids ? L->d_tok : nullptr, n_tokens, L->d_out, st) != 0)
+    return -1;
+  e = cudaMemcpyAsync(out, L->d_out, bytes, cudaMemcpyDeviceToHost, st);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+  if (e != cudaSuccess) { record_error("D2H: %s", cudaGetErrorString(e)); return -1; }
+  return 0;
+}
+
+DSV4_API int dsv4cuda_moe_last_routes(dsv4cuda_moe_layer* L, int n_tokens, int* idx, float* wt) {
+  if (!L || n_tokens < 0 || n_tokens > L->max_tokens) { record_error("bad arguments"); return -1; }
+  cudaError_t e = cudaDeviceSynchronize();
+  const size_t n = static_cast<size_t>(n_tokens) * L->cfg.topk;
+  if (e == cudaSuccess && idx) e = cudaMemcpy(idx, L->ws.idx, n * sizeof(int), cudaMemcpyDeviceToHost);
+  if (e == cudaSuccess && wt) e = cudaMemcpy(wt, L->ws.wt, n * sizeof(float), cudaMemcpyDeviceToHost);
+  int counters[4] = {0, 0, 0, 0};
+  if (e == cudaSuccess) e = cudaMemcpy(counters, L->ws.counters, sizeof(counters), cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) { record_error("routes: %s", cudaGetErrorString(e)); return -1; }
+  return counters[2];
+}
+
+DSV4_API int dsv4cuda_moe_route(dsv4cuda_moe_layer* L, const float* x, const int* token_ids,
+                                int n_tokens, int public_router, int* idx, float* wt) {
+  if (!L || !x || n_tokens <= 0 || n_tokens > L->max_tokens) { record_error("bad arguments"); return -1; }
+  cudaError_t e = dsv4::moe_route(L->cfg, L->w, L->ws, x, token_ids, n_tokens, public_router, 0);
+  if (e != cudaSuccess) { record_error("route: %s", cudaGetErrorString(e)); return -1; }
+  return dsv4cuda_moe_last_routes(L, n_tokens, idx, wt);
+}

@@ -1,0 +1,96 @@
+// gemv.cuh - work descriptors and launchers for the exact-order GEMV family
+// (FP4 E2M1, FP8 E4M3, BF16 weights), the activation quantiser and the
+// fused SwiGLU quantiser.
+#pragma once
+#include <cstddef>
+#include <cstdint>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+namespace dsv4 {
+
+constexpr int kItemTok = 8;  // tokens one GEMV work item carries
+
+// One (matrix, token set) unit of GEMV work. `mat` selects the matrix
+// (W + mat * mat_stride); tok[i].x indexes the activation rows, tok[i].y the
+// output rows.
+struct TokMap {
+  int x, y;
+};
+struct GemvItem {
+  int mat;
+  int ntok;
+  TokMap tok[kItemTok];
+};
+
+// Quantised activation in device memory: E4M3-grid values stored as f16
+// (exact), one power-of-two scale per 128 columns.
+struct QAct {
+  const __half* x;   // [rows][ld]
+  const float* s;    // [rows][ld / 128]
+  int ld;
+  const float* x32;  // optional fp32 copy [rows][ld]: set when a caller's
+                     // activation is not exactly representable in f16
+};
+
+struct Fp4GemvArgs {
+  const uint8_t* W[2];     // packed E2M1 [rows][in/2] per matrix; W[1] for pairs
+  const uint8_t* S[2];     // E8M0 [rows][in/32]
+  size_t w_stride, s_stride;  // bytes between consecutive matrices (experts)
+  int in, rows;
+  QAct act;
+  float* Y[2];             // [out rows][rows] outputs (BF16-valued floats)
+  const GemvItem* items;
+  const int* n_items;      // device count (<= max_items)
+  int max_items;
+};
+
+struct Fp8GemvArgs {
+  const uint8_t* W[2];     // E4M3 [rows][in]
+  const uint8_t* S[2];     // E8M0 [ceil(rows/128)][ceil(in/128)]
+  size_t w_stride, s_stride;
+  int in, rows;
+  int round_out;
+  QAct act;
+  float* Y[2];
+  const GemvItem* items;
+  const int* n_items;
+  int max_items;
+};
+
+struct Bf16GemvArgs {
+  const uint16_t* W;       // [rows][in]
+  int in, rows;
+  int round_out;
+  const float* x;          // [*][ldx] fp32 activations
+  int ldx;
+  float* Y;                // [*][rows]
+  const GemvItem* items;
+  const int* n_items;
+  int max_items;
+};
+
+cudaError_t launch_fp4_gemv(const Fp4GemvArgs& a, bool pair, int item_tokens,
+                            cudaStream_t st);
+cudaError_t launch_fp8_gemv(const Fp8GemvArgs& a, bool pair, int item_tokens,
+                            cudaStream_t st);
+cudaError_t launch_bf16_gemv(const Bf16GemvArgs& a, int item_tokens,
+                             cudaStream_t st);
+
+// x [rows][n] fp32 -> E4M3 grid (f16) + per-128 scales (dsv4_quant_fp8_codes).
+cudaError_t launch_quant_fp8(const float* x, int ldx, int n, int rows, __half* qx,
+                             float* qs, int ld_out, cudaStream_t st);
+// Same, but also writes the quantised values back as fp32 (drop-in API).
+cudaError_t launch_quant_fp8_f32(const float* x, int n, float* qx, float* qs,
+                                 cudaStream_t st);
+
+// gate/up [rows][n] -> SwiGLU * weight -> BF16 -> FP8 quant (routed_swiglu_quant).
+// weight == nullptr means 1.0 for every row (shared expert).
+cudaError_t launch_swiglu_quant(const float* gate, const float* up, int n, int rows,
+                                const float* weight, int limit, __half* qy, float* qs,
+                                float* y_bf16, cudaStream_t st);
+
+// fp32 activations on the E4M3 grid -> f16 (exact), for host-supplied qx.
+cudaError_t launch_f32_to_f16(const float* x, __half* y, size_t n, cudaStream_t st);
+
+}  // namespace dsv4

@@ -1,0 +1,79 @@
+// moe.cuh - device-resident MoE layer (router, expert permute, grouped
+// expert GEMVs, ordered combine).
+#pragma once
+#include <cstddef>
+#include <cstdint>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include "gemv.cuh"
+
+namespace dsv4 {
+
+enum SharedKind { kSharedNone = 0, kSharedFp8 = 1, kSharedFp4 = 2 };
+
+struct MoeConfig {
+  int hidden, moe_inter, n_experts, topk, swiglu_limit;
+  float route_scale;
+  int shared_kind;   // SharedKind
+  int hash_vocab;    // rows of tid2eid (0 = not a hash layer)
+};
+
+// Device pointers of one layer's weights (reference layouts, expert-major).
+struct MoeWeights {
+  const uint16_t* gate_w;   // [E][H] BF16
+  const float* bias;        // [E] or null
+  const int64_t* tid2eid;   // [hash_vocab][topk] or null
+  const uint8_t *w1, *s1, *w3, *s3, *w2, *s2;     // routed FP4
+  const uint8_t *sh1, *sh1s, *sh3, *sh3s, *sh2, *sh2s;  // shared (FP8 or FP4)
+};
+
+// Scratch for one forward of up to max_tokens tokens. All device memory.
+struct MoeWorkspace {
+  int max_tokens = 0;
+  __half* xq = nullptr;      // [M][H]
+  float* xs = nullptr;       // [M][H/128]
+  double* zd = nullptr;      // [M][E] exact router logits
+  double* zb = nullptr;      // [M][E] bound of the reference's rounding error
+  int* idx = nullptr;        // [M][topk] ascending ids
+  float* wt = nullptr;       // [M][topk]
+  GemvItem* items_gu = nullptr;   // [M*topk]
+  GemvItem* items_dn = nullptr;   // [M*topk]
+  GemvItem* items_sh = nullptr;   // [ceil(M/8)] (static)
+  int* counters = nullptr;   // [0]=n_items, [1]=done CTAs, [2]=tie fallbacks, [3]=n_shared_items
+  float* gate = nullptr;     // [M*topk][I]
+  float* up = nullptr;       // [M*topk][I]
+  __half* qy = nullptr;      // [M*topk][I]
+  float* qys = nullptr;      // [M*topk][I/128]
+  float* routed = nullptr;   // [M*topk][H]
+  float* sh_gate = nullptr;  // [M][I]
+  float* sh_up = nullptr;    // [M][I]
+  __half* sh_qy = nullptr;   // [M][I]
+  float* sh_qys = nullptr;   // [M][I/128]
+  float* shared = nullptr;   // [M][H]
+  size_t bytes = 0;
+  // Optional timing: when set, events are recorded around the routed expert
+  // GEMV launches (gate/up begin/end, down begin/end) on the forward stream.
+  cudaEvent_t* timing = nullptr;
+};
+
+// Bytes a workspace for `max_tokens` needs (256-byte aligned pieces).
+size_t moe_workspace_bytes(const MoeConfig& c, int max_tokens);
+// Carve a workspace out of `base` (>= moe_workspace_bytes bytes).
+void moe_workspace_carve(MoeWorkspace* ws, const MoeConfig& c, int max_tokens, void* base);
+
+// One MoE layer for n_tokens tokens: x [n][H] fp32 (BF16-valued) -> out [n][H]
+// (BF16-valued), per-token results identical to moe_forward
+// (src/dsv4/dsv4_model.c:6599) / moe_forward_batch (:6812).
+// exact_router: 1 = the reference's fused fmaf logits (moe_forward),
+// 2 = the public dsv4_router's separate multiply/add logits.
+cudaError_t moe_forward(const MoeConfig& c, const MoeWeights& w, const MoeWorkspace& ws,
+                        const float* x, const int* token_ids, int n_tokens, float* out,
+                        cudaStream_t st);
+
+// Router only: idx/wt [n][topk] (ids ascending), same numerics as above.
+cudaError_t moe_route(const MoeConfig& c, const MoeWeights& w, const MoeWorkspace& ws,
+                      const float* x, const int* token_ids, int n_tokens, int public_router,
+                      cudaStream_t st);
+
+}  // namespace dsv4

@@ -1,0 +1,290 @@
+"""Python binding of libdsv4_cuda.so (ctypes over the C ABI in
+include/dsv4_cuda.h).
+
+The drop-in kernels mirror the reference's kernel API (same names, argument
+meaning and error behaviour); numpy arrays stand in for the host pointers.
+The device-resident MoE layer takes torch CUDA tensors (data pointers and the
+current stream) - torch here only provides device memory and streams.
+
+There is no CPU fallback: if the library is missing, importing this module
+raises.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+import numpy as np
+
+PKG = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(PKG, "lib", "libdsv4_cuda.so")
+
+if not os.path.exists(LIB_PATH):
+    raise ImportError(f"{LIB_PATH} is missing: run deepseek-v4-flash-0731-in-c_b200/build.py")
+
+lib = C.CDLL(LIB_PATH)
+
+f32p = C.POINTER(C.c_float)
+u8p = C.POINTER(C.c_uint8)
+u16p = C.POINTER(C.c_uint16)
+i32p = C.POINTER(C.c_int)
+i64p = C.POINTER(C.c_int64)
+vp = C.c_void_p
+
+# Every symbol the header declares (checked by tests/test_capi_symbols.py).
+DROPIN = ["dsv4_gemv_bf16", "dsv4_gemv_bf16_batch", "dsv4_gemv_fp8_q", "dsv4_gemv_fp8_batch_q",
+          "dsv4_gemv_fp8_pair_q", "dsv4_gemv_fp4_q", "dsv4_gemv_fp4_batch_q",
+          "dsv4_gemv_fp4_pair_q", "dsv4_quant_fp8_codes", "dsv4_quant_fp8_act", "dsv4_router"]
+
+lib.dsv4cuda_last_error.restype = C.c_char_p
+lib.dsv4cuda_set_abort_on_error.restype = C.c_int
+lib.dsv4cuda_set_abort_on_error.argtypes = [C.c_int]
+lib.dsv4cuda_init.restype = C.c_int
+lib.dsv4cuda_init.argtypes = [C.c_int]
+lib.dsv4_router.argtypes = [i32p, f32p, f32p, vp, f32p, i64p, C.c_int, C.c_int, C.c_int,
+                            C.c_int, C.c_int, C.c_float, C.c_float]
+lib.dsv4cuda_moe_create.restype = C.c_int
+lib.dsv4cuda_moe_create_device.restype = C.c_int
+lib.dsv4cuda_moe_forward.restype = C.c_int
+lib.dsv4cuda_moe_forward.argtypes = [vp, vp, vp, C.c_int, vp, vp]
+lib.dsv4cuda_moe_forward_host.restype = C.c_int
+lib.dsv4cuda_moe_forward_host.argtypes = [vp, f32p, i32p, C.c_int, f32p]
+lib.dsv4cuda_moe_last_routes.restype = C.c_int
+lib.dsv4cuda_moe_last_routes.argtypes = [vp, C.c_int, i32p, f32p]
+lib.dsv4cuda_moe_route.restype = C.c_int
+lib.dsv4cuda_moe_route.argtypes = [vp, vp, vp, C.c_int, C.c_int, i32p, f32p]
+lib.dsv4cuda_moe_destroy.argtypes = [vp]
+lib.dsv4cuda_moe_device_bytes.restype = C.c_size_t
+lib.dsv4cuda_moe_device_bytes.argtypes = [vp]
+
+
+class Dsv4CudaError(RuntimeError):
+    pass
+
+
+def last_error() -> str:
+    return lib.dsv4cuda_last_error().decode()
+
+
+def _check(rc):
+    if rc < 0:
+        raise Dsv4CudaError(last_error())
+    return rc
+
+
+def _p(a, t):
+    return None if a is None else a.ctypes.data_as(t)
+
+
+def _f32(a):
+    return np.ascontiguousarray(a, dtype=np.float32)
+
+
+def _ptrs(arrs, t):
+    return (t * len(arrs))(*[a.ctypes.data_as(t) for a in arrs])
+
+
+def set_abort_on_error(flag: bool) -> int:
+    return lib.dsv4cuda_set_abort_on_error(1 if flag else 0)
+
+
+def init(device: int = 0):
+    _check(lib.dsv4cuda_init(device))
+
+
+# ------------------------------------------------------ drop-in kernels --
+def quant_fp8_codes(x):
+    x = _f32(x)
+    n = x.size
+    qx = np.empty(n, np.float32)
+    qs = np.empty((n + 127) // 128, np.float32)
+    lib.dsv4_quant_fp8_codes(_p(qx, f32p), _p(qs, f32p), _p(x, f32p), n)
+    return qx, qs
+
+
+def gemv_bf16(x, W, round_out=1):
+    out, inn = W.shape
+    y = np.empty(out, np.float32)
+    lib.dsv4_gemv_bf16(_p(y, f32p), _p(_f32(x), f32p), _p(W, u16p), inn, out, round_out)
+    return y
+
+
+def gemv_bf16_batch(xs, W, round_out=1):
+    out, inn = W.shape
+    xs = [_f32(x) for x in xs]
+    ys = [np.empty(out, np.float32) for _ in xs]
+    lib.dsv4_gemv_bf16_batch(_ptrs(ys, f32p), _ptrs(xs, f32p), len(xs), _p(W, u16p), inn, out,
+                             round_out)
+    return np.stack(ys)
+
+
+def gemv_fp8_q(qx, qs, W, S, round_out=1):
+    out, inn = W.shape
+    y = np.empty(out, np.float32)
+    lib.dsv4_gemv_fp8_q(_p(y, f32p), _p(_f32(qx), f32p), _p(_f32(qs), f32p), _p(W, u8p),
+                        _p(S, u8p), inn, out, round_out)
+    return y
+
+
+def gemv_fp8_batch_q(qxs, qss, W, S, round_out=1):
+    out, inn = W.shape
+    qxs = [_f32(a) for a in qxs]
+    qss = [_f32(a) for a in qss]
+    ys = [np.empty(out, np.float32) for _ in qxs]
+    lib.dsv4_gemv_fp8_batch_q(_ptrs(ys, f32p), _ptrs(qxs, f32p), _ptrs(qss, f32p), len(qxs),
+                              _p(W, u8p), _p(S, u8p), inn, out, round_out)
+    return np.stack(ys)
+
+
+def gemv_fp8_pair_q(qx, qs, W0, S0, W1, S1):
+    out, inn = W0.shape
+    y0 = np.empty(out, np.float32)
+    y1 = np.empty(out, np.float32)
+    lib.dsv4_gemv_fp8_pair_q(_p(y0, f32p), _p(y1, f32p), _p(_f32(qx), f32p), _p(_f32(qs), f32p),
+                             _p(W0, u8p), _p(S0, u8p), _p(W1, u8p), _p(S1, u8p), inn, out)
+    return y0, y1
+
+
+def gemv_fp4_q(qx, qs, W, S, inn):
+    rows = W.shape[0]
+    y = np.empty(rows, np.float32)
+    lib.dsv4_gemv_fp4_q(_p(y, f32p), _p(_f32(qx), f32p), _p(_f32(qs), f32p), _p(W, u8p),
+                        _p(S, u8p), inn, rows)
+    return y
+
+
+def gemv_fp4_batch_q(qxs, qss, W, S, inn):
+    rows = W.shape[0]
+    qxs = [_f32(a) for a in qxs]
+    qss = [_f32(a) for a in qss]
+    ys = [np.empty(rows, np.float32) for _ in qxs]
+    lib.dsv4_gemv_fp4_batch_q(_ptrs(ys, f32p), _ptrs(qxs, f32p), _ptrs(qss, f32p), len(qxs),
+                              _p(W, u8p), _p(S, u8p), inn, rows)
+    return np.stack(ys)
+
+
+def gemv_fp4_pair_q(qx, qs, W0, S0, W1, S1, inn):
+    rows = W0.shape[0]
+    y0 = np.empty(rows, np.float32)
+    y1 = np.empty(rows, np.float32)
+    lib.dsv4_gemv_fp4_pair_q(_p(y0, f32p), _p(y1, f32p), _p(_f32(qx), f32p), _p(_f32(qs), f32p),
+                             _p(W0, u8p), _p(S0, u8p), _p(W1, u8p), _p(S1, u8p), inn, rows)
+    return y0, y1
+
+
+def router_public(x, gate, bias, topk, route_scale, tid2eid=None, token_id=0):
+    ne, hid = gate.shape
+    idx = np.empty(topk, np.int32)
+    wt = np.empty(topk, np.float32)
+    lib.dsv4_router(_p(idx, i32p), _p(wt, f32p), _p(_f32(x), f32p), gate.ctypes.data,
+                    _p(bias, f32p), _p(tid2eid, i64p), token_id, hid, ne, topk,
+                    1 if tid2eid is not None else 0, route_scale, 1e-6)
+    return idx, wt
+
+
+# ------------------------------------------------------------ MoE layer --
+class MoeConfig(C.Structure):
+    _fields_ = [("hidden", C.c_int), ("moe_inter", C.c_int), ("n_experts", C.c_int),
+                ("topk", C.c_int), ("swiglu_limit", C.c_int), ("route_scale", C.c_float),
+                ("shared_kind", C.c_int), ("hash_vocab", C.c_int)]
+
+
+class MoeWeights(C.Structure):
+    _fields_ = [("gate_w", vp), ("bias", vp), ("tid2eid", vp)] + \
+        [(n, vp) for n in ("w1", "s1", "w3", "s3", "w2", "s2",
+                           "sh1", "sh1s", "sh3", "sh3s", "sh2", "sh2s")]
+
+
+SHARED_NONE, SHARED_FP8, SHARED_FP4 = 0, 1, 2
+
+
+def _addr(a):
+    if a is None:
+        return None
+    if hasattr(a, "data_ptr"):
+        return a.data_ptr()
+    return a.ctypes.data
+
+
+class MoeLayer:
+    """One MoE layer resident in HBM (dsv4cuda_moe_*).
+
+    `layer` is the dict produced by oracle.make_moe_layer or any dict with the
+    same keys holding numpy arrays (copied in) or torch CUDA tensors
+    (adopted, device=True).
+    """
+
+    def __init__(self, layer: dict, max_tokens: int = 8, device: bool = False):
+        sh = layer.get("shared")
+        kind = SHARED_NONE if sh is None else (SHARED_FP8 if sh["fp8"] else SHARED_FP4)
+        tid = layer.get("tid2eid")
+        self.cfg = MoeConfig(layer["hidden"], layer["moe_inter"], layer["n_experts"],
+                             layer["topk"], layer["swiglu_limit"], layer["route_scale"], kind,
+                             0 if tid is None else int(tid.shape[0]))
+        w = MoeWeights()
+        w.gate_w = _addr(layer["gate_w"])
+        w.bias = _addr(layer.get("bias"))
+        w.tid2eid = _addr(tid)
+        for n in ("w1", "s1", "w3", "s3", "w2", "s2"):
+            setattr(w, n, _addr(layer[n]))
+        if sh is not None:
+            for n, m in (("sh1", "w1"), ("sh1s", "s1"), ("sh3", "w3"), ("sh3s", "s3"),
+                         ("sh2", "w2"), ("sh2s", "s2")):
+                setattr(w, n, _addr(sh[m]))
+        self._keep = layer
+        self.max_tokens = max_tokens
+        self.handle = C.c_void_p()
+        fn = lib.dsv4cuda_moe_create_device if device else lib.dsv4cuda_moe_create
+        _check(fn(C.byref(self.handle), C.byref(self.cfg), C.byref(w), max_tokens))
+        self.hidden = layer["hidden"]
+        self.topk = layer["topk"]
+
+    def close(self):
+        if self.handle:
+            lib.dsv4cuda_moe_destroy(self.handle)
+            self.handle = C.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    @property
+    def device_bytes(self) -> int:
+        return lib.dsv4cuda_moe_device_bytes(self.handle)
+
+    def forward_host(self, x, token_ids=None):
+        x = _f32(np.atleast_2d(x))
+        n = x.shape[0]
+        out = np.empty_like(x)
+        tok = None if token_ids is None else np.ascontiguousarray(token_ids, dtype=np.int32)
+        _check(lib.dsv4cuda_moe_forward_host(self.handle, _p(x, f32p), _p(tok, i32p), n,
+                                             _p(out, f32p)))
+        return out
+
+    def forward(self, x, out, token_ids=None, stream=None):
+        """x/out: torch CUDA float32 [n][H]; token_ids: torch CUDA int32 [n]."""
+        if stream is None:
+            import torch
+            stream = torch.cuda.current_stream().cuda_stream
+        _check(lib.dsv4cuda_moe_forward(self.handle, x.data_ptr(),
+                                        None if token_ids is None else token_ids.data_ptr(),
+                                        x.shape[0], out.data_ptr(), stream))
+
+    def last_routes(self, n_tokens):
+        idx = np.empty((n_tokens, self.topk), np.int32)
+        wt = np.empty((n_tokens, self.topk), np.float32)
+        fallbacks = _check(lib.dsv4cuda_moe_last_routes(self.handle, n_tokens, _p(idx, i32p),
+                                                        _p(wt, f32p)))
+        return idx, wt, fallbacks
+
+    def route(self, x, token_ids=None, public_router=False):
+        """x: torch CUDA float32 [n][H]."""
+        n = x.shape[0]
+        idx = np.empty((n, self.topk), np.int32)
+        wt = np.empty((n, self.topk), np.float32)
+        fallbacks = _check(lib.dsv4cuda_moe_route(
+            self.handle, x.data_ptr(), None if token_ids is None else token_ids.data_ptr(), n,
+            1 if public_router else 0, _p(idx, i32p), _p(wt, f32p)))
+        return idx, wt, fallbacks

@@ -1,0 +1,211 @@
+/*
+ * dsv4_cuda.h - C ABI of libdsv4_cuda.so, the B200 (sm_100a) implementation
+ * of the DeepSeek-V4-Flash decode hot path of deepseek-v4-flash-0731-in-c.
+ *
+ * Three layers, all plain C types (no torch, no C++ in the signatures):
+ *
+ *  1. Drop-in kernel symbols. Same names, signatures, argument meaning and
+ *     error behaviour as the reference's kernel ABI, host pointers in and
+ *     out; each call stages its operands through device memory and returns
+ *     bit-identical results. A host program links (or LD_PRELOADs) this
+ *     library in place of the reference's definitions. Every one is also
+ *     exported with a dsv4cuda_ prefix so both can live in one process.
+ *  2. Device-resident entry points (dsv4cuda_*): device pointers and a CUDA
+ *     stream, int status (0 = ok, negative = error), never abort.
+ *  3. Lifecycle and error reporting.
+ *
+ * Each drop-in declaration cites the reference interface it replaces as
+ * path:line inside the reference project.
+ */
+#ifndef DSV4_CUDA_H
+#define DSV4_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ------------------------------------------------ 1. drop-in kernel ABI --
+ * Host pointers. Activations are floats on the E4M3 grid (qx) with one
+ * power-of-two scale per 128 columns (qscale); weight scales are E8M0 codes.
+ * A batch above 33 prints the reference's message and exits(1), as the
+ * reference does; a CUDA failure prints "dsv4_cuda: ..." and exits(1) unless
+ * dsv4cuda_set_abort_on_error(0) was called (then the error is recorded and
+ * the outputs are left unspecified).
+ */
+
+/* src/dsv4/dsv4_internal.h:257 (defined src/dsv4/dsv4_model.c:266) */
+void dsv4_gemv_bf16(float *y, const float *x, const uint16_t *W, int in, int out,
+                    int round_out);
+/* src/dsv4/dsv4_internal.h:259 (src/dsv4/dsv4_model.c:308) */
+void dsv4_gemv_bf16_batch(float *const *y, const float *const *x, int batch,
+                          const uint16_t *W, int in, int out, int round_out);
+/* src/dsv4/dsv4_internal.h:263 (src/dsv4/dsv4_model.c:571) */
+void dsv4_gemv_fp8_q(float *y, const float *qx, const float *qscale,
+                     const uint8_t *W, const uint8_t *wscale_code,
+                     int in, int out, int round_out);
+/* src/dsv4/dsv4_internal.h:266 (src/dsv4/dsv4_model.c:678) */
+void dsv4_gemv_fp8_batch_q(float *const *y, const float *const *qx,
+                           const float *const *qscale, int batch,
+                           const uint8_t *W, const uint8_t *wscale_code,
+                           int in, int out, int round_out);
+/* src/dsv4/dsv4_internal.h:270 (src/dsv4/dsv4_model.c:809) */
+void dsv4_gemv_fp8_pair_q(float *y0, float *y1, const float *qx,
+                          const float *qscale, const uint8_t *W0,
+                          const uint8_t *S0, const uint8_t *W1,
+                          const uint8_t *S1, int in, int out);
+/* src/dsv4/dsv4_internal.h:276 (src/dsv4/dsv4_model.c:967) */
+void dsv4_gemv_fp4_q(float *y, const float *qx, const float *qscale,
+                     const uint8_t *W, const uint8_t *wscale_code,
+                     int in, int rows);
+/* src/dsv4/dsv4_internal.h:279 (src/dsv4/dsv4_model.c:1080) */
+void dsv4_gemv_fp4_batch_q(float *const *y, const float *const *qx,
+                           const float *const *qscale, int batch,
+                           const uint8_t *W, const uint8_t *wscale_code,
+                           int in, int rows);
+/* src/dsv4/dsv4_internal.h:283 (src/dsv4/dsv4_model.c:1220) */
+void dsv4_gemv_fp4_pair_q(float *y0, float *y1, const float *qx,
+                          const float *qscale, const uint8_t *W0,
+                          const uint8_t *S0, const uint8_t *W1,
+                          const uint8_t *S1, int in, int rows);
+/* src/dsv4/dsv4_internal.h:327 (src/dsv4/dsv4_model.c:5580) */
+void dsv4_quant_fp8_codes(float *qx, float *qscale, const float *x, int n);
+/* include/dsv4/dsv4.h:195 (src/dsv4/dsv4_ops.c:122) - same arithmetic */
+void dsv4_quant_fp8_act(float *out, float *scales, const float *x, int n);
+/* include/dsv4/dsv4.h:251 (src/dsv4/dsv4_ops.c:473). `gate` is declared
+ * float* like the reference but read as a BF16 [n_experts][hidden] matrix,
+ * as the reference does (src/dsv4/dsv4_ops.c:494, :502). */
+void dsv4_router(int *idx, float *wt, const float *x, const float *gate,
+                 const float *bias, const int64_t *tid2eid, int token_id,
+                 int hidden, int n_experts, int topk, int hash_layer,
+                 float route_scale, float rms_eps);
+
+/* Prefixed aliases of the nine model-path kernels above. */
+void dsv4cuda_gemv_bf16(float *y, const float *x, const uint16_t *W, int in,
+                        int out, int round_out);
+void dsv4cuda_gemv_bf16_batch(float *const *y, const float *const *x, int batch,
+                              const uint16_t *W, int in, int out, int round_out);
+void dsv4cuda_gemv_fp8_q(float *y, const float *qx, const float *qscale,
+                         const uint8_t *W, const uint8_t *wscale_code, int in,
+                         int out, int round_out);
+void dsv4cuda_gemv_fp8_batch_q(float *const *y, const float *const *qx,
+                               const float *const *qscale, int batch,
+                               const uint8_t *W, const uint8_t *wscale_code,
+                               int in, int out, int round_out);
+void dsv4cuda_gemv_fp8_pair_q(float *y0, float *y1, const float *qx,
+                              const float *qscale, const uint8_t *W0,
+                              const uint8_t *S0, const uint8_t *W1,
+                              const uint8_t *S1, int in, int out);
+void dsv4cuda_gemv_fp4_q(float *y, const float *qx, const float *qscale,
+                         const uint8_t *W, const uint8_t *wscale_code, int in,
+                         int rows);
+void dsv4cuda_gemv_fp4_batch_q(float *const *y, const float *const *qx,
+                               const float *const *qscale, int batch,
+                               const uint8_t *W, const uint8_t *wscale_code,
+                               int in, int rows);
+void dsv4cuda_gemv_fp4_pair_q(float *y0, float *y1, const float *qx,
+                              const float *qscale, const uint8_t *W0,
+                              const uint8_t *S0, const uint8_t *W1,
+                              const uint8_t *S1, int in, int rows);
+void dsv4cuda_quant_fp8_codes(float *qx, float *qscale, const float *x, int n);
+
+/* ---------------------------------------------------- 3. lifecycle -- */
+
+/* Select the CUDA device for the calling thread's drop-in calls and create
+ * its stream and staging buffers. Optional: the first call on a thread does
+ * it for the current device. Returns 0 or a negative error. */
+int dsv4cuda_init(int device);
+/* Release the calling thread's stream and staging buffers. */
+void dsv4cuda_shutdown(void);
+/* Last error recorded on the calling thread ("" if none). */
+const char *dsv4cuda_last_error(void);
+/* 1 (default): a drop-in call that hits a CUDA error exits(1) like the
+ * reference's fatal paths; 0: record the error and return. Returns the
+ * previous mode. */
+int dsv4cuda_set_abort_on_error(int abort_on_error);
+
+/* ------------------------------------ 2. device-resident MoE layer -- */
+
+/* Shared expert formats. */
+#define DSV4CUDA_SHARED_NONE 0
+#define DSV4CUDA_SHARED_FP8 1 /* the reference's [128x128]-block FP8 expert */
+#define DSV4CUDA_SHARED_FP4 2 /* same layout as a routed FP4 expert */
+
+typedef struct {
+    int hidden;        /* H  */
+    int moe_inter;     /* I  */
+    int n_experts;     /* E  */
+    int topk;          /* k <= 32 */
+    int swiglu_limit;  /* (int)cfg.swiglu_limit, as the reference casts it */
+    float route_scale;
+    int shared_kind;   /* DSV4CUDA_SHARED_* */
+    int hash_vocab;    /* rows of tid2eid for a hash layer, else 0 */
+} dsv4cuda_moe_config;
+
+/* Weights in the reference's layouts. Routed experts are expert-major:
+ * w1/w3 [E][I][H/2] packed E2M1 (low nibble first) with s1/s3 [E][I][H/32]
+ * E8M0; w2 [E][H][I/2] with s2 [E][H][I/32]. gate_w [E][H] BF16; bias [E]
+ * f32 or NULL; tid2eid [hash_vocab][topk] int64 or NULL. Shared FP8:
+ * sh1/sh3 [I][H] E4M3 with [ceil(I/128)][ceil(H/128)] E8M0, sh2 [H][I]
+ * with [ceil(H/128)][ceil(I/128)]; shared FP4: routed layout without [E]. */
+typedef struct {
+    const uint16_t *gate_w;
+    const float *bias;
+    const int64_t *tid2eid;
+    const uint8_t *w1, *s1, *w3, *s3, *w2, *s2;
+    const uint8_t *sh1, *sh1s, *sh3, *sh3s, *sh2, *sh2s;
+} dsv4cuda_moe_weights;
+
+typedef struct dsv4cuda_moe_layer dsv4cuda_moe_layer;
+
+/* Replaces the per-layer weight binding + expert cache feeding moe_forward
+ * (src/dsv4/dsv4_model.c:1793-2056, :3642): copies every weight of the layer
+ * from host memory into HBM once. max_tokens bounds one forward's batch. */
+int dsv4cuda_moe_create(dsv4cuda_moe_layer **out, const dsv4cuda_moe_config *cfg,
+                        const dsv4cuda_moe_weights *host_weights, int max_tokens);
+/* Same, adopting weights that already live in device memory (not copied,
+ * not freed by destroy). */
+int dsv4cuda_moe_create_device(dsv4cuda_moe_layer **out,
+                               const dsv4cuda_moe_config *cfg,
+                               const dsv4cuda_moe_weights *device_weights,
+                               int max_tokens);
+void dsv4cuda_moe_destroy(dsv4cuda_moe_layer *L);
+
+/* moe_forward / moe_forward_batch (src/dsv4/dsv4_model.c:6599, :6812): x
+ * [n][H] device fp32 (BF16-valued) -> out [n][H] device, per token
+ * identical to the reference's single-token result. token_ids (device,
+ * [n]) is read only by hash layers and may be NULL otherwise. stream is a
+ * cudaStream_t (NULL = default stream). Asynchronous. */
+int dsv4cuda_moe_forward(dsv4cuda_moe_layer *L, const float *x, const int *token_ids,
+                         int n_tokens, float *out, void *stream);
+/* The same call with HOST buffers: copies x/token_ids in, runs, copies out
+ * and synchronises (the reference-facing end-to-end path). */
+int dsv4cuda_moe_forward_host(dsv4cuda_moe_layer *L, const float *x,
+                              const int *token_ids, int n_tokens, float *out);
+/* Routing of the last forward on L: idx/wt [n][topk] (ids ascending), host
+ * buffers; synchronises. Returns the number of tokens (since the layer was
+ * created) whose top-k needed the exact fp32 logit replay of a near tie,
+ * or a negative error. */
+int dsv4cuda_moe_last_routes(dsv4cuda_moe_layer *L, int n_tokens, int *idx, float *wt);
+/* Router alone (device x), writing host idx/wt. public_router selects the
+ * public dsv4_router() numerics instead of moe_forward's. */
+int dsv4cuda_moe_route(dsv4cuda_moe_layer *L, const float *x, const int *token_ids,
+                       int n_tokens, int public_router, int *idx, float *wt);
+/* Expert-GEMV timing for roofline measurement: between _begin and _end,
+ * every dsv4cuda_moe_forward on L records CUDA events around its routed
+ * gate/up and down GEMV launches (not inside graph capture). _end waits for
+ * them and returns the number of timed forwards and the summed milliseconds
+ * of the two launches. */
+int dsv4cuda_moe_timing_begin(dsv4cuda_moe_layer *L);
+int dsv4cuda_moe_timing_end(dsv4cuda_moe_layer *L, int *n_forwards, float *gateup_ms,
+                            float *down_ms);
+/* Device bytes the layer holds (weights it owns + workspace). */
+size_t dsv4cuda_moe_device_bytes(const dsv4cuda_moe_layer *L);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* DSV4_CUDA_H */
