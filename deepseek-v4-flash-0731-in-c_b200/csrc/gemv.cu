@@ -608,7 +608,7 @@ int sm_count() {
 int pick_lpr(long long rows_total, int chunks_per_row) {
   const long long want_warps = 12LL * sm_count();
   int lpr = 1;
-  while (lpr < 4 && (rows_total * lpr) / 32 < want_warps && chunks_per_row % (2 * lpr) == 0)
+  while (lpr < 4 && (rows_total * lpr) / 32 < want_warps && chunks_per_row % (4 * lpr) == 0)
     lpr *= 2;
   return lpr;
 }

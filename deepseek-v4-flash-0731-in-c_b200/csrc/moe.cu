@@ -196,9 +196,11 @@ __global__ void __launch_bounds__(kSelThreads) router_select_kernel(const Select
 
   if (hash) {
     if (threadIdx.x == 0) {
-      const int tk = tok < a.hash_vocab ? tok : 0;
-      for (int k = 0; k < a.topk; ++k)
-        order[k] = static_cast<int>(a.tid2eid[static_cast<size_t>(tk) * a.topk + k]);
+      const int tk = (tok >= 0 && tok < a.hash_vocab) ? tok : 0;
+      for (int k = 0; k < a.topk; ++k) {
+        const int64_t e = a.tid2eid[static_cast<size_t>(tk) * a.topk + k];
+        order[k] = (e >= 0 && e < E) ? static_cast<int>(e) : -1;
+      }
     }
     __syncthreads();
   } else {
