@@ -53,11 +53,17 @@ def parse():
     ap.add_argument("--tokens", type=int, default=1, help="tokens per step (M)")
     ap.add_argument("--layers", type=int, default=4, help="independent layer weight sets")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    ap.add_argument("--experts", type=int, default=E,
+                    help="routed experts per layer (smaller only for profiling captures)")
+    ap.add_argument("--inter", type=int, default=I,
+                    help="expert intermediate size (smaller only for profiling captures)")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end leg")
     return ap.parse_args()
 
 
 # ---------------------------------------------------------------- weights --
-def make_device_layer(torch, seed, dev):
+def make_device_layer(torch, seed, dev, E=E, I=I):
     """Random-init config-2 layer in the reference layouts, on the GPU."""
     g = torch.Generator(device=dev)
     g.manual_seed(seed)
@@ -266,7 +272,7 @@ def main():
     M = args.tokens
     layers = []
     for li in range(args.layers):
-        lay = make_device_layer(torch, 1000 + li, dev)
+        lay = make_device_layer(torch, 1000 + li, dev, args.experts, args.inter)
         layers.append((lay, dsv4cuda.MoeLayer(lay, max_tokens=M, device=True)))
     torch.cuda.synchronize()
     rng = np.random.default_rng(7)
@@ -326,29 +332,32 @@ def main():
 
     # ---- expert-GEMV roofline: the same forward, ungraphed, with events
     # around the routed gate/up and down launches on the forward stream
-    U_total, n_fw = 0, 0
+    U_total, n_fw, fallbacks = 0, 0, 0
     lib = dsv4cuda.lib
     for li, (_, L) in enumerate(layers):
         lib.dsv4cuda_moe_timing_begin(L.handle)
-    gu_ms = dn_ms = 0.0
+    gu_ms = dn_ms = lg_ms = sl_ms = 0.0
     n_timed = 0
     with torch.cuda.stream(stream):
         for i in range(max(8, args.steps // 4)):
             _, L = layers[i % len(layers)]
             xin.copy_(x_dev[i % pool])
             L.forward(xin, out_dev, stream=stream.cuda_stream)
-            idx, _, _ = L.last_routes(M)
+            idx, _, fb = L.last_routes(M)
             U_total += len(np.unique(idx))
+            fallbacks = fb
             n_fw += 1
     torch.cuda.synchronize()
     import ctypes as C
     for _, L in layers:
         n = C.c_int()
-        a = C.c_float()
-        b = C.c_float()
-        lib.dsv4cuda_moe_timing_end(L.handle, C.byref(n), C.byref(a), C.byref(b))
+        a, b, c, d = C.c_float(), C.c_float(), C.c_float(), C.c_float()
+        lib.dsv4cuda_moe_timing_end2(L.handle, C.byref(n), C.byref(a), C.byref(b), C.byref(c),
+                                     C.byref(d))
         gu_ms += a.value
         dn_ms += b.value
+        lg_ms += c.value
+        sl_ms += d.value
         n_timed += n.value
     U_avg = U_total / max(n_fw, 1)
     alg_bytes = U_avg * EXPERT_BYTES
@@ -361,6 +370,60 @@ def main():
         peak_src = "measured"
 
     # ---- end to end through the public C API with host buffers
+    e2e_val = None
+    if not args.no_e2e:
+        e2e_val = run_e2e(args, layers, x_host, M, pool, lib, dsv4cuda)
+
+    line = None
+    if rank == 0:
+        cpu = None
+        if world == 1 and not args.no_cpu:
+            try:
+                tps, cores, kind, sample = cpu_reference_run(args.cpu_seconds)
+                cpu = {"value": tps, "unit": "tok/s", "cores": cores, "kind": kind,
+                       "sample": sample}
+            except Exception as exc:  # report, do not hide
+                cpu = {"value": None, "unit": "tok/s", "cores": 0, "kind": "reference",
+                       "sample": f"failed: {exc}"}
+        line = {
+            "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "fp4e2m1*e4m3->f32", "data": "synthetic",
+            "config": {"workload": "config 2 MoE layer op, decode M=%d" % M, "hidden": H,
+                       "moe_inter": I, "experts": args.experts, "topk": TOPK, "shared": "fp8",
+                       "tokens_per_step": M, "layers_cycled": args.layers,
+                       "l2": "inputs larger than L2: each step reads a different layer's "
+                             "~235 MB of weights", "parallelism": f"ep{world}"},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "traffic": None,
+                         "kernel": "fp4_gemv_kernel (routed gate/up pair + down)",
+                         "alg_bytes_per_step": alg_bytes, "peak_source": peak_src,
+                         "kernel_ms_per_step": kern_ms,
+                         "phase_ms_per_step": {
+                             "router_logits": lg_ms / max(n_timed, 1),
+                             "router_select": sl_ms / max(n_timed, 1),
+                             "expert_gateup": gu_ms / max(n_timed, 1),
+                             "expert_down": dn_ms / max(n_timed, 1)}},
+            "cpu_baseline": cpu,
+            "e2e": {"value": e2e_val, "unit": "tok/s", "h2d_bytes_per_step": M * H * 4,
+                    "d2h_bytes_per_step": M * H * 4},
+            "gpu_launches": 9 * args.steps,
+            "router_tie_fallbacks": fallbacks,
+            "clocks": clk,
+        }
+        print(json.dumps(line), flush=True)
+    for _, L in layers:
+        L.close()
+    del graphs
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def run_e2e(args, layers, x_host, M, pool, lib, dsv4cuda):
+    import ctypes as C
+    import torch
     pin_x = torch.from_numpy(x_host).pin_memory()
     pin_out = torch.empty((M, H), dtype=torch.float32).pin_memory()
     L0 = layers[0][1]
@@ -380,46 +443,7 @@ def main():
             raise RuntimeError(dsv4cuda.last_error())
     e2e_s = time.perf_counter() - t0
     e2e_val = M * e2e_steps / e2e_s
-
-    line = None
-    if rank == 0:
-        cpu = None
-        if world == 1:
-            try:
-                tps, cores, kind, sample = cpu_reference_run(args.cpu_seconds)
-                cpu = {"value": tps, "unit": "tok/s", "cores": cores, "kind": kind,
-                       "sample": sample}
-            except Exception as exc:  # report, do not hide
-                cpu = {"value": None, "unit": "tok/s", "cores": 0, "kind": "reference",
-                       "sample": f"failed: {exc}"}
-        line = {
-            "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
-            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
-            "dtype": "fp4e2m1*e4m3->f32", "data": "synthetic",
-            "config": {"workload": "config 2 MoE layer op, decode M=%d" % M, "hidden": H,
-                       "moe_inter": I, "experts": E, "topk": TOPK, "shared": "fp8",
-                       "tokens_per_step": M, "layers_cycled": args.layers,
-                       "l2": "inputs larger than L2: each step reads a different layer's "
-                             "~235 MB of weights", "parallelism": f"ep{world}"},
-            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                         "frac": achieved / peak, "traffic": None,
-                         "kernel": "fp4_gemv_kernel (routed gate/up pair + down)",
-                         "alg_bytes_per_step": alg_bytes, "peak_source": peak_src,
-                         "kernel_ms_per_step": kern_ms},
-            "cpu_baseline": cpu,
-            "e2e": {"value": e2e_val, "unit": "tok/s", "h2d_bytes_per_step": M * H * 4,
-                    "d2h_bytes_per_step": M * H * 4},
-            "gpu_launches": 12 * args.steps,
-            "clocks": clk,
-        }
-        print(json.dumps(line), flush=True)
-    for _, L in layers:
-        L.close()
-    del graphs
-    if dist:
-        dist.barrier()
-        dist.destroy_process_group()
+    return e2e_val
 
 
 if __name__ == "__main__":

@@ -15,6 +15,7 @@
 
 #include <cuda_fp16.h>
 
+#include "bulk.cuh"
 #include "dsv4_common.cuh"
 #include "gemv.cuh"
 #include "moe.cuh"
@@ -393,6 +394,17 @@ DSV4_API int dsv4cuda_init(int device) {
 
 DSV4_API const char* dsv4cuda_last_error(void) { return t_last_error.c_str(); }
 
+DSV4_API int dsv4cuda_device_error(unsigned int* flags, int clear) {
+  unsigned int* w = dsv4::device_error_word();
+  if (!w) { record_error("device error word unavailable"); return -1; }
+  unsigned int v = 0;
+  cudaError_t e = cudaMemcpy(&v, w, sizeof(v), cudaMemcpyDeviceToHost);
+  if (e == cudaSuccess && clear) e = cudaMemset(w, 0, sizeof(v));
+  if (e != cudaSuccess) { record_error("device error word: %s", cudaGetErrorString(e)); return -1; }
+  if (flags) *flags = v;
+  return 0;
+}
+
 DSV4_API int dsv4cuda_set_abort_on_error(int abort_on_error) {
   return g_abort.exchange(abort_on_error ? 1 : 0);
 }
@@ -672,13 +684,13 @@ DSV4_API int dsv4cuda_moe_forward(dsv4cuda_moe_layer* L, const float* x, const i
   if (L->cfg.hash_vocab > 0 && !token_ids) { record_error("hash layer needs token_ids"); return -1; }
   dsv4::MoeWorkspace ws = L->ws;
   if (L->timing) {
-    const size_t need = static_cast<size_t>(L->timed + 1) * 4;
+    const size_t need = static_cast<size_t>(L->timed + 1) * 8;
     while (L->events.size() < need) {
       cudaEvent_t ev;
       if (cudaEventCreate(&ev) != cudaSuccess) { record_error("cudaEventCreate"); return -1; }
       L->events.push_back(ev);
     }
-    ws.timing = &L->events[static_cast<size_t>(L->timed) * 4];
+    ws.timing = &L->events[static_cast<size_t>(L->timed) * 8];
     L->timed++;
   }
   cudaError_t e = dsv4::moe_forward(L->cfg, L->w, ws, x, token_ids, n_tokens, out,
@@ -694,27 +706,39 @@ DSV4_API int dsv4cuda_moe_timing_begin(dsv4cuda_moe_layer* L) {
   return 0;
 }
 
-DSV4_API int dsv4cuda_moe_timing_end(dsv4cuda_moe_layer* L, int* n_forwards, float* gateup_ms,
-                                     float* down_ms) {
+DSV4_API int dsv4cuda_moe_timing_end2(dsv4cuda_moe_layer* L, int* n_forwards, float* gateup_ms,
+                                      float* down_ms, float* logits_ms, float* select_ms) {
   if (!L) return -1;
   L->timing = false;
-  float gu = 0.f, dn = 0.f;
+  float gu = 0.f, dn = 0.f, lg = 0.f, sl = 0.f;
   for (int i = 0; i < L->timed; ++i) {
-    float a = 0.f, b = 0.f;
-    if (cudaEventSynchronize(L->events[i * 4 + 3]) != cudaSuccess ||
-        cudaEventElapsedTime(&a, L->events[i * 4 + 0], L->events[i * 4 + 1]) != cudaSuccess ||
-        cudaEventElapsedTime(&b, L->events[i * 4 + 2], L->events[i * 4 + 3]) != cudaSuccess) {
+    float a = 0.f, b = 0.f, c = 0.f, d = 0.f;
+    cudaEvent_t* ev = &L->events[static_cast<size_t>(i) * 8];
+    if (cudaEventSynchronize(ev[3]) != cudaSuccess ||
+        cudaEventElapsedTime(&a, ev[0], ev[1]) != cudaSuccess ||
+        cudaEventElapsedTime(&b, ev[2], ev[3]) != cudaSuccess ||
+        cudaEventElapsedTime(&c, ev[4], ev[5]) != cudaSuccess ||
+        cudaEventElapsedTime(&d, ev[5], ev[6]) != cudaSuccess) {
       record_error("timing events failed");
       return -1;
     }
     gu += a;
     dn += b;
+    lg += c;
+    sl += d;
   }
   if (n_forwards) *n_forwards = L->timed;
   if (gateup_ms) *gateup_ms = gu;
   if (down_ms) *down_ms = dn;
+  if (logits_ms) *logits_ms = lg;
+  if (select_ms) *select_ms = sl;
   L->timed = 0;
   return 0;
+}
+
+DSV4_API int dsv4cuda_moe_timing_end(dsv4cuda_moe_layer* L, int* n_forwards, float* gateup_ms,
+                                     float* down_ms) {
+  return dsv4cuda_moe_timing_end2(L, n_forwards, gateup_ms, down_ms, nullptr, nullptr);
 }
 
 DSV4_API int dsv4cuda_moe_forward_host(dsv4cuda_moe_layer* L, const float* x, const int* token_ids,

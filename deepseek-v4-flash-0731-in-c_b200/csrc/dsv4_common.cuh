@@ -143,6 +143,19 @@ __device__ __forceinline__ float round_e4m3(float v) {
   return sgn * (round_half_even(av * 512.0f) / 512.0f);
 }
 
+// Round to the nearest E4M3 value (|q| <= 448, finite; callers clamp) and
+// return it as an f16 (exact). The hardware conversion is round-to-nearest-
+// even on the 3-bit mantissa and on the 2^-9 subnormal grid, which is what
+// dsv4_round_e4m3 (src/dsv4/dsv4_ops.c:92-109) computes for this range; the
+// reference maps an exact zero (either sign) to +0, so do we.
+__device__ __forceinline__ __half e4m3_round_f16(float q) {
+  uint32_t h2;
+  asm("{ .reg .b16 t; cvt.rn.satfinite.e4m3x2.f32 t, %1, %1; cvt.rn.f16x2.e4m3x2 %0, t; }"
+      : "=r"(h2) : "f"(q));
+  const unsigned short h = static_cast<unsigned short>(h2 & 0xFFFFu);
+  return __ushort_as_half(q == 0.0f ? static_cast<unsigned short>(0) : h);
+}
+
 __device__ __forceinline__ float warp_max(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));

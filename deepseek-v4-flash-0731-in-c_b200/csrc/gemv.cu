@@ -19,11 +19,87 @@
 // as fmaf on the widened values). Activations are read through L1 (every
 // lane of a warp reads the same few lines); weights bypass L1.
 #include <algorithm>
+#include <mutex>
+#include <utility>
+#include <vector>
 
+#include <cudaTypedefs.h>
+
+#include "bulk.cuh"
 #include "dsv4_common.cuh"
 #include "gemv.cuh"
 
 namespace dsv4 {
+
+namespace {
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+struct MapKey {
+  const void* base;
+  uint64_t row_bytes, rows;
+  uint32_t box_bytes, box_rows;
+  bool sw;
+  bool operator==(const MapKey& o) const {
+    return base == o.base && row_bytes == o.row_bytes && rows == o.rows &&
+           box_bytes == o.box_bytes && box_rows == o.box_rows && sw == o.sw;
+  }
+};
+}  // namespace
+
+bool make_tma_map_u8(CUtensorMap* out, const void* base, uint64_t row_bytes, uint64_t rows,
+                     uint32_t box_bytes, uint32_t box_rows, bool swizzle128) {
+  static std::mutex mu;
+  static std::vector<std::pair<MapKey, CUtensorMap>> cache;
+  const MapKey key{base, row_bytes, rows, box_bytes, box_rows, swizzle128};
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    for (const auto& e : cache)
+      if (e.first == key) { *out = e.second; return true; }
+  }
+  auto fn = encode_fn();
+  if (!fn || reinterpret_cast<uintptr_t>(base) % 16 != 0 || row_bytes % 16 != 0 ||
+      box_bytes % 16 != 0 || rows == 0)
+    return false;
+  const cuuint64_t dims[2] = {row_bytes, rows};
+  const cuuint64_t strides[1] = {row_bytes};
+  const cuuint32_t box[2] = {box_bytes, box_rows};
+  const cuuint32_t estr[2] = {1, 1};
+  CUtensorMap m;
+  if (fn(&m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
+         CU_TENSOR_MAP_INTERLEAVE_NONE,
+         swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+    return false;
+  std::lock_guard<std::mutex> lock(mu);
+  if (cache.size() > 4096) cache.clear();
+  cache.emplace_back(key, m);
+  *out = m;
+  return true;
+}
+
+unsigned int* device_error_word() {
+  static unsigned int* words[64] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+  if (!words[dev]) {
+    unsigned int* w = nullptr;
+    if (cudaMalloc(&w, sizeof(unsigned int)) != cudaSuccess) return nullptr;
+    cudaMemset(w, 0, sizeof(unsigned int));
+    words[dev] = w;
+  }
+  return words[dev];
+}
 
 namespace {
 
@@ -81,10 +157,24 @@ __device__ __forceinline__ float fp8_chain32(const uint32_t* w8, const uint32_t*
 }
 
 // ---------------------------------------------------------------- FP4 ----
-// Grid: one warp per (item, block of 32/LPR rows). NT = max tokens per item.
+// E8M0 decode table with the NaN code (255) mapped to 0. FP4 group partials
+// are always finite (E2M1 x E4M3-grid products), so fmaf(p, qs*0, acc) ==
+// acc: exactly the reference's "skip a NaN-scaled group" (the accumulator
+// starts at +0 and can never become -0).
+__device__ __forceinline__ void fill_e8m0_skip_table(float* tbl) {
+  for (int i = threadIdx.x; i < 256; i += blockDim.x) tbl[i] = i == 255 ? 0.0f : e8m0_decode(i);
+}
+
+// Grid: one warp per (item, block of 32/LPR rows); LPR lanes share a row.
+// NT = max tokens per item; PAIR streams W[0] and W[1] (gate and up) with
+// one activation.
 template <int LPR, int NT, bool PAIR>
-__global__ void __launch_bounds__(128) fp4_gemv_kernel(const Fp4GemvArgs a) {
+__global__ void __launch_bounds__(128, NT <= 2 ? 4 : 3) fp4_gemv_kernel(const Fp4GemvArgs a) {
   constexpr int RPW = 32 / LPR;
+  constexpr int PF = PAIR ? 3 : 4;  // 32-byte chunks in flight per stream
+  __shared__ float e8m0_tbl[256];
+  fill_e8m0_skip_table(e8m0_tbl);
+  __syncthreads();
   const int lane = threadIdx.x & 31;
   const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int rblocks = (a.rows + RPW - 1) / RPW;
@@ -96,125 +186,340 @@ __global__ void __launch_bounds__(128) fp4_gemv_kernel(const Fp4GemvArgs a) {
   const int row = (gw % rblocks) * RPW + lane / LPR;
   const bool row_ok = row < a.rows;
   const int rowc = row_ok ? row : a.rows - 1;
-  const int G = a.in >> 5;                  // groups per row
+  const int G = a.in >> 5;                  // 32-column groups per row
   const int NP = G / (2 * LPR);             // 32-byte chunks per lane
   const size_t rb = static_cast<size_t>(a.in) >> 1;
   const uint8_t* wp0 = a.W[0] + it.mat * a.w_stride + rowc * rb + sub * 32;
   const uint8_t* sp0 = a.S[0] + it.mat * a.s_stride + static_cast<size_t>(rowc) * G + sub * 2;
-  const uint8_t* wp1 = nullptr;
-  const uint8_t* sp1 = nullptr;
-  if (PAIR) {
-    wp1 = a.W[1] + it.mat * a.w_stride + rowc * rb + sub * 32;
-    sp1 = a.S[1] + it.mat * a.s_stride + static_cast<size_t>(rowc) * G + sub * 2;
-  }
+  const uint8_t* wp1 = PAIR ? a.W[1] + it.mat * a.w_stride + rowc * rb + sub * 32 : nullptr;
+  const uint8_t* sp1 = PAIR ? a.S[1] + it.mat * a.s_stride + static_cast<size_t>(rowc) * G + sub * 2
+                            : nullptr;
+  const int sld = (a.act.ld + 127) >> 7;
   const __half* xr[NT];
   const float* xsr[NT];
 #pragma unroll
   for (int t = 0; t < NT; ++t) {
-    const int xi = t < ntok ? it.tok[t].x : it.tok[0].x;
+    const int xi = (NT == 1 || t < ntok) ? it.tok[t].x : it.tok[0].x;
     xr[t] = a.act.x + static_cast<size_t>(xi) * a.act.ld + sub * 64;
-    xsr[t] = a.act.s + static_cast<size_t>(xi) * ((a.act.ld + 127) >> 7);
+    xsr[t] = a.act.s + static_cast<size_t>(xi) * sld;
   }
   float acc0[NT], acc1[NT];
 #pragma unroll
   for (int t = 0; t < NT; ++t) { acc0[t] = 0.0f; acc1[t] = 0.0f; }
+  const int base_lane = lane - sub;
+  constexpr size_t kStep = static_cast<size_t>(LPR) * 32;  // bytes between a lane's chunks
 
-  constexpr int PF = PAIR ? 2 : 4;
-  U8x32 buf0[PF], buf1[PF];
-#pragma unroll
-  for (int j = 0; j < PF; ++j) {
-    if (j < NP) {
-      buf0[j] = ldg32(wp0 + static_cast<size_t>(j) * LPR * 32);
-      if (PAIR) buf1[j] = ldg32(wp1 + static_cast<size_t>(j) * LPR * 32);
+  auto process = [&](const U8x32& cw0, const U8x32& cw1, int p) {
+    const int col0 = (p * LPR + sub) * 64;
+    const uint32_t sc0 = *reinterpret_cast<const uint16_t*>(sp0 + p * LPR * 2);
+    const float wa0 = e8m0_tbl[sc0 & 0xFFu], wb0 = e8m0_tbl[sc0 >> 8];
+    float wa1 = 0.f, wb1 = 0.f;
+    if (PAIR) {
+      const uint32_t sc1 = *reinterpret_cast<const uint16_t*>(sp1 + p * LPR * 2);
+      wa1 = e8m0_tbl[sc1 & 0xFFu];
+      wb1 = e8m0_tbl[sc1 >> 8];
     }
-  }
-  for (int p0 = 0; p0 < NP; p0 += PF) {
 #pragma unroll
-    for (int j = 0; j < PF; ++j) {
-      const int p = p0 + j;
-      if (p < NP) {
-        const U8x32 cw0 = buf0[j];
-        U8x32 cw1;
-        if (PAIR) cw1 = buf1[j];
-        if (p + PF < NP) {
-          buf0[j] = ldg32(wp0 + static_cast<size_t>(p + PF) * LPR * 32);
-          if (PAIR) buf1[j] = ldg32(wp1 + static_cast<size_t>(p + PF) * LPR * 32);
+    for (int t = 0; t < NT; ++t) {
+      if (NT == 1 || t < ntok) {
+        const __half* xp = xr[t] + static_cast<size_t>(p) * LPR * 64;
+        const float qs = xsr[t][col0 >> 7];
+        float pa0, pb0, pa1 = 0.f, pb1 = 0.f;
+        {
+          uint32_t xw[16];
+          const U8x32 v0 = ldg32_l1(xp), v1 = ldg32_l1(xp + 16);
+#pragma unroll
+          for (int k = 0; k < 8; ++k) { xw[k] = v0.w[k]; xw[8 + k] = v1.w[k]; }
+          pa0 = fp4_partial16(&cw0.w[0], xw);
+          if (PAIR) pa1 = fp4_partial16(&cw1.w[0], xw);
         }
-        const int col0 = (p * LPR + sub) * 64;  // first column of this chunk
-        const uint32_t sc0 = *reinterpret_cast<const uint16_t*>(sp0 + p * LPR * 2);
-        const float wsa0 = e8m0_decode(sc0 & 0xFFu), wsb0 = e8m0_decode(sc0 >> 8);
-        float wsa1 = 0.f, wsb1 = 0.f;
+        {
+          uint32_t xw[16];
+          const U8x32 v0 = ldg32_l1(xp + 32), v1 = ldg32_l1(xp + 48);
+#pragma unroll
+          for (int k = 0; k < 8; ++k) { xw[k] = v0.w[k]; xw[8 + k] = v1.w[k]; }
+          pb0 = fp4_partial16(&cw0.w[4], xw);
+          if (PAIR) pb1 = fp4_partial16(&cw1.w[4], xw);
+        }
+        const float sa0 = qs * wa0, sb0 = qs * wb0;
+        float sa1 = 0.f, sb1 = 0.f;
         if (PAIR) {
-          const uint32_t sc1 = *reinterpret_cast<const uint16_t*>(sp1 + p * LPR * 2);
-          wsa1 = e8m0_decode(sc1 & 0xFFu);
-          wsb1 = e8m0_decode(sc1 >> 8);
+          sa1 = qs * wa1;
+          sb1 = qs * wb1;
         }
+        if (LPR == 1) {
+          acc0[t] = fmaf(pb0, sb0, fmaf(pa0, sa0, acc0[t]));
+          if (PAIR) acc1[t] = fmaf(pb1, sb1, fmaf(pa1, sa1, acc1[t]));
+        } else {
 #pragma unroll
-        for (int t = 0; t < NT; ++t) {
-          if (t < ntok) {
-            uint32_t xw[32];
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-              const U8x32 v = ldg32_l1(xr[t] + static_cast<size_t>(p) * LPR * 64 + q * 16);
-#pragma unroll
-              for (int k = 0; k < 8; ++k) xw[q * 8 + k] = v.w[k];
-            }
-            const float qs = xsr[t][col0 >> 7];
-            float pa0 = fp4_partial16(&cw0.w[0], &xw[0]);
-            float pb0 = fp4_partial16(&cw0.w[4], &xw[16]);
-            float sa0 = qs * wsa0, sb0 = qs * wsb0;
-            if (isnan(wsa0)) { pa0 = 0.f; sa0 = 0.f; }
-            if (isnan(wsb0)) { pb0 = 0.f; sb0 = 0.f; }
-            float pa1 = 0.f, pb1 = 0.f, sa1 = 0.f, sb1 = 0.f;
+          for (int s = 0; s < LPR; ++s) {
+            const float qa = __shfl_sync(0xffffffffu, pa0, base_lane + s);
+            const float ra = __shfl_sync(0xffffffffu, sa0, base_lane + s);
+            const float qb = __shfl_sync(0xffffffffu, pb0, base_lane + s);
+            const float rb2 = __shfl_sync(0xffffffffu, sb0, base_lane + s);
+            acc0[t] = fmaf(qb, rb2, fmaf(qa, ra, acc0[t]));
             if (PAIR) {
-              pa1 = fp4_partial16(&cw1.w[0], &xw[0]);
-              pb1 = fp4_partial16(&cw1.w[4], &xw[16]);
-              sa1 = qs * wsa1;
-              sb1 = qs * wsb1;
-              if (isnan(wsa1)) { pa1 = 0.f; sa1 = 0.f; }
-              if (isnan(wsb1)) { pb1 = 0.f; sb1 = 0.f; }
-            }
-            if (LPR == 1) {
-              acc0[t] = fmaf(pa0, sa0, acc0[t]);
-              acc0[t] = fmaf(pb0, sb0, acc0[t]);
-              if (PAIR) {
-                acc1[t] = fmaf(pa1, sa1, acc1[t]);
-                acc1[t] = fmaf(pb1, sb1, acc1[t]);
-              }
-            } else {
-              const int base = lane - sub;
-#pragma unroll
-              for (int s = 0; s < LPR; ++s) {
-                const float qa = __shfl_sync(0xffffffffu, pa0, base + s);
-                const float qsa = __shfl_sync(0xffffffffu, sa0, base + s);
-                const float qb = __shfl_sync(0xffffffffu, pb0, base + s);
-                const float qsb = __shfl_sync(0xffffffffu, sb0, base + s);
-                acc0[t] = fmaf(qa, qsa, acc0[t]);
-                acc0[t] = fmaf(qb, qsb, acc0[t]);
-                if (PAIR) {
-                  const float ra = __shfl_sync(0xffffffffu, pa1, base + s);
-                  const float rsa = __shfl_sync(0xffffffffu, sa1, base + s);
-                  const float rb2 = __shfl_sync(0xffffffffu, pb1, base + s);
-                  const float rsb = __shfl_sync(0xffffffffu, sb1, base + s);
-                  acc1[t] = fmaf(ra, rsa, acc1[t]);
-                  acc1[t] = fmaf(rb2, rsb, acc1[t]);
-                }
-              }
+              const float ua = __shfl_sync(0xffffffffu, pa1, base_lane + s);
+              const float va = __shfl_sync(0xffffffffu, sa1, base_lane + s);
+              const float ub = __shfl_sync(0xffffffffu, pb1, base_lane + s);
+              const float vb = __shfl_sync(0xffffffffu, sb1, base_lane + s);
+              acc1[t] = fmaf(ub, vb, fmaf(ua, va, acc1[t]));
             }
           }
         }
       }
     }
+  };
+
+  U8x32 buf0[PF], buf1[PF];
+#pragma unroll
+  for (int j = 0; j < PF; ++j) {
+    if (j < NP) {
+      buf0[j] = ldg32(wp0 + j * kStep);
+      if (PAIR) buf1[j] = ldg32(wp1 + j * kStep);
+    }
   }
+  int p = 0;
+  for (; p + PF <= NP; p += PF) {
+#pragma unroll
+    for (int j = 0; j < PF; ++j) {
+      const U8x32 c0 = buf0[j];
+      U8x32 c1;
+      if (PAIR) c1 = buf1[j];
+      if (p + j + PF < NP) {
+        buf0[j] = ldg32(wp0 + (p + j + PF) * kStep);
+        if (PAIR) buf1[j] = ldg32(wp1 + (p + j + PF) * kStep);
+      }
+      process(c0, c1, p + j);
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < PF; ++j)
+    if (p + j < NP) process(buf0[j], buf1[j], p + j);
+
   if (sub == 0 && row_ok) {
 #pragma unroll
     for (int t = 0; t < NT; ++t) {
-      if (t < ntok) {
+      if (NT == 1 || t < ntok) {
         const size_t yo = static_cast<size_t>(it.tok[t].y) * a.rows + row;
         a.Y[0][yo] = bf16_round(acc0[t]);
         if (PAIR) a.Y[1][yo] = bf16_round(acc1[t]);
       }
     }
+  }
+}
+
+// -------------------------------------------------------- FP4 stream ----
+// Streaming form of the FP4 GEMV for in % 512 == 0. Each warp owns a tile of
+// 32 rows (lane = row) and walks it in 512-column chunks. Per chunk, one
+// elected lane issues three 2-D TMA box loads (two [32 rows x 128 B] weight
+// boxes with the 128-byte swizzle, one [32 x 16 B] box of E8M0 codes) and
+// one 1-D bulk copy per token of the activation slice into a per-warp ring of
+// kStages shared-memory stages, completed on an mbarrier each. The swizzle
+// makes the lane-per-row 16-byte shared loads conflict-free, and every lane
+// folds its own row's 32-column partials in column order - the reference's
+// accumulation order - with no cross-lane traffic.
+constexpr int kSCols = 512;                  // FP4 columns per stage row
+constexpr int kSRowBytes = kSCols / 2;       // 256
+constexpr int kSGroups = kSCols / 32;        // 16 E8M0 codes per stage row
+constexpr int kStages = 2;
+
+template <int NT>
+struct StreamLayout {
+  static constexpr int kW = 32 * kSRowBytes;      // two swizzled [32][128] boxes
+  static constexpr int kS = 32 * kSGroups;        // [32][16] codes
+  static constexpr int kA = NT * kSCols * 2;      // activations (f16)
+  static constexpr int kStage = (kW + kS + kA + 1023) / 1024 * 1024;  // 1 KB aligned
+  static constexpr int kWarpBytes = kStages * kStage;
+};
+
+struct Fp4Maps {
+  CUtensorMap w[2];  // [rows_total][in/2] bytes, box [32][128], 128B swizzle
+  CUtensorMap s[2];  // [rows_total][in/32] codes, box [32][16]
+};
+
+// Two 32-column partials computed with interleaved (independent) chains.
+__device__ __forceinline__ void fp4_partial16x2(const uint32_t* wa, const uint32_t* xa,
+                                                const uint32_t* wb, const uint32_t* xb,
+                                                float& pa, float& pb) {
+  pa = 0.0f;
+  pb = 0.0f;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    uint32_t a0, a1, a2, a3, b0, b1, b2, b3;
+    asm("{ .reg .b8 c0, c1, c2, c3; mov.b32 {c0, c1, c2, c3}, %4;"
+        " cvt.rn.f16x2.e2m1x2 %0, c0; cvt.rn.f16x2.e2m1x2 %1, c1;"
+        " cvt.rn.f16x2.e2m1x2 %2, c2; cvt.rn.f16x2.e2m1x2 %3, c3; }"
+        : "=r"(a0), "=r"(a1), "=r"(a2), "=r"(a3) : "r"(wa[i]));
+    asm("{ .reg .b8 c0, c1, c2, c3; mov.b32 {c0, c1, c2, c3}, %4;"
+        " cvt.rn.f16x2.e2m1x2 %0, c0; cvt.rn.f16x2.e2m1x2 %1, c1;"
+        " cvt.rn.f16x2.e2m1x2 %2, c2; cvt.rn.f16x2.e2m1x2 %3, c3; }"
+        : "=r"(b0), "=r"(b1), "=r"(b2), "=r"(b3) : "r"(wb[i]));
+    pa = fma_h_lo(a0, xa[4 * i + 0], pa);
+    pb = fma_h_lo(b0, xb[4 * i + 0], pb);
+    pa = fma_h_hi(a0, xa[4 * i + 0], pa);
+    pb = fma_h_hi(b0, xb[4 * i + 0], pb);
+    pa = fma_h_lo(a1, xa[4 * i + 1], pa);
+    pb = fma_h_lo(b1, xb[4 * i + 1], pb);
+    pa = fma_h_hi(a1, xa[4 * i + 1], pa);
+    pb = fma_h_hi(b1, xb[4 * i + 1], pb);
+    pa = fma_h_lo(a2, xa[4 * i + 2], pa);
+    pb = fma_h_lo(b2, xb[4 * i + 2], pb);
+    pa = fma_h_hi(a2, xa[4 * i + 2], pa);
+    pb = fma_h_hi(b2, xb[4 * i + 2], pb);
+    pa = fma_h_lo(a3, xa[4 * i + 3], pa);
+    pb = fma_h_lo(b3, xb[4 * i + 3], pb);
+    pa = fma_h_hi(a3, xa[4 * i + 3], pa);
+    pb = fma_h_hi(b3, xb[4 * i + 3], pb);
+  }
+}
+
+template <int NT, int WARPS>
+__global__ void __launch_bounds__(WARPS * 32, 1)
+    fp4_stream_kernel(const __grid_constant__ Fp4Maps maps, const Fp4GemvArgs a, int pair) {
+  using L = StreamLayout<NT>;
+  extern __shared__ __align__(1024) unsigned char smem[];
+  __shared__ float e8m0_tbl[256];
+  __shared__ uint64_t bars_all[WARPS][kStages];
+  fill_e8m0_skip_table(e8m0_tbl);
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  // swizzled boxes need 1 KB aligned destinations: the launch adds 1 KB of
+  // slack and the base is rounded up here
+  unsigned char* const sbase =
+      smem + ((1024u - (smem_addr(smem) & 1023u)) & 1023u);
+  unsigned char* wbase = sbase + warp * L::kWarpBytes;
+  uint64_t* bars = bars_all[warp];
+  if (lane == 0) {
+#pragma unroll
+    for (int s = 0; s < kStages; ++s) mbar_init(&bars[s], 1);
+    mbar_fence_init();
+    if (warp == 0) {
+      tma_prefetch_desc(&maps.w[0]);
+      tma_prefetch_desc(&maps.s[0]);
+      if (pair) {
+        tma_prefetch_desc(&maps.w[1]);
+        tma_prefetch_desc(&maps.s[1]);
+      }
+    }
+  }
+  __syncthreads();
+
+  const int n_items = load_n_items(a.n_items, a.max_items);
+  const int V = pair ? 2 : 1;
+  const int rblocks = (a.rows + 31) / 32;
+  const long long tiles = static_cast<long long>(n_items) * V * rblocks;
+  const int CPT = a.in / kSCols;  // chunks per tile
+  const long long nwarps = static_cast<long long>(gridDim.x) * WARPS;
+  // consecutive tiles go to consecutive CTAs first: equal work per SM
+  const long long first = static_cast<long long>(warp) * gridDim.x + blockIdx.x;
+  const long long my_tiles = tiles > first ? (tiles - first + nwarps - 1) / nwarps : 0;
+  const long long jobs = my_tiles * CPT;
+  const int sld = (a.act.ld + 127) >> 7;
+
+  auto issue = [&](long long j) {
+    if (lane != 0) return;
+    const int s = static_cast<int>(j % kStages);
+    const long long tile = first + (j / CPT) * nwarps;
+    const int chunk = static_cast<int>(j % CPT);
+    const int item_idx = static_cast<int>(tile / (V * rblocks));
+    const int rem = static_cast<int>(tile % (V * rblocks));
+    const int v = rem / rblocks, rb = rem % rblocks;
+    const GemvItem& it = a.items[item_idx];
+    const int ntok = it.ntok;
+    unsigned char* st = wbase + s * L::kStage;
+    mbar_arrive_expect_tx(&bars[s], static_cast<uint32_t>(L::kW + L::kS + ntok * kSCols * 2));
+    const int y = it.mat * a.rows + rb * 32;
+    const CUtensorMap* wm = v ? &maps.w[1] : &maps.w[0];
+    const CUtensorMap* sm = v ? &maps.s[1] : &maps.s[0];
+    tma_load_2d(st, wm, chunk * kSRowBytes, y, &bars[s]);
+    tma_load_2d(st + L::kW / 2, wm, chunk * kSRowBytes + 128, y, &bars[s]);
+    tma_load_2d(st + L::kW, sm, chunk * kSGroups, y, &bars[s]);
+    for (int t = 0; t < ntok; ++t)
+      bulk_g2s(st + L::kW + L::kS + t * kSCols * 2,
+               a.act.x + static_cast<size_t>(it.tok[t].x) * a.act.ld + chunk * kSCols,
+               kSCols * 2, &bars[s]);
+  };
+
+  float acc[NT];
+#pragma unroll
+  for (int t = 0; t < NT; ++t) acc[t] = 0.0f;
+
+  for (long long j = 0; j < jobs && j < kStages; ++j) issue(j);
+  __syncwarp();
+  bool ok = true;
+  long long j = 0;
+  for (; j < jobs; ++j) {
+    const int s = static_cast<int>(j % kStages);
+    if (!mbar_wait(&bars[s], static_cast<uint32_t>((j / kStages) & 1), a.err)) { ok = false; break; }
+    const long long tile = first + (j / CPT) * nwarps;
+    const int chunk = static_cast<int>(j % CPT);
+    const int item_idx = static_cast<int>(tile / (V * rblocks));
+    const int rem = static_cast<int>(tile % (V * rblocks));
+    const int v = rem / rblocks, rb = rem % rblocks;
+    const GemvItem& it = a.items[item_idx];
+    const int ntok = it.ntok;
+    const unsigned char* st = wbase + s * L::kStage;
+    const unsigned char* wrow = st + lane * 128;
+    const int sw = lane & 7;
+    const uint4 codes = *reinterpret_cast<const uint4*>(st + L::kW + lane * kSGroups);
+    const uint32_t cw[4] = {codes.x, codes.y, codes.z, codes.w};
+    float qs[NT][4];
+#pragma unroll
+    for (int t = 0; t < NT; ++t) {
+      const int xi = (NT == 1 || t < ntok) ? it.tok[t].x : it.tok[0].x;
+      const float4 q4 = __ldg(reinterpret_cast<const float4*>(a.act.s + static_cast<size_t>(xi) * sld +
+                                                              chunk * 4));
+      qs[t][0] = q4.x; qs[t][1] = q4.y; qs[t][2] = q4.z; qs[t][3] = q4.w;
+    }
+#pragma unroll
+    for (int g = 0; g < kSGroups; g += 2) {
+      // group g lives in box g/8, 16-byte chunk (g%8) xor (row%8)
+      const uint4 wa = *reinterpret_cast<const uint4*>(wrow + (g >> 3) * (L::kW / 2) +
+                                                       (((g & 7) ^ sw) << 4));
+      const uint4 wb = *reinterpret_cast<const uint4*>(wrow + ((g + 1) >> 3) * (L::kW / 2) +
+                                                       ((((g + 1) & 7) ^ sw) << 4));
+      const uint32_t wa4[4] = {wa.x, wa.y, wa.z, wa.w};
+      const uint32_t wb4[4] = {wb.x, wb.y, wb.z, wb.w};
+      const float sa = e8m0_tbl[(cw[g >> 2] >> (8 * (g & 3))) & 0xFFu];
+      const float sb = e8m0_tbl[(cw[(g + 1) >> 2] >> (8 * ((g + 1) & 3))) & 0xFFu];
+#pragma unroll
+      for (int t = 0; t < NT; ++t) {
+        if (NT == 1 || t < ntok) {
+          const uint4* xg = reinterpret_cast<const uint4*>(st + L::kW + L::kS + t * kSCols * 2 + g * 64);
+          uint32_t xa[16], xb[16];
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const uint4 u = xg[q], w = xg[4 + q];
+            xa[4 * q] = u.x; xa[4 * q + 1] = u.y; xa[4 * q + 2] = u.z; xa[4 * q + 3] = u.w;
+            xb[4 * q] = w.x; xb[4 * q + 1] = w.y; xb[4 * q + 2] = w.z; xb[4 * q + 3] = w.w;
+          }
+          float pa, pb;
+          fp4_partial16x2(wa4, xa, wb4, xb, pa, pb);
+          acc[t] = fmaf(pa, qs[t][g >> 2] * sa, acc[t]);
+          acc[t] = fmaf(pb, qs[t][(g + 1) >> 2] * sb, acc[t]);
+        }
+      }
+    }
+    if (chunk == CPT - 1) {
+      const int row = rb * 32 + lane;
+      if (row < a.rows) {
+        float* Yv = v ? a.Y[1] : a.Y[0];
+#pragma unroll
+        for (int t = 0; t < NT; ++t)
+          if (NT == 1 || t < ntok)
+            Yv[static_cast<size_t>(it.tok[t].y) * a.rows + row] = bf16_round(acc[t]);
+      }
+#pragma unroll
+      for (int t = 0; t < NT; ++t) acc[t] = 0.0f;
+    }
+    __syncwarp();
+    if (j + kStages < jobs) issue(j + kStages);
+    __syncwarp();
+  }
+  if (!ok) {
+    // drain this warp's copies still in flight before the CTA exits
+    for (long long k = j + 1; k < jobs && k < j + kStages; ++k)
+      mbar_wait(&bars[k % kStages], static_cast<uint32_t>((k / kStages) & 1), a.err);
   }
 }
 
@@ -496,9 +801,9 @@ __global__ void quant_fp8_kernel(const float* x, int ldx, int n, int rows, __hal
     if (i < len) {
       float q = v[k] * inv;
       q = q > 448.f ? 448.f : (q < -448.f ? -448.f : q);
-      const float g = round_e4m3(q);
-      if (qx) qx[static_cast<size_t>(r) * ld_out + b * 128 + i] = __float2half_rn(g);
-      if (qx32) qx32[static_cast<size_t>(r) * ld_out + b * 128 + i] = g;
+      const __half g = e4m3_round_f16(q);
+      if (qx) qx[static_cast<size_t>(r) * ld_out + b * 128 + i] = g;
+      if (qx32) qx32[static_cast<size_t>(r) * ld_out + b * 128 + i] = __half2float(g);
     }
   }
 }
@@ -544,7 +849,7 @@ __global__ void swiglu_quant_kernel(const float* gate, const float* up, int n, i
       const size_t o = static_cast<size_t>(r) * n + b * 128 + i;
       float q = v[k] * inv;
       q = q > 448.f ? 448.f : (q < -448.f ? -448.f : q);
-      qy[o] = __float2half_rn(round_e4m3(q));
+      qy[o] = e4m3_round_f16(q);
       if (ybf) ybf[o] = v[k];
     }
   }
@@ -603,14 +908,70 @@ int sm_count() {
   return n;
 }
 
-// Lanes per row: split rows over more lanes when there are too few warps to
-// fill the GPU (the item count is an upper bound when it lives on device).
+// Lanes per row: the largest split (1, 2 or 4 lanes per row) whose warp
+// count still fits one resident wave (16 warps per SM at <=128 registers),
+// so every row block streams concurrently and no tail wave is left.
 int pick_lpr(long long rows_total, int chunks_per_row) {
-  const long long want_warps = 12LL * sm_count();
+  const long long wave = 16LL * sm_count();
   int lpr = 1;
-  while (lpr < 4 && (rows_total * lpr) / 32 < want_warps && chunks_per_row % (4 * lpr) == 0)
+  while (lpr < 4 && (rows_total * lpr * 2) / 32 <= wave && chunks_per_row % (4 * lpr) == 0)
     lpr *= 2;
   return lpr;
+}
+
+template <int NT, int WARPS>
+cudaError_t launch_stream_nt(const Fp4Maps& maps, const Fp4GemvArgs& a, bool pair,
+                             cudaStream_t st) {
+  const size_t smem = static_cast<size_t>(WARPS) * StreamLayout<NT>::kWarpBytes + 1024;
+  static bool attr_done = false;  // per template instance
+  if (!attr_done) {
+    cudaError_t e = cudaFuncSetAttribute(fp4_stream_kernel<NT, WARPS>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(smem));
+    if (e != cudaSuccess) return e;
+    attr_done = true;
+  }
+  const long long tiles = static_cast<long long>(a.max_items) * (pair ? 2 : 1) *
+                          ((a.rows + 31) / 32);
+  const int grid = static_cast<int>(std::max<long long>(
+      1, std::min<long long>(sm_count(), (tiles + WARPS - 1) / WARPS)));
+  Fp4GemvArgs b = a;
+  if (!b.err) b.err = device_error_word();
+  fp4_stream_kernel<NT, WARPS><<<grid, WARPS * 32, smem, st>>>(maps, b, pair ? 1 : 0);
+  return cudaGetLastError();
+}
+
+// Tensor maps over every matrix of the launch: rows_total = rows of all
+// matrices an item index can select (max mat + 1 experts).
+bool fp4_maps(Fp4Maps* m, const Fp4GemvArgs& a, bool pair, long long n_mats) {
+  const uint64_t rows_total = static_cast<uint64_t>(n_mats) * a.rows;
+  for (int v = 0; v < (pair ? 2 : 1); ++v) {
+    if (!make_tma_map_u8(&m->w[v], a.W[v], static_cast<uint64_t>(a.in) / 2, rows_total, 128, 32,
+                         true))
+      return false;
+    if (!make_tma_map_u8(&m->s[v], a.S[v], static_cast<uint64_t>(a.in) / 32, rows_total, 16, 32,
+                         false))
+      return false;
+  }
+  if (!pair) {
+    m->w[1] = m->w[0];
+    m->s[1] = m->s[0];
+  }
+  return true;
+}
+
+cudaError_t launch_fp4_stream(const Fp4GemvArgs& a, bool pair, int nt, cudaStream_t st) {
+  Fp4Maps maps;
+  // matrices are w_stride apart; n_mats must cover every `mat` an item names
+  const long long n_mats = a.n_mats > 0 ? a.n_mats : 1;
+  if (!fp4_maps(&maps, a, pair, n_mats)) return cudaErrorInvalidValue;
+  switch (nt) {
+    case 1: return launch_stream_nt<1, 8>(maps, a, pair, st);
+    case 2: return launch_stream_nt<2, 8>(maps, a, pair, st);
+    case 3:
+    case 4: return launch_stream_nt<4, 8>(maps, a, pair, st);
+    default: return launch_stream_nt<8, 6>(maps, a, pair, st);
+  }
 }
 
 }  // namespace
@@ -628,8 +989,19 @@ cudaError_t launch_fp4_gemv(const Fp4GemvArgs& a, bool pair, int item_tokens, cu
       fp4_gemv_scalar_kernel<<<grid, 256, 0, st>>>(a, p);
     return cudaGetLastError();
   }
+  // the streaming kernel needs 512-column chunks, matrices stacked at their
+  // natural pitch (so one tensor map covers them) and 16-byte alignment
+  const bool stacked = (a.n_mats <= 1) ||
+                       (a.w_stride == static_cast<size_t>(a.rows) * (a.in / 2) &&
+                        a.s_stride == static_cast<size_t>(a.rows) * (a.in / 32));
+  if (a.in % kSCols == 0 && stacked && aligned(a.W[0], 16) && aligned(a.S[0], 16) &&
+      a.act.ld % kSCols == 0 && aligned(a.act.x, 16) && aligned(a.act.s, 16) &&
+      (!pair || (aligned(a.W[1], 16) && aligned(a.S[1], 16)))) {
+    cudaError_t e = launch_fp4_stream(a, pair, item_tokens, st);
+    if (e != cudaErrorInvalidValue) return e;  // else: map rejected, use the LDG kernel
+  }
   const int G = a.in / 32;
-  const int lpr = pick_lpr(static_cast<long long>(a.max_items) * a.rows * (pair ? 2 : 1), G);
+  const int lpr = pick_lpr(static_cast<long long>(a.max_items) * a.rows, G);
   if (pair) {
     if (lpr == 4) return fp4_dispatch_nt<4, true>(a, item_tokens, st);
     if (lpr == 2) return fp4_dispatch_nt<2, true>(a, item_tokens, st);
@@ -653,7 +1025,7 @@ cudaError_t launch_fp8_gemv(const Fp8GemvArgs& a, bool pair, int item_tokens, cu
     return cudaGetLastError();
   }
   const int CB = a.in / 128;
-  int lpr = pick_lpr(static_cast<long long>(a.max_items) * a.rows * (pair ? 2 : 1), 2 * CB);
+  int lpr = pick_lpr(static_cast<long long>(a.max_items) * a.rows, 2 * CB);
   while (lpr > 1 && CB % lpr != 0) lpr /= 2;
   if (pair) {
     if (lpr == 4) return fp8_dispatch_nt<4, true>(a, item_tokens, st);

@@ -43,6 +43,8 @@ struct Fp4GemvArgs {
   const GemvItem* items;
   const int* n_items;      // device count (<= max_items)
   int max_items;
+  unsigned int* err;       // device error word (null: the library's default)
+  long long n_mats;        // matrices addressable by items (w_stride apart); 0 = 1
 };
 
 struct Fp8GemvArgs {

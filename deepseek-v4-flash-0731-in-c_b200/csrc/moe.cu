@@ -28,7 +28,6 @@ namespace dsv4 {
 namespace {
 
 constexpr double kU = 5.9604644775390625e-08;  // 2^-24, fp32 unit roundoff
-constexpr int kSelThreads = 256;
 
 __device__ __forceinline__ double warp_sum_d(double v) {
 #pragma unroll
@@ -42,72 +41,6 @@ __device__ __forceinline__ float sqrt_softplus_f(float z) {
   if (z > 20.0f) return sqrtf(z);
   return sqrtf(log1pf(expf(z)));
 }
-__device__ __forceinline__ double sqrt_softplus_d(double z) {
-  if (z > 20.0) return sqrt(z);
-  return sqrt(log1p(exp(z)));
-}
-
-// One warp per (token, expert): exact fp64 logit and the reference-error bound.
-__global__ void router_logits_kernel(const float* __restrict__ x, int H,
-                                     const uint16_t* __restrict__ gate, int E,
-                                     double* __restrict__ zd, double* __restrict__ zb,
-                                     int public_router) {
-  const int lane = threadIdx.x & 31;
-  const int e = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  const int t = blockIdx.y;
-  if (e >= E) return;
-  const float* xr = x + static_cast<size_t>(t) * H;
-  const uint16_t* g = gate + static_cast<size_t>(e) * H;
-  const int seg = (H + 31) / 32;
-  const int c0 = min(lane * seg, H), c1 = min(c0 + seg, H);
-  double local = 0.0;
-  for (int c = c0; c < c1; ++c)
-    local += static_cast<double>(bf16_widen(g[c])) * static_cast<double>(xr[c]);
-  double incl = local;
-#pragma unroll
-  for (int o = 1; o < 32; o <<= 1) {
-    const double v = __shfl_up_sync(0xffffffffu, incl, o);
-    if (lane >= o) incl += v;
-  }
-  double run = __shfl_up_sync(0xffffffffu, incl, 1);
-  if (lane == 0) run = 0.0;
-  double sabs = 0.0, pabs = 0.0;
-  for (int c = c0; c < c1; ++c) {
-    const double p = static_cast<double>(bf16_widen(g[c])) * static_cast<double>(xr[c]);
-    run += p;
-    sabs += fabs(run);
-    pabs += fabs(p);
-  }
-  const double total = __shfl_sync(0xffffffffu, incl, 31);
-  sabs = warp_sum_d(sabs);
-  pabs = warp_sum_d(pabs);
-  if (lane == 0) {
-    const size_t o = static_cast<size_t>(t) * E + e;
-    zd[o] = total;
-    // fused chain: each step rounds its result (<= u|s_i|); the public
-    // router also rounds every product (<= u|p_i|). fp64 summation error and
-    // subnormal steps are covered by the last two terms.
-    const double b = kU * (sabs + (public_router ? pabs : 0.0));
-    zb[o] = b * 1.01 + 1e-12 * pabs + 1e-40 * H;
-  }
-}
-
-struct SelectArgs {
-  const float* x;
-  int H, E, topk;
-  const uint16_t* gate;
-  const float* bias;
-  const int64_t* tid2eid;
-  int hash_vocab;
-  const int* token_ids;
-  const double* zd;
-  const double* zb;
-  float route_scale;
-  int public_router;
-  int* idx;
-  float* wt;
-  int* counters;
-};
 
 struct Cand {
   float v;
@@ -123,8 +56,230 @@ __device__ __forceinline__ bool better(const Cand& a, const Cand& b) {
   return a.id < b.id;
 }
 
-__device__ Cand block_best(Cand c, Cand* red) {
-  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+// ------------------------------------------------------------- router ----
+constexpr int kLogitWarps = 4;    // warps per expert in router_logits_kernel
+constexpr int kSelThreads = 256;  // threads per token in router_select_kernel
+
+struct RouterArgs {
+  const float* x;            // [M][H] fp32 (BF16-valued)
+  int H, M, E, topk;
+  const uint16_t* gate;      // [E][H] BF16
+  const float* bias;         // [E] or null
+  const int64_t* tid2eid;    // [hash_vocab][topk] or null
+  int hash_vocab;
+  const int* token_ids;      // [M] (hash layers)
+  float route_scale;
+  int public_router;
+  double* zd;                // [M][E] logits
+  double* zb;                // [M][E] bound on |z_ref - zd|
+  __half* xq;                // [M][H] activation quant (skipped when null)
+  float* xs;                 // [M][ceil(H/128)]
+  int* idx;                  // [M][topk]
+  float* wt;                 // [M][topk]
+  GemvItem* items_gu;        // plan outputs (skipped when null)
+  GemvItem* items_dn;
+  GemvItem* items_sh;
+  int* counters;             // [0] items, [1] CTA ticket, [2] tie fallbacks, [3] shared items
+};
+
+// The reference's fp32 logit chain, replayed exactly (near-tie path):
+// moe_forward uses fmaf (src/dsv4/dsv4_model.c:299-302); the public
+// dsv4_router rounds the product and the sum separately (dsv4_ops.c:504).
+// x is staged in shared memory; the gate row streams with 8 loads ahead.
+__device__ float exact_logit(const uint16_t* g, const float* xs, int H, int pub) {
+  float z = 0.0f;
+  if ((H & 7) == 0 && (reinterpret_cast<uintptr_t>(g) & 15) == 0) {
+    constexpr int PF = 8;
+    const int n8 = H >> 3;
+    uint4 buf[PF];
+#pragma unroll
+    for (int j = 0; j < PF; ++j)
+      if (j < n8) buf[j] = __ldg(reinterpret_cast<const uint4*>(g) + j);
+    for (int i = 0; i < n8; i += PF) {
+#pragma unroll
+      for (int j = 0; j < PF; ++j) {
+        const int c8 = i + j;
+        if (c8 < n8) {
+          const uint4 gv = buf[j];
+          if (c8 + PF < n8) buf[j] = __ldg(reinterpret_cast<const uint4*>(g) + c8 + PF);
+          const float4 x0 = reinterpret_cast<const float4*>(xs)[2 * c8];
+          const float4 x1 = reinterpret_cast<const float4*>(xs)[2 * c8 + 1];
+          const float w[8] = {__uint_as_float(gv.x << 16), __uint_as_float(gv.x & 0xFFFF0000u),
+                              __uint_as_float(gv.y << 16), __uint_as_float(gv.y & 0xFFFF0000u),
+                              __uint_as_float(gv.z << 16), __uint_as_float(gv.z & 0xFFFF0000u),
+                              __uint_as_float(gv.w << 16), __uint_as_float(gv.w & 0xFFFF0000u)};
+          const float xv[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+#pragma unroll
+          for (int k = 0; k < 8; ++k)
+            z = pub ? __fadd_rn(z, __fmul_rn(w[k], xv[k])) : fmaf(w[k], xv[k], z);
+        }
+      }
+    }
+  } else {
+    for (int c = 0; c < H; ++c)
+      z = pub ? __fadd_rn(z, __fmul_rn(bf16_widen(g[c]), xs[c])) : fmaf(bf16_widen(g[c]), xs[c], z);
+  }
+  return z;
+}
+
+// One warp's pass over its chunks [c_begin, c_end) of 256 columns (lane l
+// takes 8 consecutive columns of each): running prefix sums t_i in column
+// order starting from `offset`. Returns the segment total (from 0) and adds
+// sum|offset + t_i| to *sabs and sum|fl(w x)| to *pabs when requested.
+__device__ float warp_segment(const uint16_t* g, const float* xr, int H, int c_begin, int c_end,
+                              float offset, float* sabs, float* pabs) {
+  const int lane = threadIdx.x & 31;
+  const bool vec = (H & 7) == 0;
+  float carry = 0.0f, sa = 0.0f, pa = 0.0f;
+  constexpr int CG = 4;  // chunks whose loads and scans are in flight together
+  for (int c0 = c_begin; c0 < c_end; c0 += CG) {
+    float q[CG][8], tot[CG];
+#pragma unroll
+    for (int j = 0; j < CG; ++j) {
+      const int col = (c0 + j) * 256 + lane * 8;
+      float run = 0.0f;
+      const bool live = c0 + j < c_end;
+      if (live && vec && col + 8 <= H) {
+        const uint4 gv = __ldg(reinterpret_cast<const uint4*>(g + col));
+        const float4 x0 = __ldg(reinterpret_cast<const float4*>(xr + col));
+        const float4 x1 = __ldg(reinterpret_cast<const float4*>(xr + col + 4));
+        const uint32_t gw[4] = {gv.x, gv.y, gv.z, gv.w};
+        const float xv[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const float w = __uint_as_float((k & 1) ? (gw[k >> 1] & 0xFFFF0000u) : (gw[k >> 1] << 16));
+          const float p = w * xv[k];
+          run += p;
+          q[j][k] = run;
+          pa += fabsf(p);
+        }
+      } else {
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const int c = col + k;
+          const float p = (live && c < H) ? bf16_widen(g[c]) * xr[c] : 0.0f;
+          run += p;
+          q[j][k] = run;
+          pa += fabsf(p);
+        }
+      }
+      tot[j] = run;
+    }
+    float incl[CG];
+#pragma unroll
+    for (int j = 0; j < CG; ++j) incl[j] = tot[j];
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+#pragma unroll
+      for (int j = 0; j < CG; ++j) {
+        const float v = __shfl_up_sync(0xffffffffu, incl[j], o);
+        if (lane >= o) incl[j] += v;
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < CG; ++j) {
+      if (sabs) {
+        const float base = offset + (carry + (incl[j] - tot[j]));
+#pragma unroll
+        for (int k = 0; k < 8; ++k) sa += fabsf(base + q[j][k]);
+      }
+      carry += __shfl_sync(0xffffffffu, incl[j], 31);
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    sa += __shfl_xor_sync(0xffffffffu, sa, o);
+    pa += __shfl_xor_sync(0xffffffffu, pa, o);
+  }
+  if (sabs) *sabs = sa;
+  if (pabs) *pabs = pa;
+  return carry;
+}
+
+// Launch 1, grid (E, M) x 4 warps: activation quant (spread over all warps)
+// and one router logit per CTA, in fp32, with a rigorous bound on how far
+// the reference's sequential chain can be from it. The row is split over 4
+// warps; pass 1 gives each warp's segment total, pass 2 (L2-resident data)
+// re-walks the segment from its exact offset to sum |t_i|. Notation: p_i
+// exact products, q_i = fl(p_i), P = sum |q_i|, s_i exact prefix sums, t_i
+// the computed ones (depth d: 8 in-lane + 5 scan + the segment's chunk
+// carries + 3 offset/base adds + 4 for the cross-warp sums), zc the computed
+// total. Then |zc - z| <= (d + 1) u P, |s_i - t_i| <= (d + 1) u P and
+// |z_ref - z| <= u sum_i |s_i| (+ u P for the public router's rounded
+// products), so
+//   zb = u sum|t_i| + (d + 1) u P (1 + n u) (+ u P)   (x 1.01 for the fp32
+// evaluation of the bound itself).
+__global__ void __launch_bounds__(kLogitWarps * 32) router_logits_kernel(const RouterArgs a) {
+  __shared__ float seg_tot[kLogitWarps], seg_abs[kLogitWarps], seg_p[kLogitWarps];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int e = blockIdx.x, t = blockIdx.y;
+  if (a.xq) {
+    const int nb = (a.H + 127) / 128;
+    const int gw = (blockIdx.y * gridDim.x + blockIdx.x) * kLogitWarps + warp;
+    const int nw = gridDim.x * gridDim.y * kLogitWarps;
+    for (int task = gw; task < a.M * nb; task += nw) {
+      const int r = task / nb, b = task % nb;
+      const float* xr = a.x + static_cast<size_t>(r) * a.H + b * 128;
+      const int len = min(128, a.H - b * 128);
+      float v[4];
+      float amax = 0.f;
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const int i = lane + 32 * k;
+        v[k] = i < len ? xr[i] : 0.f;
+        amax = fmaxf(amax, fabsf(v[k]));
+      }
+      amax = warp_max(amax);
+      const float scale = pow2_scale_448(amax);
+      const float inv = 1.0f / scale;
+      if (lane == 0) a.xs[static_cast<size_t>(r) * nb + b] = scale;
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const int i = lane + 32 * k;
+        if (i < len) {
+          float q = v[k] * inv;
+          q = q > 448.f ? 448.f : (q < -448.f ? -448.f : q);
+          a.xq[static_cast<size_t>(r) * a.H + b * 128 + i] = e4m3_round_f16(q);
+        }
+      }
+    }
+  }
+  const uint16_t* g = a.gate + static_cast<size_t>(e) * a.H;
+  const float* xr = a.x + static_cast<size_t>(t) * a.H;
+  const int nch = (a.H + 255) / 256;
+  const int per = (nch + kLogitWarps - 1) / kLogitWarps;
+  const int cb = min(nch, warp * per), ce = min(nch, cb + per);
+  float pw = 0.0f;
+  const float tw = warp_segment(g, xr, a.H, cb, ce, 0.0f, nullptr, &pw);
+  if (lane == 0) {
+    seg_tot[warp] = tw;
+    seg_p[warp] = pw;
+  }
+  __syncthreads();
+  float off = 0.0f;
+  for (int w = 0; w < warp; ++w) off += seg_tot[w];
+  float aw = 0.0f;
+  warp_segment(g, xr, a.H, cb, ce, off, &aw, nullptr);
+  if (lane == 0) seg_abs[warp] = aw;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float z = 0.0f, sabs = 0.0f, P = 0.0f;
+    for (int w = 0; w < kLogitWarps; ++w) {
+      z += seg_tot[w];
+      sabs += seg_abs[w];
+      P += seg_p[w];
+    }
+    const double u = kU, n = static_cast<double>(a.H);
+    const double d = 20.0 + static_cast<double>(per);
+    const size_t o = static_cast<size_t>(t) * a.E + e;
+    a.zd[o] = static_cast<double>(z);
+    a.zb[o] = 1.01 * (u * static_cast<double>(sabs) +
+                      (d + 1.0) * u * static_cast<double>(P) * (1.0 + n * u) +
+                      (a.public_router ? u * static_cast<double>(P) : 0.0)) + 1e-40 * n;
+  }
+}
+
+__device__ __forceinline__ Cand warp_best(Cand c) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {
     Cand n;
@@ -132,28 +287,31 @@ __device__ Cand block_best(Cand c, Cand* red) {
     n.id = __shfl_xor_sync(0xffffffffu, c.id, o);
     if (better(n, c)) c = n;
   }
-  if (lane == 0) red[w] = c;
-  __syncthreads();
-  Cand r = red[0];
-  for (int i = 1; i < static_cast<int>(blockDim.x >> 5); ++i)
-    if (better(red[i], r)) r = red[i];
-  __syncthreads();
-  return r;
+  return c;
 }
 
-// Top-k by the reference rule over `val`; writes order[0..k).
-__device__ void select_topk(const float* val, int E, int k, unsigned char* used, int* order,
-                            Cand* red) {
+// Block-wide top-k by the reference rule; order[] in selection order.
+__device__ void block_topk(const float* val, unsigned char* used, int E, int k, int* order,
+                           Cand* red) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int nwarp = blockDim.x >> 5;
+  for (int e = threadIdx.x; e < E; e += blockDim.x) used[e] = 0;
+  __syncthreads();
   for (int j = 0; j < k; ++j) {
     Cand c{0.f, -1};
     for (int e = threadIdx.x; e < E; e += blockDim.x) {
       const float v = val[e];
-      if (used[e] || !(v > -INFINITY)) continue;  // excludes -inf and NaN
+      if (used[e] || !(v > -INFINITY)) continue;  // -inf and NaN never win
       const Cand n{v, e};
       if (better(n, c)) c = n;
     }
-    const Cand b = block_best(c, red);
+    c = warp_best(c);
+    if (lane == 0) red[warp] = c;
+    __syncthreads();
     if (threadIdx.x == 0) {
+      Cand b = red[0];
+      for (int w = 1; w < nwarp; ++w)
+        if (better(red[w], b)) b = red[w];
       order[j] = b.id;
       if (b.id >= 0) used[b.id] = 1;
     }
@@ -161,41 +319,156 @@ __device__ void select_topk(const float* val, int E, int k, unsigned char* used,
   }
 }
 
-// One CTA per token: scores, selection (with exact fallback), weights, sort.
-__global__ void __launch_bounds__(kSelThreads) router_select_kernel(const SelectArgs a) {
-  extern __shared__ unsigned char smem[];
-  const int E = a.E;
-  float* choice = reinterpret_cast<float*>(smem);
-  float* score = choice + E;
-  double* lo = reinterpret_cast<double*>(score + E + (E & 1));
-  double* hi = lo + E;
-  unsigned char* used = reinterpret_cast<unsigned char*>(hi + E);
-  __shared__ Cand red[kSelThreads / 32];
-  __shared__ int order[kMaxTopk];
-  __shared__ float band[2];
-  __shared__ int n_cand;
-  const int t = blockIdx.x;
-  const int tok = a.token_ids ? a.token_ids[t] : 0;
-  const bool hash = a.tid2eid != nullptr;
+// Token->expert permutation (moe_forward_batch grouping,
+// src/dsv4/dsv4_model.c:6925-6926, expert_forward_batch_routes :6486): unique
+// experts ascending; each expert's routes in token order, packed into items
+// of <= kItemTok routes. Route (t,k) owns slot t*topk+k. Also the
+// shared-expert items (all tokens). One CTA; idx staged in shared memory.
+__device__ void block_plan(const RouterArgs& a, int* cnt, int* ids) {
+  const int E = a.E, K = a.topk, R = a.M * a.topk;
+  for (int r = threadIdx.x; r < R; r += blockDim.x) ids[r] = a.idx[r];
+  __syncthreads();
+  for (int e = threadIdx.x; e < E; e += blockDim.x) {
+    int n = 0;
+    for (int r = 0; r < R; ++r) n += (ids[r] == e);
+    cnt[e] = (n + kItemTok - 1) / kItemTok;
+  }
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    // exclusive scan of cnt[0..E) by one warp: 32-element tiles with a carry
+    int carry = 0;
+    for (int b0 = 0; b0 < E; b0 += 32) {
+      const int e = b0 + threadIdx.x;
+      const int v = e < E ? cnt[e] : 0;
+      int incl = v;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int tt = __shfl_up_sync(0xffffffffu, incl, o);
+        if (static_cast<int>(threadIdx.x) >= o) incl += tt;
+      }
+      if (e < E) cnt[e] = carry + incl - v;
+      carry += __shfl_sync(0xffffffffu, incl, 31);
+    }
+    if (threadIdx.x == 0) {
+      a.counters[0] = carry;
+      a.counters[3] = (a.M + kItemTok - 1) / kItemTok;
+    }
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < E; e += blockDim.x) {
+    int item = cnt[e];
+    GemvItem gu, dn;
+    gu.mat = dn.mat = e;
+    gu.ntok = dn.ntok = 0;
+    for (int r = 0; r < R; ++r) {
+      if (ids[r] != e) continue;
+      gu.tok[gu.ntok].x = r / K;
+      gu.tok[gu.ntok].y = r;
+      dn.tok[dn.ntok].x = r;
+      dn.tok[dn.ntok].y = r;
+      gu.ntok++;
+      dn.ntok++;
+      if (gu.ntok == kItemTok) {
+        a.items_gu[item] = gu;
+        a.items_dn[item] = dn;
+        ++item;
+        gu.ntok = dn.ntok = 0;
+      }
+    }
+    if (gu.ntok > 0) {
+      for (int i = gu.ntok; i < kItemTok; ++i) { gu.tok[i] = gu.tok[0]; dn.tok[i] = dn.tok[0]; }
+      a.items_gu[item] = gu;
+      a.items_dn[item] = dn;
+    }
+  }
+  const int nsh = (a.M + kItemTok - 1) / kItemTok;
+  for (int j = threadIdx.x; j < nsh; j += blockDim.x) {
+    GemvItem it;
+    it.mat = 0;
+    it.ntok = min(kItemTok, a.M - j * kItemTok);
+    for (int i = 0; i < kItemTok; ++i) {
+      const int tt = min(j * kItemTok + i, a.M - 1);
+      it.tok[i].x = tt;
+      it.tok[i].y = tt;
+    }
+    a.items_sh[j] = it;
+  }
+}
 
+struct SelectSmem {
+  float* x;       // [H] token activation (exact replay)
+  double* lo;     // [E]
+  double* hi;     // [E]
+  float* choice;  // [E]
+  float* score;   // [E]
+  int* cnt;       // [E] plan
+  int* ids;       // [R] plan
+  unsigned char* used;  // [E]
+};
+
+__host__ __device__ inline size_t select_smem_bytes(int H, int E, int R, SelectSmem* sm,
+                                                    unsigned char* base) {
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    unsigned char* p = base + off;
+    off += (bytes + 15) & ~static_cast<size_t>(15);
+    return p;
+  };
+  unsigned char* px = take(static_cast<size_t>(H) * 4);
+  unsigned char* plo = take(static_cast<size_t>(E) * 8);
+  unsigned char* phi = take(static_cast<size_t>(E) * 8);
+  unsigned char* pc = take(static_cast<size_t>(E) * 4);
+  unsigned char* ps = take(static_cast<size_t>(E) * 4);
+  unsigned char* pn = take(static_cast<size_t>(E) * 4);
+  unsigned char* pi = take(static_cast<size_t>(R) * 4);
+  unsigned char* pu = take(static_cast<size_t>(E));
+  if (sm) {
+    sm->x = reinterpret_cast<float*>(px);
+    sm->lo = reinterpret_cast<double*>(plo);
+    sm->hi = reinterpret_cast<double*>(phi);
+    sm->choice = reinterpret_cast<float*>(pc);
+    sm->score = reinterpret_cast<float*>(ps);
+    sm->cnt = reinterpret_cast<int*>(pn);
+    sm->ids = reinterpret_cast<int*>(pi);
+    sm->used = pu;
+  }
+  return off;
+}
+
+// Launch 2, one CTA per token: selection with the reference's rule and the
+// margin check (exact replay of the band on a near tie), combine weights and
+// the id sort (src/dsv4/dsv4_model.c:6615-6676; public twin
+// src/dsv4/dsv4_ops.c:473-545); the last CTA to finish builds the plan.
+__global__ void __launch_bounds__(kSelThreads) router_select_kernel(const RouterArgs a) {
+  extern __shared__ __align__(16) unsigned char ssm[];
+  __shared__ Cand red[kSelThreads / 32];
+  __shared__ double rlo[kSelThreads / 32], rhi[kSelThreads / 32];
+  __shared__ int order[kMaxTopk];
+  __shared__ int is_last;
+  SelectSmem sm;
+  select_smem_bytes(a.H, a.E, a.M * a.topk, &sm, ssm);
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int t = blockIdx.x;
+  const int E = a.E;
   for (int e = threadIdx.x; e < E; e += blockDim.x) {
     const size_t o = static_cast<size_t>(t) * E + e;
     const double z = a.zd[o];
     const float b = a.bias ? a.bias[e] : 0.0f;
     const float s = sqrt_softplus_f(static_cast<float>(z));
-    score[e] = s;
-    choice[e] = s + b;
-    const double sm = sqrt_softplus_d(z);
-    const double rad = 0.5 * a.zb[o] + 1e-6 * (fabs(sm) + fabs(static_cast<double>(b))) + 1e-37;
-    lo[e] = sm + b - rad;
-    hi[e] = sm + b + rad;
-    used[e] = 0;
+    sm.score[e] = s;
+    sm.choice[e] = s + b;
+    // |d sqrt(softplus)/dz| <= 0.5 (|z - z_ref| <= zb, plus the rounding of
+    // z to fp32); 1e-6 relative covers the few-ulp differences of expf,
+    // log1pf, sqrtf and the bias add between glibc and CUDA.
+    const double rad = 0.5 * (a.zb[o] + kU * fabs(z)) +
+                       1e-6 * (fabs(static_cast<double>(s)) + fabs(static_cast<double>(b))) + 1e-37;
+    sm.lo[e] = static_cast<double>(s) + b - rad;
+    sm.hi[e] = static_cast<double>(s) + b + rad;
   }
-  if (threadIdx.x == 0) n_cand = 0;
   __syncthreads();
-
-  if (hash) {
+  if (a.tid2eid) {
     if (threadIdx.x == 0) {
+      const int tok = a.token_ids ? a.token_ids[t] : 0;
       const int tk = (tok >= 0 && tok < a.hash_vocab) ? tok : 0;
       for (int k = 0; k < a.topk; ++k) {
         const int64_t e = a.tid2eid[static_cast<size_t>(tk) * a.topk + k];
@@ -204,64 +477,46 @@ __global__ void __launch_bounds__(kSelThreads) router_select_kernel(const Select
     }
     __syncthreads();
   } else {
-    select_topk(choice, E, a.topk, used, order, red);
-    // margin check: min lower bound of the selected vs max upper bound of the rest
+    block_topk(sm.choice, sm.used, E, a.topk, order, red);
     double mlo = INFINITY, mhi = -INFINITY;
-    bool nan_seen = false;
+    int nan_seen = 0;
     for (int e = threadIdx.x; e < E; e += blockDim.x) {
-      if (isnan(lo[e]) || isnan(hi[e])) nan_seen = true;
-      if (used[e]) mlo = fmin(mlo, lo[e]);
-      else mhi = fmax(mhi, hi[e]);
+      if (isnan(sm.lo[e]) || isnan(sm.hi[e])) nan_seen = 1;
+      if (sm.used[e]) mlo = fmin(mlo, sm.lo[e]);
+      else mhi = fmax(mhi, sm.hi[e]);
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
       mlo = fmin(mlo, __shfl_xor_sync(0xffffffffu, mlo, o));
       mhi = fmax(mhi, __shfl_xor_sync(0xffffffffu, mhi, o));
     }
-    const int any_nan = __syncthreads_or(nan_seen ? 1 : 0);
-    __shared__ double wlo[kSelThreads / 32], whi[kSelThreads / 32];
-    if ((threadIdx.x & 31) == 0) { wlo[threadIdx.x >> 5] = mlo; whi[threadIdx.x >> 5] = mhi; }
-    __syncthreads();
-    if (threadIdx.x == 0) {
-      double l = wlo[0], h = whi[0];
-      for (int i = 1; i < kSelThreads / 32; ++i) { l = fmin(l, wlo[i]); h = fmax(h, whi[i]); }
-      band[0] = static_cast<float>(l);
-      band[1] = static_cast<float>(h);
-      // the band is used only to pick candidates; keep it in double precision
-      wlo[0] = l;
-      whi[0] = h;
+    if (lane == 0) { rlo[warp] = mlo; rhi[warp] = mhi; }
+    const int any_nan = __syncthreads_or(nan_seen);
+    mlo = rlo[0];
+    mhi = rhi[0];
+    for (int w = 1; w < static_cast<int>(blockDim.x >> 5); ++w) {
+      mlo = fmin(mlo, rlo[w]);
+      mhi = fmax(mhi, rhi[w]);
     }
-    __syncthreads();
-    const double blo = wlo[0], bhi = whi[0];
-    const bool safe = !any_nan && (blo > bhi);
-    if (!safe) {
-      // replay the reference's fp32 logit chain for every expert in the band
+    if (any_nan || !(mlo > mhi)) {
+      // near tie: replay the reference's fp32 chain for every expert whose
+      // interval reaches into the ambiguous band, then select again
       const float* xr = a.x + static_cast<size_t>(t) * a.H;
-      for (int e = threadIdx.x; e < E; e += blockDim.x) {
-        const bool cand = any_nan || (hi[e] >= blo && lo[e] <= bhi);
-        if (!cand) continue;
-        atomicAdd(&n_cand, 1);
-        const uint16_t* g = a.gate + static_cast<size_t>(e) * a.H;
-        float z = 0.0f;
-        if (a.public_router) {
-          for (int c = 0; c < a.H; ++c) {
-            const float p = __fmul_rn(bf16_widen(g[c]), xr[c]);
-            z = __fadd_rn(z, p);
-          }
-        } else {
-          for (int c = 0; c < a.H; ++c) z = fmaf(bf16_widen(g[c]), xr[c], z);
-        }
-        const float s = sqrt_softplus_f(z);
-        score[e] = s;
-        choice[e] = s + (a.bias ? a.bias[e] : 0.0f);
-      }
-      for (int e = threadIdx.x; e < E; e += blockDim.x) used[e] = 0;
+      for (int i = threadIdx.x; i < a.H; i += blockDim.x) sm.x[i] = xr[i];
       __syncthreads();
-      select_topk(choice, E, a.topk, used, order, red);
+      for (int e = threadIdx.x; e < E; e += blockDim.x) {
+        if (!(any_nan || (sm.hi[e] >= mlo && sm.lo[e] <= mhi))) continue;
+        const float z = exact_logit(a.gate + static_cast<size_t>(e) * a.H, sm.x, a.H,
+                                    a.public_router);
+        const float s = sqrt_softplus_f(z);
+        sm.score[e] = s;
+        sm.choice[e] = s + (a.bias ? a.bias[e] : 0.0f);
+      }
+      __syncthreads();
+      block_topk(sm.choice, sm.used, E, a.topk, order, red);
       if (threadIdx.x == 0) atomicAdd(&a.counters[2], 1);
     }
   }
-
   if (threadIdx.x == 0) {
     const int K = a.topk;
     int id[kMaxTopk];
@@ -269,21 +524,18 @@ __global__ void __launch_bounds__(kSelThreads) router_select_kernel(const Select
     float sum = 0.0f;
     for (int k = 0; k < K; ++k) {
       id[k] = order[k];
-      sum += id[k] >= 0 ? score[id[k]] : 0.0f;
+      sum += id[k] >= 0 ? sm.score[id[k]] : 0.0f;
     }
     if (a.public_router) {
-      // dsv4_router (src/dsv4/dsv4_ops.c:528-531)
-      const float inv = sum > 0.0f ? 1.0f / sum : 0.0f;
-      for (int k = 0; k < K; ++k) w[k] = (id[k] >= 0 ? score[id[k]] : 0.f) * inv * a.route_scale;
+      const float inv = sum > 0.0f ? 1.0f / sum : 0.0f;        // dsv4_ops.c:528-531
+      for (int k = 0; k < K; ++k) w[k] = (id[k] >= 0 ? sm.score[id[k]] : 0.f) * inv * a.route_scale;
     } else if (sum > 0.0f) {
-      // moe_forward (src/dsv4/dsv4_model.c:6651-6658)
-      const float rs = a.route_scale / sum;
-      for (int k = 0; k < K; ++k) w[k] = (id[k] >= 0 ? score[id[k]] : 0.f) * rs;
+      const float rs = a.route_scale / sum;                   // dsv4_model.c:6651-6658
+      for (int k = 0; k < K; ++k) w[k] = (id[k] >= 0 ? sm.score[id[k]] : 0.f) * rs;
     } else {
       for (int k = 0; k < K; ++k) w[k] = 0.0f;
     }
-    // the reference's exchange sort by ascending id, carrying weights (:6669)
-    for (int i = 0; i < K; ++i)
+    for (int i = 0; i < K; ++i)                               // exchange sort, :6669-6676
       for (int j = i + 1; j < K; ++j)
         if (id[j] < id[i]) {
           const int ti = id[i]; id[i] = id[j]; id[j] = ti;
@@ -294,78 +546,15 @@ __global__ void __launch_bounds__(kSelThreads) router_select_kernel(const Select
       a.wt[static_cast<size_t>(t) * K + k] = w[k];
     }
   }
-}
-
-// Per-forward setup that depends on the token count: shared-expert items.
-__global__ void moe_prep_kernel(GemvItem* items_sh, int n_tokens, int* counters) {
-  const int j = threadIdx.x + blockIdx.x * blockDim.x;
-  const int n_items = (n_tokens + kItemTok - 1) / kItemTok;
-  if (j == 0) counters[3] = n_items;
-  if (j < n_items) {
-    GemvItem it;
-    it.mat = 0;
-    it.ntok = min(kItemTok, n_tokens - j * kItemTok);
-    for (int i = 0; i < kItemTok; ++i) {
-      const int t = min(j * kItemTok + i, n_tokens - 1);
-      it.tok[i].x = t;
-      it.tok[i].y = t;
-    }
-    items_sh[j] = it;
-  }
-}
-
-// Token->expert permutation (moe_forward_batch grouping,
-// src/dsv4/dsv4_model.c:6925-6926 and expert_forward_batch_routes :6486):
-// unique experts ascending; each expert's routes in token order, packed into
-// items of <= kItemTok routes. Route (t,k) owns slot t*topk+k.
-__global__ void moe_plan_kernel(const int* idx, int n_tokens, int topk, int E,
-                                GemvItem* items_gu, GemvItem* items_dn, int* counters) {
-  extern __shared__ int cnt[];  // [E] item count per expert, then exclusive offsets
-  for (int e = threadIdx.x; e < E; e += blockDim.x) {
-    int n = 0;
-    for (int r = 0; r < n_tokens * topk; ++r) n += (idx[r] == e);
-    cnt[e] = (n + kItemTok - 1) / kItemTok;
-  }
+  if (!a.items_gu) return;
+  __threadfence();
   __syncthreads();
-  if (threadIdx.x == 0) {
-    int run = 0;
-    for (int e = 0; e < E; ++e) {
-      const int c = cnt[e];
-      cnt[e] = run;
-      run += c;
-    }
-    counters[0] = run;
-  }
+  if (threadIdx.x == 0) is_last = atomicAdd(&a.counters[1], 1) == static_cast<int>(gridDim.x) - 1;
   __syncthreads();
-  for (int e = threadIdx.x; e < E; e += blockDim.x) {
-    int item = cnt[e];
-    GemvItem gu, dn;
-    gu.mat = dn.mat = e;
-    gu.ntok = dn.ntok = 0;
-    for (int t = 0; t < n_tokens; ++t) {
-      for (int k = 0; k < topk; ++k) {
-        const int slot = t * topk + k;
-        if (idx[slot] != e) continue;
-        gu.tok[gu.ntok].x = t;
-        gu.tok[gu.ntok].y = slot;
-        dn.tok[dn.ntok].x = slot;
-        dn.tok[dn.ntok].y = slot;
-        gu.ntok++;
-        dn.ntok++;
-        if (gu.ntok == kItemTok) {
-          items_gu[item] = gu;
-          items_dn[item] = dn;
-          ++item;
-          gu.ntok = dn.ntok = 0;
-        }
-      }
-    }
-    if (gu.ntok > 0) {
-      for (int i = gu.ntok; i < kItemTok; ++i) { gu.tok[i] = gu.tok[0]; dn.tok[i] = dn.tok[0]; }
-      items_gu[item] = gu;
-      items_dn[item] = dn;
-    }
-  }
+  if (!is_last) return;
+  __threadfence();
+  block_plan(a, sm.cnt, sm.ids);
+  if (threadIdx.x == 0) a.counters[1] = 0;  // ticket ready for the next launch
 }
 
 // out[t] = bf16( sum_k routed[t*topk+k] (ascending id order) + shared[t] )
@@ -464,30 +653,44 @@ void moe_workspace_carve(MoeWorkspace* ws, const MoeConfig& c, int M, void* base
 
 static cudaError_t route_impl(const MoeConfig& c, const MoeWeights& w, const MoeWorkspace& ws,
                               const float* x, const int* token_ids, int M, int public_router,
-                              cudaStream_t st) {
-  const int E = c.n_experts;
-  dim3 lg((E + 7) / 8, M);
-  router_logits_kernel<<<lg, 256, 0, st>>>(x, c.hidden, w.gate_w, E, ws.zd, ws.zb,
-                                           public_router);
-  SelectArgs sa;
-  sa.x = x;
-  sa.H = c.hidden;
-  sa.E = E;
-  sa.topk = c.topk;
-  sa.gate = w.gate_w;
-  sa.bias = w.bias;
-  sa.tid2eid = w.tid2eid;
-  sa.hash_vocab = c.hash_vocab;
-  sa.token_ids = token_ids;
-  sa.zd = ws.zd;
-  sa.zb = ws.zb;
-  sa.route_scale = c.route_scale;
-  sa.public_router = public_router;
-  sa.idx = ws.idx;
-  sa.wt = ws.wt;
-  sa.counters = ws.counters;
-  const size_t smem = static_cast<size_t>(E) * (4 + 4 + 8 + 8 + 1) + 16;
-  router_select_kernel<<<M, kSelThreads, smem, st>>>(sa);
+                              bool plan, cudaStream_t st) {
+  RouterArgs a{};
+  a.x = x;
+  a.H = c.hidden;
+  a.M = M;
+  a.E = c.n_experts;
+  a.topk = c.topk;
+  a.gate = w.gate_w;
+  a.bias = w.bias;
+  a.tid2eid = w.tid2eid;
+  a.hash_vocab = c.hash_vocab;
+  a.token_ids = token_ids;
+  a.route_scale = c.route_scale;
+  a.public_router = public_router;
+  a.zd = ws.zd;
+  a.zb = ws.zb;
+  a.idx = ws.idx;
+  a.wt = ws.wt;
+  a.counters = ws.counters;
+  if (plan) {
+    a.xq = ws.xq;
+    a.xs = ws.xs;
+    a.items_gu = ws.items_gu;
+    a.items_dn = ws.items_dn;
+    a.items_sh = ws.items_sh;
+  }
+  if (plan && ws.timing) cudaEventRecord(ws.timing[4], st);
+  router_logits_kernel<<<dim3(c.n_experts, M), kLogitWarps * 32, 0, st>>>(a);
+  if (plan && ws.timing) cudaEventRecord(ws.timing[5], st);
+  const size_t smem = select_smem_bytes(c.hidden, c.n_experts, M * c.topk, nullptr, nullptr);
+  if (smem > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(router_select_kernel,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(smem));
+    if (e != cudaSuccess) return e;
+  }
+  router_select_kernel<<<M, kSelThreads, smem, st>>>(a);
+  if (plan && ws.timing) cudaEventRecord(ws.timing[6], st);
   return cudaGetLastError();
 }
 
@@ -496,7 +699,7 @@ cudaError_t moe_route(const MoeConfig& c, const MoeWeights& w, const MoeWorkspac
                       cudaStream_t st) {
   if (M <= 0) return cudaSuccess;
   if (M > ws.max_tokens || c.topk > kMaxTopk) return cudaErrorInvalidValue;
-  return route_impl(c, w, ws, x, token_ids, M, public_router, st);
+  return route_impl(c, w, ws, x, token_ids, M, public_router, false, st);
 }
 
 cudaError_t moe_forward(const MoeConfig& c, const MoeWeights& w, const MoeWorkspace& ws,
@@ -504,13 +707,12 @@ cudaError_t moe_forward(const MoeConfig& c, const MoeWeights& w, const MoeWorksp
                         cudaStream_t st) {
   if (M <= 0) return cudaSuccess;
   if (M > ws.max_tokens || c.topk > kMaxTopk || c.n_experts <= 0) return cudaErrorInvalidValue;
-  const int H = c.hidden, I = c.moe_inter, K = c.topk, E = c.n_experts;
+  const int H = c.hidden, I = c.moe_inter, K = c.topk;
   const int R = M * K;
   cudaError_t err;
 
-  moe_prep_kernel<<<(M + kItemTok * 128 - 1) / (kItemTok * 128), 128, 0, st>>>(ws.items_sh, M,
-                                                                              ws.counters);
-  if ((err = launch_quant_fp8(x, H, H, M, ws.xq, ws.xs, H, st)) != cudaSuccess) return err;
+  // router: quant + exact logits + selection + expert plan, one launch
+  if ((err = route_impl(c, w, ws, x, token_ids, M, 0, true, st)) != cudaSuccess) return err;
   const QAct act{ws.xq, ws.xs, H, nullptr};
 
   SideStream& side = side_stream();
@@ -557,9 +759,6 @@ cudaError_t moe_forward(const MoeConfig& c, const MoeWeights& w, const MoeWorksp
     cudaEventRecord(side.join, side.s);
   }
 
-  if ((err = route_impl(c, w, ws, x, token_ids, M, 0, st)) != cudaSuccess) return err;
-  moe_plan_kernel<<<1, 256, E * sizeof(int), st>>>(ws.idx, M, K, E, ws.items_gu, ws.items_dn,
-                                                   ws.counters);
 
   const int nt = nt_bucket(std::min(M, kItemTok));
   const size_t w13 = static_cast<size_t>(I) * (H / 2), s13 = static_cast<size_t>(I) * (H / 32);
@@ -569,7 +768,7 @@ cudaError_t moe_forward(const MoeConfig& c, const MoeWeights& w, const MoeWorksp
   gu.w_stride = w13; gu.s_stride = s13;
   gu.in = H; gu.rows = I; gu.act = act;
   gu.Y[0] = ws.gate; gu.Y[1] = ws.up;
-  gu.items = ws.items_gu; gu.n_items = ws.counters; gu.max_items = R;
+  gu.items = ws.items_gu; gu.n_items = ws.counters; gu.max_items = R; gu.n_mats = c.n_experts;
   if (ws.timing) cudaEventRecord(ws.timing[0], st);
   if ((err = launch_fp4_gemv(gu, true, nt, st)) != cudaSuccess) return err;
   if (ws.timing) cudaEventRecord(ws.timing[1], st);
@@ -581,7 +780,7 @@ cudaError_t moe_forward(const MoeConfig& c, const MoeWeights& w, const MoeWorksp
   dn.w_stride = w2; dn.s_stride = s2;
   dn.in = I; dn.rows = H; dn.act = QAct{ws.qy, ws.qys, I, nullptr};
   dn.Y[0] = ws.routed;
-  dn.items = ws.items_dn; dn.n_items = ws.counters; dn.max_items = R;
+  dn.items = ws.items_dn; dn.n_items = ws.counters; dn.max_items = R; dn.n_mats = c.n_experts;
   if (ws.timing) cudaEventRecord(ws.timing[2], st);
   if ((err = launch_fp4_gemv(dn, false, nt, st)) != cudaSuccess) return err;
   if (ws.timing) cudaEventRecord(ws.timing[3], st);

@@ -52,8 +52,9 @@ struct MoeWorkspace {
   float* sh_qys = nullptr;   // [M][I/128]
   float* shared = nullptr;   // [M][H]
   size_t bytes = 0;
-  // Optional timing: when set, events are recorded around the routed expert
-  // GEMV launches (gate/up begin/end, down begin/end) on the forward stream.
+  // Optional timing: when set, events are recorded on the forward stream
+  // around the routed expert GEMV launches ([0..1] gate/up, [2..3] down) and
+  // the router ([4] before the logits, [5] after them, [6] after selection).
   cudaEvent_t* timing = nullptr;
 };
 

@@ -84,6 +84,12 @@ def _ptrs(arrs, t):
     return (t * len(arrs))(*[a.ctypes.data_as(t) for a in arrs])
 
 
+def device_error(clear: bool = False) -> int:
+    v = C.c_uint()
+    _check(lib.dsv4cuda_device_error(C.byref(v), 1 if clear else 0))
+    return v.value
+
+
 def set_abort_on_error(flag: bool) -> int:
     return lib.dsv4cuda_set_abort_on_error(1 if flag else 0)
 

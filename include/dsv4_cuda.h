@@ -121,6 +121,10 @@ int dsv4cuda_init(int device);
 void dsv4cuda_shutdown(void);
 /* Last error recorded on the calling thread ("" if none). */
 const char *dsv4cuda_last_error(void);
+/* Device-side error flags of the current device (synchronous): bit 0 = a
+ * kernel gave up waiting on a shared-memory barrier (bounded wait, the
+ * results of that launch are invalid). clear != 0 resets them. */
+int dsv4cuda_device_error(unsigned int *flags, int clear);
 /* 1 (default): a drop-in call that hits a CUDA error exits(1) like the
  * reference's fatal paths; 0: record the error and return. Returns the
  * previous mode. */
@@ -201,6 +205,9 @@ int dsv4cuda_moe_route(dsv4cuda_moe_layer *L, const float *x, const int *token_i
 int dsv4cuda_moe_timing_begin(dsv4cuda_moe_layer *L);
 int dsv4cuda_moe_timing_end(dsv4cuda_moe_layer *L, int *n_forwards, float *gateup_ms,
                             float *down_ms);
+/* Same, also returning the summed router logit and selection milliseconds. */
+int dsv4cuda_moe_timing_end2(dsv4cuda_moe_layer *L, int *n_forwards, float *gateup_ms,
+                             float *down_ms, float *logits_ms, float *select_ms);
 /* Device bytes the layer holds (weights it owns + workspace). */
 size_t dsv4cuda_moe_device_bytes(const dsv4cuda_moe_layer *L);
 

@@ -38,4 +38,6 @@ def cuda():
     import dsv4cuda
     dsv4cuda.set_abort_on_error(False)
     dsv4cuda.init(0)
-    return dsv4cuda
+    yield dsv4cuda
+    # no kernel of the session may have given up on a bounded wait
+    assert dsv4cuda.device_error() == 0
