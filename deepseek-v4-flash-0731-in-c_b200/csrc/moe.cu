@@ -85,23 +85,18 @@ struct RouterArgs {
 // The reference's fp32 logit chain, replayed exactly (near-tie path):
 // moe_forward uses fmaf (src/dsv4/dsv4_model.c:299-302); the public
 // dsv4_router rounds the product and the sum separately (dsv4_ops.c:504).
-// x is staged in shared memory; the gate row streams with 8 loads ahead.
+// Both the gate row and x are staged in shared memory, so the replay runs
+// at the FMA chain's latency.
 __device__ float exact_logit(const uint16_t* g, const float* xs, int H, int pub) {
   float z = 0.0f;
-  if ((H & 7) == 0 && (reinterpret_cast<uintptr_t>(g) & 15) == 0) {
-    constexpr int PF = 8;
+  if ((H & 7) == 0) {
     const int n8 = H >> 3;
-    uint4 buf[PF];
+    for (int i = 0; i < n8; i += 4) {
 #pragma unroll
-    for (int j = 0; j < PF; ++j)
-      if (j < n8) buf[j] = __ldg(reinterpret_cast<const uint4*>(g) + j);
-    for (int i = 0; i < n8; i += PF) {
-#pragma unroll
-      for (int j = 0; j < PF; ++j) {
+      for (int j = 0; j < 4; ++j) {
         const int c8 = i + j;
         if (c8 < n8) {
-          const uint4 gv = buf[j];
-          if (c8 + PF < n8) buf[j] = __ldg(reinterpret_cast<const uint4*>(g) + c8 + PF);
+          const uint4 gv = reinterpret_cast<const uint4*>(g)[c8];
           const float4 x0 = reinterpret_cast<const float4*>(xs)[2 * c8];
           const float4 x1 = reinterpret_cast<const float4*>(xs)[2 * c8 + 1];
           const float w[8] = {__uint_as_float(gv.x << 16), __uint_as_float(gv.x & 0xFFFF0000u),
@@ -395,8 +390,12 @@ __device__ void block_plan(const RouterArgs& a, int* cnt, int* ids) {
   }
 }
 
+constexpr int kReplayRows = 4;  // candidate gate rows staged per replay round
+
 struct SelectSmem {
   float* x;       // [H] token activation (exact replay)
+  uint16_t* g;    // [kReplayRows][H] candidate gate rows (exact replay)
+  int* cand;      // [E] candidate list
   double* lo;     // [E]
   double* hi;     // [E]
   float* choice;  // [E]
@@ -415,6 +414,8 @@ __host__ __device__ inline size_t select_smem_bytes(int H, int E, int R, SelectS
     return p;
   };
   unsigned char* px = take(static_cast<size_t>(H) * 4);
+  unsigned char* pg = take(static_cast<size_t>(kReplayRows) * H * 2);
+  unsigned char* pk = take(static_cast<size_t>(E) * 4);
   unsigned char* plo = take(static_cast<size_t>(E) * 8);
   unsigned char* phi = take(static_cast<size_t>(E) * 8);
   unsigned char* pc = take(static_cast<size_t>(E) * 4);
@@ -424,6 +425,8 @@ __host__ __device__ inline size_t select_smem_bytes(int H, int E, int R, SelectS
   unsigned char* pu = take(static_cast<size_t>(E));
   if (sm) {
     sm->x = reinterpret_cast<float*>(px);
+    sm->g = reinterpret_cast<uint16_t*>(pg);
+    sm->cand = reinterpret_cast<int*>(pk);
     sm->lo = reinterpret_cast<double*>(plo);
     sm->hi = reinterpret_cast<double*>(phi);
     sm->choice = reinterpret_cast<float*>(pc);
@@ -444,7 +447,7 @@ __global__ void __launch_bounds__(kSelThreads) router_select_kernel(const Router
   __shared__ Cand red[kSelThreads / 32];
   __shared__ double rlo[kSelThreads / 32], rhi[kSelThreads / 32];
   __shared__ int order[kMaxTopk];
-  __shared__ int is_last;
+  __shared__ int is_last, n_cand;
   SelectSmem sm;
   select_smem_bytes(a.H, a.E, a.M * a.topk, &sm, ssm);
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -502,17 +505,32 @@ __global__ void __launch_bounds__(kSelThreads) router_select_kernel(const Router
       // near tie: replay the reference's fp32 chain for every expert whose
       // interval reaches into the ambiguous band, then select again
       const float* xr = a.x + static_cast<size_t>(t) * a.H;
+      if (threadIdx.x == 0) n_cand = 0;
       for (int i = threadIdx.x; i < a.H; i += blockDim.x) sm.x[i] = xr[i];
       __syncthreads();
-      for (int e = threadIdx.x; e < E; e += blockDim.x) {
-        if (!(any_nan || (sm.hi[e] >= mlo && sm.lo[e] <= mhi))) continue;
-        const float z = exact_logit(a.gate + static_cast<size_t>(e) * a.H, sm.x, a.H,
-                                    a.public_router);
-        const float s = sqrt_softplus_f(z);
-        sm.score[e] = s;
-        sm.choice[e] = s + (a.bias ? a.bias[e] : 0.0f);
-      }
+      for (int e = threadIdx.x; e < E; e += blockDim.x)
+        if (any_nan || (sm.hi[e] >= mlo && sm.lo[e] <= mhi)) sm.cand[atomicAdd(&n_cand, 1)] = e;
       __syncthreads();
+      const int nc = n_cand;
+      for (int c0 = 0; c0 < nc; c0 += kReplayRows) {
+        const int rows = min(kReplayRows, nc - c0);
+        // stage the round's gate rows (coalesced, all threads)
+        for (int r = 0; r < rows; ++r) {
+          const uint16_t* src = a.gate + static_cast<size_t>(sm.cand[c0 + r]) * a.H;
+          uint16_t* dst = sm.g + static_cast<size_t>(r) * a.H;
+          for (int i = threadIdx.x; i < a.H; i += blockDim.x) dst[i] = src[i];
+        }
+        __syncthreads();
+        if (static_cast<int>(threadIdx.x) < rows) {
+          const int e = sm.cand[c0 + threadIdx.x];
+          const float z = exact_logit(sm.g + static_cast<size_t>(threadIdx.x) * a.H, sm.x, a.H,
+                                      a.public_router);
+          const float s = sqrt_softplus_f(z);
+          sm.score[e] = s;
+          sm.choice[e] = s + (a.bias ? a.bias[e] : 0.0f);
+        }
+        __syncthreads();
+      }
       block_topk(sm.choice, sm.used, E, a.topk, order, red);
       if (threadIdx.x == 0) atomicAdd(&a.counters[2], 1);
     }
