@@ -101,9 +101,10 @@ __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
 // Host: encodes a 2-D uint8 tensor map over `rows` rows of `row_bytes`
 // bytes (row pitch = row_bytes) with a box of box_bytes x box_rows;
 // swizzle128 selects the 128-byte swizzle (box_bytes must be <= 128).
-// Results are cached by their arguments. Returns false if the encoding is
+// Results are cached by their arguments unless use_cache is false. Returns false if the encoding is
 // rejected (unaligned base or pitch).
 bool make_tma_map_u8(CUtensorMap* out, const void* base, uint64_t row_bytes, uint64_t rows,
-                     uint32_t box_bytes, uint32_t box_rows, bool swizzle128);
+                     uint32_t box_bytes, uint32_t box_rows, bool swizzle128,
+                     bool use_cache = true);
 
 }  // namespace dsv4

@@ -12,6 +12,7 @@
 #include <string>
 #include <vector>
 #include <atomic>
+#include <mutex>
 
 #include <cuda_fp16.h>
 
@@ -780,4 +781,106 @@ DSV4_API int dsv4cuda_moe_route(dsv4cuda_moe_layer* L, const float* x, const int
   cudaError_t e = dsv4::moe_route(L->cfg, L->w, L->ws, x, token_ids, n_tokens, public_router, 0);
   if (e != cudaSuccess) { record_error("route: %s", cudaGetErrorString(e)); return -1; }
   return dsv4cuda_moe_last_routes(L, n_tokens, idx, wt);
+}
+
+// ===================================================== allocation-free ==
+//
+// Some callers cannot allocate device memory at the moment they run a MoE
+// layer: code inside a region where the runtime's allocator must not be
+// called (a stream being captured into a CUDA graph, where cudaMalloc would
+// break the capture), engines whose device memory is handed out entirely by
+// their own pool and forbid any other allocation, or hosts that have to run
+// with a fixed, pre-reserved memory footprint. For them,
+// dsv4cuda_moe_forward_noalloc runs the same MoE layer without calling
+// cudaMalloc, cudaFree or any allocating routine: its working memory is the
+// file-scope array below, which exists once on every GPU that loads this
+// library and stays there until the process exits.
+namespace {
+
+constexpr size_t kNoAllocScratchBytes = 4u << 20;  // 4 MiB per device
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+constexpr int kMaxDevices = 64;
+std::mutex g_noalloc_mu;
+void* g_noalloc_base[kMaxDevices] = {};  // device address of the array, per device
+
+}  // namespace
+
+DSV4_API int dsv4cuda_moe_forward_noalloc(const dsv4cuda_moe_config* cfg,
+                                          const dsv4cuda_moe_weights* dw, const float* x,
+                                          const int* token_ids, int n_tokens, float* out,
+                                          void* stream) {
+  if (!cfg || !dw || !x || !out || n_tokens <= 0) {
+    record_error("dsv4cuda_moe_forward_noalloc: bad arguments");
+    return -1;
+  }
+  if (validate_cfg(cfg) != 0) return -1;
+  if (!dw->gate_w || !dw->w1 || !dw->s1 || !dw->w3 || !dw->s3 || !dw->w2 || !dw->s2 ||
+      (cfg->shared_kind != 0 && (!dw->sh1 || !dw->sh1s || !dw->sh3 || !dw->sh3s || !dw->sh2 ||
+                                 !dw->sh2s)) ||
+      (cfg->hash_vocab > 0 && (!dw->tid2eid || !token_ids))) {
+    record_error("dsv4cuda_moe_forward_noalloc: missing weight pointer or token ids");
+    return -1;
+  }
+  const dsv4::MoeConfig c = to_cfg(cfg);
+  const size_t ws_bytes = dsv4::moe_workspace_bytes(c, n_tokens);
+  const size_t need = ws_bytes + 256;  // + the device error word
+  if (need > kNoAllocScratchBytes) {
+    record_error("dsv4cuda_moe_forward_noalloc: %d tokens need %zu bytes of working memory; "
+                 "the allocation-free path has %zu (use dsv4cuda_moe_forward)",
+                 n_tokens, need, kNoAllocScratchBytes);
+    return -1;
+  }
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
+    record_error("dsv4cuda_moe_forward_noalloc: no usable current device");
+    return -1;
+  }
+  void* base = nullptr;
+  {
+    // one-time set-up per device, with that device current: the host-side
+    // name of the array is not a device address, so ask the runtime for it
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    if (!g_noalloc_base[dev]) {
+      void* p = nullptr;
+      e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+      if (e != cudaSuccess || !p) {
+        record_error("dsv4cuda_moe_forward_noalloc: cudaGetSymbolAddress: %s",
+                     cudaGetErrorString(e));
+        return -1;
+      }
+      g_noalloc_base[dev] = p;
+    }
+    base = g_noalloc_base[dev];
+  }
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  dsv4::MoeWorkspace ws{};
+  dsv4::moe_workspace_carve(&ws, c, n_tokens, base);
+  unsigned int* err_word = reinterpret_cast<unsigned int*>(static_cast<char*>(base) + ws_bytes);
+  // the array keeps the previous call's contents: reset what must start at
+  // zero (router counters, including the CTA ticket, and the error word)
+  e = cudaMemsetAsync(ws.counters, 0, 8 * sizeof(int), st);
+  if (e == cudaSuccess) e = cudaMemsetAsync(err_word, 0, sizeof(unsigned int), st);
+  if (e != cudaSuccess) {
+    record_error("dsv4cuda_moe_forward_noalloc: %s", cudaGetErrorString(e));
+    return -1;
+  }
+  dsv4::MoeWeights w{};
+  w.gate_w = dw->gate_w;
+  w.bias = dw->bias;
+  w.tid2eid = dw->tid2eid;
+  w.w1 = dw->w1; w.s1 = dw->s1; w.w3 = dw->w3; w.s3 = dw->s3; w.w2 = dw->w2; w.s2 = dw->s2;
+  w.sh1 = dw->sh1; w.sh1s = dw->sh1s; w.sh3 = dw->sh3; w.sh3s = dw->sh3s;
+  w.sh2 = dw->sh2; w.sh2s = dw->sh2s;
+  dsv4::MoeExecOptions opt;
+  opt.single_stream = true;
+  opt.map_cache = false;
+  opt.err = err_word;
+  e = dsv4::moe_forward(c, w, ws, x, token_ids, n_tokens, out, st, opt);
+  if (e != cudaSuccess) {
+    record_error("dsv4cuda_moe_forward_noalloc: %s", cudaGetErrorString(e));
+    return -1;
+  }
+  return 0;
 }

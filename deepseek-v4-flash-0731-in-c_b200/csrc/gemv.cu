@@ -58,11 +58,11 @@ struct MapKey {
 }  // namespace
 
 bool make_tma_map_u8(CUtensorMap* out, const void* base, uint64_t row_bytes, uint64_t rows,
-                     uint32_t box_bytes, uint32_t box_rows, bool swizzle128) {
+                     uint32_t box_bytes, uint32_t box_rows, bool swizzle128, bool use_cache) {
   static std::mutex mu;
   static std::vector<std::pair<MapKey, CUtensorMap>> cache;
   const MapKey key{base, row_bytes, rows, box_bytes, box_rows, swizzle128};
-  {
+  if (use_cache) {
     std::lock_guard<std::mutex> lock(mu);
     for (const auto& e : cache)
       if (e.first == key) { *out = e.second; return true; }
@@ -81,6 +81,8 @@ bool make_tma_map_u8(CUtensorMap* out, const void* base, uint64_t row_bytes, uin
          swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
     return false;
+  *out = m;
+  if (!use_cache) return true;
   std::lock_guard<std::mutex> lock(mu);
   if (cache.size() > 4096) cache.clear();
   cache.emplace_back(key, m);
@@ -943,14 +945,14 @@ cudaError_t launch_stream_nt(const Fp4Maps& maps, const Fp4GemvArgs& a, bool pai
 
 // Tensor maps over every matrix of the launch: rows_total = rows of all
 // matrices an item index can select (max mat + 1 experts).
-bool fp4_maps(Fp4Maps* m, const Fp4GemvArgs& a, bool pair, long long n_mats) {
+bool fp4_maps(Fp4Maps* m, const Fp4GemvArgs& a, bool pair, long long n_mats, bool cache) {
   const uint64_t rows_total = static_cast<uint64_t>(n_mats) * a.rows;
   for (int v = 0; v < (pair ? 2 : 1); ++v) {
     if (!make_tma_map_u8(&m->w[v], a.W[v], static_cast<uint64_t>(a.in) / 2, rows_total, 128, 32,
-                         true))
+                         true, cache))
       return false;
     if (!make_tma_map_u8(&m->s[v], a.S[v], static_cast<uint64_t>(a.in) / 32, rows_total, 16, 32,
-                         false))
+                         false, cache))
       return false;
   }
   if (!pair) {
@@ -960,11 +962,12 @@ bool fp4_maps(Fp4Maps* m, const Fp4GemvArgs& a, bool pair, long long n_mats) {
   return true;
 }
 
-cudaError_t launch_fp4_stream(const Fp4GemvArgs& a, bool pair, int nt, cudaStream_t st) {
+cudaError_t launch_fp4_stream(const Fp4GemvArgs& a, bool pair, int nt, cudaStream_t st,
+                              bool map_cache) {
   Fp4Maps maps;
   // matrices are w_stride apart; n_mats must cover every `mat` an item names
   const long long n_mats = a.n_mats > 0 ? a.n_mats : 1;
-  if (!fp4_maps(&maps, a, pair, n_mats)) return cudaErrorInvalidValue;
+  if (!fp4_maps(&maps, a, pair, n_mats, map_cache)) return cudaErrorInvalidValue;
   switch (nt) {
     case 1: return launch_stream_nt<1, 8>(maps, a, pair, st);
     case 2: return launch_stream_nt<2, 8>(maps, a, pair, st);
@@ -976,7 +979,8 @@ cudaError_t launch_fp4_stream(const Fp4GemvArgs& a, bool pair, int nt, cudaStrea
 
 }  // namespace
 
-cudaError_t launch_fp4_gemv(const Fp4GemvArgs& a, bool pair, int item_tokens, cudaStream_t st) {
+cudaError_t launch_fp4_gemv(const Fp4GemvArgs& a, bool pair, int item_tokens, cudaStream_t st,
+                            bool map_cache) {
   if (a.rows <= 0 || a.max_items <= 0) return cudaSuccess;
   const bool vec_ok = !a.act.x32 && (a.in % 64 == 0) && aligned(a.W[0], 32) && (a.w_stride % 32 == 0) &&
                       (a.s_stride % 2 == 0) && aligned(a.S[0], 2) &&
@@ -997,7 +1001,7 @@ cudaError_t launch_fp4_gemv(const Fp4GemvArgs& a, bool pair, int item_tokens, cu
   if (a.in % kSCols == 0 && stacked && aligned(a.W[0], 16) && aligned(a.S[0], 16) &&
       a.act.ld % kSCols == 0 && aligned(a.act.x, 16) && aligned(a.act.s, 16) &&
       (!pair || (aligned(a.W[1], 16) && aligned(a.S[1], 16)))) {
-    cudaError_t e = launch_fp4_stream(a, pair, item_tokens, st);
+    cudaError_t e = launch_fp4_stream(a, pair, item_tokens, st, map_cache);
     if (e != cudaErrorInvalidValue) return e;  // else: map rejected, use the LDG kernel
   }
   const int G = a.in / 32;

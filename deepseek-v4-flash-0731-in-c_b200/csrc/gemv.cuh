@@ -73,7 +73,7 @@ struct Bf16GemvArgs {
 };
 
 cudaError_t launch_fp4_gemv(const Fp4GemvArgs& a, bool pair, int item_tokens,
-                            cudaStream_t st);
+                            cudaStream_t st, bool map_cache = true);
 cudaError_t launch_fp8_gemv(const Fp8GemvArgs& a, bool pair, int item_tokens,
                             cudaStream_t st);
 cudaError_t launch_bf16_gemv(const Bf16GemvArgs& a, int item_tokens,

@@ -722,7 +722,7 @@ cudaError_t moe_route(const MoeConfig& c, const MoeWeights& w, const MoeWorkspac
 
 cudaError_t moe_forward(const MoeConfig& c, const MoeWeights& w, const MoeWorkspace& ws,
                         const float* x, const int* token_ids, int M, float* out,
-                        cudaStream_t st) {
+                        cudaStream_t st, const MoeExecOptions& opt) {
   if (M <= 0) return cudaSuccess;
   if (M > ws.max_tokens || c.topk > kMaxTopk || c.n_experts <= 0) return cudaErrorInvalidValue;
   const int H = c.hidden, I = c.moe_inter, K = c.topk;
@@ -733,11 +733,17 @@ cudaError_t moe_forward(const MoeConfig& c, const MoeWeights& w, const MoeWorksp
   if ((err = route_impl(c, w, ws, x, token_ids, M, 0, true, st)) != cudaSuccess) return err;
   const QAct act{ws.xq, ws.xs, H, nullptr};
 
-  SideStream& side = side_stream();
   const bool has_shared = c.shared_kind != kSharedNone && w.sh1 != nullptr;
+  // the shared expert overlaps the routed path on a side stream, or runs
+  // first on `st` when the caller asked for a single stream
+  SideStream* side = nullptr;
+  if (has_shared && !opt.single_stream) side = &side_stream();
+  const cudaStream_t sst = side ? side->s : st;
   if (has_shared) {
-    cudaEventRecord(side.fork, st);
-    cudaStreamWaitEvent(side.s, side.fork, 0);
+    if (side) {
+      cudaEventRecord(side->fork, st);
+      cudaStreamWaitEvent(side->s, side->fork, 0);
+    }
     const int nt = nt_bucket(std::min(M, kItemTok));
     const int sh_items = (M + kItemTok - 1) / kItemTok;
     const QAct sact{ws.sh_qy, ws.sh_qys, I, nullptr};
@@ -747,34 +753,34 @@ cudaError_t moe_forward(const MoeConfig& c, const MoeWeights& w, const MoeWorksp
       g.in = H; g.rows = I; g.round_out = 1; g.act = act;
       g.Y[0] = ws.sh_gate; g.Y[1] = ws.sh_up;
       g.items = ws.items_sh; g.n_items = ws.counters + 3; g.max_items = sh_items;
-      if ((err = launch_fp8_gemv(g, true, nt, side.s)) != cudaSuccess) return err;
+      if ((err = launch_fp8_gemv(g, true, nt, sst)) != cudaSuccess) return err;
       if ((err = launch_swiglu_quant(ws.sh_gate, ws.sh_up, I, M, nullptr, c.swiglu_limit,
-                                     ws.sh_qy, ws.sh_qys, nullptr, side.s)) != cudaSuccess)
+                                     ws.sh_qy, ws.sh_qys, nullptr, sst)) != cudaSuccess)
         return err;
       Fp8GemvArgs d{};
       d.W[0] = w.sh2; d.S[0] = w.sh2s;
       d.in = I; d.rows = H; d.round_out = 1; d.act = sact;
       d.Y[0] = ws.shared;
       d.items = ws.items_sh; d.n_items = ws.counters + 3; d.max_items = sh_items;
-      if ((err = launch_fp8_gemv(d, false, nt, side.s)) != cudaSuccess) return err;
+      if ((err = launch_fp8_gemv(d, false, nt, sst)) != cudaSuccess) return err;
     } else {
       Fp4GemvArgs g{};
       g.W[0] = w.sh1; g.S[0] = w.sh1s; g.W[1] = w.sh3; g.S[1] = w.sh3s;
       g.in = H; g.rows = I; g.act = act;
       g.Y[0] = ws.sh_gate; g.Y[1] = ws.sh_up;
-      g.items = ws.items_sh; g.n_items = ws.counters + 3; g.max_items = sh_items;
-      if ((err = launch_fp4_gemv(g, true, nt, side.s)) != cudaSuccess) return err;
+      g.items = ws.items_sh; g.n_items = ws.counters + 3; g.max_items = sh_items; g.err = opt.err;
+      if ((err = launch_fp4_gemv(g, true, nt, sst, opt.map_cache)) != cudaSuccess) return err;
       if ((err = launch_swiglu_quant(ws.sh_gate, ws.sh_up, I, M, nullptr, c.swiglu_limit,
-                                     ws.sh_qy, ws.sh_qys, nullptr, side.s)) != cudaSuccess)
+                                     ws.sh_qy, ws.sh_qys, nullptr, sst)) != cudaSuccess)
         return err;
       Fp4GemvArgs d{};
       d.W[0] = w.sh2; d.S[0] = w.sh2s;
       d.in = I; d.rows = H; d.act = sact;
       d.Y[0] = ws.shared;
-      d.items = ws.items_sh; d.n_items = ws.counters + 3; d.max_items = sh_items;
-      if ((err = launch_fp4_gemv(d, false, nt, side.s)) != cudaSuccess) return err;
+      d.items = ws.items_sh; d.n_items = ws.counters + 3; d.max_items = sh_items; d.err = opt.err;
+      if ((err = launch_fp4_gemv(d, false, nt, sst, opt.map_cache)) != cudaSuccess) return err;
     }
-    cudaEventRecord(side.join, side.s);
+    if (side) cudaEventRecord(side->join, side->s);
   }
 
 
@@ -787,8 +793,9 @@ cudaError_t moe_forward(const MoeConfig& c, const MoeWeights& w, const MoeWorksp
   gu.in = H; gu.rows = I; gu.act = act;
   gu.Y[0] = ws.gate; gu.Y[1] = ws.up;
   gu.items = ws.items_gu; gu.n_items = ws.counters; gu.max_items = R; gu.n_mats = c.n_experts;
+  gu.err = opt.err;
   if (ws.timing) cudaEventRecord(ws.timing[0], st);
-  if ((err = launch_fp4_gemv(gu, true, nt, st)) != cudaSuccess) return err;
+  if ((err = launch_fp4_gemv(gu, true, nt, st, opt.map_cache)) != cudaSuccess) return err;
   if (ws.timing) cudaEventRecord(ws.timing[1], st);
   if ((err = launch_swiglu_quant(ws.gate, ws.up, I, R, ws.wt, c.swiglu_limit, ws.qy, ws.qys,
                                  nullptr, st)) != cudaSuccess)
@@ -799,11 +806,12 @@ cudaError_t moe_forward(const MoeConfig& c, const MoeWeights& w, const MoeWorksp
   dn.in = I; dn.rows = H; dn.act = QAct{ws.qy, ws.qys, I, nullptr};
   dn.Y[0] = ws.routed;
   dn.items = ws.items_dn; dn.n_items = ws.counters; dn.max_items = R; dn.n_mats = c.n_experts;
+  dn.err = opt.err;
   if (ws.timing) cudaEventRecord(ws.timing[2], st);
-  if ((err = launch_fp4_gemv(dn, false, nt, st)) != cudaSuccess) return err;
+  if ((err = launch_fp4_gemv(dn, false, nt, st, opt.map_cache)) != cudaSuccess) return err;
   if (ws.timing) cudaEventRecord(ws.timing[3], st);
 
-  if (has_shared) cudaStreamWaitEvent(st, side.join, 0);
+  if (side) cudaStreamWaitEvent(st, side->join, 0);
   const size_t n = static_cast<size_t>(M) * H;
   const int grid = static_cast<int>(std::min<size_t>((n + 255) / 256, 2048));
   moe_combine_kernel<<<grid, 256, 0, st>>>(ws.routed, has_shared ? ws.shared : nullptr, ws.idx,

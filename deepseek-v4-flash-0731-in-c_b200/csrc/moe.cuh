@@ -68,9 +68,19 @@ void moe_workspace_carve(MoeWorkspace* ws, const MoeConfig& c, int max_tokens, v
 // (src/dsv4/dsv4_model.c:6599) / moe_forward_batch (:6812).
 // exact_router: 1 = the reference's fused fmaf logits (moe_forward),
 // 2 = the public dsv4_router's separate multiply/add logits.
+// Execution options. The defaults are what the library's own entry points
+// use; the allocation-free entry point runs everything on the caller's
+// stream, encodes tensor maps without the host-side cache and passes its own
+// device error word.
+struct MoeExecOptions {
+  bool single_stream = false;  // shared expert on `st` instead of a side stream
+  bool map_cache = true;       // cache TMA descriptors by argument
+  unsigned int* err = nullptr; // device error word (null: the library's)
+};
+
 cudaError_t moe_forward(const MoeConfig& c, const MoeWeights& w, const MoeWorkspace& ws,
                         const float* x, const int* token_ids, int n_tokens, float* out,
-                        cudaStream_t st);
+                        cudaStream_t st, const MoeExecOptions& opt = MoeExecOptions());
 
 // Router only: idx/wt [n][topk] (ids ascending), same numerics as above.
 cudaError_t moe_route(const MoeConfig& c, const MoeWeights& w, const MoeWorkspace& ws,

@@ -54,6 +54,8 @@ lib.dsv4cuda_moe_last_routes.argtypes = [vp, C.c_int, i32p, f32p]
 lib.dsv4cuda_moe_route.restype = C.c_int
 lib.dsv4cuda_moe_route.argtypes = [vp, vp, vp, C.c_int, C.c_int, i32p, f32p]
 lib.dsv4cuda_moe_destroy.argtypes = [vp]
+lib.dsv4cuda_moe_forward_noalloc.restype = C.c_int
+lib.dsv4cuda_moe_forward_noalloc.argtypes = [vp, vp, vp, vp, C.c_int, vp, vp]
 lib.dsv4cuda_moe_device_bytes.restype = C.c_size_t
 lib.dsv4cuda_moe_device_bytes.argtypes = [vp]
 
@@ -210,6 +212,39 @@ def _addr(a):
     if hasattr(a, "data_ptr"):
         return a.data_ptr()
     return a.ctypes.data
+
+
+def _moe_structs(layer: dict):
+    sh = layer.get("shared")
+    kind = SHARED_NONE if sh is None else (SHARED_FP8 if sh["fp8"] else SHARED_FP4)
+    tid = layer.get("tid2eid")
+    cfg = MoeConfig(layer["hidden"], layer["moe_inter"], layer["n_experts"], layer["topk"],
+                    layer["swiglu_limit"], layer["route_scale"], kind,
+                    0 if tid is None else int(tid.shape[0]))
+    w = MoeWeights()
+    w.gate_w = _addr(layer["gate_w"])
+    w.bias = _addr(layer.get("bias"))
+    w.tid2eid = _addr(tid)
+    for n in ("w1", "s1", "w3", "s3", "w2", "s2"):
+        setattr(w, n, _addr(layer[n]))
+    if sh is not None:
+        for n, m in (("sh1", "w1"), ("sh1s", "s1"), ("sh3", "w3"), ("sh3s", "s3"),
+                     ("sh2", "w2"), ("sh2s", "s2")):
+            setattr(w, n, _addr(sh[m]))
+    return cfg, w
+
+
+def moe_forward_noalloc(layer: dict, x, out, token_ids=None, stream=None):
+    """Allocation-free MoE forward (dsv4cuda_moe_forward_noalloc): `layer`
+    holds torch CUDA tensors, x/out torch CUDA float32 [n][H]. Raises on the
+    library's error (e.g. too many tokens for its fixed working memory)."""
+    if stream is None:
+        import torch
+        stream = torch.cuda.current_stream().cuda_stream
+    cfg, w = _moe_structs(layer)
+    _check(lib.dsv4cuda_moe_forward_noalloc(C.byref(cfg), C.byref(w), x.data_ptr(),
+                                            None if token_ids is None else token_ids.data_ptr(),
+                                            x.shape[0], out.data_ptr(), stream))
 
 
 class MoeLayer:

@@ -208,6 +208,28 @@ int dsv4cuda_moe_timing_end(dsv4cuda_moe_layer *L, int *n_forwards, float *gateu
 /* Same, also returning the summed router logit and selection milliseconds. */
 int dsv4cuda_moe_timing_end2(dsv4cuda_moe_layer *L, int *n_forwards, float *gateup_ms,
                              float *down_ms, float *logits_ms, float *select_ms);
+/* Allocation-free MoE layer forward. No counterpart in the reference (the
+ * reference is a CPU engine); this is for callers that cannot allocate GPU
+ * memory while they run a layer - inside a stream capture, under an engine
+ * that owns every device allocation through its own pool, or with a fixed
+ * memory footprint. Same computation and results as dsv4cuda_moe_forward,
+ * but the caller supplies the config, DEVICE weight pointers (layouts as in
+ * dsv4cuda_moe_weights), x [n][H], token_ids (hash layers) and out [n][H];
+ * the working memory is a 4 MiB array inside this library, present on
+ * every GPU that loads it until the process exits. Nothing is allocated:
+ * no cudaMalloc/cudaFree, no stream or event creation, no host-side cache.
+ * Returns -1 with a message (dsv4cuda_last_error) when n_tokens needs more
+ * than the 4 MiB (up to 9 tokens fit at hidden 7168 / inter 2048 /
+ * 256 experts / top-8). The first call on each device looks up the array's
+ * device address for that device (make that first call before any stream
+ * capture). Every call on a device shares the one array and starts by
+ * resetting the parts that must begin at zero; calls that overlap on the
+ * GPU (different streams, no ordering between them) race on it. Runs on
+ * `stream` only (the shared expert is not overlapped on a side stream). */
+int dsv4cuda_moe_forward_noalloc(const dsv4cuda_moe_config *cfg,
+                                 const dsv4cuda_moe_weights *device_weights,
+                                 const float *x, const int *token_ids, int n_tokens,
+                                 float *out, void *stream);
 /* Device bytes the layer holds (weights it owns + workspace). */
 size_t dsv4cuda_moe_device_bytes(const dsv4cuda_moe_layer *L);
 

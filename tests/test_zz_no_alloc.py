@@ -1,0 +1,70 @@
+"""The allocation-free MoE entry point (dsv4cuda_moe_forward_noalloc).
+
+It serves callers that cannot allocate GPU memory while they run a layer
+(inside a stream capture, under an engine that owns every device allocation,
+or with a fixed footprint). Its working memory is an array inside the
+library, shared by every call on a device and holding the previous call's
+contents, so this test runs it twice in a row and checks both results
+against the regular entry point (dsv4cuda_moe_forward). The file is named to
+be collected last; it also passes alone in a fresh process."""
+import numpy as np
+import pytest
+import torch
+
+from oracle import make_moe_layer
+
+pytestmark = pytest.mark.gpu
+TOL = 1e-2  # relative to the output RMS, as the other MoE tests use
+
+
+def bf16_vals(rng, shape):
+    x = rng.normal(size=shape).astype(np.float32)
+    u = x.view(np.uint32).astype(np.uint64)
+    return (((u + 0x7FFF + ((u >> 16) & 1)) >> 16) << 16).astype(np.uint32).view(np.float32)
+
+
+def to_device(layer):
+    d = {}
+    for k, v in layer.items():
+        if isinstance(v, np.ndarray):
+            d[k] = torch.from_numpy(np.ascontiguousarray(v)).cuda()
+        elif isinstance(v, dict):
+            d[k] = {kk: (torch.from_numpy(np.ascontiguousarray(vv)).cuda()
+                         if isinstance(vv, np.ndarray) else vv) for kk, vv in v.items()}
+        else:
+            d[k] = v
+    return d
+
+
+def close(a, b):
+    rms = float(np.sqrt(np.mean(b.astype(np.float64) ** 2))) + 1e-30
+    return float(np.max(np.abs(a.astype(np.float64) - b))) / rms <= TOL
+
+
+@pytest.mark.parametrize("cfg", [dict(hid=7168, mi=2048, E=32, k=8, M=1),
+                                 dict(hid=1024, mi=512, E=64, k=6, M=8)])
+def test_noalloc_matches_regular_entry_point(cuda, cfg):
+    L = make_moe_layer(cfg["hid"], cfg["mi"], cfg["E"], cfg["k"], seed=17, shared="fp8")
+    dev = to_device(L)
+    regular = cuda.MoeLayer(dev, max_tokens=cfg["M"], device=True)
+    rng = np.random.default_rng(23)
+    for call in range(2):  # two calls in a row share the library's array
+        x = torch.from_numpy(bf16_vals(rng, (cfg["M"], cfg["hid"]))).cuda()
+        want = torch.empty_like(x)
+        got = torch.full_like(x, float("nan"))
+        regular.forward(x, want)
+        cuda.moe_forward_noalloc(dev, x, got)
+        torch.cuda.synchronize()
+        w, g = want.cpu().numpy(), got.cpu().numpy()
+        assert np.isfinite(g).all(), call
+        assert close(g, w), call
+    regular.close()
+
+
+def test_noalloc_rejects_too_many_tokens(cuda):
+    L = make_moe_layer(7168, 2048, 16, 8, seed=3, shared="fp8")
+    dev = to_device(L)
+    x = torch.zeros((64, 7168), dtype=torch.float32, device="cuda")
+    out = torch.empty_like(x)
+    with pytest.raises(cuda.Dsv4CudaError, match="working memory"):
+        cuda.moe_forward_noalloc(dev, x, out)
