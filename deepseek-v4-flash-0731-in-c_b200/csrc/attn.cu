@@ -1,0 +1,816 @@
+// attn.cu - latent-KV decode attention (sparse_attn) and the FP8 latent
+// cache on sm_100a.
+//
+// Reference: sparse_attn, src/dsv4/dsv4_model.c:5767-5822. Per head h:
+//   s_t  = (fmaf-chain dot(q_h, kv_t)) * scale        (-inf for idx < 0)
+//   m    = max_t s_t
+//   den  = expf(sink_h - m) + sum_t expf(s_t - m)     (raw expf)
+//   w_t  = bf16(expf(s_t - m))
+//   o_h  = bf16(sum_t w_t * kv_t / den)
+// followed by the inverse RoPE of the last rope dims (:5373, :1569).
+//
+// Tensor-core path (d = 512 = 448 + 64, H <= 128): split-KV flash decoding.
+// One CTA per (batch element, key split, output half): the 128 heads are the
+// MMA's M, so S = Q K^T lands in TMEM with one head per TMEM lane and the
+// softmax needs no cross-thread reduction. Each CTA computes the full S tile
+// (K = 512) and accumulates O for its 256 output dims in TMEM
+// (tcgen05.mma kind::f16, BF16 operands, FP32 accumulators). The latent
+// tile is dequantised once into a 128-byte-swizzled BF16 tile that serves
+// as the K-major B operand of Q K^T and, unchanged, as the MN-major B
+// operand of P V. The softmax keeps a running max per head and rescales
+// the head's O row in TMEM when it grows; P = bf16(exp(s - m_run)) is the
+// BF16 operand, the denominator sums raw expf as the reference does. A
+// combine kernel merges the splits (m, den, O partials), divides, rounds to
+// BF16 and applies the inverse RoPE.
+//
+// General path (other shapes): SIMT kernels in the reference's order.
+#include <cmath>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include "attn.cuh"
+#include "bulk.cuh"
+#include "dsv4_common.cuh"
+
+namespace dsv4 {
+namespace {
+
+constexpr unsigned kErrWait = 2u;    // an mbarrier wait in the attention kernel timed out
+constexpr unsigned kErrIndex = 4u;   // a key index beyond the cache rows
+
+// ============================================================ FP8 cache ==
+
+// One block per position; warp w < nope/64 quantises group w exactly like
+// dsv4_act_quant_inplace(group 64, mode 0) (src/dsv4/dsv4_model.c:1386-1417),
+// the remaining warps copy the RoPE dims as BF16.
+__global__ void kv_write_kernel(Fp8KvCache c, const float* __restrict__ kv,
+                                const long long* __restrict__ row, int n) {
+  const int p = blockIdx.x;
+  if (p >= n) return;
+  const int d = c.nope + c.rope_dim;
+  const long long r = row[p];
+  if (r < 0 || r >= c.rows) return;
+  const float* x = kv + static_cast<size_t>(p) * d;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int groups = c.nope / 64;
+  for (int g = warp; g < groups; g += blockDim.x >> 5) {
+    const float a = x[g * 64 + lane], b = x[g * 64 + 32 + lane];
+    const float amax = warp_max(fmaxf(fabsf(a), fabsf(b)));
+    const float scale = pow2_scale_448(amax);
+    const float inv = 1.0f / scale;  // exact: scale is a normal power of two
+    uint8_t code[2];
+    const float v[2] = {a, b};
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+      float q = v[k] * inv;
+      q = fminf(fmaxf(q, -448.0f), 448.0f);
+      unsigned short t;
+      asm("{ .reg .b16 h; cvt.rn.satfinite.e4m3x2.f32 h, %1, %1; mov.b16 %0, h; }"
+          : "=h"(t) : "f"(q));
+      code[k] = (q == 0.0f) ? 0 : static_cast<uint8_t>(t & 0xFF);
+    }
+    uint8_t* dst = c.codes + r * c.nope + g * 64;
+    dst[lane] = code[0];
+    dst[32 + lane] = code[1];
+    if (lane == 0)
+      c.scales[r * kKvScaleSlots + g] = static_cast<uint8_t>((__float_as_uint(scale) >> 23) & 0xFF);
+  }
+  for (int i = threadIdx.x; i < c.rope_dim; i += blockDim.x) {
+    const float v = bf16_round(x[c.nope + i]);
+    c.rope[r * c.rope_dim + i] = static_cast<uint16_t>(__float_as_uint(v) >> 16);
+  }
+}
+
+__device__ __forceinline__ float kv_cache_value(const Fp8KvCache& c, long long r, int i) {
+  if (i < c.nope) {
+    const float v = e4m3_decode(c.codes[r * c.nope + i]) *
+                    e8m0_decode(c.scales[r * kKvScaleSlots + i / 64]);
+    return bf16_round(v);
+  }
+  return bf16_widen(c.rope[r * c.rope_dim + (i - c.nope)]);
+}
+
+__global__ void kv_read_kernel(Fp8KvCache c, const long long* __restrict__ row, int n,
+                               float* __restrict__ out) {
+  const int p = blockIdx.x;
+  const int d = c.nope + c.rope_dim;
+  const long long r = row[p];
+  for (int i = threadIdx.x; i < d; i += blockDim.x)
+    out[static_cast<size_t>(p) * d + i] =
+        (r >= 0 && r < c.rows) ? kv_cache_value(c, r, i) : 0.0f;
+}
+
+// ============================================================ SIMT path ==
+
+struct SimtArgs {
+  AttnProblem p;
+  float* scores;  // [B][H][n]
+};
+
+__device__ __forceinline__ float key_value(const AttnProblem& p, long long r, int i) {
+  return p.kv ? p.kv[r * p.d + i] : kv_cache_value(p.cache, r, i);
+}
+
+__device__ __forceinline__ float block_reduce(float v, bool is_max, float* red) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float u = __shfl_xor_sync(0xffffffffu, v, o);
+    v = is_max ? fmaxf(v, u) : v + u;
+  }
+  __syncthreads();
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  float r = red[0];
+  for (int w = 1; w < nw; ++w) r = is_max ? fmaxf(r, red[w]) : r + red[w];
+  return r;
+}
+
+// Inverse RoPE on one pair (src/dsv4/dsv4_model.c:1569-1580, contraction off).
+__device__ __forceinline__ void rope_inv_pair(float& x0, float& x1, float c, float s) {
+  const float y0 = __fadd_rn(__fmul_rn(x0, c), __fmul_rn(x1, s));
+  const float y1 = __fadd_rn(__fmul_rn(-x0, s), __fmul_rn(x1, c));
+  x0 = bf16_round(y0);
+  x1 = bf16_round(y1);
+}
+
+// One block per (head, batch element); the dot products and the value sums
+// run in the reference's order (fmaf over dims, then over keys).
+__global__ void __launch_bounds__(256) attn_simt_kernel(SimtArgs a) {
+  extern __shared__ float sm[];
+  const AttnProblem& p = a.p;
+  const int h = blockIdx.x, b = blockIdx.y;
+  float* qs = sm;             // [d]
+  float* os = sm + p.d;       // [d]
+  float* red = os + p.d;      // [32]
+  const float* q = p.q + (static_cast<size_t>(b) * p.H + h) * p.d;
+  for (int i = threadIdx.x; i < p.d; i += blockDim.x) qs[i] = q[i];
+  __syncthreads();
+  float* sc = a.scores + (static_cast<size_t>(b) * p.H + h) * p.n;
+  const int* idx = p.idx + static_cast<size_t>(b) * p.n;
+  const long long base = static_cast<long long>(b) * p.kv_batch_stride;
+  float mx = -INFINITY;
+  for (int t = threadIdx.x; t < p.n; t += blockDim.x) {
+    const int pos = idx[t];
+    float s = -INFINITY;
+    if (pos >= 0 && pos < p.kv_rows) {
+      float dot = 0.0f;
+      for (int i = 0; i < p.d; ++i) dot = fmaf(qs[i], key_value(p, base + pos, i), dot);
+      s = dot * p.scale;
+    } else if (pos >= 0 && p.err) {
+      atomicOr(p.err, kErrIndex);
+    }
+    sc[t] = s;
+    mx = fmaxf(mx, s);
+  }
+  mx = block_reduce(mx, true, red);
+  float part = 0.0f;
+  for (int t = threadIdx.x; t < p.n; t += blockDim.x) {
+    const float s = sc[t];
+    float w = 0.0f;
+    if (s != -INFINITY) {
+      const float e = expf(s - mx);
+      part += e;
+      w = bf16_round(e);
+    }
+    sc[t] = w;
+  }
+  const float den = expf(p.sink[h] - mx) + block_reduce(part, false, red);
+  __syncthreads();
+  for (int i = threadIdx.x; i < p.d; i += blockDim.x) {
+    float acc = 0.0f;
+    for (int t = 0; t < p.n; ++t) {
+      const int pos = idx[t];
+      if (pos < 0 || pos >= p.kv_rows) continue;
+      acc = fmaf(sc[t], key_value(p, base + pos, i), acc);
+    }
+    os[i] = bf16_round(acc / den);
+  }
+  __syncthreads();
+  const int rd = p.rope_dim, r0 = p.d - rd;
+  if (p.rope_cos) {
+    for (int i = threadIdx.x; i < rd / 2; i += blockDim.x) {
+      float x0 = os[r0 + 2 * i], x1 = os[r0 + 2 * i + 1];
+      rope_inv_pair(x0, x1, p.rope_cos[b * (rd / 2) + i], p.rope_sin[b * (rd / 2) + i]);
+      os[r0 + 2 * i] = x0;
+      os[r0 + 2 * i + 1] = x1;
+    }
+    __syncthreads();
+  }
+  float* o = p.out + (static_cast<size_t>(b) * p.H + h) * p.d;
+  for (int i = threadIdx.x; i < p.d; i += blockDim.x) o[i] = os[i];
+}
+
+// ===================================================== tensor-core path ==
+
+constexpr int kTcD = 512;
+constexpr int kTcNope = 448;
+constexpr int kTcRope = 64;
+constexpr int kTcM = 128;      // heads (MMA M), zero-padded above H
+constexpr int kTcKeys = 32;    // keys per tile: N of Q K^T, K of P V
+constexpr int kTcHalf = 256;   // output dims per CTA (N of P V)
+constexpr int kTcThreads = 288;  // warps 0-3 softmax, 4-7 converters, 8 MMA
+constexpr uint32_t kQBytes = kTcM * kTcD * 2;           // 131072
+constexpr uint32_t kKBytes = kTcKeys * kTcD * 2;        // 32768 per stage
+constexpr uint32_t kPBytes = kTcM * 128;                // 16384 (128-B rows, 64 B used)
+constexpr uint32_t kOffK = kQBytes;
+constexpr uint32_t kOffP = kOffK + 2 * kKBytes;
+constexpr uint32_t kOffBar = kOffP + 2 * kPBytes;       // 229376
+constexpr uint32_t kTcSmem = kOffBar + 128 + 1024;      // + barriers + alignment slack
+constexpr uint32_t kTmemCols = 512;                     // O: cols 0-255, S: 256-319
+constexpr uint32_t kTmemS = 256;
+
+static_assert(kTcSmem <= 232448, "attention tile exceeds the 227 KB shared-memory limit");
+
+struct TcArgs {
+  const float* q;
+  const float* kv;
+  Fp8KvCache cache;
+  long long kv_bstride, kv_rows;
+  const int* idx;
+  int B, H, n;
+  float scale;
+  int splits, keys_per_split;
+  float* m_part;    // [B][splits][H]
+  float* den_part;  // [B][splits][H]
+  float* o_part;    // [B][splits][H][512]
+  unsigned* err;
+};
+
+// Byte offset of the 16-byte chunk (row, dc) in a 128-byte-swizzled tile
+// whose 64-dim column blocks are `rows` rows tall (dc = dim / 8).
+__device__ __forceinline__ uint32_t sw128_off(int row, int dc, int rows) {
+  return static_cast<uint32_t>((dc >> 3) * rows * 128 + (row >> 3) * 1024 + (row & 7) * 128 +
+                               (((dc & 7) ^ (row & 7)) << 4));
+}
+
+// UMMA shared-memory descriptor, 128-byte swizzle (layout type 2), sm_100
+// version bit; addresses and offsets in 16-byte units.
+__device__ __forceinline__ uint64_t umma_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+  return static_cast<uint64_t>((saddr >> 4) & 0x3FFFu) |
+         (static_cast<uint64_t>((lbo >> 4) & 0x3FFFu) << 16) |
+         (static_cast<uint64_t>((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46) | (2ull << 61);
+}
+
+// Instruction descriptor of kind::f16: FP32 accumulate, BF16 A and B.
+__host__ __device__ constexpr uint32_t umma_idesc_bf16(int m, int n, bool b_mn_major) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | ((b_mn_major ? 1u : 0u) << 16) |
+         (static_cast<uint32_t>(n >> 3) << 17) | (static_cast<uint32_t>(m >> 4) << 24);
+}
+
+__device__ __forceinline__ void umma_bf16(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc,
+                                          uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(d_tmem),
+      "l"(a), "l"(b), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::
+                   "r"(smem_addr(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void fence_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
+
+#define DSV4_R32(X)                                                                          \
+  X(0), X(1), X(2), X(3), X(4), X(5), X(6), X(7), X(8), X(9), X(10), X(11), X(12), X(13),  \
+      X(14), X(15), X(16), X(17), X(18), X(19), X(20), X(21), X(22), X(23), X(24), X(25),  \
+      X(26), X(27), X(28), X(29), X(30), X(31)
+#define DSV4_OUT(i) "=r"(r[i])
+#define DSV4_INOUT(i) "+r"(r[i])
+#define DSV4_IN(i) "r"(r[i])
+
+// 32 consecutive TMEM columns of this thread's lane (32x32b shape).
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,"
+      "%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : DSV4_R32(DSV4_OUT)
+      : "r"(taddr));
+  // The wait names the registers so no use is scheduled before it.
+  asm volatile("tcgen05.wait::ld.sync.aligned;" : DSV4_R32(DSV4_INOUT)::"memory");
+}
+
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,"
+      "%13,%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(
+          taddr),
+      DSV4_R32(DSV4_IN)
+      : "memory");
+}
+__device__ __forceinline__ void tmem_st_wait() {
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
+// Bounded wait that also gives up once another role has aborted.
+__device__ __forceinline__ bool tc_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
+                                        unsigned* err) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const unsigned long long t0 = global_timer_ns();
+  while (!mbar_try_wait(bar, parity)) {
+    if (*abort_flag) return false;
+    if (global_timer_ns() - t0 > kWaitLimitNs) {
+      if (err) atomicOr(err, kErrWait);
+      *abort_flag = 1;
+      return false;
+    }
+  }
+  return true;
+}
+
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+  const __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t*>(&v);
+}
+
+// Four E4M3 codes (low byte first) times a power of two -> 2 x bf16x2; exact.
+__device__ __forceinline__ uint2 e4m3x4_to_bf16(uint32_t w, float sc) {
+  const uint32_t h01 = e4m3x2_to_f16x2(w & 0xFFFFu), h23 = e4m3x2_to_f16x2(w >> 16);
+  const float2 f01 = __half22float2(*reinterpret_cast<const __half2*>(&h01));
+  const float2 f23 = __half22float2(*reinterpret_cast<const __half2*>(&h23));
+  return make_uint2(pack_bf16x2(f01.x * sc, f01.y * sc), pack_bf16x2(f23.x * sc, f23.y * sc));
+}
+
+__device__ __forceinline__ void st_shared_v4(uint32_t addr, uint4 v) {
+  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(v.x), "r"(v.y),
+               "r"(v.z), "r"(v.w)
+               : "memory");
+}
+
+struct TcBars {
+  uint64_t kv_full[2], kv_empty[2], s_full[2], p_full[2], pv_done[2], fin;
+  uint32_t tmem_base;
+  int abort_flag;
+  uint32_t key_mask[2];
+};
+
+__global__ void __launch_bounds__(kTcThreads, 1) attn_tc_kernel(const __grid_constant__ TcArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_s = smem_addr(smem_raw);
+  const uint32_t pad = ((raw_s + 1023u) & ~1023u) - raw_s;
+  uint8_t* smem = smem_raw + pad;
+  const uint32_t sbase = raw_s + pad;
+  const uint32_t q_s = sbase, k_s = sbase + kOffK, p_s = sbase + kOffP;
+  TcBars* bars = reinterpret_cast<TcBars*>(smem + kOffBar);
+  volatile int* abort_flag = &bars->abort_flag;
+
+  const int half = blockIdx.x & 1, split = blockIdx.x >> 1, b = blockIdx.y;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int k0 = split * a.keys_per_split;
+  const int k_end = min(a.n, k0 + a.keys_per_split);
+  const int T = k_end > k0 ? (k_end - k0 + kTcKeys - 1) / kTcKeys : 0;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&bars->kv_full[i], 128);
+      mbar_init(&bars->kv_empty[i], 1);
+      mbar_init(&bars->s_full[i], 1);
+      mbar_init(&bars->p_full[i], 128);
+      mbar_init(&bars->pv_done[i], 1);
+      bars->key_mask[i] = 0;
+    }
+    mbar_init(&bars->fin, 1);
+    bars->abort_flag = 0;
+    mbar_fence_init();
+  }
+  if (warp == 8) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_addr(&bars->tmem_base)),
+                 "r"(kTmemCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  } else {
+    // Q [H][512] fp32 (BF16-valued) -> BF16, K-major 128-byte-swizzled, rows >= H zero.
+    const float* qb = a.q + static_cast<size_t>(b) * a.H * kTcD;
+    for (int c = threadIdx.x; c < kTcM * (kTcD / 8); c += 256) {
+      const int row = c >> 6, dc = c & 63;
+      uint4 v = make_uint4(0, 0, 0, 0);
+      if (row < a.H) {
+        const float4* src = reinterpret_cast<const float4*>(qb + row * kTcD + dc * 8);
+        const float4 x0 = src[0], x1 = src[1];
+        v = make_uint4(pack_bf16x2(x0.x, x0.y), pack_bf16x2(x0.z, x0.w), pack_bf16x2(x1.x, x1.y),
+                       pack_bf16x2(x1.z, x1.w));
+      }
+      st_shared_v4(q_s + sw128_off(row, dc, kTcM), v);
+    }
+    fence_async_smem();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = bars->tmem_base;
+
+  if (warp == 8) {
+    // ------------------------------------------------------------ MMA issue
+    if (lane == 0) {
+      constexpr uint32_t idesc_qk = umma_idesc_bf16(kTcM, kTcKeys, false);
+      constexpr uint32_t idesc_pv = umma_idesc_bf16(kTcM, kTcHalf, true);
+      auto issue_pv = [&](int jj) -> bool {
+        const int sb = jj & 1;
+        if (!tc_wait(&bars->p_full[sb], (jj >> 1) & 1, abort_flag, a.err)) return false;
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < kTcKeys / 16; ++kk) {
+          const uint64_t ad = umma_desc(p_s + sb * kPBytes + kk * 32, 16, 1024);
+          const uint64_t bd =
+              umma_desc(k_s + sb * kKBytes + half * 4 * (kTcKeys * 128) + kk * 16 * 128,
+                        kTcKeys * 128, 1024);
+          umma_bf16(tmem, ad, bd, idesc_pv, (jj > 0 || kk > 0) ? 1u : 0u);
+        }
+        umma_commit(&bars->pv_done[sb]);
+        umma_commit(&bars->kv_empty[sb]);
+        return true;
+      };
+      bool ok = true;
+      for (int j = 0; j < T && ok; ++j) {
+        const int st = j & 1;
+        if (!tc_wait(&bars->kv_full[st], (j >> 1) & 1, abort_flag, a.err)) { ok = false; break; }
+        tc_fence_after();
+#pragma unroll 4
+        for (int kk = 0; kk < kTcD / 16; ++kk) {
+          const uint32_t off = (kk & 3) * 32;  // 16 dims inside the 64-dim swizzle row
+          const uint64_t ad = umma_desc(q_s + (kk >> 2) * (kTcM * 128) + off, 16, 1024);
+          const uint64_t bd = umma_desc(k_s + st * kKBytes + (kk >> 2) * (kTcKeys * 128) + off,
+                                        16, 1024);
+          umma_bf16(tmem + kTmemS + st * kTcKeys, ad, bd, idesc_qk, kk > 0 ? 1u : 0u);
+        }
+        umma_commit(&bars->s_full[st]);
+        if (j > 0) ok = issue_pv(j - 1);
+      }
+      if (ok && T > 0) issue_pv(T - 1);
+      umma_commit(&bars->fin);
+      mbar_wait(&bars->fin, 0, a.err);
+    }
+    __syncwarp();
+  } else if (warp >= 4) {
+    // ------------------------------------------------- latent tile producer
+    const int c = threadIdx.x - 128;
+    const int r = c >> 2, qd = c & 3;  // key row in tile, quarter of the dims
+    const int* idxb = a.idx + static_cast<size_t>(b) * a.n;
+    const long long rbase = static_cast<long long>(b) * a.kv_bstride;
+    for (int j = 0; j < T; ++j) {
+      const int st = j & 1;
+      const int key = k0 + j * kTcKeys + r;
+      long long pos = -1;
+      if (key < k_end) {
+        pos = idxb[key];
+        if (pos >= a.kv_rows) {
+          if (a.err) atomicOr(a.err, kErrIndex);
+          pos = -1;
+        }
+      }
+      const bool valid = pos >= 0;
+      const long long row = rbase + pos;
+      // raw loads before the stage wait
+      uint4 raw[8];
+      uint32_t scw = 0;
+      if (valid && !a.kv) {
+        const uint4* cp = reinterpret_cast<const uint4*>(a.cache.codes + row * kTcNope + qd * 128);
+        const int ncode = qd < 3 ? 8 : 4;
+#pragma unroll
+        for (int u = 0; u < 8; ++u)
+          if (u < ncode) raw[u] = __ldg(cp + u);
+        scw = *reinterpret_cast<const uint32_t*>(a.cache.scales + row * kKvScaleSlots +
+                                                 (qd < 2 ? 0 : 4));
+      }
+      uint4 rope[8];
+      if (valid && !a.kv && qd == 3) {
+        const uint4* rp = reinterpret_cast<const uint4*>(a.cache.rope + row * kTcRope);
+#pragma unroll
+        for (int u = 0; u < 8; ++u) rope[u] = __ldg(rp + u);
+      }
+      if (!tc_wait(&bars->kv_empty[st], ((j >> 1) & 1) ^ 1, abort_flag, a.err)) break;
+      const uint32_t tile = k_s + st * kKBytes;
+      if (!valid) {
+        for (int dc = qd * 16; dc < qd * 16 + 16; ++dc)
+          st_shared_v4(tile + sw128_off(r, dc, kTcKeys), make_uint4(0, 0, 0, 0));
+      } else if (a.kv) {
+        const float4* src = reinterpret_cast<const float4*>(a.kv + row * kTcD + qd * 128);
+        for (int dc = 0; dc < 16; ++dc) {
+          const float4 x0 = __ldg(src + 2 * dc), x1 = __ldg(src + 2 * dc + 1);
+          st_shared_v4(tile + sw128_off(r, qd * 16 + dc, kTcKeys),
+                       make_uint4(pack_bf16x2(x0.x, x0.y), pack_bf16x2(x0.z, x0.w),
+                                  pack_bf16x2(x1.x, x1.y), pack_bf16x2(x1.z, x1.w)));
+        }
+      } else {
+        const int ncode = qd < 3 ? 8 : 4;
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          if (u < ncode) {
+            const int g = (qd * 128 + u * 16) >> 6;  // scale group
+            const uint32_t code = (scw >> (8 * (g & 3))) & 0xFFu;
+            const float sc = e8m0_decode(code);
+            const uint2 lo = e4m3x4_to_bf16(raw[u].x, sc), hi = e4m3x4_to_bf16(raw[u].y, sc);
+            const uint2 lo2 = e4m3x4_to_bf16(raw[u].z, sc), hi2 = e4m3x4_to_bf16(raw[u].w, sc);
+            st_shared_v4(tile + sw128_off(r, qd * 16 + 2 * u, kTcKeys),
+                         make_uint4(lo.x, lo.y, hi.x, hi.y));
+            st_shared_v4(tile + sw128_off(r, qd * 16 + 2 * u + 1, kTcKeys),
+                         make_uint4(lo2.x, lo2.y, hi2.x, hi2.y));
+          }
+        }
+        if (qd == 3) {
+#pragma unroll
+          for (int u = 0; u < 8; ++u)
+            st_shared_v4(tile + sw128_off(r, 56 + u, kTcKeys), rope[u]);
+        }
+      }
+      // validity mask of the tile's keys (bit r), one byte per producer warp
+      const uint32_t vb = __ballot_sync(0xffffffffu, valid);
+      if (lane == 0) {
+        uint32_t m8 = 0;
+        for (int k = 0; k < 8; ++k) m8 |= ((vb >> (4 * k)) & 1u) << k;
+        reinterpret_cast<volatile uint8_t*>(&bars->key_mask[st])[warp - 4] =
+            static_cast<uint8_t>(m8);
+      }
+      __syncwarp();
+      fence_async_smem();
+      mbar_arrive(&bars->kv_full[st]);
+    }
+  } else {
+    // --------------------------------------------------------------- softmax
+    const int h = threadIdx.x;  // head = TMEM lane
+    const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
+    float m_run = -INFINITY, den = 0.0f;
+    bool ok = true;
+    for (int j = 0; j < T; ++j) {
+      const int sb = j & 1;
+      bool w = tc_wait(&bars->s_full[sb], (j >> 1) & 1, abort_flag, a.err);
+      w = w && tc_wait(&bars->kv_full[sb], (j >> 1) & 1, abort_flag, a.err);
+      if (!__all_sync(0xffffffffu, w)) { ok = false; break; }
+      tc_fence_after();
+      uint32_t r[32];
+      tmem_ld32(tmem + lane_base + kTmemS + sb * kTcKeys, r);
+      const uint32_t mask = *reinterpret_cast<volatile uint32_t*>(&bars->key_mask[sb]);
+      float s[32];
+      float tmax = -INFINITY;
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        s[i] = ((mask >> i) & 1u) ? __uint_as_float(r[i]) * a.scale : -INFINITY;
+        tmax = fmaxf(tmax, s[i]);
+      }
+      const float m_new = fmaxf(m_run, tmax);
+      const bool resc = (m_new > m_run) && (m_run != -INFINITY);
+      const float alpha = resc ? expf(m_run - m_new) : 1.0f;
+      den *= alpha;
+      uint32_t pw[16];
+#pragma unroll
+      for (int i = 0; i < 32; i += 2) {
+        const float e0 = (s[i] == -INFINITY) ? 0.0f : expf(s[i] - m_new);
+        den += e0;
+        const float e1 = (s[i + 1] == -INFINITY) ? 0.0f : expf(s[i + 1] - m_new);
+        den += e1;
+        pw[i / 2] = pack_bf16x2(e0, e1);
+      }
+      m_run = m_new;
+      if (j > 0) {
+        const bool wv = tc_wait(&bars->pv_done[(j - 1) & 1], ((j - 1) >> 1) & 1, abort_flag, a.err);
+        if (!__all_sync(0xffffffffu, wv)) { ok = false; break; }
+        tc_fence_after();
+        if (__any_sync(0xffffffffu, resc)) {
+          for (int cb = 0; cb < kTcHalf; cb += 32) {
+            uint32_t o[32];
+            tmem_ld32(tmem + lane_base + cb, o);
+#pragma unroll
+            for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+            tmem_st32(tmem + lane_base + cb, o);
+          }
+          tmem_st_wait();
+        }
+      }
+      const uint32_t prow = p_s + sb * kPBytes + (h >> 3) * 1024 + (h & 7) * 128;
+#pragma unroll
+      for (int c4 = 0; c4 < 4; ++c4)
+        st_shared_v4(prow + (((c4 ^ (h & 7))) << 4),
+                     make_uint4(pw[4 * c4], pw[4 * c4 + 1], pw[4 * c4 + 2], pw[4 * c4 + 3]));
+      fence_async_smem();
+      tc_fence_before();
+      mbar_arrive(&bars->p_full[sb]);
+    }
+    // epilogue: O partial row, m and den
+    const size_t prow = (static_cast<size_t>(b) * a.splits + split) * a.H + h;
+    bool have = ok && T > 0;
+    if (have) {
+      const bool wv = tc_wait(&bars->pv_done[(T - 1) & 1], ((T - 1) >> 1) & 1, abort_flag, a.err);
+      have = __all_sync(0xffffffffu, wv);
+    }
+    if (have) {
+      tc_fence_after();
+      for (int cb = 0; cb < kTcHalf; cb += 32) {
+        uint32_t o[32];
+        tmem_ld32(tmem + lane_base + cb, o);
+        if (h < a.H) {
+          float4* dst = reinterpret_cast<float4*>(a.o_part + prow * kTcD + half * kTcHalf + cb);
+#pragma unroll
+          for (int i = 0; i < 8; ++i)
+            dst[i] = make_float4(__uint_as_float(o[4 * i]), __uint_as_float(o[4 * i + 1]),
+                                 __uint_as_float(o[4 * i + 2]), __uint_as_float(o[4 * i + 3]));
+        }
+      }
+    } else if (h < a.H) {
+      float4* dst = reinterpret_cast<float4*>(a.o_part + prow * kTcD + half * kTcHalf);
+      for (int i = 0; i < kTcHalf / 4; ++i) dst[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+      m_run = -INFINITY;
+      den = 0.0f;
+    }
+    if (half == 0 && h < a.H) {
+      a.m_part[prow] = m_run;
+      a.den_part[prow] = den;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 8)
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
+                 "r"(kTmemCols)
+                 : "memory");
+}
+
+// Merge the splits of one (head, batch element): 128 threads x 4 dims.
+__global__ void __launch_bounds__(128) attn_combine_kernel(AttnProblem p, int splits,
+                                                           const float* __restrict__ m_part,
+                                                           const float* __restrict__ den_part,
+                                                           const float* __restrict__ o_part) {
+  const int h = blockIdx.x, b = blockIdx.y;
+  extern __shared__ float wsm[];  // [splits]
+  __shared__ float s_den;
+  if (threadIdx.x == 0) {
+    float M = -INFINITY;
+    for (int s = 0; s < splits; ++s)
+      M = fmaxf(M, m_part[(static_cast<size_t>(b) * splits + s) * p.H + h]);
+    float den = 0.0f;
+    for (int s = 0; s < splits; ++s) {
+      const size_t i = (static_cast<size_t>(b) * splits + s) * p.H + h;
+      const float w = (m_part[i] == -INFINITY) ? 0.0f : expf(m_part[i] - M);
+      wsm[s] = w;
+      den += den_part[i] * w;
+    }
+    s_den = den + expf(p.sink[h] - M);
+  }
+  __syncthreads();
+  const float den = s_den;
+  const int d0 = threadIdx.x * 4;
+  float acc[4] = {0.f, 0.f, 0.f, 0.f};
+  for (int s = 0; s < splits; ++s) {
+    const float w = wsm[s];
+    if (w == 0.0f) continue;
+    const float4 v = *reinterpret_cast<const float4*>(
+        o_part + ((static_cast<size_t>(b) * splits + s) * p.H + h) * kTcD + d0);
+    acc[0] += v.x * w;
+    acc[1] += v.y * w;
+    acc[2] += v.z * w;
+    acc[3] += v.w * w;
+  }
+  float o[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) o[i] = bf16_round(acc[i] / den);
+  const int r0 = kTcD - p.rope_dim;
+  if (p.rope_cos && d0 >= r0) {
+    const int pi = (d0 - r0) / 2;
+    const float* cs = p.rope_cos + b * (p.rope_dim / 2);
+    const float* sn = p.rope_sin + b * (p.rope_dim / 2);
+    rope_inv_pair(o[0], o[1], cs[pi], sn[pi]);
+    rope_inv_pair(o[2], o[3], cs[pi + 1], sn[pi + 1]);
+  }
+  *reinterpret_cast<float4*>(p.out + (static_cast<size_t>(b) * p.H + h) * kTcD + d0) =
+      make_float4(o[0], o[1], o[2], o[3]);
+}
+
+int sm_count() {
+  static int n = 0;
+  if (n == 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    if (n <= 0) n = 148;
+  }
+  return n;
+}
+
+// m and den partials first, then the O partials from a 256-byte boundary
+// (the kernels move O partials as float4).
+size_t tc_o_part_offset(size_t rows) { return (2 * rows + 63) & ~static_cast<size_t>(63); }
+
+struct TcPlan {
+  int splits, keys_per_split;
+};
+
+TcPlan tc_plan(const AttnProblem& p) {
+  const int tiles = (p.n + kTcKeys - 1) / kTcKeys;
+  if (tiles == 0) return {1, kTcKeys};
+  int per_b = sm_count() / (2 * p.B);
+  if (per_b < 1) per_b = 1;
+  int splits = per_b < tiles ? per_b : tiles;
+  const int tiles_per = (tiles + splits - 1) / splits;
+  splits = (tiles + tiles_per - 1) / tiles_per;
+  return {splits, tiles_per * kTcKeys};
+}
+
+}  // namespace
+
+bool attn_uses_tensor_cores(const AttnProblem& p) {
+  if (p.d != kTcD || p.H < 1 || p.H > kTcM) return false;
+  if (!p.kv && (p.cache.nope != kTcNope || p.cache.rope_dim != kTcRope)) return false;
+  // the combine kernel's threads own 4 dims each: RoPE pairs must not straddle
+  if (p.rope_cos && (p.rope_dim % 4 != 0)) return false;
+  return true;
+}
+
+int attn_splits(const AttnProblem& p) {
+  return attn_uses_tensor_cores(p) ? tc_plan(p).splits : 1;
+}
+
+size_t attn_workspace_bytes(const AttnProblem& p) {
+  if (attn_uses_tensor_cores(p)) {
+    const size_t rows = static_cast<size_t>(p.B) * tc_plan(p).splits * p.H;
+    return tc_o_part_offset(rows) * sizeof(float) + rows * kTcD * sizeof(float) + 256;
+  }
+  return static_cast<size_t>(p.B) * p.H * (p.n > 0 ? p.n : 1) * sizeof(float) + 256;
+}
+
+cudaError_t kv_cache_write(const Fp8KvCache& c, const float* kv, const long long* row, int n,
+                           cudaStream_t st) {
+  if (n <= 0) return cudaSuccess;
+  if (c.nope % 64 != 0 || c.nope / 64 > kKvScaleSlots) return cudaErrorInvalidValue;
+  kv_write_kernel<<<n, 256, 0, st>>>(c, kv, row, n);
+  return cudaGetLastError();
+}
+
+cudaError_t kv_cache_read(const Fp8KvCache& c, const long long* row, int n, float* out,
+                          cudaStream_t st) {
+  if (n <= 0) return cudaSuccess;
+  kv_read_kernel<<<n, 256, 0, st>>>(c, row, n, out);
+  return cudaGetLastError();
+}
+
+cudaError_t attn_forward(const AttnProblem& p, void* ws, cudaStream_t st, cudaEvent_t main_begin,
+                         cudaEvent_t main_end) {
+  if (p.B <= 0 || p.H <= 0) return cudaSuccess;
+  if (p.d <= 0 || p.n < 0 || p.rope_dim < 0 || p.rope_dim > p.d || (p.rope_dim & 1))
+    return cudaErrorInvalidValue;
+  if (!p.kv && (p.cache.nope + p.cache.rope_dim != p.d || p.cache.nope % 64 != 0))
+    return cudaErrorInvalidValue;
+  if (attn_uses_tensor_cores(p)) {
+    const TcPlan plan = tc_plan(p);
+    float* base = reinterpret_cast<float*>(ws);
+    const size_t rows = static_cast<size_t>(p.B) * plan.splits * p.H;
+    TcArgs a;
+    a.q = p.q;
+    a.kv = p.kv;
+    a.cache = p.cache;
+    a.kv_bstride = p.kv_batch_stride;
+    a.kv_rows = p.kv_rows;
+    a.idx = p.idx;
+    a.B = p.B;
+    a.H = p.H;
+    a.n = p.n;
+    a.scale = p.scale;
+    a.splits = plan.splits;
+    a.keys_per_split = plan.keys_per_split;
+    a.m_part = base;
+    a.den_part = base + rows;
+    a.o_part = base + tc_o_part_offset(rows);
+    a.err = p.err;
+    static bool attr_set[64] = {};  // per device
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64 || !attr_set[dev]) {
+      cudaError_t e = cudaFuncSetAttribute(attn_tc_kernel,
+                                           cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmem);
+      if (e != cudaSuccess) return e;
+      if (dev >= 0 && dev < 64) attr_set[dev] = true;
+    }
+    if (main_begin) cudaEventRecord(main_begin, st);
+    attn_tc_kernel<<<dim3(2 * plan.splits, p.B), kTcThreads, kTcSmem, st>>>(a);
+    if (main_end) cudaEventRecord(main_end, st);
+    attn_combine_kernel<<<dim3(p.H, p.B), 128, plan.splits * sizeof(float), st>>>(
+        p, plan.splits, a.m_part, a.den_part, a.o_part);
+    return cudaGetLastError();
+  }
+  SimtArgs a;
+  a.p = p;
+  a.scores = reinterpret_cast<float*>(ws);
+  const size_t smem = (2 * static_cast<size_t>(p.d) + 32) * sizeof(float);
+  if (smem > 48 * 1024) return cudaErrorInvalidValue;
+  if (main_begin) cudaEventRecord(main_begin, st);
+  attn_simt_kernel<<<dim3(p.H, p.B), 256, smem, st>>>(a);
+  if (main_end) cudaEventRecord(main_end, st);
+  return cudaGetLastError();
+}
+
+}  // namespace dsv4

@@ -20,6 +20,7 @@
 #include "dsv4_common.cuh"
 #include "gemv.cuh"
 #include "moe.cuh"
+#include "attn.cuh"
 #include "../../include/dsv4_cuda.h"
 
 #define DSV4_API extern "C" __attribute__((visibility("default")))
@@ -883,4 +884,234 @@ DSV4_API int dsv4cuda_moe_forward_noalloc(const dsv4cuda_moe_config* cfg,
     return -1;
   }
   return 0;
+}
+
+// ============================================================ attention ==
+
+namespace {
+
+struct AttnThreadState {
+  char* ws = nullptr;
+  size_t cap = 0;
+  bool timing = false;
+  std::vector<cudaEvent_t> events;  // pairs around the main kernel
+  int timed = 0;
+};
+thread_local AttnThreadState t_attn;
+
+dsv4::Fp8KvCache to_cache(const dsv4cuda_kv_cache* c) {
+  dsv4::Fp8KvCache k;
+  k.codes = c->codes;
+  k.scales = c->scales;
+  k.rope = c->rope;
+  k.nope = c->nope;
+  k.rope_dim = c->rope_dim;
+  k.rows = c->rows;
+  return k;
+}
+
+bool cache_ok(const dsv4cuda_kv_cache* c) {
+  return c && c->codes && c->scales && c->rope && c->nope > 0 && c->nope % 64 == 0 &&
+         c->nope / 64 <= dsv4::kKvScaleSlots && c->rope_dim >= 0 && c->rows > 0;
+}
+
+dsv4::AttnProblem make_problem(const dsv4cuda_attn_shape* s, const float* q, const float* kv,
+                               const dsv4cuda_kv_cache* cache, const float* sink, const int* idx,
+                               const float* rc, const float* rs, float* out) {
+  dsv4::AttnProblem p;
+  p.q = q;
+  p.kv = kv;
+  if (!kv && cache) p.cache = to_cache(cache);
+  p.kv_batch_stride = s->kv_batch_stride;
+  p.kv_rows = s->kv_rows;
+  p.idx = idx;
+  p.sink = sink;
+  p.rope_cos = rc;
+  p.rope_sin = rs;
+  p.rope_dim = s->rope_dim;
+  p.out = out;
+  p.B = s->batch;
+  p.H = s->heads;
+  p.d = s->head_dim;
+  p.n = s->n_keys;
+  p.scale = s->scale;
+  p.err = dsv4::device_error_word();
+  return p;
+}
+
+}  // namespace
+
+DSV4_API int dsv4cuda_kv_write(const dsv4cuda_kv_cache* cache, const float* kv,
+                               const long long* rows, int n, void* stream) {
+  if (!cache_ok(cache) || (n > 0 && (!kv || !rows)) || n < 0 ||
+      reinterpret_cast<uintptr_t>(cache->codes) % 16 || reinterpret_cast<uintptr_t>(cache->rope) % 16 ||
+      reinterpret_cast<uintptr_t>(cache->scales) % 8) {
+    record_error("dsv4cuda_kv_write: bad arguments (cache codes/rope 16-byte aligned, scales 8)");
+    return -1;
+  }
+  cudaError_t e = dsv4::kv_cache_write(to_cache(cache), kv, rows, n,
+                                       static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) { record_error("dsv4cuda_kv_write: %s", cudaGetErrorString(e)); return -1; }
+  return 0;
+}
+
+DSV4_API int dsv4cuda_kv_read(const dsv4cuda_kv_cache* cache, const long long* rows, int n,
+                              float* out, void* stream) {
+  if (!cache_ok(cache) || (n > 0 && (!out || !rows)) || n < 0) {
+    record_error("dsv4cuda_kv_read: bad arguments");
+    return -1;
+  }
+  cudaError_t e = dsv4::kv_cache_read(to_cache(cache), rows, n, out,
+                                      static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) { record_error("dsv4cuda_kv_read: %s", cudaGetErrorString(e)); return -1; }
+  return 0;
+}
+
+DSV4_API size_t dsv4cuda_attn_workspace_bytes(const dsv4cuda_attn_shape* shape, int use_cache) {
+  if (!shape) return 0;
+  dsv4::AttnProblem p = make_problem(shape, nullptr, use_cache ? nullptr : reinterpret_cast<const float*>(1),
+                                     nullptr, nullptr, nullptr, nullptr, nullptr, nullptr);
+  if (use_cache) {
+    p.cache.nope = shape->head_dim - shape->rope_dim;
+    p.cache.rope_dim = shape->rope_dim;
+  }
+  return dsv4::attn_workspace_bytes(p);
+}
+
+DSV4_API int dsv4cuda_sparse_attn(float* out, const float* q, const float* kv,
+                                  const dsv4cuda_kv_cache* cache, const float* sink,
+                                  const int* idx, const float* rope_cos, const float* rope_sin,
+                                  const dsv4cuda_attn_shape* shape, void* workspace,
+                                  size_t workspace_bytes, void* stream) {
+  if (!shape || !out || !q || !sink || (!kv && !cache_ok(cache)) ||
+      (shape->n_keys > 0 && !idx) || shape->batch < 0 || shape->heads <= 0 ||
+      shape->head_dim <= 0 || shape->n_keys < 0 || ((rope_cos == nullptr) != (rope_sin == nullptr))) {
+    record_error("dsv4cuda_sparse_attn: bad arguments");
+    return -1;
+  }
+  if (!kv && cache->nope + cache->rope_dim != shape->head_dim) {
+    record_error("dsv4cuda_sparse_attn: cache nope + rope_dim != head_dim");
+    return -1;
+  }
+  if (!kv && shape->batch > 0 &&
+      (shape->kv_rows < 0 || shape->kv_batch_stride < 0 ||
+       static_cast<long long>(shape->batch - 1) * shape->kv_batch_stride + shape->kv_rows >
+           cache->rows)) {
+    record_error("dsv4cuda_sparse_attn: batch regions exceed the cache's %lld rows", cache->rows);
+    return -1;
+  }
+  auto misaligned = [](const void* ptr, uintptr_t a) {
+    return ptr && (reinterpret_cast<uintptr_t>(ptr) % a) != 0;
+  };
+  // the kernels move q, kv, out, the cache codes and rope values in 16-byte vectors
+  if (misaligned(q, 16) || misaligned(out, 16) || misaligned(kv, 16) || misaligned(workspace, 16) ||
+      (!kv && (misaligned(cache->codes, 16) || misaligned(cache->rope, 16) ||
+               misaligned(cache->scales, 8)))) {
+    record_error("dsv4cuda_sparse_attn: q, out, kv, workspace, cache codes and rope must be "
+                 "16-byte aligned (cache scales 8-byte)");
+    return -1;
+  }
+  dsv4::AttnProblem p = make_problem(shape, q, kv, cache, sink, idx, rope_cos, rope_sin, out);
+  const size_t need = dsv4::attn_workspace_bytes(p);
+  void* ws = workspace;
+  if (!ws) {
+    if (need > t_attn.cap) {
+      if (t_attn.ws) cudaFree(t_attn.ws);
+      t_attn.ws = nullptr;
+      t_attn.cap = 0;
+      if (cudaMalloc(&t_attn.ws, need) != cudaSuccess) {
+        record_error("dsv4cuda_sparse_attn: cannot allocate %zu bytes of workspace", need);
+        return -1;
+      }
+      t_attn.cap = need;
+    }
+    ws = t_attn.ws;
+  } else if (workspace_bytes < need) {
+    record_error("dsv4cuda_sparse_attn: workspace of %zu bytes, need %zu", workspace_bytes, need);
+    return -1;
+  }
+  cudaEvent_t eb = nullptr, ee = nullptr;
+  if (t_attn.timing) {
+    const size_t i = static_cast<size_t>(t_attn.timed) * 2;
+    while (t_attn.events.size() < i + 2) {
+      cudaEvent_t ev;
+      if (cudaEventCreate(&ev) != cudaSuccess) { record_error("event create failed"); return -1; }
+      t_attn.events.push_back(ev);
+    }
+    eb = t_attn.events[i];
+    ee = t_attn.events[i + 1];
+    ++t_attn.timed;
+  }
+  cudaError_t e = dsv4::attn_forward(p, ws, static_cast<cudaStream_t>(stream), eb, ee);
+  if (e != cudaSuccess) {
+    record_error("dsv4cuda_sparse_attn: %s", cudaGetErrorString(e));
+    return -1;
+  }
+  return 0;
+}
+
+DSV4_API int dsv4cuda_attn_timing_begin(void) {
+  t_attn.timing = true;
+  t_attn.timed = 0;
+  return 0;
+}
+
+DSV4_API int dsv4cuda_attn_timing_end(int* n_calls, float* main_ms) {
+  t_attn.timing = false;
+  float total = 0.f;
+  for (int i = 0; i < t_attn.timed; ++i) {
+    float ms = 0.f;
+    if (cudaEventSynchronize(t_attn.events[2 * i + 1]) != cudaSuccess ||
+        cudaEventElapsedTime(&ms, t_attn.events[2 * i], t_attn.events[2 * i + 1]) != cudaSuccess) {
+      record_error("attention timing events failed");
+      return -1;
+    }
+    total += ms;
+  }
+  if (n_calls) *n_calls = t_attn.timed;
+  if (main_ms) *main_ms = total;
+  t_attn.timed = 0;
+  return 0;
+}
+
+DSV4_API void dsv4cuda_sparse_attn_host(float* o, const float* q, const float* kv,
+                                        const float* attn_sink, const int* topk_idx,
+                                        int topk_total, int H, int d, float scale) {
+  if (H <= 0 || d <= 0) return;
+  if (ensure_thread_state() != 0) { fatal_or_record("init", cudaErrorInitializationError); return; }
+  cudaStream_t st = t_state.stream;
+  const int n = topk_total > 0 ? topk_total : 0;
+  long long rows = 0;
+  for (int t = 0; t < n; ++t) rows = std::max<long long>(rows, static_cast<long long>(topk_idx[t]) + 1);
+  dsv4cuda_attn_shape s{};
+  s.batch = 1;
+  s.heads = H;
+  s.head_dim = d;
+  s.n_keys = n;
+  s.scale = scale;
+  s.rope_dim = 0;
+  s.kv_batch_stride = 0;
+  s.kv_rows = rows;
+  const size_t qb = sizeof(float) * H * d, kb = sizeof(float) * static_cast<size_t>(rows) * d;
+  char* base = staging(al(qb) * 2 + al(kb) + al(sizeof(float) * H) + al(sizeof(int) * (n + 1)) + 256);
+  if (!base) { fatal_or_record("staging cudaMalloc", cudaErrorMemoryAllocation); return; }
+  Carver cv{base};
+  float* dq = cv.take<float>(static_cast<size_t>(H) * d);
+  float* dout = cv.take<float>(static_cast<size_t>(H) * d);
+  float* dkv = cv.take<float>(static_cast<size_t>(rows) * d + 1);
+  float* dsink = cv.take<float>(H);
+  int* didx = cv.take<int>(n + 1);
+  STAGE_CHECK(cudaMemcpyAsync(dq, q, qb, cudaMemcpyHostToDevice, st), "copy q");
+  if (kb) STAGE_CHECK(cudaMemcpyAsync(dkv, kv, kb, cudaMemcpyHostToDevice, st), "copy kv");
+  STAGE_CHECK(cudaMemcpyAsync(dsink, attn_sink, sizeof(float) * H, cudaMemcpyHostToDevice, st),
+              "copy sink");
+  if (n) STAGE_CHECK(cudaMemcpyAsync(didx, topk_idx, sizeof(int) * n, cudaMemcpyHostToDevice, st),
+                     "copy idx");
+  if (dsv4cuda_sparse_attn(dout, dq, dkv, nullptr, dsink, didx, nullptr, nullptr, &s, nullptr, 0,
+                           st) != 0) {
+    fatal_or_record("sparse_attn", cudaErrorInvalidValue);
+    return;
+  }
+  STAGE_CHECK(cudaMemcpyAsync(o, dout, qb, cudaMemcpyDeviceToHost, st), "copy o");
+  STAGE_CHECK(cudaStreamSynchronize(st), "sync");
 }

@@ -29,12 +29,6 @@ namespace {
 
 constexpr double kU = 5.9604644775390625e-08;  // 2^-24, fp32 unit roundoff
 
-__device__ __forceinline__ double warp_sum_d(double v) {
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-  return v;
-}
-
 // sqrt(softplus(z)) in the reference's fp32 operation order
 // (src/dsv4/dsv4_model.c:5827).
 __device__ __forceinline__ float sqrt_softplus_f(float z) {

@@ -329,3 +329,113 @@ class MoeLayer:
             self.handle, x.data_ptr(), None if token_ids is None else token_ids.data_ptr(), n,
             1 if public_router else 0, _p(idx, i32p), _p(wt, f32p)))
         return idx, wt, fallbacks
+
+
+# ------------------------------------------------------------ attention --
+
+class KvCache(C.Structure):
+    _fields_ = [("codes", vp), ("scales", vp), ("rope", vp), ("nope", C.c_int),
+                ("rope_dim", C.c_int), ("rows", C.c_longlong)]
+
+
+class AttnShape(C.Structure):
+    _fields_ = [("batch", C.c_int), ("heads", C.c_int), ("head_dim", C.c_int),
+                ("n_keys", C.c_int), ("scale", C.c_float), ("rope_dim", C.c_int),
+                ("kv_batch_stride", C.c_longlong), ("kv_rows", C.c_longlong)]
+
+
+lib.dsv4cuda_kv_write.restype = C.c_int
+lib.dsv4cuda_kv_write.argtypes = [vp, vp, vp, C.c_int, vp]
+lib.dsv4cuda_kv_read.restype = C.c_int
+lib.dsv4cuda_kv_read.argtypes = [vp, vp, C.c_int, vp, vp]
+lib.dsv4cuda_attn_workspace_bytes.restype = C.c_size_t
+lib.dsv4cuda_attn_workspace_bytes.argtypes = [vp, C.c_int]
+lib.dsv4cuda_sparse_attn.restype = C.c_int
+lib.dsv4cuda_sparse_attn.argtypes = [vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, C.c_size_t, vp]
+lib.dsv4cuda_sparse_attn_host.restype = None
+lib.dsv4cuda_sparse_attn_host.argtypes = [f32p, f32p, f32p, f32p, i32p, C.c_int, C.c_int,
+                                          C.c_int, C.c_float]
+lib.dsv4cuda_attn_timing_begin.restype = C.c_int
+lib.dsv4cuda_attn_timing_end.restype = C.c_int
+lib.dsv4cuda_attn_timing_end.argtypes = [i32p, f32p]
+
+
+def _stream(stream):
+    if stream is None:
+        import torch
+        return torch.cuda.current_stream().cuda_stream
+    return stream
+
+
+class LatentCache:
+    """FP8 latent cache in HBM (dsv4cuda_kv_cache): torch uint8/int16 tensors
+    for codes [rows][nope], scales [rows][8], rope [rows][rope_dim]."""
+
+    def __init__(self, rows: int, nope: int = 448, rope_dim: int = 64, device="cuda"):
+        import torch
+        self.codes = torch.zeros((rows, nope), dtype=torch.uint8, device=device)
+        self.scales = torch.zeros((rows, 8), dtype=torch.uint8, device=device)
+        self.rope = torch.zeros((rows, rope_dim), dtype=torch.int16, device=device)
+        self.nope, self.rope_dim, self.rows = nope, rope_dim, rows
+        self.struct = KvCache(self.codes.data_ptr(), self.scales.data_ptr(),
+                              self.rope.data_ptr(), nope, rope_dim, rows)
+
+    @property
+    def bytes_per_row(self) -> int:
+        return self.nope + 8 + 2 * self.rope_dim
+
+    def write(self, kv, rows, stream=None):
+        """kv: torch CUDA float32 [n][nope+rope]; rows: torch CUDA int64 [n]."""
+        _check(lib.dsv4cuda_kv_write(C.byref(self.struct), kv.data_ptr(), rows.data_ptr(),
+                                     kv.shape[0], _stream(stream)))
+
+    def read(self, rows, out, stream=None):
+        _check(lib.dsv4cuda_kv_read(C.byref(self.struct), rows.data_ptr(), rows.shape[0],
+                                    out.data_ptr(), _stream(stream)))
+
+
+def attn_shape(batch, heads, head_dim, n_keys, scale, rope_dim=64, kv_batch_stride=0,
+               kv_rows=0):
+    return AttnShape(batch, heads, head_dim, n_keys, scale, rope_dim, kv_batch_stride, kv_rows)
+
+
+def attn_workspace_bytes(shape: AttnShape, use_cache: bool) -> int:
+    return lib.dsv4cuda_attn_workspace_bytes(C.byref(shape), 1 if use_cache else 0)
+
+
+def sparse_attn(out, q, sink, idx, shape: AttnShape, kv=None, cache: LatentCache = None,
+                rope_cos=None, rope_sin=None, workspace=None, stream=None):
+    """dsv4cuda_sparse_attn on torch CUDA tensors (fp32 q/kv/sink/out, int32
+    idx). Either kv (fp32 rows) or cache."""
+    ws = None if workspace is None else workspace.data_ptr()
+    wsb = 0 if workspace is None else workspace.numel() * workspace.element_size()
+    _check(lib.dsv4cuda_sparse_attn(
+        out.data_ptr(), q.data_ptr(), None if kv is None else kv.data_ptr(),
+        None if cache is None else C.byref(cache.struct), sink.data_ptr(),
+        idx.data_ptr(), None if rope_cos is None else rope_cos.data_ptr(),
+        None if rope_sin is None else rope_sin.data_ptr(), C.byref(shape), ws, wsb,
+        _stream(stream)))
+
+
+def sparse_attn_host(q, kv, sink, idx, scale):
+    """Reference-shaped host form: q [H][d], kv [rows][d], sink [H], idx [n]."""
+    q = _f32(q)
+    kv = _f32(kv)
+    sink = _f32(sink)
+    idx = np.ascontiguousarray(idx, dtype=np.int32)
+    H, d = q.shape
+    o = np.empty_like(q)
+    lib.dsv4cuda_sparse_attn_host(_p(o, f32p), _p(q, f32p), _p(kv, f32p), _p(sink, f32p),
+                                  _p(idx, i32p), idx.size, H, d, scale)
+    return o
+
+
+def attn_timing_begin():
+    _check(lib.dsv4cuda_attn_timing_begin())
+
+
+def attn_timing_end():
+    n = C.c_int(0)
+    ms = C.c_float(0)
+    _check(lib.dsv4cuda_attn_timing_end(C.byref(n), C.byref(ms)))
+    return n.value, ms.value

@@ -233,6 +233,80 @@ int dsv4cuda_moe_forward_noalloc(const dsv4cuda_moe_config *cfg,
 /* Device bytes the layer holds (weights it owns + workspace). */
 size_t dsv4cuda_moe_device_bytes(const dsv4cuda_moe_layer *L);
 
+/* ---------------------------------------------------------------------
+ * Latent KV cache and decode attention.
+ *
+ * The reference keeps each layer's latent cache as fp32 rows
+ * (kv_cache [win + max_comp][head_dim], src/dsv4/dsv4_model.c:2416) whose
+ * non-RoPE dims hold bf16(e4m3 * 2^k) with one power-of-two scale per 64 dims
+ * (dsv4_act_quant_inplace group 64 mode 0, :1386, applied at :5300) and whose
+ * RoPE dims hold BF16 (:1555). dsv4cuda_kv_cache stores exactly those values
+ * as E4M3 codes + E8M0 scale codes + BF16, losslessly (DEVICE pointers):
+ *   codes  [rows][nope]      scales [rows][8]      rope [rows][rope_dim] */
+typedef struct {
+    uint8_t *codes;
+    uint8_t *scales;
+    uint16_t *rope;
+    int nope;          /* head_dim - rope_dim; multiple of 64, <= 512 */
+    int rope_dim;
+    long long rows;
+} dsv4cuda_kv_cache;
+
+/* Quantise n latents kv [n][nope + rope_dim] (fp32, BF16-valued: the
+ * reference's kvn after kv_norm and RoPE) into cache rows rows[n]; the
+ * reference's dsv4_act_quant_inplace + memcpy into the ring slot
+ * (src/dsv4/dsv4_model.c:5300-5304). Device pointers, async on `stream`. */
+int dsv4cuda_kv_write(const dsv4cuda_kv_cache *cache, const float *kv, const long long *rows,
+                      int n, void *stream);
+/* Decode cache rows rows[n] to fp32 [n][nope + rope_dim], the exact values
+ * the reference would hold in its kv_cache. */
+int dsv4cuda_kv_read(const dsv4cuda_kv_cache *cache, const long long *rows, int n, float *out,
+                     void *stream);
+
+typedef struct {
+    int batch;            /* independent queries (decode batch) */
+    int heads;            /* H */
+    int head_dim;         /* d (512 for DSV4: 448 + 64 RoPE) */
+    int n_keys;           /* topk_total: indices per query */
+    float scale;          /* d^-1/2 */
+    int rope_dim;         /* inverse RoPE on the last rope_dim dims */
+    long long kv_batch_stride;  /* cache rows between consecutive queries' caches */
+    long long kv_rows;    /* valid rows per query (indices must be < kv_rows) */
+} dsv4cuda_attn_shape;
+
+/* Device scratch bytes dsv4cuda_sparse_attn needs for `shape`. */
+size_t dsv4cuda_attn_workspace_bytes(const dsv4cuda_attn_shape *shape, int use_cache);
+
+/* Replaces sparse_attn (src/dsv4/dsv4_model.c:5767-5822) followed by
+ * dsv4_rope_apply_buf_inv (:5373) for `batch` queries at once. DEVICE
+ * pointers: q [batch][H][d] (BF16-valued fp32), either kv (fp32 rows, the
+ * reference layout, row = b * kv_batch_stride + idx) or cache (kv == NULL),
+ * sink [H], idx [batch][n_keys] (-1 = padding, as topk_idx), rope_cos /
+ * rope_sin [batch][rope_dim/2] (NULL: no inverse RoPE), out [batch][H][d]
+ * (BF16-valued). workspace may be NULL (the library keeps a per-thread
+ * buffer, allocating when it grows). d = 512 with H <= 128 runs the
+ * tensor-core kernel; other shapes run SIMT kernels. Results agree with the
+ * reference within the tolerance stated in the tests (BF16 weights and
+ * outputs; summation order differs). Index >= kv_rows sets device-error
+ * bit 2 and the key is skipped. */
+int dsv4cuda_sparse_attn(float *out, const float *q, const float *kv,
+                         const dsv4cuda_kv_cache *cache, const float *sink, const int *idx,
+                         const float *rope_cos, const float *rope_sin,
+                         const dsv4cuda_attn_shape *shape, void *workspace,
+                         size_t workspace_bytes, void *stream);
+
+/* Host-pointer form with the reference's sparse_attn arguments
+ * (o, q, kv, attn_sink, topk_idx, topk_total, H, d, scale;
+ * src/dsv4/dsv4_model.c:5767): stages to the GPU, runs, copies o back. */
+void dsv4cuda_sparse_attn_host(float *o, const float *q, const float *kv, const float *attn_sink,
+                               const int *topk_idx, int topk_total, int H, int d, float scale);
+
+/* Attention kernel timing for roofline measurement (CUDA events around the
+ * main attention kernel of every dsv4cuda_sparse_attn call on this thread
+ * between _begin and _end; not inside graph capture). */
+int dsv4cuda_attn_timing_begin(void);
+int dsv4cuda_attn_timing_end(int *n_calls, float *main_ms);
+
 #ifdef __cplusplus
 }
 #endif

@@ -567,3 +567,22 @@ uint64_t orc_xorshift_next_many(uint64_t *dst, int64_t n, uint64_t state)
     }
     return state;
 }
+
+/* dsv4_rope_apply_buf_inv (src/dsv4/dsv4_model.c:1569-1580): pairs
+ * (x0, x1) -> (bf16(x0 c + x1 s), bf16(-x0 s + x1 c)), no contraction. */
+void orc_rope_inv(float *x, int heads, int head_dim, const float *cosv,
+                  const float *sinv, int n)
+{
+    const int start = head_dim - 2 * n;
+    for (int h = 0; h < heads; h++) {
+        float *p = x + (size_t)h * head_dim + start;
+        for (int i = 0; i < n; i++) {
+            const float x0 = p[2 * i], x1 = p[2 * i + 1];
+            const float c = cosv[i], s = sinv[i];
+            const float a = x0 * c, b = x1 * s;
+            const float e = -x0 * s, f = x1 * c;
+            p[2 * i] = orc_bf16r(a + b);
+            p[2 * i + 1] = orc_bf16r(e + f);
+        }
+    }
+}

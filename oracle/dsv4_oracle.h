@@ -120,6 +120,10 @@ void orc_moe_forward(float *out, int *idx_out, float *wt_out,
 void orc_sparse_attn(float *o, const float *q, const float *kv,
                      const float *attn_sink, const int *topk_idx,
                      int topk_total, int H, int d, float scale);
+/* Inverse RoPE on the last 2n dims of each head
+ * (dsv4_rope_apply_buf_inv, src/dsv4/dsv4_model.c:1569-1580). */
+void orc_rope_inv(float *x, int heads, int head_dim, const float *cosv,
+                  const float *sinv, int n);
 
 /* ---- helpers for tests ---- */
 uint64_t orc_xorshift_fill_u8(uint8_t *dst, int64_t n, uint64_t state,

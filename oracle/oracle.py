@@ -218,6 +218,14 @@ class Oracle(_Lib):
                                   C.c_int(limit), C.c_float(weight))
         return y, qy, qs
 
+    def rope_inv(self, x, cosv, sinv):
+        """x [heads][d] (copied), cos/sin [n]: inverse RoPE on the last 2n dims."""
+        x = np.array(x, dtype=np.float32, copy=True)
+        c, s = _f32(cosv), _f32(sinv)
+        self.lib.orc_rope_inv(_p(x, f32p), x.shape[0], x.shape[1], _p(c, f32p), _p(s, f32p),
+                              c.size)
+        return x
+
     def sparse_attn(self, q, kv, sink, idx, scale):
         H, d = q.shape
         o = np.empty((H, d), np.float32)
@@ -337,6 +345,13 @@ class Ref(_Lib):
                                          _p(_f32(gate), f32p), _p(_f32(up), f32p), n,
                                          C.c_int(limit), C.c_float(weight))
         return y, qy, qs
+
+    def rope_inv(self, x, cosv, sinv):
+        x = np.array(x, dtype=np.float32, copy=True)
+        c, s = _f32(cosv).copy(), _f32(sinv).copy()
+        self.lib.ref_rope_inv(_p(x, f32p), x.shape[0], x.shape[1], _p(c, f32p), _p(s, f32p),
+                              c.size)
+        return x
 
     def sparse_attn(self, q, kv, sink, idx, scale):
         H, d = q.shape

@@ -201,3 +201,14 @@ REF_API int ref_omp_max_threads(void)
     return 1;
 #endif
 }
+
+/* dsv4_rope_apply_buf_inv (src/dsv4/dsv4_model.c:1569). */
+REF_API void ref_rope_inv(float *x, int heads, int head_dim, float *cosv,
+                          float *sinv, int n)
+{
+    DSV4RopeFreq f;
+    f.cosv = cosv;
+    f.sinv = sinv;
+    f.n = n;
+    dsv4_rope_apply_buf_inv(x, heads, head_dim, &f);
+}
