@@ -59,6 +59,13 @@ def parse():
                     help="expert intermediate size (smaller only for profiling captures)")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end leg")
+    ap.add_argument("--workload", default="moe", choices=["moe", "attn"],
+                    help="moe: config 2 MoE layer (default); attn: config 3 latent decode "
+                         "attention at --attn-batch/--attn-ctx")
+    ap.add_argument("--attn-batch", type=int, default=32)
+    ap.add_argument("--attn-ctx", type=int, default=32768)
+    ap.add_argument("--no-attn-sweep", action="store_true",
+                    help="skip the config 3 attention sweep attached to the MoE line")
     return ap.parse_args()
 
 
@@ -255,6 +262,9 @@ def main():
     if args.impl == "reference":
         run_reference_arm(args, rank, world)
         return
+    if args.workload == "attn":
+        main_attn(args, rank, world, local)
+        return
 
     import torch
     torch.cuda.set_device(local)
@@ -374,6 +384,11 @@ def main():
     if not args.no_e2e:
         e2e_val = run_e2e(args, layers, x_host, M, pool, lib, dsv4cuda)
 
+    # ---- config 3 attention sweep (replicated part of the decode layer)
+    attn = None
+    if rank == 0 and not args.no_attn_sweep:
+        attn = run_attn_sweep(torch, dsv4cuda, dev)
+
     line = None
     if rank == 0:
         cpu = None
@@ -411,6 +426,7 @@ def main():
             "gpu_launches": 9 * args.steps,
             "router_tie_fallbacks": fallbacks,
             "clocks": clk,
+            "attn_config3": attn,
         }
         print(json.dumps(line), flush=True)
     for _, L in layers:
@@ -444,6 +460,236 @@ def run_e2e(args, layers, x_host, M, pool, lib, dsv4cuda):
     e2e_s = time.perf_counter() - t0
     e2e_val = M * e2e_steps / e2e_s
     return e2e_val
+
+
+# ------------------------------------------------- config 3: attention ----
+ATTN_H, ATTN_D = 128, 512
+ATTN_SWEEP = [(1, 4096), (8, 4096), (32, 4096), (1, 32768), (8, 32768), (32, 32768)]
+ATTN_METRIC = "latent decode attention queries/s (config 3: 128 heads x 512, FP8 latent cache)"
+
+
+def attn_flops(B, ctx):
+    return B * 2 * 2 * ATTN_H * ATTN_D * ctx  # Q K^T and P V
+
+
+def attn_bytes(B, ctx):
+    # FP8 cache (584 B per position) + q in + o out (fp32 at the C ABI)
+    return B * (ctx * 584 + 2 * ATTN_H * ATTN_D * 4)
+
+
+class AttnCase:
+    """Config 3 inputs on the device: latent rows N(0,1) (BF16) quantised into
+    the FP8 cache by the reference's KV QAT rule, q and sink N(0,1), positions
+    0..ctx-1 for every query of the batch."""
+
+    def __init__(self, torch, dsv4cuda, dev, B, ctx, seed=0):
+        g = torch.Generator(device=dev)
+        g.manual_seed(seed)
+        rows = B * ctx
+        self.cache = dsv4cuda.LatentCache(rows, device=dev)
+        chunk = 1 << 16
+        for r0 in range(0, rows, chunk):
+            n = min(chunk, rows - r0)
+            kv = torch.randn((n, ATTN_D), generator=g, device=dev).to(torch.bfloat16).float()
+            self.cache.write(kv, torch.arange(r0, r0 + n, device=dev, dtype=torch.int64))
+        self.q = torch.randn((B, ATTN_H, ATTN_D), generator=g, device=dev).to(
+            torch.bfloat16).float()
+        self.sink = torch.randn(ATTN_H, generator=g, device=dev)
+        self.idx = torch.arange(ctx, device=dev, dtype=torch.int32).repeat(B, 1).contiguous()
+        self.out = torch.empty_like(self.q)
+        self.shape = dsv4cuda.attn_shape(B, ATTN_H, ATTN_D, ctx, ATTN_D ** -0.5, 64, ctx, ctx)
+        self.ws = torch.empty(dsv4cuda.attn_workspace_bytes(self.shape, True), dtype=torch.uint8,
+                              device=dev)
+        self.B, self.ctx = B, ctx
+
+    def run(self, dsv4cuda, stream):
+        dsv4cuda.sparse_attn(self.out, self.q, self.sink, self.idx, self.shape, cache=self.cache,
+                             workspace=self.ws, stream=stream)
+
+
+def attn_measure(torch, dsv4cuda, case, stream, iters, warmup, flush):
+    """Mean device time of one call (all kernels) and of its main tensor-core
+    kernel, with L2 flushed before every timed call."""
+    with torch.cuda.stream(stream):
+        for _ in range(warmup):
+            case.run(dsv4cuda, stream.cuda_stream)
+    torch.cuda.synchronize()
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(iters)]
+    dsv4cuda.attn_timing_begin()
+    with torch.cuda.stream(stream):
+        for a, b in evs:
+            flush.zero_()
+            a.record(stream)
+            case.run(dsv4cuda, stream.cuda_stream)
+            b.record(stream)
+    torch.cuda.synchronize()
+    n, main_ms = dsv4cuda.attn_timing_end()
+    call_ms = sum(a.elapsed_time(b) for a, b in evs) / iters
+    return call_ms, main_ms / max(n, 1)
+
+
+def peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        p = json.load(open(path))
+        return float(p["hbm_gbs"]), float(p["bf16_tflops"]), "measured"
+    return 6650.0, 1590.0, "fallback"
+
+
+def attn_point(torch, dsv4cuda, dev, stream, B, ctx, iters, warmup, flush):
+    case = AttnCase(torch, dsv4cuda, dev, B, ctx, seed=B * 7 + ctx)
+    call_ms, main_ms = attn_measure(torch, dsv4cuda, case, stream, iters, warmup, flush)
+    hbm, tfl, src = peaks()
+    fl, by = attn_flops(B, ctx), attn_bytes(B, ctx)
+    bound_ms = max(fl / (tfl * 1e12), by / (hbm * 1e9)) * 1e3
+    res = {"batch": B, "ctx": ctx, "us_per_call": call_ms * 1e3, "main_kernel_us": main_ms * 1e3,
+           "tflops": fl / (call_ms * 1e-3) / 1e12, "gbs": by / (call_ms * 1e-3) / 1e9,
+           "frac_tensor": fl / (call_ms * 1e-3) / 1e12 / tfl,
+           "frac_hbm": by / (call_ms * 1e-3) / 1e9 / hbm,
+           "roofline_frac": bound_ms / call_ms}
+    del case
+    torch.cuda.empty_cache()
+    return res
+
+
+def run_attn_sweep(torch, dsv4cuda, dev, iters=10, warmup=3):
+    stream = torch.cuda.Stream(device=dev)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    out = [attn_point(torch, dsv4cuda, dev, stream, B, ctx, iters, warmup, flush)
+           for B, ctx in ATTN_SWEEP]
+    del flush
+    return out
+
+
+def cpu_attn_reference(seconds, B, ctx):
+    """Reference sparse_attn (oracle/_ref, OpenMP over heads) on the host:
+    queries/s on a bounded sample of the config (one query at a time)."""
+    from oracle import REF_SO, Oracle
+    rng = np.random.default_rng(5)
+    kv = rng.normal(size=(ctx, ATTN_D)).astype(np.float32)
+    o = Oracle()
+    for r in range(ctx):  # the reference's cache values (KV QAT, group 64)
+        kv[r, :448] = o.act_quant_inplace(kv[r, :448], 64, 0)
+    q = rng.normal(size=(ATTN_H, ATTN_D)).astype(np.float32)
+    sink = rng.normal(size=ATTN_H).astype(np.float32)
+    idx = np.arange(ctx, dtype=np.int32)
+    if os.path.exists(REF_SO):
+        from oracle import Ref
+        r = Ref()
+        kind, cores = "reference", r.lib.ref_omp_max_threads()
+        run = lambda: r.sparse_attn(q, kv, sink, idx, ATTN_D ** -0.5)  # noqa: E731
+    else:
+        kind, cores = "port", 1
+        run = lambda: o.sparse_attn(q, kv, sink, idx, ATTN_D ** -0.5)  # noqa: E731
+    run()
+    n, t0 = 0, time.perf_counter()
+    while True:
+        run()
+        n += 1
+        el = time.perf_counter() - t0
+        if el >= seconds:
+            break
+    return n / el, cores, kind, (f"{n} single-query sparse_attn calls (128 heads x 512, "
+                                 f"ctx {ctx}), {el:.1f} s on {cores} thread(s)")
+
+
+def main_attn(args, rank, world, local):
+    """--workload attn: config 3 at --attn-batch x --attn-ctx. Attention is
+    replicated (every rank holds every query), so N GPUs run N replicas."""
+    import torch
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    import dsv4cuda
+    dsv4cuda.set_abort_on_error(False)
+    dsv4cuda.init(local)
+    B, ctx = args.attn_batch, args.attn_ctx
+    case = AttnCase(torch, dsv4cuda, dev, B, ctx, seed=3)
+    stream = torch.cuda.Stream(device=dev)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            case.run(dsv4cuda, stream.cuda_stream)
+    torch.cuda.synchronize()
+    clocks = ClockSampler(local)
+    clocks.start()
+    time.sleep(0.3)
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    total = 0.0
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(args.steps)]
+    dsv4cuda.attn_timing_begin()
+    with torch.cuda.stream(stream):
+        for a, b in evs:
+            flush.zero_()
+            a.record(stream)
+            case.run(dsv4cuda, stream.cuda_stream)
+            b.record(stream)
+    torch.cuda.synchronize()
+    n_main, main_ms = dsv4cuda.attn_timing_end()
+    total = sum(a.elapsed_time(b) for a, b in evs)
+    if dist:
+        dist.barrier()
+        t = torch.tensor([total], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        total = float(t.item())
+    clk = clocks.stop()
+    ms = total / args.steps
+    main_ms = main_ms / max(n_main, 1)
+    hbm, tfl, src = peaks()
+    fl, by = attn_flops(B, ctx), attn_bytes(B, ctx)
+    # e2e: q from pinned host memory in, o back to pinned host memory, cache resident
+    qh = case.q.cpu().pin_memory()
+    oh = torch.empty_like(qh).pin_memory()
+    e2e_steps = max(5, args.steps // 2)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    with torch.cuda.stream(stream):
+        for _ in range(e2e_steps):
+            case.q.copy_(qh, non_blocking=True)
+            case.run(dsv4cuda, stream.cuda_stream)
+            oh.copy_(case.out, non_blocking=True)
+            stream.synchronize()
+    e2e = B * e2e_steps / (time.perf_counter() - t0)
+    if rank == 0:
+        cpu = None
+        if world == 1 and not args.no_cpu:
+            v, cores, kind, sample = cpu_attn_reference(args.cpu_seconds, B, ctx)
+            cpu = {"value": v, "unit": "queries/s", "cores": cores, "kind": kind,
+                   "sample": sample}
+        line = {
+            "metric": ATTN_METRIC, "value": B * world / (ms * 1e-3), "unit": "queries/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "bf16*bf16->f32 (FP8 e4m3 cache)", "data": "synthetic",
+            "config": {"workload": f"config 3 latent decode attention, batch {B}, ctx {ctx}",
+                       "heads": ATTN_H, "head_dim": ATTN_D, "rope": 64, "batch": B, "ctx": ctx,
+                       "l2": "flushed (256 MB write) before every timed call",
+                       "parallelism": f"replicas{world}"},
+            "roofline": {"bound": "tensor" if fl / tfl > by / hbm * 1e3 else "hbm",
+                         "achieved": fl / (main_ms * 1e-3) / 1e12, "peak": tfl,
+                         "unit": "TFLOP/s", "frac": fl / (main_ms * 1e-3) / 1e12 / tfl,
+                         "traffic": None, "kernel": "attn_tc_kernel",
+                         "alg_flops_per_call": fl, "alg_bytes_per_call": by,
+                         "hbm_gbs": by / (main_ms * 1e-3) / 1e9, "hbm_peak": hbm,
+                         "peak_source": src, "main_kernel_ms": main_ms},
+            "cpu_baseline": cpu,
+            "e2e": {"value": e2e, "unit": "queries/s", "h2d_bytes_per_step": B * ATTN_H * ATTN_D * 4,
+                    "d2h_bytes_per_step": B * ATTN_H * ATTN_D * 4},
+            "gpu_launches": 2 * args.steps,
+            "clocks": clk,
+        }
+        print(json.dumps(line), flush=True)
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
 
 
 if __name__ == "__main__":

@@ -459,41 +459,62 @@ __global__ void __launch_bounds__(kTcThreads, 1) attn_tc_kernel(const __grid_con
     __syncwarp();
   } else if (warp >= 4) {
     // ------------------------------------------------- latent tile producer
+    // Thread (r, qd) owns key r of every tile and dims [128 qd, 128 qd + 128).
+    // The indices of tile j + 2 are read and the rows bulk-prefetched into L2
+    // while tile j is converted; the registers of tile j + 1 are loaded right
+    // after tile j is handed over, so the HBM latency overlaps two tiles.
     const int c = threadIdx.x - 128;
     const int r = c >> 2, qd = c & 3;  // key row in tile, quarter of the dims
     const int* idxb = a.idx + static_cast<size_t>(b) * a.n;
     const long long rbase = static_cast<long long>(b) * a.kv_bstride;
-    for (int j = 0; j < T; ++j) {
-      const int st = j & 1;
+    auto load_idx = [&](int j) -> long long {
       const int key = k0 + j * kTcKeys + r;
-      long long pos = -1;
-      if (key < k_end) {
-        pos = idxb[key];
-        if (pos >= a.kv_rows) {
-          if (a.err) atomicOr(a.err, kErrIndex);
-          pos = -1;
+      return (j < T && key < k_end) ? static_cast<long long>(idxb[key]) : -1;
+    };
+    auto in_range = [&](long long pos) { return pos >= 0 && pos < a.kv_rows; };
+    auto prefetch_rows = [&](long long pos) {
+      if (!in_range(pos)) return;
+      const long long row = rbase + pos;
+      if (a.kv) {
+        bulk_prefetch_l2(a.kv + row * kTcD + qd * 128, 512);
+      } else if (qd == 0) {
+        bulk_prefetch_l2(a.cache.codes + row * kTcNope, kTcNope);
+      } else if (qd == 1) {
+        bulk_prefetch_l2(a.cache.rope + row * kTcRope, kTcRope * 2);
+      } else if (qd == 2 && (row & 1) == 0 && row + 1 < a.cache.rows) {
+        bulk_prefetch_l2(a.cache.scales + row * kKvScaleSlots, 16);  // this row and the next
+      }
+    };
+    // raw FP8 bytes of this thread's slice: qd < 3: 8 x 16 codes; qd == 3:
+    // 4 x 16 codes then 8 x 8 RoPE BF16 values
+    uint4 raw[12];
+    uint32_t scw = 0;
+    auto load_raw = [&](long long pos) {
+      if (!in_range(pos) || a.kv) return;
+      const long long row = rbase + pos;
+      const uint4* cp = reinterpret_cast<const uint4*>(a.cache.codes + row * kTcNope + qd * 128);
+      const uint4* rp = reinterpret_cast<const uint4*>(a.cache.rope + row * kTcRope);
+#pragma unroll
+      for (int u = 0; u < 12; ++u) {
+        if (qd < 3) {
+          if (u < 8) raw[u] = __ldg(cp + u);
+        } else {
+          raw[u] = u < 4 ? __ldg(cp + u) : __ldg(rp + (u - 4));
         }
       }
-      const bool valid = pos >= 0;
-      const long long row = rbase + pos;
-      // raw loads before the stage wait
-      uint4 raw[8];
-      uint32_t scw = 0;
-      if (valid && !a.kv) {
-        const uint4* cp = reinterpret_cast<const uint4*>(a.cache.codes + row * kTcNope + qd * 128);
-        const int ncode = qd < 3 ? 8 : 4;
-#pragma unroll
-        for (int u = 0; u < 8; ++u)
-          if (u < ncode) raw[u] = __ldg(cp + u);
-        scw = *reinterpret_cast<const uint32_t*>(a.cache.scales + row * kKvScaleSlots +
-                                                 (qd < 2 ? 0 : 4));
-      }
-      uint4 rope[8];
-      if (valid && !a.kv && qd == 3) {
-        const uint4* rp = reinterpret_cast<const uint4*>(a.cache.rope + row * kTcRope);
-#pragma unroll
-        for (int u = 0; u < 8; ++u) rope[u] = __ldg(rp + u);
-      }
+      scw = *reinterpret_cast<const uint32_t*>(a.cache.scales + row * kKvScaleSlots +
+                                               (qd < 2 ? 0 : 4));
+    };
+    long long p_cur = load_idx(0), p_nxt = load_idx(1);
+    prefetch_rows(p_cur);
+    prefetch_rows(p_nxt);
+    load_raw(p_cur);
+    for (int j = 0; j < T; ++j) {
+      const int st = j & 1;
+      const long long p_n2 = load_idx(j + 2);
+      if (p_cur >= a.kv_rows && a.err) atomicOr(a.err, kErrIndex);
+      const bool valid = in_range(p_cur);
+      const long long row = rbase + p_cur;
       if (!tc_wait(&bars->kv_empty[st], ((j >> 1) & 1) ^ 1, abort_flag, a.err)) break;
       const uint32_t tile = k_s + st * kKBytes;
       if (!valid) {
@@ -508,10 +529,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) attn_tc_kernel(const __grid_con
                                   pack_bf16x2(x1.x, x1.y), pack_bf16x2(x1.z, x1.w)));
         }
       } else {
-        const int ncode = qd < 3 ? 8 : 4;
 #pragma unroll
         for (int u = 0; u < 8; ++u) {
-          if (u < ncode) {
+          if (qd < 3 || u < 4) {
             const int g = (qd * 128 + u * 16) >> 6;  // scale group
             const uint32_t code = (scw >> (8 * (g & 3))) & 0xFFu;
             const float sc = e8m0_decode(code);
@@ -526,7 +546,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) attn_tc_kernel(const __grid_con
         if (qd == 3) {
 #pragma unroll
           for (int u = 0; u < 8; ++u)
-            st_shared_v4(tile + sw128_off(r, 56 + u, kTcKeys), rope[u]);
+            st_shared_v4(tile + sw128_off(r, 56 + u, kTcKeys), raw[4 + u]);
         }
       }
       // validity mask of the tile's keys (bit r), one byte per producer warp
@@ -540,6 +560,10 @@ __global__ void __launch_bounds__(kTcThreads, 1) attn_tc_kernel(const __grid_con
       __syncwarp();
       fence_async_smem();
       mbar_arrive(&bars->kv_full[st]);
+      prefetch_rows(p_n2);
+      load_raw(p_nxt);
+      p_cur = p_nxt;
+      p_nxt = p_n2;
     }
   } else {
     // --------------------------------------------------------------- softmax
@@ -565,17 +589,20 @@ __global__ void __launch_bounds__(kTcThreads, 1) attn_tc_kernel(const __grid_con
       }
       const float m_new = fmaxf(m_run, tmax);
       const bool resc = (m_new > m_run) && (m_run != -INFINITY);
-      const float alpha = resc ? expf(m_run - m_new) : 1.0f;
+      const float alpha = resc ? __expf(m_run - m_new) : 1.0f;
       den *= alpha;
       uint32_t pw[16];
+      float part[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
       for (int i = 0; i < 32; i += 2) {
-        const float e0 = (s[i] == -INFINITY) ? 0.0f : expf(s[i] - m_new);
-        den += e0;
-        const float e1 = (s[i + 1] == -INFINITY) ? 0.0f : expf(s[i + 1] - m_new);
-        den += e1;
+        // hardware exp2 path (MUFU): relative error ~2^-21, far below the
+        // BF16 rounding the weights get
+        const float e0 = (s[i] == -INFINITY) ? 0.0f : __expf(s[i] - m_new);
+        const float e1 = (s[i + 1] == -INFINITY) ? 0.0f : __expf(s[i + 1] - m_new);
+        part[(i >> 1) & 3] += e0 + e1;
         pw[i / 2] = pack_bf16x2(e0, e1);
       }
+      den += (part[0] + part[1]) + (part[2] + part[3]);
       m_run = m_new;
       if (j > 0) {
         const bool wv = tc_wait(&bars->pv_done[(j - 1) & 1], ((j - 1) >> 1) & 1, abort_flag, a.err);
