@@ -70,10 +70,15 @@ def parse():
 
 
 # ---------------------------------------------------------------- weights --
-def make_device_layer(torch, seed, dev, E=E, I=I):
-    """Random-init config-2 layer in the reference layouts, on the GPU."""
+def make_device_layer(torch, seed, dev, E=E, I=I, expert_range=None):
+    """Random-init config-2 layer in the reference layouts, on the GPU.
+    expert_range=(lo, hi): routed weights of those experts only (expert
+    parallelism); the router and shared expert are the same on every rank."""
+    lo, hi = expert_range if expert_range else (0, E)
     g = torch.Generator(device=dev)
     g.manual_seed(seed)
+    ge = torch.Generator(device=dev)
+    ge.manual_seed(seed * 1000 + lo + 1)
 
     def u8(*shape):
         return torch.randint(0, 256, shape, dtype=torch.uint8, device=dev, generator=g)
@@ -89,14 +94,16 @@ def make_device_layer(torch, seed, dev, E=E, I=I):
         return c.to(torch.uint8)
 
     gate = (torch.randn(E, H, device=dev, generator=g) * 0.02).to(torch.bfloat16).view(torch.uint16)
+    shared = dict(fp8=True, w1=fp8(I, H), s1=e8m0(I // 128, H // 128),
+                  w3=fp8(I, H), s3=e8m0(I // 128, H // 128),
+                  w2=fp8(H, I), s2=e8m0(H // 128, I // 128))
+    n = hi - lo
+    g = ge  # routed experts from this rank's own stream
     return dict(hidden=H, moe_inter=I, n_experts=E, topk=TOPK, route_scale=ROUTE_SCALE,
                 swiglu_limit=LIMIT, gate_w=gate, bias=None, tid2eid=None,
-                w1=u8(E, I, H // 2), s1=e8m0(E, I, H // 32),
-                w3=u8(E, I, H // 2), s3=e8m0(E, I, H // 32),
-                w2=u8(E, H, I // 2), s2=e8m0(E, H, I // 32),
-                shared=dict(fp8=True, w1=fp8(I, H), s1=e8m0(I // 128, H // 128),
-                            w3=fp8(I, H), s3=e8m0(I // 128, H // 128),
-                            w2=fp8(H, I), s2=e8m0(H // 128, I // 128)))
+                w1=u8(n, I, H // 2), s1=e8m0(n, I, H // 32),
+                w3=u8(n, I, H // 2), s3=e8m0(n, I, H // 32),
+                w2=u8(n, H, I // 2), s2=e8m0(n, H, I // 32), shared=shared)
 
 
 def bf16_tokens(rng, n, m):
@@ -280,11 +287,24 @@ def main():
     dsv4cuda.init(local)
 
     M = args.tokens
+    ep = world > 1
+    erange = (rank * args.experts // world, (rank + 1) * args.experts // world) if ep else None
     layers = []
     for li in range(args.layers):
-        lay = make_device_layer(torch, 1000 + li, dev, args.experts, args.inter)
-        layers.append((lay, dsv4cuda.MoeLayer(lay, max_tokens=M, device=True)))
+        lay = make_device_layer(torch, 1000 + li, dev, args.experts, args.inter, erange)
+        layers.append((lay, dsv4cuda.MoeLayer(lay, max_tokens=M, device=True,
+                                              expert_range=erange)))
     torch.cuda.synchronize()
+
+    def layer_forward(L, xin, out, s):
+        """One MoE layer; expert parallel: local experts, NCCL sum of the
+        zero-padded routed slots, ordered combine (bit-identical to 1 GPU)."""
+        if not ep:
+            L.forward(xin, out, stream=s)
+            return
+        L.forward_local(xin, stream=s)
+        dist.all_reduce(L.routed_slots(M), op=dist.ReduceOp.SUM)
+        L.combine(M, out, stream=s)
     rng = np.random.default_rng(7)
     pool = 32
     x_host = bf16_tokens(rng, pool, M)
@@ -296,14 +316,14 @@ def main():
     graphs = []
     xin = torch.empty((M, H), dtype=torch.float32, device=dev)
     with torch.cuda.stream(stream):
-        for _, L in layers:  # warm the kernels once outside capture
+        for _, L in layers:  # warm the kernels (and the communicator) outside capture
             xin.copy_(x_dev[0])
-            L.forward(xin, out_dev, stream=stream.cuda_stream)
+            layer_forward(L, xin, out_dev, stream.cuda_stream)
     stream.synchronize()
     for _, L in layers:
         g = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g, stream=stream):
-            L.forward(xin, out_dev, stream=torch.cuda.current_stream().cuda_stream)
+            layer_forward(L, xin, out_dev, torch.cuda.current_stream().cuda_stream)
         graphs.append(g)
 
     def step(i):
@@ -352,7 +372,7 @@ def main():
         for i in range(max(8, args.steps // 4)):
             _, L = layers[i % len(layers)]
             xin.copy_(x_dev[i % pool])
-            L.forward(xin, out_dev, stream=stream.cuda_stream)
+            layer_forward(L, xin, out_dev, stream.cuda_stream)
             idx, _, fb = L.last_routes(M)
             U_total += len(np.unique(idx))
             fallbacks = fb
@@ -370,6 +390,8 @@ def main():
         sl_ms += d.value
         n_timed += n.value
     U_avg = U_total / max(n_fw, 1)
+    if ep:  # this rank's share of the unique experts (uniform routing)
+        U_avg = U_avg * (erange[1] - erange[0]) / args.experts
     alg_bytes = U_avg * EXPERT_BYTES
     kern_ms = (gu_ms + dn_ms) / max(n_timed, 1)
     achieved = alg_bytes / (kern_ms * 1e-3) / 1e9
@@ -382,11 +404,15 @@ def main():
     # ---- end to end through the public C API with host buffers
     e2e_val = None
     if not args.no_e2e:
-        e2e_val = run_e2e(args, layers, x_host, M, pool, lib, dsv4cuda)
+        if ep:
+            e2e_val = run_e2e_graphs(torch, dist, args, graphs, xin, out_dev, x_host, M, pool,
+                                     stream, dev)
+        else:
+            e2e_val = run_e2e(args, layers, x_host, M, pool, lib, dsv4cuda)
 
     # ---- config 3 attention sweep (replicated part of the decode layer)
     attn = None
-    if rank == 0 and not args.no_attn_sweep:
+    if world == 1 and not args.no_attn_sweep:
         attn = run_attn_sweep(torch, dsv4cuda, dev)
 
     line = None
@@ -429,12 +455,37 @@ def main():
             "attn_config3": attn,
         }
         print(json.dumps(line), flush=True)
+    # graphs holding NCCL calls must be released before the process group
+    torch.cuda.synchronize()
+    for gr in graphs:
+        gr.reset()
+    graphs.clear()
+    g = gr = None  # noqa: F841  (the capture loop's last graph)
     for _, L in layers:
         L.close()
-    del graphs
     if dist:
         dist.barrier()
         dist.destroy_process_group()
+
+
+def run_e2e_graphs(torch, dist, args, graphs, xin, out_dev, x_host, M, pool, stream, dev):
+    """Expert-parallel end to end: every step copies the token from pinned
+    host memory, replays the layer's graph (C API calls + NCCL) and reads
+    the output back; wall time, max over ranks."""
+    pin_x = torch.from_numpy(x_host).pin_memory()
+    pin_out = torch.empty((M, H), dtype=torch.float32).pin_memory()
+    steps = max(20, args.steps // 2)
+    dist.barrier()
+    t0 = time.perf_counter()
+    with torch.cuda.stream(stream):
+        for i in range(steps):
+            xin.copy_(pin_x[i % pool], non_blocking=True)
+            graphs[i % len(graphs)].replay()
+            pin_out.copy_(out_dev, non_blocking=True)
+            stream.synchronize()
+    el = torch.tensor([time.perf_counter() - t0], device=dev)
+    dist.all_reduce(el, op=dist.ReduceOp.MAX)
+    return M * steps / float(el.item())
 
 
 def run_e2e(args, layers, x_host, M, pool, lib, dsv4cuda):

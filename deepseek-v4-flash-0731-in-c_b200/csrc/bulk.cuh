@@ -1,8 +1,7 @@
 // bulk.cuh - sm_100a bulk-copy (TMA engine) and mbarrier primitives.
 //
-// Only the non-multicast forms are used: cp.async.bulk global -> shared of
-// the issuing CTA, completion counted on an mbarrier in that CTA's shared
-// memory. Every wait is bounded by %globaltimer; on timeout the kernel sets
+// Every copy lands in the issuing CTA's own shared memory, its completion
+// counted on an mbarrier in that CTA's shared memory. Every wait is bounded by %globaltimer; on timeout the kernel sets
 // the device error word (read by dsv4cuda_device_error()) instead of hanging.
 #pragma once
 #include <cstdint>
@@ -87,8 +86,8 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
 
 namespace dsv4 {
 
-// 2-D tiled TMA load of one box into this CTA's shared memory (no
-// multicast), completion counted on `bar`. x is the inner (byte) coordinate
+// 2-D tiled TMA load of one box into this CTA's shared memory only,
+// completion counted on `bar`. x is the inner (byte) coordinate
 // and must be a multiple of 16 bytes; the tensor map lives in kernel
 // parameter space (__grid_constant__).
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y,

@@ -363,6 +363,21 @@ int layer_finish(dsv4cuda_moe_layer* L, int max_tokens) {
   return 0;
 }
 
+// While timing is on, the forward records its phase events into a fresh
+// group of 8 events of the layer.
+int timed_workspace(dsv4cuda_moe_layer* L, dsv4::MoeWorkspace* ws) {
+  if (!L->timing) return 0;
+  const size_t need = static_cast<size_t>(L->timed + 1) * 8;
+  while (L->events.size() < need) {
+    cudaEvent_t ev;
+    if (cudaEventCreate(&ev) != cudaSuccess) { record_error("cudaEventCreate"); return -1; }
+    L->events.push_back(ev);
+  }
+  ws->timing = &L->events[static_cast<size_t>(L->timed) * 8];
+  L->timed++;
+  return 0;
+}
+
 dsv4::MoeConfig to_cfg(const dsv4cuda_moe_config* c) {
   dsv4::MoeConfig m{};
   m.hidden = c->hidden;
@@ -664,6 +679,50 @@ DSV4_API int dsv4cuda_moe_create_device(dsv4cuda_moe_layer** out, const dsv4cuda
   return 0;
 }
 
+DSV4_API int dsv4cuda_moe_create_device_ep(dsv4cuda_moe_layer** out,
+                                           const dsv4cuda_moe_config* cfg,
+                                           const dsv4cuda_moe_weights* dw, int max_tokens,
+                                           int expert_lo, int expert_hi) {
+  if (!cfg || expert_lo < 0 || expert_hi <= expert_lo || expert_hi > cfg->n_experts) {
+    record_error("dsv4cuda_moe_create_device_ep: expert range [%d, %d) outside [0, %d)",
+                 expert_lo, expert_hi, cfg ? cfg->n_experts : 0);
+    return -1;
+  }
+  if (dsv4cuda_moe_create_device(out, cfg, dw, max_tokens) != 0) return -1;
+  (*out)->cfg.expert_lo = expert_lo;
+  (*out)->cfg.expert_hi = expert_hi;
+  return 0;
+}
+
+DSV4_API int dsv4cuda_moe_forward_local(dsv4cuda_moe_layer* L, const float* x,
+                                        const int* token_ids, int n_tokens, void* stream) {
+  if (!L || !x || n_tokens < 0 || n_tokens > L->max_tokens) {
+    record_error("dsv4cuda_moe_forward_local: bad arguments");
+    return -1;
+  }
+  if (L->cfg.hash_vocab > 0 && !token_ids) { record_error("hash layer needs token_ids"); return -1; }
+  dsv4::MoeWorkspace ws = L->ws;
+  if (timed_workspace(L, &ws) != 0) return -1;
+  cudaError_t e = dsv4::moe_forward_local(L->cfg, L->w, ws, x, token_ids, n_tokens,
+                                          static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) { record_error("moe_forward_local: %s", cudaGetErrorString(e)); return -1; }
+  return 0;
+}
+
+DSV4_API float* dsv4cuda_moe_routed_slots(dsv4cuda_moe_layer* L) { return L ? L->ws.routed : nullptr; }
+
+DSV4_API int dsv4cuda_moe_combine(dsv4cuda_moe_layer* L, int n_tokens, float* out, void* stream) {
+  if (!L || !out || n_tokens < 0 || n_tokens > L->max_tokens) {
+    record_error("dsv4cuda_moe_combine: bad arguments");
+    return -1;
+  }
+  cudaError_t e = dsv4::moe_combine(L->cfg, L->ws, n_tokens, out,
+                                    L->cfg.shared_kind != 0 && L->w.sh1 != nullptr,
+                                    static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) { record_error("moe_combine: %s", cudaGetErrorString(e)); return -1; }
+  return 0;
+}
+
 DSV4_API void dsv4cuda_moe_destroy(dsv4cuda_moe_layer* L) {
   if (!L) return;
   for (cudaEvent_t e : L->events) cudaEventDestroy(e);
@@ -676,6 +735,7 @@ DSV4_API size_t dsv4cuda_moe_device_bytes(const dsv4cuda_moe_layer* L) {
   return L ? L->owned_bytes + L->ws_bytes : 0;
 }
 
+
 DSV4_API int dsv4cuda_moe_forward(dsv4cuda_moe_layer* L, const float* x, const int* token_ids,
                                   int n_tokens, float* out, void* stream) {
   if (!L || !x || !out || n_tokens < 0) { record_error("dsv4cuda_moe_forward: bad arguments"); return -1; }
@@ -685,16 +745,7 @@ DSV4_API int dsv4cuda_moe_forward(dsv4cuda_moe_layer* L, const float* x, const i
   }
   if (L->cfg.hash_vocab > 0 && !token_ids) { record_error("hash layer needs token_ids"); return -1; }
   dsv4::MoeWorkspace ws = L->ws;
-  if (L->timing) {
-    const size_t need = static_cast<size_t>(L->timed + 1) * 8;
-    while (L->events.size() < need) {
-      cudaEvent_t ev;
-      if (cudaEventCreate(&ev) != cudaSuccess) { record_error("cudaEventCreate"); return -1; }
-      L->events.push_back(ev);
-    }
-    ws.timing = &L->events[static_cast<size_t>(L->timed) * 8];
-    L->timed++;
-  }
+  if (timed_workspace(L, &ws) != 0) return -1;
   cudaError_t e = dsv4::moe_forward(L->cfg, L->w, ws, x, token_ids, n_tokens, out,
                                     static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) { record_error("moe_forward: %s", cudaGetErrorString(e)); return -1; }

@@ -74,6 +74,7 @@ struct RouterArgs {
   GemvItem* items_dn;
   GemvItem* items_sh;
   int* counters;             // [0] items, [1] CTA ticket, [2] tie fallbacks, [3] shared items
+  int elo, ehi;              // experts computed on this device (plan only)
 };
 
 // The reference's fp32 logit chain, replayed exactly (near-tie path):
@@ -319,7 +320,8 @@ __device__ void block_plan(const RouterArgs& a, int* cnt, int* ids) {
   __syncthreads();
   for (int e = threadIdx.x; e < E; e += blockDim.x) {
     int n = 0;
-    for (int r = 0; r < R; ++r) n += (ids[r] == e);
+    if (e >= a.elo && e < a.ehi)
+      for (int r = 0; r < R; ++r) n += (ids[r] == e);
     cnt[e] = (n + kItemTok - 1) / kItemTok;
   }
   __syncthreads();
@@ -344,10 +346,10 @@ __device__ void block_plan(const RouterArgs& a, int* cnt, int* ids) {
     }
   }
   __syncthreads();
-  for (int e = threadIdx.x; e < E; e += blockDim.x) {
+  for (int e = a.elo + threadIdx.x; e < a.ehi; e += blockDim.x) {
     int item = cnt[e];
     GemvItem gu, dn;
-    gu.mat = dn.mat = e;
+    gu.mat = dn.mat = e - a.elo;  // index into this device's expert weights
     gu.ntok = dn.ntok = 0;
     for (int r = 0; r < R; ++r) {
       if (ids[r] != e) continue;
@@ -684,6 +686,8 @@ static cudaError_t route_impl(const MoeConfig& c, const MoeWeights& w, const Moe
   a.idx = ws.idx;
   a.wt = ws.wt;
   a.counters = ws.counters;
+  a.elo = c.expert_lo;
+  a.ehi = moe_local_hi(c);
   if (plan) {
     a.xq = ws.xq;
     a.xs = ws.xs;
@@ -714,14 +718,21 @@ cudaError_t moe_route(const MoeConfig& c, const MoeWeights& w, const MoeWorkspac
   return route_impl(c, w, ws, x, token_ids, M, public_router, false, st);
 }
 
-cudaError_t moe_forward(const MoeConfig& c, const MoeWeights& w, const MoeWorkspace& ws,
-                        const float* x, const int* token_ids, int M, float* out,
-                        cudaStream_t st, const MoeExecOptions& opt) {
+cudaError_t moe_forward_local(const MoeConfig& c, const MoeWeights& w, const MoeWorkspace& ws,
+                              const float* x, const int* token_ids, int M, cudaStream_t st,
+                              const MoeExecOptions& opt) {
   if (M <= 0) return cudaSuccess;
   if (M > ws.max_tokens || c.topk > kMaxTopk || c.n_experts <= 0) return cudaErrorInvalidValue;
+  if (c.expert_lo < 0 || c.expert_lo >= moe_local_hi(c) || moe_local_hi(c) > c.n_experts)
+    return cudaErrorInvalidValue;
   const int H = c.hidden, I = c.moe_inter, K = c.topk;
   const int R = M * K;
+  const int n_local = moe_local_hi(c) - c.expert_lo;
   cudaError_t err;
+  // slots of experts computed elsewhere stay zero for the cross-device sum
+  if (moe_is_partial(c) &&
+      (err = cudaMemsetAsync(ws.routed, 0, sizeof(float) * R * H, st)) != cudaSuccess)
+    return err;
 
   // router: quant + exact logits + selection + expert plan, one launch
   if ((err = route_impl(c, w, ws, x, token_ids, M, 0, true, st)) != cudaSuccess) return err;
@@ -786,7 +797,7 @@ cudaError_t moe_forward(const MoeConfig& c, const MoeWeights& w, const MoeWorksp
   gu.w_stride = w13; gu.s_stride = s13;
   gu.in = H; gu.rows = I; gu.act = act;
   gu.Y[0] = ws.gate; gu.Y[1] = ws.up;
-  gu.items = ws.items_gu; gu.n_items = ws.counters; gu.max_items = R; gu.n_mats = c.n_experts;
+  gu.items = ws.items_gu; gu.n_items = ws.counters; gu.max_items = R; gu.n_mats = n_local;
   gu.err = opt.err;
   if (ws.timing) cudaEventRecord(ws.timing[0], st);
   if ((err = launch_fp4_gemv(gu, true, nt, st, opt.map_cache)) != cudaSuccess) return err;
@@ -799,18 +810,33 @@ cudaError_t moe_forward(const MoeConfig& c, const MoeWeights& w, const MoeWorksp
   dn.w_stride = w2; dn.s_stride = s2;
   dn.in = I; dn.rows = H; dn.act = QAct{ws.qy, ws.qys, I, nullptr};
   dn.Y[0] = ws.routed;
-  dn.items = ws.items_dn; dn.n_items = ws.counters; dn.max_items = R; dn.n_mats = c.n_experts;
+  dn.items = ws.items_dn; dn.n_items = ws.counters; dn.max_items = R; dn.n_mats = n_local;
   dn.err = opt.err;
   if (ws.timing) cudaEventRecord(ws.timing[2], st);
   if ((err = launch_fp4_gemv(dn, false, nt, st, opt.map_cache)) != cudaSuccess) return err;
   if (ws.timing) cudaEventRecord(ws.timing[3], st);
 
   if (side) cudaStreamWaitEvent(st, side->join, 0);
+  return cudaGetLastError();
+}
+
+cudaError_t moe_combine(const MoeConfig& c, const MoeWorkspace& ws, int M, float* out,
+                        bool has_shared, cudaStream_t st) {
+  if (M <= 0) return cudaSuccess;
+  const int H = c.hidden, K = c.topk;
   const size_t n = static_cast<size_t>(M) * H;
   const int grid = static_cast<int>(std::min<size_t>((n + 255) / 256, 2048));
   moe_combine_kernel<<<grid, 256, 0, st>>>(ws.routed, has_shared ? ws.shared : nullptr, ws.idx,
                                            M, K, H, out);
   return cudaGetLastError();
+}
+
+cudaError_t moe_forward(const MoeConfig& c, const MoeWeights& w, const MoeWorkspace& ws,
+                        const float* x, const int* token_ids, int M, float* out,
+                        cudaStream_t st, const MoeExecOptions& opt) {
+  cudaError_t err = moe_forward_local(c, w, ws, x, token_ids, M, st, opt);
+  if (err != cudaSuccess) return err;
+  return moe_combine(c, ws, M, out, c.shared_kind != kSharedNone && w.sh1 != nullptr, st);
 }
 
 }  // namespace dsv4

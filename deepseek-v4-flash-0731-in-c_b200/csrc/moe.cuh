@@ -17,7 +17,16 @@ struct MoeConfig {
   float route_scale;
   int shared_kind;   // SharedKind
   int hash_vocab;    // rows of tid2eid (0 = not a hash layer)
+  // Expert parallelism: this device computes experts [expert_lo, expert_hi)
+  // and its routed weights hold only those (local index e - expert_lo);
+  // expert_hi == 0 means every expert.
+  int expert_lo = 0, expert_hi = 0;
 };
+
+inline int moe_local_hi(const MoeConfig& c) { return c.expert_hi > 0 ? c.expert_hi : c.n_experts; }
+inline bool moe_is_partial(const MoeConfig& c) {
+  return c.expert_lo != 0 || moe_local_hi(c) != c.n_experts;
+}
 
 // Device pointers of one layer's weights (reference layouts, expert-major).
 struct MoeWeights {
@@ -81,6 +90,17 @@ struct MoeExecOptions {
 cudaError_t moe_forward(const MoeConfig& c, const MoeWeights& w, const MoeWorkspace& ws,
                         const float* x, const int* token_ids, int n_tokens, float* out,
                         cudaStream_t st, const MoeExecOptions& opt = MoeExecOptions());
+
+// The two halves of moe_forward, for expert parallelism: moe_forward_local
+// runs the router, this device's routed experts (ws.routed slots [n][topk][H]
+// of other devices' experts are zero) and the shared expert; after the
+// caller has summed ws.routed over the devices (x + 0 is exact),
+// moe_combine forms out. moe_forward = moe_forward_local + moe_combine.
+cudaError_t moe_forward_local(const MoeConfig& c, const MoeWeights& w, const MoeWorkspace& ws,
+                              const float* x, const int* token_ids, int n_tokens,
+                              cudaStream_t st, const MoeExecOptions& opt = MoeExecOptions());
+cudaError_t moe_combine(const MoeConfig& c, const MoeWorkspace& ws, int n_tokens, float* out,
+                        bool has_shared, cudaStream_t st);
 
 // Router only: idx/wt [n][topk] (ids ascending), same numerics as above.
 cudaError_t moe_route(const MoeConfig& c, const MoeWeights& w, const MoeWorkspace& ws,

@@ -58,6 +58,14 @@ lib.dsv4cuda_moe_forward_noalloc.restype = C.c_int
 lib.dsv4cuda_moe_forward_noalloc.argtypes = [vp, vp, vp, vp, C.c_int, vp, vp]
 lib.dsv4cuda_moe_device_bytes.restype = C.c_size_t
 lib.dsv4cuda_moe_device_bytes.argtypes = [vp]
+lib.dsv4cuda_moe_create_device_ep.restype = C.c_int
+lib.dsv4cuda_moe_create_device_ep.argtypes = [vp, vp, vp, C.c_int, C.c_int, C.c_int]
+lib.dsv4cuda_moe_forward_local.restype = C.c_int
+lib.dsv4cuda_moe_forward_local.argtypes = [vp, vp, vp, C.c_int, vp]
+lib.dsv4cuda_moe_routed_slots.restype = C.c_void_p
+lib.dsv4cuda_moe_routed_slots.argtypes = [vp]
+lib.dsv4cuda_moe_combine.restype = C.c_int
+lib.dsv4cuda_moe_combine.argtypes = [vp, C.c_int, vp, vp]
 
 
 class Dsv4CudaError(RuntimeError):
@@ -80,6 +88,13 @@ def _p(a, t):
 
 def _f32(a):
     return np.ascontiguousarray(a, dtype=np.float32)
+
+
+def _stream(stream):
+    if stream is None:
+        import torch
+        return torch.cuda.current_stream().cuda_stream
+    return stream
 
 
 def _ptrs(arrs, t):
@@ -255,7 +270,10 @@ class MoeLayer:
     (adopted, device=True).
     """
 
-    def __init__(self, layer: dict, max_tokens: int = 8, device: bool = False):
+    def __init__(self, layer: dict, max_tokens: int = 8, device: bool = False,
+                 expert_range=None):
+        """expert_range=(lo, hi): expert-parallel layer (device weights of
+        experts lo..hi-1 only; layer["w1"] etc. hold hi-lo experts)."""
         sh = layer.get("shared")
         kind = SHARED_NONE if sh is None else (SHARED_FP8 if sh["fp8"] else SHARED_FP4)
         tid = layer.get("tid2eid")
@@ -275,10 +293,38 @@ class MoeLayer:
         self._keep = layer
         self.max_tokens = max_tokens
         self.handle = C.c_void_p()
-        fn = lib.dsv4cuda_moe_create_device if device else lib.dsv4cuda_moe_create
-        _check(fn(C.byref(self.handle), C.byref(self.cfg), C.byref(w), max_tokens))
+        if expert_range is not None:
+            if not device:
+                raise ValueError("expert-parallel layers take device weights")
+            _check(lib.dsv4cuda_moe_create_device_ep(C.byref(self.handle), C.byref(self.cfg),
+                                                     C.byref(w), max_tokens,
+                                                     int(expert_range[0]), int(expert_range[1])))
+        else:
+            fn = lib.dsv4cuda_moe_create_device if device else lib.dsv4cuda_moe_create
+            _check(fn(C.byref(self.handle), C.byref(self.cfg), C.byref(w), max_tokens))
         self.hidden = layer["hidden"]
         self.topk = layer["topk"]
+
+    def forward_local(self, x, token_ids=None, stream=None):
+        """Router, this device's experts and the shared expert (EP step 1)."""
+        _check(lib.dsv4cuda_moe_forward_local(self.handle, x.data_ptr(),
+                                              None if token_ids is None else token_ids.data_ptr(),
+                                              x.shape[0], _stream(stream)))
+
+    def routed_slots(self, n_tokens):
+        """torch CUDA float32 view [n][topk][H] of the layer's routed slots."""
+        import torch
+        ptr = lib.dsv4cuda_moe_routed_slots(self.handle)
+
+        class _Iface:
+            __cuda_array_interface__ = {"shape": (n_tokens, self.topk, self.hidden),
+                                        "typestr": "<f4", "data": (ptr, False), "version": 3,
+                                        "strides": None}
+        return torch.as_tensor(_Iface(), device="cuda")
+
+    def combine(self, n_tokens, out, stream=None):
+        """Ordered combine of the (summed) routed slots and the shared expert."""
+        _check(lib.dsv4cuda_moe_combine(self.handle, n_tokens, out.data_ptr(), _stream(stream)))
 
     def close(self):
         if self.handle:
@@ -358,13 +404,6 @@ lib.dsv4cuda_sparse_attn_host.argtypes = [f32p, f32p, f32p, f32p, i32p, C.c_int,
 lib.dsv4cuda_attn_timing_begin.restype = C.c_int
 lib.dsv4cuda_attn_timing_end.restype = C.c_int
 lib.dsv4cuda_attn_timing_end.argtypes = [i32p, f32p]
-
-
-def _stream(stream):
-    if stream is None:
-        import torch
-        return torch.cuda.current_stream().cuda_stream
-    return stream
 
 
 class LatentCache:

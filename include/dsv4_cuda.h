@@ -122,8 +122,10 @@ void dsv4cuda_shutdown(void);
 /* Last error recorded on the calling thread ("" if none). */
 const char *dsv4cuda_last_error(void);
 /* Device-side error flags of the current device (synchronous): bit 0 = a
- * kernel gave up waiting on a shared-memory barrier (bounded wait, the
- * results of that launch are invalid). clear != 0 resets them. */
+ * GEMV kernel gave up waiting on a shared-memory barrier, bit 1 = the
+ * attention kernel did (bounded waits; the results of that launch are
+ * invalid), bit 2 = an attention key index >= kv_rows was skipped.
+ * clear != 0 resets them. */
 int dsv4cuda_device_error(unsigned int *flags, int clear);
 /* 1 (default): a drop-in call that hits a CUDA error exits(1) like the
  * reference's fatal paths; 0: record the error and return. Returns the
@@ -232,6 +234,33 @@ int dsv4cuda_moe_forward_noalloc(const dsv4cuda_moe_config *cfg,
                                  float *out, void *stream);
 /* Device bytes the layer holds (weights it owns + workspace). */
 size_t dsv4cuda_moe_device_bytes(const dsv4cuda_moe_layer *L);
+
+/* ---- Expert parallelism (no counterpart in the reference, which runs every
+ * expert on one host; expert parallel over G GPUs, attention replicated).
+ * Device g creates its layer with the full router (gate_w/bias/tid2eid for
+ * all n_experts) but routed weights only for experts [expert_lo, expert_hi)
+ * (w1..s2 expert-major over those experts). Per step:
+ *   dsv4cuda_moe_forward_local   router (identical on every device), this
+ *                                device's experts, shared expert; the
+ *                                [n][topk][H] fp32 slots of experts held
+ *                                elsewhere are zero;
+ *   sum dsv4cuda_moe_routed_slots over the devices (e.g. ncclAllReduce,
+ *                                ncclFloat32, ncclSum, n*topk*H elements);
+ *                                every slot has one non-zero contributor, so
+ *                                the sum is exact;
+ *   dsv4cuda_moe_combine         the ascending-id ordered combine
+ *                                (src/dsv4/dsv4_model.c:6795-6805), whose
+ *                                accumulator starts at +0 like the
+ *                                reference's, so the output is bit-identical
+ *                                to the single-device layer. */
+int dsv4cuda_moe_create_device_ep(dsv4cuda_moe_layer **out, const dsv4cuda_moe_config *cfg,
+                                  const dsv4cuda_moe_weights *device_weights, int max_tokens,
+                                  int expert_lo, int expert_hi);
+int dsv4cuda_moe_forward_local(dsv4cuda_moe_layer *L, const float *x, const int *token_ids,
+                               int n_tokens, void *stream);
+/* Device pointer of the routed slots [max_tokens][topk][H] fp32. */
+float *dsv4cuda_moe_routed_slots(dsv4cuda_moe_layer *L);
+int dsv4cuda_moe_combine(dsv4cuda_moe_layer *L, int n_tokens, float *out, void *stream);
 
 /* ---------------------------------------------------------------------
  * Latent KV cache and decode attention.

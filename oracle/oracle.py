@@ -235,6 +235,36 @@ class Oracle(_Lib):
                                  C.c_float(scale))
         return o
 
+    def expert_forward_fp4(self, qx, qs, layer, e, weight):
+        """Routed expert e of `layer` for one token (expert_forward_l1/l2)."""
+        hid, mi = layer["hidden"], layer["moe_inter"]
+        ex = _OrcFp4Expert(*[_p(np.ascontiguousarray(layer[n][e]), u8p)
+                             for n in ("w1", "s1", "w3", "s3", "w2", "s2")])
+        out = np.empty(hid, np.float32)
+        self.lib.orc_expert_forward_fp4(_p(out, f32p), _p(_f32(qx), f32p), _p(_f32(qs), f32p),
+                                        C.byref(ex), hid, mi, layer["swiglu_limit"],
+                                        C.c_float(weight))
+        return out
+
+    def shared_forward(self, qx, qs, layer):
+        """The layer's shared expert for one token (zeros when it has none)."""
+        hid, mi = layer["hidden"], layer["moe_inter"]
+        out = np.zeros(hid, np.float32)
+        sh = layer.get("shared")
+        if sh is None:
+            return out
+        ex_t = _OrcFp8Expert if sh["fp8"] else _OrcFp4Expert
+        ex = ex_t(*[_p(np.ascontiguousarray(sh[n]), u8p)
+                    for n in ("w1", "s1", "w3", "s3", "w2", "s2")])
+        if sh["fp8"]:
+            self.lib.orc_shared_forward_fp8(_p(out, f32p), _p(_f32(qx), f32p), _p(_f32(qs), f32p),
+                                            C.byref(ex), hid, mi, layer["swiglu_limit"])
+        else:
+            self.lib.orc_expert_forward_fp4(_p(out, f32p), _p(_f32(qx), f32p), _p(_f32(qs), f32p),
+                                            C.byref(ex), hid, mi, layer["swiglu_limit"],
+                                            C.c_float(1.0))
+        return out
+
     def moe_forward(self, layer, x, token_id=0):
         """layer: dict from make_moe_layer (numpy weights)."""
         out = np.empty(layer["hidden"], np.float32)
