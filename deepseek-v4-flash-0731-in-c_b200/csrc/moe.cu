@@ -36,20 +36,6 @@ __device__ __forceinline__ float sqrt_softplus_f(float z) {
   return sqrtf(log1pf(expf(z)));
 }
 
-struct Cand {
-  float v;
-  int id;
-};
-__device__ __forceinline__ bool better(const Cand& a, const Cand& b) {
-  // strict ">" scan from -inf over ascending ids: larger value first, lower
-  // id on equal values; -inf and NaN never win (src/dsv4/dsv4_model.c:6636).
-  if (a.id < 0) return false;
-  if (b.id < 0) return true;
-  if (a.v > b.v) return true;
-  if (a.v < b.v) return false;
-  return a.id < b.id;
-}
-
 // ------------------------------------------------------------- router ----
 constexpr int kLogitWarps = 4;    // warps per expert in router_logits_kernel
 constexpr int kSelThreads = 256;  // threads per token in router_select_kernel
@@ -186,6 +172,85 @@ __device__ float warp_segment(const uint16_t* g, const float* xr, int H, int c_b
   return carry;
 }
 
+// warp_segment in one pass over memory for segments of at most kSegCache
+// full 256-column chunks: the products' running sums stay in registers while
+// the block exchanges the segment totals, then sabs is formed with the same
+// expressions as warp_segment's second pass (identical t_i, so the same
+// bound holds).
+constexpr int kSegCache = 8;
+struct SegState {
+  float q[kSegCache][8];
+  float part[kSegCache];  // carry + (incl - tot): lane's offset inside the segment
+  float total, pabs;
+};
+
+__device__ __forceinline__ void warp_segment_load(const uint16_t* g, const float* xr, int c_begin, int c_end,
+                                  SegState& st) {
+  const int lane = threadIdx.x & 31;
+  float tot[kSegCache];
+  float pa = 0.0f;
+#pragma unroll
+  for (int j = 0; j < kSegCache; ++j) {
+    float run = 0.0f;
+    if (c_begin + j < c_end) {
+      const int col = (c_begin + j) * 256 + lane * 8;
+      const uint4 gv = __ldg(reinterpret_cast<const uint4*>(g + col));
+      const float4 x0 = __ldg(reinterpret_cast<const float4*>(xr + col));
+      const float4 x1 = __ldg(reinterpret_cast<const float4*>(xr + col + 4));
+      const uint32_t gw[4] = {gv.x, gv.y, gv.z, gv.w};
+      const float xv[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const float w = __uint_as_float((k & 1) ? (gw[k >> 1] & 0xFFFF0000u) : (gw[k >> 1] << 16));
+        const float pr = w * xv[k];
+        run += pr;
+        st.q[j][k] = run;
+        pa += fabsf(pr);
+      }
+    } else {
+#pragma unroll
+      for (int k = 0; k < 8; ++k) st.q[j][k] = 0.0f;
+    }
+    tot[j] = run;
+  }
+  float incl[kSegCache];
+#pragma unroll
+  for (int j = 0; j < kSegCache; ++j) incl[j] = tot[j];
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+#pragma unroll
+    for (int j = 0; j < kSegCache; ++j) {
+      const float v = __shfl_up_sync(0xffffffffu, incl[j], o);
+      if (lane >= o) incl[j] += v;
+    }
+  }
+  float carry = 0.0f;
+#pragma unroll
+  for (int j = 0; j < kSegCache; ++j) {
+    st.part[j] = carry + (incl[j] - tot[j]);
+    if (c_begin + j < c_end) carry += __shfl_sync(0xffffffffu, incl[j], 31);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) pa += __shfl_xor_sync(0xffffffffu, pa, o);
+  st.total = carry;
+  st.pabs = pa;
+}
+
+__device__ __forceinline__ float warp_segment_abs(const SegState& st, int c_begin, int c_end, float offset) {
+  float sa = 0.0f;
+#pragma unroll
+  for (int j = 0; j < kSegCache; ++j) {
+    if (c_begin + j < c_end) {
+      const float base = offset + st.part[j];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) sa += fabsf(base + st.q[j][k]);
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) sa += __shfl_xor_sync(0xffffffffu, sa, o);
+  return sa;
+}
+
 // Launch 1, grid (E, M) x 4 warps: activation quant (spread over all warps)
 // and one router logit per CTA, in fp32, with a rigorous bound on how far
 // the reference's sequential chain can be from it. The row is split over 4
@@ -239,8 +304,16 @@ __global__ void __launch_bounds__(kLogitWarps * 32) router_logits_kernel(const R
   const int nch = (a.H + 255) / 256;
   const int per = (nch + kLogitWarps - 1) / kLogitWarps;
   const int cb = min(nch, warp * per), ce = min(nch, cb + per);
-  float pw = 0.0f;
-  const float tw = warp_segment(g, xr, a.H, cb, ce, 0.0f, nullptr, &pw);
+  const bool cached = (a.H % 256 == 0) && per <= kSegCache;
+  SegState seg;
+  float pw = 0.0f, tw;
+  if (cached) {
+    warp_segment_load(g, xr, cb, ce, seg);
+    tw = seg.total;
+    pw = seg.pabs;
+  } else {
+    tw = warp_segment(g, xr, a.H, cb, ce, 0.0f, nullptr, &pw);
+  }
   if (lane == 0) {
     seg_tot[warp] = tw;
     seg_p[warp] = pw;
@@ -249,7 +322,8 @@ __global__ void __launch_bounds__(kLogitWarps * 32) router_logits_kernel(const R
   float off = 0.0f;
   for (int w = 0; w < warp; ++w) off += seg_tot[w];
   float aw = 0.0f;
-  warp_segment(g, xr, a.H, cb, ce, off, &aw, nullptr);
+  if (cached) aw = warp_segment_abs(seg, cb, ce, off);
+  else warp_segment(g, xr, a.H, cb, ce, off, &aw, nullptr);
   if (lane == 0) seg_abs[warp] = aw;
   __syncthreads();
   if (threadIdx.x == 0) {
@@ -269,44 +343,75 @@ __global__ void __launch_bounds__(kLogitWarps * 32) router_logits_kernel(const R
   }
 }
 
-__device__ __forceinline__ Cand warp_best(Cand c) {
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    Cand n;
-    n.v = __shfl_xor_sync(0xffffffffu, c.v, o);
-    n.id = __shfl_xor_sync(0xffffffffu, c.id, o);
-    if (better(n, c)) c = n;
-  }
-  return c;
+// Orderable key of a selection value: a larger value gives a larger key;
+// -inf and NaN give 0 and are never selected (the reference's strict ">"
+// scan starts from -inf, src/dsv4/dsv4_model.c:6636); -0 compares equal to
+// +0 as it does in the reference.
+__device__ __forceinline__ uint32_t sel_key(float v) {
+  if (!(v > -INFINITY)) return 0u;
+  if (v == 0.0f) v = 0.0f;
+  const uint32_t b = __float_as_uint(v);
+  return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
 }
 
-// Block-wide top-k by the reference rule; order[] in selection order.
-__device__ void block_topk(const float* val, unsigned char* used, int E, int k, int* order,
-                           Cand* red) {
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int nwarp = blockDim.x >> 5;
-  for (int e = threadIdx.x; e < E; e += blockDim.x) used[e] = 0;
-  __syncthreads();
-  for (int j = 0; j < k; ++j) {
-    Cand c{0.f, -1};
-    for (int e = threadIdx.x; e < E; e += blockDim.x) {
-      const float v = val[e];
-      if (used[e] || !(v > -INFINITY)) continue;  // -inf and NaN never win
-      const Cand n{v, e};
-      if (better(n, c)) c = n;
+// Top-k by the reference rule (largest value, lowest id among equal values),
+// order[] in selection order, used[] marks the picks. Warp 0 does the work
+// with warp reductions (no block barrier per pick); every thread calls it.
+__device__ void warp_topk(const float* val, unsigned char* used, int E, int k, int* order) {
+  if (threadIdx.x < 32) {
+    const int lane = threadIdx.x;
+    for (int e = lane; e < E; e += 32) used[e] = 0;
+    __syncwarp();
+    for (int j = 0; j < k; ++j) {
+      uint32_t bk = 0u;
+      int bid = 0x7FFFFFFF;
+      for (int e = lane; e < E; e += 32) {  // ascending ids: ">" keeps the lower id
+        if (used[e]) continue;
+        const uint32_t key = sel_key(val[e]);
+        if (key > bk) { bk = key; bid = e; }
+      }
+      const uint32_t mk = __reduce_max_sync(0xffffffffu, bk);
+      const int id = static_cast<int>(__reduce_min_sync(
+          0xffffffffu, static_cast<unsigned>((bk == mk) ? bid : 0x7FFFFFFF)));
+      const int pick = mk == 0u ? -1 : id;
+      if (lane == 0) {
+        order[j] = pick;
+        if (pick >= 0) used[pick] = 1;
+      }
+      __syncwarp();
     }
-    c = warp_best(c);
-    if (lane == 0) red[warp] = c;
-    __syncthreads();
-    if (threadIdx.x == 0) {
-      Cand b = red[0];
-      for (int w = 1; w < nwarp; ++w)
-        if (better(red[w], b)) b = red[w];
-      order[j] = b.id;
-      if (b.id >= 0) used[b.id] = 1;
-    }
-    __syncthreads();
   }
+  __syncthreads();
+}
+
+// Exclusive prefix sum of one int per thread over the block (blockDim.x a
+// multiple of 32, <= 1024); *total receives the sum. Uses wsum[32].
+__device__ int block_excl_scan(int v, int* wsum, int* total) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  int incl = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int t = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += t;
+  }
+  if (lane == 31) wsum[warp] = incl;
+  __syncthreads();
+  if (warp == 0) {
+    int w = lane < nw ? wsum[lane] : 0;
+    int wi = w;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int t = __shfl_up_sync(0xffffffffu, wi, o);
+      if (lane >= o) wi += t;
+    }
+    if (lane < nw) wsum[lane] = wi - w;  // exclusive warp offsets
+    if (lane == 31) wsum[31] = wi;       // nw <= 32: lane 31 holds the block total
+  }
+  __syncthreads();
+  const int r = wsum[warp] + incl - v;
+  *total = wsum[31];
+  __syncthreads();
+  return r;
 }
 
 // Token->expert permutation (moe_forward_batch grouping,
@@ -325,7 +430,17 @@ __device__ void block_plan(const RouterArgs& a, int* cnt, int* ids) {
     cnt[e] = (n + kItemTok - 1) / kItemTok;
   }
   __syncthreads();
-  if (threadIdx.x < 32) {
+  if (E <= static_cast<int>(blockDim.x)) {
+    __shared__ int wsum[32];
+    int total = 0;
+    const int v = static_cast<int>(threadIdx.x) < E ? cnt[threadIdx.x] : 0;
+    const int off = block_excl_scan(v, wsum, &total);
+    if (static_cast<int>(threadIdx.x) < E) cnt[threadIdx.x] = off;
+    if (threadIdx.x == 0) {
+      a.counters[0] = total;
+      a.counters[3] = (a.M + kItemTok - 1) / kItemTok;
+    }
+  } else if (threadIdx.x < 32) {
     // exclusive scan of cnt[0..E) by one warp: 32-element tiles with a carry
     int carry = 0;
     for (int b0 = 0; b0 < E; b0 += 32) {
@@ -440,7 +555,6 @@ __host__ __device__ inline size_t select_smem_bytes(int H, int E, int R, SelectS
 // src/dsv4/dsv4_ops.c:473-545); the last CTA to finish builds the plan.
 __global__ void __launch_bounds__(kSelThreads) router_select_kernel(const RouterArgs a) {
   extern __shared__ __align__(16) unsigned char ssm[];
-  __shared__ Cand red[kSelThreads / 32];
   __shared__ double rlo[kSelThreads / 32], rhi[kSelThreads / 32];
   __shared__ int order[kMaxTopk];
   __shared__ int is_last, n_cand;
@@ -476,7 +590,7 @@ __global__ void __launch_bounds__(kSelThreads) router_select_kernel(const Router
     }
     __syncthreads();
   } else {
-    block_topk(sm.choice, sm.used, E, a.topk, order, red);
+    warp_topk(sm.choice, sm.used, E, a.topk, order);
     double mlo = INFINITY, mhi = -INFINITY;
     int nan_seen = 0;
     for (int e = threadIdx.x; e < E; e += blockDim.x) {
@@ -527,48 +641,51 @@ __global__ void __launch_bounds__(kSelThreads) router_select_kernel(const Router
         }
         __syncthreads();
       }
-      block_topk(sm.choice, sm.used, E, a.topk, order, red);
+      warp_topk(sm.choice, sm.used, E, a.topk, order);
       if (threadIdx.x == 0) atomicAdd(&a.counters[2], 1);
     }
   }
-  if (threadIdx.x == 0) {
-    const int K = a.topk;
-    int id[kMaxTopk];
-    float w[kMaxTopk];
+  if (threadIdx.x < 32) {
+    // warp 0, lane k = k-th pick: weights from the scores summed in pick
+    // order (src/dsv4/dsv4_model.c:6651-6658; public twin
+    // src/dsv4/dsv4_ops.c:528-531), then the ascending-id exchange sort of
+    // :6669-6676 restated as a stable rank (equal ids keep their order)
+    const int K = a.topk, k = lane;
+    const int id = k < K ? order[k] : 0x7FFFFFFF;
+    const float sc = (k < K && id >= 0) ? sm.score[id] : 0.0f;
     float sum = 0.0f;
-    for (int k = 0; k < K; ++k) {
-      id[k] = order[k];
-      sum += id[k] >= 0 ? sm.score[id[k]] : 0.0f;
-    }
+    for (int j = 0; j < K; ++j) sum += __shfl_sync(0xffffffffu, sc, j);
+    float w;
     if (a.public_router) {
-      const float inv = sum > 0.0f ? 1.0f / sum : 0.0f;        // dsv4_ops.c:528-531
-      for (int k = 0; k < K; ++k) w[k] = (id[k] >= 0 ? sm.score[id[k]] : 0.f) * inv * a.route_scale;
-    } else if (sum > 0.0f) {
-      const float rs = a.route_scale / sum;                   // dsv4_model.c:6651-6658
-      for (int k = 0; k < K; ++k) w[k] = (id[k] >= 0 ? sm.score[id[k]] : 0.f) * rs;
+      const float inv = sum > 0.0f ? 1.0f / sum : 0.0f;
+      w = sc * inv * a.route_scale;
     } else {
-      for (int k = 0; k < K; ++k) w[k] = 0.0f;
+      w = sum > 0.0f ? sc * (a.route_scale / sum) : 0.0f;
     }
-    for (int i = 0; i < K; ++i)                               // exchange sort, :6669-6676
-      for (int j = i + 1; j < K; ++j)
-        if (id[j] < id[i]) {
-          const int ti = id[i]; id[i] = id[j]; id[j] = ti;
-          const float tw = w[i]; w[i] = w[j]; w[j] = tw;
-        }
-    for (int k = 0; k < K; ++k) {
-      a.idx[static_cast<size_t>(t) * K + k] = id[k];
-      a.wt[static_cast<size_t>(t) * K + k] = w[k];
+    int rank = 0;
+    for (int j = 0; j < K; ++j) {
+      const int o = __shfl_sync(0xffffffffu, id, j);
+      rank += (o < id) || (o == id && j < k);
+    }
+    if (k < K) {
+      a.idx[static_cast<size_t>(t) * K + rank] = id;
+      a.wt[static_cast<size_t>(t) * K + rank] = w;
     }
   }
   if (!a.items_gu) return;
-  __threadfence();
-  __syncthreads();
-  if (threadIdx.x == 0) is_last = atomicAdd(&a.counters[1], 1) == static_cast<int>(gridDim.x) - 1;
-  __syncthreads();
-  if (!is_last) return;
-  __threadfence();
+  if (gridDim.x == 1) {
+    // one token: this CTA wrote every route itself
+    __syncthreads();
+  } else {
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) is_last = atomicAdd(&a.counters[1], 1) == static_cast<int>(gridDim.x) - 1;
+    __syncthreads();
+    if (!is_last) return;
+    __threadfence();
+  }
   block_plan(a, sm.cnt, sm.ids);
-  if (threadIdx.x == 0) a.counters[1] = 0;  // ticket ready for the next launch
+  if (threadIdx.x == 0 && gridDim.x > 1) a.counters[1] = 0;  // ticket ready for the next launch
 }
 
 // out[t] = bf16( sum_k routed[t*topk+k] (ascending id order) + shared[t] )
