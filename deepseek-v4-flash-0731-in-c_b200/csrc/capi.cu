@@ -21,6 +21,8 @@
 #include "gemv.cuh"
 #include "moe.cuh"
 #include "attn.cuh"
+#include "sample.cuh"
+#include "snapshot.cuh"
 #include "../../include/dsv4_cuda.h"
 
 #define DSV4_API extern "C" __attribute__((visibility("default")))
@@ -1165,4 +1167,311 @@ DSV4_API void dsv4cuda_sparse_attn_host(float* o, const float* q, const float* k
   }
   STAGE_CHECK(cudaMemcpyAsync(o, dout, qb, cudaMemcpyDeviceToHost, st), "copy o");
   STAGE_CHECK(cudaStreamSynchronize(st), "sync");
+}
+
+// ============================================== speculative acceptance ==
+
+DSV4_API uint64_t dsv4cuda_rng_next(uint64_t* state) { return dsv4::rng_next_host(state); }
+
+DSV4_API int dsv4cuda_argmax_logits(const float* logits, int vocab) {
+  return vocab > 0 ? dsv4::argmax_host(logits, vocab) : 0;
+}
+
+DSV4_API int dsv4cuda_sample_top_p(const float* logits, int vocab, double temperature,
+                                   double top_p, uint64_t* rng_state) {
+  if (!logits || !rng_state || vocab <= 0) return -1;
+  return dsv4::sample_top_p_host(logits, vocab, temperature, top_p, rng_state);
+}
+
+DSV4_API int dsv4cuda_accept_chain(const int* proposal, int proposed, const float* logits,
+                                   int vocab, double temperature, double top_p,
+                                   uint64_t* rng_state, int eos_id, int* tokens, int* n_commit,
+                                   int* n_accepted, int* n_samples) {
+  if (proposed < 0 || vocab <= 0 || !logits || !tokens || !n_commit || !n_accepted ||
+      !n_samples || (proposed > 0 && !proposal) || (temperature != 0.0 && !rng_state)) {
+    record_error("dsv4cuda_accept_chain: bad arguments");
+    return -1;
+  }
+  return dsv4::accept_chain_host(proposal, proposed, logits, vocab, temperature, top_p,
+                                 rng_state, eos_id, tokens, n_commit, n_accepted, n_samples);
+}
+
+DSV4_API int dsv4cuda_argmax_rows(const float* logits, int rows, int vocab, int* out,
+                                  void* stream) {
+  if (!logits || !out || rows < 0 || vocab <= 0) {
+    record_error("dsv4cuda_argmax_rows: bad arguments");
+    return -1;
+  }
+  cudaError_t e = dsv4::argmax_rows(logits, rows, vocab, out, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) { record_error("argmax_rows: %s", cudaGetErrorString(e)); return -1; }
+  return 0;
+}
+
+DSV4_API int dsv4cuda_sample_rows(const float* logits, int rows, int vocab, double temperature,
+                                  const double* uniforms, int* out, void* stream) {
+  if (!logits || !out || !uniforms || rows < 0 || vocab <= 0 || !(temperature > 0.0)) {
+    record_error("dsv4cuda_sample_rows: bad arguments");
+    return -1;
+  }
+  cudaError_t e = dsv4::sample_rows(logits, rows, vocab, temperature, uniforms, out,
+                                    static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) { record_error("sample_rows: %s", cudaGetErrorString(e)); return -1; }
+  return 0;
+}
+
+DSV4_API int dsv4cuda_accept_device(const int* proposal, int proposed, const float* logits,
+                                    int vocab, double temperature, const double* uniforms,
+                                    int eos_id, int* result, void* stream) {
+  if (!logits || !result || proposed < 0 || vocab <= 0 || (proposed > 0 && !proposal) ||
+      (temperature != 0.0 && (!uniforms || !(temperature > 0.0)))) {
+    record_error("dsv4cuda_accept_device: bad arguments");
+    return -1;
+  }
+  cudaError_t e = dsv4::accept_device(proposal, proposed, logits, vocab, temperature, uniforms,
+                                      eos_id, result, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) { record_error("accept_device: %s", cudaGetErrorString(e)); return -1; }
+  return 0;
+}
+
+// ==================================================== KV-ring snapshot ==
+//
+// dsv4_context_snapshot_take / _restore / _commit_prefix
+// (src/dsv4/dsv4_model.c:2842-3056) for the latent caches and the state
+// buffers a caller registers (device memory, async on the given stream).
+
+struct dsv4cuda_snapshot {
+  int max_positions = 0;
+  std::vector<dsv4::Fp8KvCache> caches;
+  std::vector<long long> ring_base;   // first cache row of each ring
+  std::vector<int> windows;
+  std::vector<float*> states;
+  std::vector<size_t> state_elems;
+  void* mem = nullptr;
+  std::vector<uint8_t*> pre_rows;     // per cache [max_positions][row bytes]
+  std::vector<float*> pre_state;      // per state [elems]
+  std::vector<float*> post_state;     // per state [max_positions][elems]
+  std::vector<char> captured;         // per step
+  int start = 0, n = 0;
+  bool ready = false;
+};
+
+namespace {
+
+dsv4::SnapRows ring_rows(const dsv4cuda_snapshot* s, size_t c, int first, int last) {
+  dsv4::SnapRows r{};
+  r.n = 0;
+  for (int p = first; p < last; ++p)
+    r.row[r.n++] = s->ring_base[c] + (s->start + p) % s->windows[c];
+  return r;
+}
+
+}  // namespace
+
+DSV4_API int dsv4cuda_snapshot_create(dsv4cuda_snapshot** out, int max_positions, int n_caches,
+                                      const dsv4cuda_kv_cache* caches,
+                                      const long long* ring_base, const int* windows,
+                                      int n_states, float* const* states,
+                                      const size_t* state_elems) {
+  if (!out || max_positions <= 0 || max_positions > dsv4::kMaxSnapPositions || n_caches < 0 ||
+      n_states < 0 || (n_caches > 0 && (!caches || !windows)) ||
+      (n_states > 0 && (!states || !state_elems))) {
+    record_error("dsv4cuda_snapshot_create: bad arguments (max_positions <= %d)",
+                 dsv4::kMaxSnapPositions);
+    return -1;
+  }
+  *out = nullptr;
+  dsv4cuda_snapshot* s = new dsv4cuda_snapshot();
+  s->max_positions = max_positions;
+  size_t bytes = 0;
+  for (int c = 0; c < n_caches; ++c) {
+    if (!cache_ok(&caches[c]) || windows[c] < max_positions) {
+      record_error("dsv4cuda_snapshot_create: cache %d invalid or window < max_positions", c);
+      delete s;
+      return -1;
+    }
+    s->caches.push_back(to_cache(&caches[c]));
+    s->ring_base.push_back(ring_base ? ring_base[c] : 0);
+    s->windows.push_back(windows[c]);
+    bytes += al(static_cast<size_t>(max_positions) * dsv4::kv_row_bytes(s->caches.back()));
+  }
+  for (int i = 0; i < n_states; ++i) {
+    s->states.push_back(states[i]);
+    s->state_elems.push_back(state_elems[i]);
+    bytes += al(state_elems[i] * sizeof(float)) * (1 + static_cast<size_t>(max_positions));
+  }
+  if (bytes && cudaMalloc(&s->mem, bytes) != cudaSuccess) {
+    record_error("dsv4cuda_snapshot_create: cannot allocate %zu bytes", bytes);
+    delete s;
+    return -1;
+  }
+  char* p = static_cast<char*>(s->mem);
+  for (size_t c = 0; c < s->caches.size(); ++c) {
+    s->pre_rows.push_back(reinterpret_cast<uint8_t*>(p));
+    p += al(static_cast<size_t>(max_positions) * dsv4::kv_row_bytes(s->caches[c]));
+  }
+  for (size_t i = 0; i < s->states.size(); ++i) {
+    s->pre_state.push_back(reinterpret_cast<float*>(p));
+    p += al(s->state_elems[i] * sizeof(float));
+    s->post_state.push_back(reinterpret_cast<float*>(p));
+    p += al(s->state_elems[i] * sizeof(float)) * max_positions;
+  }
+  s->captured.assign(max_positions, 0);
+  *out = s;
+  return 0;
+}
+
+DSV4_API void dsv4cuda_snapshot_destroy(dsv4cuda_snapshot* s) {
+  if (!s) return;
+  if (s->mem) cudaFree(s->mem);
+  delete s;
+}
+
+DSV4_API int dsv4cuda_snapshot_take(dsv4cuda_snapshot* s, int start_position, int n_positions,
+                                    void* stream) {
+  if (!s || start_position < 0 || n_positions <= 0 || n_positions > s->max_positions) {
+    record_error("dsv4cuda_snapshot_take: bad arguments");
+    return -1;
+  }
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  s->start = start_position;
+  s->n = n_positions;
+  for (size_t c = 0; c < s->caches.size(); ++c) {
+    cudaError_t e = dsv4::kv_rows_save(s->caches[c], ring_rows(s, c, 0, n_positions),
+                                       s->pre_rows[c], st);
+    if (e != cudaSuccess) { record_error("snapshot take: %s", cudaGetErrorString(e)); return -1; }
+  }
+  for (size_t i = 0; i < s->states.size(); ++i) {
+    cudaError_t e = cudaMemcpyAsync(s->pre_state[i], s->states[i], s->state_elems[i] * sizeof(float),
+                                    cudaMemcpyDeviceToDevice, st);
+    if (e != cudaSuccess) { record_error("snapshot take: %s", cudaGetErrorString(e)); return -1; }
+  }
+  std::fill(s->captured.begin(), s->captured.end(), 0);
+  s->ready = true;
+  return 0;
+}
+
+DSV4_API int dsv4cuda_snapshot_capture_state(dsv4cuda_snapshot* s, int step, void* stream) {
+  if (!s || !s->ready || step < 0 || step >= s->n) {
+    record_error("dsv4cuda_snapshot_capture_state: bad arguments");
+    return -1;
+  }
+  for (size_t i = 0; i < s->states.size(); ++i) {
+    cudaError_t e = cudaMemcpyAsync(s->post_state[i] + static_cast<size_t>(step) * s->state_elems[i],
+                                    s->states[i], s->state_elems[i] * sizeof(float),
+                                    cudaMemcpyDeviceToDevice, static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) { record_error("capture: %s", cudaGetErrorString(e)); return -1; }
+  }
+  s->captured[step] = 1;
+  return 0;
+}
+
+DSV4_API int dsv4cuda_snapshot_commit_prefix(dsv4cuda_snapshot* s, int n_positions,
+                                             void* stream) {
+  if (!s || !s->ready || n_positions <= 0 || n_positions > s->n ||
+      (!s->states.empty() && !s->captured[n_positions - 1])) {
+    record_error("dsv4cuda_snapshot_commit_prefix: bad arguments or state of step %d not captured",
+                 n_positions - 1);
+    return -1;
+  }
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  for (size_t c = 0; c < s->caches.size(); ++c) {
+    const int rb = dsv4::kv_row_bytes(s->caches[c]);
+    cudaError_t e = dsv4::kv_rows_load(s->caches[c], ring_rows(s, c, n_positions, s->n),
+                                       s->pre_rows[c] + static_cast<size_t>(n_positions) * rb, st);
+    if (e != cudaSuccess) { record_error("commit: %s", cudaGetErrorString(e)); return -1; }
+  }
+  for (size_t i = 0; i < s->states.size(); ++i) {
+    cudaError_t e = cudaMemcpyAsync(
+        s->states[i], s->post_state[i] + static_cast<size_t>(n_positions - 1) * s->state_elems[i],
+        s->state_elems[i] * sizeof(float), cudaMemcpyDeviceToDevice, st);
+    if (e != cudaSuccess) { record_error("commit: %s", cudaGetErrorString(e)); return -1; }
+  }
+  s->ready = false;
+  return 0;
+}
+
+DSV4_API int dsv4cuda_snapshot_restore(dsv4cuda_snapshot* s, void* stream) {
+  if (!s || !s->ready) { record_error("dsv4cuda_snapshot_restore: no snapshot taken"); return -1; }
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  for (size_t c = 0; c < s->caches.size(); ++c) {
+    cudaError_t e = dsv4::kv_rows_load(s->caches[c], ring_rows(s, c, 0, s->n), s->pre_rows[c], st);
+    if (e != cudaSuccess) { record_error("restore: %s", cudaGetErrorString(e)); return -1; }
+  }
+  for (size_t i = 0; i < s->states.size(); ++i) {
+    cudaError_t e = cudaMemcpyAsync(s->states[i], s->pre_state[i], s->state_elems[i] * sizeof(float),
+                                    cudaMemcpyDeviceToDevice, st);
+    if (e != cudaSuccess) { record_error("restore: %s", cudaGetErrorString(e)); return -1; }
+  }
+  s->ready = false;
+  return 0;
+}
+
+// ======================================================== tree verify ==
+//
+// A verify step over a draft tree (a chain is the tree with parents
+// -1, 0, 1, ...). Node j sits at position committed + depth(j); it attends
+// to the window the reference's window_topk (src/dsv4/dsv4_model.c:5073)
+// gives that position, except that positions >= committed are the node's
+// own ancestors (and itself), whose latents live in scratch rows
+// scratch_row + ancestor (siblings share a position, so they cannot share a
+// ring slot). After acceptance, dsv4cuda_kv_copy_rows moves the accepted
+// path's scratch rows into their ring slots.
+
+DSV4_API int dsv4cuda_tree_attn_indices(const int* parents, int n_nodes, int committed,
+                                        int window, long long ring_base, long long scratch_row,
+                                        int* idx, int row_len) {
+  if (!parents || !idx || n_nodes <= 0 || n_nodes > dsv4::kMaxSnapPositions || committed < 0 ||
+      window <= 0 || row_len <= 0) {
+    record_error("dsv4cuda_tree_attn_indices: bad arguments");
+    return -1;
+  }
+  std::vector<int> depth(n_nodes, 0);
+  for (int j = 0; j < n_nodes; ++j) {
+    const int p = parents[j];
+    if (p >= j || p < -1) {
+      record_error("dsv4cuda_tree_attn_indices: parents[%d] = %d (parents must precede children)", j, p);
+      return -1;
+    }
+    depth[j] = p < 0 ? 0 : depth[p] + 1;
+  }
+  int longest = 0;
+  for (int j = 0; j < n_nodes; ++j) {
+    const int pos = committed + depth[j];
+    const int first = std::max(0, pos - window + 1);  // oldest position in the window
+    int* out = idx + static_cast<size_t>(j) * row_len;
+    int n = 0;
+    for (int q = first; q < committed; ++q) {
+      if (n >= row_len) { record_error("row_len %d too small", row_len); return -1; }
+      out[n++] = static_cast<int>(ring_base + q % window);
+    }
+    // ancestors root..j (positions committed..pos)
+    int chain[dsv4::kMaxSnapPositions];
+    int c = 0;
+    for (int a = j; a >= 0; a = parents[a]) chain[c++] = a;
+    for (int i = c - 1; i >= 0; --i) {
+      if (committed + depth[chain[i]] < first) continue;  // fell out of the window
+      if (n >= row_len) { record_error("row_len %d too small", row_len); return -1; }
+      out[n++] = static_cast<int>(scratch_row + chain[i]);
+    }
+    longest = std::max(longest, n);
+    for (int i = n; i < row_len; ++i) out[i] = -1;
+  }
+  return longest;
+}
+
+DSV4_API int dsv4cuda_kv_copy_rows(const dsv4cuda_kv_cache* cache, const long long* src_rows,
+                                   const long long* dst_rows, int n, void* stream) {
+  if (!cache_ok(cache) || n < 0 || n > dsv4::kMaxSnapPositions || (n > 0 && (!src_rows || !dst_rows))) {
+    record_error("dsv4cuda_kv_copy_rows: bad arguments (n <= %d)", dsv4::kMaxSnapPositions);
+    return -1;
+  }
+  dsv4::SnapRows s{}, d{};
+  s.n = d.n = n;
+  for (int i = 0; i < n; ++i) {
+    s.row[i] = src_rows[i];
+    d.row[i] = dst_rows[i];
+  }
+  cudaError_t e = dsv4::kv_rows_move(to_cache(cache), s, d, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) { record_error("kv_copy_rows: %s", cudaGetErrorString(e)); return -1; }
+  return 0;
 }

@@ -385,7 +385,8 @@ __device__ void warp_topk(const float* val, unsigned char* used, int E, int k, i
 }
 
 // Exclusive prefix sum of one int per thread over the block (blockDim.x a
-// multiple of 32, <= 1024); *total receives the sum. Uses wsum[32].
+// multiple of 32, <= 1024); *total receives the sum. Uses wsum[33]
+// (wsum[32] holds the total).
 __device__ int block_excl_scan(int v, int* wsum, int* total) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
   int incl = v;
@@ -405,11 +406,11 @@ __device__ int block_excl_scan(int v, int* wsum, int* total) {
       if (lane >= o) wi += t;
     }
     if (lane < nw) wsum[lane] = wi - w;  // exclusive warp offsets
-    if (lane == 31) wsum[31] = wi;       // nw <= 32: lane 31 holds the block total
+    if (lane == 31) wsum[32] = wi;       // lane 31 holds the block total
   }
   __syncthreads();
   const int r = wsum[warp] + incl - v;
-  *total = wsum[31];
+  *total = wsum[32];
   __syncthreads();
   return r;
 }
@@ -431,7 +432,7 @@ __device__ void block_plan(const RouterArgs& a, int* cnt, int* ids) {
   }
   __syncthreads();
   if (E <= static_cast<int>(blockDim.x)) {
-    __shared__ int wsum[32];
+    __shared__ int wsum[33];
     int total = 0;
     const int v = static_cast<int>(threadIdx.x) < E ? cnt[threadIdx.x] : 0;
     const int off = block_excl_scan(v, wsum, &total);

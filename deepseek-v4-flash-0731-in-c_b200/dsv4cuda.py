@@ -478,3 +478,165 @@ def attn_timing_end():
     ms = C.c_float(0)
     _check(lib.dsv4cuda_attn_timing_end(C.byref(n), C.byref(ms)))
     return n.value, ms.value
+
+
+# ------------------------------------------------- speculative acceptance --
+u64p = C.POINTER(C.c_uint64)
+lib.dsv4cuda_rng_next.restype = C.c_uint64
+lib.dsv4cuda_rng_next.argtypes = [u64p]
+lib.dsv4cuda_argmax_logits.restype = C.c_int
+lib.dsv4cuda_argmax_logits.argtypes = [f32p, C.c_int]
+lib.dsv4cuda_sample_top_p.restype = C.c_int
+lib.dsv4cuda_sample_top_p.argtypes = [f32p, C.c_int, C.c_double, C.c_double, u64p]
+lib.dsv4cuda_accept_chain.restype = C.c_int
+lib.dsv4cuda_accept_chain.argtypes = [i32p, C.c_int, f32p, C.c_int, C.c_double, C.c_double,
+                                      u64p, C.c_int, i32p, i32p, i32p, i32p]
+lib.dsv4cuda_argmax_rows.restype = C.c_int
+lib.dsv4cuda_argmax_rows.argtypes = [vp, C.c_int, C.c_int, vp, vp]
+lib.dsv4cuda_sample_rows.restype = C.c_int
+lib.dsv4cuda_sample_rows.argtypes = [vp, C.c_int, C.c_int, C.c_double, vp, vp, vp]
+lib.dsv4cuda_accept_device.restype = C.c_int
+lib.dsv4cuda_accept_device.argtypes = [vp, C.c_int, vp, C.c_int, C.c_double, vp, C.c_int, vp, vp]
+
+
+def rng_next(state):
+    st = C.c_uint64(state)
+    v = lib.dsv4cuda_rng_next(C.byref(st))
+    return v, st.value
+
+
+def uniforms(state, n):
+    """n 53-bit uniforms in the reference's draw order; returns (array, state)."""
+    out = np.empty(n, np.float64)
+    for i in range(n):
+        v, state = rng_next(state)
+        out[i] = (v >> 11) * (1.0 / 9007199254740992.0)
+    return out, state
+
+
+def argmax_logits(logits):
+    logits = _f32(logits)
+    return lib.dsv4cuda_argmax_logits(_p(logits, f32p), logits.size)
+
+
+def sample_top_p(logits, temperature, top_p, state):
+    logits = _f32(logits)
+    st = C.c_uint64(state)
+    tok = lib.dsv4cuda_sample_top_p(_p(logits, f32p), logits.size, temperature, top_p,
+                                    C.byref(st))
+    return tok, st.value
+
+
+def accept_chain(proposal, logits, temperature, top_p, state, eos_id=1):
+    proposal = np.ascontiguousarray(proposal, dtype=np.int32)
+    logits = _f32(logits)
+    toks = np.empty(proposal.size + 1, np.int32)
+    st = C.c_uint64(state)
+    nc, na, ns = C.c_int(), C.c_int(), C.c_int()
+    n = _check(lib.dsv4cuda_accept_chain(_p(proposal, i32p), proposal.size, _p(logits, f32p),
+                                         logits.shape[-1], temperature, top_p, C.byref(st),
+                                         eos_id, _p(toks, i32p), C.byref(nc), C.byref(na),
+                                         C.byref(ns)))
+    return dict(tokens=toks[:n].copy(), n_commit=nc.value, n_accepted=na.value,
+                n_samples=ns.value, state=st.value)
+
+
+def argmax_rows(logits, out, stream=None):
+    """logits: torch CUDA float32 [rows][V]; out: torch CUDA int32 [rows]."""
+    _check(lib.dsv4cuda_argmax_rows(logits.data_ptr(), logits.shape[0], logits.shape[1],
+                                    out.data_ptr(), _stream(stream)))
+
+
+def sample_rows(logits, temperature, uniforms_dev, out, stream=None):
+    _check(lib.dsv4cuda_sample_rows(logits.data_ptr(), logits.shape[0], logits.shape[1],
+                                    temperature, uniforms_dev.data_ptr(), out.data_ptr(),
+                                    _stream(stream)))
+
+
+def accept_device(proposal_dev, logits, temperature, uniforms_dev, result, eos_id=1,
+                  stream=None):
+    """proposal_dev int32 [P]; logits [(P+1)][V]; result int32 [2P + 6]."""
+    _check(lib.dsv4cuda_accept_device(
+        proposal_dev.data_ptr(), proposal_dev.numel(), logits.data_ptr(), logits.shape[1],
+        temperature, None if uniforms_dev is None else uniforms_dev.data_ptr(), eos_id,
+        result.data_ptr(), _stream(stream)))
+
+
+# ---------------------------------------------------- KV-ring snapshot --
+lib.dsv4cuda_snapshot_create.restype = C.c_int
+lib.dsv4cuda_snapshot_create.argtypes = [vp, C.c_int, C.c_int, vp, vp, vp, C.c_int, vp, vp]
+for _n in ("take",):
+    getattr(lib, "dsv4cuda_snapshot_" + _n).restype = C.c_int
+lib.dsv4cuda_snapshot_take.argtypes = [vp, C.c_int, C.c_int, vp]
+lib.dsv4cuda_snapshot_capture_state.restype = C.c_int
+lib.dsv4cuda_snapshot_capture_state.argtypes = [vp, C.c_int, vp]
+lib.dsv4cuda_snapshot_commit_prefix.restype = C.c_int
+lib.dsv4cuda_snapshot_commit_prefix.argtypes = [vp, C.c_int, vp]
+lib.dsv4cuda_snapshot_restore.restype = C.c_int
+lib.dsv4cuda_snapshot_restore.argtypes = [vp, vp]
+lib.dsv4cuda_snapshot_destroy.argtypes = [vp]
+
+
+class Snapshot:
+    """Speculative transaction over LatentCache rings and float32 CUDA state
+    tensors (dsv4cuda_snapshot_*)."""
+
+    def __init__(self, caches, windows, ring_base=None, states=(), max_positions=16):
+        nc = len(caches)
+        arr = (KvCache * max(nc, 1))(*[c.struct for c in caches])
+        win = (C.c_int * max(nc, 1))(*windows)
+        base = None if ring_base is None else (C.c_longlong * max(nc, 1))(*ring_base)
+        ns = len(states)
+        sp = (C.c_void_p * max(ns, 1))(*[t.data_ptr() for t in states])
+        se = (C.c_size_t * max(ns, 1))(*[t.numel() for t in states])
+        self._keep = (caches, states)
+        self.handle = C.c_void_p()
+        _check(lib.dsv4cuda_snapshot_create(C.byref(self.handle), max_positions, nc, arr, base,
+                                            win, ns, sp, se))
+
+    def take(self, start, n, stream=None):
+        _check(lib.dsv4cuda_snapshot_take(self.handle, start, n, _stream(stream)))
+
+    def capture_state(self, step, stream=None):
+        _check(lib.dsv4cuda_snapshot_capture_state(self.handle, step, _stream(stream)))
+
+    def commit_prefix(self, k, stream=None):
+        _check(lib.dsv4cuda_snapshot_commit_prefix(self.handle, k, _stream(stream)))
+
+    def restore(self, stream=None):
+        _check(lib.dsv4cuda_snapshot_restore(self.handle, _stream(stream)))
+
+    def close(self):
+        if self.handle:
+            lib.dsv4cuda_snapshot_destroy(self.handle)
+            self.handle = C.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+# ------------------------------------------------------------ tree verify --
+lib.dsv4cuda_tree_attn_indices.restype = C.c_int
+lib.dsv4cuda_tree_attn_indices.argtypes = [i32p, C.c_int, C.c_int, C.c_int, C.c_longlong,
+                                           C.c_longlong, i32p, C.c_int]
+lib.dsv4cuda_kv_copy_rows.restype = C.c_int
+lib.dsv4cuda_kv_copy_rows.argtypes = [vp, vp, vp, C.c_int, vp]
+
+
+def tree_attn_indices(parents, committed, window, ring_base, scratch_row, row_len):
+    """idx [n_nodes][row_len] (-1 padded) for a verify over a draft tree."""
+    parents = np.ascontiguousarray(parents, dtype=np.int32)
+    idx = np.empty((parents.size, row_len), np.int32)
+    _check(lib.dsv4cuda_tree_attn_indices(_p(parents, i32p), parents.size, committed, window,
+                                          ring_base, scratch_row, _p(idx, i32p), row_len))
+    return idx
+
+
+def kv_copy_rows(cache, src_rows, dst_rows, stream=None):
+    s = np.ascontiguousarray(src_rows, dtype=np.int64)
+    d = np.ascontiguousarray(dst_rows, dtype=np.int64)
+    _check(lib.dsv4cuda_kv_copy_rows(C.byref(cache.struct), s.ctypes.data, d.ctypes.data, s.size,
+                                     _stream(stream)))

@@ -336,6 +336,86 @@ void dsv4cuda_sparse_attn_host(float *o, const float *q, const float *kv, const 
 int dsv4cuda_attn_timing_begin(void);
 int dsv4cuda_attn_timing_end(int *n_calls, float *main_ms);
 
+/* ---------------------------------------------------------------------
+ * Speculative-decoding acceptance (the reference runs it on the host in
+ * its CLI: rng_next src/cli/dsv4_run.c:248, sample_top_p :308, argmax_logits
+ * :355, the verify loop :951-1043; EOS is token 1 there, eos_id here).
+ *
+ * Host forms (host pointers), the same arithmetic in the same order: */
+uint64_t dsv4cuda_rng_next(uint64_t *state);
+int dsv4cuda_argmax_logits(const float *logits, int vocab);
+int dsv4cuda_sample_top_p(const float *logits, int vocab, double temperature, double top_p,
+                          uint64_t *rng_state);
+/* One verify step: proposal[proposed] drafts against logits
+ * [(proposed + 1)][vocab]; temperature 0 = greedy. Writes the emitted tokens
+ * (accepted drafts then the correction or bonus, or up to an accepted EOS)
+ * and returns their count; *n_commit = verified positions to keep (the
+ * snapshot commit length), *n_accepted, *n_samples = uniforms drawn. */
+int dsv4cuda_accept_chain(const int *proposal, int proposed, const float *logits, int vocab,
+                          double temperature, double top_p, uint64_t *rng_state, int eos_id,
+                          int *tokens, int *n_commit, int *n_accepted, int *n_samples);
+
+/* Device forms (DEVICE pointers, async on stream): logits stay in HBM.
+ * dsv4cuda_argmax_rows: out[r] = argmax_logits(row r), bit-exact.
+ * dsv4cuda_sample_rows: top_p = 1 sampling with uniforms[r] =
+ *   (rng_next() >> 11) * 2^-53 drawn in row order; the softmax sums are
+ *   formed in parallel, so a target within a few ulps of a running sum may
+ *   select the neighbouring token (use the host form for exact replay or
+ *   top_p < 1).
+ * dsv4cuda_accept_device: row targets of the proposed + 1 rows, then the
+ *   chain; result holds 2 * proposed + 6 ints: [0] emitted, [1] n_commit,
+ *   [2] n_accepted, [3] uniforms consumed (advance the host rng by this),
+ *   [4 ..] emitted tokens. */
+int dsv4cuda_argmax_rows(const float *logits, int rows, int vocab, int *out, void *stream);
+int dsv4cuda_sample_rows(const float *logits, int rows, int vocab, double temperature,
+                         const double *uniforms, int *out, void *stream);
+int dsv4cuda_accept_device(const int *proposal, int proposed, const float *logits, int vocab,
+                           double temperature, const double *uniforms, int eos_id, int *result,
+                           void *stream);
+
+/* ---------------------------------------------------------------------
+ * Speculative transaction on the latent KV ring (dsv4_context_snapshot_take
+ * / _restore / _commit_prefix, src/dsv4/dsv4_model.c:2842-3056), device
+ * memory. Each registered cache holds a window ring at rows
+ * [ring_base, ring_base + window) (position p -> row ring_base + p % window);
+ * state buffers (e.g. the hyper-connection residual state) are saved at
+ * take and captured after each verified position. Per verify step:
+ *   take(start, n)            save the ring rows positions start..start+n-1
+ *                             will overwrite, and the states (n <= window,
+ *                             n <= max_positions <= 64);
+ *   capture_state(step)       after position start+step: copy the states;
+ *   commit_prefix(k)          keep positions < k, put the saved rows back
+ *                             for the others, states = capture of step k-1;
+ *   restore()                 undo the whole step. */
+typedef struct dsv4cuda_snapshot dsv4cuda_snapshot;
+int dsv4cuda_snapshot_create(dsv4cuda_snapshot **out, int max_positions, int n_caches,
+                             const dsv4cuda_kv_cache *caches, const long long *ring_base,
+                             const int *windows, int n_states, float *const *states,
+                             const size_t *state_elems);
+int dsv4cuda_snapshot_take(dsv4cuda_snapshot *s, int start_position, int n_positions,
+                           void *stream);
+int dsv4cuda_snapshot_capture_state(dsv4cuda_snapshot *s, int step, void *stream);
+int dsv4cuda_snapshot_commit_prefix(dsv4cuda_snapshot *s, int n_positions, void *stream);
+int dsv4cuda_snapshot_restore(dsv4cuda_snapshot *s, void *stream);
+void dsv4cuda_snapshot_destroy(dsv4cuda_snapshot *s);
+
+/* ---------------------------------------------------------------------
+ * Verify step over a draft tree (a chain: parents = -1, 0, 1, ...), the
+ * batched verify of dsv4_prefill_capture (src/dsv4/dsv4_model.c:8434) with
+ * an ancestor mask. Node j is at position committed + depth(j) and sees the
+ * window window_topk (:5073) gives that position, where positions >=
+ * committed are its ancestors and itself, held in scratch rows
+ * scratch_row + node. Writes idx [n_nodes][row_len] (host, -1 padded) for
+ * dsv4cuda_sparse_attn with batch = n_nodes and kv_batch_stride = 0, and
+ * returns the longest row. */
+int dsv4cuda_tree_attn_indices(const int *parents, int n_nodes, int committed, int window,
+                               long long ring_base, long long scratch_row, int *idx,
+                               int row_len);
+/* Copy cache rows src_rows[i] -> dst_rows[i] (host arrays, n <= 64): moves
+ * the accepted path's scratch rows into their ring slots. */
+int dsv4cuda_kv_copy_rows(const dsv4cuda_kv_cache *cache, const long long *src_rows,
+                          const long long *dst_rows, int n, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

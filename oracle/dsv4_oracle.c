@@ -586,3 +586,121 @@ void orc_rope_inv(float *x, int heads, int head_dim, const float *cosv,
         }
     }
 }
+
+/* ------------------------------------------- speculative acceptance -- */
+
+/* xorshift64 13/7/17 (src/cli/dsv4_run.c:248-254). */
+uint64_t orc_rng_next(uint64_t *state)
+{
+    uint64_t x = *state;
+    x ^= x << 13;
+    x ^= x >> 7;
+    x ^= x << 17;
+    *state = x;
+    return x;
+}
+
+/* First index of the maximum under strict ">" (src/cli/dsv4_run.c:355). */
+int orc_argmax_logits(const float *logits, int vocab)
+{
+    int best = 0;
+    for (int v = 1; v < vocab; v++)
+        if (logits[v] > logits[best]) best = v;
+    return best;
+}
+
+typedef struct { double w; int id; } OrcItem;
+
+static int orc_item_desc(const void *ap, const void *bp)
+{
+    const OrcItem *a = (const OrcItem *)ap, *b = (const OrcItem *)bp;
+    if (a->w > b->w) return -1;
+    if (a->w < b->w) return 1;
+    return (a->id > b->id) - (a->id < b->id);
+}
+
+/* Temperature softmax in double, a 53-bit uniform, optional nucleus cut
+ * (src/cli/dsv4_run.c:308-353, comparator :80-87). */
+int orc_sample_top_p(const float *logits, int vocab, double temperature,
+                     double top_p, uint64_t *state)
+{
+    OrcItem *it = (OrcItem *)malloc((size_t)vocab * sizeof(OrcItem));
+    double mx = logits[0];
+    for (int v = 1; v < vocab; v++)
+        if (logits[v] > mx) mx = logits[v];
+    double total = 0.0;
+    const double inv_t = temperature > 1e-5 ? 1.0 / temperature : 1e5;
+    for (int v = 0; v < vocab; v++) {
+        it[v].w = exp(((double)logits[v] - mx) * inv_t);
+        it[v].id = v;
+        total += it[v].w;
+    }
+    const double u = (double)(orc_rng_next(state) >> 11) * (1.0 / 9007199254740992.0);
+    int r;
+    if (top_p == 1.0) {
+        const double target = u * total;
+        double cum = 0.0;
+        r = it[vocab - 1].id;
+        for (int i = 0; i < vocab; i++) {
+            cum += it[i].w;
+            if (target < cum) { r = it[i].id; break; }
+        }
+    } else {
+        qsort(it, (size_t)vocab, sizeof(*it), orc_item_desc);
+        double kept = 0.0;
+        int keep = vocab;
+        const double thr = total * top_p;
+        for (int i = 0; i < vocab; i++) {
+            kept += it[i].w;
+            if (kept >= thr) { keep = i + 1; break; }
+        }
+        const double target = u * kept;
+        double cum = 0.0;
+        r = it[keep - 1].id;
+        for (int i = 0; i < keep; i++) {
+            cum += it[i].w;
+            if (target < cum) { r = it[i].id; break; }
+        }
+    }
+    free(it);
+    return r;
+}
+
+int orc_accept_chain(const int *proposal, int proposed, const float *logits, int vocab,
+                     double temperature, double top_p, uint64_t *state, int eos_id,
+                     int *tokens, int *n_commit, int *n_accepted, int *n_samples)
+{
+    int accepted = 0, correction = -1, samples = 0;
+    while (accepted < proposed) {
+        const float *row = logits + (size_t)accepted * vocab;
+        int target;
+        if (temperature == 0.0) target = orc_argmax_logits(row, vocab);
+        else { target = orc_sample_top_p(row, vocab, temperature, top_p, state); samples++; }
+        if (proposal[accepted] != target) { correction = target; break; }
+        accepted++;
+        if (target == eos_id) break;
+    }
+    int eos_at = -1;
+    for (int i = 0; i < accepted; i++)
+        if (proposal[i] == eos_id) { eos_at = i; break; }
+    int n = 0;
+    if (eos_at >= 0) {
+        for (int i = 0; i <= eos_at; i++) tokens[n++] = proposal[i];
+        *n_commit = eos_at + 1;
+    } else if (accepted < proposed) {
+        for (int i = 0; i < accepted; i++) tokens[n++] = proposal[i];
+        tokens[n++] = correction;
+        *n_commit = accepted + 1;
+    } else {
+        const float *row = logits + (size_t)proposed * vocab;
+        int bonus;
+        if (temperature == 0.0) bonus = orc_argmax_logits(row, vocab);
+        else { bonus = orc_sample_top_p(row, vocab, temperature, top_p, state); samples++; }
+        for (int i = 0; i < proposed; i++) tokens[n++] = proposal[i];
+        tokens[n++] = bonus;
+        *n_commit = proposed + 1;
+    }
+    *n_accepted = accepted;
+    *n_samples = samples;
+    return n;
+}

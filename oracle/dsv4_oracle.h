@@ -126,6 +126,21 @@ void orc_rope_inv(float *x, int heads, int head_dim, const float *cosv,
                   const float *sinv, int n);
 
 /* ---- helpers for tests ---- */
+/* ---- speculative acceptance (src/cli/dsv4_run.c) ---- */
+uint64_t orc_rng_next(uint64_t *state);                       /* :248-254 */
+int orc_argmax_logits(const float *logits, int vocab);        /* :355 */
+int orc_sample_top_p(const float *logits, int vocab, double temperature,
+                     double top_p, uint64_t *state);          /* :308-353 */
+/* The verify-step acceptance of :951-1043 for one proposal of `proposed`
+ * draft tokens against logits [(proposed + 1)][vocab]: emits the accepted
+ * drafts and the correction or bonus token (or stops after eos_id). Returns
+ * the number of emitted tokens; *n_commit = positions to keep (the
+ * reference's snapshot commit length), *n_accepted, *n_samples = uniforms
+ * consumed (T > 0). */
+int orc_accept_chain(const int *proposal, int proposed, const float *logits, int vocab,
+                     double temperature, double top_p, uint64_t *state, int eos_id,
+                     int *tokens, int *n_commit, int *n_accepted, int *n_samples);
+
 uint64_t orc_xorshift_fill_u8(uint8_t *dst, int64_t n, uint64_t state,
                               int mod);
 uint64_t orc_xorshift_next_many(uint64_t *dst, int64_t n, uint64_t state);

@@ -18,6 +18,7 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 ORACLE_SO = os.path.join(HERE, "_build", "libdsv4_oracle.so")
 REF_SO = os.path.join(HERE, "_ref", "libdsv4_ref.so")
+REFCLI_SO = os.path.join(HERE, "_ref", "libdsv4_refcli.so")
 
 f32p = C.POINTER(C.c_float)
 u8p = C.POINTER(C.c_uint8)
@@ -485,3 +486,83 @@ def make_moe_layer(hidden, moe_inter, n_experts, topk, seed=0, shared="fp8",
     else:
         layer["shared"] = None
     return layer
+
+
+# ------------------------------------------------- speculative acceptance --
+u64p = C.POINTER(C.c_uint64)
+
+
+class _Sampler:
+    """rng_next / argmax_logits / sample_top_p with caller-held rng state;
+    `prefix` selects the library's symbol names."""
+
+    def _setup_sampler(self, lib, prefix):
+        self._s = lib
+        self._pre = prefix
+        getattr(lib, prefix + "rng_next").restype = C.c_uint64
+        getattr(lib, prefix + "rng_next").argtypes = [u64p]
+        getattr(lib, prefix + "argmax_logits").restype = C.c_int
+        getattr(lib, prefix + "argmax_logits").argtypes = [f32p, C.c_int]
+        getattr(lib, prefix + "sample_top_p").restype = C.c_int
+        getattr(lib, prefix + "sample_top_p").argtypes = [f32p, C.c_int, C.c_double, C.c_double,
+                                                          u64p]
+
+    def rng_next(self, state):
+        """Returns (value, new_state)."""
+        st = C.c_uint64(state)
+        v = getattr(self._s, self._pre + "rng_next")(C.byref(st))
+        return v, st.value
+
+    def argmax_logits(self, logits):
+        logits = _f32(logits)
+        return getattr(self._s, self._pre + "argmax_logits")(_p(logits, f32p), logits.size)
+
+    def sample_top_p(self, logits, temperature, top_p, state):
+        """Returns (token, new_state)."""
+        logits = _f32(logits)
+        st = C.c_uint64(state)
+        tok = getattr(self._s, self._pre + "sample_top_p")(_p(logits, f32p), logits.size,
+                                                           temperature, top_p, C.byref(st))
+        return tok, st.value
+
+
+class OracleSampler(_Sampler):
+    """The C restatement (dsv4_oracle.c), plus the acceptance chain."""
+
+    def __init__(self):
+        self.lib = C.CDLL(ORACLE_SO)
+        self._setup_sampler(self.lib, "orc_")
+        self.lib.orc_accept_chain.restype = C.c_int
+
+    def accept_chain(self, proposal, logits, temperature, top_p, state, eos_id=1):
+        """logits [(proposed+1)][V]. Returns dict(tokens, n_commit, n_accepted,
+        n_samples, state)."""
+        proposal = np.ascontiguousarray(proposal, dtype=np.int32)
+        logits = _f32(logits)
+        P = proposal.size
+        toks = np.empty(P + 1, np.int32)
+        st = C.c_uint64(state)
+        nc, na, ns = C.c_int(), C.c_int(), C.c_int()
+        n = self.lib.orc_accept_chain(_p(proposal, i32p), P, _p(logits, f32p), logits.shape[-1],
+                                      C.c_double(temperature), C.c_double(top_p), C.byref(st),
+                                      eos_id, _p(toks, i32p), C.byref(nc), C.byref(na),
+                                      C.byref(ns))
+        return dict(tokens=toks[:n].copy(), n_commit=nc.value, n_accepted=na.value,
+                    n_samples=ns.value, state=st.value)
+
+
+class RefSampler(_Sampler):
+    """The reference CLI's own static helpers (src/cli/dsv4_run.c), compiled
+    by oracle/Makefile into _ref/libdsv4_refcli.so."""
+
+    def __init__(self):
+        self.lib = C.CDLL(REFCLI_SO)
+        self._setup_sampler(self.lib, "ref_")
+        self.lib.ref_ngram_draft.restype = C.c_int
+
+    def ngram_draft(self, history, cap=16, min_match=2, allow_overlap=0, periodic_extend=0):
+        history = np.ascontiguousarray(history, dtype=np.int32)
+        out = np.empty(64, np.int32)
+        n = self.lib.ref_ngram_draft(_p(history, i32p), history.size, cap, min_match,
+                                     allow_overlap, periodic_extend, _p(out, i32p))
+        return out[:n].copy()
