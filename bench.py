@@ -42,6 +42,9 @@ EXPERT_BYTES = 2 * (I * H // 2 + I * H // 32) + (H * I // 2 + H * I // 32)  # 23
 SHARED_FP8_BYTES = 2 * (I * H + (I // 128) * (H // 128)) + (H * I + (H // 128) * (I // 128))
 ROUTER_BYTES = E * H * 2
 METRIC = "decode tok/s through one MoE layer (config 2: H7168, I2048, 256+1 experts, top-8)"
+# DRAM bytes of one step's two routed GEMV launches (8 experts), from ncu:
+# gate/up 125.3 MB read + 4.7 MB written, down 62.5 MB + 0.8 MB
+FP4_TRAFFIC_PER_STEP = (125.28 + 4.67 + 62.47 + 0.80) * 1e6
 
 
 def parse():
@@ -437,8 +440,11 @@ def main():
                        "l2": "inputs larger than L2: each step reads a different layer's "
                              "~235 MB of weights", "parallelism": f"ep{world}"},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                         "frac": achieved / peak, "traffic": None,
-                         "kernel": "fp4_gemv_kernel (routed gate/up pair + down)",
+                         "frac": achieved / peak, "traffic": FP4_TRAFFIC_PER_STEP,
+                         "traffic_source": "ncu dram__bytes_read+write of the gate/up and down "
+                                           "launches for 8 experts "
+                                           "(profiles/fp4_stream_kernel_experts8.md)",
+                         "kernel": "fp4_stream_kernel (routed gate/up pair + down)",
                          "alg_bytes_per_step": alg_bytes, "peak_source": peak_src,
                          "kernel_ms_per_step": kern_ms,
                          "phase_ms_per_step": {
