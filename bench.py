@@ -363,35 +363,49 @@ def main():
     ms_per_step = ms / args.steps
     value = M * args.steps / (ms / 1e3)
 
-    # ---- expert-GEMV roofline: the same forward, ungraphed, with events
-    # around the routed gate/up and down launches on the forward stream
+    # ---- expert-GEMV roofline: each layer's forward captured once more into
+    # a graph whose event nodes bracket the routed gate/up and down launches
+    # (and the router); replayed like the timed steps, read after each replay
     U_total, n_fw, fallbacks = 0, 0, 0
     lib = dsv4cuda.lib
-    for li, (_, L) in enumerate(layers):
+    import ctypes as C
+    tgraphs = []
+    for _, L in layers:
         lib.dsv4cuda_moe_timing_begin(L.handle)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            layer_forward(L, xin, out_dev, torch.cuda.current_stream().cuda_stream)
+        tgraphs.append(g)
     gu_ms = dn_ms = lg_ms = sl_ms = 0.0
     n_timed = 0
+    a_, b_, c_, d_ = C.c_float(), C.c_float(), C.c_float(), C.c_float()
     with torch.cuda.stream(stream):
         for i in range(max(8, args.steps // 4)):
-            _, L = layers[i % len(layers)]
+            li = i % len(layers)
+            _, L = layers[li]
             xin.copy_(x_dev[i % pool])
-            layer_forward(L, xin, out_dev, stream.cuda_stream)
+            tgraphs[li].replay()
+            stream.synchronize()
+            if lib.dsv4cuda_moe_timing_read(L.handle, 0, C.byref(a_), C.byref(b_), C.byref(c_),
+                                            C.byref(d_)) != 0:
+                raise RuntimeError(dsv4cuda.last_error())
+            gu_ms += a_.value
+            dn_ms += b_.value
+            lg_ms += c_.value
+            sl_ms += d_.value
+            n_timed += 1
             idx, _, fb = L.last_routes(M)
             U_total += len(np.unique(idx))
             fallbacks = fb
             n_fw += 1
     torch.cuda.synchronize()
-    import ctypes as C
+    for gr in tgraphs:
+        gr.reset()
+    tgraphs = []
+    g = None
+    n = C.c_int()
     for _, L in layers:
-        n = C.c_int()
-        a, b, c, d = C.c_float(), C.c_float(), C.c_float(), C.c_float()
-        lib.dsv4cuda_moe_timing_end2(L.handle, C.byref(n), C.byref(a), C.byref(b), C.byref(c),
-                                     C.byref(d))
-        gu_ms += a.value
-        dn_ms += b.value
-        lg_ms += c.value
-        sl_ms += d.value
-        n_timed += n.value
+        lib.dsv4cuda_moe_timing_end2(L.handle, C.byref(n), None, None, None, None)
     U_avg = U_total / max(n_fw, 1)
     if ep:  # this rank's share of the unique experts (uniform routing)
         U_avg = U_avg * (erange[1] - erange[0]) / args.experts

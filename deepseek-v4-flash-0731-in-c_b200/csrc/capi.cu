@@ -791,6 +791,26 @@ DSV4_API int dsv4cuda_moe_timing_end2(dsv4cuda_moe_layer* L, int* n_forwards, fl
   return 0;
 }
 
+DSV4_API int dsv4cuda_moe_timing_read(dsv4cuda_moe_layer* L, int index, float* gateup_ms,
+                                      float* down_ms, float* logits_ms, float* select_ms) {
+  if (!L || index < 0 || index >= L->timed) { record_error("dsv4cuda_moe_timing_read: bad index"); return -1; }
+  cudaEvent_t* ev = &L->events[static_cast<size_t>(index) * 8];
+  float a = 0.f, b = 0.f, c = 0.f, d = 0.f;
+  if (cudaEventSynchronize(ev[3]) != cudaSuccess ||
+      cudaEventElapsedTime(&a, ev[0], ev[1]) != cudaSuccess ||
+      cudaEventElapsedTime(&b, ev[2], ev[3]) != cudaSuccess ||
+      cudaEventElapsedTime(&c, ev[4], ev[5]) != cudaSuccess ||
+      cudaEventElapsedTime(&d, ev[5], ev[6]) != cudaSuccess) {
+    record_error("timing events failed");
+    return -1;
+  }
+  if (gateup_ms) *gateup_ms = a;
+  if (down_ms) *down_ms = b;
+  if (logits_ms) *logits_ms = c;
+  if (select_ms) *select_ms = d;
+  return 0;
+}
+
 DSV4_API int dsv4cuda_moe_timing_end(dsv4cuda_moe_layer* L, int* n_forwards, float* gateup_ms,
                                      float* down_ms) {
   return dsv4cuda_moe_timing_end2(L, n_forwards, gateup_ms, down_ms, nullptr, nullptr);

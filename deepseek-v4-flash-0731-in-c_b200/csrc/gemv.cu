@@ -331,7 +331,8 @@ struct StreamLayout {
   static constexpr int kW = 32 * kSRowBytes;      // two swizzled [32][128] boxes
   static constexpr int kS = 32 * kSGroups;        // [32][16] codes
   static constexpr int kA = NT * kSCols * 2;      // activations (f16)
-  static constexpr int kStage = (kW + kS + kA + 1023) / 1024 * 1024;  // 1 KB aligned
+  static constexpr int kQ = NT * 16;              // activation scales of the chunk (4 x f32)
+  static constexpr int kStage = (kW + kS + kA + kQ + 1023) / 1024 * 1024;  // 1 KB aligned
   static constexpr int kWarpBytes = kStages * kStage;
 };
 
@@ -373,6 +374,31 @@ __device__ __forceinline__ void fp4_partial16x2(const uint32_t* wa, const uint32
     pb = fma_h_lo(b3, xb[4 * i + 3], pb);
     pa = fma_h_hi(a3, xa[4 * i + 3], pa);
     pb = fma_h_hi(b3, xb[4 * i + 3], pb);
+  }
+}
+
+// Four 32-column partials with four interleaved (independent) chains: one
+// warp keeps four FMAs in flight per four-cycle FMA latency.
+__device__ __forceinline__ void fp4_partial16x4(const uint32_t (*w)[4], const uint32_t (*x)[16],
+                                                float* p) {
+#pragma unroll
+  for (int c = 0; c < 4; ++c) p[c] = 0.0f;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    uint32_t h[4][4];
+#pragma unroll
+    for (int c = 0; c < 4; ++c)
+      asm("{ .reg .b8 c0, c1, c2, c3; mov.b32 {c0, c1, c2, c3}, %4;"
+          " cvt.rn.f16x2.e2m1x2 %0, c0; cvt.rn.f16x2.e2m1x2 %1, c1;"
+          " cvt.rn.f16x2.e2m1x2 %2, c2; cvt.rn.f16x2.e2m1x2 %3, c3; }"
+          : "=r"(h[c][0]), "=r"(h[c][1]), "=r"(h[c][2]), "=r"(h[c][3]) : "r"(w[c][i]));
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+#pragma unroll
+      for (int c = 0; c < 4; ++c) p[c] = fma_h_lo(h[c][k], x[c][4 * i + k], p[c]);
+#pragma unroll
+      for (int c = 0; c < 4; ++c) p[c] = fma_h_hi(h[c][k], x[c][4 * i + k], p[c]);
+    }
   }
 }
 
@@ -418,48 +444,87 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
   const long long jobs = my_tiles * CPT;
   const int sld = (a.act.ld + 127) >> 7;
 
-  auto issue = [&](long long j) {
-    if (lane != 0) return;
-    const int s = static_cast<int>(j % kStages);
-    const long long tile = first + (j / CPT) * nwarps;
-    const int chunk = static_cast<int>(j % CPT);
-    const int item_idx = static_cast<int>(tile / (V * rblocks));
-    const int rem = static_cast<int>(tile % (V * rblocks));
-    const int v = rem / rblocks, rb = rem % rblocks;
-    const GemvItem& it = a.items[item_idx];
-    const int ntok = it.ntok;
-    unsigned char* st = wbase + s * L::kStage;
-    mbar_arrive_expect_tx(&bars[s], static_cast<uint32_t>(L::kW + L::kS + ntok * kSCols * 2));
-    const int y = it.mat * a.rows + rb * 32;
-    const CUtensorMap* wm = v ? &maps.w[1] : &maps.w[0];
-    const CUtensorMap* sm = v ? &maps.s[1] : &maps.s[0];
-    tma_load_2d(st, wm, chunk * kSRowBytes, y, &bars[s]);
-    tma_load_2d(st + L::kW / 2, wm, chunk * kSRowBytes + 128, y, &bars[s]);
-    tma_load_2d(st + L::kW, sm, chunk * kSGroups, y, &bars[s]);
-    for (int t = 0; t < ntok; ++t)
-      bulk_g2s(st + L::kW + L::kS + t * kSCols * 2,
-               a.act.x + static_cast<size_t>(it.tok[t].x) * a.act.ld + chunk * kSCols,
-               kSCols * 2, &bars[s]);
+  // Job j = (my tile j / CPT, chunk j % CPT). The consumer and the issuer
+  // (kStages jobs ahead) each walk their own cursor; a tile's item, matrix
+  // and row block are decoded with 32-bit arithmetic once per tile.
+  struct Cursor {
+    int chunk = 0, tile_n = 0, item = 0, v = 0, rb = 0, mat = 0, ntok = 0;
+    int tx[NT], ty[NT];  // the item's token rows (x) and output rows (y)
+  };
+  const int per_item = V * rblocks;
+  const long long my_tile_count = my_tiles;
+  auto decode = [&](Cursor& c) {
+    if (c.tile_n >= my_tile_count) return;  // past the last job
+    const int tile = static_cast<int>(first + static_cast<long long>(c.tile_n) * nwarps);
+    c.item = tile / per_item;
+    const int rem = tile - c.item * per_item;
+    c.v = rem / rblocks;
+    c.rb = rem - c.v * rblocks;
+    const GemvItem& it = a.items[c.item];
+    c.mat = it.mat;
+    c.ntok = it.ntok;
+#pragma unroll
+    for (int t = 0; t < NT; ++t) {
+      const int tt = (NT == 1 || t < c.ntok) ? t : 0;
+      c.tx[t] = it.tok[tt].x;
+      c.ty[t] = it.tok[tt].y;
+    }
+  };
+  auto advance = [&](Cursor& c) {
+    if (++c.chunk == CPT) {
+      c.chunk = 0;
+      ++c.tile_n;
+      decode(c);
+    }
+  };
+  Cursor ic;  // issue cursor
+  decode(ic);
+  int stage_i = 0;
+  auto issue = [&]() {
+    if (lane == 0) {
+      const int ntok = ic.ntok;
+      unsigned char* st = wbase + stage_i * L::kStage;
+      mbar_arrive_expect_tx(&bars[stage_i],
+                            static_cast<uint32_t>(L::kW + L::kS + ntok * (kSCols * 2 + 16)));
+      const int y = ic.mat * a.rows + ic.rb * 32;
+      const CUtensorMap* wm = ic.v ? &maps.w[1] : &maps.w[0];
+      const CUtensorMap* sm = ic.v ? &maps.s[1] : &maps.s[0];
+      tma_load_2d(st, wm, ic.chunk * kSRowBytes, y, &bars[stage_i]);
+      tma_load_2d(st + L::kW / 2, wm, ic.chunk * kSRowBytes + 128, y, &bars[stage_i]);
+      tma_load_2d(st + L::kW, sm, ic.chunk * kSGroups, y, &bars[stage_i]);
+#pragma unroll
+      for (int t = 0; t < NT; ++t) {
+        if (NT == 1 || t < ntok) {
+          bulk_g2s(st + L::kW + L::kS + t * kSCols * 2,
+                   a.act.x + static_cast<size_t>(ic.tx[t]) * a.act.ld + ic.chunk * kSCols,
+                   kSCols * 2, &bars[stage_i]);
+          bulk_g2s(st + L::kW + L::kS + L::kA + t * 16,
+                   a.act.s + static_cast<size_t>(ic.tx[t]) * sld + ic.chunk * 4, 16,
+                   &bars[stage_i]);
+        }
+      }
+    }
+    advance(ic);
+    stage_i = stage_i + 1 == kStages ? 0 : stage_i + 1;
   };
 
   float acc[NT];
 #pragma unroll
   for (int t = 0; t < NT; ++t) acc[t] = 0.0f;
 
-  for (long long j = 0; j < jobs && j < kStages; ++j) issue(j);
+  for (long long j = 0; j < jobs && j < kStages; ++j) issue();
   __syncwarp();
   bool ok = true;
   long long j = 0;
+  Cursor cc;  // consumer cursor
+  decode(cc);
+  int s = 0;
+  uint32_t phase = 0;
   for (; j < jobs; ++j) {
-    const int s = static_cast<int>(j % kStages);
-    if (!mbar_wait(&bars[s], static_cast<uint32_t>((j / kStages) & 1), a.err)) { ok = false; break; }
-    const long long tile = first + (j / CPT) * nwarps;
-    const int chunk = static_cast<int>(j % CPT);
-    const int item_idx = static_cast<int>(tile / (V * rblocks));
-    const int rem = static_cast<int>(tile % (V * rblocks));
-    const int v = rem / rblocks, rb = rem % rblocks;
-    const GemvItem& it = a.items[item_idx];
-    const int ntok = it.ntok;
+    if (!mbar_wait(&bars[s], phase, a.err)) { ok = false; break; }
+    const int chunk = cc.chunk;
+    const int v = cc.v, rb = cc.rb;
+    const int ntok = cc.ntok;
     const unsigned char* st = wbase + s * L::kStage;
     const unsigned char* wrow = st + lane * 128;
     const int sw = lane & 7;
@@ -468,37 +533,40 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
     float qs[NT][4];
 #pragma unroll
     for (int t = 0; t < NT; ++t) {
-      const int xi = (NT == 1 || t < ntok) ? it.tok[t].x : it.tok[0].x;
-      const float4 q4 = __ldg(reinterpret_cast<const float4*>(a.act.s + static_cast<size_t>(xi) * sld +
-                                                              chunk * 4));
+      const float4 q4 = *reinterpret_cast<const float4*>(
+          st + L::kW + L::kS + L::kA + ((NT == 1 || t < ntok) ? t : 0) * 16);
       qs[t][0] = q4.x; qs[t][1] = q4.y; qs[t][2] = q4.z; qs[t][3] = q4.w;
     }
 #pragma unroll
-    for (int g = 0; g < kSGroups; g += 2) {
+    for (int g = 0; g < kSGroups; g += 4) {
       // group g lives in box g/8, 16-byte chunk (g%8) xor (row%8)
-      const uint4 wa = *reinterpret_cast<const uint4*>(wrow + (g >> 3) * (L::kW / 2) +
-                                                       (((g & 7) ^ sw) << 4));
-      const uint4 wb = *reinterpret_cast<const uint4*>(wrow + ((g + 1) >> 3) * (L::kW / 2) +
-                                                       ((((g + 1) & 7) ^ sw) << 4));
-      const uint32_t wa4[4] = {wa.x, wa.y, wa.z, wa.w};
-      const uint32_t wb4[4] = {wb.x, wb.y, wb.z, wb.w};
-      const float sa = e8m0_tbl[(cw[g >> 2] >> (8 * (g & 3))) & 0xFFu];
-      const float sb = e8m0_tbl[(cw[(g + 1) >> 2] >> (8 * ((g + 1) & 3))) & 0xFFu];
+      uint32_t w4[4][4];
+      float sc[4];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const int gc = g + c;
+        const uint4 wv = *reinterpret_cast<const uint4*>(wrow + (gc >> 3) * (L::kW / 2) +
+                                                         (((gc & 7) ^ sw) << 4));
+        w4[c][0] = wv.x; w4[c][1] = wv.y; w4[c][2] = wv.z; w4[c][3] = wv.w;
+        sc[c] = e8m0_tbl[(cw[gc >> 2] >> (8 * (gc & 3))) & 0xFFu];
+      }
 #pragma unroll
       for (int t = 0; t < NT; ++t) {
         if (NT == 1 || t < ntok) {
           const uint4* xg = reinterpret_cast<const uint4*>(st + L::kW + L::kS + t * kSCols * 2 + g * 64);
-          uint32_t xa[16], xb[16];
+          uint32_t x4[4][16];
 #pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            const uint4 u = xg[q], w = xg[4 + q];
-            xa[4 * q] = u.x; xa[4 * q + 1] = u.y; xa[4 * q + 2] = u.z; xa[4 * q + 3] = u.w;
-            xb[4 * q] = w.x; xb[4 * q + 1] = w.y; xb[4 * q + 2] = w.z; xb[4 * q + 3] = w.w;
-          }
-          float pa, pb;
-          fp4_partial16x2(wa4, xa, wb4, xb, pa, pb);
-          acc[t] = fmaf(pa, qs[t][g >> 2] * sa, acc[t]);
-          acc[t] = fmaf(pb, qs[t][(g + 1) >> 2] * sb, acc[t]);
+          for (int c = 0; c < 4; ++c)
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              const uint4 u = xg[4 * c + q];
+              x4[c][4 * q] = u.x; x4[c][4 * q + 1] = u.y; x4[c][4 * q + 2] = u.z; x4[c][4 * q + 3] = u.w;
+            }
+          float p[4];
+          fp4_partial16x4(w4, x4, p);
+          // group g + c's 128-column activation block is (g + c) / 4 = g / 4
+#pragma unroll
+          for (int c = 0; c < 4; ++c) acc[t] = fmaf(p[c], qs[t][g >> 2] * sc[c], acc[t]);
         }
       }
     }
@@ -509,19 +577,28 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
 #pragma unroll
         for (int t = 0; t < NT; ++t)
           if (NT == 1 || t < ntok)
-            Yv[static_cast<size_t>(it.tok[t].y) * a.rows + row] = bf16_round(acc[t]);
+            Yv[static_cast<size_t>(cc.ty[t]) * a.rows + row] = bf16_round(acc[t]);
       }
 #pragma unroll
       for (int t = 0; t < NT; ++t) acc[t] = 0.0f;
     }
     __syncwarp();
-    if (j + kStages < jobs) issue(j + kStages);
+    if (j + kStages < jobs) issue();
     __syncwarp();
+    advance(cc);
+    if (++s == kStages) {
+      s = 0;
+      phase ^= 1u;
+    }
   }
   if (!ok) {
     // drain this warp's copies still in flight before the CTA exits
-    for (long long k = j + 1; k < jobs && k < j + kStages; ++k)
-      mbar_wait(&bars[k % kStages], static_cast<uint32_t>((k / kStages) & 1), a.err);
+    uint32_t ph = phase;
+    int k = s;
+    for (long long q = j + 1; q < jobs && q < j + kStages; ++q) {
+      if (++k == kStages) { k = 0; ph ^= 1u; }
+      mbar_wait(&bars[k], ph, a.err);
+    }
   }
 }
 

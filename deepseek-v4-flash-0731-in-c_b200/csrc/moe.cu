@@ -711,6 +711,12 @@ __global__ void moe_combine_kernel(const float* __restrict__ routed, const float
 
 size_t align256(size_t b) { return (b + 255) & ~static_cast<size_t>(255); }
 
+// Timing events are recorded as external event nodes when the stream is
+// being captured, so a replayed graph records them too.
+void record_timing(cudaEvent_t ev, cudaStream_t st) {
+  cudaEventRecordWithFlags(ev, st, cudaEventRecordExternal);
+}
+
 struct SideStream {
   cudaStream_t s = nullptr;
   cudaEvent_t fork = nullptr, join = nullptr;
@@ -813,9 +819,9 @@ static cudaError_t route_impl(const MoeConfig& c, const MoeWeights& w, const Moe
     a.items_dn = ws.items_dn;
     a.items_sh = ws.items_sh;
   }
-  if (plan && ws.timing) cudaEventRecord(ws.timing[4], st);
+  if (plan && ws.timing) record_timing(ws.timing[4], st);
   router_logits_kernel<<<dim3(c.n_experts, M), kLogitWarps * 32, 0, st>>>(a);
-  if (plan && ws.timing) cudaEventRecord(ws.timing[5], st);
+  if (plan && ws.timing) record_timing(ws.timing[5], st);
   const size_t smem = select_smem_bytes(c.hidden, c.n_experts, M * c.topk, nullptr, nullptr);
   if (smem > 48 * 1024) {
     cudaError_t e = cudaFuncSetAttribute(router_select_kernel,
@@ -824,7 +830,7 @@ static cudaError_t route_impl(const MoeConfig& c, const MoeWeights& w, const Moe
     if (e != cudaSuccess) return e;
   }
   router_select_kernel<<<M, kSelThreads, smem, st>>>(a);
-  if (plan && ws.timing) cudaEventRecord(ws.timing[6], st);
+  if (plan && ws.timing) record_timing(ws.timing[6], st);
   return cudaGetLastError();
 }
 
@@ -917,9 +923,9 @@ cudaError_t moe_forward_local(const MoeConfig& c, const MoeWeights& w, const Moe
   gu.Y[0] = ws.gate; gu.Y[1] = ws.up;
   gu.items = ws.items_gu; gu.n_items = ws.counters; gu.max_items = R; gu.n_mats = n_local;
   gu.err = opt.err;
-  if (ws.timing) cudaEventRecord(ws.timing[0], st);
+  if (ws.timing) record_timing(ws.timing[0], st);
   if ((err = launch_fp4_gemv(gu, true, nt, st, opt.map_cache)) != cudaSuccess) return err;
-  if (ws.timing) cudaEventRecord(ws.timing[1], st);
+  if (ws.timing) record_timing(ws.timing[1], st);
   if ((err = launch_swiglu_quant(ws.gate, ws.up, I, R, ws.wt, c.swiglu_limit, ws.qy, ws.qys,
                                  nullptr, st)) != cudaSuccess)
     return err;
@@ -930,9 +936,9 @@ cudaError_t moe_forward_local(const MoeConfig& c, const MoeWeights& w, const Moe
   dn.Y[0] = ws.routed;
   dn.items = ws.items_dn; dn.n_items = ws.counters; dn.max_items = R; dn.n_mats = n_local;
   dn.err = opt.err;
-  if (ws.timing) cudaEventRecord(ws.timing[2], st);
+  if (ws.timing) record_timing(ws.timing[2], st);
   if ((err = launch_fp4_gemv(dn, false, nt, st, opt.map_cache)) != cudaSuccess) return err;
-  if (ws.timing) cudaEventRecord(ws.timing[3], st);
+  if (ws.timing) record_timing(ws.timing[3], st);
 
   if (side) cudaStreamWaitEvent(st, side->join, 0);
   return cudaGetLastError();

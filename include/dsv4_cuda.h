@@ -207,6 +207,11 @@ int dsv4cuda_moe_route(dsv4cuda_moe_layer *L, const float *x, const int *token_i
 int dsv4cuda_moe_timing_begin(dsv4cuda_moe_layer *L);
 int dsv4cuda_moe_timing_end(dsv4cuda_moe_layer *L, int *n_forwards, float *gateup_ms,
                             float *down_ms);
+/* Reads event group `index` (0 = the first forward since _begin) without
+ * ending the timing: for forwards captured into a CUDA graph, whose event
+ * nodes are re-recorded by every replay. */
+int dsv4cuda_moe_timing_read(dsv4cuda_moe_layer *L, int index, float *gateup_ms, float *down_ms,
+                             float *logits_ms, float *select_ms);
 /* Same, also returning the summed router logit and selection milliseconds. */
 int dsv4cuda_moe_timing_end2(dsv4cuda_moe_layer *L, int *n_forwards, float *gateup_ms,
                              float *down_ms, float *logits_ms, float *select_ms);
