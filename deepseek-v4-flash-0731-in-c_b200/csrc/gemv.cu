@@ -1039,6 +1039,303 @@ bool fp4_maps(Fp4Maps* m, const Fp4GemvArgs& a, bool pair, long long n_mats, boo
   return true;
 }
 
+// -------------------------------------------------------- FP8 stream ----
+// Streaming form of the FP8 GEMV (the shared expert, dense projections) for
+// one matrix or a pair: in % 256 == 0, at most 64 128-column blocks. Each
+// warp owns a tile of 32 rows (lane = row) and walks it in 256-column chunks
+// (two 128-column blocks): one elected lane loads two [32 rows x 128 B]
+// 128-byte-swizzled TMA boxes, the chunk's activations and their scales into
+// a per-warp ring of kF8Stages stages. Each lane runs the two blocks'
+// 128-long fmaf chains interleaved and folds them in column order
+// (dsv4_model.c:571-676). The tile's 32 rows share one row of
+// [128 x 128]-block E8M0 codes, held one per lane and fetched by shuffle.
+constexpr int kF8Cols = 256;
+constexpr int kF8Stages = 4;
+
+template <int NT>
+struct F8Layout {
+  static constexpr int kW = 2 * 32 * 128;          // two swizzled [32][128 B] boxes
+  static constexpr int kA = NT * kF8Cols * 2;      // activations (f16)
+  static constexpr int kQ = NT * 16;               // 4 activation scales covering the chunk
+  static constexpr int kStage = (kW + kA + kQ + 1023) / 1024 * 1024;
+  static constexpr int kWarpBytes = kF8Stages * kStage;
+};
+
+struct Fp8Maps {
+  CUtensorMap w[2];  // [rows][in] bytes, box [32][128], 128B swizzle
+};
+
+// Two 32-value pieces of two independent 128-long chains.
+__device__ __forceinline__ void fp8_step32x2(const uint32_t* wa, const uint32_t* xa,
+                                             const uint32_t* wb, const uint32_t* xb, float& pa,
+                                             float& pb) {
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    uint32_t a0, a1, b0, b1;
+    asm("{ .reg .b16 lo, hi; mov.b32 {lo, hi}, %2; cvt.rn.f16x2.e4m3x2 %0, lo;"
+        " cvt.rn.f16x2.e4m3x2 %1, hi; }"
+        : "=r"(a0), "=r"(a1) : "r"(wa[i]));
+    asm("{ .reg .b16 lo, hi; mov.b32 {lo, hi}, %2; cvt.rn.f16x2.e4m3x2 %0, lo;"
+        " cvt.rn.f16x2.e4m3x2 %1, hi; }"
+        : "=r"(b0), "=r"(b1) : "r"(wb[i]));
+    pa = fma_h_lo(a0, xa[2 * i], pa);
+    pb = fma_h_lo(b0, xb[2 * i], pb);
+    pa = fma_h_hi(a0, xa[2 * i], pa);
+    pb = fma_h_hi(b0, xb[2 * i], pb);
+    pa = fma_h_lo(a1, xa[2 * i + 1], pa);
+    pb = fma_h_lo(b1, xb[2 * i + 1], pb);
+    pa = fma_h_hi(a1, xa[2 * i + 1], pa);
+    pb = fma_h_hi(b1, xb[2 * i + 1], pb);
+  }
+}
+
+template <int NT, int WARPS>
+__global__ void __launch_bounds__(WARPS * 32, 1)
+    fp8_stream_kernel(const __grid_constant__ Fp8Maps maps, const Fp8GemvArgs a, int pair,
+                      unsigned int* err) {
+  using L = F8Layout<NT>;
+  extern __shared__ __align__(1024) unsigned char smem[];
+  __shared__ float e8m0_tbl[256];
+  __shared__ uint64_t bars_all[WARPS][kF8Stages];
+  fill_e8m0_skip_table(e8m0_tbl);
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  unsigned char* const sbase = smem + ((1024u - (smem_addr(smem) & 1023u)) & 1023u);
+  unsigned char* wbase = sbase + warp * L::kWarpBytes;
+  uint64_t* bars = bars_all[warp];
+  if (lane == 0) {
+#pragma unroll
+    for (int s = 0; s < kF8Stages; ++s) mbar_init(&bars[s], 1);
+    mbar_fence_init();
+    if (warp == 0) {
+      tma_prefetch_desc(&maps.w[0]);
+      if (pair) tma_prefetch_desc(&maps.w[1]);
+    }
+  }
+  __syncthreads();
+
+  const int n_items = load_n_items(a.n_items, a.max_items);
+  const int V = pair ? 2 : 1;
+  const int rblocks = a.rows / 32;
+  const int per_item = V * rblocks;
+  const long long tiles = static_cast<long long>(n_items) * per_item;
+  const int CPT = a.in / kF8Cols;
+  const int CB = a.in / 128;
+  const long long nwarps = static_cast<long long>(gridDim.x) * WARPS;
+  const long long first = static_cast<long long>(warp) * gridDim.x + blockIdx.x;
+  const long long my_tiles = tiles > first ? (tiles - first + nwarps - 1) / nwarps : 0;
+  const long long jobs = my_tiles * CPT;
+  const int sld = (a.act.ld + 127) >> 7;
+
+  struct Cursor {
+    int chunk = 0, tile_n = 0, item = 0, v = 0, rb = 0, ntok = 0;
+    int tx[NT], ty[NT];
+  };
+  auto decode = [&](Cursor& c) {
+    if (c.tile_n >= my_tiles) return;
+    const int tile = static_cast<int>(first + static_cast<long long>(c.tile_n) * nwarps);
+    c.item = tile / per_item;
+    const int rem = tile - c.item * per_item;
+    c.v = rem / rblocks;
+    c.rb = rem - c.v * rblocks;
+    const GemvItem& it = a.items[c.item];
+    c.ntok = it.ntok;
+#pragma unroll
+    for (int t = 0; t < NT; ++t) {
+      const int tt = (NT == 1 || t < c.ntok) ? t : 0;
+      c.tx[t] = it.tok[tt].x;
+      c.ty[t] = it.tok[tt].y;
+    }
+  };
+  auto advance = [&](Cursor& c) {
+    if (++c.chunk == CPT) {
+      c.chunk = 0;
+      ++c.tile_n;
+      decode(c);
+    }
+  };
+  Cursor ic;
+  decode(ic);
+  int stage_i = 0;
+  auto issue = [&]() {
+    if (lane == 0) {
+      unsigned char* st = wbase + stage_i * L::kStage;
+      mbar_arrive_expect_tx(&bars[stage_i],
+                            static_cast<uint32_t>(L::kW + ic.ntok * (kF8Cols * 2 + 16)));
+      const CUtensorMap* wm = ic.v ? &maps.w[1] : &maps.w[0];
+      const int y = ic.rb * 32;
+      tma_load_2d(st, wm, ic.chunk * kF8Cols, y, &bars[stage_i]);
+      tma_load_2d(st + L::kW / 2, wm, ic.chunk * kF8Cols + 128, y, &bars[stage_i]);
+#pragma unroll
+      for (int t = 0; t < NT; ++t) {
+        if (NT == 1 || t < ic.ntok) {
+          bulk_g2s(st + L::kW + t * kF8Cols * 2,
+                   a.act.x + static_cast<size_t>(ic.tx[t]) * a.act.ld + ic.chunk * kF8Cols,
+                   kF8Cols * 2, &bars[stage_i]);
+          // blocks 2c, 2c+1 lie in the 16-byte run of scales starting at block 4 floor(c/2)
+          bulk_g2s(st + L::kW + L::kA + t * 16,
+                   a.act.s + static_cast<size_t>(ic.tx[t]) * sld + (ic.chunk >> 1) * 4, 16,
+                   &bars[stage_i]);
+        }
+      }
+    }
+    advance(ic);
+    stage_i = stage_i + 1 == kF8Stages ? 0 : stage_i + 1;
+  };
+
+  float acc[NT];
+#pragma unroll
+  for (int t = 0; t < NT; ++t) acc[t] = 0.0f;
+  for (long long j = 0; j < jobs && j < kF8Stages; ++j) issue();
+  __syncwarp();
+  Cursor cc;
+  decode(cc);
+  // the tile's row of block scale codes: lane l holds blocks l and l + 32
+  uint32_t code_lo = 0, code_hi = 0;
+  int codes_tile = -1, codes_v = -1;
+  bool ok = true;
+  long long j = 0;
+  int s = 0;
+  uint32_t phase = 0;
+  for (; j < jobs; ++j) {
+    if (cc.tile_n != codes_tile || cc.v != codes_v) {
+      const uint8_t* srow = a.S[cc.v] + static_cast<size_t>(cc.rb * 32 / 128) * CB;
+      code_lo = lane < CB ? srow[lane] : 255u;
+      code_hi = lane + 32 < CB ? srow[lane + 32] : 255u;
+      codes_tile = cc.tile_n;
+      codes_v = cc.v;
+    }
+    if (!mbar_wait(&bars[s], phase, err)) { ok = false; break; }
+    const int chunk = cc.chunk;
+    const int ntok = cc.ntok;
+    const unsigned char* st = wbase + s * L::kStage;
+    const unsigned char* wrow = st + lane * 128;
+    const int sw = lane & 7;
+    const int b0 = 2 * chunk, b1 = b0 + 1;
+    const uint32_t c0 = __shfl_sync(0xffffffffu, b0 < 32 ? code_lo : code_hi, b0 & 31);
+    const uint32_t c1 = __shfl_sync(0xffffffffu, b1 < 32 ? code_lo : code_hi, b1 & 31);
+    const float ws0 = e8m0_tbl[c0], ws1 = e8m0_tbl[c1];
+    float p0[NT], p1[NT];
+#pragma unroll
+    for (int t = 0; t < NT; ++t) { p0[t] = 0.f; p1[t] = 0.f; }
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {  // 32-column pieces of both blocks
+      uint32_t wa[8], wb[8];
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int ca = 2 * q + h;  // 16-byte chunk index within the 128-byte block row
+        const uint4 va = *reinterpret_cast<const uint4*>(wrow + ((ca ^ sw) << 4));
+        const uint4 vb = *reinterpret_cast<const uint4*>(wrow + L::kW / 2 + ((ca ^ sw) << 4));
+        wa[4 * h] = va.x; wa[4 * h + 1] = va.y; wa[4 * h + 2] = va.z; wa[4 * h + 3] = va.w;
+        wb[4 * h] = vb.x; wb[4 * h + 1] = vb.y; wb[4 * h + 2] = vb.z; wb[4 * h + 3] = vb.w;
+      }
+#pragma unroll
+      for (int t = 0; t < NT; ++t) {
+        if (NT == 1 || t < ntok) {
+          const uint4* xa4 = reinterpret_cast<const uint4*>(st + L::kW + t * kF8Cols * 2 + q * 64);
+          const uint4* xb4 = reinterpret_cast<const uint4*>(st + L::kW + t * kF8Cols * 2 + 256 + q * 64);
+          uint32_t xa[16], xb[16];
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const uint4 u = xa4[k], w = xb4[k];
+            xa[4 * k] = u.x; xa[4 * k + 1] = u.y; xa[4 * k + 2] = u.z; xa[4 * k + 3] = u.w;
+            xb[4 * k] = w.x; xb[4 * k + 1] = w.y; xb[4 * k + 2] = w.z; xb[4 * k + 3] = w.w;
+          }
+          fp8_step32x2(wa, xa, wb, xb, p0[t], p1[t]);
+        }
+      }
+    }
+#pragma unroll
+    for (int t = 0; t < NT; ++t) {
+      if (NT == 1 || t < ntok) {
+        const float* qv = reinterpret_cast<const float*>(st + L::kW + L::kA + t * 16);
+        const float q0 = qv[(2 * chunk) & 3], q1 = qv[(2 * chunk + 1) & 3];
+        // a NaN block scale (code 255) skips the block, as the reference does
+        if (c0 != 255u) acc[t] = fmaf(p0[t], q0 * ws0, acc[t]);
+        if (c1 != 255u) acc[t] = fmaf(p1[t], q1 * ws1, acc[t]);
+      }
+    }
+    if (chunk == CPT - 1) {
+      const int row = cc.rb * 32 + lane;
+      float* Yv = cc.v ? a.Y[1] : a.Y[0];
+#pragma unroll
+      for (int t = 0; t < NT; ++t)
+        if (NT == 1 || t < ntok)
+          Yv[static_cast<size_t>(cc.ty[t]) * a.rows + row] =
+              a.round_out ? bf16_round(acc[t]) : acc[t];
+#pragma unroll
+      for (int t = 0; t < NT; ++t) acc[t] = 0.0f;
+    }
+    __syncwarp();
+    if (j + kF8Stages < jobs) issue();
+    __syncwarp();
+    advance(cc);
+    if (++s == kF8Stages) {
+      s = 0;
+      phase ^= 1u;
+    }
+  }
+  if (!ok) {
+    uint32_t ph = phase;
+    int k = s;
+    for (long long q = j + 1; q < jobs && q < j + kF8Stages; ++q) {
+      if (++k == kF8Stages) { k = 0; ph ^= 1u; }
+      mbar_wait(&bars[k], ph, err);
+    }
+  }
+}
+
+template <int NT, int WARPS>
+cudaError_t launch_fp8_stream_nt(const Fp8Maps& maps, const Fp8GemvArgs& a, bool pair,
+                                 cudaStream_t st) {
+  const size_t smem = static_cast<size_t>(WARPS) * F8Layout<NT>::kWarpBytes + 1024;
+  static bool attr_done = false;  // per template instance
+  if (!attr_done) {
+    cudaError_t e = cudaFuncSetAttribute(fp8_stream_kernel<NT, WARPS>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(smem));
+    if (e != cudaSuccess) return e;
+    attr_done = true;
+  }
+  const long long tiles = static_cast<long long>(a.max_items) * (pair ? 2 : 1) * (a.rows / 32);
+  const int grid = static_cast<int>(std::max<long long>(
+      1, std::min<long long>(sm_count(), (tiles + WARPS - 1) / WARPS)));
+  fp8_stream_kernel<NT, WARPS><<<grid, WARPS * 32, smem, st>>>(maps, a, pair ? 1 : 0,
+                                                               device_error_word());
+  return cudaGetLastError();
+}
+
+// Returns cudaErrorNotSupported when the shape or alignment does not fit
+// the streaming kernel (the caller then uses the LDG kernel).
+cudaError_t launch_fp8_stream(const Fp8GemvArgs& a, bool pair, int nt, cudaStream_t st) {
+  const int CB = a.in / 128;
+  if (a.in % kF8Cols != 0 || CB > 64 || a.rows % 32 != 0 || a.act.ld % 512 != 0 ||
+      a.act.x32 || !aligned(a.W[0], 16) || !aligned(a.act.x, 16) || !aligned(a.act.s, 16) ||
+      (pair && !aligned(a.W[1], 16)))
+    return cudaErrorNotSupported;
+  // the item list names one matrix (or pair): every item's mat must be 0
+  Fp8Maps maps;
+  for (int v = 0; v < (pair ? 2 : 1); ++v)
+    if (!make_tma_map_u8(&maps.w[v], a.W[v], static_cast<uint64_t>(a.in), a.rows, 128, 32, true,
+                         true))
+      return cudaErrorNotSupported;
+  if (!pair) maps.w[1] = maps.w[0];
+  // Few tiles (one expert): spread them one or two warps per SM, so the
+  // per-lane fmaf chains of each tile get a whole SM's issue slots.
+  const long long tiles = static_cast<long long>(a.max_items) * (pair ? 2 : 1) * (a.rows / 32);
+  const bool two = tiles > sm_count();
+  switch (nt) {
+    case 1: return two ? launch_fp8_stream_nt<1, 2>(maps, a, pair, st)
+                       : launch_fp8_stream_nt<1, 1>(maps, a, pair, st);
+    case 2: return two ? launch_fp8_stream_nt<2, 2>(maps, a, pair, st)
+                       : launch_fp8_stream_nt<2, 1>(maps, a, pair, st);
+    case 3:
+    case 4: return two ? launch_fp8_stream_nt<4, 2>(maps, a, pair, st)
+                       : launch_fp8_stream_nt<4, 1>(maps, a, pair, st);
+    default: return two ? launch_fp8_stream_nt<8, 2>(maps, a, pair, st)
+                        : launch_fp8_stream_nt<8, 1>(maps, a, pair, st);
+  }
+}
+
 cudaError_t launch_fp4_stream(const Fp4GemvArgs& a, bool pair, int nt, cudaStream_t st,
                               bool map_cache) {
   Fp4Maps maps;
@@ -1104,6 +1401,10 @@ cudaError_t launch_fp8_gemv(const Fp8GemvArgs& a, bool pair, int item_tokens, cu
     for (int p = 0; p < (pair ? 2 : 1); ++p)
       fp8_gemv_scalar_kernel<<<grid, 256, 0, st>>>(a, p);
     return cudaGetLastError();
+  }
+  {
+    cudaError_t e = launch_fp8_stream(a, pair, item_tokens, st);
+    if (e != cudaErrorNotSupported) return e;
   }
   const int CB = a.in / 128;
   int lpr = pick_lpr(static_cast<long long>(a.max_items) * a.rows, 2 * CB);
