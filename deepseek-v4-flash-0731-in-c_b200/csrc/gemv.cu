@@ -28,6 +28,7 @@
 #include "bulk.cuh"
 #include "dsv4_common.cuh"
 #include "gemv.cuh"
+#include "launch.cuh"
 
 namespace dsv4 {
 
@@ -431,6 +432,8 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
     }
   }
   __syncthreads();
+  pdl_wait();  // the item list and activations come from the previous kernels
+  pdl_trigger();
 
   const int n_items = load_n_items(a.n_items, a.max_items);
   const int V = pair ? 2 : 1;
@@ -892,6 +895,8 @@ __global__ void quant_fp8_kernel(const float* x, int ldx, int n, int rows, __hal
 __global__ void swiglu_quant_kernel(const float* gate, const float* up, int n, int rows,
                                     const float* weight, int limit, __half* qy, float* qs,
                                     float* ybf) {
+  pdl_wait();
+  pdl_trigger();
   const int lane = threadIdx.x & 31;
   const int nb = (n + 127) / 128;
   const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
@@ -1016,8 +1021,8 @@ cudaError_t launch_stream_nt(const Fp4Maps& maps, const Fp4GemvArgs& a, bool pai
       1, std::min<long long>(sm_count(), (tiles + WARPS - 1) / WARPS)));
   Fp4GemvArgs b = a;
   if (!b.err) b.err = device_error_word();
-  fp4_stream_kernel<NT, WARPS><<<grid, WARPS * 32, smem, st>>>(maps, b, pair ? 1 : 0);
-  return cudaGetLastError();
+  return launch_pdl(fp4_stream_kernel<NT, WARPS>, dim3(grid), dim3(WARPS * 32), smem, st, maps, b,
+                    pair ? 1 : 0);
 }
 
 // Tensor maps over every matrix of the launch: rows_total = rows of all
@@ -1112,6 +1117,8 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
     }
   }
   __syncthreads();
+  pdl_wait();
+  pdl_trigger();
 
   const int n_items = load_n_items(a.n_items, a.max_items);
   const int V = pair ? 2 : 1;
@@ -1299,9 +1306,8 @@ cudaError_t launch_fp8_stream_nt(const Fp8Maps& maps, const Fp8GemvArgs& a, bool
   const long long tiles = static_cast<long long>(a.max_items) * (pair ? 2 : 1) * (a.rows / 32);
   const int grid = static_cast<int>(std::max<long long>(
       1, std::min<long long>(sm_count(), (tiles + WARPS - 1) / WARPS)));
-  fp8_stream_kernel<NT, WARPS><<<grid, WARPS * 32, smem, st>>>(maps, a, pair ? 1 : 0,
-                                                               device_error_word());
-  return cudaGetLastError();
+  return launch_pdl(fp8_stream_kernel<NT, WARPS>, dim3(grid), dim3(WARPS * 32), smem, st, maps, a,
+                    pair ? 1 : 0, device_error_word());
 }
 
 // Returns cudaErrorNotSupported when the shape or alignment does not fit
@@ -1464,9 +1470,8 @@ cudaError_t launch_swiglu_quant(const float* gate, const float* up, int n, int r
                                 float* y_bf16, cudaStream_t st) {
   const long long warps = static_cast<long long>(rows) * ((n + 127) / 128);
   if (warps <= 0) return cudaSuccess;
-  swiglu_quant_kernel<<<blocks_for_warps(warps), 128, 0, st>>>(gate, up, n, rows, weight,
-                                                               limit, qy, qs, y_bf16);
-  return cudaGetLastError();
+  return launch_pdl(swiglu_quant_kernel, dim3(blocks_for_warps(warps)), dim3(128), 0, st, gate,
+                    up, n, rows, weight, limit, qy, qs, y_bf16);
 }
 
 cudaError_t launch_f32_to_f16(const float* x, __half* y, size_t n, cudaStream_t st) {

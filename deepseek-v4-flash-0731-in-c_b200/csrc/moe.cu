@@ -22,6 +22,7 @@
 
 #include "dsv4_common.cuh"
 #include "moe.cuh"
+#include "launch.cuh"
 
 namespace dsv4 {
 
@@ -264,8 +265,13 @@ __device__ __forceinline__ float warp_segment_abs(const SegState& st, int c_begi
 // products), so
 //   zb = u sum|t_i| + (d + 1) u P (1 + n u) (+ u P)   (x 1.01 for the fp32
 // evaluation of the bound itself).
+__device__ void write_shared_items(const RouterArgs& a);
+
 __global__ void __launch_bounds__(kLogitWarps * 32) router_logits_kernel(const RouterArgs a) {
   __shared__ float seg_tot[kLogitWarps], seg_abs[kLogitWarps], seg_p[kLogitWarps];
+  pdl_wait();  // x comes from the previous kernel
+  pdl_trigger();
+  if (a.items_sh && blockIdx.x == 0 && blockIdx.y == 0) write_shared_items(a);
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int e = blockIdx.x, t = blockIdx.y;
   if (a.xq) {
@@ -439,7 +445,6 @@ __device__ void block_plan(const RouterArgs& a, int* cnt, int* ids) {
     if (static_cast<int>(threadIdx.x) < E) cnt[threadIdx.x] = off;
     if (threadIdx.x == 0) {
       a.counters[0] = total;
-      a.counters[3] = (a.M + kItemTok - 1) / kItemTok;
     }
   } else if (threadIdx.x < 32) {
     // exclusive scan of cnt[0..E) by one warp: 32-element tiles with a carry
@@ -458,7 +463,6 @@ __device__ void block_plan(const RouterArgs& a, int* cnt, int* ids) {
     }
     if (threadIdx.x == 0) {
       a.counters[0] = carry;
-      a.counters[3] = (a.M + kItemTok - 1) / kItemTok;
     }
   }
   __syncthreads();
@@ -488,6 +492,12 @@ __device__ void block_plan(const RouterArgs& a, int* cnt, int* ids) {
       a.items_dn[item] = dn;
     }
   }
+}
+
+// Shared-expert items (every token, in groups of kItemTok); they depend on M
+// only, so the logit kernel writes them and the shared expert can start
+// before the selection finishes.
+__device__ void write_shared_items(const RouterArgs& a) {
   const int nsh = (a.M + kItemTok - 1) / kItemTok;
   for (int j = threadIdx.x; j < nsh; j += blockDim.x) {
     GemvItem it;
@@ -500,6 +510,7 @@ __device__ void block_plan(const RouterArgs& a, int* cnt, int* ids) {
     }
     a.items_sh[j] = it;
   }
+  if (threadIdx.x == 0) a.counters[3] = nsh;
 }
 
 constexpr int kReplayRows = 4;  // candidate gate rows staged per replay round
@@ -561,6 +572,8 @@ __global__ void __launch_bounds__(kSelThreads) router_select_kernel(const Router
   __shared__ int is_last, n_cand;
   SelectSmem sm;
   select_smem_bytes(a.H, a.E, a.M * a.topk, &sm, ssm);
+  pdl_wait();  // the logits and bounds come from router_logits_kernel
+  pdl_trigger();
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int t = blockIdx.x;
   const int E = a.E;
@@ -694,6 +707,8 @@ __global__ void __launch_bounds__(kSelThreads) router_select_kernel(const Router
 __global__ void moe_combine_kernel(const float* __restrict__ routed, const float* __restrict__ shared,
                                    const int* __restrict__ idx, int n_tokens, int topk, int H,
                                    float* __restrict__ out) {
+  pdl_wait();
+  pdl_trigger();
   const size_t n = static_cast<size_t>(n_tokens) * H;
   for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n;
        i += static_cast<size_t>(gridDim.x) * blockDim.x) {
@@ -789,9 +804,9 @@ void moe_workspace_carve(MoeWorkspace* ws, const MoeConfig& c, int M, void* base
   ws->bytes = static_cast<size_t>(p - static_cast<char*>(base));
 }
 
-static cudaError_t route_impl(const MoeConfig& c, const MoeWeights& w, const MoeWorkspace& ws,
-                              const float* x, const int* token_ids, int M, int public_router,
-                              bool plan, cudaStream_t st) {
+static RouterArgs make_router_args(const MoeConfig& c, const MoeWeights& w, const MoeWorkspace& ws,
+                            const float* x, const int* token_ids, int M, int public_router,
+                            bool plan) {
   RouterArgs a{};
   a.x = x;
   a.H = c.hidden;
@@ -819,9 +834,25 @@ static cudaError_t route_impl(const MoeConfig& c, const MoeWeights& w, const Moe
     a.items_dn = ws.items_dn;
     a.items_sh = ws.items_sh;
   }
+  return a;
+}
+
+// Launch 1 of the router: logits, bounds, activation quant, shared items.
+cudaError_t route_logits(const RouterArgs& a, const MoeConfig& c, const MoeWorkspace& ws, int M,
+                         bool plan, cudaStream_t st) {
   if (plan && ws.timing) record_timing(ws.timing[4], st);
-  router_logits_kernel<<<dim3(c.n_experts, M), kLogitWarps * 32, 0, st>>>(a);
+  {
+    cudaError_t e = launch_pdl(router_logits_kernel, dim3(c.n_experts, M), dim3(kLogitWarps * 32),
+                               0, st, a);
+    if (e != cudaSuccess) return e;
+  }
   if (plan && ws.timing) record_timing(ws.timing[5], st);
+  return cudaSuccess;
+}
+
+// Launch 2: selection, weights and the expert plan.
+cudaError_t route_select(const RouterArgs& a, const MoeConfig& c, const MoeWorkspace& ws, int M,
+                         bool plan, cudaStream_t st) {
   const size_t smem = select_smem_bytes(c.hidden, c.n_experts, M * c.topk, nullptr, nullptr);
   if (smem > 48 * 1024) {
     cudaError_t e = cudaFuncSetAttribute(router_select_kernel,
@@ -829,9 +860,20 @@ static cudaError_t route_impl(const MoeConfig& c, const MoeWeights& w, const Moe
                                          static_cast<int>(smem));
     if (e != cudaSuccess) return e;
   }
-  router_select_kernel<<<M, kSelThreads, smem, st>>>(a);
+  {
+    cudaError_t e = launch_pdl(router_select_kernel, dim3(M), dim3(kSelThreads), smem, st, a);
+    if (e != cudaSuccess) return e;
+  }
   if (plan && ws.timing) record_timing(ws.timing[6], st);
   return cudaGetLastError();
+}
+
+cudaError_t route_impl(const MoeConfig& c, const MoeWeights& w, const MoeWorkspace& ws,
+                       const float* x, const int* token_ids, int M, int public_router, bool plan,
+                       cudaStream_t st) {
+  const RouterArgs a = make_router_args(c, w, ws, x, token_ids, M, public_router, plan);
+  cudaError_t e = route_logits(a, c, ws, M, plan, st);
+  return e != cudaSuccess ? e : route_select(a, c, ws, M, plan, st);
 }
 
 cudaError_t moe_route(const MoeConfig& c, const MoeWeights& w, const MoeWorkspace& ws,
@@ -858,8 +900,9 @@ cudaError_t moe_forward_local(const MoeConfig& c, const MoeWeights& w, const Moe
       (err = cudaMemsetAsync(ws.routed, 0, sizeof(float) * R * H, st)) != cudaSuccess)
     return err;
 
-  // router: quant + exact logits + selection + expert plan, one launch
-  if ((err = route_impl(c, w, ws, x, token_ids, M, 0, true, st)) != cudaSuccess) return err;
+  // router launch 1: activation quant + logits (+ the shared-expert items)
+  const RouterArgs ra = make_router_args(c, w, ws, x, token_ids, M, 0, true);
+  if ((err = route_logits(ra, c, ws, M, true, st)) != cudaSuccess) return err;
   const QAct act{ws.xq, ws.xs, H, nullptr};
 
   const bool has_shared = c.shared_kind != kSharedNone && w.sh1 != nullptr;
@@ -912,6 +955,9 @@ cudaError_t moe_forward_local(const MoeConfig& c, const MoeWeights& w, const Moe
     if (side) cudaEventRecord(side->join, side->s);
   }
 
+  // router launch 2: selection and the routed expert plan (overlaps the
+  // shared expert on the side stream)
+  if ((err = route_select(ra, c, ws, M, true, st)) != cudaSuccess) return err;
 
   const int nt = nt_bucket(std::min(M, kItemTok));
   const size_t w13 = static_cast<size_t>(I) * (H / 2), s13 = static_cast<size_t>(I) * (H / 32);
@@ -950,9 +996,10 @@ cudaError_t moe_combine(const MoeConfig& c, const MoeWorkspace& ws, int M, float
   const int H = c.hidden, K = c.topk;
   const size_t n = static_cast<size_t>(M) * H;
   const int grid = static_cast<int>(std::min<size_t>((n + 255) / 256, 2048));
-  moe_combine_kernel<<<grid, 256, 0, st>>>(ws.routed, has_shared ? ws.shared : nullptr, ws.idx,
-                                           M, K, H, out);
-  return cudaGetLastError();
+  return launch_pdl(moe_combine_kernel, dim3(grid), dim3(256), 0, st,
+                    static_cast<const float*>(ws.routed),
+                    static_cast<const float*>(has_shared ? ws.shared : nullptr),
+                    static_cast<const int*>(ws.idx), M, K, H, out);
 }
 
 cudaError_t moe_forward(const MoeConfig& c, const MoeWeights& w, const MoeWorkspace& ws,
