@@ -604,30 +604,95 @@ __global__ void __launch_bounds__(kSelThreads) router_select_kernel(const Router
     }
     __syncthreads();
   } else {
-    warp_topk(sm.choice, sm.used, E, a.topk, order);
-    double mlo = INFINITY, mhi = -INFINITY;
-    int nan_seen = 0;
-    for (int e = threadIdx.x; e < E; e += blockDim.x) {
-      if (isnan(sm.lo[e]) || isnan(sm.hi[e])) nan_seen = 1;
-      if (sm.used[e]) mlo = fmin(mlo, sm.lo[e]);
-      else mhi = fmax(mhi, sm.hi[e]);
-    }
+    __shared__ int s_replay, s_nan;
+    __shared__ double s_mlo, s_mhi;
+    if (E <= 8 * 32) {
+      // warp 0 holds every expert's choice and interval in registers (lane l:
+      // experts l + 32 i): top-k and the margin check without block barriers
+      if (warp == 0) {
+        float cv[8];
+        double lo[8], hi[8];
+        bool nan_seen = false;
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      mlo = fmin(mlo, __shfl_xor_sync(0xffffffffu, mlo, o));
-      mhi = fmax(mhi, __shfl_xor_sync(0xffffffffu, mhi, o));
+        for (int i = 0; i < 8; ++i) {
+          const int e = lane + 32 * i;
+          const bool in = e < E;
+          cv[i] = in ? sm.choice[e] : -INFINITY;
+          lo[i] = in ? sm.lo[e] : INFINITY;
+          hi[i] = in ? sm.hi[e] : -INFINITY;
+          if (in && (isnan(lo[i]) || isnan(hi[i]))) nan_seen = true;
+        }
+        uint32_t used = 0u;  // bit i: expert lane + 32 i was picked
+        for (int j = 0; j < a.topk; ++j) {
+          uint32_t bk = 0u;
+          int bi = 0x7FFFFFFF;
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {  // ascending ids within the lane
+            const uint32_t key = ((used >> i) & 1u) ? 0u : sel_key(cv[i]);
+            if (key > bk) { bk = key; bi = lane + 32 * i; }
+          }
+          const uint32_t mk = __reduce_max_sync(0xffffffffu, bk);
+          const int id = static_cast<int>(__reduce_min_sync(
+              0xffffffffu, static_cast<unsigned>((bk == mk) ? bi : 0x7FFFFFFF)));
+          const int pick = mk == 0u ? -1 : id;
+          if (pick >= 0 && (pick & 31) == lane) used |= 1u << (pick >> 5);
+          if (lane == 0) order[j] = pick;
+        }
+        double mlo = INFINITY, mhi = -INFINITY;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          if ((used >> i) & 1u) mlo = fmin(mlo, lo[i]);
+          else mhi = fmax(mhi, hi[i]);
+          const int e = lane + 32 * i;
+          if (e < E) sm.used[e] = static_cast<unsigned char>((used >> i) & 1u);
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+          mlo = fmin(mlo, __shfl_xor_sync(0xffffffffu, mlo, o));
+          mhi = fmax(mhi, __shfl_xor_sync(0xffffffffu, mhi, o));
+        }
+        const bool any_nan = __any_sync(0xffffffffu, nan_seen);
+        if (lane == 0) {
+          s_nan = any_nan ? 1 : 0;
+          s_replay = (any_nan || !(mlo > mhi)) ? 1 : 0;
+          s_mlo = mlo;
+          s_mhi = mhi;
+        }
+      }
+      __syncthreads();
+    } else {
+      warp_topk(sm.choice, sm.used, E, a.topk, order);
+      double mlo = INFINITY, mhi = -INFINITY;
+      int nan_seen = 0;
+      for (int e = threadIdx.x; e < E; e += blockDim.x) {
+        if (isnan(sm.lo[e]) || isnan(sm.hi[e])) nan_seen = 1;
+        if (sm.used[e]) mlo = fmin(mlo, sm.lo[e]);
+        else mhi = fmax(mhi, sm.hi[e]);
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        mlo = fmin(mlo, __shfl_xor_sync(0xffffffffu, mlo, o));
+        mhi = fmax(mhi, __shfl_xor_sync(0xffffffffu, mhi, o));
+      }
+      if (lane == 0) { rlo[warp] = mlo; rhi[warp] = mhi; }
+      const int any_nan = __syncthreads_or(nan_seen);
+      if (threadIdx.x == 0) {
+        for (int w = 1; w < static_cast<int>(blockDim.x >> 5); ++w) {
+          mlo = fmin(mlo, rlo[w]);
+          mhi = fmax(mhi, rhi[w]);
+        }
+        s_nan = any_nan;
+        s_replay = (any_nan || !(mlo > mhi)) ? 1 : 0;
+        s_mlo = mlo;
+        s_mhi = mhi;
+      }
+      __syncthreads();
     }
-    if (lane == 0) { rlo[warp] = mlo; rhi[warp] = mhi; }
-    const int any_nan = __syncthreads_or(nan_seen);
-    mlo = rlo[0];
-    mhi = rhi[0];
-    for (int w = 1; w < static_cast<int>(blockDim.x >> 5); ++w) {
-      mlo = fmin(mlo, rlo[w]);
-      mhi = fmax(mhi, rhi[w]);
-    }
-    if (any_nan || !(mlo > mhi)) {
+    if (s_replay) {
       // near tie: replay the reference's fp32 chain for every expert whose
       // interval reaches into the ambiguous band, then select again
+      const int any_nan = s_nan;
+      const double mlo = s_mlo, mhi = s_mhi;
       const float* xr = a.x + static_cast<size_t>(t) * a.H;
       if (threadIdx.x == 0) n_cand = 0;
       for (int i = threadIdx.x; i < a.H; i += blockDim.x) sm.x[i] = xr[i];
@@ -685,8 +750,33 @@ __global__ void __launch_bounds__(kSelThreads) router_select_kernel(const Router
       a.idx[static_cast<size_t>(t) * K + rank] = id;
       a.wt[static_cast<size_t>(t) * K + rank] = w;
     }
+    if (a.items_gu && gridDim.x == 1 && !a.tid2eid) {
+      // single token, distinct picks: one item per local route, in
+      // ascending id order (what block_plan produces for M = 1)
+      if (k < K) order[rank] = id;
+      __syncwarp();
+      const int e = k < K ? order[k] : -1;
+      const bool local = e >= a.elo && e < a.ehi;
+      const unsigned m = __ballot_sync(0xffffffffu, local);
+      if (local) {
+        const int item = __popc(m & ((1u << k) - 1u));
+        GemvItem gu, dn;
+        gu.mat = dn.mat = e - a.elo;
+        gu.ntok = dn.ntok = 1;
+#pragma unroll
+        for (int i = 0; i < kItemTok; ++i) {
+          gu.tok[i].x = 0;
+          gu.tok[i].y = k;
+          dn.tok[i].x = k;
+          dn.tok[i].y = k;
+        }
+        a.items_gu[item] = gu;
+        a.items_dn[item] = dn;
+      }
+      if (lane == 0) a.counters[0] = __popc(m);
+    }
   }
-  if (!a.items_gu) return;
+  if (!a.items_gu || (gridDim.x == 1 && !a.tid2eid)) return;  // no plan, or planned above
   if (gridDim.x == 1) {
     // one token: this CTA wrote every route itself
     __syncthreads();
