@@ -326,6 +326,7 @@ constexpr int kSCols = 512;                  // FP4 columns per stage row
 constexpr int kSRowBytes = kSCols / 2;       // 256
 constexpr int kSGroups = kSCols / 32;        // 16 E8M0 codes per stage row
 constexpr int kStages = 2;
+constexpr size_t kSplitkSmemCap = 227 * 1024 - 2048;  // dynamic bytes beside the static tables
 
 template <int NT>
 struct StreamLayout {
@@ -1342,12 +1343,259 @@ cudaError_t launch_fp8_stream(const Fp8GemvArgs& a, bool pair, int nt, cudaStrea
   }
 }
 
+// ------------------------------------------------- FP4 split-K stream ----
+// Single-token form of the FP4 GEMV with the columns of every 32-row tile
+// split over a CTA's CW compute warps. Warp w streams chunks
+// [w CPT / CW, (w + 1) CPT / CW) of each of the CTA's tiles through its own
+// two-stage TMA ring (as fp4_stream_kernel does) and writes the 32-column
+// group partials and the rows' E8M0 codes to shared memory; a fold warp then
+// folds each row's partials in column order - the reference's sequential
+// fmaf fold - and writes the row. Two partial buffers let the compute warps
+// fill tile k + 1 while tile k is folded. With the tile's columns spread
+// over the CTA, a launch with few tiles (one expert per GPU under expert
+// parallelism, or a down projection's last wave) still keeps every SM busy.
+template <int CW>
+__global__ void __launch_bounds__((CW + 1) * 32, 1)
+    fp4_splitk_kernel(const __grid_constant__ Fp4Maps maps, const Fp4GemvArgs a, int pair) {
+  using L = StreamLayout<1>;
+  extern __shared__ __align__(1024) unsigned char smem[];
+  __shared__ float e8m0_tbl[256];
+  __shared__ uint64_t sbar[CW][kStages];
+  __shared__ uint64_t full_bar[2], empty_bar[2];
+  __shared__ float qsb[64];
+  __shared__ int abort_flag;
+  fill_e8m0_skip_table(e8m0_tbl);
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  unsigned char* const sbase = smem + ((1024u - (smem_addr(smem) & 1023u)) & 1023u);
+  const int G = a.in / 32, CPT = a.in / kSCols;
+  float* pbuf = reinterpret_cast<float*>(sbase + CW * L::kWarpBytes);  // [2][G][32]
+  uint4* cbuf = reinterpret_cast<uint4*>(pbuf + 2 * G * 32);          // [2][CPT][32]
+  if (threadIdx.x == 0) {
+    for (int w = 0; w < CW; ++w)
+      for (int s = 0; s < kStages; ++s) mbar_init(&sbar[w][s], 1);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&full_bar[s], CW);
+      mbar_init(&empty_bar[s], 1);
+    }
+    abort_flag = 0;
+    mbar_fence_init();
+    tma_prefetch_desc(&maps.w[0]);
+    tma_prefetch_desc(&maps.s[0]);
+    if (pair) {
+      tma_prefetch_desc(&maps.w[1]);
+      tma_prefetch_desc(&maps.s[1]);
+    }
+  }
+  __syncthreads();
+  pdl_wait();
+  pdl_trigger();
+  volatile int* abort_v = &abort_flag;
+  auto wait_bar = [&](uint64_t* bar, uint32_t parity) -> bool {
+    if (mbar_try_wait(bar, parity)) return true;
+    const unsigned long long t0 = global_timer_ns();
+    while (!mbar_try_wait(bar, parity)) {
+      if (*abort_v) return false;
+      if (global_timer_ns() - t0 > kWaitLimitNs) {
+        if (a.err) atomicOr(a.err, 1u);
+        *abort_v = 1;
+        return false;
+      }
+    }
+    return true;
+  };
+
+  const int n_items = load_n_items(a.n_items, a.max_items);
+  const int V = pair ? 2 : 1;
+  const int rblocks = (a.rows + 31) / 32;
+  const int per_item = V * rblocks;
+  const int tiles = n_items * per_item;
+  const int n_my = tiles > static_cast<int>(blockIdx.x)
+                       ? (tiles - static_cast<int>(blockIdx.x) + gridDim.x - 1) / gridDim.x : 0;
+  const int sld = (a.act.ld + 127) >> 7;
+  struct TileInfo {
+    int item, v, rb, mat, tx, ty;
+  };
+  auto tile_info = [&](int k) {
+    TileInfo ti;
+    const int tile = static_cast<int>(blockIdx.x) + k * static_cast<int>(gridDim.x);
+    ti.item = tile / per_item;
+    const int rem = tile - ti.item * per_item;
+    ti.v = rem / rblocks;
+    ti.rb = rem - ti.v * rblocks;
+    const GemvItem& it = a.items[ti.item];
+    ti.mat = it.mat;
+    ti.tx = it.tok[0].x;
+    ti.ty = it.tok[0].y;
+    return ti;
+  };
+
+  if (warp < CW) {
+    // ------------------------------------------------------ compute warp
+    const int c_lo = (warp * CPT) / CW, c_hi = ((warp + 1) * CPT) / CW;
+    const int n_seg = c_hi - c_lo;
+    const int jobs = n_my * n_seg;
+    unsigned char* wbase = sbase + warp * L::kWarpBytes;
+    uint64_t* bars = sbar[warp];
+    // issue cursor
+    int i_k = 0, i_c = c_lo, stage_i = 0;
+    TileInfo i_ti{};
+    if (jobs > 0) i_ti = tile_info(0);
+    auto issue = [&]() {
+      if (lane == 0) {
+        unsigned char* st = wbase + stage_i * L::kStage;
+        mbar_arrive_expect_tx(&bars[stage_i], static_cast<uint32_t>(L::kW + L::kS + kSCols * 2));
+        const int y = i_ti.mat * a.rows + i_ti.rb * 32;
+        const CUtensorMap* wm = i_ti.v ? &maps.w[1] : &maps.w[0];
+        const CUtensorMap* sm = i_ti.v ? &maps.s[1] : &maps.s[0];
+        tma_load_2d(st, wm, i_c * kSRowBytes, y, &bars[stage_i]);
+        tma_load_2d(st + L::kW / 2, wm, i_c * kSRowBytes + 128, y, &bars[stage_i]);
+        tma_load_2d(st + L::kW, sm, i_c * kSGroups, y, &bars[stage_i]);
+        bulk_g2s(st + L::kW + L::kS,
+                 a.act.x + static_cast<size_t>(i_ti.tx) * a.act.ld + i_c * kSCols, kSCols * 2,
+                 &bars[stage_i]);
+      }
+      if (++i_c == c_hi) {
+        i_c = c_lo;
+        if (++i_k < n_my) i_ti = tile_info(i_k);
+      }
+      stage_i = stage_i + 1 == kStages ? 0 : stage_i + 1;
+    };
+    for (int j = 0; j < jobs && j < kStages; ++j) issue();
+    __syncwarp();
+    int k = 0, c = c_lo, s = 0;
+    uint32_t phase = 0;
+    int j = 0;
+    bool ok = true;
+    for (; j < jobs; ++j) {
+      const int slot = k & 1;
+      if (c == c_lo && k >= 2 && !wait_bar(&empty_bar[slot], ((k - 2) >> 1) & 1)) { ok = false; break; }
+      if (!wait_bar(&bars[s], phase)) { ok = false; break; }
+      const unsigned char* st = wbase + s * L::kStage;
+      const unsigned char* wrow = st + lane * 128;
+      const int sw = lane & 7;
+      cbuf[(slot * CPT + c) * 32 + lane] = *reinterpret_cast<const uint4*>(st + L::kW + lane * kSGroups);
+      float* pout = pbuf + (static_cast<size_t>(slot) * G + c * kSGroups) * 32 + lane;
+      const unsigned char* xt = st + L::kW + L::kS;
+#pragma unroll
+      for (int g = 0; g < kSGroups; g += 4) {
+        uint32_t w4[4][4];
+        uint32_t x4[4][16];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const int gq = g + q;
+          const uint4 wv = *reinterpret_cast<const uint4*>(wrow + (gq >> 3) * (L::kW / 2) +
+                                                           (((gq & 7) ^ sw) << 4));
+          w4[q][0] = wv.x; w4[q][1] = wv.y; w4[q][2] = wv.z; w4[q][3] = wv.w;
+          const uint4* xg = reinterpret_cast<const uint4*>(xt + gq * 64);
+#pragma unroll
+          for (int r = 0; r < 4; ++r) {
+            const uint4 u = xg[r];
+            x4[q][4 * r] = u.x; x4[q][4 * r + 1] = u.y; x4[q][4 * r + 2] = u.z; x4[q][4 * r + 3] = u.w;
+          }
+        }
+        float p[4];
+        fp4_partial16x4(w4, x4, p);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) pout[(g + q) * 32] = p[q];
+      }
+      __syncwarp();
+      if (c + 1 == c_hi && lane == 0) mbar_arrive(&full_bar[slot]);
+      if (j + kStages < jobs) issue();
+      __syncwarp();
+      if (++c == c_hi) {
+        c = c_lo;
+        ++k;
+      }
+      if (++s == kStages) {
+        s = 0;
+        phase ^= 1u;
+      }
+    }
+    if (!ok) {
+      uint32_t ph = phase;
+      int q = s;
+      for (int jj = j + 1; jj < jobs && jj < j + kStages; ++jj) {
+        if (++q == kStages) { q = 0; ph ^= 1u; }
+        mbar_wait(&bars[q], ph, a.err);
+      }
+    }
+  } else {
+    // --------------------------------------------------------- fold warp
+    for (int k = 0; k < n_my; ++k) {
+      const int slot = k & 1;
+      const TileInfo ti = tile_info(k);
+      const float* qrow = a.act.s + static_cast<size_t>(ti.tx) * sld;
+      for (int b = lane; b < G / 4; b += 32) qsb[b] = qrow[b];
+      if (!wait_bar(&full_bar[slot], (k >> 1) & 1)) break;
+      __syncwarp();
+      const float* pin = pbuf + static_cast<size_t>(slot) * G * 32 + lane;
+      const unsigned char* cb = reinterpret_cast<const unsigned char*>(cbuf + slot * CPT * 32);
+      float acc = 0.0f;
+      for (int c = 0; c < CPT; ++c) {
+        const uint4 codes = *reinterpret_cast<const uint4*>(cb + (c * 32 + lane) * 16);
+        const uint32_t cw[4] = {codes.x, codes.y, codes.z, codes.w};
+#pragma unroll
+        for (int g = 0; g < kSGroups; ++g) {
+          const int gg = c * kSGroups + g;
+          const float sc = e8m0_tbl[(cw[g >> 2] >> (8 * (g & 3))) & 0xFFu];
+          acc = fmaf(pin[gg * 32], qsb[gg >> 2] * sc, acc);
+        }
+      }
+      const int row = ti.rb * 32 + lane;
+      if (row < a.rows) {
+        float* Yv = ti.v ? a.Y[1] : a.Y[0];
+        Yv[static_cast<size_t>(ti.ty) * a.rows + row] = bf16_round(acc);
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty_bar[slot]);
+    }
+  }
+}
+
+template <int CW>
+cudaError_t launch_splitk_cw(const Fp4Maps& maps, const Fp4GemvArgs& a, bool pair,
+                             cudaStream_t st) {
+  const int G = a.in / 32, CPT = a.in / kSCols;
+  const size_t smem = static_cast<size_t>(CW) * StreamLayout<1>::kWarpBytes +
+                      2 * static_cast<size_t>(G) * 32 * sizeof(float) +
+                      2 * static_cast<size_t>(CPT) * 32 * 16 + 1024;
+  static bool attr_done = false;  // per template instance
+  if (!attr_done) {
+    cudaError_t e = cudaFuncSetAttribute(fp4_splitk_kernel<CW>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(kSplitkSmemCap));
+    if (e != cudaSuccess) return e;
+    attr_done = true;
+  }
+  if (smem > kSplitkSmemCap) return cudaErrorNotSupported;
+  const long long tiles = static_cast<long long>(a.max_items) * (pair ? 2 : 1) * ((a.rows + 31) / 32);
+  const int per_sm = smem * 2 + 4096 <= 232448 ? 2 : 1;
+  const int grid = static_cast<int>(std::max<long long>(
+      1, std::min<long long>(static_cast<long long>(sm_count()) * per_sm, tiles)));
+  Fp4GemvArgs b = a;
+  if (!b.err) b.err = device_error_word();
+  return launch_pdl(fp4_splitk_kernel<CW>, dim3(grid), dim3((CW + 1) * 32), smem, st, maps, b,
+                    pair ? 1 : 0);
+}
+
 cudaError_t launch_fp4_stream(const Fp4GemvArgs& a, bool pair, int nt, cudaStream_t st,
                               bool map_cache) {
   Fp4Maps maps;
   // matrices are w_stride apart; n_mats must cover every `mat` an item names
   const long long n_mats = a.n_mats > 0 ? a.n_mats : 1;
   if (!fp4_maps(&maps, a, pair, n_mats, map_cache)) return cudaErrorInvalidValue;
+  const long long tiles = static_cast<long long>(a.max_items) * (pair ? 2 : 1) * ((a.rows + 31) / 32);
+  if (nt == 1 && a.in / 32 <= 256 && tiles < 4LL * sm_count()) {
+    // one token per item and few tiles (one to four experts, e.g. a GPU's
+    // share under expert parallelism): split every tile's columns over a
+    // CTA's warps so the launch still covers every SM
+    const int CPT = a.in / kSCols;
+    cudaError_t e = cudaErrorNotSupported;
+    if (CPT >= 7) e = launch_splitk_cw<7>(maps, a, pair, st);
+    else if (CPT >= 4) e = launch_splitk_cw<4>(maps, a, pair, st);
+    else if (CPT >= 2) e = launch_splitk_cw<2>(maps, a, pair, st);
+    if (e != cudaErrorNotSupported) return e;
+  }
   switch (nt) {
     case 1: return launch_stream_nt<1, 8>(maps, a, pair, st);
     case 2: return launch_stream_nt<2, 8>(maps, a, pair, st);
