@@ -673,18 +673,24 @@ __global__ void __launch_bounds__(128) attn_combine_kernel(AttnProblem p, int sp
   const int h = blockIdx.x, b = blockIdx.y;
   extern __shared__ float wsm[];  // [splits]
   __shared__ float s_den;
-  if (threadIdx.x == 0) {
+  if (threadIdx.x < 32) {
+    // warp 0: the splits' maxima and weighted denominators, lanes striding
+    // over the splits, then warp reductions
+    const int lane = threadIdx.x;
     float M = -INFINITY;
-    for (int s = 0; s < splits; ++s)
+    for (int s = lane; s < splits; s += 32)
       M = fmaxf(M, m_part[(static_cast<size_t>(b) * splits + s) * p.H + h]);
+    M = warp_max(M);
     float den = 0.0f;
-    for (int s = 0; s < splits; ++s) {
+    for (int s = lane; s < splits; s += 32) {
       const size_t i = (static_cast<size_t>(b) * splits + s) * p.H + h;
       const float w = (m_part[i] == -INFINITY) ? 0.0f : expf(m_part[i] - M);
       wsm[s] = w;
       den += den_part[i] * w;
     }
-    s_den = den + expf(p.sink[h] - M);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) den += __shfl_xor_sync(0xffffffffu, den, o);
+    if (lane == 0) s_den = den + expf(p.sink[h] - M);
   }
   __syncthreads();
   const float den = s_den;
@@ -739,6 +745,11 @@ TcPlan tc_plan(const AttnProblem& p) {
   if (tiles == 0) return {1, kTcKeys};
   int per_b = sm_count() / (2 * p.B);
   if (per_b < 1) per_b = 1;
+  // at least kMinSplitTiles tiles per split: fewer CTAs pay the Q load and
+  // TMEM setup, and the combine reads fewer partials
+  constexpr int kMinSplitTiles = 2;
+  const int max_splits = (tiles + kMinSplitTiles - 1) / kMinSplitTiles;
+  if (per_b > max_splits) per_b = max_splits;
   int splits = per_b < tiles ? per_b : tiles;
   const int tiles_per = (tiles + splits - 1) / splits;
   splits = (tiles + tiles_per - 1) / tiles_per;
