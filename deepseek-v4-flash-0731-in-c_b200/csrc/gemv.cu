@@ -1047,20 +1047,21 @@ bool fp4_maps(Fp4Maps* m, const Fp4GemvArgs& a, bool pair, long long n_mats, boo
 
 // -------------------------------------------------------- FP8 stream ----
 // Streaming form of the FP8 GEMV (the shared expert, dense projections) for
-// one matrix or a pair: in % 256 == 0, at most 64 128-column blocks. Each
-// warp owns a tile of 32 rows (lane = row) and walks it in 256-column chunks
-// (two 128-column blocks): one elected lane loads two [32 rows x 128 B]
+// one matrix or a pair: in % 512 == 0, at most 64 128-column blocks. Each
+// warp owns a tile of 32 rows (lane = row) and walks it in 512-column chunks
+// (four 128-column blocks): one elected lane loads four [32 rows x 128 B]
 // 128-byte-swizzled TMA boxes, the chunk's activations and their scales into
-// a per-warp ring of kF8Stages stages. Each lane runs the two blocks'
+// a per-warp ring of kF8Stages stages. Each lane runs the four blocks'
 // 128-long fmaf chains interleaved and folds them in column order
 // (dsv4_model.c:571-676). The tile's 32 rows share one row of
 // [128 x 128]-block E8M0 codes, held one per lane and fetched by shuffle.
-constexpr int kF8Cols = 256;
+constexpr int kF8Cols = 512;
+constexpr int kF8Blocks = kF8Cols / 128;  // 128-column scale blocks per chunk
 constexpr int kF8Stages = 4;
 
 template <int NT>
 struct F8Layout {
-  static constexpr int kW = 2 * 32 * 128;          // two swizzled [32][128 B] boxes
+  static constexpr int kW = kF8Blocks * 32 * 128;  // one swizzled [32][128 B] box per block
   static constexpr int kA = NT * kF8Cols * 2;      // activations (f16)
   static constexpr int kQ = NT * 16;               // 4 activation scales covering the chunk
   static constexpr int kStage = (kW + kA + kQ + 1023) / 1024 * 1024;
@@ -1071,27 +1072,25 @@ struct Fp8Maps {
   CUtensorMap w[2];  // [rows][in] bytes, box [32][128], 128B swizzle
 };
 
-// Two 32-value pieces of two independent 128-long chains.
-__device__ __forceinline__ void fp8_step32x2(const uint32_t* wa, const uint32_t* xa,
-                                             const uint32_t* wb, const uint32_t* xb, float& pa,
-                                             float& pb) {
+// 32-value pieces of four independent 128-long chains (one per block).
+__device__ __forceinline__ void fp8_step32x4(const uint32_t (*w)[8], const uint32_t (*x)[16],
+                                             float* p) {
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
-    uint32_t a0, a1, b0, b1;
-    asm("{ .reg .b16 lo, hi; mov.b32 {lo, hi}, %2; cvt.rn.f16x2.e4m3x2 %0, lo;"
-        " cvt.rn.f16x2.e4m3x2 %1, hi; }"
-        : "=r"(a0), "=r"(a1) : "r"(wa[i]));
-    asm("{ .reg .b16 lo, hi; mov.b32 {lo, hi}, %2; cvt.rn.f16x2.e4m3x2 %0, lo;"
-        " cvt.rn.f16x2.e4m3x2 %1, hi; }"
-        : "=r"(b0), "=r"(b1) : "r"(wb[i]));
-    pa = fma_h_lo(a0, xa[2 * i], pa);
-    pb = fma_h_lo(b0, xb[2 * i], pb);
-    pa = fma_h_hi(a0, xa[2 * i], pa);
-    pb = fma_h_hi(b0, xb[2 * i], pb);
-    pa = fma_h_lo(a1, xa[2 * i + 1], pa);
-    pb = fma_h_lo(b1, xb[2 * i + 1], pb);
-    pa = fma_h_hi(a1, xa[2 * i + 1], pa);
-    pb = fma_h_hi(b1, xb[2 * i + 1], pb);
+    uint32_t h[4][2];
+#pragma unroll
+    for (int c = 0; c < 4; ++c)
+      asm("{ .reg .b16 lo, hi; mov.b32 {lo, hi}, %2; cvt.rn.f16x2.e4m3x2 %0, lo;"
+          " cvt.rn.f16x2.e4m3x2 %1, hi; }"
+          : "=r"(h[c][0]), "=r"(h[c][1]) : "r"(w[c][i]));
+#pragma unroll
+    for (int c = 0; c < 4; ++c) p[c] = fma_h_lo(h[c][0], x[c][2 * i], p[c]);
+#pragma unroll
+    for (int c = 0; c < 4; ++c) p[c] = fma_h_hi(h[c][0], x[c][2 * i], p[c]);
+#pragma unroll
+    for (int c = 0; c < 4; ++c) p[c] = fma_h_lo(h[c][1], x[c][2 * i + 1], p[c]);
+#pragma unroll
+    for (int c = 0; c < 4; ++c) p[c] = fma_h_hi(h[c][1], x[c][2 * i + 1], p[c]);
   }
 }
 
@@ -1171,17 +1170,18 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
                             static_cast<uint32_t>(L::kW + ic.ntok * (kF8Cols * 2 + 16)));
       const CUtensorMap* wm = ic.v ? &maps.w[1] : &maps.w[0];
       const int y = ic.rb * 32;
-      tma_load_2d(st, wm, ic.chunk * kF8Cols, y, &bars[stage_i]);
-      tma_load_2d(st + L::kW / 2, wm, ic.chunk * kF8Cols + 128, y, &bars[stage_i]);
+#pragma unroll
+      for (int q = 0; q < kF8Blocks; ++q)
+        tma_load_2d(st + q * (32 * 128), wm, ic.chunk * kF8Cols + q * 128, y, &bars[stage_i]);
 #pragma unroll
       for (int t = 0; t < NT; ++t) {
         if (NT == 1 || t < ic.ntok) {
           bulk_g2s(st + L::kW + t * kF8Cols * 2,
                    a.act.x + static_cast<size_t>(ic.tx[t]) * a.act.ld + ic.chunk * kF8Cols,
                    kF8Cols * 2, &bars[stage_i]);
-          // blocks 2c, 2c+1 lie in the 16-byte run of scales starting at block 4 floor(c/2)
+          // the chunk's four activation scales (blocks 4c .. 4c + 3)
           bulk_g2s(st + L::kW + L::kA + t * 16,
-                   a.act.s + static_cast<size_t>(ic.tx[t]) * sld + (ic.chunk >> 1) * 4, 16,
+                   a.act.s + static_cast<size_t>(ic.tx[t]) * sld + ic.chunk * 4, 16,
                    &bars[stage_i]);
         }
       }
@@ -1218,37 +1218,46 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
     const unsigned char* st = wbase + s * L::kStage;
     const unsigned char* wrow = st + lane * 128;
     const int sw = lane & 7;
-    const int b0 = 2 * chunk, b1 = b0 + 1;
-    const uint32_t c0 = __shfl_sync(0xffffffffu, b0 < 32 ? code_lo : code_hi, b0 & 31);
-    const uint32_t c1 = __shfl_sync(0xffffffffu, b1 < 32 ? code_lo : code_hi, b1 & 31);
-    const float ws0 = e8m0_tbl[c0], ws1 = e8m0_tbl[c1];
-    float p0[NT], p1[NT];
+    uint32_t cb[kF8Blocks];
+    float wsb[kF8Blocks];
 #pragma unroll
-    for (int t = 0; t < NT; ++t) { p0[t] = 0.f; p1[t] = 0.f; }
+    for (int q = 0; q < kF8Blocks; ++q) {
+      const int bq = kF8Blocks * chunk + q;
+      cb[q] = __shfl_sync(0xffffffffu, bq < 32 ? code_lo : code_hi, bq & 31);
+      wsb[q] = e8m0_tbl[cb[q]];
+    }
+    float pp[NT][kF8Blocks];
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {  // 32-column pieces of both blocks
-      uint32_t wa[8], wb[8];
+    for (int t = 0; t < NT; ++t)
 #pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        const int ca = 2 * q + h;  // 16-byte chunk index within the 128-byte block row
-        const uint4 va = *reinterpret_cast<const uint4*>(wrow + ((ca ^ sw) << 4));
-        const uint4 vb = *reinterpret_cast<const uint4*>(wrow + L::kW / 2 + ((ca ^ sw) << 4));
-        wa[4 * h] = va.x; wa[4 * h + 1] = va.y; wa[4 * h + 2] = va.z; wa[4 * h + 3] = va.w;
-        wb[4 * h] = vb.x; wb[4 * h + 1] = vb.y; wb[4 * h + 2] = vb.z; wb[4 * h + 3] = vb.w;
-      }
+      for (int q = 0; q < kF8Blocks; ++q) pp[t][q] = 0.f;
+#pragma unroll
+    for (int pc = 0; pc < 4; ++pc) {  // 32-column pieces of the four blocks
+      uint32_t w8[kF8Blocks][8];
+#pragma unroll
+      for (int q = 0; q < kF8Blocks; ++q)
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int ca = 2 * pc + h;  // 16-byte chunk index within the 128-byte block row
+          const uint4 v = *reinterpret_cast<const uint4*>(wrow + q * (32 * 128) + ((ca ^ sw) << 4));
+          w8[q][4 * h] = v.x; w8[q][4 * h + 1] = v.y; w8[q][4 * h + 2] = v.z; w8[q][4 * h + 3] = v.w;
+        }
 #pragma unroll
       for (int t = 0; t < NT; ++t) {
         if (NT == 1 || t < ntok) {
-          const uint4* xa4 = reinterpret_cast<const uint4*>(st + L::kW + t * kF8Cols * 2 + q * 64);
-          const uint4* xb4 = reinterpret_cast<const uint4*>(st + L::kW + t * kF8Cols * 2 + 256 + q * 64);
-          uint32_t xa[16], xb[16];
+          uint32_t x16[kF8Blocks][16];
 #pragma unroll
-          for (int k = 0; k < 4; ++k) {
-            const uint4 u = xa4[k], w = xb4[k];
-            xa[4 * k] = u.x; xa[4 * k + 1] = u.y; xa[4 * k + 2] = u.z; xa[4 * k + 3] = u.w;
-            xb[4 * k] = w.x; xb[4 * k + 1] = w.y; xb[4 * k + 2] = w.z; xb[4 * k + 3] = w.w;
+          for (int q = 0; q < kF8Blocks; ++q) {
+            const uint4* xq = reinterpret_cast<const uint4*>(st + L::kW + t * kF8Cols * 2 +
+                                                             q * 256 + pc * 64);
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              const uint4 u = xq[k];
+              x16[q][4 * k] = u.x; x16[q][4 * k + 1] = u.y; x16[q][4 * k + 2] = u.z;
+              x16[q][4 * k + 3] = u.w;
+            }
           }
-          fp8_step32x2(wa, xa, wb, xb, p0[t], p1[t]);
+          fp8_step32x4(w8, x16, pp[t]);
         }
       }
     }
@@ -1256,10 +1265,10 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
     for (int t = 0; t < NT; ++t) {
       if (NT == 1 || t < ntok) {
         const float* qv = reinterpret_cast<const float*>(st + L::kW + L::kA + t * 16);
-        const float q0 = qv[(2 * chunk) & 3], q1 = qv[(2 * chunk + 1) & 3];
-        // a NaN block scale (code 255) skips the block, as the reference does
-        if (c0 != 255u) acc[t] = fmaf(p0[t], q0 * ws0, acc[t]);
-        if (c1 != 255u) acc[t] = fmaf(p1[t], q1 * ws1, acc[t]);
+#pragma unroll
+        for (int q = 0; q < kF8Blocks; ++q)
+          // a NaN block scale (code 255) skips the block, as the reference does
+          if (cb[q] != 255u) acc[t] = fmaf(pp[t][q], qv[q] * wsb[q], acc[t]);
       }
     }
     if (chunk == CPT - 1) {
