@@ -306,6 +306,9 @@ struct dsv4cuda_moe_layer {
   std::vector<cudaEvent_t> events;
   int timed = 0;
   bool timing = false;
+  // dsv4cuda_moe_forward_host: the forward of n tokens (d_x -> d_out)
+  // captured once into a CUDA graph per n and replayed after that
+  std::vector<cudaGraphExec_t> host_graphs;
 };
 
 namespace {
@@ -727,6 +730,8 @@ DSV4_API int dsv4cuda_moe_combine(dsv4cuda_moe_layer* L, int n_tokens, float* ou
 
 DSV4_API void dsv4cuda_moe_destroy(dsv4cuda_moe_layer* L) {
   if (!L) return;
+  for (cudaGraphExec_t g : L->host_graphs)
+    if (g) cudaGraphExecDestroy(g);
   for (cudaEvent_t e : L->events) cudaEventDestroy(e);
   if (L->owned) cudaFree(L->owned);
   if (L->ws_mem) cudaFree(L->ws_mem);
@@ -829,8 +834,33 @@ DSV4_API int dsv4cuda_moe_forward_host(dsv4cuda_moe_layer* L, const float* x, co
   if (e == cudaSuccess && token_ids)
     e = cudaMemcpyAsync(L->d_tok, token_ids, sizeof(int) * n_tokens, cudaMemcpyHostToDevice, st);
   if (e != cudaSuccess) { record_error("H2D: %s", cudaGetErrorString(e)); return -1; }
-  if (dsv4cuda_moe_forward(L, L->d_x, token_ids ? L->d_tok : nullptr, n_tokens, L->d_out, st) != 0)
-    return -1;
+  const int* dtok = L->cfg.hash_vocab > 0 ? L->d_tok : nullptr;
+  if (L->host_graphs.size() < static_cast<size_t>(L->max_tokens) + 1)
+    L->host_graphs.assign(static_cast<size_t>(L->max_tokens) + 1, nullptr);
+  cudaGraphExec_t& ge = L->host_graphs[n_tokens];
+  if (ge && !L->timing) {
+    e = cudaGraphLaunch(ge, st);
+    if (e != cudaSuccess) { record_error("graph launch: %s", cudaGetErrorString(e)); return -1; }
+  } else {
+    if (dsv4cuda_moe_forward(L, L->d_x, dtok, n_tokens, L->d_out, st) != 0) return -1;
+    if (!L->timing && n_tokens > 0) {
+      // capture this token count's forward for the next calls (the first,
+      // ungraphed call has set up kernel attributes, streams and maps)
+      cudaGraph_t g = nullptr;
+      e = cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal);
+      int rc = 0;
+      if (e == cudaSuccess) {
+        rc = dsv4cuda_moe_forward(L, L->d_x, dtok, n_tokens, L->d_out, st);
+        e = cudaStreamEndCapture(st, &g);
+      }
+      if (e == cudaSuccess && rc == 0 && g) e = cudaGraphInstantiate(&ge, g, 0);
+      if (g) cudaGraphDestroy(g);
+      if (e != cudaSuccess || rc != 0) {
+        ge = nullptr;  // keep running ungraphed
+        cudaGetLastError();
+      }
+    }
+  }
   e = cudaMemcpyAsync(out, L->d_out, bytes, cudaMemcpyDeviceToHost, st);
   if (e == cudaSuccess) e = cudaStreamSynchronize(st);
   if (e != cudaSuccess) { record_error("D2H: %s", cudaGetErrorString(e)); return -1; }
