@@ -206,19 +206,28 @@ __global__ void __launch_bounds__(256) attn_simt_kernel(SimtArgs a) {
 constexpr int kTcD = 512;
 constexpr int kTcNope = 448;
 constexpr int kTcRope = 64;
-constexpr int kTcM = 128;      // heads (MMA M), zero-padded above H
-constexpr int kTcKeys = 32;    // keys per tile: N of Q K^T, K of P V
-constexpr int kTcHalf = 256;   // output dims per CTA (N of P V)
-constexpr int kTcThreads = 288;  // warps 0-3 softmax, 4-7 converters, 8 MMA
-constexpr uint32_t kQBytes = kTcM * kTcD * 2;           // 131072
-constexpr uint32_t kKBytes = kTcKeys * kTcD * 2;        // 32768 per stage
-constexpr uint32_t kPBytes = kTcM * 128;                // 16384 (128-B rows, 64 B used)
-constexpr uint32_t kOffK = kQBytes;
-constexpr uint32_t kOffP = kOffK + 2 * kKBytes;
-constexpr uint32_t kOffBar = kOffP + 2 * kPBytes;       // 229376
-constexpr uint32_t kTcSmem = kOffBar + 128 + 1024;      // + barriers + alignment slack
-constexpr uint32_t kTmemCols = 512;                     // O: cols 0-255, S: 256-319
+constexpr int kTcM = 128;       // heads (MMA M), zero-padded above H
+constexpr int kTcKeys = 64;     // keys per tile: N of Q K^T, K of P V
+constexpr int kTcHalf = 256;    // latent dims per CTA of a pair: K of Q K^T, N of P V
+constexpr int kTcStages = 3;    // latent tile ring
+constexpr int kTcProdWarps = 4;
+constexpr int kTcMmaWarp = 4 + kTcProdWarps;
+constexpr int kTcThreads = 32 * (kTcMmaWarp + 1);  // 288: softmax 0-3, producers 4-7, MMA 8
+constexpr float kTcLazyMargin = 8.0f;  // the running max moves only when a score exceeds it by this
+constexpr uint32_t kKBlock = kTcKeys * 128;             // one 64-dim column block of a tile (8 KB)
+constexpr uint32_t kKBytes = kTcKeys * kTcHalf * 2;     // 32768 per stage
+constexpr uint32_t kPBytes = kTcM * kTcKeys * 2;        // 16384
+constexpr uint32_t kXBytes = kTcM * kTcKeys * 4;        // 32768: one tile of partial scores
+constexpr uint32_t kOffK = 0;
+constexpr uint32_t kOffP = kOffK + kTcStages * kKBytes;
+constexpr uint32_t kOffX = kOffP + 2 * kPBytes;          // 2 buffers: the peer's partials
+constexpr uint32_t kOffStage = kOffX + 2 * kXBytes;      // this CTA's partials, sent to the peer
+constexpr uint32_t kOffBar = kOffStage + kXBytes;        // 229376
+constexpr uint32_t kTcSmem = kOffBar + 256 + 1024;      // + barriers + alignment slack
+constexpr uint32_t kTmemCols = 512;  // O: cols 0-255, S: 256-383, Q (A operand): 384-511
 constexpr uint32_t kTmemS = 256;
+constexpr uint32_t kTmemQ = 384;
+constexpr float kLog2e = 1.4426950408889634f;
 
 static_assert(kTcSmem <= 232448, "attention tile exceeds the 227 KB shared-memory limit");
 
@@ -231,7 +240,7 @@ struct TcArgs {
   int B, H, n;
   float scale;
   int splits, keys_per_split;
-  float* m_part;    // [B][splits][H]
+  float* m_part;    // [B][splits][H] running max of the scores, log2 units
   float* den_part;  // [B][splits][H]
   float* o_part;    // [B][splits][H][512]
   unsigned* err;
@@ -265,6 +274,23 @@ __device__ __forceinline__ void umma_bf16(uint32_t d_tmem, uint64_t a, uint64_t 
       " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(d_tmem),
       "l"(a), "l"(b), "r"(idesc), "r"(accumulate)
       : "memory");
+}
+
+// D += A B with A (M x 16, BF16 pairs packed along K) in TMEM.
+__device__ __forceinline__ void umma_bf16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b,
+                                             uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}\n" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// 2^x on the MUFU unit (ex2.approx.ftz: relative error ~2^-22, 2^-inf = +0).
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
 }
 
 __device__ __forceinline__ void umma_commit(uint64_t* bar) {
@@ -350,122 +376,224 @@ __device__ __forceinline__ void st_shared_v4(uint32_t addr, uint4 v) {
 }
 
 struct TcBars {
-  uint64_t kv_full[2], kv_empty[2], s_full[2], p_full[2], pv_done[2], fin;
+  uint64_t kv_full[kTcStages], kv_empty[kTcStages], s_full[2], p_full[2], pv_done[2];
+  uint64_t x_full[2], stage_ready, stage_free, fin;
+  unsigned long long key_mask[kTcStages];
   uint32_t tmem_base;
   int abort_flag;
-  uint32_t key_mask[2];
 };
+static_assert(sizeof(TcBars) <= 256, "barrier block exceeds its reservation");
 
-__global__ void __launch_bounds__(kTcThreads, 1) attn_tc_kernel(const __grid_constant__ TcArgs a) {
+// Distributed shared memory of the CTA pair.
+__device__ __forceinline__ uint32_t cluster_map(uint32_t saddr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
+}
+__device__ __forceinline__ void st_cluster_v4(uint32_t addr, uint32_t x, uint32_t y, uint32_t z,
+                                              uint32_t w) {
+  asm volatile("st.shared::cluster.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(x), "r"(y),
+               "r"(z), "r"(w)
+               : "memory");
+}
+// Bulk copy of this CTA's shared memory into the peer's, completion
+// counted (complete_tx) on the peer's mbarrier.
+__device__ __forceinline__ void bulk_s2peer(uint32_t dst_cluster, uint32_t src, uint32_t bytes,
+                                            uint32_t mbar_cluster) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, "
+      "[%3];" ::"r"(dst_cluster),
+      "r"(src), "r"(bytes), "r"(mbar_cluster)
+      : "memory");
+}
+__device__ __forceinline__ uint4 ld_shared_v4(uint32_t addr) {
+  uint4 v;
+  asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "r"(addr)
+               : "memory");
+  return v;
+}
+// Arrive on an mbarrier of the peer CTA, releasing this thread's prior
+// stores to it at cluster scope.
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr)
+               : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait_acq_cluster(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{ .reg .pred p; mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;"
+      " selp.u32 %0, 1, 0, p; }"
+      : "=r"(ok)
+      : "r"(smem_addr(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// tc_wait for a barrier the peer CTA arrives on.
+__device__ __forceinline__ bool tc_wait_peer(uint64_t* bar, uint32_t parity,
+                                             volatile int* abort_flag, unsigned* err) {
+  if (mbar_try_wait_acq_cluster(bar, parity)) return true;
+  const unsigned long long t0 = global_timer_ns();
+  while (!mbar_try_wait_acq_cluster(bar, parity)) {
+    if (*abort_flag) return false;
+    if (global_timer_ns() - t0 > kWaitLimitNs) {
+      if (err) atomicOr(err, kErrWait);
+      *abort_flag = 1;
+      return false;
+    }
+  }
+  return true;
+}
+
+// One CTA pair (a cluster of two) per (batch element, key split). CTA
+// `half` holds latent dims [256 half, 256 half + 256) of Q and of every key
+// tile: it computes that half's partial Q K^T, the pair swaps the partial
+// scores through distributed shared memory and both CTAs run the identical
+// softmax on S = partial(0) + partial(1) (an FP32 sum, the same bits in
+// both), then each accumulates O for its 256 dims. Roles per CTA:
+//   warps 0-3   softmax, thread = head = TMEM lane
+//   warps 4-7   tile producers: 64 keys x 4 column blocks of 64 dims
+//   warp 8      TMEM allocation and MMA issue (one thread)
+// The key tiles cycle through a 3-stage ring; a stage is released when the
+// P V that reads it as V has completed.
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
+    attn_tc_kernel(const __grid_constant__ TcArgs a) {
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_s = smem_addr(smem_raw);
   const uint32_t pad = ((raw_s + 1023u) & ~1023u) - raw_s;
   uint8_t* smem = smem_raw + pad;
   const uint32_t sbase = raw_s + pad;
-  const uint32_t q_s = sbase, k_s = sbase + kOffK, p_s = sbase + kOffP;
+  const uint32_t k_s = sbase + kOffK, p_s = sbase + kOffP, x_s = sbase + kOffX;
+  const uint32_t stage_s = sbase + kOffStage;
   TcBars* bars = reinterpret_cast<TcBars*>(smem + kOffBar);
   volatile int* abort_flag = &bars->abort_flag;
 
   const int half = blockIdx.x & 1, split = blockIdx.x >> 1, b = blockIdx.y;
+  const uint32_t peer = static_cast<uint32_t>(half ^ 1);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int k0 = split * a.keys_per_split;
   const int k_end = min(a.n, k0 + a.keys_per_split);
   const int T = k_end > k0 ? (k_end - k0 + kTcKeys - 1) / kTcKeys : 0;
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(&bars->kv_full[i], 128);
+    for (int i = 0; i < kTcStages; ++i) {
+      mbar_init(&bars->kv_full[i], 32 * kTcProdWarps);
       mbar_init(&bars->kv_empty[i], 1);
+      bars->key_mask[i] = 0;
+    }
+    for (int i = 0; i < 2; ++i) {
       mbar_init(&bars->s_full[i], 1);
       mbar_init(&bars->p_full[i], 128);
       mbar_init(&bars->pv_done[i], 1);
-      bars->key_mask[i] = 0;
     }
+    mbar_init(&bars->x_full[0], 1);
+    mbar_init(&bars->x_full[1], 1);
+    mbar_init(&bars->stage_ready, 128);
+    mbar_init(&bars->stage_free, 1);
     mbar_init(&bars->fin, 1);
     bars->abort_flag = 0;
     mbar_fence_init();
   }
-  if (warp == 8) {
+  if (warp == kTcMmaWarp) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                      smem_addr(&bars->tmem_base)),
                  "r"(kTmemCols)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
-  } else {
-    // Q [H][512] fp32 (BF16-valued) -> BF16, K-major 128-byte-swizzled, rows >= H zero.
-    const float* qb = a.q + static_cast<size_t>(b) * a.H * kTcD;
-    for (int c = threadIdx.x; c < kTcM * (kTcD / 8); c += 256) {
-      const int row = c >> 6, dc = c & 63;
-      uint4 v = make_uint4(0, 0, 0, 0);
-      if (row < a.H) {
-        const float4* src = reinterpret_cast<const float4*>(qb + row * kTcD + dc * 8);
-        const float4 x0 = src[0], x1 = src[1];
-        v = make_uint4(pack_bf16x2(x0.x, x0.y), pack_bf16x2(x0.z, x0.w), pack_bf16x2(x1.x, x1.y),
-                       pack_bf16x2(x1.z, x1.w));
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync_all();  // both CTAs' barriers are initialised before any remote arrive
+  tc_fence_after();
+  const uint32_t tmem = bars->tmem_base;
+  if (warp < 4) {
+    // this half of Q row h [512] fp32 (BF16-valued) -> BF16 pairs in TMEM
+    // lane h, columns kTmemQ.. (the A operand of Q K^T); rows >= H zero
+    const int h = threadIdx.x;
+    const float4* src = reinterpret_cast<const float4*>(
+        a.q + (static_cast<size_t>(b) * a.H + (h < a.H ? h : 0)) * kTcD + half * kTcHalf);
+#pragma unroll 1
+    for (int c32 = 0; c32 < kTcHalf / 2; c32 += 32) {
+      uint32_t r[32];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const float4 x = h < a.H ? src[c32 / 2 + i] : make_float4(0.f, 0.f, 0.f, 0.f);
+        r[2 * i] = pack_bf16x2(x.x, x.y);
+        r[2 * i + 1] = pack_bf16x2(x.z, x.w);
       }
-      st_shared_v4(q_s + sw128_off(row, dc, kTcM), v);
+      tmem_st32(tmem + (static_cast<uint32_t>(warp * 32) << 16) + kTmemQ + c32, r);
     }
-    fence_async_smem();
+    tmem_st_wait();
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  const uint32_t tmem = bars->tmem_base;
 
-  if (warp == 8) {
+  if (warp == kTcMmaWarp) {
     // ------------------------------------------------------------ MMA issue
     if (lane == 0) {
       constexpr uint32_t idesc_qk = umma_idesc_bf16(kTcM, kTcKeys, false);
       constexpr uint32_t idesc_pv = umma_idesc_bf16(kTcM, kTcHalf, true);
-      auto issue_pv = [&](int jj) -> bool {
+      // O += P V for tile jj, V = the tile's stage read MN-major
+      auto issue_pv = [&](int jj, int st) -> bool {
         const int sb = jj & 1;
         if (!tc_wait(&bars->p_full[sb], (jj >> 1) & 1, abort_flag, a.err)) return false;
         tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < kTcKeys / 16; ++kk) {
           const uint64_t ad = umma_desc(p_s + sb * kPBytes + kk * 32, 16, 1024);
-          const uint64_t bd =
-              umma_desc(k_s + sb * kKBytes + half * 4 * (kTcKeys * 128) + kk * 16 * 128,
-                        kTcKeys * 128, 1024);
+          const uint64_t bd = umma_desc(k_s + st * kKBytes + kk * 16 * 128, kKBlock, 1024);
           umma_bf16(tmem, ad, bd, idesc_pv, (jj > 0 || kk > 0) ? 1u : 0u);
         }
         umma_commit(&bars->pv_done[sb]);
-        umma_commit(&bars->kv_empty[sb]);
+        umma_commit(&bars->kv_empty[st]);
         return true;
       };
       bool ok = true;
+      int st = 0, prev_st = 0;
+      uint32_t ph = 0;
       for (int j = 0; j < T && ok; ++j) {
-        const int st = j & 1;
-        if (!tc_wait(&bars->kv_full[st], (j >> 1) & 1, abort_flag, a.err)) { ok = false; break; }
+        if (!tc_wait(&bars->kv_full[st], ph, abort_flag, a.err)) { ok = false; break; }
         tc_fence_after();
 #pragma unroll 4
-        for (int kk = 0; kk < kTcD / 16; ++kk) {
+        for (int kk = 0; kk < kTcHalf / 16; ++kk) {
           const uint32_t off = (kk & 3) * 32;  // 16 dims inside the 64-dim swizzle row
-          const uint64_t ad = umma_desc(q_s + (kk >> 2) * (kTcM * 128) + off, 16, 1024);
-          const uint64_t bd = umma_desc(k_s + st * kKBytes + (kk >> 2) * (kTcKeys * 128) + off,
-                                        16, 1024);
-          umma_bf16(tmem + kTmemS + st * kTcKeys, ad, bd, idesc_qk, kk > 0 ? 1u : 0u);
+          const uint64_t bd = umma_desc(k_s + st * kKBytes + (kk >> 2) * kKBlock + off, 16, 1024);
+          umma_bf16_ts(tmem + kTmemS + (j & 1) * kTcKeys, tmem + kTmemQ + kk * 8, bd, idesc_qk,
+                       kk > 0 ? 1u : 0u);
         }
-        umma_commit(&bars->s_full[st]);
-        if (j > 0) ok = issue_pv(j - 1);
+        umma_commit(&bars->s_full[j & 1]);
+        if (j > 0) ok = issue_pv(j - 1, prev_st);
+        prev_st = st;
+        if (++st == kTcStages) { st = 0; ph ^= 1u; }
       }
-      if (ok && T > 0) issue_pv(T - 1);
+      if (ok && T > 0) issue_pv(T - 1, prev_st);
       umma_commit(&bars->fin);
       mbar_wait(&bars->fin, 0, a.err);
     }
     __syncwarp();
   } else if (warp >= 4) {
     // ------------------------------------------------- latent tile producer
-    // Thread (r, qd) owns key r of every tile and dims [128 qd, 128 qd + 128).
-    // The indices of tile j + 2 are read and the rows bulk-prefetched into L2
-    // while tile j is converted; the registers of tile j + 1 are loaded right
-    // after tile j is handed over, so the HBM latency overlaps two tiles.
+    // Thread (r, q) owns keys r and r + 32 of every tile and the 64 dims of
+    // column block q of this half: FP8 codes [256 half + 64 q, +64) with
+    // scale slot 4 half + q, or for half 1, q 3 the 64 BF16 RoPE dims. The
+    // indices of tile j + 2 are read and its rows bulk-prefetched into L2
+    // while tile j is converted; the registers of tile j + 1 are loaded
+    // right after tile j is handed over.
+    constexpr int kSub = kTcKeys / (8 * kTcProdWarps);  // keys per thread
     const int c = threadIdx.x - 128;
-    const int r = c >> 2, qd = c & 3;  // key row in tile, quarter of the dims
+    const int r = c >> 2, q = c & 3;
+    const bool rope_part = half == 1 && q == 3;
+    const int code_off = half * kTcHalf + q * 64;
+    const int sslot = half * 4 + q;
     const int* idxb = a.idx + static_cast<size_t>(b) * a.n;
     const long long rbase = static_cast<long long>(b) * a.kv_bstride;
-    auto load_idx = [&](int j) -> long long {
-      const int key = k0 + j * kTcKeys + r;
+    auto load_idx = [&](int j, int kk) -> long long {
+      const int key = k0 + j * kTcKeys + r + kk * (8 * kTcProdWarps);
       return (j < T && key < k_end) ? static_cast<long long>(idxb[key]) : -1;
     };
     auto in_range = [&](long long pos) { return pos >= 0 && pos < a.kv_rows; };
@@ -473,158 +601,234 @@ __global__ void __launch_bounds__(kTcThreads, 1) attn_tc_kernel(const __grid_con
       if (!in_range(pos)) return;
       const long long row = rbase + pos;
       if (a.kv) {
-        bulk_prefetch_l2(a.kv + row * kTcD + qd * 128, 512);
-      } else if (qd == 0) {
-        bulk_prefetch_l2(a.cache.codes + row * kTcNope, kTcNope);
-      } else if (qd == 1) {
+        if (q == 0) bulk_prefetch_l2(a.kv + row * kTcD + half * kTcHalf, kTcHalf * 4);
+      } else if (q == 0) {
+        bulk_prefetch_l2(a.cache.codes + row * kTcNope + half * kTcHalf,
+                         half ? kTcNope - kTcHalf : kTcHalf);
+      } else if (q == 1 && half) {
         bulk_prefetch_l2(a.cache.rope + row * kTcRope, kTcRope * 2);
-      } else if (qd == 2 && (row & 1) == 0 && row + 1 < a.cache.rows) {
-        bulk_prefetch_l2(a.cache.scales + row * kKvScaleSlots, 16);  // this row and the next
+      } else if (q == 2) {
+        const long long r2 = row & ~1ll;  // the 16-byte pair of scale rows holding this one
+        if (r2 + 1 < a.cache.rows) bulk_prefetch_l2(a.cache.scales + r2 * kKvScaleSlots, 16);
       }
     };
-    // raw FP8 bytes of this thread's slice: qd < 3: 8 x 16 codes; qd == 3:
-    // 4 x 16 codes then 8 x 8 RoPE BF16 values
-    uint4 raw[12];
-    uint32_t scw = 0;
-    auto load_raw = [&](long long pos) {
+    // per key: q < 3 or half 0: 4 x 16 codes; half 1, q 3: 8 x 8 RoPE BF16 values
+    uint4 raw[kSub][8];
+    uint32_t scode[kSub];
+    auto load_raw = [&](long long pos, int kk) {
       if (!in_range(pos) || a.kv) return;
       const long long row = rbase + pos;
-      const uint4* cp = reinterpret_cast<const uint4*>(a.cache.codes + row * kTcNope + qd * 128);
-      const uint4* rp = reinterpret_cast<const uint4*>(a.cache.rope + row * kTcRope);
+      if (!rope_part) {
+        const uint4* cp = reinterpret_cast<const uint4*>(a.cache.codes + row * kTcNope + code_off);
 #pragma unroll
-      for (int u = 0; u < 12; ++u) {
-        if (qd < 3) {
-          if (u < 8) raw[u] = __ldg(cp + u);
-        } else {
-          raw[u] = u < 4 ? __ldg(cp + u) : __ldg(rp + (u - 4));
-        }
-      }
-      scw = *reinterpret_cast<const uint32_t*>(a.cache.scales + row * kKvScaleSlots +
-                                               (qd < 2 ? 0 : 4));
-    };
-    long long p_cur = load_idx(0), p_nxt = load_idx(1);
-    prefetch_rows(p_cur);
-    prefetch_rows(p_nxt);
-    load_raw(p_cur);
-    for (int j = 0; j < T; ++j) {
-      const int st = j & 1;
-      const long long p_n2 = load_idx(j + 2);
-      if (p_cur >= a.kv_rows && a.err) atomicOr(a.err, kErrIndex);
-      const bool valid = in_range(p_cur);
-      const long long row = rbase + p_cur;
-      if (!tc_wait(&bars->kv_empty[st], ((j >> 1) & 1) ^ 1, abort_flag, a.err)) break;
-      const uint32_t tile = k_s + st * kKBytes;
-      if (!valid) {
-        for (int dc = qd * 16; dc < qd * 16 + 16; ++dc)
-          st_shared_v4(tile + sw128_off(r, dc, kTcKeys), make_uint4(0, 0, 0, 0));
-      } else if (a.kv) {
-        const float4* src = reinterpret_cast<const float4*>(a.kv + row * kTcD + qd * 128);
-        for (int dc = 0; dc < 16; ++dc) {
-          const float4 x0 = __ldg(src + 2 * dc), x1 = __ldg(src + 2 * dc + 1);
-          st_shared_v4(tile + sw128_off(r, qd * 16 + dc, kTcKeys),
-                       make_uint4(pack_bf16x2(x0.x, x0.y), pack_bf16x2(x0.z, x0.w),
-                                  pack_bf16x2(x1.x, x1.y), pack_bf16x2(x1.z, x1.w)));
-        }
+        for (int u = 0; u < 4; ++u) raw[kk][u] = __ldg(cp + u);
+        scode[kk] = a.cache.scales[row * kKvScaleSlots + sslot];
       } else {
+        const uint4* rp = reinterpret_cast<const uint4*>(a.cache.rope + row * kTcRope);
 #pragma unroll
-        for (int u = 0; u < 8; ++u) {
-          if (qd < 3 || u < 4) {
-            const int g = (qd * 128 + u * 16) >> 6;  // scale group
-            const uint32_t code = (scw >> (8 * (g & 3))) & 0xFFu;
-            const float sc = e8m0_decode(code);
-            const uint2 lo = e4m3x4_to_bf16(raw[u].x, sc), hi = e4m3x4_to_bf16(raw[u].y, sc);
-            const uint2 lo2 = e4m3x4_to_bf16(raw[u].z, sc), hi2 = e4m3x4_to_bf16(raw[u].w, sc);
-            st_shared_v4(tile + sw128_off(r, qd * 16 + 2 * u, kTcKeys),
-                         make_uint4(lo.x, lo.y, hi.x, hi.y));
-            st_shared_v4(tile + sw128_off(r, qd * 16 + 2 * u + 1, kTcKeys),
-                         make_uint4(lo2.x, lo2.y, hi2.x, hi2.y));
-          }
-        }
-        if (qd == 3) {
+        for (int u = 0; u < 8; ++u) raw[kk][u] = __ldg(rp + u);
+      }
+    };
+    long long p_cur[kSub], p_nxt[kSub];
+#pragma unroll
+    for (int kk = 0; kk < kSub; ++kk) {
+      p_cur[kk] = load_idx(0, kk);
+      p_nxt[kk] = load_idx(1, kk);
+      prefetch_rows(p_cur[kk]);
+      prefetch_rows(p_nxt[kk]);
+      load_raw(p_cur[kk], kk);
+    }
+    int st = 0;
+    uint32_t ph = 0;
+    for (int j = 0; j < T; ++j) {
+      long long p_n2[kSub];
+#pragma unroll
+      for (int kk = 0; kk < kSub; ++kk) {
+        p_n2[kk] = load_idx(j + 2, kk);
+        if (p_cur[kk] >= a.kv_rows && a.err) atomicOr(a.err, kErrIndex);
+      }
+      if (!tc_wait(&bars->kv_empty[st], ph ^ 1u, abort_flag, a.err)) break;
+      const uint32_t tile = k_s + st * kKBytes;
+#pragma unroll
+      for (int kk = 0; kk < kSub; ++kk) {
+        const int key = r + kk * (8 * kTcProdWarps);
+        const bool valid = in_range(p_cur[kk]);
+        const long long row = rbase + p_cur[kk];
+        if (!valid) {
 #pragma unroll
           for (int u = 0; u < 8; ++u)
-            st_shared_v4(tile + sw128_off(r, 56 + u, kTcKeys), raw[4 + u]);
+            st_shared_v4(tile + sw128_off(key, q * 8 + u, kTcKeys), make_uint4(0, 0, 0, 0));
+        } else if (a.kv) {
+          const float4* src =
+              reinterpret_cast<const float4*>(a.kv + row * kTcD + half * kTcHalf + q * 64);
+#pragma unroll 2
+          for (int u = 0; u < 8; ++u) {
+            const float4 x0 = __ldg(src + 2 * u), x1 = __ldg(src + 2 * u + 1);
+            st_shared_v4(tile + sw128_off(key, q * 8 + u, kTcKeys),
+                         make_uint4(pack_bf16x2(x0.x, x0.y), pack_bf16x2(x0.z, x0.w),
+                                    pack_bf16x2(x1.x, x1.y), pack_bf16x2(x1.z, x1.w)));
+          }
+        } else if (!rope_part) {
+          const float sc = e8m0_decode(scode[kk]);
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            const uint2 lo = e4m3x4_to_bf16(raw[kk][u].x, sc), hi = e4m3x4_to_bf16(raw[kk][u].y, sc);
+            const uint2 lo2 = e4m3x4_to_bf16(raw[kk][u].z, sc),
+                        hi2 = e4m3x4_to_bf16(raw[kk][u].w, sc);
+            st_shared_v4(tile + sw128_off(key, q * 8 + 2 * u, kTcKeys),
+                         make_uint4(lo.x, lo.y, hi.x, hi.y));
+            st_shared_v4(tile + sw128_off(key, q * 8 + 2 * u + 1, kTcKeys),
+                         make_uint4(lo2.x, lo2.y, hi2.x, hi2.y));
+          }
+        } else {
+#pragma unroll
+          for (int u = 0; u < 8; ++u)
+            st_shared_v4(tile + sw128_off(key, q * 8 + u, kTcKeys), raw[kk][u]);
         }
-      }
-      // validity mask of the tile's keys (bit r), one byte per producer warp
-      const uint32_t vb = __ballot_sync(0xffffffffu, valid);
-      if (lane == 0) {
-        uint32_t m8 = 0;
-        for (int k = 0; k < 8; ++k) m8 |= ((vb >> (4 * k)) & 1u) << k;
-        reinterpret_cast<volatile uint8_t*>(&bars->key_mask[st])[warp - 4] =
-            static_cast<uint8_t>(m8);
+        // validity mask of the tile's keys (bit key), one byte per 8 keys
+        const uint32_t vb = __ballot_sync(0xffffffffu, valid);
+        if (lane == 0) {
+          uint32_t m8 = 0;
+          for (int k = 0; k < 8; ++k) m8 |= ((vb >> (4 * k)) & 1u) << k;
+          reinterpret_cast<volatile uint8_t*>(&bars->key_mask[st])[(warp - 4) + kk * kTcProdWarps] =
+              static_cast<uint8_t>(m8);
+        }
       }
       __syncwarp();
       fence_async_smem();
       mbar_arrive(&bars->kv_full[st]);
-      prefetch_rows(p_n2);
-      load_raw(p_nxt);
-      p_cur = p_nxt;
-      p_nxt = p_n2;
+#pragma unroll
+      for (int kk = 0; kk < kSub; ++kk) {
+        prefetch_rows(p_n2[kk]);
+        load_raw(p_nxt[kk], kk);
+        p_cur[kk] = p_nxt[kk];
+        p_nxt[kk] = p_n2[kk];
+      }
+      if (++st == kTcStages) { st = 0; ph ^= 1u; }
     }
   } else {
     // --------------------------------------------------------------- softmax
     const int h = threadIdx.x;  // head = TMEM lane
     const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
+    const uint32_t row_off = h * (kTcKeys * 4);  // this head's row in a partial-score tile
+    const uint32_t x_peer = cluster_map(x_s, peer);
+    const uint32_t x_full_peer = cluster_map(smem_addr(&bars->x_full[0]), peer);
+    const uint32_t stage_free_peer = cluster_map(smem_addr(&bars->stage_free), peer);
+    // scores in log2 units: t = dot * scale * log2(e), weights 2^(t - m)
+    const float sc2 = a.scale * kLog2e;
     float m_run = -INFINITY, den = 0.0f;
     bool ok = true;
+    int kst = 0;
+    uint32_t kph = 0;
     for (int j = 0; j < T; ++j) {
       const int sb = j & 1;
       bool w = tc_wait(&bars->s_full[sb], (j >> 1) & 1, abort_flag, a.err);
-      w = w && tc_wait(&bars->kv_full[sb], (j >> 1) & 1, abort_flag, a.err);
+      w = w && tc_wait(&bars->kv_full[kst], kph, abort_flag, a.err);
+      // the staging tile is free once the peer holds the previous one
+      if (j > 0) w = w && tc_wait_peer(&bars->stage_free, (j - 1) & 1, abort_flag, a.err);
       if (!__all_sync(0xffffffffu, w)) { ok = false; break; }
       tc_fence_after();
-      uint32_t r[32];
-      tmem_ld32(tmem + lane_base + kTmemS + sb * kTcKeys, r);
-      const uint32_t mask = *reinterpret_cast<volatile uint32_t*>(&bars->key_mask[sb]);
-      float s[32];
+      // this CTA's partial scores -> staging tile -> one bulk copy into the
+      // peer's receive buffer sb
+#pragma unroll
+      for (int c32 = 0; c32 < kTcKeys; c32 += 32) {
+        uint32_t r[32];
+        tmem_ld32(tmem + lane_base + kTmemS + sb * kTcKeys + c32, r);
+#pragma unroll
+        for (int cc = 0; cc < 8; ++cc)
+          st_shared_v4(stage_s + row_off + (((c32 / 4 + cc) ^ (h & 7)) << 4),
+                       make_uint4(r[4 * cc], r[4 * cc + 1], r[4 * cc + 2], r[4 * cc + 3]));
+      }
+      fence_async_smem();
+      mbar_arrive(&bars->stage_ready);
+      if (h == 0 && tc_wait(&bars->stage_ready, j & 1, abort_flag, a.err)) {
+        mbar_arrive_expect_tx(&bars->x_full[sb], kXBytes);  // the peer's tile j, arriving here
+        bulk_s2peer(x_peer + sb * kXBytes, stage_s, kXBytes, x_full_peer + sb * 8);
+      }
+      const bool wx = tc_wait_peer(&bars->x_full[sb], (j >> 1) & 1, abort_flag, a.err);
+      if (!__all_sync(0xffffffffu, wx)) { ok = false; break; }
+      if (h == 0) mbar_arrive_remote(stage_free_peer);  // the peer's copy has landed here
+      const unsigned long long mask =
+          *reinterpret_cast<volatile unsigned long long*>(&bars->key_mask[kst]);
+      // S = own partial + the peer's (the same FP32 sum in both CTAs)
+      float s[kTcKeys];
       float tmax = -INFINITY;
 #pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        s[i] = ((mask >> i) & 1u) ? __uint_as_float(r[i]) * a.scale : -INFINITY;
-        tmax = fmaxf(tmax, s[i]);
-      }
-      const float m_new = fmaxf(m_run, tmax);
-      const bool resc = (m_new > m_run) && (m_run != -INFINITY);
-      const float alpha = resc ? __expf(m_run - m_new) : 1.0f;
-      den *= alpha;
-      uint32_t pw[16];
-      float part[4] = {0.f, 0.f, 0.f, 0.f};
+      for (int c4 = 0; c4 < kTcKeys / 4; ++c4) {
+        const uint32_t off = row_off + ((c4 ^ (h & 7)) << 4);
+        const uint4 u = ld_shared_v4(stage_s + off);
+        const uint4 v = ld_shared_v4(x_s + sb * kXBytes + off);
+        const uint32_t mine[4] = {u.x, u.y, u.z, u.w};
+        const uint32_t other[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
-      for (int i = 0; i < 32; i += 2) {
-        // hardware exp2 path (MUFU): relative error ~2^-21, far below the
-        // BF16 rounding the weights get
-        const float e0 = (s[i] == -INFINITY) ? 0.0f : __expf(s[i] - m_new);
-        const float e1 = (s[i + 1] == -INFINITY) ? 0.0f : __expf(s[i + 1] - m_new);
+        for (int i = 0; i < 4; ++i) {
+          const int k = 4 * c4 + i;
+          const float sum = __uint_as_float(mine[i]) + __uint_as_float(other[i]);
+          s[k] = ((mask >> k) & 1ull) ? sum * sc2 : -INFINITY;
+          tmax = fmaxf(tmax, s[k]);
+        }
+      }
+      // lazy running max: it moves only when a score exceeds it by the
+      // margin (then O and den are rescaled), so the weights stay <= 2^8
+      float m_use = m_run, alpha = 1.0f;
+      bool resc = false;
+      if (tmax != -INFINITY) {
+        if (m_run == -INFINITY) {
+          m_use = tmax;
+        } else if (tmax > m_run + kTcLazyMargin) {
+          m_use = tmax;
+          alpha = ex2_approx(m_run - tmax);
+          resc = true;
+        }
+      }
+      den *= alpha;
+      uint32_t pw[kTcKeys / 2];
+      float part[4] = {0.f, 0.f, 0.f, 0.f};
+      const float m_sub = m_use == -INFINITY ? 0.0f : m_use;  // a masked tile: 2^-inf = 0
+#pragma unroll
+      for (int i = 0; i < kTcKeys; i += 2) {
+        // MUFU exp2: relative error ~2^-22, far below the BF16 rounding the
+        // weights get
+        const float e0 = ex2_approx(s[i] - m_sub);
+        const float e1 = ex2_approx(s[i + 1] - m_sub);
         part[(i >> 1) & 3] += e0 + e1;
         pw[i / 2] = pack_bf16x2(e0, e1);
       }
       den += (part[0] + part[1]) + (part[2] + part[3]);
-      m_run = m_new;
-      if (j > 0) {
+      m_run = m_use;
+      // P buffer sb was last read by P V of tile j - 2
+      if (j >= 2) {
+        const bool wp = tc_wait(&bars->pv_done[sb], ((j - 2) >> 1) & 1, abort_flag, a.err);
+        if (!__all_sync(0xffffffffu, wp)) { ok = false; break; }
+      }
+      if (__any_sync(0xffffffffu, resc)) {
+        // O holds tiles < j once P V of tile j - 1 is done (j >= 1 here: a
+        // finite running max comes from an earlier tile)
         const bool wv = tc_wait(&bars->pv_done[(j - 1) & 1], ((j - 1) >> 1) & 1, abort_flag, a.err);
         if (!__all_sync(0xffffffffu, wv)) { ok = false; break; }
         tc_fence_after();
-        if (__any_sync(0xffffffffu, resc)) {
-          for (int cb = 0; cb < kTcHalf; cb += 32) {
-            uint32_t o[32];
-            tmem_ld32(tmem + lane_base + cb, o);
+#pragma unroll 1
+        for (int cb = 0; cb < kTcHalf; cb += 32) {
+          uint32_t o[32];
+          tmem_ld32(tmem + lane_base + cb, o);
 #pragma unroll
-            for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
-            tmem_st32(tmem + lane_base + cb, o);
-          }
-          tmem_st_wait();
+          for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+          tmem_st32(tmem + lane_base + cb, o);
         }
+        tmem_st_wait();
       }
       const uint32_t prow = p_s + sb * kPBytes + (h >> 3) * 1024 + (h & 7) * 128;
 #pragma unroll
-      for (int c4 = 0; c4 < 4; ++c4)
-        st_shared_v4(prow + (((c4 ^ (h & 7))) << 4),
-                     make_uint4(pw[4 * c4], pw[4 * c4 + 1], pw[4 * c4 + 2], pw[4 * c4 + 3]));
+      for (int c8 = 0; c8 < 8; ++c8)
+        st_shared_v4(prow + ((c8 ^ (h & 7)) << 4),
+                     make_uint4(pw[4 * c8], pw[4 * c8 + 1], pw[4 * c8 + 2], pw[4 * c8 + 3]));
       fence_async_smem();
       tc_fence_before();
       mbar_arrive(&bars->p_full[sb]);
+      if (++kst == kTcStages) { kst = 0; kph ^= 1u; }
     }
+    // the last partial sent has landed in the peer before this CTA may end
+    if (ok && T > 0) ok = tc_wait_peer(&bars->stage_free, (T - 1) & 1, abort_flag, a.err) && ok;
     // epilogue: O partial row, m and den
     const size_t prow = (static_cast<size_t>(b) * a.splits + split) * a.H + h;
     bool have = ok && T > 0;
@@ -658,8 +862,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) attn_tc_kernel(const __grid_con
   }
   tc_fence_before();
   __syncthreads();
+  cluster_sync_all();  // no CTA leaves while its peer may still write to it
   tc_fence_after();
-  if (warp == 8)
+  if (warp == kTcMmaWarp)
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
                  "r"(kTmemCols)
                  : "memory");
@@ -684,13 +889,13 @@ __global__ void __launch_bounds__(128) attn_combine_kernel(AttnProblem p, int sp
     float den = 0.0f;
     for (int s = lane; s < splits; s += 32) {
       const size_t i = (static_cast<size_t>(b) * splits + s) * p.H + h;
-      const float w = (m_part[i] == -INFINITY) ? 0.0f : expf(m_part[i] - M);
+      const float w = (m_part[i] == -INFINITY) ? 0.0f : exp2f(m_part[i] - M);
       wsm[s] = w;
       den += den_part[i] * w;
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) den += __shfl_xor_sync(0xffffffffu, den, o);
-    if (lane == 0) s_den = den + expf(p.sink[h] - M);
+    if (lane == 0) s_den = den + exp2f(p.sink[h] * kLog2e - M);
   }
   __syncthreads();
   const float den = s_den;
