@@ -208,23 +208,24 @@ constexpr int kTcNope = 448;
 constexpr int kTcRope = 64;
 constexpr int kTcM = 128;       // heads (MMA M), zero-padded above H
 constexpr int kTcKeys = 64;     // keys per tile: N of Q K^T, K of P V
-constexpr int kTcHalf = 256;    // latent dims per CTA of a pair: K of Q K^T, N of P V
-constexpr int kTcStages = 3;    // latent tile ring
-constexpr int kTcProdWarps = 4;
+constexpr int kTcHalf = 256;    // output dims per CTA: N of P V
+constexpr int kTcOwnStages = 3;  // ring of the tile's own-half dims (the V of P V)
+constexpr int kTcProdWarps = 8;
 constexpr int kTcMmaWarp = 4 + kTcProdWarps;
-constexpr int kTcThreads = 32 * (kTcMmaWarp + 1);  // 288: softmax 0-3, producers 4-7, MMA 8
-constexpr float kTcLazyMargin = 8.0f;  // the running max moves only when a score exceeds it by this
+constexpr int kTcThreads = 32 * (kTcMmaWarp + 1);  // 416: softmax 0-3, producers 4-11, MMA 12
+constexpr float kTcLazyMargin = 8.0f;  // log2 units: the running max moves only past this margin
+constexpr uint32_t kQBlock = kTcM * 128;                // one 64-dim column block of Q (16 KB)
 constexpr uint32_t kKBlock = kTcKeys * 128;             // one 64-dim column block of a tile (8 KB)
-constexpr uint32_t kKBytes = kTcKeys * kTcHalf * 2;     // 32768 per stage
+constexpr uint32_t kQSmemBytes = 4 * kQBlock;           // Q dims 256-511 (64 KB)
+constexpr uint32_t kHalfTile = 4 * kKBlock;             // 256 dims of a tile (32 KB)
 constexpr uint32_t kPBytes = kTcM * kTcKeys * 2;        // 16384
-constexpr uint32_t kXBytes = kTcM * kTcKeys * 4;        // 32768: one tile of partial scores
-constexpr uint32_t kOffK = 0;
-constexpr uint32_t kOffP = kOffK + kTcStages * kKBytes;
-constexpr uint32_t kOffX = kOffP + 2 * kPBytes;          // 2 buffers: the peer's partials
-constexpr uint32_t kOffStage = kOffX + 2 * kXBytes;      // this CTA's partials, sent to the peer
-constexpr uint32_t kOffBar = kOffStage + kXBytes;        // 229376
+constexpr uint32_t kOffQ = 0;
+constexpr uint32_t kOffOwn = kOffQ + kQSmemBytes;
+constexpr uint32_t kOffOther = kOffOwn + kTcOwnStages * kHalfTile;
+constexpr uint32_t kOffP = kOffOther + kHalfTile;
+constexpr uint32_t kOffBar = kOffP + 2 * kPBytes;       // 229376
 constexpr uint32_t kTcSmem = kOffBar + 256 + 1024;      // + barriers + alignment slack
-constexpr uint32_t kTmemCols = 512;  // O: cols 0-255, S: 256-383, Q (A operand): 384-511
+constexpr uint32_t kTmemCols = 512;  // O: cols 0-255, S: 256-383, Q dims 0-255 (A operand): 384-511
 constexpr uint32_t kTmemS = 256;
 constexpr uint32_t kTmemQ = 384;
 constexpr float kLog2e = 1.4426950408889634f;
@@ -283,6 +284,33 @@ __device__ __forceinline__ void umma_bf16_ts(uint32_t d_tmem, uint32_t a_tmem, u
       "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
       " tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}\n" ::"r"(d_tmem),
       "r"(a_tmem), "l"(b), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Warp-converged issue: every lane of the MMA warp executes these, one
+// elected lane (the same one each time) issues. A rolled single-lane issue
+// loop runs several times slower than the tensor pipe.
+__device__ __forceinline__ void umma_bf16_e(uint32_t d_tmem, uint64_t a, uint64_t b,
+                                            uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p, e;\n setp.ne.b32 p, %4, 0;\n elect.sync _|e, 0xffffffff;\n"
+      " @e tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(d_tmem),
+      "l"(a), "l"(b), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+__device__ __forceinline__ void umma_bf16_ts_e(uint32_t d_tmem, uint32_t a_tmem, uint64_t b,
+                                               uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p, e;\n setp.ne.b32 p, %4, 0;\n elect.sync _|e, 0xffffffff;\n"
+      " @e tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}\n" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+__device__ __forceinline__ void umma_commit_e(uint64_t* bar) {
+  asm volatile(
+      "{\n .reg .pred e;\n elect.sync _|e, 0xffffffff;\n"
+      " @e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n}\n" ::"r"(
+          smem_addr(bar))
       : "memory");
 }
 
@@ -369,6 +397,31 @@ __device__ __forceinline__ uint2 e4m3x4_to_bf16(uint32_t w, float sc) {
   return make_uint2(pack_bf16x2(f01.x * sc, f01.y * sc), pack_bf16x2(f23.x * sc, f23.y * sc));
 }
 
+// Four E4M3 codes times 2^(c - 127) -> 2 x bf16x2 on the integer and FMA
+// pipes. Each code's 7 magnitude bits placed at BF16 bits 4-10 read as a
+// BF16 number equal to the E4M3 value times 2^-120 (subnormal codes become
+// BF16 subnormals, zero stays zero), the sign goes to bit 15, and one BF16
+// multiply by k2 = 2^(c - 7) (exponent field c + 120) in both halves scales
+// exactly. Valid for 10 <= c <= 134 (every product a normal BF16) and codes
+// other than 0x7F/0xFF (NaN); the caller checks.
+__device__ __forceinline__ uint2 e4m3x4_to_bf16_mul(uint32_t w, uint32_t k2) {
+  const uint32_t m = w & 0x7F7F7F7Fu;
+  uint32_t t0, t1, s0, s1, r0, r1;
+  asm("prmt.b32 %0, %1, 0, 0x4140;" : "=r"(t0) : "r"(m));  // [b0, 0, b1, 0]
+  asm("prmt.b32 %0, %1, 0, 0x4342;" : "=r"(t1) : "r"(m));  // [b2, 0, b3, 0]
+  asm("prmt.b32 %0, %1, 0, 0x9484;" : "=r"(s0) : "r"(w));  // sign bytes of b0, b1
+  asm("prmt.b32 %0, %1, 0, 0xB4A4;" : "=r"(s1) : "r"(w));  // sign bytes of b2, b3
+  const uint32_t v0 = (t0 << 4) | (s0 & 0x80008000u), v1 = (t1 << 4) | (s1 & 0x80008000u);
+  asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(r0) : "r"(v0), "r"(k2));
+  asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(r1) : "r"(v1), "r"(k2));
+  return make_uint2(r0, r1);
+}
+
+// Nonzero iff a byte of w is an E4M3 NaN code (0x7F or 0xFF).
+__device__ __forceinline__ uint32_t e4m3_nan_bytes(uint32_t w) {
+  return ((w & 0x7F7F7F7Fu) + 0x01010101u) & 0x80808080u;
+}
+
 __device__ __forceinline__ void st_shared_v4(uint32_t addr, uint4 v) {
   asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(v.x), "r"(v.y),
                "r"(v.z), "r"(v.w)
@@ -376,124 +429,61 @@ __device__ __forceinline__ void st_shared_v4(uint32_t addr, uint4 v) {
 }
 
 struct TcBars {
-  uint64_t kv_full[kTcStages], kv_empty[kTcStages], s_full[2], p_full[2], pv_done[2];
-  uint64_t x_full[2], stage_ready, stage_free, fin;
-  unsigned long long key_mask[kTcStages];
+  // A tile's dims split in two: "own" = this CTA's output half (also the V
+  // of P V), held in a 3-slot ring, and "other" = the rest, in one slot.
+  // full_*: that part of a tile is written; empty_other: Q K^T has read
+  // the other part; empty_own: P V has read the own part.
+  uint64_t full_own[kTcOwnStages], empty_own[kTcOwnStages], full_other, empty_other;
+  uint64_t s_full[2], p_full[2], pv_done[2], fin;
+  // validity bits of tile j's keys in slot j & 3, written by the first
+  // own-quarter producers (tile j + 4 only after P V of tile j + 1, so after
+  // the softmax of tile j has read slot j & 3)
+  unsigned long long key_mask[4];
   uint32_t tmem_base;
   int abort_flag;
 };
 static_assert(sizeof(TcBars) <= 256, "barrier block exceeds its reservation");
 
-// Distributed shared memory of the CTA pair.
-__device__ __forceinline__ uint32_t cluster_map(uint32_t saddr, uint32_t rank) {
-  uint32_t r;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
-  return r;
-}
-__device__ __forceinline__ void cluster_sync_all() {
-  asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
-}
-__device__ __forceinline__ void st_cluster_v4(uint32_t addr, uint32_t x, uint32_t y, uint32_t z,
-                                              uint32_t w) {
-  asm volatile("st.shared::cluster.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(x), "r"(y),
-               "r"(z), "r"(w)
-               : "memory");
-}
-// Bulk copy of this CTA's shared memory into the peer's, completion
-// counted (complete_tx) on the peer's mbarrier.
-__device__ __forceinline__ void bulk_s2peer(uint32_t dst_cluster, uint32_t src, uint32_t bytes,
-                                            uint32_t mbar_cluster) {
-  asm volatile(
-      "cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, "
-      "[%3];" ::"r"(dst_cluster),
-      "r"(src), "r"(bytes), "r"(mbar_cluster)
-      : "memory");
-}
-__device__ __forceinline__ uint4 ld_shared_v4(uint32_t addr) {
-  uint4 v;
-  asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
-               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-               : "r"(addr)
-               : "memory");
-  return v;
-}
-// Arrive on an mbarrier of the peer CTA, releasing this thread's prior
-// stores to it at cluster scope.
-__device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
-  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr)
-               : "memory");
-}
-__device__ __forceinline__ bool mbar_try_wait_acq_cluster(uint64_t* bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{ .reg .pred p; mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;"
-      " selp.u32 %0, 1, 0, p; }"
-      : "=r"(ok)
-      : "r"(smem_addr(bar)), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-// tc_wait for a barrier the peer CTA arrives on.
-__device__ __forceinline__ bool tc_wait_peer(uint64_t* bar, uint32_t parity,
-                                             volatile int* abort_flag, unsigned* err) {
-  if (mbar_try_wait_acq_cluster(bar, parity)) return true;
-  const unsigned long long t0 = global_timer_ns();
-  while (!mbar_try_wait_acq_cluster(bar, parity)) {
-    if (*abort_flag) return false;
-    if (global_timer_ns() - t0 > kWaitLimitNs) {
-      if (err) atomicOr(err, kErrWait);
-      *abort_flag = 1;
-      return false;
-    }
-  }
-  return true;
-}
-
-// One CTA pair (a cluster of two) per (batch element, key split). CTA
-// `half` holds latent dims [256 half, 256 half + 256) of Q and of every key
-// tile: it computes that half's partial Q K^T, the pair swaps the partial
-// scores through distributed shared memory and both CTAs run the identical
-// softmax on S = partial(0) + partial(1) (an FP32 sum, the same bits in
-// both), then each accumulates O for its 256 dims. Roles per CTA:
+// One CTA per (batch element, key split, output half): the 128 heads are
+// the MMA's M, S = Q K^T (K = all 512 dims) lands in TMEM with one head per
+// lane, and the CTA accumulates O for its 256 output dims. The two CTAs of
+// a (batch element, split) read the same latent rows (the second read hits
+// L2) and compute the same S and P, so no data moves between CTAs. Q K^T
+// takes dims 0-255 of Q from TMEM and dims 256-511 from shared memory.
+// Roles:
 //   warps 0-3   softmax, thread = head = TMEM lane
-//   warps 4-7   tile producers: 64 keys x 4 column blocks of 64 dims
-//   warp 8      TMEM allocation and MMA issue (one thread)
-// The key tiles cycle through a 3-stage ring; a stage is released when the
-// P V that reads it as V has completed.
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
-    attn_tc_kernel(const __grid_constant__ TcArgs a) {
+//   warps 4-11  tile producers: 64 keys x 4 quarters of 128 dims
+//   warp 12     TMEM allocation and MMA issue (one thread)
+__global__ void __launch_bounds__(kTcThreads, 1) attn_tc_kernel(const __grid_constant__ TcArgs a) {
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_s = smem_addr(smem_raw);
   const uint32_t pad = ((raw_s + 1023u) & ~1023u) - raw_s;
   uint8_t* smem = smem_raw + pad;
   const uint32_t sbase = raw_s + pad;
-  const uint32_t k_s = sbase + kOffK, p_s = sbase + kOffP, x_s = sbase + kOffX;
-  const uint32_t stage_s = sbase + kOffStage;
+  const uint32_t q_s = sbase + kOffQ, own_s = sbase + kOffOwn, other_s = sbase + kOffOther;
+  const uint32_t p_s = sbase + kOffP;
   TcBars* bars = reinterpret_cast<TcBars*>(smem + kOffBar);
   volatile int* abort_flag = &bars->abort_flag;
 
   const int half = blockIdx.x & 1, split = blockIdx.x >> 1, b = blockIdx.y;
-  const uint32_t peer = static_cast<uint32_t>(half ^ 1);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int k0 = split * a.keys_per_split;
   const int k_end = min(a.n, k0 + a.keys_per_split);
   const int T = k_end > k0 ? (k_end - k0 + kTcKeys - 1) / kTcKeys : 0;
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < kTcStages; ++i) {
-      mbar_init(&bars->kv_full[i], 32 * kTcProdWarps);
-      mbar_init(&bars->kv_empty[i], 1);
-      bars->key_mask[i] = 0;
+    for (int i = 0; i < kTcOwnStages; ++i) {
+      mbar_init(&bars->full_own[i], 16 * kTcProdWarps);
+      mbar_init(&bars->empty_own[i], 1);
     }
+    mbar_init(&bars->full_other, 16 * kTcProdWarps);
+    mbar_init(&bars->empty_other, 1);
+    for (int i = 0; i < 4; ++i) bars->key_mask[i] = 0;
     for (int i = 0; i < 2; ++i) {
       mbar_init(&bars->s_full[i], 1);
       mbar_init(&bars->p_full[i], 128);
       mbar_init(&bars->pv_done[i], 1);
     }
-    mbar_init(&bars->x_full[0], 1);
-    mbar_init(&bars->x_full[1], 1);
-    mbar_init(&bars->stage_ready, 128);
-    mbar_init(&bars->stage_free, 1);
     mbar_init(&bars->fin, 1);
     bars->abort_flag = 0;
     mbar_fence_init();
@@ -504,18 +494,32 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
                  "r"(kTmemCols)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  } else {
+    // Q dims 256-511: fp32 (BF16-valued) -> BF16, K-major 128-byte swizzled,
+    // rows >= H zero
+    const float* qb = a.q + static_cast<size_t>(b) * a.H * kTcD + kTcHalf;
+    for (int c = threadIdx.x; c < kTcM * (kTcHalf / 8); c += 32 * kTcMmaWarp) {
+      const int row = c >> 5, dc = c & 31;
+      uint4 v = make_uint4(0, 0, 0, 0);
+      if (row < a.H) {
+        const float4* src = reinterpret_cast<const float4*>(qb + row * kTcD + dc * 8);
+        const float4 x0 = src[0], x1 = src[1];
+        v = make_uint4(pack_bf16x2(x0.x, x0.y), pack_bf16x2(x0.z, x0.w), pack_bf16x2(x1.x, x1.y),
+                       pack_bf16x2(x1.z, x1.w));
+      }
+      st_shared_v4(q_s + sw128_off(row, dc, kTcM), v);
+    }
+    fence_async_smem();
   }
   tc_fence_before();
   __syncthreads();
-  cluster_sync_all();  // both CTAs' barriers are initialised before any remote arrive
   tc_fence_after();
   const uint32_t tmem = bars->tmem_base;
   if (warp < 4) {
-    // this half of Q row h [512] fp32 (BF16-valued) -> BF16 pairs in TMEM
-    // lane h, columns kTmemQ.. (the A operand of Q K^T); rows >= H zero
+    // Q dims 0-255 of row h -> BF16 pairs in TMEM lane h, columns kTmemQ..
     const int h = threadIdx.x;
     const float4* src = reinterpret_cast<const float4*>(
-        a.q + (static_cast<size_t>(b) * a.H + (h < a.H ? h : 0)) * kTcD + half * kTcHalf);
+        a.q + (static_cast<size_t>(b) * a.H + (h < a.H ? h : 0)) * kTcD);
 #pragma unroll 1
     for (int c32 = 0; c32 < kTcHalf / 2; c32 += 32) {
       uint32_t r[32];
@@ -535,65 +539,96 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
 
   if (warp == kTcMmaWarp) {
     // ------------------------------------------------------------ MMA issue
-    if (lane == 0) {
-      constexpr uint32_t idesc_qk = umma_idesc_bf16(kTcM, kTcKeys, false);
-      constexpr uint32_t idesc_pv = umma_idesc_bf16(kTcM, kTcHalf, true);
-      // O += P V for tile jj, V = the tile's stage read MN-major
-      auto issue_pv = [&](int jj, int st) -> bool {
-        const int sb = jj & 1;
-        if (!tc_wait(&bars->p_full[sb], (jj >> 1) & 1, abort_flag, a.err)) return false;
-        tc_fence_after();
+    // The whole warp waits and runs the unrolled issue code; one elected
+    // lane issues. Descriptor addresses advance in 16-byte units.
+    constexpr uint32_t idesc_qk = umma_idesc_bf16(kTcM, kTcKeys, false);
+    constexpr uint32_t idesc_pv = umma_idesc_bf16(kTcM, kTcHalf, true);
+    const uint64_t q_desc = umma_desc(q_s, 16, 1024);
+    // O += P V for tile jj, V = its own-half slot read MN-major
+    auto issue_pv = [&](int jj, int slot) -> bool {
+      const int sb = jj & 1;
+      const bool w = tc_wait(&bars->p_full[sb], (jj >> 1) & 1, abort_flag, a.err);
+      if (!__all_sync(0xffffffffu, w)) return false;
+      tc_fence_after();
+      const uint64_t ad = umma_desc(p_s + sb * kPBytes, 16, 1024);
+      const uint64_t bd = umma_desc(own_s + slot * kHalfTile, kKBlock, 1024);
 #pragma unroll
-        for (int kk = 0; kk < kTcKeys / 16; ++kk) {
-          const uint64_t ad = umma_desc(p_s + sb * kPBytes + kk * 32, 16, 1024);
-          const uint64_t bd = umma_desc(k_s + st * kKBytes + kk * 16 * 128, kKBlock, 1024);
-          umma_bf16(tmem, ad, bd, idesc_pv, (jj > 0 || kk > 0) ? 1u : 0u);
-        }
-        umma_commit(&bars->pv_done[sb]);
-        umma_commit(&bars->kv_empty[st]);
-        return true;
-      };
-      bool ok = true;
-      int st = 0, prev_st = 0;
-      uint32_t ph = 0;
-      for (int j = 0; j < T && ok; ++j) {
-        if (!tc_wait(&bars->kv_full[st], ph, abort_flag, a.err)) { ok = false; break; }
-        tc_fence_after();
-#pragma unroll 4
-        for (int kk = 0; kk < kTcHalf / 16; ++kk) {
-          const uint32_t off = (kk & 3) * 32;  // 16 dims inside the 64-dim swizzle row
-          const uint64_t bd = umma_desc(k_s + st * kKBytes + (kk >> 2) * kKBlock + off, 16, 1024);
-          umma_bf16_ts(tmem + kTmemS + (j & 1) * kTcKeys, tmem + kTmemQ + kk * 8, bd, idesc_qk,
-                       kk > 0 ? 1u : 0u);
-        }
-        umma_commit(&bars->s_full[j & 1]);
-        if (j > 0) ok = issue_pv(j - 1, prev_st);
-        prev_st = st;
-        if (++st == kTcStages) { st = 0; ph ^= 1u; }
-      }
-      if (ok && T > 0) issue_pv(T - 1, prev_st);
-      umma_commit(&bars->fin);
-      mbar_wait(&bars->fin, 0, a.err);
+      for (int kk = 0; kk < kTcKeys / 16; ++kk)
+        umma_bf16_e(tmem, ad + kk * 2, bd + kk * 128, idesc_pv, (jj > 0 || kk > 0) ? 1u : 0u);
+      umma_commit_e(&bars->pv_done[sb]);
+      umma_commit_e(&bars->empty_own[slot]);
+      return true;
+    };
+    // Q K^T over 256 dims of a half-tile (column block kk / 4, 32 bytes into
+    // its swizzle row): Q dims 0-255 come from TMEM, 256-511 from shared
+    // memory. Fully unrolled with compile-time offsets: the issue rate of
+    // this warp bounds the MMA rate.
+    auto qk_tmem_a = [&](uint32_t s_col, uint64_t k_desc, bool first) {
+#pragma unroll
+      for (int kk = 0; kk < kTcHalf / 16; ++kk)
+        umma_bf16_ts_e(s_col, tmem + kTmemQ + kk * 8,
+                       k_desc + ((kk >> 2) * kKBlock + (kk & 3) * 32) / 16, idesc_qk,
+                       (first && kk == 0) ? 0u : 1u);
+    };
+    auto qk_smem_a = [&](uint32_t s_col, uint64_t k_desc, bool first) {
+#pragma unroll
+      for (int kk = 0; kk < kTcHalf / 16; ++kk)
+        umma_bf16_e(s_col, q_desc + ((kk >> 2) * kQBlock + (kk & 3) * 32) / 16,
+                    k_desc + ((kk >> 2) * kKBlock + (kk & 3) * 32) / 16, idesc_qk,
+                    (first && kk == 0) ? 0u : 1u);
+    };
+    const uint64_t other_desc = umma_desc(other_s, 16, 1024);
+    bool ok = true;
+    int slot = 0, prev_slot = 0;
+    uint32_t ph = 0;
+    for (int j = 0; j < T && ok; ++j) {
+      const uint32_t s_col = tmem + kTmemS + (j & 1) * kTcKeys;
+      // the other half of the dims first (its single slot is released as
+      // soon as these MMAs complete), then the own half
+      bool w = tc_wait(&bars->full_other, j & 1, abort_flag, a.err);
+      if (!__all_sync(0xffffffffu, w)) { ok = false; break; }
+      tc_fence_after();
+      if (half == 0)
+        qk_smem_a(s_col, other_desc, true);
+      else
+        qk_tmem_a(s_col, other_desc, true);
+      umma_commit_e(&bars->empty_other);
+      w = tc_wait(&bars->full_own[slot], ph, abort_flag, a.err);
+      if (!__all_sync(0xffffffffu, w)) { ok = false; break; }
+      tc_fence_after();
+      const uint64_t own_desc = umma_desc(own_s + slot * kHalfTile, 16, 1024);
+      if (half == 0)
+        qk_tmem_a(s_col, own_desc, false);
+      else
+        qk_smem_a(s_col, own_desc, false);
+      umma_commit_e(&bars->s_full[j & 1]);
+      // P V of the previous tile runs while the softmax works on this one
+      if (j > 0 && !issue_pv(j - 1, prev_slot)) { ok = false; break; }
+      prev_slot = slot;
+      if (++slot == kTcOwnStages) { slot = 0; ph ^= 1u; }
     }
+    if (ok && T > 0) issue_pv(T - 1, prev_slot);
+    umma_commit_e(&bars->fin);
+    mbar_wait(&bars->fin, 0, a.err);
     __syncwarp();
   } else if (warp >= 4) {
     // ------------------------------------------------- latent tile producer
-    // Thread (r, q) owns keys r and r + 32 of every tile and the 64 dims of
-    // column block q of this half: FP8 codes [256 half + 64 q, +64) with
-    // scale slot 4 half + q, or for half 1, q 3 the 64 BF16 RoPE dims. The
-    // indices of tile j + 2 are read and its rows bulk-prefetched into L2
-    // while tile j is converted; the registers of tile j + 1 are loaded
-    // right after tile j is handed over.
-    constexpr int kSub = kTcKeys / (8 * kTcProdWarps);  // keys per thread
+    // Thread (r, q) owns key r of every tile and dims [128 q, 128 q + 128)
+    // (column blocks 2q, 2q + 1): FP8 codes with scale slots 2q, 2q + 1, or
+    // for q 3 the codes 384-447 (slot 6) and the 64 BF16 RoPE dims; a warp
+    // holds one quarter q for 32 keys. The quarters of this CTA's output half
+    // go to the own ring and wait for P V to release a slot, the others to
+    // the other slot and wait only for Q K^T. The indices of tile j + 3 are
+    // read and the rows of tile j + 2 bulk-prefetched into L2 while tile j
+    // is converted; the registers of tile j + 1 are loaded right after tile
+    // j is handed over.
     const int c = threadIdx.x - 128;
-    const int r = c >> 2, q = c & 3;
-    const bool rope_part = half == 1 && q == 3;
-    const int code_off = half * kTcHalf + q * 64;
-    const int sslot = half * 4 + q;
+    const int r = c & (kTcKeys - 1), q = c / kTcKeys;
+    const bool own = (q >> 1) == half;
     const int* idxb = a.idx + static_cast<size_t>(b) * a.n;
     const long long rbase = static_cast<long long>(b) * a.kv_bstride;
-    auto load_idx = [&](int j, int kk) -> long long {
-      const int key = k0 + j * kTcKeys + r + kk * (8 * kTcProdWarps);
+    auto load_idx = [&](int j) -> long long {
+      const int key = k0 + j * kTcKeys + r;
       return (j < T && key < k_end) ? static_cast<long long>(idxb[key]) : -1;
     };
     auto in_range = [&](long long pos) { return pos >= 0 && pos < a.kv_rows; };
@@ -601,119 +636,137 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
       if (!in_range(pos)) return;
       const long long row = rbase + pos;
       if (a.kv) {
-        if (q == 0) bulk_prefetch_l2(a.kv + row * kTcD + half * kTcHalf, kTcHalf * 4);
+        bulk_prefetch_l2(a.kv + row * kTcD + q * 128, 512);
       } else if (q == 0) {
-        bulk_prefetch_l2(a.cache.codes + row * kTcNope + half * kTcHalf,
-                         half ? kTcNope - kTcHalf : kTcHalf);
-      } else if (q == 1 && half) {
+        bulk_prefetch_l2(a.cache.codes + row * kTcNope, kTcNope);
+      } else if (q == 1) {
         bulk_prefetch_l2(a.cache.rope + row * kTcRope, kTcRope * 2);
       } else if (q == 2) {
         const long long r2 = row & ~1ll;  // the 16-byte pair of scale rows holding this one
         if (r2 + 1 < a.cache.rows) bulk_prefetch_l2(a.cache.scales + r2 * kKvScaleSlots, 16);
       }
     };
-    // per key: q < 3 or half 0: 4 x 16 codes; half 1, q 3: 8 x 8 RoPE BF16 values
-    uint4 raw[kSub][8];
-    uint32_t scode[kSub];
-    auto load_raw = [&](long long pos, int kk) {
+    // q < 3: 8 x 16 codes; q == 3: 4 x 16 codes then 8 x 8 RoPE BF16 values
+    uint4 raw[12];
+    uint32_t sc2 = 0;  // scale codes of the thread's two column blocks
+    auto load_raw = [&](long long pos) {
       if (!in_range(pos) || a.kv) return;
       const long long row = rbase + pos;
-      if (!rope_part) {
-        const uint4* cp = reinterpret_cast<const uint4*>(a.cache.codes + row * kTcNope + code_off);
+      const uint4* cp = reinterpret_cast<const uint4*>(a.cache.codes + row * kTcNope + q * 128);
+      const uint4* rp = reinterpret_cast<const uint4*>(a.cache.rope + row * kTcRope);
 #pragma unroll
-        for (int u = 0; u < 4; ++u) raw[kk][u] = __ldg(cp + u);
-        scode[kk] = a.cache.scales[row * kKvScaleSlots + sslot];
-      } else {
-        const uint4* rp = reinterpret_cast<const uint4*>(a.cache.rope + row * kTcRope);
-#pragma unroll
-        for (int u = 0; u < 8; ++u) raw[kk][u] = __ldg(rp + u);
+      for (int u = 0; u < 12; ++u) {
+        if (q < 3) {
+          if (u < 8) raw[u] = __ldg(cp + u);
+        } else {
+          raw[u] = u < 4 ? __ldg(cp + u) : __ldg(rp + (u - 4));
+        }
       }
+      sc2 = *reinterpret_cast<const uint16_t*>(a.cache.scales + row * kKvScaleSlots + 2 * q);
     };
-    long long p_cur[kSub], p_nxt[kSub];
-#pragma unroll
-    for (int kk = 0; kk < kSub; ++kk) {
-      p_cur[kk] = load_idx(0, kk);
-      p_nxt[kk] = load_idx(1, kk);
-      prefetch_rows(p_cur[kk]);
-      prefetch_rows(p_nxt[kk]);
-      load_raw(p_cur[kk], kk);
-    }
-    int st = 0;
-    uint32_t ph = 0;
-    for (int j = 0; j < T; ++j) {
-      long long p_n2[kSub];
-#pragma unroll
-      for (int kk = 0; kk < kSub; ++kk) {
-        p_n2[kk] = load_idx(j + 2, kk);
-        if (p_cur[kk] >= a.kv_rows && a.err) atomicOr(a.err, kErrIndex);
+    if (c == 0 && T > 0) {
+      // the split's key indices into L2 up front (whole 16-byte blocks
+      // inside the array): the per-tile index loads then miss only to L2
+      const uintptr_t lo = reinterpret_cast<uintptr_t>(idxb + k0);
+      const uintptr_t hi = reinterpret_cast<uintptr_t>(idxb + k_end);
+      for (uintptr_t p0 = (lo + 15) & ~static_cast<uintptr_t>(15); p0 + 16 <= hi; p0 += 16384) {
+        const uintptr_t p1 = p0 + 16384 < hi ? p0 + 16384 : (hi & ~static_cast<uintptr_t>(15));
+        bulk_prefetch_l2(reinterpret_cast<const void*>(p0), static_cast<uint32_t>(p1 - p0));
       }
-      if (!tc_wait(&bars->kv_empty[st], ph ^ 1u, abort_flag, a.err)) break;
-      const uint32_t tile = k_s + st * kKBytes;
+    }
+    long long p_cur = load_idx(0), p_nxt = load_idx(1), p_n2 = load_idx(2);
+    prefetch_rows(p_cur);
+    prefetch_rows(p_nxt);
+    load_raw(p_cur);
+    int slot = 0;
+    uint32_t ph = 0;
+    const int qb = (q & 1) * 16;  // the quarter's first 16-byte chunk in its half-tile
+    for (int j = 0; j < T; ++j) {
+      const long long p_n3 = load_idx(j + 3);
+      if (p_cur >= a.kv_rows && a.err) atomicOr(a.err, kErrIndex);
+      const bool valid = in_range(p_cur);
+      const long long row = rbase + p_cur;
+      const bool w = own ? tc_wait(&bars->empty_own[slot], ph ^ 1u, abort_flag, a.err)
+                         : tc_wait(&bars->empty_other, (j & 1) ^ 1, abort_flag, a.err);
+      if (!w) break;
+      const uint32_t tile = own ? own_s + slot * kHalfTile : other_s;
+      if (!valid) {
 #pragma unroll
-      for (int kk = 0; kk < kSub; ++kk) {
-        const int key = r + kk * (8 * kTcProdWarps);
-        const bool valid = in_range(p_cur[kk]);
-        const long long row = rbase + p_cur[kk];
-        if (!valid) {
+        for (int dc = 0; dc < 16; ++dc)
+          st_shared_v4(tile + sw128_off(r, qb + dc, kTcKeys), make_uint4(0, 0, 0, 0));
+      } else if (a.kv) {
+        const float4* src = reinterpret_cast<const float4*>(a.kv + row * kTcD + q * 128);
+#pragma unroll 4
+        for (int dc = 0; dc < 16; ++dc) {
+          const float4 x0 = __ldg(src + 2 * dc), x1 = __ldg(src + 2 * dc + 1);
+          st_shared_v4(tile + sw128_off(r, qb + dc, kTcKeys),
+                       make_uint4(pack_bf16x2(x0.x, x0.y), pack_bf16x2(x0.z, x0.w),
+                                  pack_bf16x2(x1.x, x1.y), pack_bf16x2(x1.z, x1.w)));
+        }
+      } else {
+        // the integer path unless a scale is out of its range or a code is NaN
+        uint32_t nan = 0;
 #pragma unroll
-          for (int u = 0; u < 8; ++u)
-            st_shared_v4(tile + sw128_off(key, q * 8 + u, kTcKeys), make_uint4(0, 0, 0, 0));
-        } else if (a.kv) {
-          const float4* src =
-              reinterpret_cast<const float4*>(a.kv + row * kTcD + half * kTcHalf + q * 64);
-#pragma unroll 2
+        for (int u = 0; u < 8; ++u)
+          if (q < 3 || u < 4)
+            nan |= e4m3_nan_bytes(raw[u].x) | e4m3_nan_bytes(raw[u].y) |
+                   e4m3_nan_bytes(raw[u].z) | e4m3_nan_bytes(raw[u].w);
+        const uint32_t c0 = sc2 & 0xFFu, c1 = q < 3 ? (sc2 >> 8) & 0xFFu : c0;
+        if (nan == 0 && c0 >= 10 && c0 <= 134 && c1 >= 10 && c1 <= 134) {
+          const uint32_t k0s = (c0 + 120) * 0x00800080u, k1s = (c1 + 120) * 0x00800080u;
+#pragma unroll
           for (int u = 0; u < 8; ++u) {
-            const float4 x0 = __ldg(src + 2 * u), x1 = __ldg(src + 2 * u + 1);
-            st_shared_v4(tile + sw128_off(key, q * 8 + u, kTcKeys),
-                         make_uint4(pack_bf16x2(x0.x, x0.y), pack_bf16x2(x0.z, x0.w),
-                                    pack_bf16x2(x1.x, x1.y), pack_bf16x2(x1.z, x1.w)));
-          }
-        } else if (!rope_part) {
-          const float sc = e8m0_decode(scode[kk]);
-#pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            const uint2 lo = e4m3x4_to_bf16(raw[kk][u].x, sc), hi = e4m3x4_to_bf16(raw[kk][u].y, sc);
-            const uint2 lo2 = e4m3x4_to_bf16(raw[kk][u].z, sc),
-                        hi2 = e4m3x4_to_bf16(raw[kk][u].w, sc);
-            st_shared_v4(tile + sw128_off(key, q * 8 + 2 * u, kTcKeys),
-                         make_uint4(lo.x, lo.y, hi.x, hi.y));
-            st_shared_v4(tile + sw128_off(key, q * 8 + 2 * u + 1, kTcKeys),
-                         make_uint4(lo2.x, lo2.y, hi2.x, hi2.y));
+            if (q < 3 || u < 4) {
+              const uint32_t k2 = u < 4 ? k0s : k1s;
+              const uint2 lo = e4m3x4_to_bf16_mul(raw[u].x, k2),
+                          hi = e4m3x4_to_bf16_mul(raw[u].y, k2);
+              const uint2 lo2 = e4m3x4_to_bf16_mul(raw[u].z, k2),
+                          hi2 = e4m3x4_to_bf16_mul(raw[u].w, k2);
+              st_shared_v4(tile + sw128_off(r, qb + 2 * u, kTcKeys),
+                           make_uint4(lo.x, lo.y, hi.x, hi.y));
+              st_shared_v4(tile + sw128_off(r, qb + 2 * u + 1, kTcKeys),
+                           make_uint4(lo2.x, lo2.y, hi2.x, hi2.y));
+            }
           }
         } else {
 #pragma unroll
-          for (int u = 0; u < 8; ++u)
-            st_shared_v4(tile + sw128_off(key, q * 8 + u, kTcKeys), raw[kk][u]);
+          for (int u = 0; u < 8; ++u) {
+            if (q < 3 || u < 4) {
+              const float sc = e8m0_decode((sc2 >> (8 * (u >> 2))) & 0xFFu);
+              const uint2 lo = e4m3x4_to_bf16(raw[u].x, sc), hi = e4m3x4_to_bf16(raw[u].y, sc);
+              const uint2 lo2 = e4m3x4_to_bf16(raw[u].z, sc), hi2 = e4m3x4_to_bf16(raw[u].w, sc);
+              st_shared_v4(tile + sw128_off(r, qb + 2 * u, kTcKeys),
+                           make_uint4(lo.x, lo.y, hi.x, hi.y));
+              st_shared_v4(tile + sw128_off(r, qb + 2 * u + 1, kTcKeys),
+                           make_uint4(lo2.x, lo2.y, hi2.x, hi2.y));
+            }
+          }
         }
-        // validity mask of the tile's keys (bit key), one byte per 8 keys
-        const uint32_t vb = __ballot_sync(0xffffffffu, valid);
-        if (lane == 0) {
-          uint32_t m8 = 0;
-          for (int k = 0; k < 8; ++k) m8 |= ((vb >> (4 * k)) & 1u) << k;
-          reinterpret_cast<volatile uint8_t*>(&bars->key_mask[st])[(warp - 4) + kk * kTcProdWarps] =
-              static_cast<uint8_t>(m8);
+        if (q == 3) {
+#pragma unroll
+          for (int u = 0; u < 8; ++u)
+            st_shared_v4(tile + sw128_off(r, 24 + u, kTcKeys), raw[4 + u]);
         }
       }
+      // validity mask of the tile's keys (bit r), written by the warps of the
+      // first own quarter
+      const uint32_t vb = __ballot_sync(0xffffffffu, valid);
+      if (q == 2 * half && lane == 0)
+        reinterpret_cast<volatile uint32_t*>(&bars->key_mask[j & 3])[r >> 5] = vb;
       __syncwarp();
       fence_async_smem();
-      mbar_arrive(&bars->kv_full[st]);
-#pragma unroll
-      for (int kk = 0; kk < kSub; ++kk) {
-        prefetch_rows(p_n2[kk]);
-        load_raw(p_nxt[kk], kk);
-        p_cur[kk] = p_nxt[kk];
-        p_nxt[kk] = p_n2[kk];
-      }
-      if (++st == kTcStages) { st = 0; ph ^= 1u; }
+      mbar_arrive(own ? &bars->full_own[slot] : &bars->full_other);
+      prefetch_rows(p_n2);
+      load_raw(p_nxt);
+      p_cur = p_nxt;
+      p_nxt = p_n2;
+      p_n2 = p_n3;
+      if (++slot == kTcOwnStages) { slot = 0; ph ^= 1u; }
     }
   } else {
     // --------------------------------------------------------------- softmax
     const int h = threadIdx.x;  // head = TMEM lane
     const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
-    const uint32_t row_off = h * (kTcKeys * 4);  // this head's row in a partial-score tile
-    const uint32_t x_peer = cluster_map(x_s, peer);
-    const uint32_t x_full_peer = cluster_map(smem_addr(&bars->x_full[0]), peer);
-    const uint32_t stage_free_peer = cluster_map(smem_addr(&bars->stage_free), peer);
     // scores in log2 units: t = dot * scale * log2(e), weights 2^(t - m)
     const float sc2 = a.scale * kLog2e;
     float m_run = -INFINITY, den = 0.0f;
@@ -722,49 +775,24 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
     uint32_t kph = 0;
     for (int j = 0; j < T; ++j) {
       const int sb = j & 1;
+      // full_own (its producers wrote the key mask) cannot run a phase
+      // ahead: tile j + 3's own part waits for P V of tile j
       bool w = tc_wait(&bars->s_full[sb], (j >> 1) & 1, abort_flag, a.err);
-      w = w && tc_wait(&bars->kv_full[kst], kph, abort_flag, a.err);
-      // the staging tile is free once the peer holds the previous one
-      if (j > 0) w = w && tc_wait_peer(&bars->stage_free, (j - 1) & 1, abort_flag, a.err);
+      w = w && tc_wait(&bars->full_own[kst], kph, abort_flag, a.err);
       if (!__all_sync(0xffffffffu, w)) { ok = false; break; }
       tc_fence_after();
-      // this CTA's partial scores -> staging tile -> one bulk copy into the
-      // peer's receive buffer sb
+      const unsigned long long mask =
+          *reinterpret_cast<volatile unsigned long long*>(&bars->key_mask[j & 3]);
+      float s[kTcKeys];
+      float tmax = -INFINITY;
 #pragma unroll
       for (int c32 = 0; c32 < kTcKeys; c32 += 32) {
         uint32_t r[32];
         tmem_ld32(tmem + lane_base + kTmemS + sb * kTcKeys + c32, r);
 #pragma unroll
-        for (int cc = 0; cc < 8; ++cc)
-          st_shared_v4(stage_s + row_off + (((c32 / 4 + cc) ^ (h & 7)) << 4),
-                       make_uint4(r[4 * cc], r[4 * cc + 1], r[4 * cc + 2], r[4 * cc + 3]));
-      }
-      fence_async_smem();
-      mbar_arrive(&bars->stage_ready);
-      if (h == 0 && tc_wait(&bars->stage_ready, j & 1, abort_flag, a.err)) {
-        mbar_arrive_expect_tx(&bars->x_full[sb], kXBytes);  // the peer's tile j, arriving here
-        bulk_s2peer(x_peer + sb * kXBytes, stage_s, kXBytes, x_full_peer + sb * 8);
-      }
-      const bool wx = tc_wait_peer(&bars->x_full[sb], (j >> 1) & 1, abort_flag, a.err);
-      if (!__all_sync(0xffffffffu, wx)) { ok = false; break; }
-      if (h == 0) mbar_arrive_remote(stage_free_peer);  // the peer's copy has landed here
-      const unsigned long long mask =
-          *reinterpret_cast<volatile unsigned long long*>(&bars->key_mask[kst]);
-      // S = own partial + the peer's (the same FP32 sum in both CTAs)
-      float s[kTcKeys];
-      float tmax = -INFINITY;
-#pragma unroll
-      for (int c4 = 0; c4 < kTcKeys / 4; ++c4) {
-        const uint32_t off = row_off + ((c4 ^ (h & 7)) << 4);
-        const uint4 u = ld_shared_v4(stage_s + off);
-        const uint4 v = ld_shared_v4(x_s + sb * kXBytes + off);
-        const uint32_t mine[4] = {u.x, u.y, u.z, u.w};
-        const uint32_t other[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const int k = 4 * c4 + i;
-          const float sum = __uint_as_float(mine[i]) + __uint_as_float(other[i]);
-          s[k] = ((mask >> k) & 1ull) ? sum * sc2 : -INFINITY;
+        for (int i = 0; i < 32; ++i) {
+          const int k = c32 + i;
+          s[k] = ((mask >> k) & 1ull) ? __uint_as_float(r[i]) * sc2 : -INFINITY;
           tmax = fmaxf(tmax, s[k]);
         }
       }
@@ -825,10 +853,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
       fence_async_smem();
       tc_fence_before();
       mbar_arrive(&bars->p_full[sb]);
-      if (++kst == kTcStages) { kst = 0; kph ^= 1u; }
+      if (++kst == kTcOwnStages) { kst = 0; kph ^= 1u; }
     }
-    // the last partial sent has landed in the peer before this CTA may end
-    if (ok && T > 0) ok = tc_wait_peer(&bars->stage_free, (T - 1) & 1, abort_flag, a.err) && ok;
     // epilogue: O partial row, m and den
     const size_t prow = (static_cast<size_t>(b) * a.splits + split) * a.H + h;
     bool have = ok && T > 0;
@@ -862,7 +888,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
   }
   tc_fence_before();
   __syncthreads();
-  cluster_sync_all();  // no CTA leaves while its peer may still write to it
   tc_fence_after();
   if (warp == kTcMmaWarp)
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),

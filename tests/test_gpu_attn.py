@@ -159,6 +159,30 @@ def test_attn_tensor_core_fp8_cache_batched_rope(cuda, orc):
         rowwise_check(got[b], want, mag)
 
 
+def test_attn_fp8_cache_subnormal_codes(cuda, orc):
+    """Groups whose small members quantise to E4M3 subnormal codes (one large
+    value per group of 64 sets the scale): the tile conversion must keep
+    them exactly. Few keys, so a lost subnormal changes an output element by
+    its whole value."""
+    rng = np.random.default_rng(21)
+    H, n = 128, 3
+    raw = bf16_vals(rng, (n, D), scale=0.004)
+    raw[:, :NOPE:64] = 400.0                         # scale 2^0: |x| < 2^-6 -> subnormal
+    raw[1, 1:NOPE:64] = -2.0 ** -9                   # the smallest subnormal
+    raw = (raw.view(np.uint32) & 0xFFFF0000).view(np.float32)
+    cache = cuda.LatentCache(rows=n)
+    cache.write(dev(raw), dev(np.arange(n, dtype=np.int64)))
+    kv = qat_rows(orc, raw)
+    tiny = np.abs(kv[:, :NOPE]) < 2.0 ** -6
+    assert np.count_nonzero(tiny & (kv[:, :NOPE] != 0)) > 100
+    q = bf16_vals(rng, (1, H, D), scale=0.01)
+    sink = np.full(H, -3.0, np.float32)
+    idx = np.arange(n, dtype=np.int32)[None, :]
+    got = run_attn(cuda, q, sink, idx, D ** -0.5, cache=cache, kv_rows=n)
+    want = orc.sparse_attn(q[0], kv, sink, idx[0], D ** -0.5)
+    rowwise_check(got[0], want, attn_magnitude(q[0], kv, sink, idx[0], D ** -0.5))
+
+
 def test_attn_rescale_path(cuda, orc):
     """Key norms grow along the index order so the running max rises on
     almost every tile (exercises the O rescale in TMEM)."""
