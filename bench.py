@@ -43,8 +43,8 @@ SHARED_FP8_BYTES = 2 * (I * H + (I // 128) * (H // 128)) + (H * I + (H // 128) *
 ROUTER_BYTES = E * H * 2
 METRIC = "decode tok/s through one MoE layer (config 2: H7168, I2048, 256+1 experts, top-8)"
 # DRAM bytes of one step's two routed GEMV launches (8 experts), from ncu:
-# gate/up 125.3 MB read + 4.7 MB written, down 62.5 MB + 0.8 MB
-FP4_TRAFFIC_PER_STEP = (125.28 + 4.67 + 62.47 + 0.80) * 1e6
+# gate/up 125.3 MB read + 4.2 MB written, down 62.5 MB + 0.8 MB
+FP4_TRAFFIC_PER_STEP = (125.28 + 4.16 + 62.47 + 0.80) * 1e6
 
 
 def parse():
