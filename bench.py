@@ -53,6 +53,8 @@ def parse():
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--ep-exchange", default="p2p", choices=["p2p", "nccl"],
+                    help="expert-parallel slot exchange: peer-memory kernels or NCCL all-reduce")
     ap.add_argument("--tokens", type=int, default=1, help="tokens per step (M)")
     ap.add_argument("--layers", type=int, default=4, help="independent layer weight sets")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
@@ -298,12 +300,39 @@ def main():
         layers.append((lay, dsv4cuda.MoeLayer(lay, max_tokens=M, device=True,
                                               expert_range=erange)))
     torch.cuda.synchronize()
+    p2p = ep and args.ep_exchange == "p2p"
+    ipc_own, ipc_peers = [], []
+    if p2p:
+        # one exchange buffer per layer and rank, mapped into every rank
+        handles = []
+        for _, L in layers:
+            addr, h = dsv4cuda.ipc_alloc(L.ep_buffer_bytes())
+            ipc_own.append(addr)
+            handles.append(h)
+        all_h = [None] * world
+        dist.all_gather_object(all_h, handles)
+        for li, (_, L) in enumerate(layers):
+            addrs = []
+            for r in range(world):
+                if r == rank:
+                    addrs.append(ipc_own[li])
+                else:
+                    a = dsv4cuda.ipc_open(all_h[r][li])
+                    ipc_peers.append(a)
+                    addrs.append(a)
+            L.ep_attach(rank, world, addrs)
+        dist.barrier()
 
     def layer_forward(L, xin, out, s):
-        """One MoE layer; expert parallel: local experts, NCCL sum of the
-        zero-padded routed slots, ordered combine (bit-identical to 1 GPU)."""
+        """One MoE layer; expert parallel: local experts, then the routed
+        slots reach every rank either through the peer-memory exchange
+        kernels or as an NCCL sum of the zero-padded slots, then the ordered
+        combine (bit-identical to 1 GPU either way)."""
         if not ep:
             L.forward(xin, out, stream=s)
+            return
+        if p2p:
+            L.forward_ep(xin, out, stream=s)
             return
         L.forward_local(xin, stream=s)
         dist.all_reduce(L.routed_slots(M), op=dist.ReduceOp.SUM)
@@ -452,7 +481,8 @@ def main():
                        "moe_inter": I, "experts": args.experts, "topk": TOPK, "shared": "fp8",
                        "tokens_per_step": M, "layers_cycled": args.layers,
                        "l2": "inputs larger than L2: each step reads a different layer's "
-                             "~235 MB of weights", "parallelism": f"ep{world}"},
+                             "~235 MB of weights", "parallelism": f"ep{world}",
+                       "ep_exchange": (args.ep_exchange if ep else None)},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "traffic": FP4_TRAFFIC_PER_STEP,
                          "traffic_source": "ncu dram__bytes_read+write of the gate/up and down "
@@ -481,6 +511,14 @@ def main():
         gr.reset()
     graphs.clear()
     g = gr = None  # noqa: F841  (the capture loop's last graph)
+    if p2p:
+        # every rank stops touching peer memory before any buffer is unmapped
+        dist.barrier()
+        for a in ipc_peers:
+            dsv4cuda.ipc_close(a)
+        dist.barrier()
+        for a in ipc_own:
+            dsv4cuda.ipc_free(a)
     for _, L in layers:
         L.close()
     if dist:

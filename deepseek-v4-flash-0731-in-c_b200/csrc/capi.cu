@@ -23,6 +23,7 @@
 #include "attn.cuh"
 #include "sample.cuh"
 #include "snapshot.cuh"
+#include "ep.cuh"
 #include "../../include/dsv4_cuda.h"
 
 #define DSV4_API extern "C" __attribute__((visibility("default")))
@@ -309,6 +310,9 @@ struct dsv4cuda_moe_layer {
   // dsv4cuda_moe_forward_host: the forward of n tokens (d_x -> d_out)
   // captured once into a CUDA graph per n and replayed after that
   std::vector<cudaGraphExec_t> host_graphs;
+  // expert-parallel exchange over peer memory (dsv4cuda_moe_ep_attach)
+  dsv4::EpExchange ep{};
+  bool ep_attached = false;
 };
 
 namespace {
@@ -715,6 +719,107 @@ DSV4_API int dsv4cuda_moe_forward_local(dsv4cuda_moe_layer* L, const float* x,
 }
 
 DSV4_API float* dsv4cuda_moe_routed_slots(dsv4cuda_moe_layer* L) { return L ? L->ws.routed : nullptr; }
+
+DSV4_API size_t dsv4cuda_moe_ep_buffer_bytes(const dsv4cuda_moe_layer* L) {
+  return L ? dsv4::ep_exchange_bytes(L->max_tokens * L->cfg.topk, L->cfg.hidden) : 0;
+}
+
+DSV4_API int dsv4cuda_moe_ep_attach(dsv4cuda_moe_layer* L, int rank, int world, void* const* bufs) {
+  if (!L || !bufs || world < 1 || world > dsv4::kEpMaxRanks || rank < 0 || rank >= world) {
+    record_error("dsv4cuda_moe_ep_attach: bad arguments");
+    return -1;
+  }
+  for (int r = 0; r < world; ++r) {
+    if (!bufs[r] || (reinterpret_cast<uintptr_t>(bufs[r]) & 255) != 0) {
+      record_error("dsv4cuda_moe_ep_attach: buffer %d missing or not 256-byte aligned", r);
+      return -1;
+    }
+  }
+  if (L->cfg.hidden % 4 != 0) {
+    record_error("dsv4cuda_moe_ep_attach: hidden %% 4 != 0");
+    return -1;
+  }
+  cudaError_t e = cudaMemset(bufs[rank], 0, dsv4cuda_moe_ep_buffer_bytes(L));
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) { record_error("ep_attach memset: %s", cudaGetErrorString(e)); return -1; }
+  L->ep = dsv4::ep_exchange_make(bufs, rank, world, L->max_tokens * L->cfg.topk, L->cfg.hidden);
+  L->ep_attached = true;
+  return 0;
+}
+
+DSV4_API int dsv4cuda_moe_ep_push(dsv4cuda_moe_layer* L, int n_tokens, void* stream) {
+  if (!L || !L->ep_attached || n_tokens < 0 || n_tokens > L->max_tokens) {
+    record_error("dsv4cuda_moe_ep_push: bad arguments or no exchange attached");
+    return -1;
+  }
+  cudaError_t e = dsv4::ep_push(L->ep, L->ws.routed, L->ws.idx, n_tokens * L->cfg.topk,
+                                L->cfg.hidden, L->cfg.expert_lo, dsv4::moe_local_hi(L->cfg),
+                                static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) { record_error("ep_push: %s", cudaGetErrorString(e)); return -1; }
+  return 0;
+}
+
+DSV4_API int dsv4cuda_moe_ep_combine(dsv4cuda_moe_layer* L, int n_tokens, float* out, void* stream) {
+  if (!L || !L->ep_attached || !out || n_tokens < 0 || n_tokens > L->max_tokens) {
+    record_error("dsv4cuda_moe_ep_combine: bad arguments or no exchange attached");
+    return -1;
+  }
+  const bool has_shared = L->cfg.shared_kind != dsv4::kSharedNone && L->w.sh1 != nullptr;
+  cudaError_t e = dsv4::ep_combine(L->ep, has_shared ? L->ws.shared : nullptr, L->ws.idx,
+                                   n_tokens, L->cfg.topk, L->cfg.hidden, out,
+                                   dsv4::device_error_word(), static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) { record_error("ep_combine: %s", cudaGetErrorString(e)); return -1; }
+  return 0;
+}
+
+DSV4_API int dsv4cuda_moe_forward_ep(dsv4cuda_moe_layer* L, const float* x, const int* token_ids,
+                                     int n_tokens, float* out, void* stream) {
+  if (!L || !L->ep_attached) {
+    record_error("dsv4cuda_moe_forward_ep: no exchange attached");
+    return -1;
+  }
+  if (dsv4cuda_moe_forward_local(L, x, token_ids, n_tokens, stream) != 0) return -1;
+  if (dsv4cuda_moe_ep_push(L, n_tokens, stream) != 0) return -1;
+  return dsv4cuda_moe_ep_combine(L, n_tokens, out, stream);
+}
+
+DSV4_API int dsv4cuda_ipc_alloc(size_t bytes, void** ptr, unsigned char* handle) {
+  if (!ptr || !handle || bytes == 0) { record_error("dsv4cuda_ipc_alloc: bad arguments"); return -1; }
+  *ptr = nullptr;
+  cudaError_t e = cudaMalloc(ptr, bytes);
+  if (e != cudaSuccess) { record_error("ipc cudaMalloc: %s", cudaGetErrorString(e)); return -1; }
+  cudaIpcMemHandle_t h;
+  e = cudaIpcGetMemHandle(&h, *ptr);
+  if (e != cudaSuccess) {
+    cudaFree(*ptr);
+    *ptr = nullptr;
+    record_error("cudaIpcGetMemHandle: %s", cudaGetErrorString(e));
+    return -1;
+  }
+  std::memcpy(handle, &h, sizeof(h));
+  return 0;
+}
+
+DSV4_API int dsv4cuda_ipc_open(const unsigned char* handle, void** ptr) {
+  if (!ptr || !handle) { record_error("dsv4cuda_ipc_open: bad arguments"); return -1; }
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle, sizeof(h));
+  cudaError_t e = cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess) { record_error("cudaIpcOpenMemHandle: %s", cudaGetErrorString(e)); return -1; }
+  return 0;
+}
+
+DSV4_API int dsv4cuda_ipc_close(void* ptr) {
+  cudaError_t e = cudaIpcCloseMemHandle(ptr);
+  if (e != cudaSuccess) { record_error("cudaIpcCloseMemHandle: %s", cudaGetErrorString(e)); return -1; }
+  return 0;
+}
+
+DSV4_API int dsv4cuda_ipc_free(void* ptr) {
+  cudaError_t e = cudaFree(ptr);
+  if (e != cudaSuccess) { record_error("ipc cudaFree: %s", cudaGetErrorString(e)); return -1; }
+  return 0;
+}
 
 DSV4_API int dsv4cuda_moe_combine(dsv4cuda_moe_layer* L, int n_tokens, float* out, void* stream) {
   if (!L || !out || n_tokens < 0 || n_tokens > L->max_tokens) {

@@ -66,6 +66,24 @@ lib.dsv4cuda_moe_routed_slots.restype = C.c_void_p
 lib.dsv4cuda_moe_routed_slots.argtypes = [vp]
 lib.dsv4cuda_moe_combine.restype = C.c_int
 lib.dsv4cuda_moe_combine.argtypes = [vp, C.c_int, vp, vp]
+lib.dsv4cuda_moe_ep_buffer_bytes.restype = C.c_size_t
+lib.dsv4cuda_moe_ep_buffer_bytes.argtypes = [vp]
+lib.dsv4cuda_moe_ep_attach.restype = C.c_int
+lib.dsv4cuda_moe_ep_attach.argtypes = [vp, C.c_int, C.c_int, C.POINTER(vp)]
+lib.dsv4cuda_moe_forward_ep.restype = C.c_int
+lib.dsv4cuda_moe_forward_ep.argtypes = [vp, vp, vp, C.c_int, vp, vp]
+lib.dsv4cuda_moe_ep_push.restype = C.c_int
+lib.dsv4cuda_moe_ep_push.argtypes = [vp, C.c_int, vp]
+lib.dsv4cuda_moe_ep_combine.restype = C.c_int
+lib.dsv4cuda_moe_ep_combine.argtypes = [vp, C.c_int, vp, vp]
+lib.dsv4cuda_ipc_alloc.restype = C.c_int
+lib.dsv4cuda_ipc_alloc.argtypes = [C.c_size_t, C.POINTER(vp), C.c_char_p]
+lib.dsv4cuda_ipc_open.restype = C.c_int
+lib.dsv4cuda_ipc_open.argtypes = [C.c_char_p, C.POINTER(vp)]
+lib.dsv4cuda_ipc_close.restype = C.c_int
+lib.dsv4cuda_ipc_close.argtypes = [vp]
+lib.dsv4cuda_ipc_free.restype = C.c_int
+lib.dsv4cuda_ipc_free.argtypes = [vp]
 
 
 class Dsv4CudaError(RuntimeError):
@@ -262,6 +280,29 @@ def moe_forward_noalloc(layer: dict, x, out, token_ids=None, stream=None):
                                             x.shape[0], out.data_ptr(), stream))
 
 
+def ipc_alloc(nbytes):
+    """Device buffer exportable to other processes: (address, 64-byte handle)."""
+    ptr = C.c_void_p()
+    h = C.create_string_buffer(64)
+    _check(lib.dsv4cuda_ipc_alloc(nbytes, C.byref(ptr), h))
+    return int(ptr.value), bytes(h.raw)
+
+
+def ipc_open(handle):
+    """Maps another process's buffer (ipc_alloc handle) here; returns its address."""
+    ptr = C.c_void_p()
+    _check(lib.dsv4cuda_ipc_open(C.create_string_buffer(bytes(handle), 64), C.byref(ptr)))
+    return int(ptr.value)
+
+
+def ipc_close(addr):
+    _check(lib.dsv4cuda_ipc_close(C.c_void_p(addr)))
+
+
+def ipc_free(addr):
+    _check(lib.dsv4cuda_ipc_free(C.c_void_p(addr)))
+
+
 class MoeLayer:
     """One MoE layer resident in HBM (dsv4cuda_moe_*).
 
@@ -325,6 +366,28 @@ class MoeLayer:
     def combine(self, n_tokens, out, stream=None):
         """Ordered combine of the (summed) routed slots and the shared expert."""
         _check(lib.dsv4cuda_moe_combine(self.handle, n_tokens, out.data_ptr(), _stream(stream)))
+
+    def ep_buffer_bytes(self):
+        """Bytes of this layer's exchange buffer for the P2P expert parallelism."""
+        return int(lib.dsv4cuda_moe_ep_buffer_bytes(self.handle))
+
+    def ep_attach(self, rank, world, bufs):
+        """bufs[r]: device address (int) of rank r's exchange buffer here."""
+        arr = (vp * world)(*[C.c_void_p(int(b)) for b in bufs])
+        _check(lib.dsv4cuda_moe_ep_attach(self.handle, rank, world, arr))
+
+    def forward_ep(self, x, out, token_ids=None, stream=None):
+        """Router, local experts, shared expert, P2P slot exchange, combine."""
+        _check(lib.dsv4cuda_moe_forward_ep(self.handle, x.data_ptr(),
+                                           None if token_ids is None else token_ids.data_ptr(),
+                                           x.shape[0], out.data_ptr(), _stream(stream)))
+
+    def ep_push(self, n_tokens, stream=None):
+        _check(lib.dsv4cuda_moe_ep_push(self.handle, n_tokens, _stream(stream)))
+
+    def ep_combine(self, n_tokens, out, stream=None):
+        _check(lib.dsv4cuda_moe_ep_combine(self.handle, n_tokens, out.data_ptr(),
+                                           _stream(stream)))
 
     def close(self):
         if self.handle:

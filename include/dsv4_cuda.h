@@ -267,6 +267,43 @@ int dsv4cuda_moe_forward_local(dsv4cuda_moe_layer *L, const float *x, const int 
 float *dsv4cuda_moe_routed_slots(dsv4cuda_moe_layer *L);
 int dsv4cuda_moe_combine(dsv4cuda_moe_layer *L, int n_tokens, float *out, void *stream);
 
+/* Expert parallelism without a collective: the slot exchange runs over peer
+ * memory (NVLink P2P) inside two kernels of the forward.
+ *   dsv4cuda_moe_ep_buffer_bytes  size of one rank's exchange buffer
+ *                                 (flags, counters, 2 x [max_tokens*topk][H]
+ *                                 fp32 slots);
+ *   dsv4cuda_moe_ep_attach        bufs[r] = rank r's exchange buffer as
+ *                                 mapped in this process (bufs[rank] is this
+ *                                 rank's own, e.g. from dsv4cuda_ipc_alloc;
+ *                                 the others from dsv4cuda_ipc_open); zeroes
+ *                                 this rank's buffer, so every rank attaches
+ *                                 before any rank runs a forward;
+ *   dsv4cuda_moe_forward_ep       router + local experts + shared expert,
+ *                                 then this rank's slots are written into
+ *                                 every rank's buffer and a step epoch into
+ *                                 each peer's flags, then the ordered combine
+ *                                 waits (bounded: a peer that never arrives
+ *                                 sets bit 3 of the device error word) for
+ *                                 every peer's epoch. Output bit-identical to
+ *                                 the single-device layer; no host sync, so
+ *                                 the call can be captured in a CUDA graph.
+ * Ranks may also be emulated in one process on one device (bufs in the same
+ * memory) when every rank's forward is issued before any rank waits, i.e.
+ * in stream order on one stream. */
+size_t dsv4cuda_moe_ep_buffer_bytes(const dsv4cuda_moe_layer *L);
+int dsv4cuda_moe_ep_attach(dsv4cuda_moe_layer *L, int rank, int world, void *const *bufs);
+int dsv4cuda_moe_forward_ep(dsv4cuda_moe_layer *L, const float *x, const int *token_ids,
+                            int n_tokens, float *out, void *stream);
+/* The exchange's two halves, separately (dsv4cuda_moe_forward_local first). */
+int dsv4cuda_moe_ep_push(dsv4cuda_moe_layer *L, int n_tokens, void *stream);
+int dsv4cuda_moe_ep_combine(dsv4cuda_moe_layer *L, int n_tokens, float *out, void *stream);
+
+/* Device memory shared across processes (CUDA IPC): handle = 64 bytes. */
+int dsv4cuda_ipc_alloc(size_t bytes, void **ptr, unsigned char *handle);
+int dsv4cuda_ipc_open(const unsigned char *handle, void **ptr);
+int dsv4cuda_ipc_close(void *ptr);
+int dsv4cuda_ipc_free(void *ptr);
+
 /* ---------------------------------------------------------------------
  * Latent KV cache and decode attention.
  *
