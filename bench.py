@@ -53,8 +53,12 @@ def parse():
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--ep-mode", default="tokens", choices=["tokens", "replicated"],
+                    help="N > 1: each rank brings its own --tokens tokens (weak scaling, "
+                         "tokens gathered and slots returned over peer memory) or every rank "
+                         "runs the same tokens (strong scaling)")
     ap.add_argument("--ep-exchange", default="p2p", choices=["p2p", "nccl"],
-                    help="expert-parallel slot exchange: peer-memory kernels or NCCL all-reduce")
+                    help="replicated mode's slot exchange: peer-memory kernels or NCCL all-reduce")
     ap.add_argument("--tokens", type=int, default=1, help="tokens per step (M)")
     ap.add_argument("--layers", type=int, default=4, help="independent layer weight sets")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
@@ -253,7 +257,8 @@ def run_reference_arm(args, rank, world):
     line = {
         "impl": "reference", "metric": METRIC, "value": tps, "unit": "tok/s",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": 1e3 / tps, "higher_is_better": True, "scaling": "strong",
+        "ms_per_step": 1e3 / tps, "higher_is_better": True,
+        "scaling": "strong" if args.ep_mode == "replicated" else "weak",
         "vs_baseline": None, "dtype": "fp4e2m1*e4m3->f32", "data": "synthetic",
         "config": {"workload": "config 2 MoE layer op, decode M=1", "hidden": H,
                    "moe_inter": I, "experts": E, "topk": TOPK, "shared": "fp8",
@@ -293,14 +298,16 @@ def main():
 
     M = args.tokens
     ep = world > 1
+    tok_mode = ep and args.ep_mode == "tokens"
+    M_all = M * world if tok_mode else M  # tokens each rank's layer routes per step
     erange = (rank * args.experts // world, (rank + 1) * args.experts // world) if ep else None
     layers = []
     for li in range(args.layers):
         lay = make_device_layer(torch, 1000 + li, dev, args.experts, args.inter, erange)
-        layers.append((lay, dsv4cuda.MoeLayer(lay, max_tokens=M, device=True,
+        layers.append((lay, dsv4cuda.MoeLayer(lay, max_tokens=M_all, device=True,
                                               expert_range=erange)))
     torch.cuda.synchronize()
-    p2p = ep and args.ep_exchange == "p2p"
+    p2p = ep and (tok_mode or args.ep_exchange == "p2p")
     ipc_own, ipc_peers = [], []
     if p2p:
         # one exchange buffer per layer and rank, mapped into every rank
@@ -331,13 +338,16 @@ def main():
         if not ep:
             L.forward(xin, out, stream=s)
             return
+        if tok_mode:
+            L.forward_ep_tokens(xin, out, stream=s)
+            return
         if p2p:
             L.forward_ep(xin, out, stream=s)
             return
         L.forward_local(xin, stream=s)
         dist.all_reduce(L.routed_slots(M), op=dist.ReduceOp.SUM)
         L.combine(M, out, stream=s)
-    rng = np.random.default_rng(7)
+    rng = np.random.default_rng(7 + (1000 * rank if tok_mode else 0))  # own tokens per rank
     pool = 32
     x_host = bf16_tokens(rng, pool, M)
     x_dev = torch.from_numpy(x_host).to(dev)
@@ -390,7 +400,7 @@ def main():
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
     ms_per_step = ms / args.steps
-    value = M * args.steps / (ms / 1e3)
+    value = M * world * args.steps / (ms / 1e3) if tok_mode else M * args.steps / (ms / 1e3)
 
     # ---- expert-GEMV roofline: each layer's forward captured once more into
     # a graph whose event nodes bracket the routed gate/up and down launches
@@ -423,7 +433,7 @@ def main():
             lg_ms += c_.value
             sl_ms += d_.value
             n_timed += 1
-            idx, _, fb = L.last_routes(M)
+            idx, _, fb = L.last_routes(M_all)
             U_total += len(np.unique(idx))
             fallbacks = fb
             n_fw += 1
@@ -452,7 +462,7 @@ def main():
     if not args.no_e2e:
         if ep:
             e2e_val = run_e2e_graphs(torch, dist, args, graphs, xin, out_dev, x_host, M, pool,
-                                     stream, dev)
+                                     stream, dev) * (world if tok_mode else 1)
         else:
             e2e_val = run_e2e(args, layers, x_host, M, pool, lib, dsv4cuda)
 
@@ -475,14 +485,17 @@ def main():
         line = {
             "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
-            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "higher_is_better": True,
+            "scaling": "strong" if (ep and not tok_mode) else "weak", "vs_baseline": None,
             "dtype": "fp4e2m1*e4m3->f32", "data": "synthetic",
             "config": {"workload": "config 2 MoE layer op, decode M=%d" % M, "hidden": H,
                        "moe_inter": I, "experts": args.experts, "topk": TOPK, "shared": "fp8",
-                       "tokens_per_step": M, "layers_cycled": args.layers,
+                       "tokens_per_step": M_all if tok_mode else M, "tokens_per_gpu": M,
+                       "layers_cycled": args.layers,
                        "l2": "inputs larger than L2: each step reads a different layer's "
                              "~235 MB of weights", "parallelism": f"ep{world}",
-                       "ep_exchange": (args.ep_exchange if ep else None)},
+                       "ep_mode": (args.ep_mode if ep else None),
+                       "ep_exchange": (("p2p" if p2p else "nccl") if ep else None)},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "traffic": FP4_TRAFFIC_PER_STEP,
                          "traffic_source": "ncu dram__bytes_read+write of the gate/up and down "

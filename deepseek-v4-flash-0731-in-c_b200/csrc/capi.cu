@@ -721,7 +721,8 @@ DSV4_API int dsv4cuda_moe_forward_local(dsv4cuda_moe_layer* L, const float* x,
 DSV4_API float* dsv4cuda_moe_routed_slots(dsv4cuda_moe_layer* L) { return L ? L->ws.routed : nullptr; }
 
 DSV4_API size_t dsv4cuda_moe_ep_buffer_bytes(const dsv4cuda_moe_layer* L) {
-  return L ? dsv4::ep_exchange_bytes(L->max_tokens * L->cfg.topk, L->cfg.hidden) : 0;
+  return L ? dsv4::ep_exchange_bytes(L->max_tokens * L->cfg.topk, L->max_tokens, L->cfg.hidden)
+           : 0;
 }
 
 DSV4_API int dsv4cuda_moe_ep_attach(dsv4cuda_moe_layer* L, int rank, int world, void* const* bufs) {
@@ -742,7 +743,8 @@ DSV4_API int dsv4cuda_moe_ep_attach(dsv4cuda_moe_layer* L, int rank, int world, 
   cudaError_t e = cudaMemset(bufs[rank], 0, dsv4cuda_moe_ep_buffer_bytes(L));
   if (e == cudaSuccess) e = cudaDeviceSynchronize();
   if (e != cudaSuccess) { record_error("ep_attach memset: %s", cudaGetErrorString(e)); return -1; }
-  L->ep = dsv4::ep_exchange_make(bufs, rank, world, L->max_tokens * L->cfg.topk, L->cfg.hidden);
+  L->ep = dsv4::ep_exchange_make(bufs, rank, world, L->max_tokens * L->cfg.topk, L->max_tokens,
+                                 L->cfg.hidden);
   L->ep_attached = true;
   return 0;
 }
@@ -781,6 +783,63 @@ DSV4_API int dsv4cuda_moe_forward_ep(dsv4cuda_moe_layer* L, const float* x, cons
   if (dsv4cuda_moe_forward_local(L, x, token_ids, n_tokens, stream) != 0) return -1;
   if (dsv4cuda_moe_ep_push(L, n_tokens, stream) != 0) return -1;
   return dsv4cuda_moe_ep_combine(L, n_tokens, out, stream);
+}
+
+namespace {
+int ep_tokens_check(dsv4cuda_moe_layer* L, int n_local, const char* what) {
+  if (!L || !L->ep_attached || n_local <= 0 || n_local * L->ep.world > L->max_tokens) {
+    record_error("%s: bad arguments (world * n_local must fit max_tokens) or no exchange "
+                 "attached", what);
+    return -1;
+  }
+  if (L->cfg.hash_vocab > 0) {
+    record_error("%s: hash-routed layers need token ids; not supported", what);
+    return -1;
+  }
+  return 0;
+}
+}  // namespace
+
+DSV4_API int dsv4cuda_moe_ep_tokens_gather(dsv4cuda_moe_layer* L, const float* x_local,
+                                           int n_local, void* stream) {
+  if (ep_tokens_check(L, n_local, "dsv4cuda_moe_ep_tokens_gather") != 0 || !x_local) return -1;
+  cudaError_t e = dsv4::ep_gather(L->ep, x_local, n_local, L->cfg.hidden,
+                                  static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) { record_error("ep_gather: %s", cudaGetErrorString(e)); return -1; }
+  return 0;
+}
+
+DSV4_API int dsv4cuda_moe_ep_tokens_compute(dsv4cuda_moe_layer* L, int n_local, void* stream) {
+  if (ep_tokens_check(L, n_local, "dsv4cuda_moe_ep_tokens_compute") != 0) return -1;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  cudaError_t e = dsv4::ep_gather_wait(L->ep, dsv4::device_error_word(), st);
+  if (e != cudaSuccess) { record_error("ep_gather_wait: %s", cudaGetErrorString(e)); return -1; }
+  if (dsv4cuda_moe_forward_local(L, L->ep.tokens[L->ep.rank], nullptr, n_local * L->ep.world,
+                                 stream) != 0)
+    return -1;
+  e = dsv4::ep_push_owner(L->ep, L->ws.routed, L->ws.idx, n_local, L->cfg.topk, L->cfg.hidden,
+                          L->cfg.expert_lo, dsv4::moe_local_hi(L->cfg), st);
+  if (e != cudaSuccess) { record_error("ep_push_owner: %s", cudaGetErrorString(e)); return -1; }
+  return 0;
+}
+
+DSV4_API int dsv4cuda_moe_ep_tokens_combine(dsv4cuda_moe_layer* L, int n_local, float* out_local,
+                                            void* stream) {
+  if (ep_tokens_check(L, n_local, "dsv4cuda_moe_ep_tokens_combine") != 0 || !out_local) return -1;
+  const bool has_shared = L->cfg.shared_kind != dsv4::kSharedNone && L->w.sh1 != nullptr;
+  cudaError_t e = dsv4::ep_combine_owner(L->ep, has_shared ? L->ws.shared : nullptr, L->ws.idx,
+                                         n_local, L->cfg.topk, L->cfg.hidden, out_local,
+                                         dsv4::device_error_word(),
+                                         static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) { record_error("ep_combine_owner: %s", cudaGetErrorString(e)); return -1; }
+  return 0;
+}
+
+DSV4_API int dsv4cuda_moe_forward_ep_tokens(dsv4cuda_moe_layer* L, const float* x_local,
+                                            int n_local, float* out_local, void* stream) {
+  if (dsv4cuda_moe_ep_tokens_gather(L, x_local, n_local, stream) != 0) return -1;
+  if (dsv4cuda_moe_ep_tokens_compute(L, n_local, stream) != 0) return -1;
+  return dsv4cuda_moe_ep_tokens_combine(L, n_local, out_local, stream);
 }
 
 DSV4_API int dsv4cuda_ipc_alloc(size_t bytes, void** ptr, unsigned char* handle) {

@@ -19,19 +19,43 @@ constexpr int kEpMaxRanks = 8;
 constexpr unsigned kErrEpWait = 8u;  // device error word: a peer's epoch never arrived
 
 // One rank's exchange buffer (one per MoE layer):
-//   [0, 256)    flags[r]: last step epoch rank r finished writing here
-//   [256, 512)  counters of this rank: [0] epoch, [1] push CTAs done
-//   [512, ...)  slots: 2 halves x [slot_cap][H] fp32, step epoch e uses half e & 1
+//   [0, 64)      flags[r]: last step epoch rank r finished writing slots here
+//   [64, 128)    gflags[r]: last step epoch rank r finished writing tokens here
+//   [256, 512)   counters of this rank: [0] epoch, [1] CTAs done
+//   [512, ...)   slots: 2 halves x [slot_cap][H] fp32, step epoch e uses half e & 1
+//   then         tokens: [tok_cap][H] fp32 (the gathered inputs of every rank)
 struct EpExchange {
   float* slots[kEpMaxRanks];     // every rank's slots, as mapped in this process
-  unsigned* flags[kEpMaxRanks];  // every rank's flag array
+  float* tokens[kEpMaxRanks];    // every rank's gathered-token rows
+  unsigned* flags[kEpMaxRanks];  // every rank's slot flag array
+  unsigned* gflags[kEpMaxRanks]; // every rank's token flag array
   unsigned* ctr = nullptr;       // this rank's counters
   int rank = 0, world = 0;
   size_t half_floats = 0;        // slot_cap * H
 };
 
-size_t ep_exchange_bytes(int slot_cap, int H);
-EpExchange ep_exchange_make(void* const* bufs, int rank, int world, int slot_cap, int H);
+size_t ep_exchange_bytes(int slot_cap, int tok_cap, int H);
+EpExchange ep_exchange_make(void* const* bufs, int rank, int world, int slot_cap, int tok_cap,
+                            int H);
+
+// Token-parallel step (each rank brings its own n_local tokens): this rank's
+// rows go to rows [rank * n_local, +n_local) of every rank's token buffer,
+// then this step's epoch (new: counter + 1) into each peer's token flags.
+cudaError_t ep_gather(const EpExchange& x, const float* x_local, int n_local, int H,
+                      cudaStream_t st);
+// Waits (bounded) for every peer's token epoch of this step.
+cudaError_t ep_gather_wait(const EpExchange& x, unsigned* err, cudaStream_t st);
+// Slots of experts [lo, hi) for all world * n_local tokens go only to the
+// token's owner (rank t / n_local, its slot (t % n_local) * topk + k), then
+// this step's epoch into each peer's slot flags.
+cudaError_t ep_push_owner(const EpExchange& x, const float* routed, const int* idx, int n_local,
+                          int topk, int H, int lo, int hi, cudaStream_t st);
+// Waits for every peer's slot epoch, then the ordered combine of this rank's
+// n_local tokens: slots from its own buffer, router ids and shared-expert
+// rows at token offset rank * n_local.
+cudaError_t ep_combine_owner(const EpExchange& x, const float* shared, const int* idx,
+                             int n_local, int topk, int H, float* out, unsigned* err,
+                             cudaStream_t st);
 
 // Slots of experts [lo, hi) from this rank's routed buffer into the current
 // half of every rank's buffer, then this step's epoch into every peer's flags.

@@ -72,6 +72,14 @@ lib.dsv4cuda_moe_ep_attach.restype = C.c_int
 lib.dsv4cuda_moe_ep_attach.argtypes = [vp, C.c_int, C.c_int, C.POINTER(vp)]
 lib.dsv4cuda_moe_forward_ep.restype = C.c_int
 lib.dsv4cuda_moe_forward_ep.argtypes = [vp, vp, vp, C.c_int, vp, vp]
+lib.dsv4cuda_moe_forward_ep_tokens.restype = C.c_int
+lib.dsv4cuda_moe_forward_ep_tokens.argtypes = [vp, vp, C.c_int, vp, vp]
+lib.dsv4cuda_moe_ep_tokens_gather.restype = C.c_int
+lib.dsv4cuda_moe_ep_tokens_gather.argtypes = [vp, vp, C.c_int, vp]
+lib.dsv4cuda_moe_ep_tokens_compute.restype = C.c_int
+lib.dsv4cuda_moe_ep_tokens_compute.argtypes = [vp, C.c_int, vp]
+lib.dsv4cuda_moe_ep_tokens_combine.restype = C.c_int
+lib.dsv4cuda_moe_ep_tokens_combine.argtypes = [vp, C.c_int, vp, vp]
 lib.dsv4cuda_moe_ep_push.restype = C.c_int
 lib.dsv4cuda_moe_ep_push.argtypes = [vp, C.c_int, vp]
 lib.dsv4cuda_moe_ep_combine.restype = C.c_int
@@ -381,6 +389,23 @@ class MoeLayer:
         _check(lib.dsv4cuda_moe_forward_ep(self.handle, x.data_ptr(),
                                            None if token_ids is None else token_ids.data_ptr(),
                                            x.shape[0], out.data_ptr(), _stream(stream)))
+
+    def forward_ep_tokens(self, x_local, out_local, stream=None):
+        """Token-parallel EP step: this rank's tokens in, their outputs out."""
+        _check(lib.dsv4cuda_moe_forward_ep_tokens(self.handle, x_local.data_ptr(),
+                                                  x_local.shape[0], out_local.data_ptr(),
+                                                  _stream(stream)))
+
+    def ep_tokens_gather(self, x_local, stream=None):
+        _check(lib.dsv4cuda_moe_ep_tokens_gather(self.handle, x_local.data_ptr(),
+                                                 x_local.shape[0], _stream(stream)))
+
+    def ep_tokens_compute(self, n_local, stream=None):
+        _check(lib.dsv4cuda_moe_ep_tokens_compute(self.handle, n_local, _stream(stream)))
+
+    def ep_tokens_combine(self, n_local, out_local, stream=None):
+        _check(lib.dsv4cuda_moe_ep_tokens_combine(self.handle, n_local, out_local.data_ptr(),
+                                                  _stream(stream)))
 
     def ep_push(self, n_tokens, stream=None):
         _check(lib.dsv4cuda_moe_ep_push(self.handle, n_tokens, _stream(stream)))

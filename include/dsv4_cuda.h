@@ -294,6 +294,23 @@ size_t dsv4cuda_moe_ep_buffer_bytes(const dsv4cuda_moe_layer *L);
 int dsv4cuda_moe_ep_attach(dsv4cuda_moe_layer *L, int rank, int world, void *const *bufs);
 int dsv4cuda_moe_forward_ep(dsv4cuda_moe_layer *L, const float *x, const int *token_ids,
                             int n_tokens, float *out, void *stream);
+/* Token-parallel expert parallelism (each rank brings its own tokens, as
+ * with data-parallel attention): the n_local rows of x_local are gathered
+ * into every rank over peer memory, every rank routes all world * n_local
+ * tokens (identically) and runs its experts for them, each slot goes only
+ * to its token's owner, and each rank combines its own n_local tokens into
+ * out_local. Requires world * n_local <= max_tokens; not for hash-routed
+ * layers. Output rows bit-identical to the single-device layer on the same
+ * tokens. */
+int dsv4cuda_moe_forward_ep_tokens(dsv4cuda_moe_layer *L, const float *x_local, int n_local,
+                                   float *out_local, void *stream);
+/* Its three stages (gather; wait + route + local experts + push; wait +
+ * combine), for callers that interleave ranks in one process. */
+int dsv4cuda_moe_ep_tokens_gather(dsv4cuda_moe_layer *L, const float *x_local, int n_local,
+                                  void *stream);
+int dsv4cuda_moe_ep_tokens_compute(dsv4cuda_moe_layer *L, int n_local, void *stream);
+int dsv4cuda_moe_ep_tokens_combine(dsv4cuda_moe_layer *L, int n_local, float *out_local,
+                                   void *stream);
 /* The exchange's two halves, separately (dsv4cuda_moe_forward_local first). */
 int dsv4cuda_moe_ep_push(dsv4cuda_moe_layer *L, int n_tokens, void *stream);
 int dsv4cuda_moe_ep_combine(dsv4cuda_moe_layer *L, int n_tokens, float *out, void *stream);
