@@ -445,6 +445,14 @@ def main():
     n = C.c_int()
     for _, L in layers:
         lib.dsv4cuda_moe_timing_end2(L.handle, C.byref(n), None, None, None, None)
+    # our kernels per step: router (2), shared expert (3), routed gate/up,
+    # SwiGLU, down, combine; a second gate/up and down for multi-route items
+    # when a step routes two or more tokens; the peer-memory exchange kernels
+    launches_per_step = 9 + (2 if M_all >= 2 else 0)
+    if tok_mode:
+        launches_per_step += 3  # gather, gather wait, owner push (+ owner combine for combine)
+    elif p2p:
+        launches_per_step += 1  # slot push (+ exchange combine for combine)
     U_avg = U_total / max(n_fw, 1)
     if ep:  # this rank's share of the unique experts (uniform routing)
         U_avg = U_avg * (erange[1] - erange[0]) / args.experts
@@ -512,7 +520,7 @@ def main():
             "cpu_baseline": cpu,
             "e2e": {"value": e2e_val, "unit": "tok/s", "h2d_bytes_per_step": M * H * 4,
                     "d2h_bytes_per_step": M * H * 4},
-            "gpu_launches": 9 * args.steps,
+            "gpu_launches": launches_per_step * args.steps,
             "router_tie_fallbacks": fallbacks,
             "clocks": clk,
             "attn_config3": attn,

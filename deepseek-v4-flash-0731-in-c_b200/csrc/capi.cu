@@ -718,6 +718,22 @@ DSV4_API int dsv4cuda_moe_forward_local(dsv4cuda_moe_layer* L, const float* x,
   return 0;
 }
 
+namespace {
+// moe_forward_local with the shared expert restricted to tokens [t0, t0 + n)
+int forward_local_shared_range(dsv4cuda_moe_layer* L, const float* x, int n_tokens, int t0, int n,
+                               void* stream) {
+  dsv4::MoeWorkspace ws = L->ws;
+  if (timed_workspace(L, &ws) != 0) return -1;
+  dsv4::MoeExecOptions opt;
+  opt.shared_t0 = t0;
+  opt.shared_n = n;
+  cudaError_t e = dsv4::moe_forward_local(L->cfg, L->w, ws, x, nullptr, n_tokens,
+                                          static_cast<cudaStream_t>(stream), opt);
+  if (e != cudaSuccess) { record_error("moe_forward_local: %s", cudaGetErrorString(e)); return -1; }
+  return 0;
+}
+}  // namespace
+
 DSV4_API float* dsv4cuda_moe_routed_slots(dsv4cuda_moe_layer* L) { return L ? L->ws.routed : nullptr; }
 
 DSV4_API size_t dsv4cuda_moe_ep_buffer_bytes(const dsv4cuda_moe_layer* L) {
@@ -814,8 +830,10 @@ DSV4_API int dsv4cuda_moe_ep_tokens_compute(dsv4cuda_moe_layer* L, int n_local, 
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   cudaError_t e = dsv4::ep_gather_wait(L->ep, dsv4::device_error_word(), st);
   if (e != cudaSuccess) { record_error("ep_gather_wait: %s", cudaGetErrorString(e)); return -1; }
-  if (dsv4cuda_moe_forward_local(L, L->ep.tokens[L->ep.rank], nullptr, n_local * L->ep.world,
-                                 stream) != 0)
+  // every rank routes all tokens; the shared expert runs for this rank's
+  // tokens only (rows rank * n_local of the shared output)
+  if (forward_local_shared_range(L, L->ep.tokens[L->ep.rank], n_local * L->ep.world,
+                                 L->ep.rank * n_local, n_local, stream) != 0)
     return -1;
   e = dsv4::ep_push_owner(L->ep, L->ws.routed, L->ws.idx, n_local, L->cfg.topk, L->cfg.hidden,
                           L->cfg.expert_lo, dsv4::moe_local_hi(L->cfg), st);

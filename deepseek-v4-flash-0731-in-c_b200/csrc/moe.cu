@@ -57,11 +57,15 @@ struct RouterArgs {
   float* xs;                 // [M][ceil(H/128)]
   int* idx;                  // [M][topk]
   float* wt;                 // [M][topk]
-  GemvItem* items_gu;        // plan outputs (skipped when null)
+  GemvItem* items_gu;        // plan outputs (skipped when null): multi-token items
   GemvItem* items_dn;
+  GemvItem* items_gu1;       // single-token items
+  GemvItem* items_dn1;
   GemvItem* items_sh;
-  int* counters;             // [0] items, [1] CTA ticket, [2] tie fallbacks, [3] shared items
+  int* counters;             // [0] multi items, [1] CTA ticket, [2] tie fallbacks,
+                             // [3] shared items, [4] single items
   int elo, ehi;              // experts computed on this device (plan only)
+  int sh_t0, sh_n;           // tokens the shared expert runs for
 };
 
 // The reference's fp32 logit chain, replayed exactly (near-tie path):
@@ -421,56 +425,72 @@ __device__ int block_excl_scan(int v, int* wsum, int* total) {
   return r;
 }
 
-// Token->expert permutation (moe_forward_batch grouping,
-// src/dsv4/dsv4_model.c:6925-6926, expert_forward_batch_routes :6486): unique
-// experts ascending; each expert's routes in token order, packed into items
-// of <= kItemTok routes. Route (t,k) owns slot t*topk+k. Also the
-// shared-expert items (all tokens). One CTA; idx staged in shared memory.
-__device__ void block_plan(const RouterArgs& a, int* cnt, int* ids) {
-  const int E = a.E, K = a.topk, R = a.M * a.topk;
-  for (int r = threadIdx.x; r < R; r += blockDim.x) ids[r] = a.idx[r];
-  __syncthreads();
-  for (int e = threadIdx.x; e < E; e += blockDim.x) {
-    int n = 0;
-    if (e >= a.elo && e < a.ehi)
-      for (int r = 0; r < R; ++r) n += (ids[r] == e);
-    cnt[e] = (n + kItemTok - 1) / kItemTok;
-  }
-  __syncthreads();
+// In-place exclusive scan of arr[0..E) by the whole block; the total goes
+// to *total (shared memory) for every thread.
+__device__ void plan_excl_scan(int* arr, int E, int* total) {
   if (E <= static_cast<int>(blockDim.x)) {
     __shared__ int wsum[33];
-    int total = 0;
-    const int v = static_cast<int>(threadIdx.x) < E ? cnt[threadIdx.x] : 0;
-    const int off = block_excl_scan(v, wsum, &total);
-    if (static_cast<int>(threadIdx.x) < E) cnt[threadIdx.x] = off;
-    if (threadIdx.x == 0) {
-      a.counters[0] = total;
-    }
+    int t = 0;
+    const int v = static_cast<int>(threadIdx.x) < E ? arr[threadIdx.x] : 0;
+    const int off = block_excl_scan(v, wsum, &t);
+    if (static_cast<int>(threadIdx.x) < E) arr[threadIdx.x] = off;
+    if (threadIdx.x == 0) *total = t;
   } else if (threadIdx.x < 32) {
-    // exclusive scan of cnt[0..E) by one warp: 32-element tiles with a carry
+    // one warp: 32-element tiles with a carry
     int carry = 0;
     for (int b0 = 0; b0 < E; b0 += 32) {
       const int e = b0 + threadIdx.x;
-      const int v = e < E ? cnt[e] : 0;
+      const int v = e < E ? arr[e] : 0;
       int incl = v;
 #pragma unroll
       for (int o = 1; o < 32; o <<= 1) {
         const int tt = __shfl_up_sync(0xffffffffu, incl, o);
         if (static_cast<int>(threadIdx.x) >= o) incl += tt;
       }
-      if (e < E) cnt[e] = carry + incl - v;
+      if (e < E) arr[e] = carry + incl - v;
       carry += __shfl_sync(0xffffffffu, incl, 31);
     }
-    if (threadIdx.x == 0) {
-      a.counters[0] = carry;
-    }
+    if (threadIdx.x == 0) *total = carry;
   }
   __syncthreads();
+}
+
+// Token->expert permutation (moe_forward_batch grouping,
+// src/dsv4/dsv4_model.c:6925-6926, expert_forward_batch_routes :6486): unique
+// experts ascending; each expert's routes in token order. An expert with one
+// route becomes a single-token item (items_gu1/dn1, counters[4]); one with
+// more becomes items of <= kItemTok routes (items_gu/dn, counters[0]), so the
+// single-token items run on the one-token GEMV kernel. Route (t,k) owns slot
+// t*topk+k. One CTA; idx staged in shared memory.
+__device__ void block_plan(const RouterArgs& a, int* cnt, int* cnt1, int* ids) {
+  const int E = a.E, K = a.topk, R = a.M * a.topk;
+  __shared__ int n_multi, n_single;
+  for (int r = threadIdx.x; r < R; r += blockDim.x) ids[r] = a.idx[r];
+  __syncthreads();
+  for (int e = threadIdx.x; e < E; e += blockDim.x) {
+    int n = 0;
+    if (e >= a.elo && e < a.ehi)
+      for (int r = 0; r < R; ++r) n += (ids[r] == e);
+    cnt[e] = n >= 2 ? (n + kItemTok - 1) / kItemTok : 0;
+    cnt1[e] = n == 1 ? 1 : 0;
+  }
+  __syncthreads();
+  plan_excl_scan(cnt, E, &n_multi);
+  plan_excl_scan(cnt1, E, &n_single);
+  if (threadIdx.x == 0) {
+    a.counters[0] = n_multi;
+    a.counters[4] = n_single;
+  }
   for (int e = a.elo + threadIdx.x; e < a.ehi; e += blockDim.x) {
-    int item = cnt[e];
+    int n = 0;
+    for (int r = 0; r < R; ++r) n += (ids[r] == e);
+    if (n == 0) continue;
     GemvItem gu, dn;
     gu.mat = dn.mat = e - a.elo;  // index into this device's expert weights
     gu.ntok = dn.ntok = 0;
+    GemvItem* out_gu = n == 1 ? a.items_gu1 : a.items_gu;
+    GemvItem* out_dn = n == 1 ? a.items_dn1 : a.items_dn;
+    int item = n == 1 ? cnt1[e] : cnt[e];
     for (int r = 0; r < R; ++r) {
       if (ids[r] != e) continue;
       gu.tok[gu.ntok].x = r / K;
@@ -480,16 +500,16 @@ __device__ void block_plan(const RouterArgs& a, int* cnt, int* ids) {
       gu.ntok++;
       dn.ntok++;
       if (gu.ntok == kItemTok) {
-        a.items_gu[item] = gu;
-        a.items_dn[item] = dn;
+        out_gu[item] = gu;
+        out_dn[item] = dn;
         ++item;
         gu.ntok = dn.ntok = 0;
       }
     }
     if (gu.ntok > 0) {
       for (int i = gu.ntok; i < kItemTok; ++i) { gu.tok[i] = gu.tok[0]; dn.tok[i] = dn.tok[0]; }
-      a.items_gu[item] = gu;
-      a.items_dn[item] = dn;
+      out_gu[item] = gu;
+      out_dn[item] = dn;
     }
   }
 }
@@ -498,13 +518,13 @@ __device__ void block_plan(const RouterArgs& a, int* cnt, int* ids) {
 // only, so the logit kernel writes them and the shared expert can start
 // before the selection finishes.
 __device__ void write_shared_items(const RouterArgs& a) {
-  const int nsh = (a.M + kItemTok - 1) / kItemTok;
+  const int nsh = (a.sh_n + kItemTok - 1) / kItemTok;
   for (int j = threadIdx.x; j < nsh; j += blockDim.x) {
     GemvItem it;
     it.mat = 0;
-    it.ntok = min(kItemTok, a.M - j * kItemTok);
+    it.ntok = min(kItemTok, a.sh_n - j * kItemTok);
     for (int i = 0; i < kItemTok; ++i) {
-      const int tt = min(j * kItemTok + i, a.M - 1);
+      const int tt = a.sh_t0 + min(j * kItemTok + i, a.sh_n - 1);
       it.tok[i].x = tt;
       it.tok[i].y = tt;
     }
@@ -523,7 +543,8 @@ struct SelectSmem {
   double* hi;     // [E]
   float* choice;  // [E]
   float* score;   // [E]
-  int* cnt;       // [E] plan
+  int* cnt;       // [E] plan (multi-token items)
+  int* cnt1;      // [E] plan (single-token items)
   int* ids;       // [R] plan
   unsigned char* used;  // [E]
 };
@@ -544,6 +565,7 @@ __host__ __device__ inline size_t select_smem_bytes(int H, int E, int R, SelectS
   unsigned char* pc = take(static_cast<size_t>(E) * 4);
   unsigned char* ps = take(static_cast<size_t>(E) * 4);
   unsigned char* pn = take(static_cast<size_t>(E) * 4);
+  unsigned char* pn1 = take(static_cast<size_t>(E) * 4);
   unsigned char* pi = take(static_cast<size_t>(R) * 4);
   unsigned char* pu = take(static_cast<size_t>(E));
   if (sm) {
@@ -555,6 +577,7 @@ __host__ __device__ inline size_t select_smem_bytes(int H, int E, int R, SelectS
     sm->choice = reinterpret_cast<float*>(pc);
     sm->score = reinterpret_cast<float*>(ps);
     sm->cnt = reinterpret_cast<int*>(pn);
+    sm->cnt1 = reinterpret_cast<int*>(pn1);
     sm->ids = reinterpret_cast<int*>(pi);
     sm->used = pu;
   }
@@ -770,10 +793,13 @@ __global__ void __launch_bounds__(kSelThreads) router_select_kernel(const Router
           dn.tok[i].x = k;
           dn.tok[i].y = k;
         }
-        a.items_gu[item] = gu;
-        a.items_dn[item] = dn;
+        a.items_gu1[item] = gu;
+        a.items_dn1[item] = dn;
       }
-      if (lane == 0) a.counters[0] = __popc(m);
+      if (lane == 0) {
+        a.counters[4] = __popc(m);
+        a.counters[0] = 0;
+      }
     }
   }
   if (!a.items_gu || (gridDim.x == 1 && !a.tid2eid)) return;  // no plan, or planned above
@@ -788,7 +814,7 @@ __global__ void __launch_bounds__(kSelThreads) router_select_kernel(const Router
     if (!is_last) return;
     __threadfence();
   }
-  block_plan(a, sm.cnt, sm.ids);
+  block_plan(a, sm.cnt, sm.cnt1, sm.ids);
   if (threadIdx.x == 0 && gridDim.x > 1) a.counters[1] = 0;  // ticket ready for the next launch
 }
 
@@ -849,7 +875,7 @@ size_t moe_workspace_bytes(const MoeConfig& c, int M) {
   b += align256(M * (H / 128 + 1) * sizeof(float));
   b += 2 * align256(M * E * sizeof(double));
   b += align256(R * sizeof(int)) + align256(R * sizeof(float));
-  b += 2 * align256(R * sizeof(GemvItem));
+  b += 4 * align256(R * sizeof(GemvItem));
   b += align256(((M + kItemTok - 1) / kItemTok) * sizeof(GemvItem));
   b += align256(8 * sizeof(int));
   b += 2 * align256(R * I * sizeof(float));
@@ -879,6 +905,8 @@ void moe_workspace_carve(MoeWorkspace* ws, const MoeConfig& c, int M, void* base
   ws->wt = static_cast<float*>(take(R * sizeof(float)));
   ws->items_gu = static_cast<GemvItem*>(take(R * sizeof(GemvItem)));
   ws->items_dn = static_cast<GemvItem*>(take(R * sizeof(GemvItem)));
+  ws->items_gu1 = static_cast<GemvItem*>(take(R * sizeof(GemvItem)));
+  ws->items_dn1 = static_cast<GemvItem*>(take(R * sizeof(GemvItem)));
   ws->items_sh = static_cast<GemvItem*>(take(((M + kItemTok - 1) / kItemTok) * sizeof(GemvItem)));
   ws->counters = static_cast<int*>(take(8 * sizeof(int)));
   ws->gate = static_cast<float*>(take(R * I * sizeof(float)));
@@ -917,11 +945,15 @@ static RouterArgs make_router_args(const MoeConfig& c, const MoeWeights& w, cons
   a.counters = ws.counters;
   a.elo = c.expert_lo;
   a.ehi = moe_local_hi(c);
+  a.sh_t0 = 0;
+  a.sh_n = M;
   if (plan) {
     a.xq = ws.xq;
     a.xs = ws.xs;
     a.items_gu = ws.items_gu;
     a.items_dn = ws.items_dn;
+    a.items_gu1 = ws.items_gu1;
+    a.items_dn1 = ws.items_dn1;
     a.items_sh = ws.items_sh;
   }
   return a;
@@ -991,7 +1023,12 @@ cudaError_t moe_forward_local(const MoeConfig& c, const MoeWeights& w, const Moe
     return err;
 
   // router launch 1: activation quant + logits (+ the shared-expert items)
-  const RouterArgs ra = make_router_args(c, w, ws, x, token_ids, M, 0, true);
+  const int sh_t0 = opt.shared_n < 0 ? 0 : opt.shared_t0;
+  const int sh_n = opt.shared_n < 0 ? M : opt.shared_n;
+  if (sh_t0 < 0 || sh_n < 1 || sh_t0 + sh_n > M) return cudaErrorInvalidValue;
+  RouterArgs ra = make_router_args(c, w, ws, x, token_ids, M, 0, true);
+  ra.sh_t0 = sh_t0;
+  ra.sh_n = sh_n;
   if ((err = route_logits(ra, c, ws, M, true, st)) != cudaSuccess) return err;
   const QAct act{ws.xq, ws.xs, H, nullptr};
 
@@ -1006,9 +1043,11 @@ cudaError_t moe_forward_local(const MoeConfig& c, const MoeWeights& w, const Moe
       cudaEventRecord(side->fork, st);
       cudaStreamWaitEvent(side->s, side->fork, 0);
     }
-    const int nt = nt_bucket(std::min(M, kItemTok));
-    const int sh_items = (M + kItemTok - 1) / kItemTok;
+    const int nt = nt_bucket(std::min(sh_n, kItemTok));
+    const int sh_items = (sh_n + kItemTok - 1) / kItemTok;
     const QAct sact{ws.sh_qy, ws.sh_qys, I, nullptr};
+    const size_t so = static_cast<size_t>(sh_t0) * I;  // first shared row
+    const size_t sq = static_cast<size_t>(sh_t0) * ((I + 127) / 128);
     if (c.shared_kind == kSharedFp8) {
       Fp8GemvArgs g{};
       g.W[0] = w.sh1; g.S[0] = w.sh1s; g.W[1] = w.sh3; g.S[1] = w.sh3s;
@@ -1016,8 +1055,9 @@ cudaError_t moe_forward_local(const MoeConfig& c, const MoeWeights& w, const Moe
       g.Y[0] = ws.sh_gate; g.Y[1] = ws.sh_up;
       g.items = ws.items_sh; g.n_items = ws.counters + 3; g.max_items = sh_items;
       if ((err = launch_fp8_gemv(g, true, nt, sst)) != cudaSuccess) return err;
-      if ((err = launch_swiglu_quant(ws.sh_gate, ws.sh_up, I, M, nullptr, c.swiglu_limit,
-                                     ws.sh_qy, ws.sh_qys, nullptr, sst)) != cudaSuccess)
+      if ((err = launch_swiglu_quant(ws.sh_gate + so, ws.sh_up + so, I, sh_n, nullptr,
+                                     c.swiglu_limit, ws.sh_qy + so, ws.sh_qys + sq, nullptr,
+                                     sst)) != cudaSuccess)
         return err;
       Fp8GemvArgs d{};
       d.W[0] = w.sh2; d.S[0] = w.sh2s;
@@ -1032,8 +1072,9 @@ cudaError_t moe_forward_local(const MoeConfig& c, const MoeWeights& w, const Moe
       g.Y[0] = ws.sh_gate; g.Y[1] = ws.sh_up;
       g.items = ws.items_sh; g.n_items = ws.counters + 3; g.max_items = sh_items; g.err = opt.err;
       if ((err = launch_fp4_gemv(g, true, nt, sst, opt.map_cache)) != cudaSuccess) return err;
-      if ((err = launch_swiglu_quant(ws.sh_gate, ws.sh_up, I, M, nullptr, c.swiglu_limit,
-                                     ws.sh_qy, ws.sh_qys, nullptr, sst)) != cudaSuccess)
+      if ((err = launch_swiglu_quant(ws.sh_gate + so, ws.sh_up + so, I, sh_n, nullptr,
+                                     c.swiglu_limit, ws.sh_qy + so, ws.sh_qys + sq, nullptr,
+                                     sst)) != cudaSuccess)
         return err;
       Fp4GemvArgs d{};
       d.W[0] = w.sh2; d.S[0] = w.sh2s;
@@ -1049,7 +1090,10 @@ cudaError_t moe_forward_local(const MoeConfig& c, const MoeWeights& w, const Moe
   // shared expert on the side stream)
   if ((err = route_select(ra, c, ws, M, true, st)) != cudaSuccess) return err;
 
+  // single-token items on the one-token kernel; items of two or more routes
+  // (only possible when M >= 2) on the kernel for their token count
   const int nt = nt_bucket(std::min(M, kItemTok));
+  const int R_multi = R / 2;  // each multi item holds at least two routes
   const size_t w13 = static_cast<size_t>(I) * (H / 2), s13 = static_cast<size_t>(I) * (H / 32);
   const size_t w2 = static_cast<size_t>(H) * (I / 2), s2 = static_cast<size_t>(H) * (I / 32);
   Fp4GemvArgs gu{};
@@ -1057,10 +1101,15 @@ cudaError_t moe_forward_local(const MoeConfig& c, const MoeWeights& w, const Moe
   gu.w_stride = w13; gu.s_stride = s13;
   gu.in = H; gu.rows = I; gu.act = act;
   gu.Y[0] = ws.gate; gu.Y[1] = ws.up;
-  gu.items = ws.items_gu; gu.n_items = ws.counters; gu.max_items = R; gu.n_mats = n_local;
+  gu.items = ws.items_gu1; gu.n_items = ws.counters + 4; gu.max_items = R; gu.n_mats = n_local;
   gu.err = opt.err;
   if (ws.timing) record_timing(ws.timing[0], st);
-  if ((err = launch_fp4_gemv(gu, true, nt, st, opt.map_cache)) != cudaSuccess) return err;
+  if ((err = launch_fp4_gemv(gu, true, 1, st, opt.map_cache)) != cudaSuccess) return err;
+  if (M >= 2) {
+    Fp4GemvArgs gm = gu;
+    gm.items = ws.items_gu; gm.n_items = ws.counters; gm.max_items = R_multi;
+    if ((err = launch_fp4_gemv(gm, true, nt, st, opt.map_cache)) != cudaSuccess) return err;
+  }
   if (ws.timing) record_timing(ws.timing[1], st);
   if ((err = launch_swiglu_quant(ws.gate, ws.up, I, R, ws.wt, c.swiglu_limit, ws.qy, ws.qys,
                                  nullptr, st)) != cudaSuccess)
@@ -1070,10 +1119,15 @@ cudaError_t moe_forward_local(const MoeConfig& c, const MoeWeights& w, const Moe
   dn.w_stride = w2; dn.s_stride = s2;
   dn.in = I; dn.rows = H; dn.act = QAct{ws.qy, ws.qys, I, nullptr};
   dn.Y[0] = ws.routed;
-  dn.items = ws.items_dn; dn.n_items = ws.counters; dn.max_items = R; dn.n_mats = n_local;
+  dn.items = ws.items_dn1; dn.n_items = ws.counters + 4; dn.max_items = R; dn.n_mats = n_local;
   dn.err = opt.err;
   if (ws.timing) record_timing(ws.timing[2], st);
-  if ((err = launch_fp4_gemv(dn, false, nt, st, opt.map_cache)) != cudaSuccess) return err;
+  if ((err = launch_fp4_gemv(dn, false, 1, st, opt.map_cache)) != cudaSuccess) return err;
+  if (M >= 2) {
+    Fp4GemvArgs dm = dn;
+    dm.items = ws.items_dn; dm.n_items = ws.counters; dm.max_items = R_multi;
+    if ((err = launch_fp4_gemv(dm, false, nt, st, opt.map_cache)) != cudaSuccess) return err;
+  }
   if (ws.timing) record_timing(ws.timing[3], st);
 
   if (side) cudaStreamWaitEvent(st, side->join, 0);

@@ -46,10 +46,13 @@ struct MoeWorkspace {
   double* zb = nullptr;      // [M][E] bound of the reference's rounding error
   int* idx = nullptr;        // [M][topk] ascending ids
   float* wt = nullptr;       // [M][topk]
-  GemvItem* items_gu = nullptr;   // [M*topk]
+  GemvItem* items_gu = nullptr;   // [M*topk] items of two or more routes
   GemvItem* items_dn = nullptr;   // [M*topk]
+  GemvItem* items_gu1 = nullptr;  // [M*topk] single-route items
+  GemvItem* items_dn1 = nullptr;  // [M*topk]
   GemvItem* items_sh = nullptr;   // [ceil(M/8)] (static)
-  int* counters = nullptr;   // [0]=n_items, [1]=done CTAs, [2]=tie fallbacks, [3]=n_shared_items
+  int* counters = nullptr;   // [0]=multi items, [1]=done CTAs, [2]=tie fallbacks,
+                             // [3]=n_shared_items, [4]=single items
   float* gate = nullptr;     // [M*topk][I]
   float* up = nullptr;       // [M*topk][I]
   __half* qy = nullptr;      // [M*topk][I]
@@ -85,6 +88,10 @@ struct MoeExecOptions {
   bool single_stream = false;  // shared expert on `st` instead of a side stream
   bool map_cache = true;       // cache TMA descriptors by argument
   unsigned int* err = nullptr; // device error word (null: the library's)
+  // shared expert only for tokens [shared_t0, shared_t0 + shared_n) (-1: all);
+  // token-parallel expert parallelism computes it for this rank's tokens
+  int shared_t0 = 0;
+  int shared_n = -1;
 };
 
 cudaError_t moe_forward(const MoeConfig& c, const MoeWeights& w, const MoeWorkspace& ws,
