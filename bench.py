@@ -8,7 +8,8 @@ expert, ordered combine. Weights are random-init with the config's
 distributions and resident in HBM; successive steps cycle through --layers
 independent layer weight sets and a pool of tokens, so a step never finds
 the previous step's weights in L2 (126 MB) - each layer's step reads
-~235 MB.
+~235 MB. One CUDA graph replay runs the layers back to back (a decode pass
+through consecutive MoE layers), each layer on its own token rows.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
@@ -348,7 +349,7 @@ def main():
         dist.all_reduce(L.routed_slots(M), op=dist.ReduceOp.SUM)
         L.combine(M, out, stream=s)
     rng = np.random.default_rng(7 + (1000 * rank if tok_mode else 0))  # own tokens per rank
-    pool = 32
+    pool = 8 * len(layers)
     x_host = bf16_tokens(rng, pool, M)
     x_dev = torch.from_numpy(x_host).to(dev)
     out_dev = torch.empty((M, H), dtype=torch.float32, device=dev)
@@ -368,13 +369,35 @@ def main():
             layer_forward(L, xin, out_dev, torch.cuda.current_stream().cuda_stream)
         graphs.append(g)
 
-    def step(i):
-        xin.copy_(x_dev[i % pool], non_blocking=True)
-        graphs[i % len(graphs)].replay()
+    # The timed loop replays graphs that chain the layers back to back: one
+    # decode token through len(layers) consecutive MoE layers, each layer on
+    # its own token rows, as a model's decode step runs its layers; chains of
+    # 1..len(layers) layers let a run cover exactly the requested steps.
+    n_lay = len(layers)
+    xch = torch.empty((n_lay, M, H), dtype=torch.float32, device=dev)
+    chains = []
+    for n in range(1, n_lay + 1):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            cs = torch.cuda.current_stream().cuda_stream
+            for li in range(n):
+                layer_forward(layers[li][1], xch[li], out_dev, cs)
+        chains.append(g)
+    replays = [0]
+
+    def run_steps(count):
+        """`count` steps: new token rows for each chained layer, one replay
+        per chain."""
+        while count > 0:
+            n = min(n_lay, count)
+            s0 = (replays[0] * n_lay) % pool
+            xch[:n].copy_(x_dev[s0:s0 + n], non_blocking=True)
+            chains[n - 1].replay()
+            replays[0] += 1
+            count -= n
 
     with torch.cuda.stream(stream):
-        for i in range(args.warmup):
-            step(i)
+        run_steps(args.warmup)
     torch.cuda.synchronize()
 
     clocks = ClockSampler(local)
@@ -387,8 +410,7 @@ def main():
     ev1 = torch.cuda.Event(enable_timing=True)
     with torch.cuda.stream(stream):
         ev0.record(stream)
-        for i in range(args.steps):
-            step(args.warmup + i)
+        run_steps(args.steps)
         ev1.record(stream)
     torch.cuda.synchronize()
     if dist:
@@ -445,10 +467,11 @@ def main():
     n = C.c_int()
     for _, L in layers:
         lib.dsv4cuda_moe_timing_end2(L.handle, C.byref(n), None, None, None, None)
-    # our kernels per step: router (2), shared expert (3), routed gate/up,
-    # SwiGLU, down, combine; a second gate/up and down for multi-route items
-    # when a step routes two or more tokens; the peer-memory exchange kernels
-    launches_per_step = 9 + (2 if M_all >= 2 else 0)
+    # our kernels per step: activation quant, router (2), shared expert (3),
+    # routed gate/up, SwiGLU, down, combine; a second gate/up and down for
+    # multi-route items when a step routes two or more tokens; the
+    # peer-memory exchange kernels
+    launches_per_step = 10 + (2 if M_all >= 2 else 0)
     if tok_mode:
         launches_per_step += 3  # gather, gather wait, owner push (+ owner combine for combine)
     elif p2p:
@@ -500,6 +523,8 @@ def main():
                        "moe_inter": I, "experts": args.experts, "topk": TOPK, "shared": "fp8",
                        "tokens_per_step": M_all if tok_mode else M, "tokens_per_gpu": M,
                        "layers_cycled": args.layers,
+                       "graph": "one CUDA graph replay chains the %d layers (a step = one "
+                                "layer pass of one token)" % args.layers,
                        "l2": "inputs larger than L2: each step reads a different layer's "
                              "~235 MB of weights", "parallelism": f"ep{world}",
                        "ep_mode": (args.ep_mode if ep else None),
@@ -528,9 +553,10 @@ def main():
         print(json.dumps(line), flush=True)
     # graphs holding NCCL calls must be released before the process group
     torch.cuda.synchronize()
-    for gr in graphs:
+    for gr in graphs + chains:
         gr.reset()
     graphs.clear()
+    chains.clear()
     g = gr = None  # noqa: F841  (the capture loop's last graph)
     if p2p:
         # every rank stops touching peer memory before any buffer is unmapped

@@ -1336,9 +1336,10 @@ cudaError_t launch_fp8_stream(const Fp8GemvArgs& a, bool pair, int nt, cudaStrea
       return cudaErrorNotSupported;
   if (!pair) maps.w[1] = maps.w[0];
   // Few tiles (one expert): spread them one or two warps per SM, so the
-  // per-lane fmaf chains of each tile get a whole SM's issue slots.
+  // per-lane fmaf chains of each tile get a whole SM's issue slots; a launch
+  // beside other kernels packs two warps per CTA and leaves SMs to them.
   const long long tiles = static_cast<long long>(a.max_items) * (pair ? 2 : 1) * (a.rows / 32);
-  const bool two = tiles > sm_count();
+  const bool two = a.beside || tiles > sm_count();
   switch (nt) {
     case 1: return two ? launch_fp8_stream_nt<1, 2>(maps, a, pair, st)
                        : launch_fp8_stream_nt<1, 1>(maps, a, pair, st);

@@ -58,6 +58,9 @@ struct Fp8GemvArgs {
   const GemvItem* items;
   const int* n_items;
   int max_items;
+  // 1: the launch runs beside other kernels (the shared expert beside the
+  // router and the routed experts): two warps per CTA on half as many SMs
+  int beside = 0;
 };
 
 struct Bf16GemvArgs {

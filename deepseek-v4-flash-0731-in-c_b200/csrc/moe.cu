@@ -271,6 +271,40 @@ __device__ __forceinline__ float warp_segment_abs(const SegState& st, int c_begi
 // evaluation of the bound itself).
 __device__ void write_shared_items(const RouterArgs& a);
 
+// FP8 (E4M3 grid, power-of-two per-128 scale) quant of every token row of x
+// into xq/xs, one (row, 128-column block) per warp task; gw/nw = this warp's
+// index and the warp count over the launch.
+__device__ void quant_rows(const RouterArgs& a, int gw, int nw) {
+  const int lane = threadIdx.x & 31;
+  const int nb = (a.H + 127) / 128;
+  for (int task = gw; task < a.M * nb; task += nw) {
+    const int r = task / nb, b = task % nb;
+    const float* xr = a.x + static_cast<size_t>(r) * a.H + b * 128;
+    const int len = min(128, a.H - b * 128);
+    float v[4];
+    float amax = 0.f;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int i = lane + 32 * k;
+      v[k] = i < len ? xr[i] : 0.f;
+      amax = fmaxf(amax, fabsf(v[k]));
+    }
+    amax = warp_max(amax);
+    const float scale = pow2_scale_448(amax);
+    const float inv = 1.0f / scale;
+    if (lane == 0) a.xs[static_cast<size_t>(r) * nb + b] = scale;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int i = lane + 32 * k;
+      if (i < len) {
+        float q = v[k] * inv;
+        q = q > 448.f ? 448.f : (q < -448.f ? -448.f : q);
+        a.xq[static_cast<size_t>(r) * a.H + b * 128 + i] = e4m3_round_f16(q);
+      }
+    }
+  }
+}
+
 __global__ void __launch_bounds__(kLogitWarps * 32) router_logits_kernel(const RouterArgs a) {
   __shared__ float seg_tot[kLogitWarps], seg_abs[kLogitWarps], seg_p[kLogitWarps];
   pdl_wait();  // x comes from the previous kernel
@@ -278,37 +312,8 @@ __global__ void __launch_bounds__(kLogitWarps * 32) router_logits_kernel(const R
   if (a.items_sh && blockIdx.x == 0 && blockIdx.y == 0) write_shared_items(a);
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int e = blockIdx.x, t = blockIdx.y;
-  if (a.xq) {
-    const int nb = (a.H + 127) / 128;
-    const int gw = (blockIdx.y * gridDim.x + blockIdx.x) * kLogitWarps + warp;
-    const int nw = gridDim.x * gridDim.y * kLogitWarps;
-    for (int task = gw; task < a.M * nb; task += nw) {
-      const int r = task / nb, b = task % nb;
-      const float* xr = a.x + static_cast<size_t>(r) * a.H + b * 128;
-      const int len = min(128, a.H - b * 128);
-      float v[4];
-      float amax = 0.f;
-#pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        const int i = lane + 32 * k;
-        v[k] = i < len ? xr[i] : 0.f;
-        amax = fmaxf(amax, fabsf(v[k]));
-      }
-      amax = warp_max(amax);
-      const float scale = pow2_scale_448(amax);
-      const float inv = 1.0f / scale;
-      if (lane == 0) a.xs[static_cast<size_t>(r) * nb + b] = scale;
-#pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        const int i = lane + 32 * k;
-        if (i < len) {
-          float q = v[k] * inv;
-          q = q > 448.f ? 448.f : (q < -448.f ? -448.f : q);
-          a.xq[static_cast<size_t>(r) * a.H + b * 128 + i] = e4m3_round_f16(q);
-        }
-      }
-    }
-  }
+  if (a.xq) quant_rows(a, (blockIdx.y * gridDim.x + blockIdx.x) * kLogitWarps + warp,
+                      gridDim.x * gridDim.y * kLogitWarps);
   const uint16_t* g = a.gate + static_cast<size_t>(e) * a.H;
   const float* xr = a.x + static_cast<size_t>(t) * a.H;
   const int nch = (a.H + 255) / 256;
@@ -512,6 +517,16 @@ __device__ void block_plan(const RouterArgs& a, int* cnt, int* cnt1, int* ids) {
       out_dn[item] = dn;
     }
   }
+}
+
+// The activation quant and the shared-expert items as a launch of their
+// own, ahead of the logits, so the shared expert (which needs only these)
+// starts while the router is still running.
+__global__ void __launch_bounds__(kLogitWarps * 32) act_quant_kernel(const RouterArgs a) {
+  pdl_wait();  // x comes from the previous kernel
+  pdl_trigger();
+  if (a.items_sh && blockIdx.x == 0) write_shared_items(a);
+  quant_rows(a, blockIdx.x * kLogitWarps + (threadIdx.x >> 5), gridDim.x * kLogitWarps);
 }
 
 // Shared-expert items (every token, in groups of kItemTok); they depend on M
@@ -961,8 +976,8 @@ static RouterArgs make_router_args(const MoeConfig& c, const MoeWeights& w, cons
 
 // Launch 1 of the router: logits, bounds, activation quant, shared items.
 cudaError_t route_logits(const RouterArgs& a, const MoeConfig& c, const MoeWorkspace& ws, int M,
-                         bool plan, cudaStream_t st) {
-  if (plan && ws.timing) record_timing(ws.timing[4], st);
+                         bool plan, cudaStream_t st, bool mark_start = true) {
+  if (plan && ws.timing && mark_start) record_timing(ws.timing[4], st);
   {
     cudaError_t e = launch_pdl(router_logits_kernel, dim3(c.n_experts, M), dim3(kLogitWarps * 32),
                                0, st, a);
@@ -1029,15 +1044,32 @@ cudaError_t moe_forward_local(const MoeConfig& c, const MoeWeights& w, const Moe
   RouterArgs ra = make_router_args(c, w, ws, x, token_ids, M, 0, true);
   ra.sh_t0 = sh_t0;
   ra.sh_n = sh_n;
-  if ((err = route_logits(ra, c, ws, M, true, st)) != cudaSuccess) return err;
   const QAct act{ws.xq, ws.xs, H, nullptr};
 
   const bool has_shared = c.shared_kind != kSharedNone && w.sh1 != nullptr;
-  // the shared expert overlaps the routed path on a side stream, or runs
-  // first on `st` when the caller asked for a single stream
+  // the shared expert overlaps the router and the routed path on a side
+  // stream, or runs first on `st` when the caller asked for a single stream
   SideStream* side = nullptr;
   if (has_shared && !opt.single_stream) side = &side_stream();
   const cudaStream_t sst = side ? side->s : st;
+  // With a side stream the activation quant runs as its own launch and the
+  // shared expert forks right after it, ahead of the logits; otherwise the
+  // logit kernel does the quant on the side.
+  const bool early = side != nullptr;
+  RouterArgs rl = ra;  // the logit launch's arguments
+  if (early) {
+    if (ws.timing) record_timing(ws.timing[4], st);  // the router's time includes the quant
+    const int nb = (H + 127) / 128;
+    const int grid = std::max(1, std::min((M * nb + kLogitWarps - 1) / kLogitWarps, 1024));
+    if ((err = launch_pdl(act_quant_kernel, dim3(grid), dim3(kLogitWarps * 32), 0, st, ra)) !=
+        cudaSuccess)
+      return err;
+    rl.xq = nullptr;
+    rl.xs = nullptr;
+    rl.items_sh = nullptr;
+  } else if ((err = route_logits(ra, c, ws, M, true, st)) != cudaSuccess) {
+    return err;
+  }
   if (has_shared) {
     if (side) {
       cudaEventRecord(side->fork, st);
@@ -1054,6 +1086,7 @@ cudaError_t moe_forward_local(const MoeConfig& c, const MoeWeights& w, const Moe
       g.in = H; g.rows = I; g.round_out = 1; g.act = act;
       g.Y[0] = ws.sh_gate; g.Y[1] = ws.sh_up;
       g.items = ws.items_sh; g.n_items = ws.counters + 3; g.max_items = sh_items;
+      g.beside = side != nullptr;
       if ((err = launch_fp8_gemv(g, true, nt, sst)) != cudaSuccess) return err;
       if ((err = launch_swiglu_quant(ws.sh_gate + so, ws.sh_up + so, I, sh_n, nullptr,
                                      c.swiglu_limit, ws.sh_qy + so, ws.sh_qys + sq, nullptr,
@@ -1064,6 +1097,7 @@ cudaError_t moe_forward_local(const MoeConfig& c, const MoeWeights& w, const Moe
       d.in = I; d.rows = H; d.round_out = 1; d.act = sact;
       d.Y[0] = ws.shared;
       d.items = ws.items_sh; d.n_items = ws.counters + 3; d.max_items = sh_items;
+      d.beside = side != nullptr;
       if ((err = launch_fp8_gemv(d, false, nt, sst)) != cudaSuccess) return err;
     } else {
       Fp4GemvArgs g{};
@@ -1085,6 +1119,7 @@ cudaError_t moe_forward_local(const MoeConfig& c, const MoeWeights& w, const Moe
     }
     if (side) cudaEventRecord(side->join, side->s);
   }
+  if (early && (err = route_logits(rl, c, ws, M, true, st, false)) != cudaSuccess) return err;
 
   // router launch 2: selection and the routed expert plan (overlaps the
   // shared expert on the side stream)
