@@ -9,10 +9,31 @@
 // kernel calls pdl_wait() before its first read of data another kernel
 // produced.
 #pragma once
+#include <mutex>
 #include <utility>
+#include <vector>
 #include <cuda_runtime.h>
 
 namespace dsv4 {
+
+// Every kernel of the chains asks for the largest shared-memory carveout:
+// a CTA of a small kernel (router, SwiGLU, combine) and one of a streaming
+// GEMV (~150 KB of shared memory) then share an SM without the SM first
+// draining to change its L1 / shared-memory split, which otherwise delays
+// a kernel forked onto a side stream by several microseconds.
+inline void prefer_max_shared(const void* fn) {
+  static std::mutex mu;
+  static std::vector<std::pair<const void*, int>> done;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return;
+  std::lock_guard<std::mutex> lock(mu);
+  for (const auto& d : done)
+    if (d.first == fn && d.second == dev) return;
+  if (cudaFuncSetAttribute(fn, cudaFuncAttributePreferredSharedMemoryCarveout,
+                           cudaSharedmemCarveoutMaxShared) != cudaSuccess)
+    (void)cudaGetLastError();  // a preference only: clear the failure
+  done.emplace_back(fn, dev);
+}
 
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_trigger() {
@@ -22,6 +43,7 @@ __device__ __forceinline__ void pdl_trigger() {
 template <typename... KArgs, typename... Args>
 cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
                        cudaStream_t st, Args&&... args) {
+  prefer_max_shared(reinterpret_cast<const void*>(kernel));
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
   cfg.blockDim = block;
