@@ -926,15 +926,27 @@ __global__ void __launch_bounds__(128) attn_combine_kernel(AttnProblem p, int sp
   const float den = s_den;
   const int d0 = threadIdx.x * 4;
   float acc[4] = {0.f, 0.f, 0.f, 0.f};
-  for (int s = 0; s < splits; ++s) {
-    const float w = wsm[s];
-    if (w == 0.0f) continue;
-    const float4 v = *reinterpret_cast<const float4*>(
-        o_part + ((static_cast<size_t>(b) * splits + s) * p.H + h) * kTcD + d0);
-    acc[0] += v.x * w;
-    acc[1] += v.y * w;
-    acc[2] += v.z * w;
-    acc[3] += v.w * w;
+  const float* ob = o_part + (static_cast<size_t>(b) * splits * p.H + h) * kTcD + d0;
+  const size_t sstride = static_cast<size_t>(p.H) * kTcD;  // floats between splits
+  // kBatch splits' partial rows are loaded together (independent L2 reads in
+  // flight), then added in split order; an empty split (w == 0) adds nothing
+  constexpr int kBatch = 16;
+  for (int s = 0; s < splits; s += kBatch) {
+    float4 v[kBatch];
+#pragma unroll
+    for (int k = 0; k < kBatch; ++k)
+      if (s + k < splits)
+        v[k] = *reinterpret_cast<const float4*>(ob + static_cast<size_t>(s + k) * sstride);
+#pragma unroll
+    for (int k = 0; k < kBatch; ++k) {
+      const float w = s + k < splits ? wsm[s + k] : 0.0f;
+      if (w != 0.0f) {
+        acc[0] += v[k].x * w;
+        acc[1] += v[k].y * w;
+        acc[2] += v[k].z * w;
+        acc[3] += v[k].w * w;
+      }
+    }
   }
   float o[4];
 #pragma unroll
