@@ -80,6 +80,32 @@ __device__ __forceinline__ uint32_t e4m3x2_to_f16x2(uint32_t two) {
 
 // acc = fma(a, b, acc) with a, b f16 halves widened exactly to f32; one
 // rounding, i.e. identical to fmaf((float)a, (float)b, acc).
+// Sum over routes k = 0..topk-1 of vals[k * stride] for the routes with
+// ids[k] >= 0, added in route order (the reference's combine order,
+// src/dsv4/dsv4_model.c:6795-6805); eight routes' loads are issued together
+// so their latencies overlap. Every vals[k * stride] must be readable.
+__device__ __forceinline__ float sum_routes(const int* ids, const float* vals, size_t stride,
+                                            int topk) {
+  float acc = 0.0f;
+  for (int k0 = 0; k0 < topk; k0 += 8) {
+    int id[8];
+    float v[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      id[k] = -1;
+      v[k] = 0.0f;
+      if (k0 + k < topk) {
+        id[k] = ids[k0 + k];
+        v[k] = vals[static_cast<size_t>(k0 + k) * stride];
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < 8; ++k)
+      if (id[k] >= 0) acc += v[k];
+  }
+  return acc;
+}
+
 __device__ __forceinline__ float fma_h_lo(uint32_t a2, uint32_t b2, float acc) {
   asm("{ .reg .b16 al, ah, bl, bh; mov.b32 {al, ah}, %1; mov.b32 {bl, bh}, %2;"
       " fma.rn.f32.f16 %0, al, bl, %0; }"

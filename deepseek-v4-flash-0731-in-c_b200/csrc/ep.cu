@@ -101,11 +101,8 @@ __global__ void __launch_bounds__(256) ep_combine_kernel(EpExchange x, const flo
        i += static_cast<size_t>(gridDim.x) * blockDim.x) {
     const int t = static_cast<int>(i / H);
     const int c = static_cast<int>(i % H);
-    float acc = 0.0f;
-    for (int k = 0; k < topk; ++k) {
-      const int slot = t * topk + k;
-      if (idx[slot] >= 0) acc += slots[static_cast<size_t>(slot) * H + c];
-    }
+    float acc = sum_routes(idx + t * topk, slots + static_cast<size_t>(t) * topk * H + c, H,
+                           topk);
     if (shared) acc += shared[i];
     out[i] = bf16_round(acc);
   }
@@ -183,11 +180,8 @@ __global__ void __launch_bounds__(256) ep_combine_owner_kernel(EpExchange x, con
        i += static_cast<size_t>(gridDim.x) * blockDim.x) {
     const int tl = static_cast<int>(i / H);
     const int c = static_cast<int>(i % H);
-    float acc = 0.0f;
-    for (int k = 0; k < topk; ++k) {
-      if (idx[(t0 + tl) * topk + k] >= 0)
-        acc += slots[static_cast<size_t>(tl * topk + k) * H + c];
-    }
+    float acc = sum_routes(idx + (t0 + tl) * topk,
+                           slots + static_cast<size_t>(tl) * topk * H + c, H, topk);
     if (shared) acc += shared[static_cast<size_t>(t0) * H + i];
     out[i] = bf16_round(acc);
   }

@@ -845,11 +845,8 @@ __global__ void moe_combine_kernel(const float* __restrict__ routed, const float
        i += static_cast<size_t>(gridDim.x) * blockDim.x) {
     const int t = static_cast<int>(i / H);
     const int c = static_cast<int>(i % H);
-    float acc = 0.0f;
-    for (int k = 0; k < topk; ++k) {
-      const int slot = t * topk + k;
-      if (idx[slot] >= 0) acc += routed[static_cast<size_t>(slot) * H + c];
-    }
+    float acc = sum_routes(idx + t * topk, routed + static_cast<size_t>(t) * topk * H + c, H,
+                           topk);
     if (shared) acc += shared[i];
     out[i] = bf16_round(acc);
   }
