@@ -194,14 +194,26 @@ __device__ __forceinline__ void warp_segment_load(const uint16_t* g, const float
   const int lane = threadIdx.x & 31;
   float tot[kSegCache];
   float pa = 0.0f;
+  // every chunk's gate and activation vectors are requested before the
+  // first is used, so the segment costs one memory round trip
+  uint4 gvs[kSegCache];
+  float4 x0s[kSegCache], x1s[kSegCache];
+#pragma unroll
+  for (int j = 0; j < kSegCache; ++j) {
+    if (c_begin + j < c_end) {
+      const int col = (c_begin + j) * 256 + lane * 8;
+      gvs[j] = __ldg(reinterpret_cast<const uint4*>(g + col));
+      x0s[j] = __ldg(reinterpret_cast<const float4*>(xr + col));
+      x1s[j] = __ldg(reinterpret_cast<const float4*>(xr + col + 4));
+    }
+  }
 #pragma unroll
   for (int j = 0; j < kSegCache; ++j) {
     float run = 0.0f;
     if (c_begin + j < c_end) {
-      const int col = (c_begin + j) * 256 + lane * 8;
-      const uint4 gv = __ldg(reinterpret_cast<const uint4*>(g + col));
-      const float4 x0 = __ldg(reinterpret_cast<const float4*>(xr + col));
-      const float4 x1 = __ldg(reinterpret_cast<const float4*>(xr + col + 4));
+      const uint4 gv = gvs[j];
+      const float4 x0 = x0s[j];
+      const float4 x1 = x1s[j];
       const uint32_t gw[4] = {gv.x, gv.y, gv.z, gv.w};
       const float xv[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
 #pragma unroll
