@@ -1,4 +1,4 @@
-"""bench.py - decode throughput of one DeepSeek-V4-Flash MoE layer (BASELINE
+"""bench.py - decode throughput of one DeepSeek-V4-Flash MoE layer (benchmark
 config 2) on B200, through libdsv4_cuda.so.
 
 A step is one decode token (M=1 by default) through one MoE layer: router
@@ -16,9 +16,12 @@ through consecutive MoE layers), each layer on its own token rows.
 --impl reference times the reference engine's own CPU implementation of the
 same step (oracle/_ref, built from the reference sources; the C restatement
 when that library is absent) on the host cores. Under torchrun (N>1) the
-MoE layer is expert-parallel: each rank owns E/N routed experts, the router
-and shared expert are replicated, and one NCCL all-reduce of the zero-padded
-[M][topk][H] expert outputs precedes the ordered combine.
+MoE layer is expert-parallel: each rank owns E/N routed experts and, by
+default, brings its own tokens (--ep-mode tokens): the tokens are gathered
+and each routed slot returned to its token's owner over peer memory, and
+the owner runs the ordered combine (--ep-mode replicated runs the same
+tokens on every rank, with a peer-memory slot exchange or an NCCL
+all-reduce, --ep-exchange).
 """
 from __future__ import annotations
 

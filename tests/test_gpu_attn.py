@@ -264,7 +264,7 @@ def test_attn_host_dropin_matches_reference(cuda, ref, orc):
 
 @pytest.mark.parametrize("B,ctx", [(1, 4096), (2, 32768)])
 def test_attn_config3_shapes(cuda, orc, B, ctx):
-    """BASELINE config 3 shapes through the FP8 cache: 128 heads x 512,
+    """Benchmark config 3 shapes through the FP8 cache: 128 heads x 512,
     positions 0..ctx-1; checked against the oracle on a subset of heads."""
     rng = np.random.default_rng(ctx + B)
     H = 128

@@ -31,7 +31,7 @@ def check_close(got, want, min_exact=0.9):
 
 
 @pytest.mark.parametrize("cfg", [
-    dict(hid=256, mi=128, E=16, k=2, shared="fp8", hv=0),     # BASELINE config-1 MoE shape
+    dict(hid=256, mi=128, E=16, k=2, shared="fp8", hv=0),     # benchmark config-1 MoE shape
     dict(hid=256, mi=128, E=16, k=2, shared="fp4", hv=0),
     dict(hid=256, mi=128, E=16, k=2, shared="fp8", hv=40),    # hash layer
     dict(hid=1024, mi=512, E=64, k=6, shared=None, hv=0),
