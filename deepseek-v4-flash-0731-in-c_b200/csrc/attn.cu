@@ -907,16 +907,42 @@ __global__ void __launch_bounds__(128) attn_combine_kernel(AttnProblem p, int sp
     // warp 0: the splits' maxima and weighted denominators, lanes striding
     // over the splits, then warp reductions
     const int lane = threadIdx.x;
+    // a lane's splits (lane, lane + 32, ...) four at a time: their maxima
+    // and denominators are loaded together
+    constexpr int kPer = 4;
     float M = -INFINITY;
-    for (int s = lane; s < splits; s += 32)
-      M = fmaxf(M, m_part[(static_cast<size_t>(b) * splits + s) * p.H + h]);
-    M = warp_max(M);
     float den = 0.0f;
-    for (int s = lane; s < splits; s += 32) {
-      const size_t i = (static_cast<size_t>(b) * splits + s) * p.H + h;
-      const float w = (m_part[i] == -INFINITY) ? 0.0f : exp2f(m_part[i] - M);
-      wsm[s] = w;
-      den += den_part[i] * w;
+    if (splits <= 32 * kPer) {
+      float mv[kPer], dv[kPer];
+#pragma unroll
+      for (int k = 0; k < kPer; ++k) {
+        const int s = lane + 32 * k;
+        const size_t i = (static_cast<size_t>(b) * splits + s) * p.H + h;
+        mv[k] = s < splits ? m_part[i] : -INFINITY;
+        dv[k] = s < splits ? den_part[i] : 0.0f;
+      }
+#pragma unroll
+      for (int k = 0; k < kPer; ++k) M = fmaxf(M, mv[k]);
+      M = warp_max(M);
+#pragma unroll
+      for (int k = 0; k < kPer; ++k) {
+        const int s = lane + 32 * k;
+        if (s < splits) {
+          const float w = (mv[k] == -INFINITY) ? 0.0f : exp2f(mv[k] - M);
+          wsm[s] = w;
+          den += dv[k] * w;
+        }
+      }
+    } else {
+      for (int s = lane; s < splits; s += 32)
+        M = fmaxf(M, m_part[(static_cast<size_t>(b) * splits + s) * p.H + h]);
+      M = warp_max(M);
+      for (int s = lane; s < splits; s += 32) {
+        const size_t i = (static_cast<size_t>(b) * splits + s) * p.H + h;
+        const float w = (m_part[i] == -INFINITY) ? 0.0f : exp2f(m_part[i] - M);
+        wsm[s] = w;
+        den += den_part[i] * w;
+      }
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) den += __shfl_xor_sync(0xffffffffu, den, o);
