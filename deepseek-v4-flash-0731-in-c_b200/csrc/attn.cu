@@ -31,6 +31,7 @@
 #include "attn.cuh"
 #include "bulk.cuh"
 #include "dsv4_common.cuh"
+#include "launch.cuh"
 
 namespace dsv4 {
 namespace {
@@ -488,6 +489,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) attn_tc_kernel(const __grid_con
     bars->abort_flag = 0;
     mbar_fence_init();
   }
+  pdl_wait();  // q, the cache rows and the indices come from earlier kernels
+  pdl_trigger();
   if (warp == kTcMmaWarp) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                      smem_addr(&bars->tmem_base)),
@@ -903,6 +906,8 @@ __global__ void __launch_bounds__(128) attn_combine_kernel(AttnProblem p, int sp
   const int h = blockIdx.x, b = blockIdx.y;
   extern __shared__ float wsm[];  // [splits]
   __shared__ float s_den;
+  pdl_wait();  // the partials come from attn_tc_kernel
+  pdl_trigger();
   if (threadIdx.x < 32) {
     // warp 0: the splits' maxima and weighted denominators, lanes striding
     // over the splits, then warp reductions
@@ -1099,11 +1104,14 @@ cudaError_t attn_forward(const AttnProblem& p, void* ws, cudaStream_t st, cudaEv
       if (dev >= 0 && dev < 64) attr_set[dev] = true;
     }
     if (main_begin) cudaEventRecord(main_begin, st);
-    attn_tc_kernel<<<dim3(2 * plan.splits, p.B), kTcThreads, kTcSmem, st>>>(a);
+    cudaError_t e = launch_pdl(attn_tc_kernel, dim3(2 * plan.splits, p.B), dim3(kTcThreads),
+                               kTcSmem, st, a);
+    if (e != cudaSuccess) return e;
     if (main_end) cudaEventRecord(main_end, st);
-    attn_combine_kernel<<<dim3(p.H, p.B), 128, plan.splits * sizeof(float), st>>>(
-        p, plan.splits, a.m_part, a.den_part, a.o_part);
-    return cudaGetLastError();
+    e = launch_pdl(attn_combine_kernel, dim3(p.H, p.B), dim3(128), plan.splits * sizeof(float), st,
+                   p, plan.splits, static_cast<const float*>(a.m_part),
+                   static_cast<const float*>(a.den_part), static_cast<const float*>(a.o_part));
+    return e != cudaSuccess ? e : cudaGetLastError();
   }
   SimtArgs a;
   a.p = p;
