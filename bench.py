@@ -82,6 +82,16 @@ def parse():
     return ap.parse_args()
 
 
+def chain_lengths(count, n_layers):
+    """Layers per graph replay covering exactly `count` steps: full chains of
+    n_layers, then one shorter chain for the remainder."""
+    out = []
+    while count > 0:
+        out.append(min(n_layers, count))
+        count -= out[-1]
+    return out
+
+
 # ---------------------------------------------------------------- weights --
 def make_device_layer(torch, seed, dev, E=E, I=I, expert_range=None):
     """Random-init config-2 layer in the reference layouts, on the GPU.
@@ -391,13 +401,11 @@ def main():
     def run_steps(count):
         """`count` steps: new token rows for each chained layer, one replay
         per chain."""
-        while count > 0:
-            n = min(n_lay, count)
+        for n in chain_lengths(count, n_lay):
             s0 = (replays[0] * n_lay) % pool
             xch[:n].copy_(x_dev[s0:s0 + n], non_blocking=True)
             chains[n - 1].replay()
             replays[0] += 1
-            count -= n
 
     with torch.cuda.stream(stream):
         run_steps(args.warmup)
