@@ -269,28 +269,10 @@ __host__ __device__ constexpr uint32_t umma_idesc_bf16(int m, int n, bool b_mn_m
          (static_cast<uint32_t>(n >> 3) << 17) | (static_cast<uint32_t>(m >> 4) << 24);
 }
 
-__device__ __forceinline__ void umma_bf16(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc,
-                                          uint32_t accumulate) {
-  asm volatile(
-      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
-      " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(d_tmem),
-      "l"(a), "l"(b), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
-
-// D += A B with A (M x 16, BF16 pairs packed along K) in TMEM.
-__device__ __forceinline__ void umma_bf16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b,
-                                             uint32_t idesc, uint32_t accumulate) {
-  asm volatile(
-      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
-      " tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}\n" ::"r"(d_tmem),
-      "r"(a_tmem), "l"(b), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
-
-// Warp-converged issue: every lane of the MMA warp executes these, one
+// MMA issue, warp-converged: every lane of the MMA warp executes these, one
 // elected lane (the same one each time) issues. A rolled single-lane issue
-// loop runs several times slower than the tensor pipe.
+// loop runs several times slower than the tensor pipe. The _ts form takes
+// A (M x 16, BF16 pairs packed along K) from TMEM.
 __device__ __forceinline__ void umma_bf16_e(uint32_t d_tmem, uint64_t a, uint64_t b,
                                             uint32_t idesc, uint32_t accumulate) {
   asm volatile(
@@ -320,12 +302,6 @@ __device__ __forceinline__ float ex2_approx(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
-}
-
-__device__ __forceinline__ void umma_commit(uint64_t* bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::
-                   "r"(smem_addr(bar))
-               : "memory");
 }
 
 __device__ __forceinline__ void tc_fence_before() {
