@@ -343,42 +343,6 @@ struct Fp4Maps {
   CUtensorMap s[2];  // [rows_total][in/32] codes, box [32][16]
 };
 
-// Two 32-column partials computed with interleaved (independent) chains.
-__device__ __forceinline__ void fp4_partial16x2(const uint32_t* wa, const uint32_t* xa,
-                                                const uint32_t* wb, const uint32_t* xb,
-                                                float& pa, float& pb) {
-  pa = 0.0f;
-  pb = 0.0f;
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    uint32_t a0, a1, a2, a3, b0, b1, b2, b3;
-    asm("{ .reg .b8 c0, c1, c2, c3; mov.b32 {c0, c1, c2, c3}, %4;"
-        " cvt.rn.f16x2.e2m1x2 %0, c0; cvt.rn.f16x2.e2m1x2 %1, c1;"
-        " cvt.rn.f16x2.e2m1x2 %2, c2; cvt.rn.f16x2.e2m1x2 %3, c3; }"
-        : "=r"(a0), "=r"(a1), "=r"(a2), "=r"(a3) : "r"(wa[i]));
-    asm("{ .reg .b8 c0, c1, c2, c3; mov.b32 {c0, c1, c2, c3}, %4;"
-        " cvt.rn.f16x2.e2m1x2 %0, c0; cvt.rn.f16x2.e2m1x2 %1, c1;"
-        " cvt.rn.f16x2.e2m1x2 %2, c2; cvt.rn.f16x2.e2m1x2 %3, c3; }"
-        : "=r"(b0), "=r"(b1), "=r"(b2), "=r"(b3) : "r"(wb[i]));
-    pa = fma_h_lo(a0, xa[4 * i + 0], pa);
-    pb = fma_h_lo(b0, xb[4 * i + 0], pb);
-    pa = fma_h_hi(a0, xa[4 * i + 0], pa);
-    pb = fma_h_hi(b0, xb[4 * i + 0], pb);
-    pa = fma_h_lo(a1, xa[4 * i + 1], pa);
-    pb = fma_h_lo(b1, xb[4 * i + 1], pb);
-    pa = fma_h_hi(a1, xa[4 * i + 1], pa);
-    pb = fma_h_hi(b1, xb[4 * i + 1], pb);
-    pa = fma_h_lo(a2, xa[4 * i + 2], pa);
-    pb = fma_h_lo(b2, xb[4 * i + 2], pb);
-    pa = fma_h_hi(a2, xa[4 * i + 2], pa);
-    pb = fma_h_hi(b2, xb[4 * i + 2], pb);
-    pa = fma_h_lo(a3, xa[4 * i + 3], pa);
-    pb = fma_h_lo(b3, xb[4 * i + 3], pb);
-    pa = fma_h_hi(a3, xa[4 * i + 3], pa);
-    pb = fma_h_hi(b3, xb[4 * i + 3], pb);
-  }
-}
-
 // Four 32-column partials with four interleaved (independent) chains: one
 // warp keeps four FMAs in flight per four-cycle FMA latency.
 __device__ __forceinline__ void fp4_partial16x4(const uint32_t (*w)[4], const uint32_t (*x)[16],
