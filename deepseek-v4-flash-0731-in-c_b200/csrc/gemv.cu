@@ -972,13 +972,10 @@ template <int NT, int WARPS>
 cudaError_t launch_stream_nt(const Fp4Maps& maps, const Fp4GemvArgs& a, bool pair,
                              cudaStream_t st) {
   const size_t smem = static_cast<size_t>(WARPS) * StreamLayout<NT>::kWarpBytes + 1024;
-  static bool attr_done = false;  // per template instance
-  if (!attr_done) {
-    cudaError_t e = cudaFuncSetAttribute(fp4_stream_kernel<NT, WARPS>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+  {
+    cudaError_t e = set_max_dynamic_smem(reinterpret_cast<const void*>(fp4_stream_kernel<NT, WARPS>),
                                          static_cast<int>(smem));
     if (e != cudaSuccess) return e;
-    attr_done = true;
   }
   const long long tiles = static_cast<long long>(a.max_items) * (pair ? 2 : 1) *
                           ((a.rows + 31) / 32);
@@ -1269,24 +1266,23 @@ template <int NT, int WARPS>
 cudaError_t launch_fp8_stream_nt(const Fp8Maps& maps, const Fp8GemvArgs& a, bool pair,
                                  cudaStream_t st) {
   const size_t smem = static_cast<size_t>(WARPS) * F8Layout<NT>::kWarpBytes + 1024;
-  static bool attr_done = false;  // per template instance
-  if (!attr_done) {
-    cudaError_t e = cudaFuncSetAttribute(fp8_stream_kernel<NT, WARPS>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+  {
+    cudaError_t e = set_max_dynamic_smem(reinterpret_cast<const void*>(fp8_stream_kernel<NT, WARPS>),
                                          static_cast<int>(smem));
     if (e != cudaSuccess) return e;
-    attr_done = true;
   }
   const long long tiles = static_cast<long long>(a.max_items) * (pair ? 2 : 1) * (a.rows / 32);
   const int grid = static_cast<int>(std::max<long long>(
       1, std::min<long long>(sm_count(), (tiles + WARPS - 1) / WARPS)));
+  unsigned int* err = a.err ? a.err : device_error_word();
   return launch_pdl(fp8_stream_kernel<NT, WARPS>, dim3(grid), dim3(WARPS * 32), smem, st, maps, a,
-                    pair ? 1 : 0, device_error_word());
+                    pair ? 1 : 0, err);
 }
 
 // Returns cudaErrorNotSupported when the shape or alignment does not fit
 // the streaming kernel (the caller then uses the LDG kernel).
-cudaError_t launch_fp8_stream(const Fp8GemvArgs& a, bool pair, int nt, cudaStream_t st) {
+cudaError_t launch_fp8_stream(const Fp8GemvArgs& a, bool pair, int nt, cudaStream_t st,
+                              bool map_cache) {
   const int CB = a.in / 128;
   if (a.in % kF8Cols != 0 || CB > 64 || a.rows % 32 != 0 || a.act.ld % 512 != 0 ||
       a.act.x32 || !aligned(a.W[0], 16) || !aligned(a.act.x, 16) || !aligned(a.act.s, 16) ||
@@ -1296,7 +1292,7 @@ cudaError_t launch_fp8_stream(const Fp8GemvArgs& a, bool pair, int nt, cudaStrea
   Fp8Maps maps;
   for (int v = 0; v < (pair ? 2 : 1); ++v)
     if (!make_tma_map_u8(&maps.w[v], a.W[v], static_cast<uint64_t>(a.in), a.rows, 128, 32, true,
-                         true))
+                         map_cache))
       return cudaErrorNotSupported;
   if (!pair) maps.w[1] = maps.w[0];
   // Few tiles (one expert): spread them one or two warps per SM, so the
@@ -1533,13 +1529,10 @@ cudaError_t launch_splitk_cw(const Fp4Maps& maps, const Fp4GemvArgs& a, bool pai
   const size_t smem = static_cast<size_t>(CW) * StreamLayout<1>::kWarpBytes +
                       2 * static_cast<size_t>(G) * 32 * sizeof(float) +
                       2 * static_cast<size_t>(CPT) * 32 * 16 + 1024;
-  static bool attr_done = false;  // per template instance
-  if (!attr_done) {
-    cudaError_t e = cudaFuncSetAttribute(fp4_splitk_kernel<CW>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+  {
+    cudaError_t e = set_max_dynamic_smem(reinterpret_cast<const void*>(fp4_splitk_kernel<CW>),
                                          static_cast<int>(kSplitkSmemCap));
     if (e != cudaSuccess) return e;
-    attr_done = true;
   }
   if (smem > kSplitkSmemCap) return cudaErrorNotSupported;
   const long long tiles = static_cast<long long>(a.max_items) * (pair ? 2 : 1) * ((a.rows + 31) / 32);
@@ -1618,7 +1611,8 @@ cudaError_t launch_fp4_gemv(const Fp4GemvArgs& a, bool pair, int item_tokens, cu
   return fp4_dispatch_nt<1, false>(a, item_tokens, st);
 }
 
-cudaError_t launch_fp8_gemv(const Fp8GemvArgs& a, bool pair, int item_tokens, cudaStream_t st) {
+cudaError_t launch_fp8_gemv(const Fp8GemvArgs& a, bool pair, int item_tokens, cudaStream_t st,
+                            bool map_cache) {
   if (a.rows <= 0 || a.max_items <= 0) return cudaSuccess;
   const bool vec_ok = !a.act.x32 && (a.in % 128 == 0) && aligned(a.W[0], 32) && (a.w_stride % 32 == 0) &&
                       aligned(a.act.x, 32) && (a.act.ld % 128 == 0) &&
@@ -1631,7 +1625,7 @@ cudaError_t launch_fp8_gemv(const Fp8GemvArgs& a, bool pair, int item_tokens, cu
     return cudaGetLastError();
   }
   {
-    cudaError_t e = launch_fp8_stream(a, pair, item_tokens, st);
+    cudaError_t e = launch_fp8_stream(a, pair, item_tokens, st, map_cache);
     if (e != cudaErrorNotSupported) return e;
   }
   const int CB = a.in / 128;

@@ -61,6 +61,7 @@ struct Fp8GemvArgs {
   // 1: the launch runs beside other kernels (the shared expert beside the
   // router and the routed experts): two warps per CTA on half as many SMs
   int beside = 0;
+  unsigned int* err = nullptr;  // device error word (null: the library's default)
 };
 
 struct Bf16GemvArgs {
@@ -78,7 +79,7 @@ struct Bf16GemvArgs {
 cudaError_t launch_fp4_gemv(const Fp4GemvArgs& a, bool pair, int item_tokens,
                             cudaStream_t st, bool map_cache = true);
 cudaError_t launch_fp8_gemv(const Fp8GemvArgs& a, bool pair, int item_tokens,
-                            cudaStream_t st);
+                            cudaStream_t st, bool map_cache = true);
 cudaError_t launch_bf16_gemv(const Bf16GemvArgs& a, int item_tokens,
                              cudaStream_t st);
 

@@ -35,6 +35,22 @@ inline void prefer_max_shared(const void* fn) {
   done.emplace_back(fn, dev);
 }
 
+// Raises a kernel's dynamic shared-memory limit to `bytes` once per
+// (kernel, device): the attribute belongs to the device current at the call.
+inline cudaError_t set_max_dynamic_smem(const void* fn, int bytes) {
+  static std::mutex mu;
+  static std::vector<std::pair<const void*, int>> done;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  std::lock_guard<std::mutex> lock(mu);
+  for (const auto& d : done)
+    if (d.first == fn && d.second == dev) return cudaSuccess;
+  e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e == cudaSuccess) done.emplace_back(fn, dev);
+  return e;
+}
+
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_trigger() {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");

@@ -1096,7 +1096,8 @@ cudaError_t moe_forward_local(const MoeConfig& c, const MoeWeights& w, const Moe
       g.Y[0] = ws.sh_gate; g.Y[1] = ws.sh_up;
       g.items = ws.items_sh; g.n_items = ws.counters + 3; g.max_items = sh_items;
       g.beside = side != nullptr;
-      if ((err = launch_fp8_gemv(g, true, nt, sst)) != cudaSuccess) return err;
+      g.err = opt.err;
+      if ((err = launch_fp8_gemv(g, true, nt, sst, opt.map_cache)) != cudaSuccess) return err;
       if ((err = launch_swiglu_quant(ws.sh_gate + so, ws.sh_up + so, I, sh_n, nullptr,
                                      c.swiglu_limit, ws.sh_qy + so, ws.sh_qys + sq, nullptr,
                                      sst)) != cudaSuccess)
@@ -1107,7 +1108,8 @@ cudaError_t moe_forward_local(const MoeConfig& c, const MoeWeights& w, const Moe
       d.Y[0] = ws.shared;
       d.items = ws.items_sh; d.n_items = ws.counters + 3; d.max_items = sh_items;
       d.beside = side != nullptr;
-      if ((err = launch_fp8_gemv(d, false, nt, sst)) != cudaSuccess) return err;
+      d.err = opt.err;
+      if ((err = launch_fp8_gemv(d, false, nt, sst, opt.map_cache)) != cudaSuccess) return err;
     } else {
       Fp4GemvArgs g{};
       g.W[0] = w.sh1; g.S[0] = w.sh1s; g.W[1] = w.sh3; g.S[1] = w.sh3s;

@@ -223,8 +223,10 @@ int dsv4cuda_moe_timing_end2(dsv4cuda_moe_layer *L, int *n_forwards, float *gate
  * but the caller supplies the config, DEVICE weight pointers (layouts as in
  * dsv4cuda_moe_weights), x [n][H], token_ids (hash layers) and out [n][H];
  * the working memory is a 4 MiB array inside this library, present on
- * every GPU that loads it until the process exits. Nothing is allocated:
- * no cudaMalloc/cudaFree, no stream or event creation, no host-side cache.
+ * every GPU that loads it until the process exits. No device memory is
+ * allocated or freed (no cudaMalloc/cudaFree, no stream or event creation,
+ * no allocating library routine); the device error word lives in the same
+ * array and the TMA descriptors are encoded on every call, not cached.
  * Returns -1 with a message (dsv4cuda_last_error) when n_tokens needs more
  * than the 4 MiB (up to 9 tokens fit at hidden 7168 / inter 2048 /
  * 256 experts / top-8). The first call on each device looks up the array's

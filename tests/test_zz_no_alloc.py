@@ -58,6 +58,8 @@ def test_noalloc_matches_regular_entry_point(cuda, cfg):
         w, g = want.cpu().numpy(), got.cpu().numpy()
         assert np.isfinite(g).all(), call
         assert close(g, w), call
+        # the same kernels in the same order: the results are bit-identical
+        assert np.array_equal(g.view(np.uint32), w.view(np.uint32)), call
     regular.close()
 
 
@@ -68,3 +70,56 @@ def test_noalloc_rejects_too_many_tokens(cuda):
     out = torch.empty_like(x)
     with pytest.raises(cuda.Dsv4CudaError, match="working memory"):
         cuda.moe_forward_noalloc(dev, x, out)
+
+
+_FRESH = r"""
+import sys
+sys.path[:0] = sys.argv[1:4]
+import numpy as np
+import torch
+from oracle import make_moe_layer
+torch.cuda.init()
+import dsv4cuda
+dsv4cuda.set_abort_on_error(False)
+L = make_moe_layer(7168, 2048, 16, 8, seed=5, shared="fp8")
+dev = {}
+for k, v in L.items():
+    if isinstance(v, np.ndarray):
+        dev[k] = torch.from_numpy(np.ascontiguousarray(v)).cuda()
+    elif isinstance(v, dict):
+        dev[k] = {kk: (torch.from_numpy(np.ascontiguousarray(vv)).cuda()
+                       if isinstance(vv, np.ndarray) else vv) for kk, vv in v.items()}
+    else:
+        dev[k] = v
+x = torch.randn((2, 7168), device="cuda").to(torch.bfloat16).float()
+out = torch.empty_like(x)
+stream = torch.cuda.current_stream().cuda_stream
+torch.cuda.synchronize()
+free0, _ = torch.cuda.mem_get_info()
+dsv4cuda.moe_forward_noalloc(dev, x, out, stream=stream)  # the first library call
+torch.cuda.synchronize()
+free1, _ = torch.cuda.mem_get_info()
+assert torch.isfinite(out).all()
+print("FREE", free0, free1)
+"""
+
+
+def test_noalloc_first_call_in_fresh_process_allocates_nothing():
+    """A caller that cannot allocate (it owns the device memory through its
+    own pool, or runs inside a capture) must not see the first call take any
+    device memory: in a fresh process whose modules load eagerly, the free
+    bytes the driver reports are the same before and after the first call,
+    which runs the FP8 shared expert's streaming kernels."""
+    import os
+    import subprocess
+    import sys
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    paths = [os.path.join(root, "oracle"), os.path.join(root, "tests", "golden"),
+             os.path.join(root, "deepseek-v4-flash-0731-in-c_b200")]
+    env = dict(os.environ, CUDA_MODULE_LOADING="EAGER")
+    r = subprocess.run([sys.executable, "-c", _FRESH, *paths], env=env, capture_output=True,
+                       text=True, timeout=600)
+    assert r.returncode == 0, r.stdout + r.stderr
+    line = [ln for ln in r.stdout.splitlines() if ln.startswith("FREE")][-1]
+    free0, free1 = (int(v) for v in line.split()[1:])
+    assert free0 == free1, (free0, free1)
