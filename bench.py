@@ -93,22 +93,37 @@ def chain_lengths(count, n_layers):
 
 
 # ---------------------------------------------------------------- weights --
-def make_device_layer(torch, seed, dev, E=E, I=I, expert_range=None):
+EXPERT_BLOCK = 32  # routed experts drawn per generator seed
+
+
+def expert_blocks(n_experts, world):
+    """Experts per generator block: a divisor of every rank's share, so any
+    rank can regenerate any expert's weights bit for bit."""
+    blk = min(EXPERT_BLOCK, n_experts)
+    while blk > 1 and (n_experts % blk or (n_experts // max(world, 1)) % blk):
+        blk //= 2
+    return max(blk, 1)
+
+
+def make_device_layer(torch, seed, dev, E=E, I=I, expert_range=None, block=None):
     """Random-init config-2 layer in the reference layouts, on the GPU.
     expert_range=(lo, hi): routed weights of those experts only (expert
-    parallelism); the router and shared expert are the same on every rank."""
+    parallelism); the router and shared expert are the same on every rank.
+    Routed experts are drawn in blocks of `block` experts, each block from
+    its own seed, so a rank's share equals the same experts of the full
+    layer bit for bit."""
     lo, hi = expert_range if expert_range else (0, E)
+    blk = block or expert_blocks(E, 1)
+    assert lo % blk == 0 and hi % blk == 0, (lo, hi, blk)
     g = torch.Generator(device=dev)
     g.manual_seed(seed)
-    ge = torch.Generator(device=dev)
-    ge.manual_seed(seed * 1000 + lo + 1)
 
-    def u8(*shape):
-        return torch.randint(0, 256, shape, dtype=torch.uint8, device=dev, generator=g)
+    def u8(*shape, gen):
+        return torch.randint(0, 256, shape, dtype=torch.uint8, device=dev, generator=gen)
 
-    def e8m0(*shape):
+    def e8m0(*shape, gen):
         # lognormal(0, 0.5) scale rounded to a power of two: 127 + round(log2 s)
-        z = torch.randn(shape, device=dev, generator=g) * (0.5 / np.log(2.0))
+        z = torch.randn(shape, device=dev, generator=gen) * (0.5 / np.log(2.0))
         return (127 + torch.round(z)).clamp(0, 254).to(torch.uint8)
 
     def fp8(*shape):
@@ -117,16 +132,23 @@ def make_device_layer(torch, seed, dev, E=E, I=I, expert_range=None):
         return c.to(torch.uint8)
 
     gate = (torch.randn(E, H, device=dev, generator=g) * 0.02).to(torch.bfloat16).view(torch.uint16)
-    shared = dict(fp8=True, w1=fp8(I, H), s1=e8m0(I // 128, H // 128),
-                  w3=fp8(I, H), s3=e8m0(I // 128, H // 128),
-                  w2=fp8(H, I), s2=e8m0(H // 128, I // 128))
+    shared = dict(fp8=True, w1=fp8(I, H), s1=e8m0(I // 128, H // 128, gen=g),
+                  w3=fp8(I, H), s3=e8m0(I // 128, H // 128, gen=g),
+                  w2=fp8(H, I), s2=e8m0(H // 128, I // 128, gen=g))
     n = hi - lo
-    g = ge  # routed experts from this rank's own stream
+    shapes = dict(w1=(I, H // 2), s1=(I, H // 32), w3=(I, H // 2), s3=(I, H // 32),
+                  w2=(H, I // 2), s2=(H, I // 32))
+    routed = {k: torch.empty((n, *sh), dtype=torch.uint8, device=dev) for k, sh in shapes.items()}
+    for b in range(lo // blk, hi // blk):
+        gb = torch.Generator(device=dev)
+        gb.manual_seed(seed * 1000 + b + 1)
+        r0 = b * blk - lo
+        for k, sh in shapes.items():
+            draw = u8 if k[0] == "w" else e8m0
+            routed[k][r0:r0 + blk].copy_(draw(blk, *sh, gen=gb))
     return dict(hidden=H, moe_inter=I, n_experts=E, topk=TOPK, route_scale=ROUTE_SCALE,
-                swiglu_limit=LIMIT, gate_w=gate, bias=None, tid2eid=None,
-                w1=u8(n, I, H // 2), s1=e8m0(n, I, H // 32),
-                w3=u8(n, I, H // 2), s3=e8m0(n, I, H // 32),
-                w2=u8(n, H, I // 2), s2=e8m0(n, H, I // 32), shared=shared)
+                swiglu_limit=LIMIT, gate_w=gate, bias=None, tid2eid=None, shared=shared,
+                **routed)
 
 
 def bf16_tokens(rng, n, m):
@@ -216,11 +238,21 @@ def host_layer_for_reference(rng):
         (scales, weights)
 
 
-def cpu_reference_run(seconds, steps_cap=None, warmup=1):
-    """Times the reference's own MoE-layer step on the host cores. Returns
-    (tok/s, cores, kind, sample description)."""
+def host_threads():
+    try:
+        return len(os.sched_getaffinity(0))
+    except (AttributeError, OSError):
+        return os.cpu_count() or 1
+
+
+def cpu_reference_run(seconds, steps_cap=None, warmup=1, threads=None):
+    """Times the reference's own MoE-layer step on the host cores with
+    `threads` OpenMP threads (default: every core this process may use; set
+    explicitly because launchers such as torchrun pre-set OMP_NUM_THREADS=1).
+    Returns (tok/s, cores, kind, sample description)."""
     from oracle import REF_SO
     ncpu = os.cpu_count() or 1
+    threads = threads or host_threads()
     rng = np.random.default_rng(99)
     layer, slots = host_layer_for_reference(rng)
     toks = bf16_tokens(rng, 64, 1)[:, 0]
@@ -228,7 +260,7 @@ def cpu_reference_run(seconds, steps_cap=None, warmup=1):
         from oracle import Ref
         r = Ref()
         kind = "reference"
-        cores = r.lib.ref_omp_max_threads()
+        cores = r.lib.ref_omp_set_threads(threads)
         run = lambda x: r.moe_forward(layer, x, slots=slots)  # noqa: E731
     else:
         from oracle import Oracle
@@ -259,11 +291,27 @@ def cpu_reference_run(seconds, steps_cap=None, warmup=1):
         f"256 experts resident in host RAM, {el:.1f} s on {cores} thread(s) of {ncpu} cores"
 
 
+def moe_config(args, world):
+    """The `config` of the MoE line, the same in both arms."""
+    M = args.tokens
+    ep = world > 1
+    tok_mode = ep and args.ep_mode == "tokens"
+    return {"workload": "config 2 MoE layer op, decode M=%d" % M, "hidden": H,
+            "moe_inter": args.inter, "experts": args.experts, "topk": TOPK, "shared": "fp8",
+            "tokens_per_step": M * world if tok_mode else M, "tokens_per_gpu": M,
+            "layers_cycled": args.layers,
+            "graph": "one CUDA graph replay chains the %d layers (a step = one "
+                     "layer pass of one token)" % args.layers,
+            "l2": "inputs larger than L2: each step reads a different layer's "
+                  "~235 MB of weights", "parallelism": f"ep{world}",
+            "ep_mode": (args.ep_mode if ep else None),
+            "ep_exchange": (("p2p" if (tok_mode or args.ep_exchange == "p2p") else "nccl")
+                            if ep else None)}
+
+
 def run_reference_arm(args, rank, world):
     if rank != 0:
         return
-    ncpu = os.cpu_count() or 1
-    os.environ.setdefault("OMP_NUM_THREADS", str(ncpu))
     per_step_cap = max(args.steps, 1)
     # warm-up, then K timed steps, each step one decode token (bounded run)
     tps, cores, kind, sample = cpu_reference_run(seconds=max(args.cpu_seconds * 5, 60.0),
@@ -274,9 +322,7 @@ def run_reference_arm(args, rank, world):
         "ms_per_step": 1e3 / tps, "higher_is_better": True,
         "scaling": "strong" if args.ep_mode == "replicated" else "weak",
         "vs_baseline": None, "dtype": "fp4e2m1*e4m3->f32", "data": "synthetic",
-        "config": {"workload": "config 2 MoE layer op, decode M=1", "hidden": H,
-                   "moe_inter": I, "experts": E, "topk": TOPK, "shared": "fp8",
-                   "tokens_per_step": 1},
+        "config": moe_config(args, world),
         "cpu_baseline": {"value": tps, "unit": "tok/s", "cores": cores, "kind": kind,
                          "sample": sample},
         "e2e": {"value": tps, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -316,8 +362,9 @@ def main():
     M_all = M * world if tok_mode else M  # tokens each rank's layer routes per step
     erange = (rank * args.experts // world, (rank + 1) * args.experts // world) if ep else None
     layers = []
+    block = expert_blocks(args.experts, world)
     for li in range(args.layers):
-        lay = make_device_layer(torch, 1000 + li, dev, args.experts, args.inter, erange)
+        lay = make_device_layer(torch, 1000 + li, dev, args.experts, args.inter, erange, block)
         layers.append((lay, dsv4cuda.MoeLayer(lay, max_tokens=M_all, device=True,
                                               expert_range=erange)))
     torch.cuda.synchronize()
@@ -388,52 +435,72 @@ def main():
     # 1..len(layers) layers let a run cover exactly the requested steps.
     n_lay = len(layers)
     xch = torch.empty((n_lay, M, H), dtype=torch.float32, device=dev)
+    och = torch.empty((n_lay, M, H), dtype=torch.float32, device=dev)
     chains = []
     for n in range(1, n_lay + 1):
         g = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g, stream=stream):
             cs = torch.cuda.current_stream().cuda_stream
             for li in range(n):
-                layer_forward(layers[li][1], xch[li], out_dev, cs)
+                layer_forward(layers[li][1], xch[li], och[li], cs)
         chains.append(g)
     replays = [0]
 
-    def run_steps(count):
+    def run_steps(count, host=None):
         """`count` steps: new token rows for each chained layer, one replay
-        per chain."""
+        per chain. host=(pinned inputs, pinned outputs): the rows come from
+        and the outputs go back to host memory, synchronised per replay."""
         for n in chain_lengths(count, n_lay):
             s0 = (replays[0] * n_lay) % pool
-            xch[:n].copy_(x_dev[s0:s0 + n], non_blocking=True)
+            if host is None:
+                xch[:n].copy_(x_dev[s0:s0 + n], non_blocking=True)
+            else:
+                xch[:n].copy_(host[0][s0:s0 + n], non_blocking=True)
             chains[n - 1].replay()
+            if host is not None:
+                host[1][:n].copy_(och[:n], non_blocking=True)
+                stream.synchronize()
             replays[0] += 1
 
     with torch.cuda.stream(stream):
         run_steps(args.warmup)
     torch.cuda.synchronize()
 
+    def timed_window():
+        """K steps between two events on the forward stream, max over ranks.
+        Under expert parallelism one untimed step runs first: its peer-memory
+        waits line the ranks up, so the window holds no start skew."""
+        if dist:
+            dist.barrier()
+        torch.cuda.synchronize()
+        ev0 = torch.cuda.Event(enable_timing=True)
+        ev1 = torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
+            if ep:
+                run_steps(1)
+            ev0.record(stream)
+            run_steps(args.steps)
+            ev1.record(stream)
+        torch.cuda.synchronize()
+        if dist:
+            dist.barrier()
+        t = ev0.elapsed_time(ev1)
+        if dist:
+            tt = torch.tensor([t], device=dev)
+            dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+            t = float(tt.item())
+        return t
+
     clocks = ClockSampler(local)
     clocks.start()
     time.sleep(0.3)
-    if dist:
-        dist.barrier()
-    torch.cuda.synchronize()
-    ev0 = torch.cuda.Event(enable_timing=True)
-    ev1 = torch.cuda.Event(enable_timing=True)
-    with torch.cuda.stream(stream):
-        ev0.record(stream)
-        run_steps(args.steps)
-        ev1.record(stream)
-    torch.cuda.synchronize()
-    if dist:
-        dist.barrier()
-    ms = ev0.elapsed_time(ev1)
+    windows = [timed_window() for _ in range(5)]
     clk = clocks.stop()
-    if dist:
-        t = torch.tensor([ms], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
+    ms = windows[0]
     ms_per_step = ms / args.steps
-    value = M * world * args.steps / (ms / 1e3) if tok_mode else M * args.steps / (ms / 1e3)
+    tok_per_step = M * world if tok_mode else M
+    value = tok_per_step * args.steps / (ms / 1e3)
+    win_vals = [tok_per_step * args.steps / (w / 1e3) for w in windows]
 
     # ---- expert-GEMV roofline: each layer's forward captured once more into
     # a graph whose event nodes bracket the routed gate/up and down launches
@@ -503,10 +570,44 @@ def main():
     e2e_val = None
     if not args.no_e2e:
         if ep:
-            e2e_val = run_e2e_graphs(torch, dist, args, graphs, xin, out_dev, x_host, M, pool,
-                                     stream, dev) * (world if tok_mode else 1)
+            pin_x = torch.from_numpy(x_host).pin_memory()
+            pin_out = torch.empty((n_lay, M, H), dtype=torch.float32).pin_memory()
+            e2e_steps = max(20, args.steps // 2)
+            with torch.cuda.stream(stream):
+                run_steps(n_lay, host=(pin_x, pin_out))  # untimed: aligns the ranks
+            dist.barrier()
+            t0 = time.perf_counter()
+            with torch.cuda.stream(stream):
+                run_steps(e2e_steps, host=(pin_x, pin_out))
+            el = torch.tensor([time.perf_counter() - t0], device=dev)
+            dist.all_reduce(el, op=dist.ReduceOp.MAX)
+            e2e_val = tok_per_step * e2e_steps / float(el.item())
         else:
             e2e_val = run_e2e(args, layers, x_host, M, pool, lib, dsv4cuda)
+
+    # ---- expert parallelism: this rank's outputs of one step against the
+    # full layer (every expert, same weights) run on this GPU alone
+    ep_check = None
+    if ep:
+        full = make_device_layer(torch, 1000, dev, args.experts, args.inter, None, block)
+        Lfull = dsv4cuda.MoeLayer(full, max_tokens=M_all, device=True)
+        xin.copy_(x_dev[0])
+        got = torch.empty((M, H), dtype=torch.float32, device=dev)
+        want = torch.empty((M, H), dtype=torch.float32, device=dev)
+        with torch.cuda.stream(stream):
+            layer_forward(layers[0][1], xin, got, stream.cuda_stream)
+            Lfull.forward(xin, want, stream=stream.cuda_stream)
+        torch.cuda.synchronize()
+        same = torch.tensor([1 if torch.equal(got.view(torch.int32), want.view(torch.int32))
+                             else 0], device=dev)
+        dist.all_reduce(same, op=dist.ReduceOp.MIN)
+        ep_check = {"bit_identical_to_1gpu": bool(same.item()),
+                    "tokens_checked": M * world if tok_mode else M,
+                    "how": "one step of layer 0 on every rank vs the same layer with all "
+                           "experts on one GPU, output bits compared, min over ranks"}
+        Lfull.close()
+        del full, Lfull
+        torch.cuda.empty_cache()
 
     # ---- config 3 attention sweep (replicated part of the decode layer)
     attn = None
@@ -515,12 +616,16 @@ def main():
 
     line = None
     if rank == 0:
-        cpu = None
+        cpu = cpu1 = None
         if world == 1 and not args.no_cpu:
             try:
                 tps, cores, kind, sample = cpu_reference_run(args.cpu_seconds)
                 cpu = {"value": tps, "unit": "tok/s", "cores": cores, "kind": kind,
                        "sample": sample}
+                tps, cores, kind, sample = cpu_reference_run(min(args.cpu_seconds, 8.0),
+                                                             threads=1)
+                cpu1 = {"value": tps, "unit": "tok/s", "cores": cores, "kind": kind,
+                        "sample": sample}
             except Exception as exc:  # report, do not hide
                 cpu = {"value": None, "unit": "tok/s", "cores": 0, "kind": "reference",
                        "sample": f"failed: {exc}"}
@@ -530,16 +635,7 @@ def main():
             "higher_is_better": True,
             "scaling": "strong" if (ep and not tok_mode) else "weak", "vs_baseline": None,
             "dtype": "fp4e2m1*e4m3->f32", "data": "synthetic",
-            "config": {"workload": "config 2 MoE layer op, decode M=%d" % M, "hidden": H,
-                       "moe_inter": I, "experts": args.experts, "topk": TOPK, "shared": "fp8",
-                       "tokens_per_step": M_all if tok_mode else M, "tokens_per_gpu": M,
-                       "layers_cycled": args.layers,
-                       "graph": "one CUDA graph replay chains the %d layers (a step = one "
-                                "layer pass of one token)" % args.layers,
-                       "l2": "inputs larger than L2: each step reads a different layer's "
-                             "~235 MB of weights", "parallelism": f"ep{world}",
-                       "ep_mode": (args.ep_mode if ep else None),
-                       "ep_exchange": (("p2p" if p2p else "nccl") if ep else None)},
+            "config": moe_config(args, world),
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "traffic": FP4_TRAFFIC_PER_STEP,
                          "traffic_source": "ncu dram__bytes_read+write of the gate/up and down "
@@ -554,6 +650,12 @@ def main():
                              "expert_gateup": gu_ms / max(n_timed, 1),
                              "expert_down": dn_ms / max(n_timed, 1)}},
             "cpu_baseline": cpu,
+            "cpu_baseline_1thread": cpu1,
+            "repeat_windows": {"n": len(win_vals), "steps_each": args.steps,
+                               "values": win_vals, "min": min(win_vals), "max": max(win_vals),
+                               "spread_pct": 100.0 * (max(win_vals) - min(win_vals)) /
+                               max(win_vals)},
+            "ep_check": ep_check,
             "e2e": {"value": e2e_val, "unit": "tok/s", "h2d_bytes_per_step": M * H * 4,
                     "d2h_bytes_per_step": M * H * 4},
             "gpu_launches": launches_per_step * args.steps,
@@ -582,26 +684,6 @@ def main():
     if dist:
         dist.barrier()
         dist.destroy_process_group()
-
-
-def run_e2e_graphs(torch, dist, args, graphs, xin, out_dev, x_host, M, pool, stream, dev):
-    """Expert-parallel end to end: every step copies the token from pinned
-    host memory, replays the layer's graph (C API calls + NCCL) and reads
-    the output back; wall time, max over ranks."""
-    pin_x = torch.from_numpy(x_host).pin_memory()
-    pin_out = torch.empty((M, H), dtype=torch.float32).pin_memory()
-    steps = max(20, args.steps // 2)
-    dist.barrier()
-    t0 = time.perf_counter()
-    with torch.cuda.stream(stream):
-        for i in range(steps):
-            xin.copy_(pin_x[i % pool], non_blocking=True)
-            graphs[i % len(graphs)].replay()
-            pin_out.copy_(out_dev, non_blocking=True)
-            stream.synchronize()
-    el = torch.tensor([time.perf_counter() - t0], device=dev)
-    dist.all_reduce(el, op=dist.ReduceOp.MAX)
-    return M * steps / float(el.item())
 
 
 def run_e2e(args, layers, x_host, M, pool, lib, dsv4cuda):

@@ -547,6 +547,54 @@ DSV4_API void dsv4_quant_fp8_act(float* out, float* scales, const float* x, int 
   quant_codes(out, scales, x, n);
 }
 
+// routed_swiglu_quant (src/dsv4/dsv4_model.c:6239, file-static in the
+// reference): host pointers staged through the thread's device buffers.
+DSV4_API void dsv4cuda_routed_swiglu_quant(float* y, float* qy, float* qscale, const float* gate,
+                                           const float* up, int n, int limit,
+                                           float route_weight) {
+  if (n <= 0) return;
+  if (ensure_thread_state() != 0) { fatal_or_record("init", cudaErrorInitializationError); return; }
+  cudaStream_t st = t_state.stream;
+  const int nb = (n + 127) / 128;
+  const size_t need = al(sizeof(float) * n) * 3 + al(sizeof(__half) * n) +
+                      al(sizeof(float) * nb) + al(sizeof(float)) + 1024;
+  char* base = staging(need);
+  if (!base) { fatal_or_record("staging cudaMalloc", cudaErrorMemoryAllocation); return; }
+  Carver cv{base};
+  float* dg = cv.take<float>(n);
+  float* du = cv.take<float>(n);
+  float* dy = cv.take<float>(n);
+  __half* dq = cv.take<__half>(n);
+  float* ds = cv.take<float>(nb);
+  float* dw = cv.take<float>(1);
+  STAGE_CHECK(cudaMemcpyAsync(dg, gate, sizeof(float) * n, cudaMemcpyHostToDevice, st), "copy gate");
+  STAGE_CHECK(cudaMemcpyAsync(du, up, sizeof(float) * n, cudaMemcpyHostToDevice, st), "copy up");
+  STAGE_CHECK(cudaMemcpyAsync(dw, &route_weight, sizeof(float), cudaMemcpyHostToDevice, st),
+              "copy weight");
+  STAGE_CHECK(dsv4::launch_swiglu_quant(dg, du, n, 1, dw, limit, dq, ds, dy, st), "swiglu");
+  std::vector<__half> hq(static_cast<size_t>(n));
+  STAGE_CHECK(cudaMemcpyAsync(y, dy, sizeof(float) * n, cudaMemcpyDeviceToHost, st), "copy y");
+  STAGE_CHECK(cudaMemcpyAsync(hq.data(), dq, sizeof(__half) * n, cudaMemcpyDeviceToHost, st),
+              "copy qy");
+  STAGE_CHECK(cudaMemcpyAsync(qscale, ds, sizeof(float) * nb, cudaMemcpyDeviceToHost, st),
+              "copy qscale");
+  STAGE_CHECK(cudaStreamSynchronize(st), "sync");
+  for (int i = 0; i < n; ++i) qy[i] = __half2float(hq[static_cast<size_t>(i)]);
+}
+
+DSV4_API int dsv4cuda_router_scores(const float* z, float* scores, int n, void* stream) {
+  if (n < 0 || (n > 0 && (!z || !scores))) {
+    record_error("dsv4cuda_router_scores: bad arguments");
+    return -1;
+  }
+  const cudaError_t e = dsv4::router_scores(z, scores, n, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) {
+    record_error("dsv4cuda_router_scores: %s", cudaGetErrorString(e));
+    return -1;
+  }
+  return 0;
+}
+
 // Public dsv4_router (src/dsv4/dsv4_ops.c:473): stages the BF16 gate, runs
 // the device router with the public numerics (separate multiply and add,
 // 1/sum weights) for one token.

@@ -882,7 +882,7 @@ __global__ void swiglu_quant_kernel(const float* gate, const float* up, int n, i
       if (u > L) u = L;
       else if (u < -L) u = -L;
       if (g > L) g = L;
-      const float silu = g / (1.0f + expf(-g));
+      const float silu = g / (1.0f + expf_r1(-g));
       v[k] = bf16_round(silu * u * w);
       amax = fmaxf(amax, fabsf(v[k]));
     }

@@ -5,18 +5,19 @@
 // Router (src/dsv4/dsv4_model.c:6615-6676). The reference's logit z is one
 // sequential fp32 fmaf chain over the hidden dimension; replaying that chain
 // costs hidden x 4 cycles of latency (~15 us at 7168), so the router instead
-//   1. computes the exact dot product in fp64 (bf16 x fp32 products are exact
-//      in fp64) together with a rigorous bound on how far the reference's
-//      fp32 chain can drift from it: |z_ref - z| <= u * sum_i |s_i| (u=2^-24,
-//      s_i the prefix sums; a warp scan supplies them);
+//   1. computes the dot product in fp32 with a warp prefix scan, together
+//      with a rigorous bound on how far the reference's sequential fp32
+//      chain can be from it: the chain's own roundings, u * sum_i |s_i|
+//      (u = 2^-24, s_i its prefix sums), plus the scan's rounding error;
 //   2. selects the top-k with the reference's rule (score + bias, strict >,
 //      lower id wins ties) and checks that every selected expert's lower
 //      bound clears every unselected expert's upper bound;
 //   3. when the check fails (a near tie), replays the reference's fp32 chain
 //      exactly for the experts inside the ambiguous band and selects again.
-// The selected SET therefore equals the reference's; combine weights come
-// from sqrt(softplus) of the rounded logit and agree to ~1e-6 relative
-// (transcendentals differ from glibc in the last ulp).
+// The selected SET therefore equals the reference's unless two candidates'
+// scores sit within the last-ulp difference between this device's
+// sqrt(softplus) and the host libm's; combine weights come from the same
+// scores in the reference's order and agree to ~1e-6 relative.
 #include <algorithm>
 #include <mutex>
 
@@ -31,10 +32,17 @@ namespace {
 constexpr double kU = 5.9604644775390625e-08;  // 2^-24, fp32 unit roundoff
 
 // sqrt(softplus(z)) in the reference's fp32 operation order
-// (src/dsv4/dsv4_model.c:5827).
+// (src/dsv4/dsv4_model.c:5827), each transcendental rounded once from
+// double precision (dsv4_common.cuh states how close that is to the host's
+// libm).
 __device__ __forceinline__ float sqrt_softplus_f(float z) {
   if (z > 20.0f) return sqrtf(z);
-  return sqrtf(log1pf(expf(z)));
+  return sqrtf(log1pf_r1(expf_r1(z)));
+}
+
+__global__ void router_scores_kernel(const float* z, float* s, int n) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) s[i] = sqrt_softplus_f(z[i]);
 }
 
 // ------------------------------------------------------------- router ----
@@ -1177,6 +1185,12 @@ cudaError_t moe_forward_local(const MoeConfig& c, const MoeWeights& w, const Moe
   if (ws.timing) record_timing(ws.timing[3], st);
 
   if (side) cudaStreamWaitEvent(st, side->join, 0);
+  return cudaGetLastError();
+}
+
+cudaError_t router_scores(const float* z, float* s, int n, cudaStream_t st) {
+  if (n <= 0) return cudaSuccess;
+  router_scores_kernel<<<(n + 255) / 256, 256, 0, st>>>(z, s, n);
   return cudaGetLastError();
 }
 

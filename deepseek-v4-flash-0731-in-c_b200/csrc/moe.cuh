@@ -109,6 +109,10 @@ cudaError_t moe_forward_local(const MoeConfig& c, const MoeWeights& w, const Moe
 cudaError_t moe_combine(const MoeConfig& c, const MoeWorkspace& ws, int n_tokens, float* out,
                         bool has_shared, cudaStream_t st);
 
+// The router's score function sqrt(softplus(z)) as the selection evaluates
+// it, elementwise over n device floats.
+cudaError_t router_scores(const float* z, float* s, int n, cudaStream_t st);
+
 // Router only: idx/wt [n][topk] (ids ascending), same numerics as above.
 cudaError_t moe_route(const MoeConfig& c, const MoeWeights& w, const MoeWorkspace& ws,
                       const float* x, const int* token_ids, int n_tokens, int public_router,

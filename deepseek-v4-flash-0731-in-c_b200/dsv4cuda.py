@@ -54,6 +54,10 @@ lib.dsv4cuda_moe_last_routes.argtypes = [vp, C.c_int, i32p, f32p]
 lib.dsv4cuda_moe_route.restype = C.c_int
 lib.dsv4cuda_moe_route.argtypes = [vp, vp, vp, C.c_int, C.c_int, i32p, f32p]
 lib.dsv4cuda_moe_destroy.argtypes = [vp]
+lib.dsv4cuda_router_scores.restype = C.c_int
+lib.dsv4cuda_router_scores.argtypes = [vp, vp, C.c_int, vp]
+lib.dsv4cuda_routed_swiglu_quant.restype = None
+lib.dsv4cuda_routed_swiglu_quant.argtypes = [vp, vp, vp, vp, vp, C.c_int, C.c_int, C.c_float]
 lib.dsv4cuda_moe_forward_noalloc.restype = C.c_int
 lib.dsv4cuda_moe_forward_noalloc.argtypes = [vp, vp, vp, vp, C.c_int, vp, vp]
 lib.dsv4cuda_moe_device_bytes.restype = C.c_size_t
@@ -219,6 +223,23 @@ def gemv_fp4_pair_q(qx, qs, W0, S0, W1, S1, inn):
     lib.dsv4_gemv_fp4_pair_q(_p(y0, f32p), _p(y1, f32p), _p(_f32(qx), f32p), _p(_f32(qs), f32p),
                              _p(W0, u8p), _p(S0, u8p), _p(W1, u8p), _p(S1, u8p), inn, rows)
     return y0, y1
+
+
+def routed_swiglu_quant(gate, up, limit, weight):
+    """routed_swiglu_quant on the device (host arrays): (y, qy, qscale)."""
+    g, u = _f32(gate), _f32(up)
+    n = g.size
+    y = np.empty(n, np.float32)
+    qy = np.empty(n, np.float32)
+    qs = np.empty((n + 127) // 128, np.float32)
+    lib.dsv4cuda_routed_swiglu_quant(y.ctypes.data, qy.ctypes.data, qs.ctypes.data, g.ctypes.data,
+                                     u.ctypes.data, n, int(limit), float(weight))
+    return y, qy, qs
+
+
+def router_scores(z, out, stream=None):
+    """Device sqrt(softplus) of the router, z/out torch CUDA float32."""
+    _check(lib.dsv4cuda_router_scores(z.data_ptr(), out.data_ptr(), z.numel(), _stream(stream)))
 
 
 def router_public(x, gate, bias, topk, route_scale, tid2eid=None, token_id=0):

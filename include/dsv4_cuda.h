@@ -82,6 +82,12 @@ void dsv4_router(int *idx, float *wt, const float *x, const float *gate,
                  int hidden, int n_experts, int topk, int hash_layer,
                  float route_scale, float rms_eps);
 
+/* routed_swiglu_quant (src/dsv4/dsv4_model.c:6239, file-static there):
+ * clamp, SiLU, x route_weight, BF16 into y, then per-128 FP8 quant into qy
+ * (E4M3-grid floats) and qscale. Host pointers, like the drop-ins above. */
+void dsv4cuda_routed_swiglu_quant(float *y, float *qy, float *qscale, const float *gate,
+                                  const float *up, int n, int limit, float route_weight);
+
 /* Prefixed aliases of the nine model-path kernels above. */
 void dsv4cuda_gemv_bf16(float *y, const float *x, const uint16_t *W, int in,
                         int out, int round_out);
@@ -195,6 +201,10 @@ int dsv4cuda_moe_forward_host(dsv4cuda_moe_layer *L, const float *x,
  * created) whose top-k needed the exact fp32 logit replay of a near tie,
  * or a negative error. */
 int dsv4cuda_moe_last_routes(dsv4cuda_moe_layer *L, int n_tokens, int *idx, float *wt);
+/* The router's score sqrt(softplus(z)) (src/dsv4/dsv4_model.c:5827) exactly
+ * as the device selection evaluates it: scores[i] for z[i], DEVICE pointers,
+ * async on stream. For checking the device score against the host libm's. */
+int dsv4cuda_router_scores(const float *z, float *scores, int n, void *stream);
 /* Router alone (device x), writing host idx/wt. public_router selects the
  * public dsv4_router() numerics instead of moe_forward's. */
 int dsv4cuda_moe_route(dsv4cuda_moe_layer *L, const float *x, const int *token_ids,

@@ -333,6 +333,8 @@ class Ref(_Lib):
         L.ref_sqrt_softplus.restype = C.c_float
         L.ref_sqrt_softplus.argtypes = [C.c_float]
         L.ref_omp_max_threads.restype = C.c_int
+        L.ref_omp_set_threads.restype = C.c_int
+        L.ref_omp_set_threads.argtypes = [C.c_int]
 
     def f32_to_bf16(self, f):
         return self.lib.dsv4_f32_to_bf16(f)
@@ -348,6 +350,12 @@ class Ref(_Lib):
 
     def sqrt_softplus(self, z):
         return self.lib.ref_sqrt_softplus(z)
+
+    def sqrt_softplus_many(self, z):
+        z = _f32(z)
+        s = np.empty_like(z)
+        self.lib.ref_sqrt_softplus_many(_p(z, f32p), _p(s, f32p), z.size)
+        return s
 
     def act_quant_inplace(self, x, group, mode):
         x = _f32(x).copy()

@@ -48,6 +48,11 @@ REF_API void ref_routed_swiglu_quant(float *y, float *qy, float *qscale,
 
 REF_API float ref_sqrt_softplus(float z) { return sqrt_softplus(z); }
 
+REF_API void ref_sqrt_softplus_many(const float *z, float *s, int n)
+{
+    for (int i = 0; i < n; i++) s[i] = sqrt_softplus(z[i]);
+}
+
 /* Expert slot layout used by the reference's cache (dsv4_internal.h:13-16,
  * :33-37): scale run [w1][w2][w3], weight run [w1][w2][w3]. */
 REF_API void ref_expert_slot_pack(uint8_t *scales, uint8_t *weights,
@@ -198,6 +203,19 @@ REF_API int ref_omp_max_threads(void)
 #ifdef _OPENMP
     return omp_get_max_threads();
 #else
+    return 1;
+#endif
+}
+
+/* Threads of the next OpenMP teams (launchers such as torchrun pre-set
+ * OMP_NUM_THREADS=1 in the environment); returns the new maximum. */
+REF_API int ref_omp_set_threads(int n)
+{
+#ifdef _OPENMP
+    if (n > 0) omp_set_num_threads(n);
+    return omp_get_max_threads();
+#else
+    (void)n;
     return 1;
 #endif
 }
