@@ -33,6 +33,29 @@ namespace {
 std::atomic<int> g_abort{1};
 thread_local std::string t_last_error;
 
+// Drop-in calls served, per kernel family (the order of
+// dsv4cuda_dropin_calls): FP4 GEMVs, FP8 GEMVs, BF16 GEMVs, activation
+// quant, router, SwiGLU quant.
+constexpr int kDropinKinds = 6;
+std::atomic<unsigned long long> g_dropin_calls[kDropinKinds];
+
+void dropin_report() {
+  fprintf(stderr, "dsv4_cuda drop-in calls: fp4=%llu fp8=%llu bf16=%llu quant=%llu router=%llu "
+                  "swiglu=%llu\n",
+          g_dropin_calls[0].load(), g_dropin_calls[1].load(), g_dropin_calls[2].load(),
+          g_dropin_calls[3].load(), g_dropin_calls[4].load(), g_dropin_calls[5].load());
+}
+
+// DSV4CUDA_DROPIN_REPORT=1 in the environment: print the counts at exit, so
+// a host program that preloads the library can show which of its kernel
+// calls the GPU served.
+struct DropinReportAtExit {
+  DropinReportAtExit() {
+    const char* v = getenv("DSV4CUDA_DROPIN_REPORT");
+    if (v && v[0] && v[0] != '0') atexit(dropin_report);
+  }
+} g_dropin_report_at_exit;
+
 struct ThreadState {
   int device = -1;
   cudaStream_t stream = nullptr;
@@ -150,6 +173,7 @@ struct StagedAct {
 void fp4_or_fp8_gemv(bool fp4, float* const* y0, float* const* y1, const float* const* qx,
                      const float* const* qscale, int batch, const uint8_t* W0, const uint8_t* S0,
                      const uint8_t* W1, const uint8_t* S1, int in, int rows, int round_out) {
+  g_dropin_calls[fp4 ? 0 : 1].fetch_add(1, std::memory_order_relaxed);
   if (batch <= 0 || rows <= 0) return;
   if (ensure_thread_state() != 0) { fatal_or_record("init", cudaErrorInitializationError); return; }
   cudaStream_t st = t_state.stream;
@@ -232,6 +256,7 @@ void fp4_or_fp8_gemv(bool fp4, float* const* y0, float* const* y1, const float* 
 
 void bf16_gemv(float* const* y, const float* const* x, int batch, const uint16_t* W, int in,
                int out, int round_out) {
+  g_dropin_calls[2].fetch_add(1, std::memory_order_relaxed);
   if (batch <= 0 || out <= 0) return;
   if (ensure_thread_state() != 0) { fatal_or_record("init", cudaErrorInitializationError); return; }
   cudaStream_t st = t_state.stream;
@@ -270,6 +295,7 @@ void bf16_gemv(float* const* y, const float* const* x, int batch, const uint16_t
 }
 
 void quant_codes(float* qx, float* qscale, const float* x, int n) {
+  g_dropin_calls[3].fetch_add(1, std::memory_order_relaxed);
   if (n <= 0) return;
   if (ensure_thread_state() != 0) { fatal_or_record("init", cudaErrorInitializationError); return; }
   cudaStream_t st = t_state.stream;
@@ -431,6 +457,12 @@ DSV4_API int dsv4cuda_device_error(unsigned int* flags, int clear) {
   return 0;
 }
 
+DSV4_API int dsv4cuda_dropin_calls(unsigned long long* counts, int n) {
+  const int k = n < kDropinKinds ? n : kDropinKinds;
+  for (int i = 0; i < k; ++i) counts[i] = g_dropin_calls[i].load();
+  return kDropinKinds;
+}
+
 DSV4_API int dsv4cuda_set_abort_on_error(int abort_on_error) {
   return g_abort.exchange(abort_on_error ? 1 : 0);
 }
@@ -552,6 +584,7 @@ DSV4_API void dsv4_quant_fp8_act(float* out, float* scales, const float* x, int 
 DSV4_API void dsv4cuda_routed_swiglu_quant(float* y, float* qy, float* qscale, const float* gate,
                                            const float* up, int n, int limit,
                                            float route_weight) {
+  g_dropin_calls[5].fetch_add(1, std::memory_order_relaxed);
   if (n <= 0) return;
   if (ensure_thread_state() != 0) { fatal_or_record("init", cudaErrorInitializationError); return; }
   cudaStream_t st = t_state.stream;
@@ -602,6 +635,7 @@ DSV4_API void dsv4_router(int* idx, float* wt, const float* x, const float* gate
                           const float* bias, const int64_t* tid2eid, int token_id, int hidden,
                           int n_experts, int topk, int hash_layer, float route_scale,
                           float rms_eps) {
+  g_dropin_calls[4].fetch_add(1, std::memory_order_relaxed);
   (void)rms_eps;
   if (topk <= 0) return;
   if (ensure_thread_state() != 0) { fatal_or_record("init", cudaErrorInitializationError); return; }

@@ -133,6 +133,13 @@ const char *dsv4cuda_last_error(void);
  * invalid), bit 2 = an attention key index >= kv_rows was skipped.
  * clear != 0 resets them. */
 int dsv4cuda_device_error(unsigned int *flags, int clear);
+/* Drop-in calls served since the library loaded, per kernel family:
+ * counts[0] FP4 GEMVs, [1] FP8 GEMVs, [2] BF16 GEMVs, [3] activation quant,
+ * [4] router, [5] SwiGLU quant (the first n of them). Returns the number of
+ * families. With DSV4CUDA_DROPIN_REPORT=1 in the environment the library
+ * prints the counts to stderr at exit, so a host program that preloads it
+ * can show which of its kernel calls ran on the GPU. */
+int dsv4cuda_dropin_calls(unsigned long long *counts, int n);
 /* 1 (default): a drop-in call that hits a CUDA error exits(1) like the
  * reference's fatal paths; 0: record the error and return. Returns the
  * previous mode. */
