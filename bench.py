@@ -72,9 +72,14 @@ def parse():
                     help="expert intermediate size (smaller only for profiling captures)")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end leg")
-    ap.add_argument("--workload", default="moe", choices=["moe", "attn"],
+    ap.add_argument("--workload", default="moe", choices=["moe", "attn", "decode"],
                     help="moe: config 2 MoE layer (default); attn: config 3 latent decode "
-                         "attention at --attn-batch/--attn-ctx")
+                         "attention at --attn-batch/--attn-ctx; decode: config 5 batch-1 "
+                         "greedy decode through every layer on the device")
+    ap.add_argument("--decode-sets", type=int, default=4,
+                    help="decode: distinct random-init layer weight sets the 43 layers cycle "
+                         "through (each ~3.6 GB; L2 never holds a layer between uses)")
+    ap.add_argument("--decode-layers", type=int, default=43)
     ap.add_argument("--attn-batch", type=int, default=32)
     ap.add_argument("--attn-ctx", type=int, default=32768)
     ap.add_argument("--no-attn-sweep", action="store_true",
@@ -341,6 +346,9 @@ def main():
         return
     if args.workload == "attn":
         main_attn(args, rank, world, local)
+        return
+    if args.workload == "decode":
+        main_decode(args, rank, world, local)
         return
 
     import torch
@@ -936,6 +944,236 @@ def main_attn(args, rank, world, local):
             "clocks": clk,
         }
         print(json.dumps(line), flush=True)
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+# ------------------------------------------ config 5: whole-model decode ----
+C5 = dict(hidden=4096, vocab=129280, n_heads=64, head_dim=512, rope_dim=64, q_lora=1024,
+          o_groups=8, o_lora=1024, window=128, hc_mult=4, hc_iters=20, rms_eps=1e-6,
+          hc_eps=1e-6, rope_theta=10000.0, experts=256, topk=6, inter=2048)
+DECODE_METRIC = ("decode tok/s, batch 1, speculation off (config 5: DSV4-Flash shapes, "
+                 "43 layers, 256+1 experts top-6, FP4 experts / FP8 attention)")
+
+
+def decode_bytes_per_token(c, n_layers):
+    """Algorithmic HBM bytes one greedy token reads: every layer's dense
+    weights (FP8 projections with their [128x128] scales, BF16 wo_a, the HC
+    mixes, the BF16 router), the shared expert, topk routed FP4 experts
+    (codes + per-32 scales), the latent ring, then the HC head and the BF16
+    vocab head."""
+    H, I, hd, nh = c["hidden"], c["inter"], c["head_dim"], c["n_heads"]
+    fp8 = lambda r, k: r * k + ((r + 127) // 128) * ((k + 127) // 128)  # noqa: E731
+    mult = c["hc_mult"]
+    dense = (fp8(c["q_lora"], H) + fp8(nh * hd, c["q_lora"]) + fp8(hd, H) +
+             c["o_groups"] * c["o_lora"] * (nh * hd // c["o_groups"]) * 2 +
+             fp8(H, c["o_groups"] * c["o_lora"]) +
+             2 * (2 + mult) * mult * mult * H * 4 + c["experts"] * H * 2 +
+             3 * fp8(I, H) + c["window"] * 584)
+    expert = 3 * (I * H // 2 + I * H // 32)
+    per_layer = dense + c["topk"] * expert
+    return n_layers * per_layer + c["vocab"] * H * 2 + mult * mult * H * 4 + H * 2
+
+
+def make_decode_set(torch, seed, dev, c):
+    """One random-init layer weight set at config-5 shapes (distributions as
+    config 2: FP4 codes uniform, E8M0 lognormal(0, 0.5) rounded to powers of
+    two, FP8 codes uniform over the finite values, BF16 N(0, 0.02), RMSNorm
+    gains 1 + N(0, 0.02), HC parameters N(0, 0.02) with unit scales)."""
+    g = torch.Generator(device=dev)
+    g.manual_seed(seed)
+    H, I, E, hd, nh = c["hidden"], c["inter"], c["experts"], c["head_dim"], c["n_heads"]
+    mult = c["hc_mult"]
+    mix = (2 + mult) * mult
+
+    def u8(*shape):
+        return torch.randint(0, 256, shape, dtype=torch.uint8, device=dev, generator=g)
+
+    def e8m0(*shape):
+        z = torch.randn(shape, device=dev, generator=g) * (0.5 / np.log(2.0))
+        return (127 + torch.round(z)).clamp(0, 254).to(torch.uint8)
+
+    def fp8(r, k):
+        cd = torch.randint(0, 254, (r, k), dtype=torch.int32, device=dev, generator=g)
+        cd = torch.where((cd & 0x7F) == 0x7F, cd - 1, cd).to(torch.uint8)
+        return cd, e8m0((r + 127) // 128, (k + 127) // 128)
+
+    def bf16(*shape, mean=0.0):
+        return (mean + torch.randn(shape, device=dev, generator=g) * 0.02).to(
+            torch.bfloat16).view(torch.uint16)
+
+    def f32(*shape):
+        return torch.randn(shape, device=dev, generator=g) * 0.02
+
+    wq_a, wq_a_s = fp8(c["q_lora"], H)
+    wq_b, wq_b_s = fp8(nh * hd, c["q_lora"])
+    wkv, wkv_s = fp8(hd, H)
+    wo_b, wo_b_s = fp8(H, c["o_groups"] * c["o_lora"])
+    sh = {}
+    for k, (r, cc) in (("1", (I, H)), ("3", (I, H)), ("2", (H, I))):
+        sh["w" + k], sh["s" + k] = fp8(r, cc)
+    moe = dict(hidden=H, moe_inter=I, n_experts=E, topk=c["topk"], route_scale=1.5,
+               swiglu_limit=10, gate_w=bf16(E, H), bias=f32(E), tid2eid=None,
+               w1=u8(E, I, H // 2), s1=e8m0(E, I, H // 32), w3=u8(E, I, H // 2),
+               s3=e8m0(E, I, H // 32), w2=u8(E, H, I // 2), s2=e8m0(E, H, I // 32),
+               shared=dict(fp8=True, **sh))
+    ones3 = torch.ones(3, device=dev)
+    return dict(attn_norm=bf16(H, mean=1.0), ffn_norm=bf16(H, mean=1.0),
+                hc_attn_fn=f32(mix, mult * H), hc_attn_scale=ones3, hc_attn_base=f32(mix),
+                hc_ffn_fn=f32(mix, mult * H), hc_ffn_scale=ones3.clone(), hc_ffn_base=f32(mix),
+                attn_sink=f32(nh), wq_a=wq_a, wq_a_s=wq_a_s, q_norm=bf16(c["q_lora"], mean=1.0),
+                wq_b=wq_b, wq_b_s=wq_b_s, wkv=wkv, wkv_s=wkv_s, kv_norm=bf16(hd, mean=1.0),
+                wo_a=bf16(c["o_groups"] * c["o_lora"], nh * hd // c["o_groups"]),
+                wo_b=wo_b, wo_b_s=wo_b_s, moe=moe)
+
+
+def main_decode(args, rank, world, local):
+    """--workload decode: config 5 batch-1 greedy decode. Every rank runs the
+    whole model on its own GPU (replicas; the expert-parallel split of the
+    decoder is not built), so N GPUs decode N independent sequences."""
+    import torch
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+    import ctypes as C
+    import dsv4cuda
+    dsv4cuda.set_abort_on_error(False)
+    dsv4cuda.init(local)
+    c = dict(C5)
+    n_layers = args.decode_layers
+    sets = [make_decode_set(torch, 500 + i, dev, c) for i in range(args.decode_sets)]
+    g = torch.Generator(device=dev)
+    g.manual_seed(7)
+    model = dict(embed=(torch.randn(c["vocab"], c["hidden"], device=dev, generator=g) * 0.02)
+                 .to(torch.bfloat16).view(torch.uint16),
+                 head=(torch.randn(c["vocab"], c["hidden"], device=dev, generator=g) * 0.02)
+                 .to(torch.bfloat16).view(torch.uint16),
+                 norm=(1.0 + torch.randn(c["hidden"], device=dev, generator=g) * 0.02)
+                 .to(torch.bfloat16).view(torch.uint16),
+                 hc_head_fn=torch.randn(c["hc_mult"], c["hc_mult"] * c["hidden"], device=dev,
+                                        generator=g) * 0.02,
+                 hc_head_base=torch.randn(c["hc_mult"], device=dev, generator=g) * 0.02,
+                 hc_head_scale=torch.ones(1, device=dev))
+    prompt, gen = 2048, args.steps
+    cfg = dict(hidden=c["hidden"], n_layers=n_layers, vocab=c["vocab"], n_heads=c["n_heads"],
+               head_dim=c["head_dim"], rope_dim=c["rope_dim"], q_lora=c["q_lora"],
+               o_groups=c["o_groups"], o_lora=c["o_lora"], window=c["window"],
+               hc_mult=c["hc_mult"], hc_iters=c["hc_iters"], rms_eps=c["rms_eps"],
+               hc_eps=c["hc_eps"], rope_theta=c["rope_theta"],
+               max_context=prompt + gen + args.warmup + 8,
+               moe=dict(hidden=c["hidden"], moe_inter=c["inter"], n_experts=c["experts"],
+                        topk=c["topk"], swiglu_limit=10, route_scale=1.5,
+                        shared_kind=dsv4cuda.SHARED_FP8, hash_vocab=0))
+    layers = [sets[i % len(sets)] for i in range(n_layers)]
+    dec = dsv4cuda.Decoder(cfg, model, layers)
+    lib = dsv4cuda.lib
+    h = dec.handle
+    _, _, _, am_slot = dec.slots()
+    pos = torch.full((1,), prompt - args.warmup - 1, dtype=torch.int32, device=dev)
+    tok = torch.full((1,), 1, dtype=torch.int32, device=dev)
+    stream = torch.cuda.Stream(device=dev)
+    with torch.cuda.stream(stream):  # one eager step: its argmax seeds the greedy chain
+        dec.step_device(tok, pos, stream.cuda_stream)
+        pos.add_(1)
+    stream.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        cs = torch.cuda.current_stream()
+        if lib.dsv4cuda_decoder_step_device(h, C.c_void_p(am_slot), C.c_void_p(pos.data_ptr()),
+                                            C.c_void_p(cs.cuda_stream)) != 0:
+            raise RuntimeError(lib.dsv4cuda_decoder_last_error().decode())
+        pos.add_(1)
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            graph.replay()
+    torch.cuda.synchronize()
+    clocks = ClockSampler(local)
+    clocks.start()
+    time.sleep(0.3)
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    ev0 = torch.cuda.Event(enable_timing=True)
+    ev1 = torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        ev0.record(stream)
+        for _ in range(args.steps):
+            graph.replay()
+        ev1.record(stream)
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    ms = ev0.elapsed_time(ev1)
+    clk = clocks.stop()
+    if dist:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    ms_tok = ms / args.steps
+    value = world * 1e3 / ms_tok
+    # e2e: the public host-argument call, greedy on the host, logits to host
+    e2e = None
+    if not args.no_e2e:
+        logits = np.empty(c["vocab"], np.float32)
+        nxt = C.c_int()
+        p0 = int(pos.item())
+        t0v = 1
+        for i in range(2):  # eager step, then the call that captures its graph
+            lib.dsv4cuda_decoder_forward_token(h, t0v, p0 + i, logits.ctypes.data, C.byref(nxt))
+            t0v = nxt.value
+        n_e2e = max(8, args.steps // 4)
+        t0 = time.perf_counter()
+        for i in range(n_e2e):
+            if lib.dsv4cuda_decoder_forward_token(h, t0v, p0 + 2 + i, logits.ctypes.data,
+                                                  C.byref(nxt)) != 0:
+                raise RuntimeError(lib.dsv4cuda_decoder_last_error().decode())
+            t0v = nxt.value
+        el = time.perf_counter() - t0
+        if dist:
+            tt = torch.tensor([el], device=dev)
+            dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+            el = float(tt.item())
+        e2e = world * n_e2e / el
+    hbm, _, src = peaks()
+    alg = decode_bytes_per_token(c, n_layers)
+    achieved = alg / (ms_tok * 1e-3) / 1e9
+    if rank == 0:
+        line = {
+            "metric": DECODE_METRIC, "value": value, "unit": "tok/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_tok,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "fp4e2m1/fp8e4m3 weights, bf16 activations, f32 accumulate",
+            "data": "synthetic (random-init weights with the checkpoint's formats)",
+            "config": {"workload": "config 5 batch-1 greedy decode, speculation off",
+                       "layers": n_layers, "hidden": c["hidden"], "vocab": c["vocab"],
+                       "heads": c["n_heads"], "head_dim": c["head_dim"],
+                       "experts": c["experts"], "topk": c["topk"], "moe_inter": c["inter"],
+                       "attention": "sliding window of 128 on every layer (compress ratio "
+                                    "0; the compressor/indexer path is not built)",
+                       "positions": f"{prompt - args.warmup}..{prompt + args.steps}",
+                       "weight_sets": f"{n_layers} layers cycle {len(sets)} distinct "
+                                      "random-init layer weight sets of ~3.6 GB; every token "
+                                      "reads a whole model's bytes, none of it L2-resident",
+                       "graph": "one CUDA graph per token (argmax fed back on the device)",
+                       "parallelism": f"replicas{world}"},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
+                         "frac": achieved / hbm, "traffic": None,
+                         "alg_bytes_per_token": alg, "peak_source": src,
+                         "note": "whole-step bytes / whole-step time (every kernel of the "
+                                 "token, launch gaps included)"},
+            "cpu_baseline": None,
+            "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": 8,
+                    "d2h_bytes_per_step": c["vocab"] * 4 + 4},
+            "gpu_launches": None, "clocks": clk,
+        }
+        print(json.dumps(line), flush=True)
+    graph.reset()
+    dec.close()
     if dist:
         dist.barrier()
         dist.destroy_process_group()

@@ -16,7 +16,8 @@ PKG = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(PKG, "csrc")
 LIBDIR = os.path.join(PKG, "lib")
 LIB = os.path.join(LIBDIR, "libdsv4_cuda.so")
-SOURCES = ["gemv.cu", "moe.cu", "attn.cu", "sample.cu", "snapshot.cu", "ep.cu", "capi.cu"]
+SOURCES = ["gemv.cu", "moe.cu", "attn.cu", "sample.cu", "snapshot.cu", "ep.cu", "decode.cu",
+           "capi.cu"]
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",
     "-O3", "-lineinfo", "-std=c++17",

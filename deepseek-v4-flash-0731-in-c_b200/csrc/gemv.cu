@@ -752,7 +752,7 @@ __global__ void __launch_bounds__(128) bf16_gemv_kernel(const Bf16GemvArgs a) {
   const int row = (gw % rblocks) * 32 + lane;
   const bool row_ok = row < a.rows;
   const int rowc = row_ok ? row : a.rows - 1;
-  const uint16_t* wp = a.W + static_cast<size_t>(rowc) * a.in;
+  const uint16_t* wp = a.W + static_cast<size_t>(it.mat) * a.w_stride + static_cast<size_t>(rowc) * a.in;
   const float* xr[NT];
 #pragma unroll
   for (int t = 0; t < NT; ++t)
@@ -810,7 +810,7 @@ __global__ void bf16_gemv_scalar_kernel(const Bf16GemvArgs a) {
     const int item = static_cast<int>(i / (static_cast<long long>(a.rows) * kItemTok));
     const GemvItem& it = a.items[item];
     if (t >= it.ntok) continue;
-    const uint16_t* w = a.W + static_cast<size_t>(row) * a.in;
+    const uint16_t* w = a.W + static_cast<size_t>(it.mat) * a.w_stride + static_cast<size_t>(row) * a.in;
     const float* x = a.x + static_cast<size_t>(it.tok[t].x) * a.ldx;
     float acc = 0.0f;
     for (int c = 0; c < a.in; ++c) acc = fmaf(bf16_widen(w[c]), x[c], acc);
@@ -986,6 +986,7 @@ cudaError_t launch_stream_nt(const Fp4Maps& maps, const Fp4GemvArgs& a, bool pai
   return launch_pdl(fp4_stream_kernel<NT, WARPS>, dim3(grid), dim3(WARPS * 32), smem, st, maps, b,
                     pair ? 1 : 0);
 }
+
 
 // Tensor maps over every matrix of the launch: rows_total = rows of all
 // matrices an item index can select (max mat + 1 experts).
@@ -1641,8 +1642,206 @@ cudaError_t launch_fp8_gemv(const Fp8GemvArgs& a, bool pair, int item_tokens, cu
   return fp8_dispatch_nt<1, false>(a, item_tokens, st);
 }
 
+// ------------------------------------------------------ FP8 split-K ----
+// One-token FP8 GEMV with every 128-column block's partial computed
+// independently (the decode step's projections, whose few row tiles leave
+// most SMs idle when a warp walks a whole row): kernel A gives each warp 32
+// rows (lane = row) x `bps` consecutive blocks and writes the blocks'
+// sequential fmaf partials to part[block][row]; kernel B folds each row's
+// partials in block order, acc = fmaf(partial, qscale * ws, acc) with
+// NaN-scaled blocks skipped, as dsv4_gemv_fp8_q does
+// (src/dsv4/dsv4_model.c:657-672). Same operations in the same order as the
+// other FP8 kernels, so the same bits.
+__global__ void __launch_bounds__(128) fp8_partials_kernel(const Fp8GemvArgs a, int bps,
+                                                           float* part) {
+  pdl_wait();
+  pdl_trigger();
+  const int lane = threadIdx.x & 31;
+  const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int CB = a.in / 128;
+  const int nseg = (CB + bps - 1) / bps;
+  const int tiles = a.rows / 32;
+  if (gw >= tiles * nseg) return;
+  const int tile = gw / nseg, seg = gw % nseg;
+  const int row = tile * 32 + lane;
+  const GemvItem& it = a.items[0];
+  const __half* xr = a.act.x + static_cast<size_t>(it.tok[0].x) * a.act.ld;
+  const uint8_t* wr = a.W[0] + static_cast<size_t>(row) * a.in;
+  for (int b = seg * bps; b < min(CB, (seg + 1) * bps); ++b) {
+    U8x32 w[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) w[k] = ldg32(wr + b * 128 + 32 * k);
+    float p = 0.0f;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const U8x32 x0 = ldg32_l1(xr + b * 128 + 32 * k);
+      const U8x32 x1 = ldg32_l1(xr + b * 128 + 32 * k + 16);
+      uint32_t x16[16];
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        x16[q] = x0.w[q];
+        x16[8 + q] = x1.w[q];
+      }
+      p = fp8_chain32(w[k].w, x16, p);
+    }
+    part[static_cast<size_t>(b) * a.rows + row] = p;
+  }
+}
+
+__global__ void __launch_bounds__(128) fp8_fold_kernel(const Fp8GemvArgs a, const float* part) {
+  pdl_wait();
+  pdl_trigger();
+  const int row = blockIdx.x * blockDim.x + threadIdx.x;
+  if (row >= a.rows) return;
+  const int CB = a.in / 128;
+  const GemvItem& it = a.items[0];
+  const float* qs = a.act.s + static_cast<size_t>(it.tok[0].x) * (a.act.ld / 128);
+  const uint8_t* sr = a.S[0] + static_cast<size_t>(row / 128) * ((a.in + 127) / 128);
+  float acc = 0.0f;
+  for (int b = 0; b < CB; ++b) {
+    const float ws = e8m0_decode(sr[b]);
+    if (!isnan(ws)) acc = fmaf(part[static_cast<size_t>(b) * a.rows + row], qs[b] * ws, acc);
+  }
+  a.Y[0][static_cast<size_t>(it.tok[0].y) * a.rows + row] = a.round_out ? bf16_round(acc) : acc;
+}
+
+// ------------------------------------------------------- BF16 stream ----
+// Streaming BF16 GEMV for one-token items (the decode step's grouped wo_a and
+// vocab head). A warp owns 32 rows (lane = row) and walks them in 256-column
+// chunks through a ring of kBStages shared-memory stages: every lane
+// bulk-copies its own row's 512-byte segment into a slot padded to 528 bytes
+// (the lanes' 16-byte reads then hit distinct banks) and lane 0 copies the
+// chunk's fp32 activations; completion is counted on the stage's mbarrier
+// (bounded wait). Each lane runs its row's fmaf chain in column order, the
+// reference's order, so the result is the LDG kernel's bit for bit.
+constexpr int kBCols = 256;
+constexpr int kBStages = 4;
+constexpr int kBRowPitch = kBCols * 2 + 16;
+constexpr int kBStage = 32 * kBRowPitch + kBCols * 4;
+
+template <int WARPS>
+__global__ void __launch_bounds__(WARPS * 32, 1) bf16_stream_kernel(const Bf16GemvArgs a,
+                                                                      unsigned int* err) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  __shared__ uint64_t bars_all[WARPS][kBStages];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  unsigned char* wbase = smem + static_cast<size_t>(warp) * kBStages * kBStage;
+  uint64_t* bars = bars_all[warp];
+  if (lane == 0) {
+#pragma unroll
+    for (int q = 0; q < kBStages; ++q) mbar_init(&bars[q], 32);
+    mbar_fence_init();
+  }
+  __syncthreads();
+  pdl_wait();
+  pdl_trigger();
+  const int n_items = load_n_items(a.n_items, a.max_items);
+  const int rblocks = a.rows / 32;
+  const long long tiles = static_cast<long long>(n_items) * rblocks;
+  const int CPT = a.in / kBCols;
+  const long long nwarps = static_cast<long long>(gridDim.x) * WARPS;
+  const long long first = static_cast<long long>(warp) * gridDim.x + blockIdx.x;
+  const long long my_tiles = tiles > first ? (tiles - first + nwarps - 1) / nwarps : 0;
+  const long long jobs = my_tiles * CPT;
+  auto issue = [&](long long j, int q) {
+    const long long tile = first + (j / CPT) * nwarps;
+    const int chunk = static_cast<int>(j % CPT);
+    const int item = static_cast<int>(tile / rblocks);
+    const int rb = static_cast<int>(tile - static_cast<long long>(item) * rblocks);
+    const GemvItem& it = a.items[item];
+    unsigned char* st = wbase + q * kBStage;
+    const uint16_t* src = a.W + static_cast<size_t>(it.mat) * a.w_stride +
+                          static_cast<size_t>(rb * 32 + lane) * a.in + chunk * kBCols;
+    mbar_arrive_expect_tx(&bars[q], kBCols * 2 + (lane == 0 ? kBCols * 4 : 0));
+    bulk_g2s(st + lane * kBRowPitch, src, kBCols * 2, &bars[q]);
+    if (lane == 0)
+      bulk_g2s(st + 32 * kBRowPitch, a.x + static_cast<size_t>(it.tok[0].x) * a.ldx + chunk * kBCols,
+               kBCols * 4, &bars[q]);
+  };
+  for (long long j = 0; j < jobs && j < kBStages; ++j) issue(j, static_cast<int>(j));
+  float acc = 0.0f;
+  int q = 0;
+  uint32_t phase = 0;
+  long long j = 0;
+  bool ok = true;
+  for (; j < jobs; ++j) {
+    if (!mbar_wait(&bars[q], phase, err)) { ok = false; break; }
+    const unsigned char* st = wbase + q * kBStage;
+    const uint4* wrow = reinterpret_cast<const uint4*>(st + lane * kBRowPitch);
+    const float4* xs = reinterpret_cast<const float4*>(st + 32 * kBRowPitch);
+#pragma unroll 4
+    for (int k = 0; k < kBCols / 8; ++k) {
+      const uint4 w8 = wrow[k];
+      const float4 x0 = xs[2 * k], x1 = xs[2 * k + 1];
+      acc = fmaf(__uint_as_float(w8.x << 16), x0.x, acc);
+      acc = fmaf(__uint_as_float(w8.x & 0xFFFF0000u), x0.y, acc);
+      acc = fmaf(__uint_as_float(w8.y << 16), x0.z, acc);
+      acc = fmaf(__uint_as_float(w8.y & 0xFFFF0000u), x0.w, acc);
+      acc = fmaf(__uint_as_float(w8.z << 16), x1.x, acc);
+      acc = fmaf(__uint_as_float(w8.z & 0xFFFF0000u), x1.y, acc);
+      acc = fmaf(__uint_as_float(w8.w << 16), x1.z, acc);
+      acc = fmaf(__uint_as_float(w8.w & 0xFFFF0000u), x1.w, acc);
+    }
+    if (j % CPT == CPT - 1) {
+      const long long tile = first + (j / CPT) * nwarps;
+      const int item = static_cast<int>(tile / rblocks);
+      const int rb = static_cast<int>(tile - static_cast<long long>(item) * rblocks);
+      a.Y[static_cast<size_t>(a.items[item].tok[0].y) * a.rows + rb * 32 + lane] =
+          a.round_out ? bf16_round(acc) : acc;
+      acc = 0.0f;
+    }
+    __syncwarp();  // every lane is done with stage q before it is refilled
+    if (j + kBStages < jobs) issue(j + kBStages, q);
+    if (++q == kBStages) {
+      q = 0;
+      phase ^= 1u;
+    }
+  }
+  if (!ok) {
+    // drain this warp's copies still in flight before the CTA exits
+    uint32_t ph = phase;
+    int k = q;
+    for (long long r = j + 1; r < jobs && r < j + kBStages; ++r) {
+      if (++k == kBStages) { k = 0; ph ^= 1u; }
+      mbar_wait(&bars[k], ph, err);
+    }
+  }
+}
+
+cudaError_t launch_fp8_gemv_splitk(const Fp8GemvArgs& a, float* part, cudaStream_t st) {
+  if (a.rows <= 0) return cudaSuccess;
+  if (a.rows % 32 != 0 || a.in % 128 != 0 || !aligned(a.W[0], 32) || !aligned(a.act.x, 32) ||
+      a.act.ld % 128 != 0 || a.act.x32 || a.max_items != 1)
+    return cudaErrorNotSupported;
+  const int CB = a.in / 128, tiles = a.rows / 32;
+  // about 16 warps per SM, at least one block per warp
+  const long long target = 16LL * sm_count();
+  int bps = static_cast<int>(std::max<long long>(1, (static_cast<long long>(tiles) * CB + target - 1) / target));
+  bps = std::min(bps, CB);
+  const int nseg = (CB + bps - 1) / bps;
+  const long long warps = static_cast<long long>(tiles) * nseg;
+  cudaError_t e = launch_pdl(fp8_partials_kernel, dim3(static_cast<unsigned>((warps + 3) / 4)),
+                             dim3(128), 0, st, a, bps, part);
+  if (e != cudaSuccess) return e;
+  return launch_pdl(fp8_fold_kernel, dim3((a.rows + 127) / 128), dim3(128), 0, st, a,
+                    static_cast<const float*>(part));
+}
+
 cudaError_t launch_bf16_gemv(const Bf16GemvArgs& a, int item_tokens, cudaStream_t st) {
   if (a.rows <= 0 || a.max_items <= 0) return cudaSuccess;
+  if (item_tokens == 1 && a.rows % 32 == 0 && a.in % kBCols == 0 && aligned(a.W, 16) &&
+      (a.w_stride * 2) % 16 == 0 && aligned(a.x, 16) && a.ldx % 4 == 0) {
+    constexpr int WARPS = 2;
+    const size_t smem = static_cast<size_t>(WARPS) * kBStages * kBStage;
+    cudaError_t e = set_max_dynamic_smem(reinterpret_cast<const void*>(bf16_stream_kernel<WARPS>),
+                                         static_cast<int>(smem));
+    if (e != cudaSuccess) return e;
+    const long long tiles = static_cast<long long>(a.max_items) * (a.rows / 32);
+    const int grid = static_cast<int>(std::max<long long>(
+        1, std::min<long long>(sm_count(), (tiles + WARPS - 1) / WARPS)));
+    return launch_pdl(bf16_stream_kernel<WARPS>, dim3(grid), dim3(WARPS * 32), smem, st, a,
+                      device_error_word());
+  }
   const bool vec_ok = (a.in % 16 == 0) && aligned(a.W, 32) && aligned(a.x, 32) &&
                       (a.ldx % 8 == 0);
   if (!vec_ok) {

@@ -65,7 +65,8 @@ struct Fp8GemvArgs {
 };
 
 struct Bf16GemvArgs {
-  const uint16_t* W;       // [rows][in]
+  const uint16_t* W;       // [rows][in]; an item's matrix is W + mat * w_stride
+  size_t w_stride;         // elements between matrices (grouped projections)
   int in, rows;
   int round_out;
   const float* x;          // [*][ldx] fp32 activations
@@ -82,6 +83,10 @@ cudaError_t launch_fp8_gemv(const Fp8GemvArgs& a, bool pair, int item_tokens,
                             cudaStream_t st, bool map_cache = true);
 cudaError_t launch_bf16_gemv(const Bf16GemvArgs& a, int item_tokens,
                              cudaStream_t st);
+// One-token, one-item FP8 GEMV split over 128-column blocks (more warps for
+// matrices with few row tiles); part holds in/128 * rows floats of scratch.
+// cudaErrorNotSupported when the shape or alignment does not fit.
+cudaError_t launch_fp8_gemv_splitk(const Fp8GemvArgs& a, float* part, cudaStream_t st);
 
 // x [rows][n] fp32 -> E4M3 grid (f16) + per-128 scales (dsv4_quant_fp8_codes).
 cudaError_t launch_quant_fp8(const float* x, int ldx, int n, int rows, __half* qx,

@@ -749,3 +749,220 @@ def kv_copy_rows(cache, src_rows, dst_rows, stream=None):
     d = np.ascontiguousarray(dst_rows, dtype=np.int64)
     _check(lib.dsv4cuda_kv_copy_rows(C.byref(cache.struct), s.ctypes.data, d.ctypes.data, s.size,
                                      _stream(stream)))
+
+
+# ------------------------------------------------------- whole-model decode --
+class DecoderConfig(C.Structure):
+    _fields_ = [(n, C.c_int) for n in ("hidden", "n_layers", "vocab", "n_heads", "head_dim",
+                                       "rope_dim", "q_lora", "o_groups", "o_lora", "window",
+                                       "hc_mult", "hc_iters")] + \
+        [("rms_eps", C.c_float), ("hc_eps", C.c_float), ("rope_theta", C.c_float),
+         ("max_context", C.c_int), ("moe", MoeConfig), ("hc_exact", C.c_int)]
+
+
+class ModelWeights(C.Structure):
+    _fields_ = [(n, vp) for n in ("embed", "head", "norm", "hc_head_fn", "hc_head_base",
+                                  "hc_head_scale")]
+
+
+class LayerWeights(C.Structure):
+    _fields_ = [(n, vp) for n in (
+        "attn_norm", "ffn_norm", "hc_attn_fn", "hc_attn_scale", "hc_attn_base",
+        "hc_ffn_fn", "hc_ffn_scale", "hc_ffn_base", "attn_sink", "wq_a", "wq_a_s", "q_norm",
+        "wq_b", "wq_b_s", "wkv", "wkv_s", "kv_norm", "wo_a", "wo_a_fp8", "wo_a_fp8_s",
+        "wo_b", "wo_b_s")] + [("moe", MoeWeights)]
+
+
+for _n, _r, _a in (("dsv4cuda_decoder_create", C.c_int, [vp, vp, vp, vp]),
+                   ("dsv4cuda_decoder_destroy", None, [vp]),
+                   ("dsv4cuda_decoder_last_error", C.c_char_p, []),
+                   ("dsv4cuda_decoder_reset", C.c_int, [vp, vp]),
+                   ("dsv4cuda_decoder_forward_token", C.c_int, [vp, C.c_int, C.c_int, vp, vp]),
+                   ("dsv4cuda_decoder_step", C.c_int, [vp, vp]),
+                   ("dsv4cuda_decoder_step_device", C.c_int, [vp, vp, vp, vp]),
+                   ("dsv4cuda_decoder_token_slot", C.c_void_p, [vp]),
+                   ("dsv4cuda_decoder_position_slot", C.c_void_p, [vp]),
+                   ("dsv4cuda_decoder_logits", C.c_void_p, [vp]),
+                   ("dsv4cuda_decoder_argmax", C.c_void_p, [vp]),
+                   ("dsv4cuda_decoder_read", C.c_int, [vp, vp, vp]),
+                   ("dsv4cuda_decoder_cache", C.c_int, [vp, C.c_int, vp])):
+    getattr(lib, _n).restype = _r
+    getattr(lib, _n).argtypes = _a
+
+
+class Decoder:
+    """dsv4_forward_token on the device (dsv4cuda_decoder_*). `cfg` is a
+    dict of the DecoderConfig fields (moe: a dict of MoeConfig fields);
+    `model` and `layers` hold torch CUDA tensors named like the C structs'
+    fields (layers[i]["moe"] like a MoE layer dict). The tensors must stay
+    alive as long as the decoder."""
+
+    def __init__(self, cfg: dict, model: dict, layers: list):
+        c = DecoderConfig()
+        for k, v in cfg.items():
+            if k != "moe":
+                setattr(c, k, v)
+        for k, v in cfg["moe"].items():
+            setattr(c.moe, k, v)
+        self.vocab = cfg["vocab"]
+        self._keep = (model, layers)
+        mw = ModelWeights(*[_addr(model.get(f[0])) for f in ModelWeights._fields_])
+        lws = (LayerWeights * len(layers))()
+        for i, L in enumerate(layers):
+            for name, _ in LayerWeights._fields_:
+                if name == "moe":
+                    _, w = _moe_structs(L["moe"])
+                    lws[i].moe = w
+                else:
+                    setattr(lws[i], name, _addr(L.get(name)))
+        h = vp()
+        if lib.dsv4cuda_decoder_create(C.byref(h), C.byref(c), C.byref(mw), lws) != 0:
+            raise Dsv4CudaError(lib.dsv4cuda_decoder_last_error().decode())
+        self.handle = h
+
+    def forward_token(self, token, position):
+        """(logits [vocab] float32, greedy next token)."""
+        logits = np.empty(self.vocab, np.float32)
+        nxt = C.c_int()
+        if lib.dsv4cuda_decoder_forward_token(self.handle, int(token), int(position),
+                                              logits.ctypes.data, C.byref(nxt)) != 0:
+            raise Dsv4CudaError(lib.dsv4cuda_decoder_last_error().decode())
+        return logits, nxt.value
+
+    def step_device(self, token, position, stream=None):
+        """Step with token / position from device int32 tensors (capturable)."""
+        if lib.dsv4cuda_decoder_step_device(self.handle, token.data_ptr(), position.data_ptr(),
+                                            _stream(stream)) != 0:
+            raise Dsv4CudaError(lib.dsv4cuda_decoder_last_error().decode())
+
+    def read(self):
+        """The last step's (logits, argmax), copied to the host."""
+        logits = np.empty(self.vocab, np.float32)
+        nxt = C.c_int()
+        if lib.dsv4cuda_decoder_read(self.handle, logits.ctypes.data, C.byref(nxt)) != 0:
+            raise Dsv4CudaError(lib.dsv4cuda_decoder_last_error().decode())
+        return logits, nxt.value
+
+    def step(self, stream=None):
+        if lib.dsv4cuda_decoder_step(self.handle, _stream(stream)) != 0:
+            raise Dsv4CudaError(lib.dsv4cuda_decoder_last_error().decode())
+
+    def slots(self):
+        """Device addresses: (token slot, position slot, logits, argmax)."""
+        return (lib.dsv4cuda_decoder_token_slot(self.handle),
+                lib.dsv4cuda_decoder_position_slot(self.handle),
+                lib.dsv4cuda_decoder_logits(self.handle), lib.dsv4cuda_decoder_argmax(self.handle))
+
+    def cache(self, layer):
+        """Layer `layer`'s latent ring as a KvCache structure (device pointers)."""
+        kc = KvCache()
+        if lib.dsv4cuda_decoder_cache(self.handle, layer, C.byref(kc)) != 0:
+            raise Dsv4CudaError(lib.dsv4cuda_decoder_last_error().decode())
+        return kc
+
+    def reset(self, stream=None):
+        if lib.dsv4cuda_decoder_reset(self.handle, _stream(stream)) != 0:
+            raise Dsv4CudaError(lib.dsv4cuda_decoder_last_error().decode())
+
+    def close(self):
+        if getattr(self, "handle", None):
+            lib.dsv4cuda_decoder_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def read_safetensors(path):
+    """{name: numpy array} of a single-file safetensors checkpoint (F32, BF16
+    as uint16, F8_E4M3 / F8_E8M0 / I8 as uint8, I64)."""
+    import json
+    import struct
+    dt = {"F32": np.float32, "BF16": np.uint16, "F8_E4M3": np.uint8, "F8_E8M0": np.uint8,
+          "I8": np.uint8, "I64": np.int64}
+    with open(path, "rb") as f:
+        n = struct.unpack("<Q", f.read(8))[0]
+        hdr = json.loads(f.read(n))
+        data = f.read()
+    out = {}
+    for name, t in hdr.items():
+        if name == "__metadata__":
+            continue
+        a, b = t["data_offsets"]
+        out[name] = np.frombuffer(data[a:b], dtype=dt[t["dtype"]]).reshape(t["shape"])
+    return out
+
+
+def decoder_from_checkpoint(ckpt_dir, max_context, device="cuda", hc_exact=False):
+    """Weight ingest for the device decoder: reads a checkpoint directory in
+    the reference's format (config.json + one safetensors file), stacks the
+    routed experts expert-major and uploads everything to `device`.
+    Returns a Decoder. Layers must be of compress ratio 0."""
+    import json
+    import torch
+    with open(os.path.join(ckpt_dir, "config.json")) as f:
+        cj = json.load(f)
+    files = [fn for fn in os.listdir(ckpt_dir) if fn.endswith(".safetensors")]
+    t = {}
+    for fn in files:
+        t.update(read_safetensors(os.path.join(ckpt_dir, fn)))
+    if any(cj["compress_ratios"][:cj["num_hidden_layers"]]):
+        raise ValueError("the device decoder covers compress-ratio-0 layers only")
+
+    def dev(a):
+        return torch.from_numpy(np.ascontiguousarray(a)).to(device)
+
+    E = cj["n_routed_experts"]
+    cfg = dict(hidden=cj["hidden_size"], n_layers=cj["num_hidden_layers"],
+               vocab=cj["vocab_size"], n_heads=cj["num_attention_heads"],
+               head_dim=cj["head_dim"], rope_dim=cj["qk_rope_head_dim"],
+               q_lora=cj["q_lora_rank"], o_groups=cj["o_groups"], o_lora=cj["o_lora_rank"],
+               window=cj["sliding_window"], hc_mult=cj["hc_mult"],
+               hc_iters=cj["hc_sinkhorn_iters"], rms_eps=cj["rms_norm_eps"],
+               hc_eps=cj["hc_eps"], rope_theta=cj["rope_theta"], max_context=max_context,
+               hc_exact=1 if hc_exact else 0,
+               moe=dict(hidden=cj["hidden_size"], moe_inter=cj["moe_intermediate_size"],
+                        n_experts=E, topk=cj["num_experts_per_tok"],
+                        swiglu_limit=int(cj["swiglu_limit"]),
+                        route_scale=cj["routed_scaling_factor"], shared_kind=SHARED_FP8,
+                        hash_vocab=0))
+    model = dict(embed=dev(t["embed.weight"]), head=dev(t["head.weight"]),
+                 norm=dev(t["norm.weight"]), hc_head_fn=dev(t["hc_head_fn"]),
+                 hc_head_base=dev(t["hc_head_base"]), hc_head_scale=dev(t["hc_head_scale"]))
+    layers = []
+    for L in range(cfg["n_layers"]):
+        p = f"layers.{L}."
+        a = p + "attn."
+        ex = lambda e, n: t[f"{p}ffn.experts.{e}.{n}"]  # noqa: E731
+        moe = dict(hidden=cfg["hidden"], moe_inter=cfg["moe"]["moe_inter"], n_experts=E,
+                   topk=cfg["moe"]["topk"], route_scale=cfg["moe"]["route_scale"],
+                   swiglu_limit=cfg["moe"]["swiglu_limit"],
+                   gate_w=dev(t[p + "ffn.gate.weight"]), bias=dev(t[p + "ffn.gate.bias"]),
+                   tid2eid=None,
+                   shared=dict(fp8=True,
+                               w1=dev(t[p + "ffn.shared_experts.w1.weight"]),
+                               s1=dev(t[p + "ffn.shared_experts.w1.scale"]),
+                               w3=dev(t[p + "ffn.shared_experts.w3.weight"]),
+                               s3=dev(t[p + "ffn.shared_experts.w3.scale"]),
+                               w2=dev(t[p + "ffn.shared_experts.w2.weight"]),
+                               s2=dev(t[p + "ffn.shared_experts.w2.scale"])))
+        for w in ("w1", "w2", "w3"):
+            moe[w] = dev(np.stack([ex(e, w + ".weight") for e in range(E)]))
+            moe["s" + w[1]] = dev(np.stack([ex(e, w + ".scale") for e in range(E)]))
+        layers.append(dict(
+            attn_norm=dev(t[p + "attn_norm.weight"]), ffn_norm=dev(t[p + "ffn_norm.weight"]),
+            hc_attn_fn=dev(t[p + "hc_attn_fn"]), hc_attn_scale=dev(t[p + "hc_attn_scale"]),
+            hc_attn_base=dev(t[p + "hc_attn_base"]), hc_ffn_fn=dev(t[p + "hc_ffn_fn"]),
+            hc_ffn_scale=dev(t[p + "hc_ffn_scale"]), hc_ffn_base=dev(t[p + "hc_ffn_base"]),
+            attn_sink=dev(t[a + "attn_sink"]),
+            wq_a=dev(t[a + "wq_a.weight"]), wq_a_s=dev(t[a + "wq_a.scale"]),
+            q_norm=dev(t[a + "q_norm.weight"]),
+            wq_b=dev(t[a + "wq_b.weight"]), wq_b_s=dev(t[a + "wq_b.scale"]),
+            wkv=dev(t[a + "wkv.weight"]), wkv_s=dev(t[a + "wkv.scale"]),
+            kv_norm=dev(t[a + "kv_norm.weight"]),
+            wo_a_fp8=dev(t[a + "wo_a.weight"]), wo_a_fp8_s=dev(t[a + "wo_a.scale"]),
+            wo_b=dev(t[a + "wo_b.weight"]), wo_b_s=dev(t[a + "wo_b.scale"]), moe=moe))
+    return Decoder(cfg, model, layers)

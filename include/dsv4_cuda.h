@@ -494,6 +494,96 @@ int dsv4cuda_tree_attn_indices(const int *parents, int n_nodes, int committed, i
 int dsv4cuda_kv_copy_rows(const dsv4cuda_kv_cache *cache, const long long *src_rows,
                           const long long *dst_rows, int n, void *stream);
 
+/* ---------------------------------------------------------------------
+ * Whole-model decode on the device: dsv4_forward_token
+ * (src/dsv4/dsv4_model.c:8388, public API include/dsv4/dsv4.h:161) with
+ * every weight resident in HBM, for layers of compress ratio 0 (the
+ * sliding-window attention; the compressor and indexer of ratio-4/128
+ * layers are not part of this path). One call per token: embedding, per
+ * layer hyper-connection pre, RMSNorm, attention (FP8 projections, norms,
+ * RoPE, FP8 latent ring, sparse attention over the window, inverse RoPE,
+ * grouped wo_a, wo_b), HC post, HC pre, RMSNorm, MoE layer, HC post; then
+ * the HC head, final RMSNorm, BF16 vocab head and argmax. All weight
+ * pointers are DEVICE pointers in the checkpoint's layouts. */
+typedef struct {
+    int hidden, n_layers, vocab;
+    int n_heads, head_dim, rope_dim, q_lora, o_groups, o_lora, window;
+    int hc_mult, hc_iters;        /* hc_mult <= 4 */
+    float rms_eps, hc_eps, rope_theta;
+    int max_context;              /* positions 0 .. max_context - 1 */
+    dsv4cuda_moe_config moe;      /* moe.hidden == hidden */
+    /* 1: the hyper-connection mixes run the reference's sequential fp32
+     * fmaf chains (hc_mult * hidden long; one thread per mix row) and the
+     * step reproduces dsv4_forward_token bit for bit up to the host libm's
+     * last-ulp expf differences; 0: the mixes are summed in double in
+     * parallel (fast, within the chains' rounding of the reference). */
+    int hc_exact;
+} dsv4cuda_decoder_config;
+
+typedef struct {
+    const uint16_t *embed;        /* [vocab][hidden] BF16 */
+    const uint16_t *head;         /* [vocab][hidden] BF16 */
+    const uint16_t *norm;         /* [hidden] BF16 final RMSNorm gain */
+    const float *hc_head_fn;      /* [hc_mult][hc_mult * hidden] */
+    const float *hc_head_base;    /* [hc_mult] */
+    const float *hc_head_scale;   /* [1] */
+} dsv4cuda_model_weights;
+
+typedef struct {
+    const uint16_t *attn_norm, *ffn_norm;                    /* [hidden] BF16 */
+    const float *hc_attn_fn, *hc_attn_scale, *hc_attn_base;  /* [(2+m)m][m*hidden], [3], [(2+m)m] */
+    const float *hc_ffn_fn, *hc_ffn_scale, *hc_ffn_base;
+    const float *attn_sink;                                  /* [n_heads] */
+    const uint8_t *wq_a, *wq_a_s;     /* FP8 [q_lora][hidden] + [128x128] E8M0 */
+    const uint16_t *q_norm;           /* [q_lora] */
+    const uint8_t *wq_b, *wq_b_s;     /* FP8 [n_heads*head_dim][q_lora] */
+    const uint8_t *wkv, *wkv_s;       /* FP8 [head_dim][hidden] */
+    const uint16_t *kv_norm;          /* [head_dim] */
+    const uint16_t *wo_a;             /* BF16 [o_groups*o_lora][n_heads*head_dim/o_groups], or NULL: */
+    const uint8_t *wo_a_fp8, *wo_a_fp8_s;  /* the checkpoint's FP8 form, decoded to BF16 at create
+                                              as the reference does at load (:1927-1936) */
+    const uint8_t *wo_b, *wo_b_s;     /* FP8 [hidden][o_groups*o_lora] */
+    dsv4cuda_moe_weights moe;         /* expert-major routed FP4 + shared expert */
+} dsv4cuda_layer_weights;
+
+typedef struct dsv4cuda_decoder dsv4cuda_decoder;
+
+/* Builds a decoder over the given device weights (not copied; wo_a is
+ * decoded into a decoder-owned BF16 copy when only its FP8 form is given)
+ * and allocates the per-layer FP8 latent rings (window rows each), the
+ * RoPE tables of every position and the step buffers. Returns 0 or -1
+ * (dsv4cuda_decoder_last_error). */
+int dsv4cuda_decoder_create(dsv4cuda_decoder **out, const dsv4cuda_decoder_config *cfg,
+                            const dsv4cuda_model_weights *model,
+                            const dsv4cuda_layer_weights *layers);
+void dsv4cuda_decoder_destroy(dsv4cuda_decoder *D);
+const char *dsv4cuda_decoder_last_error(void);
+/* Clears the latent rings (dsv4_model_reset_context). Async on stream. */
+int dsv4cuda_decoder_reset(dsv4cuda_decoder *D, void *stream);
+/* dsv4_forward_token: host token/position in, host logits[vocab] (may be
+ * NULL) and the greedy next token (argmax, lowest id on ties; may be NULL)
+ * out; synchronous. */
+int dsv4cuda_decoder_forward_token(dsv4cuda_decoder *D, int token, int position, float *logits,
+                                   int *next_token);
+/* The same step reading token and position from the decoder's own device
+ * slots (dsv4cuda_decoder_token_slot / _position_slot) and leaving logits and
+ * argmax in device memory (dsv4cuda_decoder_logits / _argmax): no host
+ * synchronisation, so a captured CUDA graph of it replays for any position. */
+int dsv4cuda_decoder_step(dsv4cuda_decoder *D, void *stream);
+/* Copies device token/position into the slots, then steps. */
+int dsv4cuda_decoder_step_device(dsv4cuda_decoder *D, const int *token, const int *position,
+                                 void *stream);
+/* Waits for the device, then copies the last step's logits[vocab] and
+ * argmax to host memory (either may be NULL). */
+int dsv4cuda_decoder_read(dsv4cuda_decoder *D, float *logits, int *next_token);
+/* Layer `layer`'s latent ring (window rows; position p at row p % window),
+ * e.g. to register it with dsv4cuda_snapshot_create for a verify step. */
+int dsv4cuda_decoder_cache(dsv4cuda_decoder *D, int layer, dsv4cuda_kv_cache *out);
+int *dsv4cuda_decoder_token_slot(dsv4cuda_decoder *D);
+int *dsv4cuda_decoder_position_slot(dsv4cuda_decoder *D);
+float *dsv4cuda_decoder_logits(dsv4cuda_decoder *D);
+int *dsv4cuda_decoder_argmax(dsv4cuda_decoder *D);
+
 #ifdef __cplusplus
 }
 #endif

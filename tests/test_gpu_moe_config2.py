@@ -58,7 +58,10 @@ def test_config2_256_experts_vs_reference(cuda, ref, config2, M):
     for t in range(M):
         want, widx, wwt = ref.moe_forward(L, x[t], slots=slots)
         assert np.array_equal(idx[t], widx), (t, idx[t], widx)
-        np.testing.assert_allclose(wt[t], wwt, rtol=1e-6)
+        # weights come from the router's parallel-scan logits, which sit within
+        # a rigorous bound of the reference's sequential chain (a near tie
+        # replays the chain exactly): a few ulps of the score
+        np.testing.assert_allclose(wt[t], wwt, rtol=4e-6)
         err, exact = compare(got[t], want)
         stats.append((err, exact))
         assert err <= MAX_ERR_RMS, (t, err, exact)
@@ -98,10 +101,13 @@ def test_router_score_vs_host_libm(cuda, ref):
     the z = 20 branch point. At most one ulp apart, and rarely."""
     grid = np.linspace(-30, 30, 1 << 21, dtype=np.float32)
     runs = []
-    for c in (-3.0, -1.0, -0.25, 0.0, 0.1, 0.5, 1.0, 2.5, 19.99, 20.0):
-        base = np.float32(c).view(np.int32)
-        runs.append((base + np.arange(-20000, 20000, dtype=np.int32)).view(np.float32))
-    z = np.concatenate([grid, *runs]).astype(np.float32)
+    for c in (3.0, 1.0, 0.25, 0.1, 0.5, 2.5, 19.99, 20.0):
+        # 40000 adjacent fp32 values around +c and around -c
+        mag = (np.float32(c).view(np.int32) + np.arange(-20000, 20000, dtype=np.int32))
+        runs += [mag.view(np.float32), -mag.view(np.float32)]
+    tiny = np.arange(1, 20000, dtype=np.int32).view(np.float32)  # smallest magnitudes
+    z = np.concatenate([grid, *runs, tiny, -tiny, np.zeros(1, np.float32)]).astype(np.float32)
+    assert np.isfinite(z).all()
     zd = torch.from_numpy(z).cuda()
     sd = torch.empty_like(zd)
     cuda.router_scores(zd, sd)
@@ -145,7 +151,9 @@ def test_router_adjacent_ulp_logits_256_experts(cuda, ref, orc):
         if int(row[i]) & 0x7FFF:  # -1, 0 or +1 BF16 step (a zero weight stays)
             row[i] = np.uint16(int(row[i]) + (case % 3) - 1)
         L["gate_w"][e9] = row
-        dev["gate_w"].view(torch.int16)[e9].copy_(torch.from_numpy(row.view(np.int16)))
+        # the device gate gets the same rows (earlier cases' edits undone)
+        dev["gate_w"].view(torch.int16).copy_(torch.from_numpy(L["gate_w"].view(np.int16)))
+        torch.cuda.synchronize()  # the library reads the gate on its own stream
         want, widx, _ = ref.moe_forward(L, x[0], slots=slots)
         got = layer.forward_host(x)
         idx, _, replays = layer.last_routes(1)
