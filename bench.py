@@ -72,10 +72,12 @@ def parse():
                     help="expert intermediate size (smaller only for profiling captures)")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end leg")
-    ap.add_argument("--workload", default="moe", choices=["moe", "attn", "decode"],
-                    help="moe: config 2 MoE layer (default); attn: config 3 latent decode "
-                         "attention at --attn-batch/--attn-ctx; decode: config 5 batch-1 "
-                         "greedy decode through every layer on the device")
+    ap.add_argument("--workload", default="decode", choices=["moe", "attn", "decode"],
+                    help="decode (default): config 5 batch-1 greedy decode through every "
+                         "layer on the device; moe: config 2 MoE layer; attn: config 3 latent "
+                         "decode attention at --attn-batch/--attn-ctx")
+    ap.add_argument("--no-moe-sub", action="store_true",
+                    help="decode: skip the config 2 expert-GEMV measurement attached to the line")
     ap.add_argument("--decode-sets", type=int, default=4,
                     help="decode: distinct random-init layer weight sets the 43 layers cycle "
                          "through (each ~3.6 GB; L2 never holds a layer between uses)")
@@ -316,6 +318,26 @@ def moe_config(args, world):
 
 def run_reference_arm(args, rank, world):
     if rank != 0:
+        return
+    if args.workload == "decode":
+        res = cpu_reference_decode(args.decode_layers)
+        if res is None:
+            print(json.dumps({"impl": "reference", "unavailable":
+                              "oracle/_ref/ref_decode_bench was not built (reference sources absent)"}))
+            return
+        tps, cores, sample = res
+        print(json.dumps({
+            "impl": "reference", "metric": DECODE_METRIC, "value": tps, "unit": "tok/s",
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": 1e3 / tps, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "fp4e2m1/fp8e4m3 weights, bf16 activations, f32 accumulate",
+            "data": "synthetic (random-init weights with the checkpoint's formats)",
+            "config": {"workload": "config 5 batch-1 greedy decode, speculation off",
+                       "layers": args.decode_layers},
+            "cpu_baseline": {"value": tps, "unit": "tok/s", "cores": cores, "kind": "reference",
+                             "sample": sample, "extrapolated": True},
+            "e2e": {"value": tps, "unit": "tok/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}), flush=True)
         return
     per_step_cap = max(args.steps, 1)
     # warm-up, then K timed steps, each step one decode token (bounded run)
@@ -976,7 +998,7 @@ def decode_bytes_per_token(c, n_layers):
     return n_layers * per_layer + c["vocab"] * H * 2 + mult * mult * H * 4 + H * 2
 
 
-def make_decode_set(torch, seed, dev, c):
+def make_decode_set(torch, seed, dev, c, expert_range=None):
     """One random-init layer weight set at config-5 shapes (distributions as
     config 2: FP4 codes uniform, E8M0 lognormal(0, 0.5) rounded to powers of
     two, FP8 codes uniform over the finite values, BF16 N(0, 0.02), RMSNorm
@@ -1013,10 +1035,11 @@ def make_decode_set(torch, seed, dev, c):
     sh = {}
     for k, (r, cc) in (("1", (I, H)), ("3", (I, H)), ("2", (H, I))):
         sh["w" + k], sh["s" + k] = fp8(r, cc)
+    n = (expert_range[1] - expert_range[0]) if expert_range else E  # experts held here
     moe = dict(hidden=H, moe_inter=I, n_experts=E, topk=c["topk"], route_scale=1.5,
                swiglu_limit=10, gate_w=bf16(E, H), bias=f32(E), tid2eid=None,
-               w1=u8(E, I, H // 2), s1=e8m0(E, I, H // 32), w3=u8(E, I, H // 2),
-               s3=e8m0(E, I, H // 32), w2=u8(E, H, I // 2), s2=e8m0(E, H, I // 32),
+               w1=u8(n, I, H // 2), s1=e8m0(n, I, H // 32), w3=u8(n, I, H // 2),
+               s3=e8m0(n, I, H // 32), w2=u8(n, H, I // 2), s2=e8m0(n, H, I // 32),
                shared=dict(fp8=True, **sh))
     ones3 = torch.ones(3, device=dev)
     return dict(attn_norm=bf16(H, mean=1.0), ffn_norm=bf16(H, mean=1.0),
@@ -1028,10 +1051,52 @@ def make_decode_set(torch, seed, dev, c):
                 wo_b=wo_b, wo_b_s=wo_b_s, moe=moe)
 
 
+def cpu_reference_decode(n_layers=43, threads=None, warm=8, timed=8):
+    """The reference engine's own decode step on the host cores
+    (oracle/_ref/ref_decode_bench: dsv4_forward_token over a config-5-shaped
+    random checkpoint of ONE layer, written to RAM). A 43-layer checkpoint
+    (~156 GB) does not fit the host, so the per-token time is extrapolated:
+    43 x (one layer) + the vocab head + the embedding, the head and the
+    embedding split off with the engine's own profile counters. Returns
+    (tok/s, threads, sample description) or None when the reference was not
+    built here."""
+    import shutil
+    import tempfile
+    exe = os.path.join(ROOT, "oracle", "_ref", "ref_decode_bench")
+    if not os.path.exists(exe):
+        return None
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import random_checkpoint
+    threads = threads or host_threads()
+    base = "/dev/shm" if os.path.isdir("/dev/shm") else None
+    d = tempfile.mkdtemp(prefix="dsv4_c5_", dir=base)
+    try:
+        random_checkpoint.write(d, 1)
+        r = subprocess.run([exe, d, str(warm), str(timed), str(threads)], capture_output=True,
+                           text=True, timeout=1800)
+        line = [ln for ln in r.stdout.splitlines() if ln.startswith("RESULT")]
+        if r.returncode != 0 or not line:
+            raise RuntimeError(r.stderr[-500:])
+        f = line[-1].split()
+        tok, total, head, emb = int(f[4]), float(f[6]), float(f[8]), float(f[10])
+        layer = (total - head - emb) / tok
+        per_token = n_layers * layer + (head + emb) / tok
+        return 1.0 / per_token, threads, (
+            f"dsv4_forward_token on a 1-layer config-5 random checkpoint in RAM, {tok} timed "
+            f"tokens after {warm} warm-up, {threads} thread(s): {layer * 1e3:.1f} ms per layer, "
+            f"{head / tok * 1e3:.1f} ms head; per token extrapolated to {n_layers} layers "
+            f"({per_token:.2f} s)")
+    finally:
+        shutil.rmtree(d, ignore_errors=True)
+
+
 def main_decode(args, rank, world, local):
-    """--workload decode: config 5 batch-1 greedy decode. Every rank runs the
-    whole model on its own GPU (replicas; the expert-parallel split of the
-    decoder is not built), so N GPUs decode N independent sequences."""
+    """--workload decode: config 5 batch-1 greedy decode. Under torchrun the
+    MoE blocks are expert-parallel (rank r holds experts [r E/N, (r+1) E/N)
+    of every layer) and token-parallel: each rank decodes its own sequence,
+    attention and the dense weights replicated, and every layer's tokens are
+    routed together and their expert slots exchanged over peer memory; N GPUs
+    decode N sequences (weak scaling)."""
     import torch
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
@@ -1046,7 +1111,9 @@ def main_decode(args, rank, world, local):
     dsv4cuda.init(local)
     c = dict(C5)
     n_layers = args.decode_layers
-    sets = [make_decode_set(torch, 500 + i, dev, c) for i in range(args.decode_sets)]
+    ep = world > 1
+    erange = (rank * c["experts"] // world, (rank + 1) * c["experts"] // world) if ep else None
+    sets = [make_decode_set(torch, 500 + i, dev, c, erange) for i in range(args.decode_sets)]
     g = torch.Generator(device=dev)
     g.manual_seed(7)
     model = dict(embed=(torch.randn(c["vocab"], c["hidden"], device=dev, generator=g) * 0.02)
@@ -1071,6 +1138,31 @@ def main_decode(args, rank, world, local):
                         shared_kind=dsv4cuda.SHARED_FP8, hash_vocab=0))
     layers = [sets[i % len(sets)] for i in range(n_layers)]
     dec = dsv4cuda.Decoder(cfg, model, layers)
+    ipc_own, ipc_peers, moe_ep = [], [], []
+    if ep:
+        # one EP-attached MoE layer per weight set, its exchange buffer mapped
+        # into every rank
+        moe_ep = [dsv4cuda.MoeLayer(st_["moe"], max_tokens=world, device=True,
+                                    expert_range=erange) for st_ in sets]
+        handles = []
+        for L in moe_ep:
+            addr, hnd = dsv4cuda.ipc_alloc(L.ep_buffer_bytes())
+            ipc_own.append(addr)
+            handles.append(hnd)
+        all_h = [None] * world
+        dist.all_gather_object(all_h, handles)
+        for li, L in enumerate(moe_ep):
+            addrs = []
+            for r in range(world):
+                if r == rank:
+                    addrs.append(ipc_own[li])
+                else:
+                    a_ = dsv4cuda.ipc_open(all_h[r][li])
+                    ipc_peers.append(a_)
+                    addrs.append(a_)
+            L.ep_attach(rank, world, addrs)
+        dist.barrier()
+        dec.set_moe_layers([moe_ep[i % len(moe_ep)] for i in range(n_layers)])
     lib = dsv4cuda.lib
     h = dec.handle
     _, _, _, am_slot = dec.slots()
@@ -1139,9 +1231,35 @@ def main_decode(args, rank, world, local):
             dist.all_reduce(tt, op=dist.ReduceOp.MAX)
             el = float(tt.item())
         e2e = world * n_e2e / el
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        try:
+            res = cpu_reference_decode(n_layers)
+            if res:
+                cpu = {"value": res[0], "unit": "tok/s", "cores": res[1], "kind": "reference",
+                       "sample": res[2], "extrapolated": True}
+        except Exception as exc:  # report, do not hide
+            cpu = {"value": None, "unit": "tok/s", "cores": 0, "kind": "reference",
+                   "sample": f"failed: {exc}"}
     hbm, _, src = peaks()
     alg = decode_bytes_per_token(c, n_layers)
     achieved = alg / (ms_tok * 1e-3) / 1e9
+    kernels = lib.dsv4cuda_decoder_step_kernels(h)
+    # the expert-GEMV half of the metric: the config 2 MoE layer workload in a
+    # child process (its routed FP4 GEMV against the HBM roofline)
+    moe_sub = None
+    if rank == 0 and world == 1 and not args.no_moe_sub:
+        r = subprocess.run([sys.executable, os.path.join(ROOT, "bench.py"), "--workload", "moe",
+                            "--steps", "200", "--warmup", "20", "--no-cpu", "--no-attn-sweep"],
+                           capture_output=True, text=True, timeout=900)
+        ln = [x for x in r.stdout.splitlines() if x.startswith("{")]
+        if r.returncode == 0 and ln:
+            m = json.loads(ln[-1])
+            moe_sub = {"metric": m["metric"], "value": m["value"], "unit": m["unit"],
+                       "ms_per_step": m["ms_per_step"], "roofline": m["roofline"],
+                       "e2e": m["e2e"], "clocks": m["clocks"]}
+        else:
+            moe_sub = {"failed": r.stderr[-500:]}
     if rank == 0:
         line = {
             "metric": DECODE_METRIC, "value": value, "unit": "tok/s", "n_gpus": world,
@@ -1160,20 +1278,34 @@ def main_decode(args, rank, world, local):
                                       "random-init layer weight sets of ~3.6 GB; every token "
                                       "reads a whole model's bytes, none of it L2-resident",
                        "graph": "one CUDA graph per token (argmax fed back on the device)",
-                       "parallelism": f"replicas{world}"},
+                       "parallelism": (f"ep{world} (token-parallel: one sequence per GPU, "
+                                       "experts split, slots exchanged over peer memory)"
+                                       if ep else "ep1")},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
                          "frac": achieved / hbm, "traffic": None,
                          "alg_bytes_per_token": alg, "peak_source": src,
                          "note": "whole-step bytes / whole-step time (every kernel of the "
                                  "token, launch gaps included)"},
-            "cpu_baseline": None,
+            "cpu_baseline": cpu,
             "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": 8,
                     "d2h_bytes_per_step": c["vocab"] * 4 + 4},
-            "gpu_launches": None, "clocks": clk,
+            "gpu_launches": kernels * args.steps, "clocks": clk,
+            "expert_gemv_config2": moe_sub,
         }
         print(json.dumps(line), flush=True)
+    torch.cuda.synchronize()
     graph.reset()
     dec.close()
+    if ep:
+        # every rank stops touching peer memory before any buffer is unmapped
+        dist.barrier()
+        for a_ in ipc_peers:
+            dsv4cuda.ipc_close(a_)
+        dist.barrier()
+        for a_ in ipc_own:
+            dsv4cuda.ipc_free(a_)
+        for L in moe_ep:
+            L.close()
     if dist:
         dist.barrier()
         dist.destroy_process_group()

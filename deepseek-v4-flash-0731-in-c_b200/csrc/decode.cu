@@ -191,50 +191,60 @@ __device__ __forceinline__ float mul_add(float a, float b, float c) {
   return __fadd_rn(__fmul_rn(a, b), c);
 }
 
-// dsv4_hc_split (src/dsv4/dsv4_ops.c:412-460) on one warp: lane l < m*m
-// holds comb[l / m][l % m]; every row or column sum is formed by each lane
-// from shuffled values in the reference's sequential order, so the result
-// is that of the reference's loops (lanes >= m*m follow along unused).
-// mixes in shared memory; pre/post (lanes < m) and comb are returned through
-// pre_out/post_out/comb_out.
-__device__ void hc_split_warp(const float* mixes, const float* scale3, const float* base, int m,
+// dsv4_hc_split (src/dsv4/dsv4_ops.c:412-460) on one warp for a compile-time
+// M: lane l < M*M holds comb[l / M][l % M]; each row or column sum is formed
+// by every lane from shuffled values in the reference's sequential order
+// (unrolled, so a sum costs one round of independent shuffles), and every
+// division is the lane's own IEEE division, as in the reference's loops.
+template <int M>
+__device__ void hc_split_warp(const float* mixes, const float* scale3, const float* base,
                               int iters, float eps, float* pre_out, float* post_out,
                               float* comb_out) {
   const int lane = threadIdx.x & 31;
-  const int mm = m * m;
-  const int li = lane < mm ? lane : 0;
-  const int ri = li / m, cj = li % m;
-  if (lane < m) {
+  const int li = lane < M * M ? lane : 0;
+  const int ri = li / M, cj = li % M;
+  if (lane < M) {
     pre_out[lane] = sigmoid_stable(mul_add(mixes[lane], scale3[0], base[lane])) + eps;
-    post_out[lane] = 2.0f * sigmoid_stable(mul_add(mixes[m + lane], scale3[1], base[m + lane]));
+    post_out[lane] = 2.0f * sigmoid_stable(mul_add(mixes[M + lane], scale3[1], base[M + lane]));
   }
-  float c = mul_add(mixes[2 * m + li], scale3[2], base[2 * m + li]);
-  auto at = [&](float v, int i, int j) { return __shfl_sync(0xffffffffu, v, i * m + j); };
+  float c = mul_add(mixes[2 * M + li], scale3[2], base[2 * M + li]);
+  float v[M];
   {  // softmax rows
-    float mx = at(c, ri, 0);
-    for (int j = 1; j < m; ++j) {
-      const float v = at(c, ri, j);
-      mx = v > mx ? v : mx;
-    }
+#pragma unroll
+    for (int j = 0; j < M; ++j) v[j] = __shfl_sync(0xffffffffu, c, ri * M + j);
+    float mx = v[0];
+#pragma unroll
+    for (int j = 1; j < M; ++j) mx = v[j] > mx ? v[j] : mx;
     const float e = expf_r1(c - mx);
+#pragma unroll
+    for (int j = 0; j < M; ++j) v[j] = __shfl_sync(0xffffffffu, e, ri * M + j);
     float sum = 0.0f;
-    for (int j = 0; j < m; ++j) sum += at(e, ri, j);
+#pragma unroll
+    for (int j = 0; j < M; ++j) sum += v[j];
     c = e / sum + eps;
   }
-  {  // one column normalisation
+  auto col_norm = [&]() {
+#pragma unroll
+    for (int i = 0; i < M; ++i) v[i] = __shfl_sync(0xffffffffu, c, i * M + cj);
     float sum = 0.0f;
-    for (int i = 0; i < m; ++i) sum += at(c, i, cj);
+#pragma unroll
+    for (int i = 0; i < M; ++i) sum += v[i];
     c /= (sum + eps);
-  }
+  };
+  auto row_norm = [&]() {
+#pragma unroll
+    for (int j = 0; j < M; ++j) v[j] = __shfl_sync(0xffffffffu, c, ri * M + j);
+    float sum = 0.0f;
+#pragma unroll
+    for (int j = 0; j < M; ++j) sum += v[j];
+    c /= (sum + eps);
+  };
+  col_norm();
   for (int it = 0; it < iters - 1; ++it) {
-    float sum = 0.0f;
-    for (int j = 0; j < m; ++j) sum += at(c, ri, j);
-    c /= (sum + eps);
-    sum = 0.0f;
-    for (int i = 0; i < m; ++i) sum += at(c, i, cj);
-    c /= (sum + eps);
+    row_norm();
+    col_norm();
   }
-  if (lane < mm) comb_out[lane] = c;
+  if (lane < M * M) comb_out[lane] = c;
 }
 
 struct HcReduceArgs {
@@ -282,7 +292,12 @@ __global__ void __launch_bounds__(kHcThreads) hc_reduce_kernel(const HcReduceArg
         pre_s[lane] =
             1.0f / (1.0f + expf_r1(-mul_add(mixes[lane], a.scale[0], a.base[lane]))) + a.hc_eps;
     } else {
-      hc_split_warp(mixes, a.scale, a.base, a.mult, a.iters, a.hc_eps, pre_s, post_s, comb_s);
+      switch (a.mult) {
+        case 1: hc_split_warp<1>(mixes, a.scale, a.base, a.iters, a.hc_eps, pre_s, post_s, comb_s); break;
+        case 2: hc_split_warp<2>(mixes, a.scale, a.base, a.iters, a.hc_eps, pre_s, post_s, comb_s); break;
+        case 3: hc_split_warp<3>(mixes, a.scale, a.base, a.iters, a.hc_eps, pre_s, post_s, comb_s); break;
+        default: hc_split_warp<4>(mixes, a.scale, a.base, a.iters, a.hc_eps, pre_s, post_s, comb_s); break;
+      }
       __syncwarp();
       if (lane < a.mult) a.post[lane] = post_s[lane];
       if (lane < a.mult * a.mult) a.comb[lane] = comb_s[lane];
@@ -396,8 +411,8 @@ __device__ __forceinline__ float cache_value(const Fp8KvCache& c, long long r, i
   return bf16_widen(c.rope[r * c.rope_dim + (i - c.nope)]);
 }
 
-// The window's cached rows, decoded once into both layouts the next two
-// kernels read coalesced: kvdec [n][d] and kvt [d][n]. Padding keys get
+// The window's cached rows, decoded once into kvdec [n][d] and its transpose
+// kvt [d][n] (each read coalesced by one of the next kernels). Padding keys get
 // zeros (their BF16 weight is 0 too, so a chain term 0 * 0 adds +0 and
 // leaves the chain's value as the reference's skip does: the chains start
 // at +0 and never hold -0).
@@ -414,33 +429,61 @@ __global__ void win_decode_kernel(const WinAttnArgs a) {
   }
 }
 
-// CTA h, thread t = key: the head's scores (512-long fmaf dots in dimension
-// order), max, exponentials, BF16 weights and the denominator summed in key
-// order by thread 0.
-__global__ void __launch_bounds__(256) win_scores_kernel(const WinAttnArgs a) {
-  extern __shared__ float sm[];  // q_h [d], e [n]
+// Scores: CTA = kWinHeads heads (warps) x 32 keys (lanes). The keys' cached
+// columns [d][32] are staged in shared memory from the transposed copy (lane
+// t reads word t of each row: distinct banks), the heads' q rows beside
+// them; each thread runs its (head, key) dot as one fmaf chain in dimension
+// order, times the scale.
+constexpr int kWinHeads = 8, kWinKeys = 32;
+__global__ void __launch_bounds__(kWinHeads * 32) win_scores_kernel(const WinAttnArgs a) {
+  extern __shared__ __align__(16) float sm[];  // q [kWinHeads][d], k [d][kWinKeys]
+  pdl_wait();
+  pdl_trigger();
+  const int h0 = blockIdx.x * kWinHeads, t0 = blockIdx.y * kWinKeys;
+  float* qs = sm;
+  float* ks = sm + kWinHeads * a.d;
+  const int d4 = a.d / 4;
+  for (int e = threadIdx.x; e < kWinHeads * d4; e += blockDim.x) {
+    const int hh = e / d4, i4 = e - hh * d4;
+    const int h = h0 + hh;
+    reinterpret_cast<float4*>(qs)[e] =
+        h < a.H ? reinterpret_cast<const float4*>(a.q + static_cast<size_t>(h) * a.d)[i4]
+                : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  for (int e = threadIdx.x; e < a.d * (kWinKeys / 4); e += blockDim.x) {
+    const int i = e / (kWinKeys / 4), t4 = e - i * (kWinKeys / 4);
+    const int t = t0 + 4 * t4;  // n is a multiple of 4: a group is all in or all out
+    reinterpret_cast<float4*>(ks)[e] =
+        t < a.n ? *reinterpret_cast<const float4*>(a.kvt + static_cast<size_t>(i) * a.n + t)
+                : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  __syncthreads();
+  const int lane = threadIdx.x & 31, hw = threadIdx.x >> 5;
+  const int h = h0 + hw, t = t0 + lane;
+  if (h >= a.H || t >= a.n) return;
+  float st = -INFINITY;
+  const int r = a.idx[t];
+  if (r >= 0 && r < a.cache.rows) {
+    const float* q = qs + hw * a.d;
+    float dot = 0.0f;
+#pragma unroll 16
+    for (int i = 0; i < a.d; ++i) dot = fmaf(q[i], ks[i * kWinKeys + lane], dot);
+    st = __fmul_rn(dot, a.scale);
+  }
+  a.s[static_cast<size_t>(h) * a.n + t] = st;
+}
+
+// CTA h: the head's max, exponentials, BF16 weights and the denominator
+// summed in key order by thread 0.
+__global__ void __launch_bounds__(256) win_softmax_kernel(const WinAttnArgs a) {
+  extern __shared__ float ex[];
   __shared__ float red[8];
   pdl_wait();
   pdl_trigger();
   const int h = blockIdx.x;
-  float* qs = sm;
-  float* ex = sm + a.d;
-  for (int i = threadIdx.x; i < a.d; i += blockDim.x) qs[i] = a.q[static_cast<size_t>(h) * a.d + i];
-  __syncthreads();
+  const float* sh = a.s + static_cast<size_t>(h) * a.n;
   float mxl = -INFINITY;
-  for (int t = threadIdx.x; t < a.n; t += blockDim.x) {
-    float st = -INFINITY;
-    const int r = a.idx[t];
-    if (r >= 0 && r < a.cache.rows) {
-      float dot = 0.0f;
-      const float* col = a.kvt + t;
-#pragma unroll 8
-      for (int i = 0; i < a.d; ++i) dot = fmaf(qs[i], col[static_cast<size_t>(i) * a.n], dot);
-      st = __fmul_rn(dot, a.scale);
-    }
-    ex[t] = st;
-    mxl = fmaxf(mxl, st);
-  }
+  for (int t = threadIdx.x; t < a.n; t += blockDim.x) mxl = fmaxf(mxl, sh[t]);
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) mxl = fmaxf(mxl, __shfl_xor_sync(0xffffffffu, mxl, o));
   if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = mxl;
@@ -448,7 +491,7 @@ __global__ void __launch_bounds__(256) win_scores_kernel(const WinAttnArgs a) {
   float mx = red[0];
   for (int w = 1; w < static_cast<int>(blockDim.x >> 5); ++w) mx = fmaxf(mx, red[w]);
   for (int t = threadIdx.x; t < a.n; t += blockDim.x) {
-    const float st = ex[t];
+    const float st = sh[t];
     const bool live = st != -INFINITY;
     const float e = live ? expf_r1(st - mx) : 0.0f;
     ex[t] = e;
@@ -457,18 +500,16 @@ __global__ void __launch_bounds__(256) win_scores_kernel(const WinAttnArgs a) {
   __syncthreads();
   if (threadIdx.x == 0) {
     float sum = expf_r1(a.sink[h] - mx);
-    for (int t = 0; t < a.n; ++t) {
-      const int r = a.idx[t];
-      if (r >= 0 && r < a.cache.rows) sum += ex[t];
-    }
+    for (int t = 0; t < a.n; ++t)
+      if (sh[t] != -INFINITY) sum += ex[t];
     a.den[h] = sum;
   }
 }
 
-// CTA h, thread = dimension pair: the two value chains over the keys in key
-// order, the division, BF16, and the inverse RoPE of the pair when it lies
-// in the RoPE dims.
-__global__ void __launch_bounds__(256) win_values_kernel(const WinAttnArgs a) {
+// CTA (h, 128-dim block), thread = dimension pair: the two value chains
+// over the keys in key order, the division, BF16, and the inverse RoPE of
+// the pair when it lies in the RoPE dims.
+__global__ void __launch_bounds__(64) win_values_kernel(const WinAttnArgs a) {
   extern __shared__ float ws[];  // w_h [n]
   pdl_wait();
   pdl_trigger();
@@ -476,7 +517,8 @@ __global__ void __launch_bounds__(256) win_values_kernel(const WinAttnArgs a) {
   for (int t = threadIdx.x; t < a.n; t += blockDim.x) ws[t] = a.w[static_cast<size_t>(h) * a.n + t];
   __syncthreads();
   const int pairs = a.d / 2;
-  for (int p = threadIdx.x; p < pairs; p += blockDim.x) {
+  for (int p = blockIdx.y * 64 + threadIdx.x; p < min(pairs, (blockIdx.y + 1) * 64);
+       p += blockDim.x) {
     const int i = 2 * p;
     float o0 = 0.0f, o1 = 0.0f;
 #pragma unroll 8
@@ -500,6 +542,51 @@ __global__ void __launch_bounds__(256) win_values_kernel(const WinAttnArgs a) {
     oh[i] = x0;
     oh[i + 1] = x1;
   }
+}
+
+// Greedy token: argmax_logits (src/cli/dsv4_run.c:355; first maximum, strict
+// >) in two stages - each CTA finds its chunk's first maximum, then one warp
+// takes the chunks' results in chunk order with the same strict >. For
+// finite logits this is the sequential scan's answer.
+constexpr int kArgmaxCtas = 148;
+__global__ void __launch_bounds__(256) argmax_chunks_kernel(const float* x, int n, float* cv,
+                                                            int* ci) {
+  __shared__ float sv[8];
+  __shared__ int si[8];
+  pdl_wait();
+  pdl_trigger();
+  const int chunk = (n + gridDim.x - 1) / gridDim.x;
+  const int b = blockIdx.x * chunk, e = min(n, b + chunk);
+  float bv = -INFINITY;
+  int bi = 0x7FFFFFFF;
+  for (int i = b + threadIdx.x; i < e; i += blockDim.x) {
+    const float v = x[i];
+    if (v > bv || (v == bv && i < bi)) { bv = v; bi = i; }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+    if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+  }
+  if ((threadIdx.x & 31) == 0) { sv[threadIdx.x >> 5] = bv; si[threadIdx.x >> 5] = bi; }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int w = 1; w < static_cast<int>(blockDim.x >> 5); ++w)
+      if (sv[w] > bv || (sv[w] == bv && si[w] < bi)) { bv = sv[w]; bi = si[w]; }
+    cv[blockIdx.x] = bv;
+    ci[blockIdx.x] = bi < e ? bi : b;
+  }
+}
+
+__global__ void argmax_final_kernel(const float* cv, const int* ci, int chunks, int* out) {
+  pdl_wait();
+  pdl_trigger();
+  if (threadIdx.x != 0) return;
+  int best = 0;
+  for (int c = 1; c < chunks; ++c)
+    if (cv[c] > cv[best]) best = c;
+  *out = ci[best];
 }
 
 // hc_post (src/dsv4/dsv4_model.c:7165-7177): thread = column j of the state.
@@ -551,6 +638,9 @@ struct dsv4cuda_decoder {
   dsv4cuda_decoder_config cfg{};
   dsv4cuda_model_weights g{};
   std::vector<dsv4::Layer> layers;
+  // expert parallelism: per layer an EP-attached MoE layer (token-parallel
+  // exchange over peer memory); empty = every expert on this device
+  std::vector<dsv4cuda_moe_layer*> ep;
   std::vector<void*> owned;  // device allocations to free
   // per-step buffers
   int* d_token = nullptr;
@@ -571,6 +661,7 @@ struct dsv4cuda_decoder {
   float* kvdec = nullptr;     // [window][d] the window's cached values
   float* kvt = nullptr;       // [d][window] transposed
   float* fp8_part = nullptr;  // split-K FP8 GEMV partials [in / 128][rows]
+  size_t win_smem = 0;        // dynamic shared memory of win_scores_kernel
   float* att_s = nullptr;     // [H][window] scores
   float* att_w = nullptr;     // [H][window] BF16 weights
   float* att_den = nullptr;   // [H]
@@ -578,6 +669,8 @@ struct dsv4cuda_decoder {
   float* branch = nullptr;    // [hid]
   float* logits = nullptr;    // [vocab]
   int* argmax = nullptr;      // [1]
+  float* am_v = nullptr;      // per-chunk maxima of the argmax
+  int* am_i = nullptr;
   int* idx = nullptr;         // [window]
   long long* row = nullptr;   // [1]
   float *cosv = nullptr, *sinv = nullptr;      // [rope/2] of the current position
@@ -667,6 +760,7 @@ cudaError_t quant(dsv4cuda_decoder* D, const float* x, int n, cudaStream_t st) {
     if (e__ != cudaSuccess) return e__;             \
   } while (0)
 
+
 cudaError_t hc_pre(dsv4cuda_decoder* D, const float* fn, const float* scale, const float* base,
                    const uint16_t* norm, int head, cudaStream_t st) {
   const auto& c = D->cfg;
@@ -753,9 +847,13 @@ cudaError_t attention(dsv4cuda_decoder* D, dsv4::Layer& L, cudaStream_t st) {
   wa.den = D->att_den;
   wa.out = D->o;
   DEC_CHECK(dsv4::launch_pdl(dsv4::win_decode_kernel, dim3(c.window), dim3(128), 0, st, wa));
-  DEC_CHECK(dsv4::launch_pdl(dsv4::win_scores_kernel, dim3(H), dim3(256),
-                             sizeof(float) * (d + c.window), st, wa));
-  DEC_CHECK(dsv4::launch_pdl(dsv4::win_values_kernel, dim3(H), dim3(256),
+  DEC_CHECK(dsv4::launch_pdl(
+      dsv4::win_scores_kernel,
+      dim3((H + dsv4::kWinHeads - 1) / dsv4::kWinHeads, (c.window + dsv4::kWinKeys - 1) / dsv4::kWinKeys),
+      dim3(dsv4::kWinHeads * 32), D->win_smem, st, wa));
+  DEC_CHECK(dsv4::launch_pdl(dsv4::win_softmax_kernel, dim3(H), dim3(256),
+                             sizeof(float) * c.window, st, wa));
+  DEC_CHECK(dsv4::launch_pdl(dsv4::win_values_kernel, dim3(H, (d / 2 + 63) / 64), dim3(64),
                              sizeof(float) * c.window, st, wa));
   // grouped BF16 wo_a, then quant -> FP8 wo_b
   dsv4::Bf16GemvArgs ga{};
@@ -789,13 +887,19 @@ cudaError_t step(dsv4cuda_decoder* D, cudaStream_t st) {
                              static_cast<const float*>(D->sin_tab), D->idx, D->row, D->cosv,
                              D->sinv));
   dsv4::MoeExecOptions opt;
-  for (auto& L : D->layers) {
+  for (size_t li = 0; li < D->layers.size(); ++li) {
+    auto& L = D->layers[li];
     const auto& w = L.w;
     DEC_CHECK(hc_pre(D, w.hc_attn_fn, w.hc_attn_scale, w.hc_attn_base, w.attn_norm, 0, st));
     DEC_CHECK(attention(D, L, st));
     DEC_CHECK(hc_post(D, st));
     DEC_CHECK(hc_pre(D, w.hc_ffn_fn, w.hc_ffn_scale, w.hc_ffn_base, w.ffn_norm, 0, st));
-    DEC_CHECK(dsv4::moe_forward(L.mc, L.mw, D->moe_ws, D->x, D->d_token, 1, D->branch, st, opt));
+    if (!D->ep.empty()) {
+      if (dsv4cuda_moe_forward_ep_tokens(D->ep[li], D->x, 1, D->branch, st) != 0)
+        return cudaErrorLaunchFailure;
+    } else {
+      DEC_CHECK(dsv4::moe_forward(L.mc, L.mw, D->moe_ws, D->x, D->d_token, 1, D->branch, st, opt));
+    }
     DEC_CHECK(hc_post(D, st));
   }
   // model_head + head_logits (src/dsv4/dsv4_model.c:7755-7760), argmax
@@ -812,7 +916,12 @@ cudaError_t step(dsv4cuda_decoder* D, cudaStream_t st) {
   ha.n_items = D->n_one;
   ha.max_items = 1;
   DEC_CHECK(dsv4::launch_bf16_gemv(ha, 1, st));
-  return dsv4::argmax_rows(D->logits, 1, c.vocab, D->argmax, st);
+  const int chunks = std::min(dsv4::kArgmaxCtas, c.vocab);
+  DEC_CHECK(dsv4::launch_pdl(dsv4::argmax_chunks_kernel, dim3(chunks), dim3(256), 0, st,
+                             static_cast<const float*>(D->logits), c.vocab, D->am_v, D->am_i));
+  return dsv4::launch_pdl(dsv4::argmax_final_kernel, dim3(1), dim3(32), 0, st,
+                          static_cast<const float*>(D->am_v), static_cast<const int*>(D->am_i),
+                          chunks, D->argmax);
 }
 
 bool cfg_ok(const dsv4cuda_decoder_config* c) {
@@ -821,7 +930,8 @@ bool cfg_ok(const dsv4cuda_decoder_config* c) {
          c->rope_dim <= c->head_dim && (c->head_dim - c->rope_dim) % 64 == 0 &&
          (c->head_dim - c->rope_dim) / 64 <= dsv4::kKvScaleSlots && c->q_lora > 0 &&
          c->o_groups > 0 && (c->n_heads * c->head_dim) % c->o_groups == 0 && c->o_lora > 0 &&
-         c->window > 0 && c->hc_mult > 0 && c->hc_mult <= 4 && c->hc_iters > 0 &&
+         c->window > 0 && c->window % 4 == 0 && c->hc_mult > 0 && c->hc_mult <= 4 &&
+         c->hc_iters > 0 &&
          c->hidden <= 8 * dsv4::kHcThreads &&
          c->max_context > 0 && c->moe.hidden == c->hidden;
 }
@@ -879,6 +989,8 @@ DSV4_API int dsv4cuda_decoder_create(dsv4cuda_decoder** out, const dsv4cuda_deco
   chk(D->branch = dalloc<float>(D, c.hidden));
   chk(D->logits = dalloc<float>(D, c.vocab));
   chk(D->argmax = dalloc<int>(D, 1));
+  chk(D->am_v = dalloc<float>(D, dsv4::kArgmaxCtas));
+  chk(D->am_i = dalloc<int>(D, dsv4::kArgmaxCtas));
   chk(D->idx = dalloc<int>(D, c.window));
   chk(D->row = dalloc<long long>(D, 1));
   chk(D->cosv = dalloc<float>(D, half));
@@ -914,6 +1026,13 @@ DSV4_API int dsv4cuda_decoder_create(dsv4cuda_decoder** out, const dsv4cuda_deco
                cudaMemcpyHostToDevice);
     cudaMemcpy(D->n_one, &n1, sizeof(int), cudaMemcpyHostToDevice);
     cudaMemcpy(D->n_groups, &ng, sizeof(int), cudaMemcpyHostToDevice);
+  }
+  D->win_smem = sizeof(float) * (dsv4::kWinHeads + dsv4::kWinKeys) * static_cast<size_t>(d);
+  if (D->win_smem > 48 * 1024 &&
+      dsv4::set_max_dynamic_smem(reinterpret_cast<const void*>(dsv4::win_scores_kernel),
+                                 static_cast<int>(D->win_smem)) != cudaSuccess) {
+    dsv4cuda_decoder_destroy(D);
+    return fail("dsv4cuda_decoder_create: head_dim %d needs too much shared memory", d);
   }
   // per layer: the FP8 latent ring, wo_a as BF16, the MoE layer's view
   const int nope = d - c.rope_dim;
@@ -988,6 +1107,20 @@ DSV4_API void dsv4cuda_decoder_destroy(dsv4cuda_decoder* D) {
   delete D;
 }
 
+DSV4_API int dsv4cuda_decoder_set_moe_layers(dsv4cuda_decoder* D, dsv4cuda_moe_layer* const* layers,
+                                             int n) {
+  if (!D || n < 0 || (n > 0 && (!layers || n != static_cast<int>(D->layers.size()))))
+    return fail("dsv4cuda_decoder_set_moe_layers: give one MoE layer per decoder layer, or none");
+  D->ep.assign(layers, layers + n);
+  for (auto* L : D->ep)
+    if (!L) return fail("dsv4cuda_decoder_set_moe_layers: null layer");
+  if (D->graph) {  // the captured step called the previous MoE path
+    cudaGraphExecDestroy(D->graph);
+    D->graph = nullptr;
+  }
+  return 0;
+}
+
 DSV4_API int dsv4cuda_decoder_reset(dsv4cuda_decoder* D, void* stream) {
   if (!D) return fail("dsv4cuda_decoder_reset: null decoder");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
@@ -1052,6 +1185,36 @@ DSV4_API int dsv4cuda_decoder_forward_token(dsv4cuda_decoder* D, int token, int 
     e = cudaMemcpyAsync(next_token, D->argmax, sizeof(int), cudaMemcpyDeviceToHost, st);
   if (e == cudaSuccess) e = cudaStreamSynchronize(st);
   return e == cudaSuccess ? 0 : fail("dsv4cuda_decoder_forward_token: %s", cudaGetErrorString(e));
+}
+
+// Kernels one step launches: a step captured into a graph (not run), its
+// kernel nodes counted (the MoE layers' side-stream kernels included).
+DSV4_API int dsv4cuda_decoder_step_kernels(dsv4cuda_decoder* D) {
+  if (!D) return fail("dsv4cuda_decoder_step_kernels: null decoder");
+  cudaStream_t st = nullptr;
+  cudaError_t e = cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking);
+  cudaGraph_t g = nullptr;
+  if (e == cudaSuccess) e = cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal);
+  if (e == cudaSuccess) {
+    const cudaError_t es = step(D, st);
+    e = cudaStreamEndCapture(st, &g);
+    if (e == cudaSuccess) e = es;
+  }
+  int kernels = 0;
+  size_t n = 0;
+  if (e == cudaSuccess) e = cudaGraphGetNodes(g, nullptr, &n);
+  if (e == cudaSuccess && n) {
+    std::vector<cudaGraphNode_t> nodes(n);
+    e = cudaGraphGetNodes(g, nodes.data(), &n);
+    for (size_t i = 0; e == cudaSuccess && i < n; ++i) {
+      cudaGraphNodeType t;
+      e = cudaGraphNodeGetType(nodes[i], &t);
+      if (e == cudaSuccess && t == cudaGraphNodeTypeKernel) ++kernels;
+    }
+  }
+  if (g) cudaGraphDestroy(g);
+  if (st) cudaStreamDestroy(st);
+  return e == cudaSuccess ? kernels : fail("dsv4cuda_decoder_step_kernels: %s", cudaGetErrorString(e));
 }
 
 DSV4_API int dsv4cuda_decoder_read(dsv4cuda_decoder* D, float* logits, int* next_token) {

@@ -761,7 +761,7 @@ __global__ void __launch_bounds__(128) bf16_gemv_kernel(const Bf16GemvArgs a) {
 #pragma unroll
   for (int t = 0; t < NT; ++t) acc[t] = 0.f;
   const int NC = a.in >> 4;  // 16-column chunks
-  constexpr int PF = 4;
+  constexpr int PF = NT == 1 ? 8 : 4;  // 32-byte chunks in flight per lane
   U8x32 buf[PF];
 #pragma unroll
   for (int j = 0; j < PF; ++j)
@@ -1553,7 +1553,10 @@ cudaError_t launch_fp4_stream(const Fp4GemvArgs& a, bool pair, int nt, cudaStrea
   const long long n_mats = a.n_mats > 0 ? a.n_mats : 1;
   if (!fp4_maps(&maps, a, pair, n_mats, map_cache)) return cudaErrorInvalidValue;
   const long long tiles = static_cast<long long>(a.max_items) * (pair ? 2 : 1) * ((a.rows + 31) / 32);
-  if (nt == 1 && a.in / 32 <= 256 && tiles < 4LL * sm_count()) {
+  // single matrices up to six tiles per SM (down projections), pairs below
+  // four (a pair's two chains per tile fill an SM on their own)
+  if (nt == 1 && a.in / 32 <= 256 && tiles <= (pair ? 4LL : 6LL) * sm_count() &&
+      (pair ? tiles < 4LL * sm_count() : true)) {
     // one token per item and few tiles (one to four experts, e.g. a GPU's
     // share under expert parallelism): split every tile's columns over a
     // CTA's warps so the launch still covers every SM
@@ -1698,9 +1701,22 @@ __global__ void __launch_bounds__(128) fp8_fold_kernel(const Fp8GemvArgs a, cons
   const float* qs = a.act.s + static_cast<size_t>(it.tok[0].x) * (a.act.ld / 128);
   const uint8_t* sr = a.S[0] + static_cast<size_t>(row / 128) * ((a.in + 127) / 128);
   float acc = 0.0f;
-  for (int b = 0; b < CB; ++b) {
-    const float ws = e8m0_decode(sr[b]);
-    if (!isnan(ws)) acc = fmaf(part[static_cast<size_t>(b) * a.rows + row], qs[b] * ws, acc);
+  for (int b0 = 0; b0 < CB; b0 += 8) {
+    float pv[8], sv[8];
+    uint32_t code[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int b = b0 + j < CB ? b0 + j : CB - 1;
+      pv[j] = part[static_cast<size_t>(b) * a.rows + row];
+      sv[j] = qs[b];
+      code[j] = sr[b];
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      if (b0 + j >= CB) break;
+      const float ws = e8m0_decode(code[j]);
+      if (!isnan(ws)) acc = fmaf(pv[j], sv[j] * ws, acc);
+    }
   }
   a.Y[0][static_cast<size_t>(it.tok[0].y) * a.rows + row] = a.round_out ? bf16_round(acc) : acc;
 }
@@ -1708,29 +1724,33 @@ __global__ void __launch_bounds__(128) fp8_fold_kernel(const Fp8GemvArgs a, cons
 // ------------------------------------------------------- BF16 stream ----
 // Streaming BF16 GEMV for one-token items (the decode step's grouped wo_a and
 // vocab head). A warp owns 32 rows (lane = row) and walks them in 256-column
-// chunks through a ring of kBStages shared-memory stages: every lane
-// bulk-copies its own row's 512-byte segment into a slot padded to 528 bytes
-// (the lanes' 16-byte reads then hit distinct banks) and lane 0 copies the
-// chunk's fp32 activations; completion is counted on the stage's mbarrier
-// (bounded wait). Each lane runs its row's fmaf chain in column order, the
-// reference's order, so the result is the LDG kernel's bit for bit.
+// chunks through a ring of kBStages shared-memory stages: per chunk one lane
+// issues four 2-D TMA boxes of [32 rows x 128 B] with the 128-byte swizzle
+// (the matrix read 128 contiguous bytes per row at a time; the swizzle makes
+// the lanes' 16-byte reads conflict-free) and a bulk copy of the chunk's
+// fp32 activations, completed on the stage's mbarrier (bounded wait). Each
+// lane runs its row's fmaf chain in column order, the reference's order, so
+// the result is the LDG kernel's bit for bit.
 constexpr int kBCols = 256;
-constexpr int kBStages = 4;
-constexpr int kBRowPitch = kBCols * 2 + 16;
-constexpr int kBStage = 32 * kBRowPitch + kBCols * 4;
+constexpr int kBStages = 3;
+constexpr int kBW = 32 * kBCols * 2;             // four swizzled [32][128 B] boxes
+constexpr int kBStage = kBW + kBCols * 4;        // + the activation chunk
 
 template <int WARPS>
-__global__ void __launch_bounds__(WARPS * 32, 1) bf16_stream_kernel(const Bf16GemvArgs a,
-                                                                      unsigned int* err) {
-  extern __shared__ __align__(16) unsigned char smem[];
+__global__ void __launch_bounds__(WARPS * 32, 1)
+    bf16_stream_kernel(const __grid_constant__ CUtensorMap wmap, const Bf16GemvArgs a,
+                       unsigned int* err) {
+  extern __shared__ __align__(1024) unsigned char smem[];
   __shared__ uint64_t bars_all[WARPS][kBStages];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  unsigned char* wbase = smem + static_cast<size_t>(warp) * kBStages * kBStage;
+  unsigned char* const sbase = smem + ((1024u - (smem_addr(smem) & 1023u)) & 1023u);
+  unsigned char* wbase = sbase + static_cast<size_t>(warp) * kBStages * kBStage;
   uint64_t* bars = bars_all[warp];
   if (lane == 0) {
 #pragma unroll
-    for (int q = 0; q < kBStages; ++q) mbar_init(&bars[q], 32);
+    for (int q = 0; q < kBStages; ++q) mbar_init(&bars[q], 1);
     mbar_fence_init();
+    if (warp == 0) tma_prefetch_desc(&wmap);
   }
   __syncthreads();
   pdl_wait();
@@ -1744,43 +1764,48 @@ __global__ void __launch_bounds__(WARPS * 32, 1) bf16_stream_kernel(const Bf16Ge
   const long long my_tiles = tiles > first ? (tiles - first + nwarps - 1) / nwarps : 0;
   const long long jobs = my_tiles * CPT;
   auto issue = [&](long long j, int q) {
+    if (lane != 0) return;
     const long long tile = first + (j / CPT) * nwarps;
     const int chunk = static_cast<int>(j % CPT);
     const int item = static_cast<int>(tile / rblocks);
     const int rb = static_cast<int>(tile - static_cast<long long>(item) * rblocks);
     const GemvItem& it = a.items[item];
     unsigned char* st = wbase + q * kBStage;
-    const uint16_t* src = a.W + static_cast<size_t>(it.mat) * a.w_stride +
-                          static_cast<size_t>(rb * 32 + lane) * a.in + chunk * kBCols;
-    mbar_arrive_expect_tx(&bars[q], kBCols * 2 + (lane == 0 ? kBCols * 4 : 0));
-    bulk_g2s(st + lane * kBRowPitch, src, kBCols * 2, &bars[q]);
-    if (lane == 0)
-      bulk_g2s(st + 32 * kBRowPitch, a.x + static_cast<size_t>(it.tok[0].x) * a.ldx + chunk * kBCols,
-               kBCols * 4, &bars[q]);
+    mbar_arrive_expect_tx(&bars[q], kBStage);
+    const int y = it.mat * a.rows + rb * 32;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) tma_load_2d(st + k * 4096, &wmap, chunk * 512 + k * 128, y, &bars[q]);
+    bulk_g2s(st + kBW, a.x + static_cast<size_t>(it.tok[0].x) * a.ldx + chunk * kBCols, kBCols * 4,
+             &bars[q]);
   };
   for (long long j = 0; j < jobs && j < kBStages; ++j) issue(j, static_cast<int>(j));
+  __syncwarp();
   float acc = 0.0f;
   int q = 0;
   uint32_t phase = 0;
   long long j = 0;
   bool ok = true;
+  const int sw = lane & 7;
   for (; j < jobs; ++j) {
     if (!mbar_wait(&bars[q], phase, err)) { ok = false; break; }
     const unsigned char* st = wbase + q * kBStage;
-    const uint4* wrow = reinterpret_cast<const uint4*>(st + lane * kBRowPitch);
-    const float4* xs = reinterpret_cast<const float4*>(st + 32 * kBRowPitch);
-#pragma unroll 4
-    for (int k = 0; k < kBCols / 8; ++k) {
-      const uint4 w8 = wrow[k];
-      const float4 x0 = xs[2 * k], x1 = xs[2 * k + 1];
-      acc = fmaf(__uint_as_float(w8.x << 16), x0.x, acc);
-      acc = fmaf(__uint_as_float(w8.x & 0xFFFF0000u), x0.y, acc);
-      acc = fmaf(__uint_as_float(w8.y << 16), x0.z, acc);
-      acc = fmaf(__uint_as_float(w8.y & 0xFFFF0000u), x0.w, acc);
-      acc = fmaf(__uint_as_float(w8.z << 16), x1.x, acc);
-      acc = fmaf(__uint_as_float(w8.z & 0xFFFF0000u), x1.y, acc);
-      acc = fmaf(__uint_as_float(w8.w << 16), x1.z, acc);
-      acc = fmaf(__uint_as_float(w8.w & 0xFFFF0000u), x1.w, acc);
+    const float4* xs = reinterpret_cast<const float4*>(st + kBW);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const unsigned char* box = st + k * 4096 + lane * 128;
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        const uint4 w8 = *reinterpret_cast<const uint4*>(box + ((c ^ sw) << 4));
+        const float4 x0 = xs[k * 16 + 2 * c], x1 = xs[k * 16 + 2 * c + 1];
+        acc = fmaf(__uint_as_float(w8.x << 16), x0.x, acc);
+        acc = fmaf(__uint_as_float(w8.x & 0xFFFF0000u), x0.y, acc);
+        acc = fmaf(__uint_as_float(w8.y << 16), x0.z, acc);
+        acc = fmaf(__uint_as_float(w8.y & 0xFFFF0000u), x0.w, acc);
+        acc = fmaf(__uint_as_float(w8.z << 16), x1.x, acc);
+        acc = fmaf(__uint_as_float(w8.z & 0xFFFF0000u), x1.y, acc);
+        acc = fmaf(__uint_as_float(w8.w << 16), x1.z, acc);
+        acc = fmaf(__uint_as_float(w8.w & 0xFFFF0000u), x1.w, acc);
+      }
     }
     if (j % CPT == CPT - 1) {
       const long long tile = first + (j / CPT) * nwarps;
@@ -1792,6 +1817,7 @@ __global__ void __launch_bounds__(WARPS * 32, 1) bf16_stream_kernel(const Bf16Ge
     }
     __syncwarp();  // every lane is done with stage q before it is refilled
     if (j + kBStages < jobs) issue(j + kBStages, q);
+    __syncwarp();
     if (++q == kBStages) {
       q = 0;
       phase ^= 1u;
@@ -1829,18 +1855,29 @@ cudaError_t launch_fp8_gemv_splitk(const Fp8GemvArgs& a, float* part, cudaStream
 
 cudaError_t launch_bf16_gemv(const Bf16GemvArgs& a, int item_tokens, cudaStream_t st) {
   if (a.rows <= 0 || a.max_items <= 0) return cudaSuccess;
+  // few row tiles (grouped projections): the streaming kernel keeps more
+  // bytes in flight per warp; many tiles (the vocab head): the LDG kernel's
+  // full occupancy does better
+  // the streaming kernel when the matrices are stacked at their natural pitch
+  // (one tensor map covers every item's matrix)
+  const long long n_mats = a.w_stride ? a.max_items : 1;
   if (item_tokens == 1 && a.rows % 32 == 0 && a.in % kBCols == 0 && aligned(a.W, 16) &&
-      (a.w_stride * 2) % 16 == 0 && aligned(a.x, 16) && a.ldx % 4 == 0) {
-    constexpr int WARPS = 2;
-    const size_t smem = static_cast<size_t>(WARPS) * kBStages * kBStage;
-    cudaError_t e = set_max_dynamic_smem(reinterpret_cast<const void*>(bf16_stream_kernel<WARPS>),
-                                         static_cast<int>(smem));
-    if (e != cudaSuccess) return e;
-    const long long tiles = static_cast<long long>(a.max_items) * (a.rows / 32);
-    const int grid = static_cast<int>(std::max<long long>(
-        1, std::min<long long>(sm_count(), (tiles + WARPS - 1) / WARPS)));
-    return launch_pdl(bf16_stream_kernel<WARPS>, dim3(grid), dim3(WARPS * 32), smem, st, a,
-                      device_error_word());
+      (a.w_stride == 0 || a.w_stride == static_cast<size_t>(a.rows) * a.in) && aligned(a.x, 16) &&
+      a.ldx % 4 == 0) {
+    CUtensorMap wmap;
+    if (make_tma_map_u8(&wmap, a.W, static_cast<uint64_t>(a.in) * 2,
+                        static_cast<uint64_t>(n_mats) * a.rows, 128, 32, true)) {
+      constexpr int WARPS = 4;
+      const size_t smem = static_cast<size_t>(WARPS) * kBStages * kBStage + 1024;
+      cudaError_t e = set_max_dynamic_smem(reinterpret_cast<const void*>(bf16_stream_kernel<WARPS>),
+                                           static_cast<int>(smem));
+      if (e != cudaSuccess) return e;
+      const long long tiles = static_cast<long long>(a.max_items) * (a.rows / 32);
+      const int grid = static_cast<int>(std::max<long long>(
+          1, std::min<long long>(sm_count(), (tiles + WARPS - 1) / WARPS)));
+      return launch_pdl(bf16_stream_kernel<WARPS>, dim3(grid), dim3(WARPS * 32), smem, st, wmap,
+                        a, device_error_word());
+    }
   }
   const bool vec_ok = (a.in % 16 == 0) && aligned(a.W, 32) && aligned(a.x, 32) &&
                       (a.ldx % 8 == 0);

@@ -785,7 +785,9 @@ for _n, _r, _a in (("dsv4cuda_decoder_create", C.c_int, [vp, vp, vp, vp]),
                    ("dsv4cuda_decoder_logits", C.c_void_p, [vp]),
                    ("dsv4cuda_decoder_argmax", C.c_void_p, [vp]),
                    ("dsv4cuda_decoder_read", C.c_int, [vp, vp, vp]),
-                   ("dsv4cuda_decoder_cache", C.c_int, [vp, C.c_int, vp])):
+                   ("dsv4cuda_decoder_cache", C.c_int, [vp, C.c_int, vp]),
+                   ("dsv4cuda_decoder_step_kernels", C.c_int, [vp]),
+                   ("dsv4cuda_decoder_set_moe_layers", C.c_int, [vp, vp, C.c_int])):
     getattr(lib, _n).restype = _r
     getattr(lib, _n).argtypes = _a
 
@@ -833,6 +835,13 @@ class Decoder:
         """Step with token / position from device int32 tensors (capturable)."""
         if lib.dsv4cuda_decoder_step_device(self.handle, token.data_ptr(), position.data_ptr(),
                                             _stream(stream)) != 0:
+            raise Dsv4CudaError(lib.dsv4cuda_decoder_last_error().decode())
+
+    def set_moe_layers(self, moe_layers):
+        """Expert parallelism: one EP-attached MoeLayer per decoder layer."""
+        arr = (vp * max(len(moe_layers), 1))(*[m.handle for m in moe_layers])
+        self._ep = list(moe_layers)
+        if lib.dsv4cuda_decoder_set_moe_layers(self.handle, arr, len(moe_layers)) != 0:
             raise Dsv4CudaError(lib.dsv4cuda_decoder_last_error().decode())
 
     def read(self):

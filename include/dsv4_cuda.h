@@ -558,6 +558,14 @@ int dsv4cuda_decoder_create(dsv4cuda_decoder **out, const dsv4cuda_decoder_confi
                             const dsv4cuda_layer_weights *layers);
 void dsv4cuda_decoder_destroy(dsv4cuda_decoder *D);
 const char *dsv4cuda_decoder_last_error(void);
+/* Expert parallelism: layers[i] (n == n_layers) is an EP-attached MoE layer
+ * (dsv4cuda_moe_create_device_ep + dsv4cuda_moe_ep_attach, max_tokens >=
+ * world) that layer i's MoE block runs through, token-parallel: each rank's
+ * decoder brings its own token, the tokens of all ranks are routed
+ * together, every rank computes its own experts and each slot returns to
+ * its token's owner over peer memory (dsv4cuda_moe_forward_ep_tokens). All
+ * ranks step in lockstep. n == 0 returns to the local MoE weights. */
+int dsv4cuda_decoder_set_moe_layers(dsv4cuda_decoder *D, dsv4cuda_moe_layer *const *layers, int n);
 /* Clears the latent rings (dsv4_model_reset_context). Async on stream. */
 int dsv4cuda_decoder_reset(dsv4cuda_decoder *D, void *stream);
 /* dsv4_forward_token: host token/position in, host logits[vocab] (may be
@@ -573,6 +581,9 @@ int dsv4cuda_decoder_step(dsv4cuda_decoder *D, void *stream);
 /* Copies device token/position into the slots, then steps. */
 int dsv4cuda_decoder_step_device(dsv4cuda_decoder *D, const int *token, const int *position,
                                  void *stream);
+/* Number of kernels one step launches (counted from a captured graph of
+ * one step, which is not run), or -1. */
+int dsv4cuda_decoder_step_kernels(dsv4cuda_decoder *D);
 /* Waits for the device, then copies the last step's logits[vocab] and
  * argmax to host memory (either may be NULL). */
 int dsv4cuda_decoder_read(dsv4cuda_decoder *D, float *logits, int *next_token);
