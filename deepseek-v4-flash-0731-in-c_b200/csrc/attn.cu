@@ -54,28 +54,8 @@ __global__ void kv_write_kernel(Fp8KvCache c, const float* __restrict__ kv,
   const float* x = kv + static_cast<size_t>(p) * d;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int groups = c.nope / 64;
-  for (int g = warp; g < groups; g += blockDim.x >> 5) {
-    const float a = x[g * 64 + lane], b = x[g * 64 + 32 + lane];
-    const float amax = warp_max(fmaxf(fabsf(a), fabsf(b)));
-    const float scale = pow2_scale_448(amax);
-    const float inv = 1.0f / scale;  // exact: scale is a normal power of two
-    uint8_t code[2];
-    const float v[2] = {a, b};
-#pragma unroll
-    for (int k = 0; k < 2; ++k) {
-      float q = v[k] * inv;
-      q = fminf(fmaxf(q, -448.0f), 448.0f);
-      unsigned short t;
-      asm("{ .reg .b16 h; cvt.rn.satfinite.e4m3x2.f32 h, %1, %1; mov.b16 %0, h; }"
-          : "=h"(t) : "f"(q));
-      code[k] = (q == 0.0f) ? 0 : static_cast<uint8_t>(t & 0xFF);
-    }
-    uint8_t* dst = c.codes + r * c.nope + g * 64;
-    dst[lane] = code[0];
-    dst[32 + lane] = code[1];
-    if (lane == 0)
-      c.scales[r * kKvScaleSlots + g] = static_cast<uint8_t>((__float_as_uint(scale) >> 23) & 0xFF);
-  }
+  for (int g = warp; g < groups; g += blockDim.x >> 5)
+    kv_quant_group(c, r, g, x[g * 64 + lane], x[g * 64 + 32 + lane], lane);
   for (int i = threadIdx.x; i < c.rope_dim; i += blockDim.x) {
     const float v = bf16_round(x[c.nope + i]);
     c.rope[r * c.rope_dim + i] = static_cast<uint16_t>(__float_as_uint(v) >> 16);

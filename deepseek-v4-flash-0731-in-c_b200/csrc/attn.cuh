@@ -4,6 +4,10 @@
 #include <cstdint>
 #include <cuda_runtime.h>
 
+#ifdef __CUDACC__
+#include "dsv4_common.cuh"
+#endif
+
 namespace dsv4 {
 
 // Lossless FP8 layout of one cached latent. The reference stores each
@@ -24,6 +28,34 @@ struct Fp8KvCache {
 };
 
 constexpr int kKvScaleSlots = 8;
+
+#ifdef __CUDACC__
+// One 64-dim group g of a latent into cache row r, dsv4_act_quant_inplace
+// (group 64, mode 0; src/dsv4/dsv4_model.c:1386-1417): lane l of a whole warp
+// holds dims g*64 + l (a) and g*64 + 32 + l (b).
+__device__ __forceinline__ void kv_quant_group(const Fp8KvCache& c, long long r, int g, float a,
+                                               float b, int lane) {
+  const float amax = warp_max(fmaxf(fabsf(a), fabsf(b)));
+  const float scale = pow2_scale_448(amax);
+  const float inv = 1.0f / scale;  // exact: scale is a normal power of two
+  uint8_t code[2];
+  const float v[2] = {a, b};
+#pragma unroll
+  for (int k = 0; k < 2; ++k) {
+    float q = v[k] * inv;
+    q = fminf(fmaxf(q, -448.0f), 448.0f);
+    unsigned short t;
+    asm("{ .reg .b16 h; cvt.rn.satfinite.e4m3x2.f32 h, %1, %1; mov.b16 %0, h; }"
+        : "=h"(t) : "f"(q));
+    code[k] = (q == 0.0f) ? 0 : static_cast<uint8_t>(t & 0xFF);
+  }
+  uint8_t* dst = c.codes + r * c.nope + g * 64;
+  dst[lane] = code[0];
+  dst[32 + lane] = code[1];
+  if (lane == 0)
+    c.scales[r * kKvScaleSlots + g] = static_cast<uint8_t>((__float_as_uint(scale) >> 23) & 0xFF);
+}
+#endif
 
 // Quantise fp32 latents [n][nope + rope] (BF16-valued) into cache rows
 // row[n]: the reference's KV write (memcpy into the ring slot,

@@ -74,6 +74,10 @@ __device__ __forceinline__ float rms_factor(double ss, int n, float eps) {
   return 1.0f / sqrtf(__fadd_rn(static_cast<float>(ss / n), eps));
 }
 
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+  return (__float_as_uint(bf16_round(lo)) >> 16) | (__float_as_uint(bf16_round(hi)) & 0xFFFF0000u);
+}
+
 // ------------------------------------------------------------ kernels ----
 
 // embed_token (src/dsv4/dsv4_model.c:7478): every HC copy gets the BF16 row.
@@ -329,28 +333,436 @@ __global__ void __launch_bounds__(kHcThreads) hc_reduce_kernel(const HcReduceArg
   }
 }
 
-// rmsnorm_bf16 with a gain (src/dsv4/dsv4_model.c:4934), optionally followed
-// by dsv4_rope_apply_buf on the last 2 * half dims (:1547-1558). One CTA.
-__global__ void __launch_bounds__(256) rmsnorm_rope_kernel(const float* x, int n, const uint16_t* w,
-                                                           float eps, int half, const float* cosv,
-                                                           const float* sinv, float* y) {
-  __shared__ double red[8];
-  pdl_wait();
+// Sums 32 doubles over a warp with 31 shuffles instead of 160: at each
+// level a lane keeps half of its values and trades the other half with its
+// partner, so lane l ends with the warp's sum of value l. A fixed butterfly,
+// so the same bits on every run.
+__device__ __forceinline__ double warp_transpose_sum32(double (&v)[32]) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int s = 16; s >= 1; s >>= 1) {
+    const bool upper = (lane & s) != 0;
+#pragma unroll
+    for (int k = 0; k < s; ++k) {
+      const double send = upper ? v[k] : v[k + s];
+      const double keep = upper ? v[k + s] : v[k];
+      v[k] = keep + __shfl_xor_sync(0xffffffffu, send, s);
+    }
+  }
+  return v[0];
+}
+
+// One hyper-connection boundary in one launch (the fast mode's path):
+// hc_post of the branch that just finished (src/dsv4/dsv4_model.c:7165-7177;
+// skipped when branch is null), then hc_pre of the next one (:7123-7153, or
+// the model head :7190-7216): the HC mixes of the new state, the pre
+// weights (sigmoid of the first mult mixes), the weighted reduce, RMSNorm
+// with the gain (:4934) and, when xq is set, the per-128 FP8 quantisation of
+// the result (dsv4_quant_fp8_codes, :5580) for the projections that read it.
+// The mixes are written out; the Sinkhorn split of the post and comb mixes
+// (hc_sinkhorn_kernel) is only needed by the next boundary's post step and
+// runs beside the branch.
+// Thread = one column of the state (all mult rows): the post update needs
+// only the column, so it is done in place; the column's mix partials are
+// summed over the CTA into part[cta][32]; the last CTA to arrive (a ticket
+// counter it resets) sums the CTAs' partials in CTA order and finishes the
+// step. Weights (the mix rows, the norm gain, scale and base) are loaded
+// before the wait on the previous kernel.
+struct HcFusedArgs {
+  float* state;                 // [mult][hid], updated in place
+  const float* branch;          // [hid] or null (no post step)
+  const float* post_in;         // [mult] from the previous boundary's split
+  const float* comb_in;         // [mult][mult]
+  const float* fn;              // [rows][mult * hid]
+  int rows;                     // (2 + mult) * mult, or mult for the head
+  int head;
+  const float* scale;           // [3] (layer) or [1] (head)
+  const float* base;            // [rows]
+  int hid;
+  float hc_eps, rms_eps;
+  const uint16_t* norm;         // RMSNorm gain [hid] (BF16)
+  float* mix_out;               // [rows] the mixes (for the split)
+  float* out;                   // [hid]
+  __half* xq;                   // optional FP8-grid quant of out [hid]
+  float* xs;                    // [hid / 128] its scales
+  double* part;                 // [gridDim.x][32]
+  unsigned int* ticket;         // zero between launches
+};
+
+constexpr int kHcfThreads = 256;
+constexpr int kHcfMaxCtas = 32;  // hid <= 8192
+constexpr int kHcfPer = 8;       // tail chunks of 4 columns per thread: hid <= 8 * 256 * 4
+template <int M>
+__global__ void __launch_bounds__(kHcfThreads) hc_fused_kernel(const HcFusedArgs a) {
+  constexpr int R = (2 + M) * M;
+  __shared__ double red[kHcfThreads / 32][32];
+  __shared__ double tot[32];
+  __shared__ double red2[kHcfThreads / 32];
+  __shared__ float pre_s[kHcMultMax];
+  __shared__ int last;
+  __shared__ double pall[kHcfMaxCtas * 32];
   pdl_trigger();
-  double ss = 0.0;
-  for (int i = threadIdx.x; i < n; i += blockDim.x) ss += static_cast<double>(x[i]) * x[i];
-  ss = block_sum_d(ss, red);
-  const float r = rms_factor(ss, n, eps);
-  for (int i = threadIdx.x; i < n; i += blockDim.x)
-    y[i] = bf16_round(__fmul_rn(__fmul_rn(x[i], r), bf16_widen(w[i])));
-  if (half <= 0) return;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int i = blockIdx.x * kHcfThreads + tid;
+  const bool col = i < a.hid;
+  const size_t n = static_cast<size_t>(M) * a.hid;
+  float f[R][M];
+#pragma unroll
+  for (int j = 0; j < R; ++j)
+#pragma unroll
+    for (int m = 0; m < M; ++m)
+      f[j][m] = (col && j < a.rows) ? __ldg(a.fn + j * n + static_cast<size_t>(m) * a.hid + i) : 0.f;
+  // what the tail needs, in case this CTA is the last one: the gain row
+  // toward L2, scale and base into registers
+  for (int o = tid * 128; o < a.hid * 2; o += kHcfThreads * 128)
+    asm volatile("prefetch.global.L2 [%0];" ::"l"(reinterpret_cast<const char*>(a.norm) + o));
+  const float sc0 = __ldg(a.scale);
+  const float bs = lane < M ? __ldg(a.base + lane) : 0.f;
+  pdl_wait();
+  float v[M];
+#pragma unroll
+  for (int m = 0; m < M; ++m) v[m] = 0.f;
+  if (col) {
+    float old[M];
+#pragma unroll
+    for (int m = 0; m < M; ++m) old[m] = a.state[static_cast<size_t>(m) * a.hid + i];
+    if (a.branch) {
+      const float b = a.branch[i];
+#pragma unroll
+      for (int m = 0; m < M; ++m) {
+        float y = __fmul_rn(a.post_in[m], b);
+#pragma unroll
+        for (int k = 0; k < M; ++k) y = fmaf(a.comb_in[m * M + k], old[k], y);
+        v[m] = bf16_round(y);
+        a.state[static_cast<size_t>(m) * a.hid + i] = v[m];
+      }
+    } else {
+#pragma unroll
+      for (int m = 0; m < M; ++m) v[m] = old[m];
+    }
+  }
+  double p[32];
+  p[0] = 0.0;
+#pragma unroll
+  for (int m = 0; m < M; ++m) p[0] += static_cast<double>(v[m]) * v[m];
+#pragma unroll
+  for (int j = 0; j < 31; ++j) {
+    double s = 0.0;
+    if (j < R) {
+#pragma unroll
+      for (int m = 0; m < M; ++m) s += static_cast<double>(f[j][m]) * v[m];
+    }
+    p[1 + j] = s;
+  }
+  red[warp][lane] = warp_transpose_sum32(p);
   __syncthreads();
-  const int start = n - 2 * half;
-  for (int i = threadIdx.x; i < half; i += blockDim.x) {
-    const float x0 = y[start + 2 * i], x1 = y[start + 2 * i + 1];
-    const float c = cosv[i], s = sinv[i];
-    y[start + 2 * i] = bf16_round(__fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, s)));
-    y[start + 2 * i + 1] = bf16_round(__fadd_rn(__fmul_rn(x0, s), __fmul_rn(x1, c)));
+  if (tid < 32) {
+    double t = 0.0;
+#pragma unroll
+    for (int w = 0; w < kHcfThreads / 32; ++w) t += red[w][tid];
+    a.part[static_cast<size_t>(blockIdx.x) * 32 + tid] = t;
+  }
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) last = atomicAdd(a.ticket, 1u) == gridDim.x - 1;
+  __syncthreads();
+  if (!last) return;
+  __threadfence();
+  if (tid == 0) *a.ticket = 0u;
+  uint16_t g4[kHcfPer][4];
+#pragma unroll
+  for (int k = 0; k < kHcfPer; ++k) {
+    const int c0 = (k * kHcfThreads + tid) * 4;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) g4[k][e] = c0 < a.hid ? __ldg(a.norm + c0 + e) : uint16_t(0);
+  }
+  // every CTA's partials into shared memory (all loads in flight), then
+  // summed in CTA order
+  for (int e = tid; e < static_cast<int>(gridDim.x) * 32; e += kHcfThreads) pall[e] = __ldcg(a.part + e);
+  __syncthreads();
+  if (tid < 32) {
+    double t = 0.0;
+    for (unsigned b = 0; b < gridDim.x; ++b) t += pall[b * 32 + tid];
+    tot[tid] = t;
+  }
+  __syncthreads();
+  const float rs = rms_factor(tot[0], static_cast<int>(n), a.rms_eps);
+  if (warp == 0) {
+    const float mix = lane < a.rows ? static_cast<float>(tot[1 + lane]) * rs : 0.f;
+    if (lane < a.rows) a.mix_out[lane] = mix;
+    if (lane < M) {
+      const float z = mul_add(mix, sc0, bs);
+      // the head's pre (src/dsv4/dsv4_model.c:7203-7206) or the layer's
+      // (dsv4_hc_split, src/dsv4/dsv4_ops.c:418)
+      pre_s[lane] = (a.head ? 1.0f / (1.0f + expf_r1(-z)) : sigmoid_stable(z)) + a.hc_eps;
+    }
+  }
+  __syncthreads();
+  // bin = bf16(pre . state) over 4 consecutive columns per chunk, the norm
+  float y[kHcfPer][4];
+  double ss = 0.0;
+  // the state in rounds of four chunks, each round's loads issued together
+  float4 sv[4][M];
+#pragma unroll
+  for (int k = 0; k < kHcfPer; ++k) {
+    const int c0 = (k * kHcfThreads + tid) * 4;
+    if (k % 4 == 0) {
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) {
+        const int cc = ((k + kk) * kHcfThreads + tid) * 4;
+#pragma unroll
+        for (int m = 0; m < M; ++m)
+          sv[kk][m] = cc < a.hid ? __ldcg(reinterpret_cast<const float4*>(a.state + static_cast<size_t>(m) * a.hid + cc))
+                                 : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+    }
+#pragma unroll
+    for (int e = 0; e < 4; ++e) y[k][e] = 0.f;
+    if (c0 < a.hid) {
+      const float4* s = sv[k % 4];
+      float acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int m = 0; m < M; ++m) {
+        acc[0] = fmaf(pre_s[m], s[m].x, acc[0]);
+        acc[1] = fmaf(pre_s[m], s[m].y, acc[1]);
+        acc[2] = fmaf(pre_s[m], s[m].z, acc[2]);
+        acc[3] = fmaf(pre_s[m], s[m].w, acc[3]);
+      }
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        y[k][e] = bf16_round(acc[e]);
+        ss += static_cast<double>(y[k][e]) * y[k][e];
+      }
+    }
+  }
+  ss = block_sum_d(ss, red2);
+  const float r = rms_factor(ss, a.hid, a.rms_eps);
+#pragma unroll
+  for (int k = 0; k < kHcfPer; ++k) {
+    const int c0 = (k * kHcfThreads + tid) * 4;
+    if (k * kHcfThreads * 4 >= a.hid) break;  // uniform over the CTA
+    const float gn[4] = {bf16_widen(g4[k][0]), bf16_widen(g4[k][1]), bf16_widen(g4[k][2]),
+                         bf16_widen(g4[k][3])};
+    float o[4];
+    float amax = 0.f;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      o[e] = c0 < a.hid ? bf16_round(__fmul_rn(__fmul_rn(y[k][e], r), gn[e])) : 0.f;
+      amax = fmaxf(amax, fabsf(o[e]));
+    }
+    if (c0 < a.hid) *reinterpret_cast<float4*>(a.out + c0) = make_float4(o[0], o[1], o[2], o[3]);
+    if (a.xq) {
+      // this warp's 32 x 4 columns are one 128-column quantisation block
+      amax = warp_max(amax);
+      const float scale = pow2_scale_448(amax);
+      const float inv = 1.0f / scale;
+      if (c0 < a.hid) {
+        if (lane == 0) a.xs[c0 / 128] = scale;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          float q = o[e] * inv;
+          q = q > 448.f ? 448.f : (q < -448.f ? -448.f : q);
+          a.xq[c0 + e] = e4m3_round_f16(q);
+        }
+      }
+    }
+  }
+}
+
+// The Sinkhorn split of a layer boundary's mixes (dsv4_hc_split,
+// src/dsv4/dsv4_ops.c:412-460) into the post weights and the comb matrix
+// the next boundary's post step applies. One warp.
+template <int M>
+__global__ void hc_sinkhorn_kernel(const float* mix, const float* scale, const float* base, int iters,
+                                   float eps, float* post, float* comb) {
+  __shared__ float pre_s[kHcMultMax], post_s[kHcMultMax], comb_s[kHcMultMax * kHcMultMax];
+  hc_split_warp<M>(mix, scale, base, iters, eps, pre_s, post_s, comb_s);
+  __syncwarp();
+  const int lane = threadIdx.x;
+  if (lane < M) post[lane] = post_s[lane];
+  if (lane < M * M) comb[lane] = comb_s[lane];
+}
+
+// rmsnorm_bf16 with a gain (src/dsv4/dsv4_model.c:4934), optionally followed
+// by dsv4_rope_apply_buf on the last 2 * half dims (:1547-1558), kept in
+// shared memory and handed straight to its consumer in the same launch: the
+// per-128 FP8 quantisation of the q latent for wq_b (xq set), or the KV
+// write of the kv latent into its ring row (kv_quant_group per 64 dims, the
+// RoPE dims as BF16; cache.codes set). One CTA.
+struct NormTailArgs {
+  const float* x;
+  int n;
+  const uint16_t* w;
+  float eps;
+  int half;
+  const float* cosv;
+  const float* sinv;
+  __half* xq;             // optional: FP8-grid quant of the result
+  float* xs;
+  Fp8KvCache cache;       // optional (codes != null): KV write at *row
+  const long long* row;
+  // with the KV write: the window's rows as BF16, win[t] = the cached value
+  // of ring row idx[t] (zeros for padding); CTA 0 provides the new row,
+  // CTAs 1.. decode the others from the cache (null: no staging)
+  uint16_t* win;          // [n_win][nope + rope]
+  const int* idx;         // [n_win]
+  int n_win;
+};
+
+// Rows [t0, t1) of the window into win (warp = row, lane = 16 dims), all
+// but the ring row `skip` (being rewritten by CTA 0).
+__device__ void stage_window_rows(const NormTailArgs& a, long long skip) {
+  const Fp8KvCache& c = a.cache;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  const int d = c.nope + c.rope_dim, pieces = d / 16, np16 = c.nope / 16;
+  for (int t = (blockIdx.x - 1) * nw + warp; t < a.n_win; t += (gridDim.x - 1) * nw) {
+    const int r = a.idx[t];
+    if (r == skip || lane >= pieces) continue;
+    const bool live = r >= 0 && r < c.rows;
+    uint4 o0 = make_uint4(0u, 0u, 0u, 0u), o1 = o0;
+    if (live && lane < np16) {
+      const uint4 raw = *reinterpret_cast<const uint4*>(c.codes + static_cast<size_t>(r) * c.nope + 16 * lane);
+      const float sc = e8m0_decode(c.scales[static_cast<size_t>(r) * kKvScaleSlots + lane / 4]);
+      const uint32_t cw[4] = {raw.x, raw.y, raw.z, raw.w};
+      uint32_t o[8];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        uint32_t h01, h23;
+        asm("{ .reg .b16 lo, hi; mov.b32 {lo, hi}, %2; cvt.rn.f16x2.e4m3x2 %0, lo;"
+            " cvt.rn.f16x2.e4m3x2 %1, hi; }"
+            : "=r"(h01), "=r"(h23) : "r"(cw[k]));
+        const __half2 p01 = *reinterpret_cast<const __half2*>(&h01);
+        const __half2 p23 = *reinterpret_cast<const __half2*>(&h23);
+        o[2 * k] = pack_bf16x2(__fmul_rn(__low2float(p01), sc), __fmul_rn(__high2float(p01), sc));
+        o[2 * k + 1] = pack_bf16x2(__fmul_rn(__low2float(p23), sc), __fmul_rn(__high2float(p23), sc));
+      }
+      o0 = make_uint4(o[0], o[1], o[2], o[3]);
+      o1 = make_uint4(o[4], o[5], o[6], o[7]);
+    } else if (live) {
+      const uint16_t* rp = c.rope + static_cast<size_t>(r) * c.rope_dim + 16 * (lane - np16);
+      o0 = *reinterpret_cast<const uint4*>(rp);
+      o1 = *reinterpret_cast<const uint4*>(rp + 8);
+    }
+    uint4* dst = reinterpret_cast<uint4*>(a.win + static_cast<size_t>(t) * d + 16 * lane);
+    dst[0] = o0;
+    dst[1] = o1;
+  }
+}
+
+__global__ void __launch_bounds__(256) norm_tail_kernel(const NormTailArgs a) {
+  extern __shared__ float ys[];  // [n]
+  __shared__ double red[8];
+  pdl_trigger();
+  if (blockIdx.x > 0) {
+    pdl_wait();
+    stage_window_rows(a, *a.row);
+    return;
+  }
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  // up to kPer values per thread in registers, all loads in flight at once
+  // (the gain before the wait: it is a weight); longer rows in rounds
+  constexpr int kPer = 4;
+  const int step = blockDim.x * kPer;
+  float g[kPer];
+#pragma unroll
+  for (int k = 0; k < kPer; ++k) {
+    const int i = tid + k * blockDim.x;
+    g[k] = i < a.n ? bf16_widen(a.w[i]) : 0.f;
+  }
+  pdl_wait();
+  double ss = 0.0;
+  for (int i0 = 0; i0 < a.n; i0 += step) {
+    float v[kPer];
+#pragma unroll
+    for (int k = 0; k < kPer; ++k) {
+      const int i = i0 + tid + k * blockDim.x;
+      v[k] = i < a.n ? a.x[i] : 0.f;
+    }
+#pragma unroll
+    for (int k = 0; k < kPer; ++k) {
+      const int i = i0 + tid + k * blockDim.x;
+      if (i < a.n) {
+        ss += static_cast<double>(v[k]) * v[k];
+        ys[i] = v[k];
+      }
+    }
+  }
+  ss = block_sum_d(ss, red);
+  const float r = rms_factor(ss, a.n, a.eps);
+  for (int i0 = 0; i0 < a.n; i0 += step) {
+#pragma unroll
+    for (int k = 0; k < kPer; ++k) {
+      const int i = i0 + tid + k * blockDim.x;
+      if (i < a.n)
+        ys[i] = bf16_round(__fmul_rn(__fmul_rn(ys[i], r), i0 == 0 ? g[k] : bf16_widen(a.w[i])));
+    }
+  }
+  __syncthreads();
+  if (a.half > 0) {
+    const int start = a.n - 2 * a.half;
+    for (int i = tid; i < a.half; i += blockDim.x) {
+      const float x0 = ys[start + 2 * i], x1 = ys[start + 2 * i + 1];
+      const float c = a.cosv[i], s = a.sinv[i];
+      ys[start + 2 * i] = bf16_round(__fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, s)));
+      ys[start + 2 * i + 1] = bf16_round(__fadd_rn(__fmul_rn(x0, s), __fmul_rn(x1, c)));
+    }
+    __syncthreads();
+  }
+  if (a.xq) {
+    for (int b = warp; b < (a.n + 127) / 128; b += blockDim.x >> 5) {
+      const int len = min(128, a.n - b * 128);
+      float v[4];
+      float amax = 0.f;
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const int i = lane + 32 * k;
+        v[k] = i < len ? ys[b * 128 + i] : 0.f;
+        amax = fmaxf(amax, fabsf(v[k]));
+      }
+      amax = warp_max(amax);
+      const float scale = pow2_scale_448(amax);
+      const float inv = 1.0f / scale;
+      if (lane == 0) a.xs[b] = scale;
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const int i = lane + 32 * k;
+        if (i >= len) continue;
+        float q = v[k] * inv;
+        q = q > 448.f ? 448.f : (q < -448.f ? -448.f : q);
+        a.xq[b * 128 + i] = e4m3_round_f16(q);
+      }
+    }
+  }
+  if (a.cache.codes) {
+    const long long rr = *a.row;
+    if (rr < 0 || rr >= a.cache.rows) return;
+    __shared__ int tw_s;  // the new row's window slot
+    if (tid == 0) tw_s = -1;
+    __syncthreads();
+    if (a.win)
+      for (int t = tid; t < a.n_win; t += blockDim.x)
+        if (a.idx[t] == rr) tw_s = t;
+    __syncthreads();
+    const int tw = tw_s;
+    const int d = a.cache.nope + a.cache.rope_dim;
+    for (int g = warp; g < a.cache.nope / 64; g += blockDim.x >> 5) {
+      kv_quant_group(a.cache, rr, g, ys[g * 64 + lane], ys[g * 64 + 32 + lane], lane);
+      if (tw >= 0) {
+        // the cached value of what was just written: bf16(e4m3 * 2^k)
+        __syncwarp();
+        const uint8_t* cd = a.cache.codes + rr * a.cache.nope + g * 64;
+        const float sc = e8m0_decode(a.cache.scales[rr * kKvScaleSlots + g]);
+        uint16_t* wr = a.win + static_cast<size_t>(tw) * d + g * 64;
+        wr[lane] = static_cast<uint16_t>(__float_as_uint(bf16_round(__fmul_rn(e4m3_decode(cd[lane]), sc))) >> 16);
+        wr[32 + lane] =
+            static_cast<uint16_t>(__float_as_uint(bf16_round(__fmul_rn(e4m3_decode(cd[32 + lane]), sc))) >> 16);
+      }
+    }
+    for (int i = tid; i < a.cache.rope_dim; i += blockDim.x) {
+      const uint16_t b = static_cast<uint16_t>(__float_as_uint(bf16_round(ys[a.cache.nope + i])) >> 16);
+      a.cache.rope[rr * a.cache.rope_dim + i] = b;
+      if (tw >= 0) a.win[static_cast<size_t>(tw) * d + a.cache.nope + i] = b;
+    }
   }
 }
 
@@ -359,21 +771,40 @@ __global__ void __launch_bounds__(256) rmsnorm_rope_kernel(const float* x, int n
 __global__ void __launch_bounds__(128) q_head_kernel(float* q, int d, float eps, int half,
                                                      const float* cosv, const float* sinv) {
   __shared__ double red[4];
-  pdl_wait();
+  __shared__ float qs[512];
   pdl_trigger();
+  pdl_wait();
   float* qh = q + static_cast<size_t>(blockIdx.x) * d;
+  // d <= 512: four values per thread, loaded together
+  float v[4];
   double ss = 0.0;
-  for (int i = threadIdx.x; i < d; i += blockDim.x) ss += static_cast<double>(qh[i]) * qh[i];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const int i = threadIdx.x + 128 * k;
+    v[k] = i < d ? qh[i] : 0.f;
+  }
+#pragma unroll
+  for (int k = 0; k < 4; ++k) ss += static_cast<double>(v[k]) * v[k];
   ss = block_sum_d(ss, red);
   const float rr = rms_factor(ss, d, eps);
-  for (int i = threadIdx.x; i < d; i += blockDim.x) qh[i] = bf16_round(__fmul_rn(qh[i], rr));
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const int i = threadIdx.x + 128 * k;
+    if (i < d) qs[i] = bf16_round(__fmul_rn(v[k], rr));
+  }
   __syncthreads();
   const int start = d - 2 * half;
   for (int i = threadIdx.x; i < half; i += blockDim.x) {
-    const float x0 = qh[start + 2 * i], x1 = qh[start + 2 * i + 1];
+    const float x0 = qs[start + 2 * i], x1 = qs[start + 2 * i + 1];
     const float c = cosv[i], s = sinv[i];
-    qh[start + 2 * i] = bf16_round(__fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, s)));
-    qh[start + 2 * i + 1] = bf16_round(__fadd_rn(__fmul_rn(x0, s), __fmul_rn(x1, c)));
+    qs[start + 2 * i] = bf16_round(__fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, s)));
+    qs[start + 2 * i + 1] = bf16_round(__fadd_rn(__fmul_rn(x0, s), __fmul_rn(x1, c)));
+  }
+  __syncthreads();
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const int i = threadIdx.x + 128 * k;
+    if (i < d) qh[i] = qs[i];
   }
 }
 
@@ -544,6 +975,144 @@ __global__ void __launch_bounds__(64) win_values_kernel(const WinAttnArgs a) {
   }
 }
 
+__device__ __forceinline__ void bf16x8_to_f32(const uint4 u, float (&f)[8]) {
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    f[2 * k] = __uint_as_float(w[k] << 16);
+    f[2 * k + 1] = __uint_as_float(w[k] & 0xFFFF0000u);
+  }
+}
+
+// The same attention for one head per CTA over the window staged as BF16
+// rows (NormTailArgs::win): each row lands in shared memory by one bulk
+// copy (rows padded by 8 elements so 16-byte reads of consecutive keys are
+// conflict-free); thread = key for the scores (the dimension-order chain),
+// warp 0 for the softmax, thread = dimension pairs for the values (the
+// key-order chains), then the division, BF16 and the inverse RoPE.
+constexpr int kWhThreads = 128;
+
+__host__ __device__ inline size_t win_head_smem(int n, int d) {
+  return static_cast<size_t>(n) * (d + 8) * 2 + static_cast<size_t>(d) * 4 +
+         static_cast<size_t>(3) * n * 4 + 16;
+}
+
+__global__ void __launch_bounds__(kWhThreads) win_head_kernel(const WinAttnArgs a, const uint16_t* win,
+                                                              unsigned int* err) {
+  extern __shared__ __align__(16) unsigned char wsm[];
+  __shared__ uint64_t bar;
+  __shared__ float den_s;
+  const int n = a.n, d = a.d, ldk = d + 8;
+  uint16_t* ks = reinterpret_cast<uint16_t*>(wsm);                                // [n][d + 8]
+  float* qs = reinterpret_cast<float*>(wsm + static_cast<size_t>(n) * ldk * 2);   // [d]
+  float* ss = qs + d;                                                              // [n]
+  float* ws = ss + n;                                                              // [n]
+  int* sidx = reinterpret_cast<int*>(ws + n);                                      // [n]
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int h = blockIdx.x;
+  if (tid == 0) {
+    mbar_init(&bar, 1);
+    mbar_fence_init();
+  }
+  __syncthreads();
+  pdl_trigger();
+  pdl_wait();
+  const uint32_t row_bytes = static_cast<uint32_t>(d) * 2;
+  if (tid == 0) mbar_arrive_expect_tx(&bar, row_bytes * static_cast<uint32_t>(n));
+  __syncthreads();
+  for (int t = tid; t < n; t += kWhThreads) {
+    bulk_g2s(ks + static_cast<size_t>(t) * ldk, win + static_cast<size_t>(t) * d, row_bytes, &bar);
+    sidx[t] = a.idx[t];
+  }
+  for (int i = tid; i < d / 4; i += kWhThreads)
+    reinterpret_cast<float4*>(qs)[i] = reinterpret_cast<const float4*>(a.q + static_cast<size_t>(h) * d)[i];
+  bool ok = mbar_wait(&bar, 0, err);
+  if (!__syncthreads_and(ok)) {
+    if (!ok) mbar_wait(&bar, 0, err);  // the copies in flight land before the CTA exits
+    return;
+  }
+  // scores
+  for (int t = tid; t < n; t += kWhThreads) {
+    const int r = sidx[t];
+    float st = -INFINITY;
+    if (r >= 0 && r < a.cache.rows) {
+      const uint16_t* kr = ks + static_cast<size_t>(t) * ldk;
+      float dot = 0.0f;
+#pragma unroll 4
+      for (int i = 0; i < d; i += 8) {
+        float kf[8];
+        bf16x8_to_f32(*reinterpret_cast<const uint4*>(kr + i), kf);
+        const float4 q0 = *reinterpret_cast<const float4*>(qs + i);
+        const float4 q1 = *reinterpret_cast<const float4*>(qs + i + 4);
+        dot = fmaf(q0.x, kf[0], dot);
+        dot = fmaf(q0.y, kf[1], dot);
+        dot = fmaf(q0.z, kf[2], dot);
+        dot = fmaf(q0.w, kf[3], dot);
+        dot = fmaf(q1.x, kf[4], dot);
+        dot = fmaf(q1.y, kf[5], dot);
+        dot = fmaf(q1.z, kf[6], dot);
+        dot = fmaf(q1.w, kf[7], dot);
+      }
+      st = __fmul_rn(dot, a.scale);
+    }
+    ss[t] = st;
+  }
+  __syncthreads();
+  if (warp == 0) {
+    float mx = -INFINITY;
+    for (int t = lane; t < n; t += 32) mx = fmaxf(mx, ss[t]);
+    mx = warp_max(mx);
+    for (int t = lane; t < n; t += 32) {
+      const float st = ss[t];
+      ws[t] = st != -INFINITY ? expf_r1(st - mx) : 0.0f;
+    }
+    __syncwarp();
+    if (lane == 0) {
+      float sum = expf_r1(a.sink[h] - mx);
+      for (int t = 0; t < n; ++t)
+        if (ss[t] != -INFINITY) sum += ws[t];
+      den_s = sum;
+    }
+    __syncwarp();
+    for (int t = lane; t < n; t += 32) ws[t] = bf16_round(ws[t]);
+  }
+  __syncthreads();
+  const float den = den_s;
+  const int start = d - a.rope_dim;
+  for (int p0 = tid; p0 < d / 2; p0 += 2 * kWhThreads) {
+    // two dimension pairs per pass: four independent key-order chains
+    const int p1 = p0 + kWhThreads;
+    const bool has1 = p1 < d / 2;
+    float o[2][2] = {{0.f, 0.f}, {0.f, 0.f}};
+#pragma unroll 4
+    for (int t = 0; t < n; ++t) {
+      const float wt = ws[t];
+      const uint16_t* vr = ks + static_cast<size_t>(t) * ldk;
+      const uint32_t v0 = *reinterpret_cast<const uint32_t*>(vr + 2 * p0);
+      const uint32_t v1 = has1 ? *reinterpret_cast<const uint32_t*>(vr + 2 * p1) : 0u;
+      o[0][0] = fmaf(wt, __uint_as_float(v0 << 16), o[0][0]);
+      o[0][1] = fmaf(wt, __uint_as_float(v0 & 0xFFFF0000u), o[0][1]);
+      o[1][0] = fmaf(wt, __uint_as_float(v1 << 16), o[1][0]);
+      o[1][1] = fmaf(wt, __uint_as_float(v1 & 0xFFFF0000u), o[1][1]);
+    }
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      if (u == 1 && !has1) break;
+      const int i = 2 * (u ? p1 : p0);
+      float x0 = bf16_round(o[u][0] / den), x1 = bf16_round(o[u][1] / den);
+      if (a.cosv && i >= start) {
+        const int k = (i - start) / 2;
+        const float cs = a.cosv[k], sn = a.sinv[k];
+        const float y0 = bf16_round(__fadd_rn(__fmul_rn(x0, cs), __fmul_rn(x1, sn)));
+        const float y1 = bf16_round(__fadd_rn(__fmul_rn(-x0, sn), __fmul_rn(x1, cs)));
+        x0 = y0;
+        x1 = y1;
+      }
+      *reinterpret_cast<float2*>(a.out + static_cast<size_t>(h) * d + i) = make_float2(x0, x1);
+    }
+  }
+}
+
 // Greedy token: argmax_logits (src/cli/dsv4_run.c:355; first maximum, strict
 // >) in two stages - each CTA finds its chunk's first maximum, then one warp
 // takes the chunks' results in chunk order with the same strict >. For
@@ -647,6 +1216,10 @@ struct dsv4cuda_decoder {
   int* d_pos = nullptr;
   float* state = nullptr;     // [mult][hid]
   double* part = nullptr;     // [nblk][kMixMax + 1]
+  unsigned int* hc_ticket = nullptr;  // last-CTA counter of hc_fused_kernel
+  float* mix = nullptr;       // [kMixMax] the last boundary's mixes
+  cudaStream_t hc_side = nullptr;      // the Sinkhorn split's stream
+  cudaEvent_t hc_fork = nullptr, hc_join = nullptr;
   int nblk = 0;
   float *post = nullptr, *comb = nullptr;
   float* x = nullptr;         // [hid] normed branch input
@@ -656,12 +1229,14 @@ struct dsv4cuda_decoder {
   float* qn = nullptr;        // [q_lora]
   float* q = nullptr;         // [H][d]
   float* kv = nullptr;        // [d]
-  float* kvn = nullptr;       // [d]
   float* o = nullptr;         // [H][d]
   float* kvdec = nullptr;     // [window][d] the window's cached values
   float* kvt = nullptr;       // [d][window] transposed
   float* fp8_part = nullptr;  // split-K FP8 GEMV partials [in / 128][rows]
+  unsigned int* tile_cnt = nullptr;  // split-K row-tile counters (zero between launches)
   size_t win_smem = 0;        // dynamic shared memory of win_scores_kernel
+  bool win_staged = false;    // the window attention runs as win_head_kernel
+  uint16_t* kvwin = nullptr;  // [window][head_dim] the window's rows as BF16
   float* att_s = nullptr;     // [H][window] scores
   float* att_w = nullptr;     // [H][window] BF16 weights
   float* att_den = nullptr;   // [H]
@@ -732,9 +1307,15 @@ void rope_tables(const dsv4cuda_decoder_config& c, std::vector<float>& cs, std::
     }
 }
 
+#define DEC_CHECK(expr)                             \
+  do {                                              \
+    cudaError_t e__ = (expr);                       \
+    if (e__ != cudaSuccess) return e__;             \
+  } while (0)
+
 cudaError_t fp8_gemv(const uint8_t* W, const uint8_t* S, int in, int rows, const __half* x,
                      const float* xs, int ld, float* y, const dsv4::GemvItem* item, const int* n_one,
-                     float* part, cudaStream_t st) {
+                     float* part, unsigned int* cnt, cudaStream_t st) {
   dsv4::Fp8GemvArgs a{};
   a.W[0] = W;
   a.S[0] = S;
@@ -746,19 +1327,40 @@ cudaError_t fp8_gemv(const uint8_t* W, const uint8_t* S, int in, int rows, const
   a.items = item;
   a.n_items = n_one;
   a.max_items = 1;
-  const cudaError_t e = dsv4::launch_fp8_gemv_splitk(a, part, st);
+  const cudaError_t e = dsv4::launch_fp8_gemv_splitk(a, part, st, cnt);
   return e == cudaErrorNotSupported ? dsv4::launch_fp8_gemv(a, false, 1, st) : e;
+}
+
+// Two projections of the same activations (wq_a and wkv) in one split-K
+// launch pair when their shapes allow, else one after the other.
+cudaError_t fp8_gemv2(const uint8_t* W0, const uint8_t* S0, int rows0, float* y0,
+                      const uint8_t* W1, const uint8_t* S1, int rows1, float* y1, int in,
+                      const __half* x, const float* xs, int ld, const dsv4::GemvItem* item,
+                      const int* n_one, float* part, unsigned int* cnt, cudaStream_t st) {
+  dsv4::Fp8GemvArgs a{};
+  a.W[0] = W0;
+  a.S[0] = S0;
+  a.W[1] = W1;
+  a.S[1] = S1;
+  a.in = in;
+  a.rows = rows0;
+  a.rows1 = rows1;
+  a.round_out = 1;
+  a.act = dsv4::QAct{x, xs, ld, nullptr};
+  a.Y[0] = y0;
+  a.Y[1] = y1;
+  a.items = item;
+  a.n_items = n_one;
+  a.max_items = 1;
+  const cudaError_t e = dsv4::launch_fp8_gemv_splitk(a, part, st, cnt);
+  if (e != cudaErrorNotSupported) return e;
+  DEC_CHECK(fp8_gemv(W0, S0, in, rows0, x, xs, ld, y0, item, n_one, part, cnt, st));
+  return fp8_gemv(W1, S1, in, rows1, x, xs, ld, y1, item, n_one, part, cnt, st);
 }
 
 cudaError_t quant(dsv4cuda_decoder* D, const float* x, int n, cudaStream_t st) {
   return dsv4::launch_quant_fp8(x, n, n, 1, D->xq, D->xs, D->ld, st);
 }
-
-#define DEC_CHECK(expr)                             \
-  do {                                              \
-    cudaError_t e__ = (expr);                       \
-    if (e__ != cudaSuccess) return e__;             \
-  } while (0)
 
 
 cudaError_t hc_pre(dsv4cuda_decoder* D, const float* fn, const float* scale, const float* base,
@@ -800,33 +1402,114 @@ cudaError_t hc_post(dsv4cuda_decoder* D, cudaStream_t st) {
                           D->cfg.hc_mult, hid);
 }
 
+// One hyper-connection boundary: hc_post of D->branch (when `post`), then
+// hc_pre of the next branch into D->x, and when xq is set its FP8 quant into
+// xq / xs. The fast mode runs it as one launch, with a layer boundary's
+// Sinkhorn split forked onto D->hc_side (joined by hc_join before the next
+// boundary); the exact mode keeps the sequential mix chains in launches of
+// their own.
+cudaError_t hc_boundary(dsv4cuda_decoder* D, bool post, const float* fn, const float* scale,
+                        const float* base, const uint16_t* norm, int head, __half* xq,
+                        float* xs, cudaStream_t st) {
+  const auto& c = D->cfg;
+  if (c.hc_exact) {
+    if (post) DEC_CHECK(hc_post(D, st));
+    DEC_CHECK(hc_pre(D, fn, scale, base, norm, head, st));
+    return xq ? dsv4::launch_quant_fp8(D->x, c.hidden, c.hidden, 1, xq, xs, c.hidden, st)
+              : cudaSuccess;
+  }
+  dsv4::HcFusedArgs a{};
+  a.state = D->state;
+  a.branch = post ? D->branch : nullptr;
+  a.post_in = D->post;
+  a.comb_in = D->comb;
+  a.fn = fn;
+  a.rows = head ? c.hc_mult : (2 + c.hc_mult) * c.hc_mult;
+  a.head = head;
+  a.scale = scale;
+  a.base = base;
+  a.hid = c.hidden;
+  a.hc_eps = c.hc_eps;
+  a.rms_eps = c.rms_eps;
+  a.norm = norm;
+  a.mix_out = D->mix;
+  a.out = D->x;
+  a.xq = xq;
+  a.xs = xs;
+  a.part = D->part;
+  a.ticket = D->hc_ticket;
+  const dim3 grid((c.hidden + dsv4::kHcfThreads - 1) / dsv4::kHcfThreads), block(dsv4::kHcfThreads);
+  cudaError_t e;
+  switch (c.hc_mult) {
+    case 1: e = dsv4::launch_pdl(dsv4::hc_fused_kernel<1>, grid, block, 0, st, a); break;
+    case 2: e = dsv4::launch_pdl(dsv4::hc_fused_kernel<2>, grid, block, 0, st, a); break;
+    case 3: e = dsv4::launch_pdl(dsv4::hc_fused_kernel<3>, grid, block, 0, st, a); break;
+    default: e = dsv4::launch_pdl(dsv4::hc_fused_kernel<4>, grid, block, 0, st, a); break;
+  }
+  if (e != cudaSuccess || head) return e;
+  // the split of the post / comb mixes beside the branch
+  DEC_CHECK(cudaEventRecord(D->hc_fork, st));
+  DEC_CHECK(cudaStreamWaitEvent(D->hc_side, D->hc_fork, 0));
+  const float* mx = D->mix;
+  switch (c.hc_mult) {
+    case 1: dsv4::hc_sinkhorn_kernel<1><<<1, 32, 0, D->hc_side>>>(mx, scale, base, c.hc_iters, c.hc_eps, D->post, D->comb); break;
+    case 2: dsv4::hc_sinkhorn_kernel<2><<<1, 32, 0, D->hc_side>>>(mx, scale, base, c.hc_iters, c.hc_eps, D->post, D->comb); break;
+    case 3: dsv4::hc_sinkhorn_kernel<3><<<1, 32, 0, D->hc_side>>>(mx, scale, base, c.hc_iters, c.hc_eps, D->post, D->comb); break;
+    default: dsv4::hc_sinkhorn_kernel<4><<<1, 32, 0, D->hc_side>>>(mx, scale, base, c.hc_iters, c.hc_eps, D->post, D->comb); break;
+  }
+  DEC_CHECK(cudaGetLastError());
+  return cudaEventRecord(D->hc_join, D->hc_side);
+}
+
+// Makes `st` wait for the last forked split (fast mode; a no-op otherwise).
+cudaError_t hc_join(dsv4cuda_decoder* D, cudaStream_t st) {
+  return D->cfg.hc_exact ? cudaSuccess : cudaStreamWaitEvent(st, D->hc_join, 0);
+}
+
 // attention_forward_impl for a compress-ratio-0 layer (src/dsv4/dsv4_model.c:
 // 5241-5429): writes the branch output [hid] into D->branch.
+// D->x arrives with its FP8 quant in D->xq / D->xs.
 cudaError_t attention(dsv4cuda_decoder* D, dsv4::Layer& L, cudaStream_t st) {
   const auto& c = D->cfg;
   const auto& w = L.w;
   const int H = c.n_heads, d = c.head_dim, ql = c.q_lora, half = c.rope_dim / 2;
   const int G = c.o_groups, ol = c.o_lora, hid = c.hidden;
-  // q: quant(x) -> wq_a -> q_norm -> quant -> wq_b -> per-head RMS + RoPE
-  DEC_CHECK(quant(D, D->x, hid, st));
-  DEC_CHECK(fp8_gemv(w.wq_a, w.wq_a_s, hid, ql, D->xq, D->xs, D->ld, D->qr, D->item1, D->n_one, D->fp8_part, st));
-  DEC_CHECK(dsv4::launch_pdl(dsv4::rmsnorm_rope_kernel, dim3(1), dim3(256), 0, st,
-                             static_cast<const float*>(D->qr), ql, w.q_norm, c.rms_eps, 0,
-                             static_cast<const float*>(nullptr), static_cast<const float*>(nullptr),
-                             D->qn));
-  // wkv reads quant(x) too: run it before the activation buffer is reused
-  DEC_CHECK(fp8_gemv(w.wkv, w.wkv_s, hid, d, D->xq, D->xs, D->ld, D->kv, D->item1, D->n_one, D->fp8_part, st));
-  DEC_CHECK(quant(D, D->qn, ql, st));
-  DEC_CHECK(fp8_gemv(w.wq_b, w.wq_b_s, ql, H * d, D->xq, D->xs, D->ld, D->q, D->item1, D->n_one, D->fp8_part, st));
+  // wq_a and wkv on quant(x); kv: kv_norm -> RoPE -> FP8 latent into the
+  // ring row of the position; q: q_norm -> quant -> wq_b -> per-head RMS + RoPE
+  DEC_CHECK(fp8_gemv2(w.wq_a, w.wq_a_s, ql, D->qr, w.wkv, w.wkv_s, d, D->kv, hid, D->xq, D->xs,
+                      D->ld, D->item1, D->n_one, D->fp8_part, D->tile_cnt, st));
+  dsv4::NormTailArgs kt{};
+  kt.x = D->kv;
+  kt.n = d;
+  kt.w = w.kv_norm;
+  kt.eps = c.rms_eps;
+  kt.half = half;
+  kt.cosv = D->cosv;
+  kt.sinv = D->sinv;
+  kt.cache = L.cache;
+  kt.row = D->row;
+  if (D->win_staged) {
+    kt.win = D->kvwin;
+    kt.idx = D->idx;
+    kt.n_win = c.window;
+  }
+  // CTA 0 writes the new latent; with staging, CTAs 1.. (eight rows each)
+  // decode the rest of the window
+  const int stage_ctas = D->win_staged ? (c.window + 7) / 8 : 0;
+  DEC_CHECK(dsv4::launch_pdl(dsv4::norm_tail_kernel, dim3(1 + stage_ctas), dim3(256),
+                             sizeof(float) * d, st, kt));
+  dsv4::NormTailArgs qt{};
+  qt.x = D->qr;
+  qt.n = ql;
+  qt.w = w.q_norm;
+  qt.eps = c.rms_eps;
+  qt.xq = D->xq;
+  qt.xs = D->xs;
+  DEC_CHECK(dsv4::launch_pdl(dsv4::norm_tail_kernel, dim3(1), dim3(256), sizeof(float) * ql, st, qt));
+  DEC_CHECK(fp8_gemv(w.wq_b, w.wq_b_s, ql, H * d, D->xq, D->xs, D->ld, D->q, D->item1, D->n_one, D->fp8_part, D->tile_cnt, st));
   DEC_CHECK(dsv4::launch_pdl(dsv4::q_head_kernel, dim3(H), dim3(128), 0, st, D->q, d, c.rms_eps,
                              half, static_cast<const float*>(D->cosv),
                              static_cast<const float*>(D->sinv)));
-  // kv: kv_norm -> RoPE -> FP8 latent into the ring row of the position
-  DEC_CHECK(dsv4::launch_pdl(dsv4::rmsnorm_rope_kernel, dim3(1), dim3(256), 0, st,
-                             static_cast<const float*>(D->kv), d, w.kv_norm, c.rms_eps, half,
-                             static_cast<const float*>(D->cosv), static_cast<const float*>(D->sinv),
-                             D->kvn));
-  DEC_CHECK(dsv4::kv_cache_write(L.cache, D->kvn, D->row, 1, st));
   // sparse_attn over the window, inverse RoPE (exact order)
   dsv4::WinAttnArgs wa{};
   wa.q = D->q;
@@ -846,15 +1529,24 @@ cudaError_t attention(dsv4cuda_decoder* D, dsv4::Layer& L, cudaStream_t st) {
   wa.w = D->att_w;
   wa.den = D->att_den;
   wa.out = D->o;
-  DEC_CHECK(dsv4::launch_pdl(dsv4::win_decode_kernel, dim3(c.window), dim3(128), 0, st, wa));
-  DEC_CHECK(dsv4::launch_pdl(
-      dsv4::win_scores_kernel,
-      dim3((H + dsv4::kWinHeads - 1) / dsv4::kWinHeads, (c.window + dsv4::kWinKeys - 1) / dsv4::kWinKeys),
-      dim3(dsv4::kWinHeads * 32), D->win_smem, st, wa));
-  DEC_CHECK(dsv4::launch_pdl(dsv4::win_softmax_kernel, dim3(H), dim3(256),
-                             sizeof(float) * c.window, st, wa));
-  DEC_CHECK(dsv4::launch_pdl(dsv4::win_values_kernel, dim3(H, (d / 2 + 63) / 64), dim3(64),
-                             sizeof(float) * c.window, st, wa));
+  // the attention boundary's split (consumed by the FFN boundary) joins here,
+  // long after it finished
+  DEC_CHECK(hc_join(D, st));
+  if (D->win_staged) {
+    DEC_CHECK(dsv4::launch_pdl(dsv4::win_head_kernel, dim3(H), dim3(dsv4::kWhThreads),
+                               dsv4::win_head_smem(c.window, d), st, wa,
+                               static_cast<const uint16_t*>(D->kvwin), dsv4::device_error_word()));
+  } else {
+    DEC_CHECK(dsv4::launch_pdl(dsv4::win_decode_kernel, dim3(c.window), dim3(128), 0, st, wa));
+    DEC_CHECK(dsv4::launch_pdl(
+        dsv4::win_scores_kernel,
+        dim3((H + dsv4::kWinHeads - 1) / dsv4::kWinHeads, (c.window + dsv4::kWinKeys - 1) / dsv4::kWinKeys),
+        dim3(dsv4::kWinHeads * 32), D->win_smem, st, wa));
+    DEC_CHECK(dsv4::launch_pdl(dsv4::win_softmax_kernel, dim3(H), dim3(256),
+                               sizeof(float) * c.window, st, wa));
+    DEC_CHECK(dsv4::launch_pdl(dsv4::win_values_kernel, dim3(H, (d / 2 + 63) / 64), dim3(64),
+                               sizeof(float) * c.window, st, wa));
+  }
   // grouped BF16 wo_a, then quant -> FP8 wo_b
   dsv4::Bf16GemvArgs ga{};
   ga.W = L.wo_a;
@@ -868,10 +1560,11 @@ cudaError_t attention(dsv4cuda_decoder* D, dsv4::Layer& L, cudaStream_t st) {
   ga.items = D->items_g;
   ga.n_items = D->n_groups;
   ga.max_items = G;
+  ga.static_items = 1;
   DEC_CHECK(dsv4::launch_bf16_gemv(ga, 1, st));
   DEC_CHECK(quant(D, D->oall, G * ol, st));
   return fp8_gemv(w.wo_b, w.wo_b_s, G * ol, hid, D->xq, D->xs, D->ld, D->branch, D->item1,
-                  D->n_one, D->fp8_part, st);
+                  D->n_one, D->fp8_part, D->tile_cnt, st);
 }
 
 // One decode step from device token/position into logits + argmax.
@@ -887,23 +1580,31 @@ cudaError_t step(dsv4cuda_decoder* D, cudaStream_t st) {
                              static_cast<const float*>(D->sin_tab), D->idx, D->row, D->cosv,
                              D->sinv));
   dsv4::MoeExecOptions opt;
+  opt.x_quantized = true;
+  if (!c.hc_exact) opt.join = D->hc_join;  // the FFN boundary's split, before the combine
   for (size_t li = 0; li < D->layers.size(); ++li) {
     auto& L = D->layers[li];
     const auto& w = L.w;
-    DEC_CHECK(hc_pre(D, w.hc_attn_fn, w.hc_attn_scale, w.hc_attn_base, w.attn_norm, 0, st));
+    DEC_CHECK(hc_boundary(D, li > 0, w.hc_attn_fn, w.hc_attn_scale, w.hc_attn_base, w.attn_norm,
+                          0, D->xq, D->xs, st));
     DEC_CHECK(attention(D, L, st));
-    DEC_CHECK(hc_post(D, st));
-    DEC_CHECK(hc_pre(D, w.hc_ffn_fn, w.hc_ffn_scale, w.hc_ffn_base, w.ffn_norm, 0, st));
-    if (!D->ep.empty()) {
+    // the MoE layer's input quant comes out of the boundary kernel (its
+    // shared-expert item for the one token was written at create)
+    const bool local = D->ep.empty();
+    DEC_CHECK(hc_boundary(D, true, w.hc_ffn_fn, w.hc_ffn_scale, w.hc_ffn_base, w.ffn_norm, 0,
+                          local ? D->moe_ws.xq : nullptr, local ? D->moe_ws.xs : nullptr, st));
+    if (!local) {
       if (dsv4cuda_moe_forward_ep_tokens(D->ep[li], D->x, 1, D->branch, st) != 0)
         return cudaErrorLaunchFailure;
+      DEC_CHECK(hc_join(D, st));
     } else {
       DEC_CHECK(dsv4::moe_forward(L.mc, L.mw, D->moe_ws, D->x, D->d_token, 1, D->branch, st, opt));
     }
-    DEC_CHECK(hc_post(D, st));
   }
-  // model_head + head_logits (src/dsv4/dsv4_model.c:7755-7760), argmax
-  DEC_CHECK(hc_pre(D, D->g.hc_head_fn, D->g.hc_head_scale, D->g.hc_head_base, D->g.norm, 1, st));
+  // the last layer's hc_post, model_head + head_logits (src/dsv4/dsv4_model.c:
+  // 7755-7760), argmax
+  DEC_CHECK(hc_boundary(D, true, D->g.hc_head_fn, D->g.hc_head_scale, D->g.hc_head_base,
+                        D->g.norm, 1, nullptr, nullptr, st));
   dsv4::Bf16GemvArgs ha{};
   ha.W = D->g.head;
   ha.in = hid;
@@ -915,6 +1616,7 @@ cudaError_t step(dsv4cuda_decoder* D, cudaStream_t st) {
   ha.items = D->item1;
   ha.n_items = D->n_one;
   ha.max_items = 1;
+  ha.static_items = 1;
   DEC_CHECK(dsv4::launch_bf16_gemv(ha, 1, st));
   const int chunks = std::min(dsv4::kArgmaxCtas, c.vocab);
   DEC_CHECK(dsv4::launch_pdl(dsv4::argmax_chunks_kernel, dim3(chunks), dim3(256), 0, st,
@@ -932,7 +1634,7 @@ bool cfg_ok(const dsv4cuda_decoder_config* c) {
          c->o_groups > 0 && (c->n_heads * c->head_dim) % c->o_groups == 0 && c->o_lora > 0 &&
          c->window > 0 && c->window % 4 == 0 && c->hc_mult > 0 && c->hc_mult <= 4 &&
          c->hc_iters > 0 &&
-         c->hidden <= 8 * dsv4::kHcThreads &&
+         c->hidden <= 8 * dsv4::kHcThreads && c->head_dim <= 512 &&
          c->max_context > 0 && c->moe.hidden == c->hidden;
 }
 
@@ -961,7 +1663,14 @@ DSV4_API int dsv4cuda_decoder_create(dsv4cuda_decoder** out, const dsv4cuda_deco
   chk(D->d_token = dalloc<int>(D, 1));
   chk(D->d_pos = dalloc<int>(D, 1));
   chk(D->state = dalloc<float>(D, n));
-  chk(D->part = dalloc<double>(D, static_cast<size_t>(D->nblk) * (dsv4::kMixMax + 1)));
+  chk(D->part = dalloc<double>(D, std::max(static_cast<size_t>(D->nblk) * (dsv4::kMixMax + 1),
+                                           static_cast<size_t>(c.hidden / dsv4::kHcfThreads + 1) * 32)));
+  chk(D->hc_ticket = dalloc<unsigned int>(D, 1));
+  chk(D->mix = dalloc<float>(D, dsv4::kMixMax));
+  if (ok && (cudaStreamCreateWithFlags(&D->hc_side, cudaStreamNonBlocking) != cudaSuccess ||
+             cudaEventCreateWithFlags(&D->hc_fork, cudaEventDisableTiming) != cudaSuccess ||
+             cudaEventCreateWithFlags(&D->hc_join, cudaEventDisableTiming) != cudaSuccess))
+    ok = false;
   chk(D->post = dalloc<float>(D, dsv4::kHcMultMax));
   chk(D->comb = dalloc<float>(D, dsv4::kHcMultMax * dsv4::kHcMultMax));
   chk(D->x = dalloc<float>(D, c.hidden));
@@ -971,7 +1680,6 @@ DSV4_API int dsv4cuda_decoder_create(dsv4cuda_decoder** out, const dsv4cuda_deco
   chk(D->qn = dalloc<float>(D, c.q_lora));
   chk(D->q = dalloc<float>(D, static_cast<size_t>(H) * d));
   chk(D->kv = dalloc<float>(D, d));
-  chk(D->kvn = dalloc<float>(D, d));
   chk(D->o = dalloc<float>(D, static_cast<size_t>(H) * d));
   chk(D->oall = dalloc<float>(D, static_cast<size_t>(c.o_groups) * c.o_lora));
   chk(D->kvdec = dalloc<float>(D, static_cast<size_t>(c.window) * d));
@@ -979,9 +1687,11 @@ DSV4_API int dsv4cuda_decoder_create(dsv4cuda_decoder** out, const dsv4cuda_deco
   {
     const size_t hid = c.hidden, ql = c.q_lora, hd = static_cast<size_t>(H) * d;
     const size_t go = static_cast<size_t>(c.o_groups) * c.o_lora;
-    const size_t np = std::max(std::max((hid + 127) / 128 * ql, (ql + 127) / 128 * hd),
-                               std::max((hid + 127) / 128 * d, (go + 127) / 128 * hid));
+    const size_t np = std::max(std::max((hid + 127) / 128 * (ql + d), (ql + 127) / 128 * hd),
+                               (go + 127) / 128 * hid);
     chk(D->fp8_part = dalloc<float>(D, np));
+    const size_t maxr = std::max(std::max(ql + d, hd), std::max(hid, go));
+    chk(D->tile_cnt = dalloc<unsigned int>(D, maxr / 32 + 1));
   }
   chk(D->att_s = dalloc<float>(D, static_cast<size_t>(H) * c.window));
   chk(D->att_w = dalloc<float>(D, static_cast<size_t>(H) * c.window));
@@ -1033,6 +1743,18 @@ DSV4_API int dsv4cuda_decoder_create(dsv4cuda_decoder** out, const dsv4cuda_deco
                                  static_cast<int>(D->win_smem)) != cudaSuccess) {
     dsv4cuda_decoder_destroy(D);
     return fail("dsv4cuda_decoder_create: head_dim %d needs too much shared memory", d);
+  }
+  {
+    // the one-launch window attention holds the window's rows in shared
+    // memory; larger windows keep the four-launch form
+    const size_t wsm = dsv4::win_head_smem(c.window, d);
+    D->win_staged = d % 16 == 0 && c.rope_dim % 16 == 0 && wsm <= 220 * 1024 &&
+                    dsv4::set_max_dynamic_smem(reinterpret_cast<const void*>(dsv4::win_head_kernel),
+                                               220 * 1024) == cudaSuccess;
+    if (D->win_staged && !(D->kvwin = dalloc<uint16_t>(D, static_cast<size_t>(c.window) * d))) {
+      dsv4cuda_decoder_destroy(D);
+      return fail("dsv4cuda_decoder_create: out of device memory");
+    }
   }
   // per layer: the FP8 latent ring, wo_a as BF16, the MoE layer's view
   const int nope = d - c.rope_dim;
@@ -1089,6 +1811,14 @@ DSV4_API int dsv4cuda_decoder_create(dsv4cuda_decoder** out, const dsv4cuda_deco
       return fail("dsv4cuda_decoder_create: out of device memory (MoE workspace)");
     }
     dsv4::moe_workspace_carve(&D->moe_ws, mc, 1, base);
+    // the one token's shared-expert item, written once: the steps hand the
+    // MoE layer an input that is already quantised
+    dsv4::GemvItem sh{};
+    sh.mat = 0;
+    sh.ntok = 1;
+    const int one = 1;
+    cudaMemcpy(D->moe_ws.items_sh, &sh, sizeof(sh), cudaMemcpyHostToDevice);
+    cudaMemcpy(D->moe_ws.counters + 3, &one, sizeof(int), cudaMemcpyHostToDevice);
   }
   const cudaError_t e = cudaDeviceSynchronize();
   if (e != cudaSuccess) {
@@ -1103,6 +1833,9 @@ DSV4_API void dsv4cuda_decoder_destroy(dsv4cuda_decoder* D) {
   if (!D) return;
   if (D->graph) cudaGraphExecDestroy(D->graph);
   if (D->graph_stream) cudaStreamDestroy(D->graph_stream);
+  if (D->hc_side) cudaStreamDestroy(D->hc_side);
+  if (D->hc_fork) cudaEventDestroy(D->hc_fork);
+  if (D->hc_join) cudaEventDestroy(D->hc_join);
   for (void* p : D->owned) cudaFree(p);
   delete D;
 }

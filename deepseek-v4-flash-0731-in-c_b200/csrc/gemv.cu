@@ -1655,25 +1655,68 @@ cudaError_t launch_fp8_gemv(const Fp8GemvArgs& a, bool pair, int item_tokens, cu
 // NaN-scaled blocks skipped, as dsv4_gemv_fp8_q does
 // (src/dsv4/dsv4_model.c:657-672). Same operations in the same order as the
 // other FP8 kernels, so the same bits.
+// The fold of a row tile in block order from every segment's partials
+// (fp8_fold_kernel's arithmetic, for the warp that finishes the tile).
+__device__ __forceinline__ float fp8_fold_tile(const Fp8GemvArgs& a, const float* part, int total,
+                                               int row, int CB) {
+  const int mat = row >= a.rows;
+  const int lrow = mat ? row - a.rows : row;
+  const GemvItem& it = a.items[0];
+  const float* qs = a.act.s + static_cast<size_t>(it.tok[0].x) * (a.act.ld / 128);
+  const uint8_t* sr = a.S[mat] + static_cast<size_t>(lrow / 128) * ((a.in + 127) / 128);
+  float acc = 0.0f;
+  for (int b0 = 0; b0 < CB; b0 += 16) {
+    float pv[16], sv[16];
+    uint32_t code[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const int b = b0 + j < CB ? b0 + j : CB - 1;
+      pv[j] = __ldcg(part + static_cast<size_t>(b) * total + row);
+      sv[j] = qs[b];
+      code[j] = sr[b];
+    }
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      if (b0 + j >= CB) break;
+      const float ws = e8m0_decode(code[j]);
+      if (!isnan(ws)) acc = fmaf(pv[j], sv[j] * ws, acc);
+    }
+  }
+  return acc;
+}
+
 __global__ void __launch_bounds__(128) fp8_partials_kernel(const Fp8GemvArgs a, int bps,
-                                                           float* part) {
-  pdl_wait();
+                                                           float* part, unsigned int* tile_cnt) {
   pdl_trigger();
   const int lane = threadIdx.x & 31;
   const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int CB = a.in / 128;
   const int nseg = (CB + bps - 1) / bps;
-  const int tiles = a.rows / 32;
-  if (gw >= tiles * nseg) return;
+  const int total = a.rows + a.rows1;
+  const int tiles = total / 32;
+  if (gw >= tiles * nseg) {
+    pdl_wait();
+    return;
+  }
   const int tile = gw / nseg, seg = gw % nseg;
   const int row = tile * 32 + lane;
+  const int mat = row >= a.rows;
+  const uint8_t* wr = a.W[mat] + static_cast<size_t>(mat ? row - a.rows : row) * a.in;
+  const int b0 = seg * bps, b1 = min(CB, (seg + 1) * bps);
+  // weights do not depend on the previous kernel: the first block into
+  // registers and the rest into L2 while it finishes
+  U8x32 w[4];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) w[k] = ldg32(wr + b0 * 128 + 32 * k);
+  for (int b = b0 + 1; b < b1; ++b) asm volatile("prefetch.global.L2 [%0];" ::"l"(wr + b * 128));
+  pdl_wait();
   const GemvItem& it = a.items[0];
   const __half* xr = a.act.x + static_cast<size_t>(it.tok[0].x) * a.act.ld;
-  const uint8_t* wr = a.W[0] + static_cast<size_t>(row) * a.in;
-  for (int b = seg * bps; b < min(CB, (seg + 1) * bps); ++b) {
-    U8x32 w[4];
+  for (int b = b0; b < b1; ++b) {
+    if (b > b0) {
 #pragma unroll
-    for (int k = 0; k < 4; ++k) w[k] = ldg32(wr + b * 128 + 32 * k);
+      for (int k = 0; k < 4; ++k) w[k] = ldg32(wr + b * 128 + 32 * k);
+    }
     float p = 0.0f;
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
@@ -1687,19 +1730,36 @@ __global__ void __launch_bounds__(128) fp8_partials_kernel(const Fp8GemvArgs a, 
       }
       p = fp8_chain32(w[k].w, x16, p);
     }
-    part[static_cast<size_t>(b) * a.rows + row] = p;
+    part[static_cast<size_t>(b) * total + row] = p;
   }
+  if (!tile_cnt) return;
+  // the last of the tile's segments to finish folds the tile
+  __threadfence();
+  __syncwarp();
+  unsigned int prev = 0;
+  if (lane == 0) prev = atomicAdd(tile_cnt + tile, 1u);
+  prev = __shfl_sync(0xffffffffu, prev, 0);
+  if (prev != static_cast<unsigned>(nseg - 1)) return;
+  __threadfence();
+  if (lane == 0) tile_cnt[tile] = 0u;  // zero again for the next launch
+  const float acc = fp8_fold_tile(a, part, total, row, CB);
+  const int rows_m = mat ? a.rows1 : a.rows;
+  a.Y[mat][static_cast<size_t>(it.tok[0].y) * rows_m + (mat ? row - a.rows : row)] =
+      a.round_out ? bf16_round(acc) : acc;
 }
 
 __global__ void __launch_bounds__(128) fp8_fold_kernel(const Fp8GemvArgs a, const float* part) {
-  pdl_wait();
   pdl_trigger();
+  pdl_wait();
+  const int total = a.rows + a.rows1;
   const int row = blockIdx.x * blockDim.x + threadIdx.x;
-  if (row >= a.rows) return;
+  if (row >= total) return;
+  const int mat = row >= a.rows;
+  const int lrow = mat ? row - a.rows : row;
   const int CB = a.in / 128;
   const GemvItem& it = a.items[0];
   const float* qs = a.act.s + static_cast<size_t>(it.tok[0].x) * (a.act.ld / 128);
-  const uint8_t* sr = a.S[0] + static_cast<size_t>(row / 128) * ((a.in + 127) / 128);
+  const uint8_t* sr = a.S[mat] + static_cast<size_t>(lrow / 128) * ((a.in + 127) / 128);
   float acc = 0.0f;
   for (int b0 = 0; b0 < CB; b0 += 8) {
     float pv[8], sv[8];
@@ -1707,7 +1767,7 @@ __global__ void __launch_bounds__(128) fp8_fold_kernel(const Fp8GemvArgs a, cons
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
       const int b = b0 + j < CB ? b0 + j : CB - 1;
-      pv[j] = part[static_cast<size_t>(b) * a.rows + row];
+      pv[j] = part[static_cast<size_t>(b) * total + row];
       sv[j] = qs[b];
       code[j] = sr[b];
     }
@@ -1718,13 +1778,14 @@ __global__ void __launch_bounds__(128) fp8_fold_kernel(const Fp8GemvArgs a, cons
       if (!isnan(ws)) acc = fmaf(pv[j], sv[j] * ws, acc);
     }
   }
-  a.Y[0][static_cast<size_t>(it.tok[0].y) * a.rows + row] = a.round_out ? bf16_round(acc) : acc;
+  const int rows_m = mat ? a.rows1 : a.rows;
+  a.Y[mat][static_cast<size_t>(it.tok[0].y) * rows_m + lrow] = a.round_out ? bf16_round(acc) : acc;
 }
 
 // ------------------------------------------------------- BF16 stream ----
 // Streaming BF16 GEMV for one-token items (the decode step's grouped wo_a and
 // vocab head). A warp owns 32 rows (lane = row) and walks them in 256-column
-// chunks through a ring of kBStages shared-memory stages: per chunk one lane
+// chunks through a ring of STAGES shared-memory stages: per chunk one lane
 // issues four 2-D TMA boxes of [32 rows x 128 B] with the 128-byte swizzle
 // (the matrix read 128 contiguous bytes per row at a time; the swizzle makes
 // the lanes' 16-byte reads conflict-free) and a bulk copy of the chunk's
@@ -1732,29 +1793,28 @@ __global__ void __launch_bounds__(128) fp8_fold_kernel(const Fp8GemvArgs a, cons
 // lane runs its row's fmaf chain in column order, the reference's order, so
 // the result is the LDG kernel's bit for bit.
 constexpr int kBCols = 256;
-constexpr int kBStages = 3;
 constexpr int kBW = 32 * kBCols * 2;             // four swizzled [32][128 B] boxes
 constexpr int kBStage = kBW + kBCols * 4;        // + the activation chunk
 
-template <int WARPS>
+template <int WARPS, int STAGES>
 __global__ void __launch_bounds__(WARPS * 32, 1)
     bf16_stream_kernel(const __grid_constant__ CUtensorMap wmap, const Bf16GemvArgs a,
                        unsigned int* err) {
   extern __shared__ __align__(1024) unsigned char smem[];
-  __shared__ uint64_t bars_all[WARPS][kBStages];
+  __shared__ uint64_t bars_all[WARPS][STAGES];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   unsigned char* const sbase = smem + ((1024u - (smem_addr(smem) & 1023u)) & 1023u);
-  unsigned char* wbase = sbase + static_cast<size_t>(warp) * kBStages * kBStage;
+  unsigned char* wbase = sbase + static_cast<size_t>(warp) * STAGES * kBStage;
   uint64_t* bars = bars_all[warp];
   if (lane == 0) {
 #pragma unroll
-    for (int q = 0; q < kBStages; ++q) mbar_init(&bars[q], 1);
+    for (int q = 0; q < STAGES; ++q) mbar_init(&bars[q], 1);
     mbar_fence_init();
     if (warp == 0) tma_prefetch_desc(&wmap);
   }
   __syncthreads();
-  pdl_wait();
   pdl_trigger();
+  if (!a.static_items) pdl_wait();
   const int n_items = load_n_items(a.n_items, a.max_items);
   const int rblocks = a.rows / 32;
   const long long tiles = static_cast<long long>(n_items) * rblocks;
@@ -1763,7 +1823,9 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
   const long long first = static_cast<long long>(warp) * gridDim.x + blockIdx.x;
   const long long my_tiles = tiles > first ? (tiles - first + nwarps - 1) / nwarps : 0;
   const long long jobs = my_tiles * CPT;
-  auto issue = [&](long long j, int q) {
+  // a job's weight boxes and its activation chunk land on one mbarrier; the
+  // weights of the first stages may be requested before the wait
+  auto issue_w = [&](long long j, int q) {
     if (lane != 0) return;
     const long long tile = first + (j / CPT) * nwarps;
     const int chunk = static_cast<int>(j % CPT);
@@ -1775,10 +1837,24 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
     const int y = it.mat * a.rows + rb * 32;
 #pragma unroll
     for (int k = 0; k < 4; ++k) tma_load_2d(st + k * 4096, &wmap, chunk * 512 + k * 128, y, &bars[q]);
+  };
+  auto issue_x = [&](long long j, int q) {
+    if (lane != 0) return;
+    const long long tile = first + (j / CPT) * nwarps;
+    const int chunk = static_cast<int>(j % CPT);
+    const int item = static_cast<int>(tile / rblocks);
+    const GemvItem& it = a.items[item];
+    unsigned char* st = wbase + q * kBStage;
     bulk_g2s(st + kBW, a.x + static_cast<size_t>(it.tok[0].x) * a.ldx + chunk * kBCols, kBCols * 4,
              &bars[q]);
   };
-  for (long long j = 0; j < jobs && j < kBStages; ++j) issue(j, static_cast<int>(j));
+  auto issue = [&](long long j, int q) {
+    issue_w(j, q);
+    issue_x(j, q);
+  };
+  for (long long j = 0; j < jobs && j < STAGES; ++j) issue_w(j, static_cast<int>(j));
+  if (a.static_items) pdl_wait();
+  for (long long j = 0; j < jobs && j < STAGES; ++j) issue_x(j, static_cast<int>(j));
   __syncwarp();
   float acc = 0.0f;
   int q = 0;
@@ -1816,9 +1892,9 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
       acc = 0.0f;
     }
     __syncwarp();  // every lane is done with stage q before it is refilled
-    if (j + kBStages < jobs) issue(j + kBStages, q);
+    if (j + STAGES < jobs) issue(j + STAGES, q);
     __syncwarp();
-    if (++q == kBStages) {
+    if (++q == STAGES) {
       q = 0;
       phase ^= 1u;
     }
@@ -1827,19 +1903,22 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
     // drain this warp's copies still in flight before the CTA exits
     uint32_t ph = phase;
     int k = q;
-    for (long long r = j + 1; r < jobs && r < j + kBStages; ++r) {
-      if (++k == kBStages) { k = 0; ph ^= 1u; }
+    for (long long r = j + 1; r < jobs && r < j + STAGES; ++r) {
+      if (++k == STAGES) { k = 0; ph ^= 1u; }
       mbar_wait(&bars[k], ph, err);
     }
   }
 }
 
-cudaError_t launch_fp8_gemv_splitk(const Fp8GemvArgs& a, float* part, cudaStream_t st) {
+cudaError_t launch_fp8_gemv_splitk(const Fp8GemvArgs& a, float* part, cudaStream_t st,
+                                   unsigned int* tile_cnt) {
   if (a.rows <= 0) return cudaSuccess;
   if (a.rows % 32 != 0 || a.in % 128 != 0 || !aligned(a.W[0], 32) || !aligned(a.act.x, 32) ||
-      a.act.ld % 128 != 0 || a.act.x32 || a.max_items != 1)
+      a.act.ld % 128 != 0 || a.act.x32 || a.max_items != 1 || a.rows1 < 0 || a.rows1 % 32 != 0 ||
+      (a.rows1 > 0 && !aligned(a.W[1], 32)))
     return cudaErrorNotSupported;
-  const int CB = a.in / 128, tiles = a.rows / 32;
+  const int total = a.rows + a.rows1;
+  const int CB = a.in / 128, tiles = total / 32;
   // about 16 warps per SM, at least one block per warp
   const long long target = 16LL * sm_count();
   int bps = static_cast<int>(std::max<long long>(1, (static_cast<long long>(tiles) * CB + target - 1) / target));
@@ -1847,9 +1926,9 @@ cudaError_t launch_fp8_gemv_splitk(const Fp8GemvArgs& a, float* part, cudaStream
   const int nseg = (CB + bps - 1) / bps;
   const long long warps = static_cast<long long>(tiles) * nseg;
   cudaError_t e = launch_pdl(fp8_partials_kernel, dim3(static_cast<unsigned>((warps + 3) / 4)),
-                             dim3(128), 0, st, a, bps, part);
-  if (e != cudaSuccess) return e;
-  return launch_pdl(fp8_fold_kernel, dim3((a.rows + 127) / 128), dim3(128), 0, st, a,
+                             dim3(128), 0, st, a, bps, part, tile_cnt);
+  if (e != cudaSuccess || tile_cnt) return e;
+  return launch_pdl(fp8_fold_kernel, dim3((total + 127) / 128), dim3(128), 0, st, a,
                     static_cast<const float*>(part));
 }
 
@@ -1867,16 +1946,20 @@ cudaError_t launch_bf16_gemv(const Bf16GemvArgs& a, int item_tokens, cudaStream_
     CUtensorMap wmap;
     if (make_tma_map_u8(&wmap, a.W, static_cast<uint64_t>(a.in) * 2,
                         static_cast<uint64_t>(n_mats) * a.rows, 128, 32, true)) {
-      constexpr int WARPS = 4;
-      const size_t smem = static_cast<size_t>(WARPS) * kBStages * kBStage + 1024;
-      cudaError_t e = set_max_dynamic_smem(reinterpret_cast<const void*>(bf16_stream_kernel<WARPS>),
-                                           static_cast<int>(smem));
-      if (e != cudaSuccess) return e;
       const long long tiles = static_cast<long long>(a.max_items) * (a.rows / 32);
-      const int grid = static_cast<int>(std::max<long long>(
-          1, std::min<long long>(sm_count(), (tiles + WARPS - 1) / WARPS)));
-      return launch_pdl(bf16_stream_kernel<WARPS>, dim3(grid), dim3(WARPS * 32), smem, st, wmap,
-                        a, device_error_word());
+      // few tiles (grouped wo_a): two warps per SM, each with a deep ring
+      // (a warp's 32 fmaf chains are latency-bound, so its copies must run
+      // far ahead); many tiles (the vocab head): four warps, three stages
+      auto run = [&](auto kern, int warps, int stages) -> cudaError_t {
+        const size_t smem = static_cast<size_t>(warps) * stages * kBStage + 1024;
+        cudaError_t e = set_max_dynamic_smem(reinterpret_cast<const void*>(kern), static_cast<int>(smem));
+        if (e != cudaSuccess) return e;
+        const int grid = static_cast<int>(std::max<long long>(
+            1, std::min<long long>(sm_count(), (tiles + warps - 1) / warps)));
+        return launch_pdl(kern, dim3(grid), dim3(warps * 32), smem, st, wmap, a, device_error_word());
+      };
+      if (tiles <= 2LL * sm_count()) return run(bf16_stream_kernel<2, 6>, 2, 6);
+      return run(bf16_stream_kernel<4, 3>, 4, 3);
     }
   }
   const bool vec_ok = (a.in % 16 == 0) && aligned(a.W, 32) && aligned(a.x, 32) &&

@@ -62,6 +62,9 @@ struct Fp8GemvArgs {
   // router and the routed experts): two warps per CTA on half as many SMs
   int beside = 0;
   unsigned int* err = nullptr;  // device error word (null: the library's default)
+  // split-K kernels only: a second matrix W[1] / S[1] of rows1 rows (same
+  // input) whose outputs go to Y[1]; one launch computes both
+  int rows1 = 0;
 };
 
 struct Bf16GemvArgs {
@@ -75,6 +78,10 @@ struct Bf16GemvArgs {
   const GemvItem* items;
   const int* n_items;
   int max_items;
+  // 1: items / n_items are fixed before the launch (not written by the
+  // previous kernel), so the streaming kernel starts its weight copies
+  // before waiting on that kernel
+  int static_items = 0;
 };
 
 cudaError_t launch_fp4_gemv(const Fp4GemvArgs& a, bool pair, int item_tokens,
@@ -86,7 +93,10 @@ cudaError_t launch_bf16_gemv(const Bf16GemvArgs& a, int item_tokens,
 // One-token, one-item FP8 GEMV split over 128-column blocks (more warps for
 // matrices with few row tiles); part holds in/128 * rows floats of scratch.
 // cudaErrorNotSupported when the shape or alignment does not fit.
-cudaError_t launch_fp8_gemv_splitk(const Fp8GemvArgs& a, float* part, cudaStream_t st);
+// tile_cnt (zeroed, rows / 32 counters): the last segment of each row tile
+// folds it in the same launch; null: a separate fold launch.
+cudaError_t launch_fp8_gemv_splitk(const Fp8GemvArgs& a, float* part, cudaStream_t st,
+                                   unsigned int* tile_cnt = nullptr);
 
 // x [rows][n] fp32 -> E4M3 grid (f16) + per-128 scales (dsv4_quant_fp8_codes).
 cudaError_t launch_quant_fp8(const float* x, int ldx, int n, int rows, __half* qx,

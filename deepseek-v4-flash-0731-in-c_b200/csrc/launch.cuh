@@ -9,6 +9,7 @@
 // kernel calls pdl_wait() before its first read of data another kernel
 // produced.
 #pragma once
+#include <cstdlib>
 #include <mutex>
 #include <utility>
 #include <vector>
@@ -56,6 +57,17 @@ __device__ __forceinline__ void pdl_trigger() {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
+// DSV4_PDL=0 in the environment launches every kernel the ordinary way
+// (each starts after the previous one has finished): a profile then shows
+// each kernel's own duration.
+inline bool pdl_enabled() {
+  static const bool on = [] {
+    const char* v = std::getenv("DSV4_PDL");
+    return !(v && v[0] == '0');
+  }();
+  return on;
+}
+
 template <typename... KArgs, typename... Args>
 cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
                        cudaStream_t st, Args&&... args) {
@@ -69,7 +81,7 @@ cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t s
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
   return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 

@@ -327,8 +327,14 @@ __device__ void quant_rows(const RouterArgs& a, int gw, int nw) {
 
 __global__ void __launch_bounds__(kLogitWarps * 32) router_logits_kernel(const RouterArgs a) {
   __shared__ float seg_tot[kLogitWarps], seg_abs[kLogitWarps], seg_p[kLogitWarps];
-  pdl_wait();  // x comes from the previous kernel
   pdl_trigger();
+  {
+    // the expert's gate row toward L2 while the previous kernel finishes
+    const char* gr = reinterpret_cast<const char*>(a.gate + static_cast<size_t>(blockIdx.x) * a.H);
+    for (int o = threadIdx.x * 128; o < a.H * 2; o += blockDim.x * 128)
+      asm volatile("prefetch.global.L2 [%0];" ::"l"(gr + o));
+  }
+  pdl_wait();  // x comes from the previous kernel
   if (a.items_sh && blockIdx.x == 0 && blockIdx.y == 0) write_shared_items(a);
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int e = blockIdx.x, t = blockIdx.y;
@@ -1074,17 +1080,24 @@ cudaError_t moe_forward_local(const MoeConfig& c, const MoeWeights& w, const Moe
   // logit kernel does the quant on the side.
   const bool early = side != nullptr;
   RouterArgs rl = ra;  // the logit launch's arguments
-  if (early) {
-    if (ws.timing) record_timing(ws.timing[4], st);  // the router's time includes the quant
-    const int nb = (H + 127) / 128;
-    const int grid = std::max(1, std::min((M * nb + kLogitWarps - 1) / kLogitWarps, 1024));
-    if ((err = launch_pdl(act_quant_kernel, dim3(grid), dim3(kLogitWarps * 32), 0, st, ra)) !=
-        cudaSuccess)
-      return err;
+  if (opt.x_quantized) {
     rl.xq = nullptr;
     rl.xs = nullptr;
     rl.items_sh = nullptr;
-  } else if ((err = route_logits(ra, c, ws, M, true, st)) != cudaSuccess) {
+  }
+  if (early) {
+    if (ws.timing) record_timing(ws.timing[4], st);  // the router's time includes the quant
+    if (!opt.x_quantized) {
+      const int nb = (H + 127) / 128;
+      const int grid = std::max(1, std::min((M * nb + kLogitWarps - 1) / kLogitWarps, 1024));
+      if ((err = launch_pdl(act_quant_kernel, dim3(grid), dim3(kLogitWarps * 32), 0, st, ra)) !=
+          cudaSuccess)
+        return err;
+    }
+    rl.xq = nullptr;
+    rl.xs = nullptr;
+    rl.items_sh = nullptr;
+  } else if ((err = route_logits(rl, c, ws, M, true, st)) != cudaSuccess) {
     return err;
   }
   if (has_shared) {
@@ -1185,6 +1198,7 @@ cudaError_t moe_forward_local(const MoeConfig& c, const MoeWeights& w, const Moe
   if (ws.timing) record_timing(ws.timing[3], st);
 
   if (side) cudaStreamWaitEvent(st, side->join, 0);
+  if (opt.join) cudaStreamWaitEvent(st, opt.join, 0);
   return cudaGetLastError();
 }
 

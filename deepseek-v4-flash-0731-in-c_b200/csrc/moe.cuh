@@ -92,6 +92,13 @@ struct MoeExecOptions {
   // token-parallel expert parallelism computes it for this rank's tokens
   int shared_t0 = 0;
   int shared_n = -1;
+  // ws.xq / ws.xs already hold x's FP8 quant (written by the caller's last
+  // kernel), and ws.items_sh / ws.counters[3] the shared expert's items for
+  // these tokens: no quant launch ahead of the router
+  bool x_quantized = false;
+  // an event `st` also waits on before the combine (work forked by the
+  // caller that must finish before the layer's output is consumed)
+  cudaEvent_t join = nullptr;
 };
 
 cudaError_t moe_forward(const MoeConfig& c, const MoeWeights& w, const MoeWorkspace& ws,
