@@ -390,11 +390,12 @@ struct HcFusedArgs {
 };
 
 constexpr int kHcfThreads = 256;
-constexpr int kHcfMaxCtas = 32;  // hid <= 8192
-constexpr int kHcfPer = 8;       // tail chunks of 4 columns per thread: hid <= 8 * 256 * 4
+constexpr int kHcfMaxCtas = 128;  // hid <= 8192 at 64 columns per CTA
+constexpr int kHcfPer = 8;        // tail chunks of 4 columns per thread: hid <= 8 * 256 * 4
 template <int M>
 __global__ void __launch_bounds__(kHcfThreads) hc_fused_kernel(const HcFusedArgs a) {
   constexpr int R = (2 + M) * M;
+  constexpr int COLS = kHcfThreads / M;  // columns per CTA; thread = (row m, column)
   __shared__ double red[kHcfThreads / 32][32];
   __shared__ double tot[32];
   __shared__ double red2[kHcfThreads / 32];
@@ -403,15 +404,14 @@ __global__ void __launch_bounds__(kHcfThreads) hc_fused_kernel(const HcFusedArgs
   __shared__ double pall[kHcfMaxCtas * 32];
   pdl_trigger();
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int i = blockIdx.x * kHcfThreads + tid;
-  const bool col = i < a.hid;
+  const int m = tid / COLS, ic = tid - m * COLS;
+  const int i = blockIdx.x * COLS + ic;
+  const bool col = m < M && i < a.hid;
   const size_t n = static_cast<size_t>(M) * a.hid;
-  float f[R][M];
+  const size_t e_mi = col ? static_cast<size_t>(m) * a.hid + i : 0;  // this thread's element
+  float f[R];
 #pragma unroll
-  for (int j = 0; j < R; ++j)
-#pragma unroll
-    for (int m = 0; m < M; ++m)
-      f[j][m] = (col && j < a.rows) ? __ldg(a.fn + j * n + static_cast<size_t>(m) * a.hid + i) : 0.f;
+  for (int j = 0; j < R; ++j) f[j] = (col && j < a.rows) ? __ldg(a.fn + j * n + e_mi) : 0.f;
   // what the tail needs, in case this CTA is the last one: the gain row
   // toward L2, scale and base into registers
   for (int o = tid * 128; o < a.hid * 2; o += kHcfThreads * 128)
@@ -419,41 +419,26 @@ __global__ void __launch_bounds__(kHcfThreads) hc_fused_kernel(const HcFusedArgs
   const float sc0 = __ldg(a.scale);
   const float bs = lane < M ? __ldg(a.base + lane) : 0.f;
   pdl_wait();
-  float v[M];
-#pragma unroll
-  for (int m = 0; m < M; ++m) v[m] = 0.f;
-  if (col) {
+  float v = 0.f;
+  if (a.branch) {
     float old[M];
 #pragma unroll
-    for (int m = 0; m < M; ++m) old[m] = a.state[static_cast<size_t>(m) * a.hid + i];
-    if (a.branch) {
-      const float b = a.branch[i];
+    for (int k = 0; k < M; ++k) old[k] = col ? a.state[static_cast<size_t>(k) * a.hid + i] : 0.f;
+    __syncthreads();  // the CTA's columns are read whole before any row is rewritten
+    if (col) {
+      float y = __fmul_rn(a.post_in[m], a.branch[i]);
 #pragma unroll
-      for (int m = 0; m < M; ++m) {
-        float y = __fmul_rn(a.post_in[m], b);
-#pragma unroll
-        for (int k = 0; k < M; ++k) y = fmaf(a.comb_in[m * M + k], old[k], y);
-        v[m] = bf16_round(y);
-        a.state[static_cast<size_t>(m) * a.hid + i] = v[m];
-      }
-    } else {
-#pragma unroll
-      for (int m = 0; m < M; ++m) v[m] = old[m];
+      for (int k = 0; k < M; ++k) y = fmaf(a.comb_in[m * M + k], old[k], y);
+      v = bf16_round(y);
+      a.state[e_mi] = v;
     }
+  } else if (col) {
+    v = a.state[e_mi];
   }
   double p[32];
-  p[0] = 0.0;
+  p[0] = static_cast<double>(v) * v;
 #pragma unroll
-  for (int m = 0; m < M; ++m) p[0] += static_cast<double>(v[m]) * v[m];
-#pragma unroll
-  for (int j = 0; j < 31; ++j) {
-    double s = 0.0;
-    if (j < R) {
-#pragma unroll
-      for (int m = 0; m < M; ++m) s += static_cast<double>(f[j][m]) * v[m];
-    }
-    p[1 + j] = s;
-  }
+  for (int j = 0; j < 31; ++j) p[1 + j] = j < R ? static_cast<double>(f[j]) * v : 0.0;
   red[warp][lane] = warp_transpose_sum32(p);
   __syncthreads();
   if (tid < 32) {
@@ -462,9 +447,11 @@ __global__ void __launch_bounds__(kHcfThreads) hc_fused_kernel(const HcFusedArgs
     for (int w = 0; w < kHcfThreads / 32; ++w) t += red[w][tid];
     a.part[static_cast<size_t>(blockIdx.x) * 32 + tid] = t;
   }
-  __threadfence();
   __syncthreads();
-  if (tid == 0) last = atomicAdd(a.ticket, 1u) == gridDim.x - 1;
+  if (tid == 0) {
+    __threadfence();
+    last = atomicAdd(a.ticket, 1u) == gridDim.x - 1;
+  }
   __syncthreads();
   if (!last) return;
   __threadfence();
@@ -476,8 +463,17 @@ __global__ void __launch_bounds__(kHcfThreads) hc_fused_kernel(const HcFusedArgs
 #pragma unroll
     for (int e = 0; e < 4; ++e) g4[k][e] = c0 < a.hid ? __ldg(a.norm + c0 + e) : uint16_t(0);
   }
-  // every CTA's partials into shared memory (all loads in flight), then
-  // summed in CTA order
+  // the state's first four chunks, every CTA's partials: all loads in flight
+  // together; the partials are then summed in CTA order
+  float4 sv[4][M];
+#pragma unroll
+  for (int kk = 0; kk < 4; ++kk) {
+    const int cc = (kk * kHcfThreads + tid) * 4;
+#pragma unroll
+    for (int mm = 0; mm < M; ++mm)
+      sv[kk][mm] = cc < a.hid ? __ldcg(reinterpret_cast<const float4*>(a.state + static_cast<size_t>(mm) * a.hid + cc))
+                              : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
   for (int e = tid; e < static_cast<int>(gridDim.x) * 32; e += kHcfThreads) pall[e] = __ldcg(a.part + e);
   __syncthreads();
   if (tid < 32) {
@@ -501,19 +497,17 @@ __global__ void __launch_bounds__(kHcfThreads) hc_fused_kernel(const HcFusedArgs
   // bin = bf16(pre . state) over 4 consecutive columns per chunk, the norm
   float y[kHcfPer][4];
   double ss = 0.0;
-  // the state in rounds of four chunks, each round's loads issued together
-  float4 sv[4][M];
 #pragma unroll
   for (int k = 0; k < kHcfPer; ++k) {
     const int c0 = (k * kHcfThreads + tid) * 4;
-    if (k % 4 == 0) {
+    if (k > 0 && k % 4 == 0 && k * kHcfThreads * 4 < a.hid) {
 #pragma unroll
       for (int kk = 0; kk < 4; ++kk) {
         const int cc = ((k + kk) * kHcfThreads + tid) * 4;
 #pragma unroll
-        for (int m = 0; m < M; ++m)
-          sv[kk][m] = cc < a.hid ? __ldcg(reinterpret_cast<const float4*>(a.state + static_cast<size_t>(m) * a.hid + cc))
-                                 : make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int mm = 0; mm < M; ++mm)
+          sv[kk][mm] = cc < a.hid ? __ldcg(reinterpret_cast<const float4*>(a.state + static_cast<size_t>(mm) * a.hid + cc))
+                                  : make_float4(0.f, 0.f, 0.f, 0.f);
       }
     }
 #pragma unroll
@@ -522,11 +516,11 @@ __global__ void __launch_bounds__(kHcfThreads) hc_fused_kernel(const HcFusedArgs
       const float4* s = sv[k % 4];
       float acc[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-      for (int m = 0; m < M; ++m) {
-        acc[0] = fmaf(pre_s[m], s[m].x, acc[0]);
-        acc[1] = fmaf(pre_s[m], s[m].y, acc[1]);
-        acc[2] = fmaf(pre_s[m], s[m].z, acc[2]);
-        acc[3] = fmaf(pre_s[m], s[m].w, acc[3]);
+      for (int mm = 0; mm < M; ++mm) {
+        acc[0] = fmaf(pre_s[mm], s[mm].x, acc[0]);
+        acc[1] = fmaf(pre_s[mm], s[mm].y, acc[1]);
+        acc[2] = fmaf(pre_s[mm], s[mm].z, acc[2]);
+        acc[3] = fmaf(pre_s[mm], s[mm].w, acc[3]);
       }
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
@@ -611,11 +605,11 @@ struct NormTailArgs {
 
 // Rows [t0, t1) of the window into win (warp = row, lane = 16 dims), all
 // but the ring row `skip` (being rewritten by CTA 0).
-__device__ void stage_window_rows(const NormTailArgs& a, long long skip) {
+__device__ void stage_window_rows(const NormTailArgs& a, long long skip, int cta, int n_cta) {
   const Fp8KvCache& c = a.cache;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
   const int d = c.nope + c.rope_dim, pieces = d / 16, np16 = c.nope / 16;
-  for (int t = (blockIdx.x - 1) * nw + warp; t < a.n_win; t += (gridDim.x - 1) * nw) {
+  for (int t = cta * nw + warp; t < a.n_win; t += n_cta * nw) {
     const int r = a.idx[t];
     if (r == skip || lane >= pieces) continue;
     const bool live = r >= 0 && r < c.rows;
@@ -649,15 +643,19 @@ __device__ void stage_window_rows(const NormTailArgs& a, long long skip) {
   }
 }
 
-__global__ void __launch_bounds__(256) norm_tail_kernel(const NormTailArgs a) {
+// CTA 0 runs `a0`; CTA 1 runs `a1` when a1.x is set (two independent
+// norms in one launch); the remaining CTAs stage a0's window.
+__global__ void __launch_bounds__(256) norm_tail_kernel(const NormTailArgs a0, const NormTailArgs a1) {
   extern __shared__ float ys[];  // [n]
   __shared__ double red[8];
   pdl_trigger();
-  if (blockIdx.x > 0) {
+  const int n_norm = a1.x ? 2 : 1;
+  if (static_cast<int>(blockIdx.x) >= n_norm) {
     pdl_wait();
-    stage_window_rows(a, *a.row);
+    stage_window_rows(a0, *a0.row, blockIdx.x - n_norm, gridDim.x - n_norm);
     return;
   }
+  const NormTailArgs& a = blockIdx.x == 0 ? a0 : a1;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   // up to kPer values per thread in registers, all loads in flight at once
   // (the gain before the wait: it is a weight); longer rows in rounds
@@ -832,6 +830,10 @@ struct WinAttnArgs {
   float* w;                   // scratch [H][n] BF16 weights
   float* den;                 // scratch [H] denominators
   float* out;                 // [H][d]
+  // win_head_kernel only: q arrives before its per-head RMS and RoPE
+  // (q_head_kernel's step, done by the head's CTA) when q_raw is set
+  int q_raw;
+  float q_eps;
 };
 
 __device__ __forceinline__ float cache_value(const Fp8KvCache& c, long long r, int i) {
@@ -1026,6 +1028,25 @@ __global__ void __launch_bounds__(kWhThreads) win_head_kernel(const WinAttnArgs 
   }
   for (int i = tid; i < d / 4; i += kWhThreads)
     reinterpret_cast<float4*>(qs)[i] = reinterpret_cast<const float4*>(a.q + static_cast<size_t>(h) * d)[i];
+  if (a.q_raw) {
+    // the head's RMS and RoPE (src/dsv4/dsv4_model.c:5283-5291), as
+    // q_head_kernel computes them
+    __shared__ double qred[kWhThreads / 32];
+    __syncthreads();
+    double ss = 0.0;
+    for (int i = tid; i < d; i += kWhThreads) ss += static_cast<double>(qs[i]) * qs[i];
+    ss = block_sum_d(ss, qred);
+    const float rr = rms_factor(ss, d, a.q_eps);
+    for (int i = tid; i < d; i += kWhThreads) qs[i] = bf16_round(__fmul_rn(qs[i], rr));
+    __syncthreads();
+    const int half = a.rope_dim / 2, start = d - a.rope_dim;
+    for (int i = tid; i < half; i += kWhThreads) {
+      const float x0 = qs[start + 2 * i], x1 = qs[start + 2 * i + 1];
+      const float c = a.cosv[i], sn = a.sinv[i];
+      qs[start + 2 * i] = bf16_round(__fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, sn)));
+      qs[start + 2 * i + 1] = bf16_round(__fadd_rn(__fmul_rn(x0, sn), __fmul_rn(x1, c)));
+    }
+  }
   bool ok = mbar_wait(&bar, 0, err);
   if (!__syncthreads_and(ok)) {
     if (!ok) mbar_wait(&bar, 0, err);  // the copies in flight land before the CTA exits
@@ -1313,9 +1334,28 @@ void rope_tables(const dsv4cuda_decoder_config& c, std::vector<float>& cs, std::
     if (e__ != cudaSuccess) return e__;             \
   } while (0)
 
+// xf set: the fp32 activations, quantised inside the split-K kernel (into
+// x / xs) or by a quant launch first when that kernel cannot take them.
 cudaError_t fp8_gemv(const uint8_t* W, const uint8_t* S, int in, int rows, const __half* x,
                      const float* xs, int ld, float* y, const dsv4::GemvItem* item, const int* n_one,
-                     float* part, unsigned int* cnt, cudaStream_t st) {
+                     float* part, unsigned int* cnt, cudaStream_t st, const float* xf = nullptr) {
+  if (xf) {
+    dsv4::Fp8GemvArgs q{};
+    q.W[0] = W;
+    q.S[0] = S;
+    q.in = in;
+    q.rows = rows;
+    q.round_out = 1;
+    q.act = dsv4::QAct{x, xs, ld, nullptr};
+    q.Y[0] = y;
+    q.items = item;
+    q.n_items = n_one;
+    q.max_items = 1;
+    q.xf = xf;
+    const cudaError_t e = dsv4::launch_fp8_gemv_splitk(q, part, st, cnt);
+    if (e != cudaErrorNotSupported) return e;
+    DEC_CHECK(dsv4::launch_quant_fp8(xf, in, in, 1, const_cast<__half*>(x), const_cast<float*>(xs), ld, st));
+  }
   dsv4::Fp8GemvArgs a{};
   a.W[0] = W;
   a.S[0] = S;
@@ -1327,7 +1367,7 @@ cudaError_t fp8_gemv(const uint8_t* W, const uint8_t* S, int in, int rows, const
   a.items = item;
   a.n_items = n_one;
   a.max_items = 1;
-  const cudaError_t e = dsv4::launch_fp8_gemv_splitk(a, part, st, cnt);
+  cudaError_t e = dsv4::launch_fp8_gemv_splitk(a, part, st, cnt);
   return e == cudaErrorNotSupported ? dsv4::launch_fp8_gemv(a, false, 1, st) : e;
 }
 
@@ -1352,14 +1392,10 @@ cudaError_t fp8_gemv2(const uint8_t* W0, const uint8_t* S0, int rows0, float* y0
   a.items = item;
   a.n_items = n_one;
   a.max_items = 1;
-  const cudaError_t e = dsv4::launch_fp8_gemv_splitk(a, part, st, cnt);
+  cudaError_t e = dsv4::launch_fp8_gemv_splitk(a, part, st, cnt);
   if (e != cudaErrorNotSupported) return e;
   DEC_CHECK(fp8_gemv(W0, S0, in, rows0, x, xs, ld, y0, item, n_one, part, cnt, st));
   return fp8_gemv(W1, S1, in, rows1, x, xs, ld, y1, item, n_one, part, cnt, st);
-}
-
-cudaError_t quant(dsv4cuda_decoder* D, const float* x, int n, cudaStream_t st) {
-  return dsv4::launch_quant_fp8(x, n, n, 1, D->xq, D->xs, D->ld, st);
 }
 
 
@@ -1438,7 +1474,8 @@ cudaError_t hc_boundary(dsv4cuda_decoder* D, bool post, const float* fn, const f
   a.xs = xs;
   a.part = D->part;
   a.ticket = D->hc_ticket;
-  const dim3 grid((c.hidden + dsv4::kHcfThreads - 1) / dsv4::kHcfThreads), block(dsv4::kHcfThreads);
+  const int cols = dsv4::kHcfThreads / c.hc_mult;
+  const dim3 grid((c.hidden + cols - 1) / cols), block(dsv4::kHcfThreads);
   cudaError_t e;
   switch (c.hc_mult) {
     case 1: e = dsv4::launch_pdl(dsv4::hc_fused_kernel<1>, grid, block, 0, st, a); break;
@@ -1493,11 +1530,6 @@ cudaError_t attention(dsv4cuda_decoder* D, dsv4::Layer& L, cudaStream_t st) {
     kt.idx = D->idx;
     kt.n_win = c.window;
   }
-  // CTA 0 writes the new latent; with staging, CTAs 1.. (eight rows each)
-  // decode the rest of the window
-  const int stage_ctas = D->win_staged ? (c.window + 7) / 8 : 0;
-  DEC_CHECK(dsv4::launch_pdl(dsv4::norm_tail_kernel, dim3(1 + stage_ctas), dim3(256),
-                             sizeof(float) * d, st, kt));
   dsv4::NormTailArgs qt{};
   qt.x = D->qr;
   qt.n = ql;
@@ -1505,11 +1537,18 @@ cudaError_t attention(dsv4cuda_decoder* D, dsv4::Layer& L, cudaStream_t st) {
   qt.eps = c.rms_eps;
   qt.xq = D->xq;
   qt.xs = D->xs;
-  DEC_CHECK(dsv4::launch_pdl(dsv4::norm_tail_kernel, dim3(1), dim3(256), sizeof(float) * ql, st, qt));
+  // one launch: CTA 0 writes the new latent, CTA 1 normalises and quantises
+  // the q latent for wq_b, and with staging CTAs 2.. (eight rows each)
+  // decode the rest of the window
+  const int stage_ctas = D->win_staged ? (c.window + 7) / 8 : 0;
+  DEC_CHECK(dsv4::launch_pdl(dsv4::norm_tail_kernel, dim3(2 + stage_ctas), dim3(256),
+                             sizeof(float) * std::max(d, ql), st, kt, qt));
   DEC_CHECK(fp8_gemv(w.wq_b, w.wq_b_s, ql, H * d, D->xq, D->xs, D->ld, D->q, D->item1, D->n_one, D->fp8_part, D->tile_cnt, st));
-  DEC_CHECK(dsv4::launch_pdl(dsv4::q_head_kernel, dim3(H), dim3(128), 0, st, D->q, d, c.rms_eps,
-                             half, static_cast<const float*>(D->cosv),
-                             static_cast<const float*>(D->sinv)));
+  // the per-head RMS + RoPE of q: inside the attention CTAs when staged
+  if (!D->win_staged)
+    DEC_CHECK(dsv4::launch_pdl(dsv4::q_head_kernel, dim3(H), dim3(128), 0, st, D->q, d, c.rms_eps,
+                               half, static_cast<const float*>(D->cosv),
+                               static_cast<const float*>(D->sinv)));
   // sparse_attn over the window, inverse RoPE (exact order)
   dsv4::WinAttnArgs wa{};
   wa.q = D->q;
@@ -1533,6 +1572,8 @@ cudaError_t attention(dsv4cuda_decoder* D, dsv4::Layer& L, cudaStream_t st) {
   // long after it finished
   DEC_CHECK(hc_join(D, st));
   if (D->win_staged) {
+    wa.q_raw = 1;
+    wa.q_eps = c.rms_eps;
     DEC_CHECK(dsv4::launch_pdl(dsv4::win_head_kernel, dim3(H), dim3(dsv4::kWhThreads),
                                dsv4::win_head_smem(c.window, d), st, wa,
                                static_cast<const uint16_t*>(D->kvwin), dsv4::device_error_word()));
@@ -1562,9 +1603,8 @@ cudaError_t attention(dsv4cuda_decoder* D, dsv4::Layer& L, cudaStream_t st) {
   ga.max_items = G;
   ga.static_items = 1;
   DEC_CHECK(dsv4::launch_bf16_gemv(ga, 1, st));
-  DEC_CHECK(quant(D, D->oall, G * ol, st));
   return fp8_gemv(w.wo_b, w.wo_b_s, G * ol, hid, D->xq, D->xs, D->ld, D->branch, D->item1,
-                  D->n_one, D->fp8_part, D->tile_cnt, st);
+                  D->n_one, D->fp8_part, D->tile_cnt, st, D->oall);
 }
 
 // One decode step from device token/position into logits + argmax.
@@ -1664,7 +1704,7 @@ DSV4_API int dsv4cuda_decoder_create(dsv4cuda_decoder** out, const dsv4cuda_deco
   chk(D->d_pos = dalloc<int>(D, 1));
   chk(D->state = dalloc<float>(D, n));
   chk(D->part = dalloc<double>(D, std::max(static_cast<size_t>(D->nblk) * (dsv4::kMixMax + 1),
-                                           static_cast<size_t>(c.hidden / dsv4::kHcfThreads + 1) * 32)));
+                                           static_cast<size_t>(dsv4::kHcfMaxCtas) * 32)));
   chk(D->hc_ticket = dalloc<unsigned int>(D, 1));
   chk(D->mix = dalloc<float>(D, dsv4::kMixMax));
   if (ok && (cudaStreamCreateWithFlags(&D->hc_side, cudaStreamNonBlocking) != cudaSuccess ||

@@ -560,7 +560,9 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
     }
   }
   if (!ok) {
-    // drain this warp's copies still in flight before the CTA exits
+    // drain this warp's copies still in flight (the failed stage's
+    // included) before the CTA exits
+    mbar_wait(&bars[s], phase, a.err);
     uint32_t ph = phase;
     int k = s;
     for (long long q = j + 1; q < jobs && q < j + kStages; ++q) {
@@ -1254,6 +1256,8 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
     }
   }
   if (!ok) {
+    // the copies still in flight (the failed stage's included) land first
+    mbar_wait(&bars[s], phase, err);
     uint32_t ph = phase;
     int k = s;
     for (long long q = j + 1; q < jobs && q < j + kF8Stages; ++q) {
@@ -1483,6 +1487,8 @@ __global__ void __launch_bounds__((CW + 1) * 32, 1)
       }
     }
     if (!ok) {
+      // the copies still in flight (the failed stage's included) land first
+      mbar_wait(&bars[s], phase, a.err);
       uint32_t ph = phase;
       int q = s;
       for (int jj = j + 1; jj < jobs && jj < j + kStages; ++jj) {
@@ -1685,10 +1691,12 @@ __device__ __forceinline__ float fp8_fold_tile(const Fp8GemvArgs& a, const float
   return acc;
 }
 
+constexpr int kPartMaxBps = 8;  // blocks per warp when the kernel quantises its input
 __global__ void __launch_bounds__(128) fp8_partials_kernel(const Fp8GemvArgs a, int bps,
                                                            float* part, unsigned int* tile_cnt) {
+  __shared__ __align__(16) __half xsm[4][kPartMaxBps * 128];  // per warp: its quantised blocks
   pdl_trigger();
-  const int lane = threadIdx.x & 31;
+  const int lane = threadIdx.x & 31, wl = threadIdx.x >> 5;
   const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int CB = a.in / 128;
   const int nseg = (CB + bps - 1) / bps;
@@ -1712,23 +1720,64 @@ __global__ void __launch_bounds__(128) fp8_partials_kernel(const Fp8GemvArgs a, 
   pdl_wait();
   const GemvItem& it = a.items[0];
   const __half* xr = a.act.x + static_cast<size_t>(it.tok[0].x) * a.act.ld;
-  for (int b = b0; b < b1; ++b) {
-    if (b > b0) {
+  if (a.xf) {
+    // the activation quant of this warp's blocks (quant_fp8_kernel's
+    // arithmetic); every warp covering a block writes the same scale
+    const float* xf = a.xf + static_cast<size_t>(it.tok[0].x) * a.act.ld;
+    float* qs = const_cast<float*>(a.act.s) + static_cast<size_t>(it.tok[0].x) * (a.act.ld / 128);
+    for (int b = b0; b < b1; ++b) {
+      float v[4];
+      float amax = 0.f;
 #pragma unroll
-      for (int k = 0; k < 4; ++k) w[k] = ldg32(wr + b * 128 + 32 * k);
+      for (int k = 0; k < 4; ++k) {
+        v[k] = xf[b * 128 + lane + 32 * k];
+        amax = fmaxf(amax, fabsf(v[k]));
+      }
+      amax = warp_max(amax);
+      const float scale = pow2_scale_448(amax);
+      const float inv = 1.0f / scale;
+      if (lane == 0) qs[b] = scale;
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        float q = v[k] * inv;
+        q = q > 448.f ? 448.f : (q < -448.f ? -448.f : q);
+        xsm[wl][(b - b0) * 128 + lane + 32 * k] = e4m3_round_f16(q);
+      }
+    }
+    __syncwarp();
+  }
+  for (int b = b0; b < b1; ++b) {
+    // the next block's weights are requested before this block's chain runs
+    U8x32 wn[4];
+    if (b + 1 < b1) {
+#pragma unroll
+      for (int k = 0; k < 4; ++k) wn[k] = ldg32(wr + (b + 1) * 128 + 32 * k);
     }
     float p = 0.0f;
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
-      const U8x32 x0 = ldg32_l1(xr + b * 128 + 32 * k);
-      const U8x32 x1 = ldg32_l1(xr + b * 128 + 32 * k + 16);
       uint32_t x16[16];
+      if (a.xf) {
+        const uint4* xs4 = reinterpret_cast<const uint4*>(&xsm[wl][(b - b0) * 128 + 32 * k]);
 #pragma unroll
-      for (int q = 0; q < 8; ++q) {
-        x16[q] = x0.w[q];
-        x16[8 + q] = x1.w[q];
+        for (int q = 0; q < 4; ++q) {
+          const uint4 u = xs4[q];
+          x16[4 * q] = u.x; x16[4 * q + 1] = u.y; x16[4 * q + 2] = u.z; x16[4 * q + 3] = u.w;
+        }
+      } else {
+        const U8x32 x0 = ldg32_l1(xr + b * 128 + 32 * k);
+        const U8x32 x1 = ldg32_l1(xr + b * 128 + 32 * k + 16);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          x16[q] = x0.w[q];
+          x16[8 + q] = x1.w[q];
+        }
       }
       p = fp8_chain32(w[k].w, x16, p);
+    }
+    if (b + 1 < b1) {
+#pragma unroll
+      for (int k = 0; k < 4; ++k) w[k] = wn[k];
     }
     part[static_cast<size_t>(b) * total + row] = p;
   }
@@ -1866,22 +1915,37 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
     if (!mbar_wait(&bars[q], phase, err)) { ok = false; break; }
     const unsigned char* st = wbase + q * kBStage;
     const float4* xs = reinterpret_cast<const float4*>(st + kBW);
+    // 32 pieces of 8 columns (4 boxes x 8 swizzled 16-byte chunks), the
+    // operands of piece p + 2 loaded while piece p's eight fmaf run, so the
+    // chain never waits on shared memory
+    auto wld = [&](int p) {
+      return *reinterpret_cast<const uint4*>(st + (p >> 3) * 4096 + lane * 128 + (((p & 7) ^ sw) << 4));
+    };
+    uint4 wq[3];
+    float4 xq0[3], xq1[3];
 #pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      const unsigned char* box = st + k * 4096 + lane * 128;
+    for (int p = 0; p < 2; ++p) {
+      wq[p] = wld(p);
+      xq0[p] = xs[2 * p];
+      xq1[p] = xs[2 * p + 1];
+    }
 #pragma unroll
-      for (int c = 0; c < 8; ++c) {
-        const uint4 w8 = *reinterpret_cast<const uint4*>(box + ((c ^ sw) << 4));
-        const float4 x0 = xs[k * 16 + 2 * c], x1 = xs[k * 16 + 2 * c + 1];
-        acc = fmaf(__uint_as_float(w8.x << 16), x0.x, acc);
-        acc = fmaf(__uint_as_float(w8.x & 0xFFFF0000u), x0.y, acc);
-        acc = fmaf(__uint_as_float(w8.y << 16), x0.z, acc);
-        acc = fmaf(__uint_as_float(w8.y & 0xFFFF0000u), x0.w, acc);
-        acc = fmaf(__uint_as_float(w8.z << 16), x1.x, acc);
-        acc = fmaf(__uint_as_float(w8.z & 0xFFFF0000u), x1.y, acc);
-        acc = fmaf(__uint_as_float(w8.w << 16), x1.z, acc);
-        acc = fmaf(__uint_as_float(w8.w & 0xFFFF0000u), x1.w, acc);
+    for (int p = 0; p < 32; ++p) {
+      if (p + 2 < 32) {
+        wq[(p + 2) % 3] = wld(p + 2);
+        xq0[(p + 2) % 3] = xs[2 * (p + 2)];
+        xq1[(p + 2) % 3] = xs[2 * (p + 2) + 1];
       }
+      const uint4 w8 = wq[p % 3];
+      const float4 x0 = xq0[p % 3], x1 = xq1[p % 3];
+      acc = fmaf(__uint_as_float(w8.x << 16), x0.x, acc);
+      acc = fmaf(__uint_as_float(w8.x & 0xFFFF0000u), x0.y, acc);
+      acc = fmaf(__uint_as_float(w8.y << 16), x0.z, acc);
+      acc = fmaf(__uint_as_float(w8.y & 0xFFFF0000u), x0.w, acc);
+      acc = fmaf(__uint_as_float(w8.z << 16), x1.x, acc);
+      acc = fmaf(__uint_as_float(w8.z & 0xFFFF0000u), x1.y, acc);
+      acc = fmaf(__uint_as_float(w8.w << 16), x1.z, acc);
+      acc = fmaf(__uint_as_float(w8.w & 0xFFFF0000u), x1.w, acc);
     }
     if (j % CPT == CPT - 1) {
       const long long tile = first + (j / CPT) * nwarps;
@@ -1900,7 +1964,9 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
     }
   }
   if (!ok) {
-    // drain this warp's copies still in flight before the CTA exits
+    // drain this warp's copies still in flight (the failed stage's
+    // included) before the CTA exits
+    mbar_wait(&bars[q], phase, err);
     uint32_t ph = phase;
     int k = q;
     for (long long r = j + 1; r < jobs && r < j + STAGES; ++r) {
@@ -1919,10 +1985,12 @@ cudaError_t launch_fp8_gemv_splitk(const Fp8GemvArgs& a, float* part, cudaStream
     return cudaErrorNotSupported;
   const int total = a.rows + a.rows1;
   const int CB = a.in / 128, tiles = total / 32;
+  if (a.xf && (!tile_cnt || a.rows1 != 0)) return cudaErrorNotSupported;
   // about 16 warps per SM, at least one block per warp
   const long long target = 16LL * sm_count();
   int bps = static_cast<int>(std::max<long long>(1, (static_cast<long long>(tiles) * CB + target - 1) / target));
   bps = std::min(bps, CB);
+  if (a.xf && bps > kPartMaxBps) return cudaErrorNotSupported;
   const int nseg = (CB + bps - 1) / bps;
   const long long warps = static_cast<long long>(tiles) * nseg;
   cudaError_t e = launch_pdl(fp8_partials_kernel, dim3(static_cast<unsigned>((warps + 3) / 4)),

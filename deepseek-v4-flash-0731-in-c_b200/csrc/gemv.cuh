@@ -65,6 +65,10 @@ struct Fp8GemvArgs {
   // split-K kernels only: a second matrix W[1] / S[1] of rows1 rows (same
   // input) whose outputs go to Y[1]; one launch computes both
   int rows1 = 0;
+  // split-K kernel with in-kernel folds only: fp32 activations [*][act.ld]
+  // that the kernel quantises itself (act.x unused, act.s receives the
+  // per-128 scales)
+  const float* xf = nullptr;
 };
 
 struct Bf16GemvArgs {

@@ -5,6 +5,8 @@
  *
  *   tiny_decode <checkpoint dir> <n_generate> <prompt id> [<prompt id> ...]
  *
+ * TINY_DECODE_THREADS sets the engine's thread count (default 2).
+ *
  * Prefills the prompt layer-major, then decodes n_generate tokens greedily
  * (argmax, lowest id on ties, as the reference CLI's argmax_logits,
  * src/cli/dsv4_run.c:355). Prints one line per generated position,
@@ -49,7 +51,8 @@ int main(int argc, char **argv)
 
     DSV4Options opt = {0};
     opt.max_context = n_prompt + n_gen + 8;
-    opt.threads = 2;
+    const char *th = getenv("TINY_DECODE_THREADS");
+    opt.threads = th && atoi(th) > 0 ? atoi(th) : 2;
     opt.expert_cache_bytes = 64ull * (13369344ull + 4 * 4096ull);
     DSV4Model *m = dsv4_model_open(argv[1], &opt);
     if (!m) { fprintf(stderr, "FAIL: model open\n"); return 1; }

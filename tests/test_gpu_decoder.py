@@ -41,14 +41,15 @@ FAST_REL_L2 = 2e-2
 N_PROMPT, N_GEN = 32, 16
 
 
-def reference_steps(ckpt, ids):
+def reference_steps(ckpt, ids, n_gen=N_GEN):
     exe = os.path.join(REFDIR, "tiny_decode")
     if not os.path.exists(exe):
         pytest.skip("oracle/_ref/tiny_decode not built here (needs the reference sources)")
     env = dict(os.environ)
     env.pop("LD_PRELOAD", None)
-    r = subprocess.run([exe, ckpt, str(N_GEN), *map(str, ids)], cwd=REFDIR, env=env,
-                       capture_output=True, text=True, timeout=600)
+    env["TINY_DECODE_THREADS"] = str(max(2, min(16, os.cpu_count() or 2)))
+    r = subprocess.run([exe, ckpt, str(n_gen), *map(str, ids)], cwd=REFDIR, env=env,
+                       capture_output=True, text=True, timeout=900)
     assert r.returncode == 0, r.stderr[-2000:]
     steps = []
     for ln in r.stdout.splitlines():
@@ -56,8 +57,36 @@ def reference_steps(ckpt, ids):
             f = ln.split()
             steps.append((int(f[1]), int(f[3]),
                           np.array([float.fromhex(v) for v in f[5:]], np.float32)))
-    assert len(steps) == N_GEN
+    assert len(steps) == n_gen
     return steps
+
+
+def compare_decode(dec, ids, want, tol):
+    """Feeds the prompt, then the reference's own tokens; returns (steps
+    bit-identical, worst relative L2, greedy tokens equal, near ties)."""
+    n_prompt = len(ids)
+    for p, t in enumerate(ids[:-1]):
+        dec.forward_token(t, p)
+    logits, nxt = dec.forward_token(ids[-1], n_prompt - 1)
+    worst, agree, same, near = 0.0, 0, 0, []
+    for g, (pos, wtok, wlog) in enumerate(want):
+        assert pos == n_prompt + g
+        err = float(np.linalg.norm(logits.astype(np.float64) - wlog) /
+                    (np.linalg.norm(wlog.astype(np.float64)) + 1e-30))
+        worst = max(worst, err)
+        same += int(np.array_equal(logits.view(np.uint32), wlog.view(np.uint32)))
+        assert err <= tol, (g, err)
+        top2 = np.sort(wlog)[-2:]
+        margin = float(top2[1] - top2[0]) / (float(np.abs(wlog).max()) + 1e-30)
+        if nxt == wtok:
+            agree += 1
+        elif margin > tol:
+            raise AssertionError((g, nxt, wtok, margin))
+        else:
+            near.append((g, nxt, wtok, margin))
+        if g + 1 < len(want):
+            logits, nxt = dec.forward_token(wtok, pos)
+    return same, worst, agree, near
 
 
 @pytest.mark.parametrize("exact", [True, False], ids=["exact", "fast"])
@@ -70,27 +99,7 @@ def test_decoder_t1_window_layers_vs_reference(cuda, tmp_path, exact):
     dec = cuda.decoder_from_checkpoint(ckpt, max_context=N_PROMPT + N_GEN + 8, hc_exact=exact)
     tol = 0.0 if exact else FAST_REL_L2
     try:
-        for p, t in enumerate(ids[:-1]):
-            dec.forward_token(t, p)
-        logits, nxt = dec.forward_token(ids[-1], N_PROMPT - 1)
-        worst, agree, same, near = 0.0, 0, 0, []
-        for g, (pos, wtok, wlog) in enumerate(want):
-            assert pos == N_PROMPT + g
-            err = float(np.linalg.norm(logits.astype(np.float64) - wlog) /
-                        (np.linalg.norm(wlog.astype(np.float64)) + 1e-30))
-            worst = max(worst, err)
-            same += int(np.array_equal(logits.view(np.uint32), wlog.view(np.uint32)))
-            assert err <= tol, (g, err)
-            top2 = np.sort(wlog)[-2:]
-            margin = float(top2[1] - top2[0]) / (float(np.abs(wlog).max()) + 1e-30)
-            if nxt == wtok:
-                agree += 1
-            elif margin > tol:
-                raise AssertionError((g, nxt, wtok, margin))
-            else:
-                near.append((g, nxt, wtok, margin))
-            if g + 1 < N_GEN:
-                logits, nxt = dec.forward_token(wtok, pos)
+        same, worst, agree, near = compare_decode(dec, ids, want, tol)
         print(f"decoder T1 ({'exact' if exact else 'fast'}): {same}/{N_GEN} steps bit-identical, "
               f"worst logits rel L2 {worst:.2e}, greedy tokens {agree}/{N_GEN} equal, "
               f"near ties {near}")
@@ -196,3 +205,38 @@ def test_decoder_snapshot_commit_prefix_equals_plain_decode(cuda, tmp_path):
         snap.close()
         a.close()
         b.close()
+
+
+@pytest.mark.parametrize("exact", [True, False], ids=["exact", "fast"])
+def test_decoder_c5_shapes_vs_reference(cuda, tmp_path, exact):
+    """One layer at the benchmark's DeepSeek-V4-Flash shapes (hidden 4096,
+    64 heads x 512, q_lora 1024, 8 x 1024 wo_a groups, window 128, hc 4;
+    16 experts and a 2048-token vocabulary to keep the host reference
+    quick), random weights in the checkpoint's formats, against the
+    reference engine: the kernel shapes the small T1 model does not reach
+    (split-K FP8 projections with in-kernel folds, the staged window
+    attention, the fused boundaries at 16 K state columns, the streamed
+    grouped wo_a) and a 136-token prompt, so the 128-row ring has wrapped.
+    Exact mode: every step bit-identical. Fast mode: these weights (FP8
+    codes uniform over +-448) make the activations large and the HC split
+    sensitive, so a one-ulp mix difference moves the logits more than on
+    T1; the bound is 5e-2 relative L2 and the greedy tokens must agree
+    wherever the reference's top-two margin exceeds it."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import random_checkpoint
+    c = dict(random_checkpoint.CONFIG5, vocab=2048, experts=16)
+    ckpt = random_checkpoint.write(str(tmp_path / "c5"), 1, c=c, seed=3)
+    ids = [int(v) for v in np.random.default_rng(3).integers(0, c["vocab"], 136)]
+    n_gen = 6
+    want = reference_steps(ckpt, ids, n_gen)
+    dec = cuda.decoder_from_checkpoint(ckpt, max_context=len(ids) + n_gen + 8, hc_exact=exact)
+    tol = 0.0 if exact else 5e-2
+    try:
+        same, worst, agree, near = compare_decode(dec, ids, want, tol)
+        print(f"decoder C5 layer ({'exact' if exact else 'fast'}): {same}/{n_gen} steps "
+              f"bit-identical, worst logits rel L2 {worst:.2e}, greedy {agree}/{n_gen}, "
+              f"near ties {near}")
+        if exact:
+            assert same == n_gen and agree == n_gen
+    finally:
+        dec.close()
