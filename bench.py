@@ -1,27 +1,31 @@
-"""bench.py - decode throughput of one DeepSeek-V4-Flash MoE layer (benchmark
-config 2) on B200, through libdsv4_cuda.so.
-
-A step is one decode token (M=1 by default) through one MoE layer: router
-(BF16 gate [256x7168], sqrt-softplus, top-8), 8 routed FP4 experts
-(gate/up 7168->2048, down 2048->7168, E8M0 per-32 scales) and the FP8 shared
-expert, ordered combine. Weights are random-init with the config's
-distributions and resident in HBM; successive steps cycle through --layers
-independent layer weight sets and a pool of tokens, so a step never finds
-the previous step's weights in L2 (126 MB) - each layer's step reads
-~235 MB. One CUDA graph replay runs the layers back to back (a decode pass
-through consecutive MoE layers), each layer on its own token rows.
+"""bench.py - greedy decode throughput of DeepSeek-V4-Flash on B200 through
+libdsv4_cuda.so (BASELINE config 5 shapes: 43 layers, hidden 4096, 64 heads
+x 512, 256 + 1 experts top-6, FP4 experts / FP8 projections, vocabulary
+129,280).
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
---impl reference times the reference engine's own CPU implementation of the
-same step (oracle/_ref, built from the reference sources; the C restatement
-when that library is absent) on the host cores. Under torchrun (N>1) the
-MoE layer is expert-parallel: each rank owns E/N routed experts and, by
-default, brings its own tokens (--ep-mode tokens): the tokens are gathered
-and each routed slot returned to its token's owner over peer memory, and
-the owner runs the ordered combine (--ep-mode replicated runs the same
-tokens on every rank, with a peer-memory slot exchange or an NCCL
-all-reduce, --ep-exchange).
+A step is one greedy token: the embedding, every layer (hyper-connection
+boundaries, sliding-window attention with FP8 projections and the latent
+ring, the MoE layer with its router, six routed FP4 experts and the FP8
+shared expert), the HC head, the BF16 vocabulary head and the argmax, all
+on the device and replayed as one CUDA graph per token (the argmax feeds
+the next step's embedding on the device). Weights are random-init in the
+checkpoint's formats; the 43 layers cycle through --decode-sets distinct
+weight sets (~3.6 GB each), so no layer's weights are in L2 when it runs.
+`e2e` is the same decode through the public host call
+(dsv4cuda_decoder_forward_token: token in, logits and next token out).
+
+--impl reference times the reference engine's own dsv4_forward_token on the
+host cores (oracle/_ref/ref_decode_bench, built from the reference sources)
+on a one-layer checkpoint of the same shapes, extrapolated to 43 layers.
+Under torchrun (N > 1) each rank decodes its own sequence and the MoE
+layers are expert-parallel (rank r holds experts [r E/N, (r+1) E/N)); the
+tokens are gathered and the routed slots returned over peer memory.
+
+--workload moe times the config 2 MoE layer alone (router, 8 routed FP4
+experts, FP8 shared expert, combine; four layer weight sets cycled) and
+--workload attn the config 3 latent attention (tensor-core kernel).
 """
 from __future__ import annotations
 
@@ -1127,12 +1131,13 @@ def main_decode(args, rank, world, local):
                  hc_head_base=torch.randn(c["hc_mult"], device=dev, generator=g) * 0.02,
                  hc_head_scale=torch.ones(1, device=dev))
     prompt, gen = 2048, args.steps
+    n_e2e = max(8, args.steps // 4)  # host-call tokens after the timed graph replays
     cfg = dict(hidden=c["hidden"], n_layers=n_layers, vocab=c["vocab"], n_heads=c["n_heads"],
                head_dim=c["head_dim"], rope_dim=c["rope_dim"], q_lora=c["q_lora"],
                o_groups=c["o_groups"], o_lora=c["o_lora"], window=c["window"],
                hc_mult=c["hc_mult"], hc_iters=c["hc_iters"], rms_eps=c["rms_eps"],
                hc_eps=c["hc_eps"], rope_theta=c["rope_theta"],
-               max_context=prompt + gen + args.warmup + 8,
+               max_context=prompt + gen + args.warmup + n_e2e + 16,
                moe=dict(hidden=c["hidden"], moe_inter=c["inter"], n_experts=c["experts"],
                         topk=c["topk"], swiglu_limit=10, route_scale=1.5,
                         shared_kind=dsv4cuda.SHARED_FP8, hash_vocab=0))
@@ -1218,7 +1223,6 @@ def main_decode(args, rank, world, local):
         for i in range(2):  # eager step, then the call that captures its graph
             lib.dsv4cuda_decoder_forward_token(h, t0v, p0 + i, logits.ctypes.data, C.byref(nxt))
             t0v = nxt.value
-        n_e2e = max(8, args.steps // 4)
         t0 = time.perf_counter()
         for i in range(n_e2e):
             if lib.dsv4cuda_decoder_forward_token(h, t0v, p0 + 2 + i, logits.ctypes.data,

@@ -392,33 +392,37 @@ struct HcFusedArgs {
 constexpr int kHcfThreads = 256;
 constexpr int kHcfMaxCtas = 128;  // hid <= 8192 at 64 columns per CTA
 constexpr int kHcfPer = 8;        // tail chunks of 4 columns per thread: hid <= 8 * 256 * 4
+
+// Unit u of a boundary: the state columns [u COLS, (u + 1) COLS), thread =
+// (row m, column). hc_unit_load: the unit's mix weights (before the wait on
+// the previous work) and the gain row toward L2; hc_unit_run: the post step
+// in place and the unit's mix partials, summed over the CTA into part[u].
 template <int M>
-__global__ void __launch_bounds__(kHcfThreads) hc_fused_kernel(const HcFusedArgs a) {
+__device__ __forceinline__ void hc_unit_load(const HcFusedArgs& a, int u, float (&f)[(2 + M) * M]) {
   constexpr int R = (2 + M) * M;
-  constexpr int COLS = kHcfThreads / M;  // columns per CTA; thread = (row m, column)
-  __shared__ double red[kHcfThreads / 32][32];
-  __shared__ double tot[32];
-  __shared__ double red2[kHcfThreads / 32];
-  __shared__ float pre_s[kHcMultMax];
-  __shared__ int last;
-  __shared__ double pall[kHcfMaxCtas * 32];
-  pdl_trigger();
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  constexpr int COLS = kHcfThreads / M;
+  const int tid = threadIdx.x;
   const int m = tid / COLS, ic = tid - m * COLS;
-  const int i = blockIdx.x * COLS + ic;
+  const int i = u * COLS + ic;
   const bool col = m < M && i < a.hid;
   const size_t n = static_cast<size_t>(M) * a.hid;
-  const size_t e_mi = col ? static_cast<size_t>(m) * a.hid + i : 0;  // this thread's element
-  float f[R];
+  const size_t e_mi = col ? static_cast<size_t>(m) * a.hid + i : 0;
 #pragma unroll
   for (int j = 0; j < R; ++j) f[j] = (col && j < a.rows) ? __ldg(a.fn + j * n + e_mi) : 0.f;
-  // what the tail needs, in case this CTA is the last one: the gain row
-  // toward L2, scale and base into registers
-  for (int o = tid * 128; o < a.hid * 2; o += kHcfThreads * 128)
+  for (int o = tid * 128; o < a.hid * 2; o += static_cast<int>(blockDim.x) * 128)
     asm volatile("prefetch.global.L2 [%0];" ::"l"(reinterpret_cast<const char*>(a.norm) + o));
-  const float sc0 = __ldg(a.scale);
-  const float bs = lane < M ? __ldg(a.base + lane) : 0.f;
-  pdl_wait();
+}
+
+template <int M>
+__device__ __forceinline__ void hc_unit_run(const HcFusedArgs& a, int u, const float (&f)[(2 + M) * M],
+                                            double (*red)[32]) {
+  constexpr int R = (2 + M) * M;
+  constexpr int COLS = kHcfThreads / M;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int m = tid / COLS, ic = tid - m * COLS;
+  const int i = u * COLS + ic;
+  const bool col = m < M && i < a.hid;
+  const size_t e_mi = col ? static_cast<size_t>(m) * a.hid + i : 0;
   float v = 0.f;
   if (a.branch) {
     float old[M];
@@ -444,22 +448,28 @@ __global__ void __launch_bounds__(kHcfThreads) hc_fused_kernel(const HcFusedArgs
   if (tid < 32) {
     double t = 0.0;
 #pragma unroll
-    for (int w = 0; w < kHcfThreads / 32; ++w) t += red[w][tid];
-    a.part[static_cast<size_t>(blockIdx.x) * 32 + tid] = t;
+    for (int w = 0; w < static_cast<int>(blockDim.x >> 5); ++w) t += red[w][tid];
+    a.part[static_cast<size_t>(u) * 32 + tid] = t;
   }
-  __syncthreads();
-  if (tid == 0) {
-    __threadfence();
-    last = atomicAdd(a.ticket, 1u) == gridDim.x - 1;
-  }
-  __syncthreads();
-  if (!last) return;
-  __threadfence();
-  if (tid == 0) *a.ticket = 0u;
+}
+
+// The boundary's tail on one CTA once every unit's partials are written:
+// the mixes (summed in unit order), the pre weights, the bin, RMSNorm,
+// the optional quant. pall: n_units * 32 doubles of shared memory.
+template <int M>
+__device__ void hc_tail(const HcFusedArgs& a, int n_units, double* pall) {
+  __shared__ double tot[32];
+  __shared__ double red2[32];
+  __shared__ float pre_s[kHcMultMax];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int nt = blockDim.x;  // columns are dealt 4 per thread, nt threads per chunk
+  const size_t n = static_cast<size_t>(M) * a.hid;
+  const float sc0 = __ldg(a.scale);
+  const float bs = lane < M ? __ldg(a.base + lane) : 0.f;
   uint16_t g4[kHcfPer][4];
 #pragma unroll
   for (int k = 0; k < kHcfPer; ++k) {
-    const int c0 = (k * kHcfThreads + tid) * 4;
+    const int c0 = (k * nt + tid) * 4;
 #pragma unroll
     for (int e = 0; e < 4; ++e) g4[k][e] = c0 < a.hid ? __ldg(a.norm + c0 + e) : uint16_t(0);
   }
@@ -468,17 +478,17 @@ __global__ void __launch_bounds__(kHcfThreads) hc_fused_kernel(const HcFusedArgs
   float4 sv[4][M];
 #pragma unroll
   for (int kk = 0; kk < 4; ++kk) {
-    const int cc = (kk * kHcfThreads + tid) * 4;
+    const int cc = (kk * nt + tid) * 4;
 #pragma unroll
     for (int mm = 0; mm < M; ++mm)
       sv[kk][mm] = cc < a.hid ? __ldcg(reinterpret_cast<const float4*>(a.state + static_cast<size_t>(mm) * a.hid + cc))
                               : make_float4(0.f, 0.f, 0.f, 0.f);
   }
-  for (int e = tid; e < static_cast<int>(gridDim.x) * 32; e += kHcfThreads) pall[e] = __ldcg(a.part + e);
+  for (int e = tid; e < n_units * 32; e += nt) pall[e] = __ldcg(a.part + e);
   __syncthreads();
   if (tid < 32) {
     double t = 0.0;
-    for (unsigned b = 0; b < gridDim.x; ++b) t += pall[b * 32 + tid];
+    for (int b = 0; b < n_units; ++b) t += pall[b * 32 + tid];
     tot[tid] = t;
   }
   __syncthreads();
@@ -499,11 +509,11 @@ __global__ void __launch_bounds__(kHcfThreads) hc_fused_kernel(const HcFusedArgs
   double ss = 0.0;
 #pragma unroll
   for (int k = 0; k < kHcfPer; ++k) {
-    const int c0 = (k * kHcfThreads + tid) * 4;
-    if (k > 0 && k % 4 == 0 && k * kHcfThreads * 4 < a.hid) {
+    const int c0 = (k * nt + tid) * 4;
+    if (k > 0 && k % 4 == 0 && k * nt * 4 < a.hid) {
 #pragma unroll
       for (int kk = 0; kk < 4; ++kk) {
-        const int cc = ((k + kk) * kHcfThreads + tid) * 4;
+        const int cc = ((k + kk) * nt + tid) * 4;
 #pragma unroll
         for (int mm = 0; mm < M; ++mm)
           sv[kk][mm] = cc < a.hid ? __ldcg(reinterpret_cast<const float4*>(a.state + static_cast<size_t>(mm) * a.hid + cc))
@@ -533,8 +543,8 @@ __global__ void __launch_bounds__(kHcfThreads) hc_fused_kernel(const HcFusedArgs
   const float r = rms_factor(ss, a.hid, a.rms_eps);
 #pragma unroll
   for (int k = 0; k < kHcfPer; ++k) {
-    const int c0 = (k * kHcfThreads + tid) * 4;
-    if (k * kHcfThreads * 4 >= a.hid) break;  // uniform over the CTA
+    const int c0 = (k * nt + tid) * 4;
+    if (k * nt * 4 >= a.hid) break;  // uniform over the CTA
     const float gn[4] = {bf16_widen(g4[k][0]), bf16_widen(g4[k][1]), bf16_widen(g4[k][2]),
                          bf16_widen(g4[k][3])};
     float o[4];
@@ -561,6 +571,28 @@ __global__ void __launch_bounds__(kHcfThreads) hc_fused_kernel(const HcFusedArgs
       }
     }
   }
+}
+
+template <int M>
+__global__ void __launch_bounds__(kHcfThreads) hc_fused_kernel(const HcFusedArgs a) {
+  __shared__ double red[kHcfThreads / 32][32];
+  __shared__ double pall[kHcfMaxCtas * 32];
+  __shared__ int last;
+  pdl_trigger();
+  float f[(2 + M) * M];
+  hc_unit_load<M>(a, blockIdx.x, f);
+  pdl_wait();
+  hc_unit_run<M>(a, blockIdx.x, f, red);
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    last = atomicAdd(a.ticket, 1u) == gridDim.x - 1;
+  }
+  __syncthreads();
+  if (!last) return;
+  __threadfence();
+  if (threadIdx.x == 0) *a.ticket = 0u;
+  hc_tail<M>(a, gridDim.x, pall);
 }
 
 // The Sinkhorn split of a layer boundary's mixes (dsv4_hc_split,
@@ -643,19 +675,11 @@ __device__ void stage_window_rows(const NormTailArgs& a, long long skip, int cta
   }
 }
 
-// CTA 0 runs `a0`; CTA 1 runs `a1` when a1.x is set (two independent
-// norms in one launch); the remaining CTAs stage a0's window.
-__global__ void __launch_bounds__(256) norm_tail_kernel(const NormTailArgs a0, const NormTailArgs a1) {
-  extern __shared__ float ys[];  // [n]
-  __shared__ double red[8];
-  pdl_trigger();
-  const int n_norm = a1.x ? 2 : 1;
-  if (static_cast<int>(blockIdx.x) >= n_norm) {
-    pdl_wait();
-    stage_window_rows(a0, *a0.row, blockIdx.x - n_norm, gridDim.x - n_norm);
-    return;
-  }
-  const NormTailArgs& a = blockIdx.x == 0 ? a0 : a1;
+// One norm CTA (any multiple of 32 threads); ys: a.n floats of shared memory. The gain is
+// loaded before `wait` runs (the PDL wait of a standalone launch).
+template <class Wait>
+__device__ void norm_tail_run(const NormTailArgs& a, float* ys, Wait wait) {
+  __shared__ double red[32];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   // up to kPer values per thread in registers, all loads in flight at once
   // (the gain before the wait: it is a weight); longer rows in rounds
@@ -667,7 +691,7 @@ __global__ void __launch_bounds__(256) norm_tail_kernel(const NormTailArgs a0, c
     const int i = tid + k * blockDim.x;
     g[k] = i < a.n ? bf16_widen(a.w[i]) : 0.f;
   }
-  pdl_wait();
+  wait();
   double ss = 0.0;
   for (int i0 = 0; i0 < a.n; i0 += step) {
     float v[kPer];
@@ -762,6 +786,20 @@ __global__ void __launch_bounds__(256) norm_tail_kernel(const NormTailArgs a0, c
       if (tw >= 0) a.win[static_cast<size_t>(tw) * d + a.cache.nope + i] = b;
     }
   }
+}
+
+// CTA 0 runs `a0`; CTA 1 runs `a1` when a1.x is set (two independent
+// norms in one launch); the remaining CTAs stage a0's window.
+__global__ void __launch_bounds__(256) norm_tail_kernel(const NormTailArgs a0, const NormTailArgs a1) {
+  extern __shared__ float ys[];  // [n]
+  pdl_trigger();
+  const int n_norm = a1.x ? 2 : 1;
+  if (static_cast<int>(blockIdx.x) >= n_norm) {
+    pdl_wait();
+    stage_window_rows(a0, *a0.row, blockIdx.x - n_norm, gridDim.x - n_norm);
+    return;
+  }
+  norm_tail_run(blockIdx.x == 0 ? a0 : a1, ys, [] { pdl_wait(); });
 }
 
 // Per-head RMS of q and its RoPE (src/dsv4/dsv4_model.c:5283-5291), one CTA
@@ -999,9 +1037,9 @@ __host__ __device__ inline size_t win_head_smem(int n, int d) {
          static_cast<size_t>(3) * n * 4 + 16;
 }
 
-__global__ void __launch_bounds__(kWhThreads) win_head_kernel(const WinAttnArgs a, const uint16_t* win,
-                                                              unsigned int* err) {
-  extern __shared__ __align__(16) unsigned char wsm[];
+template <class Wait>
+__device__ void win_head_run(const WinAttnArgs& a, const uint16_t* win, unsigned int* err, int h,
+                             unsigned char* wsm, Wait wait) {
   __shared__ uint64_t bar;
   __shared__ float den_s;
   const int n = a.n, d = a.d, ldk = d + 8;
@@ -1011,36 +1049,35 @@ __global__ void __launch_bounds__(kWhThreads) win_head_kernel(const WinAttnArgs 
   float* ws = ss + n;                                                              // [n]
   int* sidx = reinterpret_cast<int*>(ws + n);                                      // [n]
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int h = blockIdx.x;
+  const int nth = blockDim.x;  // any multiple of 32 up to 1024
   if (tid == 0) {
     mbar_init(&bar, 1);
     mbar_fence_init();
   }
   __syncthreads();
-  pdl_trigger();
-  pdl_wait();
+  wait();
   const uint32_t row_bytes = static_cast<uint32_t>(d) * 2;
   if (tid == 0) mbar_arrive_expect_tx(&bar, row_bytes * static_cast<uint32_t>(n));
   __syncthreads();
-  for (int t = tid; t < n; t += kWhThreads) {
+  for (int t = tid; t < n; t += nth) {
     bulk_g2s(ks + static_cast<size_t>(t) * ldk, win + static_cast<size_t>(t) * d, row_bytes, &bar);
     sidx[t] = a.idx[t];
   }
-  for (int i = tid; i < d / 4; i += kWhThreads)
+  for (int i = tid; i < d / 4; i += nth)
     reinterpret_cast<float4*>(qs)[i] = reinterpret_cast<const float4*>(a.q + static_cast<size_t>(h) * d)[i];
   if (a.q_raw) {
     // the head's RMS and RoPE (src/dsv4/dsv4_model.c:5283-5291), as
     // q_head_kernel computes them
-    __shared__ double qred[kWhThreads / 32];
+    __shared__ double qred[32];
     __syncthreads();
     double ss = 0.0;
-    for (int i = tid; i < d; i += kWhThreads) ss += static_cast<double>(qs[i]) * qs[i];
+    for (int i = tid; i < d; i += nth) ss += static_cast<double>(qs[i]) * qs[i];
     ss = block_sum_d(ss, qred);
     const float rr = rms_factor(ss, d, a.q_eps);
-    for (int i = tid; i < d; i += kWhThreads) qs[i] = bf16_round(__fmul_rn(qs[i], rr));
+    for (int i = tid; i < d; i += nth) qs[i] = bf16_round(__fmul_rn(qs[i], rr));
     __syncthreads();
     const int half = a.rope_dim / 2, start = d - a.rope_dim;
-    for (int i = tid; i < half; i += kWhThreads) {
+    for (int i = tid; i < half; i += nth) {
       const float x0 = qs[start + 2 * i], x1 = qs[start + 2 * i + 1];
       const float c = a.cosv[i], sn = a.sinv[i];
       qs[start + 2 * i] = bf16_round(__fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, sn)));
@@ -1053,7 +1090,7 @@ __global__ void __launch_bounds__(kWhThreads) win_head_kernel(const WinAttnArgs 
     return;
   }
   // scores
-  for (int t = tid; t < n; t += kWhThreads) {
+  for (int t = tid; t < n; t += nth) {
     const int r = sidx[t];
     float st = -INFINITY;
     if (r >= 0 && r < a.cache.rows) {
@@ -1100,9 +1137,9 @@ __global__ void __launch_bounds__(kWhThreads) win_head_kernel(const WinAttnArgs 
   __syncthreads();
   const float den = den_s;
   const int start = d - a.rope_dim;
-  for (int p0 = tid; p0 < d / 2; p0 += 2 * kWhThreads) {
+  for (int p0 = tid; p0 < d / 2; p0 += 2 * nth) {
     // two dimension pairs per pass: four independent key-order chains
-    const int p1 = p0 + kWhThreads;
+    const int p1 = p0 + nth;
     const bool has1 = p1 < d / 2;
     float o[2][2] = {{0.f, 0.f}, {0.f, 0.f}};
 #pragma unroll 4
@@ -1132,6 +1169,13 @@ __global__ void __launch_bounds__(kWhThreads) win_head_kernel(const WinAttnArgs 
       *reinterpret_cast<float2*>(a.out + static_cast<size_t>(h) * d + i) = make_float2(x0, x1);
     }
   }
+}
+
+__global__ void __launch_bounds__(kWhThreads) win_head_kernel(const WinAttnArgs a, const uint16_t* win,
+                                                              unsigned int* err) {
+  extern __shared__ __align__(16) unsigned char wsm[];
+  pdl_trigger();
+  win_head_run(a, win, err, blockIdx.x, wsm, [] { pdl_wait(); });
 }
 
 // Greedy token: argmax_logits (src/cli/dsv4_run.c:355; first maximum, strict

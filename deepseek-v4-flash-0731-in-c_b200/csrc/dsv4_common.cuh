@@ -144,6 +144,32 @@ __device__ __forceinline__ U8x32 ldg32(const void* p) {
   return r;
 }
 
+// 32-byte global load that may stay in L1 (activations every lane reads).
+__device__ __forceinline__ U8x32 ldg32_l1(const void* p) {
+  U8x32 r;
+  asm volatile("ld.global.nc.v8.u32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+               : "=r"(r.w[0]), "=r"(r.w[1]), "=r"(r.w[2]), "=r"(r.w[3]),
+                 "=r"(r.w[4]), "=r"(r.w[5]), "=r"(r.w[6]), "=r"(r.w[7])
+               : "l"(p));
+  return r;
+}
+
+// Sequential FP8 partial over 32 columns (8 words of codes, 16 f16x2 words).
+__device__ __forceinline__ float fp8_chain32(const uint32_t* w8, const uint32_t* x16, float p) {
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    uint32_t h0, h1;
+    asm("{ .reg .b16 lo, hi; mov.b32 {lo, hi}, %2; cvt.rn.f16x2.e4m3x2 %0, lo;"
+        " cvt.rn.f16x2.e4m3x2 %1, hi; }"
+        : "=r"(h0), "=r"(h1) : "r"(w8[i]));
+    p = fma_h_lo(h0, x16[2 * i + 0], p);
+    p = fma_h_hi(h0, x16[2 * i + 0], p);
+    p = fma_h_lo(h1, x16[2 * i + 1], p);
+    p = fma_h_hi(h1, x16[2 * i + 1], p);
+  }
+  return p;
+}
+
 // ceil(log2(amax/448)) power-of-two activation scale with the 1e-4 amax
 // floor (src/dsv4/dsv4_model.c:5591-5596); returns 2^e.
 __device__ __forceinline__ float pow2_scale_448(float amax) {

@@ -28,6 +28,7 @@
 #include "bulk.cuh"
 #include "dsv4_common.cuh"
 #include "gemv.cuh"
+#include "gemv_dev.cuh"
 #include "launch.cuh"
 
 namespace dsv4 {
@@ -106,19 +107,6 @@ unsigned int* device_error_word() {
 
 namespace {
 
-__device__ __forceinline__ int load_n_items(const int* p, int max_items) {
-  const int n = *p;
-  return n < max_items ? n : max_items;
-}
-
-__device__ __forceinline__ U8x32 ldg32_l1(const void* p) {
-  U8x32 r;
-  asm volatile("ld.global.nc.v8.u32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
-               : "=r"(r.w[0]), "=r"(r.w[1]), "=r"(r.w[2]), "=r"(r.w[3]),
-                 "=r"(r.w[4]), "=r"(r.w[5]), "=r"(r.w[6]), "=r"(r.w[7])
-               : "l"(p));
-  return r;
-}
 
 // Sequential 32-column FP4 partial: 16 packed bytes (4 words) of weights
 // against 16 f16x2 activation words, columns in order.
@@ -143,21 +131,6 @@ __device__ __forceinline__ float fp4_partial16(const uint32_t* w4, const uint32_
   return p;
 }
 
-// Sequential FP8 partial over 32 columns (8 words of codes, 16 f16x2 words).
-__device__ __forceinline__ float fp8_chain32(const uint32_t* w8, const uint32_t* x16, float p) {
-#pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    uint32_t h0, h1;
-    asm("{ .reg .b16 lo, hi; mov.b32 {lo, hi}, %2; cvt.rn.f16x2.e4m3x2 %0, lo;"
-        " cvt.rn.f16x2.e4m3x2 %1, hi; }"
-        : "=r"(h0), "=r"(h1) : "r"(w8[i]));
-    p = fma_h_lo(h0, x16[2 * i + 0], p);
-    p = fma_h_hi(h0, x16[2 * i + 0], p);
-    p = fma_h_lo(h1, x16[2 * i + 1], p);
-    p = fma_h_hi(h1, x16[2 * i + 1], p);
-  }
-  return p;
-}
 
 // ---------------------------------------------------------------- FP4 ----
 // E8M0 decode table with the NaN code (255) mapped to 0. FP4 group partials
@@ -1661,140 +1634,15 @@ cudaError_t launch_fp8_gemv(const Fp8GemvArgs& a, bool pair, int item_tokens, cu
 // NaN-scaled blocks skipped, as dsv4_gemv_fp8_q does
 // (src/dsv4/dsv4_model.c:657-672). Same operations in the same order as the
 // other FP8 kernels, so the same bits.
-// The fold of a row tile in block order from every segment's partials
-// (fp8_fold_kernel's arithmetic, for the warp that finishes the tile).
-__device__ __forceinline__ float fp8_fold_tile(const Fp8GemvArgs& a, const float* part, int total,
-                                               int row, int CB) {
-  const int mat = row >= a.rows;
-  const int lrow = mat ? row - a.rows : row;
-  const GemvItem& it = a.items[0];
-  const float* qs = a.act.s + static_cast<size_t>(it.tok[0].x) * (a.act.ld / 128);
-  const uint8_t* sr = a.S[mat] + static_cast<size_t>(lrow / 128) * ((a.in + 127) / 128);
-  float acc = 0.0f;
-  for (int b0 = 0; b0 < CB; b0 += 16) {
-    float pv[16], sv[16];
-    uint32_t code[16];
-#pragma unroll
-    for (int j = 0; j < 16; ++j) {
-      const int b = b0 + j < CB ? b0 + j : CB - 1;
-      pv[j] = __ldcg(part + static_cast<size_t>(b) * total + row);
-      sv[j] = qs[b];
-      code[j] = sr[b];
-    }
-#pragma unroll
-    for (int j = 0; j < 16; ++j) {
-      if (b0 + j >= CB) break;
-      const float ws = e8m0_decode(code[j]);
-      if (!isnan(ws)) acc = fmaf(pv[j], sv[j] * ws, acc);
-    }
-  }
-  return acc;
-}
-
-constexpr int kPartMaxBps = 8;  // blocks per warp when the kernel quantises its input
 __global__ void __launch_bounds__(128) fp8_partials_kernel(const Fp8GemvArgs a, int bps,
                                                            float* part, unsigned int* tile_cnt) {
   __shared__ __align__(16) __half xsm[4][kPartMaxBps * 128];  // per warp: its quantised blocks
   pdl_trigger();
-  const int lane = threadIdx.x & 31, wl = threadIdx.x >> 5;
-  const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-  const int CB = a.in / 128;
-  const int nseg = (CB + bps - 1) / bps;
-  const int total = a.rows + a.rows1;
-  const int tiles = total / 32;
-  if (gw >= tiles * nseg) {
-    pdl_wait();
-    return;
-  }
-  const int tile = gw / nseg, seg = gw % nseg;
-  const int row = tile * 32 + lane;
-  const int mat = row >= a.rows;
-  const uint8_t* wr = a.W[mat] + static_cast<size_t>(mat ? row - a.rows : row) * a.in;
-  const int b0 = seg * bps, b1 = min(CB, (seg + 1) * bps);
-  // weights do not depend on the previous kernel: the first block into
-  // registers and the rest into L2 while it finishes
+  const Fp8Unit u = fp8_unit(a, bps, (blockIdx.x * blockDim.x + threadIdx.x) >> 5);
   U8x32 w[4];
-#pragma unroll
-  for (int k = 0; k < 4; ++k) w[k] = ldg32(wr + b0 * 128 + 32 * k);
-  for (int b = b0 + 1; b < b1; ++b) asm volatile("prefetch.global.L2 [%0];" ::"l"(wr + b * 128));
+  if (u.valid) fp8_unit_preload(u, w);
   pdl_wait();
-  const GemvItem& it = a.items[0];
-  const __half* xr = a.act.x + static_cast<size_t>(it.tok[0].x) * a.act.ld;
-  if (a.xf) {
-    // the activation quant of this warp's blocks (quant_fp8_kernel's
-    // arithmetic); every warp covering a block writes the same scale
-    const float* xf = a.xf + static_cast<size_t>(it.tok[0].x) * a.act.ld;
-    float* qs = const_cast<float*>(a.act.s) + static_cast<size_t>(it.tok[0].x) * (a.act.ld / 128);
-    for (int b = b0; b < b1; ++b) {
-      float v[4];
-      float amax = 0.f;
-#pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        v[k] = xf[b * 128 + lane + 32 * k];
-        amax = fmaxf(amax, fabsf(v[k]));
-      }
-      amax = warp_max(amax);
-      const float scale = pow2_scale_448(amax);
-      const float inv = 1.0f / scale;
-      if (lane == 0) qs[b] = scale;
-#pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        float q = v[k] * inv;
-        q = q > 448.f ? 448.f : (q < -448.f ? -448.f : q);
-        xsm[wl][(b - b0) * 128 + lane + 32 * k] = e4m3_round_f16(q);
-      }
-    }
-    __syncwarp();
-  }
-  for (int b = b0; b < b1; ++b) {
-    // the next block's weights are requested before this block's chain runs
-    U8x32 wn[4];
-    if (b + 1 < b1) {
-#pragma unroll
-      for (int k = 0; k < 4; ++k) wn[k] = ldg32(wr + (b + 1) * 128 + 32 * k);
-    }
-    float p = 0.0f;
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      uint32_t x16[16];
-      if (a.xf) {
-        const uint4* xs4 = reinterpret_cast<const uint4*>(&xsm[wl][(b - b0) * 128 + 32 * k]);
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const uint4 u = xs4[q];
-          x16[4 * q] = u.x; x16[4 * q + 1] = u.y; x16[4 * q + 2] = u.z; x16[4 * q + 3] = u.w;
-        }
-      } else {
-        const U8x32 x0 = ldg32_l1(xr + b * 128 + 32 * k);
-        const U8x32 x1 = ldg32_l1(xr + b * 128 + 32 * k + 16);
-#pragma unroll
-        for (int q = 0; q < 8; ++q) {
-          x16[q] = x0.w[q];
-          x16[8 + q] = x1.w[q];
-        }
-      }
-      p = fp8_chain32(w[k].w, x16, p);
-    }
-    if (b + 1 < b1) {
-#pragma unroll
-      for (int k = 0; k < 4; ++k) w[k] = wn[k];
-    }
-    part[static_cast<size_t>(b) * total + row] = p;
-  }
-  if (!tile_cnt) return;
-  // the last of the tile's segments to finish folds the tile
-  __threadfence();
-  __syncwarp();
-  unsigned int prev = 0;
-  if (lane == 0) prev = atomicAdd(tile_cnt + tile, 1u);
-  prev = __shfl_sync(0xffffffffu, prev, 0);
-  if (prev != static_cast<unsigned>(nseg - 1)) return;
-  __threadfence();
-  if (lane == 0) tile_cnt[tile] = 0u;  // zero again for the next launch
-  const float acc = fp8_fold_tile(a, part, total, row, CB);
-  const int rows_m = mat ? a.rows1 : a.rows;
-  a.Y[mat][static_cast<size_t>(it.tok[0].y) * rows_m + (mat ? row - a.rows : row)] =
-      a.round_out ? bf16_round(acc) : acc;
+  if (u.valid) fp8_unit_run(a, bps, part, tile_cnt, u, w, xsm[threadIdx.x >> 5]);
 }
 
 __global__ void __launch_bounds__(128) fp8_fold_kernel(const Fp8GemvArgs a, const float* part) {
@@ -1841,9 +1689,6 @@ __global__ void __launch_bounds__(128) fp8_fold_kernel(const Fp8GemvArgs a, cons
 // fp32 activations, completed on the stage's mbarrier (bounded wait). Each
 // lane runs its row's fmaf chain in column order, the reference's order, so
 // the result is the LDG kernel's bit for bit.
-constexpr int kBCols = 256;
-constexpr int kBW = 32 * kBCols * 2;             // four swizzled [32][128 B] boxes
-constexpr int kBStage = kBW + kBCols * 4;        // + the activation chunk
 
 template <int WARPS, int STAGES>
 __global__ void __launch_bounds__(WARPS * 32, 1)
@@ -1853,7 +1698,6 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
   __shared__ uint64_t bars_all[WARPS][STAGES];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   unsigned char* const sbase = smem + ((1024u - (smem_addr(smem) & 1023u)) & 1023u);
-  unsigned char* wbase = sbase + static_cast<size_t>(warp) * STAGES * kBStage;
   uint64_t* bars = bars_all[warp];
   if (lane == 0) {
 #pragma unroll
@@ -1863,117 +1707,24 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
   }
   __syncthreads();
   pdl_trigger();
-  if (!a.static_items) pdl_wait();
-  const int n_items = load_n_items(a.n_items, a.max_items);
-  const int rblocks = a.rows / 32;
-  const long long tiles = static_cast<long long>(n_items) * rblocks;
-  const int CPT = a.in / kBCols;
-  const long long nwarps = static_cast<long long>(gridDim.x) * WARPS;
-  const long long first = static_cast<long long>(warp) * gridDim.x + blockIdx.x;
-  const long long my_tiles = tiles > first ? (tiles - first + nwarps - 1) / nwarps : 0;
-  const long long jobs = my_tiles * CPT;
-  // a job's weight boxes and its activation chunk land on one mbarrier; the
-  // weights of the first stages may be requested before the wait
-  auto issue_w = [&](long long j, int q) {
-    if (lane != 0) return;
-    const long long tile = first + (j / CPT) * nwarps;
-    const int chunk = static_cast<int>(j % CPT);
-    const int item = static_cast<int>(tile / rblocks);
-    const int rb = static_cast<int>(tile - static_cast<long long>(item) * rblocks);
-    const GemvItem& it = a.items[item];
-    unsigned char* st = wbase + q * kBStage;
-    mbar_arrive_expect_tx(&bars[q], kBStage);
-    const int y = it.mat * a.rows + rb * 32;
-#pragma unroll
-    for (int k = 0; k < 4; ++k) tma_load_2d(st + k * 4096, &wmap, chunk * 512 + k * 128, y, &bars[q]);
-  };
-  auto issue_x = [&](long long j, int q) {
-    if (lane != 0) return;
-    const long long tile = first + (j / CPT) * nwarps;
-    const int chunk = static_cast<int>(j % CPT);
-    const int item = static_cast<int>(tile / rblocks);
-    const GemvItem& it = a.items[item];
-    unsigned char* st = wbase + q * kBStage;
-    bulk_g2s(st + kBW, a.x + static_cast<size_t>(it.tok[0].x) * a.ldx + chunk * kBCols, kBCols * 4,
-             &bars[q]);
-  };
-  auto issue = [&](long long j, int q) {
-    issue_w(j, q);
-    issue_x(j, q);
-  };
-  for (long long j = 0; j < jobs && j < STAGES; ++j) issue_w(j, static_cast<int>(j));
-  if (a.static_items) pdl_wait();
-  for (long long j = 0; j < jobs && j < STAGES; ++j) issue_x(j, static_cast<int>(j));
-  __syncwarp();
-  float acc = 0.0f;
-  int q = 0;
-  uint32_t phase = 0;
-  long long j = 0;
-  bool ok = true;
-  const int sw = lane & 7;
-  for (; j < jobs; ++j) {
-    if (!mbar_wait(&bars[q], phase, err)) { ok = false; break; }
-    const unsigned char* st = wbase + q * kBStage;
-    const float4* xs = reinterpret_cast<const float4*>(st + kBW);
-    // 32 pieces of 8 columns (4 boxes x 8 swizzled 16-byte chunks), the
-    // operands of piece p + 2 loaded while piece p's eight fmaf run, so the
-    // chain never waits on shared memory
-    auto wld = [&](int p) {
-      return *reinterpret_cast<const uint4*>(st + (p >> 3) * 4096 + lane * 128 + (((p & 7) ^ sw) << 4));
-    };
-    uint4 wq[3];
-    float4 xq0[3], xq1[3];
-#pragma unroll
-    for (int p = 0; p < 2; ++p) {
-      wq[p] = wld(p);
-      xq0[p] = xs[2 * p];
-      xq1[p] = xs[2 * p + 1];
-    }
-#pragma unroll
-    for (int p = 0; p < 32; ++p) {
-      if (p + 2 < 32) {
-        wq[(p + 2) % 3] = wld(p + 2);
-        xq0[(p + 2) % 3] = xs[2 * (p + 2)];
-        xq1[(p + 2) % 3] = xs[2 * (p + 2) + 1];
-      }
-      const uint4 w8 = wq[p % 3];
-      const float4 x0 = xq0[p % 3], x1 = xq1[p % 3];
-      acc = fmaf(__uint_as_float(w8.x << 16), x0.x, acc);
-      acc = fmaf(__uint_as_float(w8.x & 0xFFFF0000u), x0.y, acc);
-      acc = fmaf(__uint_as_float(w8.y << 16), x0.z, acc);
-      acc = fmaf(__uint_as_float(w8.y & 0xFFFF0000u), x0.w, acc);
-      acc = fmaf(__uint_as_float(w8.z << 16), x1.x, acc);
-      acc = fmaf(__uint_as_float(w8.z & 0xFFFF0000u), x1.y, acc);
-      acc = fmaf(__uint_as_float(w8.w << 16), x1.z, acc);
-      acc = fmaf(__uint_as_float(w8.w & 0xFFFF0000u), x1.w, acc);
-    }
-    if (j % CPT == CPT - 1) {
-      const long long tile = first + (j / CPT) * nwarps;
-      const int item = static_cast<int>(tile / rblocks);
-      const int rb = static_cast<int>(tile - static_cast<long long>(item) * rblocks);
-      a.Y[static_cast<size_t>(a.items[item].tok[0].y) * a.rows + rb * 32 + lane] =
-          a.round_out ? bf16_round(acc) : acc;
-      acc = 0.0f;
-    }
-    __syncwarp();  // every lane is done with stage q before it is refilled
-    if (j + STAGES < jobs) issue(j + STAGES, q);
-    __syncwarp();
-    if (++q == STAGES) {
-      q = 0;
-      phase ^= 1u;
-    }
-  }
-  if (!ok) {
-    // drain this warp's copies still in flight (the failed stage's
-    // included) before the CTA exits
-    mbar_wait(&bars[q], phase, err);
-    uint32_t ph = phase;
-    int k = q;
-    for (long long r = j + 1; r < jobs && r < j + STAGES; ++r) {
-      if (++k == STAGES) { k = 0; ph ^= 1u; }
-      mbar_wait(&bars[k], ph, err);
-    }
-  }
+  bf16_stream_warp<STAGES>(&wmap, a, static_cast<long long>(warp) * gridDim.x + blockIdx.x,
+                           static_cast<long long>(gridDim.x) * WARPS,
+                           sbase + static_cast<size_t>(warp) * STAGES * kBStage, bars, err,
+                           [] { pdl_wait(); });
+}
+
+
+int device_sm_count() { return sm_count(); }
+
+int fp8_splitk_bps(const Fp8GemvArgs& a) {
+  const int total = a.rows + a.rows1;
+  if (total <= 0 || total % 32 != 0 || a.in % 128 != 0) return 0;
+  const int CB = a.in / 128, tiles = total / 32;
+  // about 16 warps per SM, at least one block per warp
+  const long long target = 16LL * sm_count();
+  int bps = static_cast<int>(std::max<long long>(1, (static_cast<long long>(tiles) * CB + target - 1) / target));
+  bps = std::min(bps, CB);
+  return a.xf && bps > kPartMaxBps ? 0 : bps;
 }
 
 cudaError_t launch_fp8_gemv_splitk(const Fp8GemvArgs& a, float* part, cudaStream_t st,
@@ -1986,11 +1737,8 @@ cudaError_t launch_fp8_gemv_splitk(const Fp8GemvArgs& a, float* part, cudaStream
   const int total = a.rows + a.rows1;
   const int CB = a.in / 128, tiles = total / 32;
   if (a.xf && (!tile_cnt || a.rows1 != 0)) return cudaErrorNotSupported;
-  // about 16 warps per SM, at least one block per warp
-  const long long target = 16LL * sm_count();
-  int bps = static_cast<int>(std::max<long long>(1, (static_cast<long long>(tiles) * CB + target - 1) / target));
-  bps = std::min(bps, CB);
-  if (a.xf && bps > kPartMaxBps) return cudaErrorNotSupported;
+  const int bps = fp8_splitk_bps(a);
+  if (bps <= 0) return cudaErrorNotSupported;
   const int nseg = (CB + bps - 1) / bps;
   const long long warps = static_cast<long long>(tiles) * nseg;
   cudaError_t e = launch_pdl(fp8_partials_kernel, dim3(static_cast<unsigned>((warps + 3) / 4)),

@@ -97,6 +97,11 @@ cudaError_t launch_bf16_gemv(const Bf16GemvArgs& a, int item_tokens,
 // One-token, one-item FP8 GEMV split over 128-column blocks (more warps for
 // matrices with few row tiles); part holds in/128 * rows floats of scratch.
 // cudaErrorNotSupported when the shape or alignment does not fit.
+// Blocks per split-K unit for `a` (0: the split-K form does not apply).
+int fp8_splitk_bps(const Fp8GemvArgs& a);
+// Streaming multiprocessors of the current device.
+int device_sm_count();
+
 // tile_cnt (zeroed, rows / 32 counters): the last segment of each row tile
 // folds it in the same launch; null: a separate fold launch.
 cudaError_t launch_fp8_gemv_splitk(const Fp8GemvArgs& a, float* part, cudaStream_t st,

@@ -240,3 +240,4 @@ def test_decoder_c5_shapes_vs_reference(cuda, tmp_path, exact):
             assert same == n_gen and agree == n_gen
     finally:
         dec.close()
+
