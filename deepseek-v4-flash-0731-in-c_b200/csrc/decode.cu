@@ -81,12 +81,14 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
 // ------------------------------------------------------------ kernels ----
 
 // embed_token (src/dsv4/dsv4_model.c:7478): every HC copy gets the BF16 row.
+// Row blockIdx.y of a verify step embeds token[blockIdx.y] into its own state.
 __global__ void embed_kernel(const uint16_t* embed, const int* token, int vocab, int hid, int mult,
                              float* state) {
   pdl_wait();
   pdl_trigger();
-  int t = *token;
+  int t = token[blockIdx.y];
   if (t < 0 || t >= vocab) t = 0;
+  state += static_cast<size_t>(blockIdx.y) * mult * hid;
   const uint16_t* row = embed + static_cast<size_t>(t) * hid;
   for (int j = blockIdx.x * blockDim.x + threadIdx.x; j < hid; j += gridDim.x * blockDim.x) {
     const float v = bf16_widen(row[j]);
@@ -114,6 +116,34 @@ __global__ void position_kernel(const int* pos_ptr, int win, int half, int max_p
     sinv[i] = sin_tab[static_cast<size_t>(pos) * half + i];
   }
   if (threadIdx.x == 0) *row = pos % win;
+}
+
+// The verify step's per-row set-up (dsv4_prefill_capture's rows at positions
+// start + r, src/dsv4/dsv4_model.c:8434): row r's window lists the same
+// positions in the same order as window_topk gives position start + r
+// (:5073), but the positions start .. start + r are the verify rows' own
+// latents, held in the scratch cache rows win + (position - start) until a
+// commit moves the accepted ones into the ring; the ring itself is not
+// written, so a rejected draft leaves nothing to undo. CTA r = row r.
+__global__ void verify_position_kernel(const int* start_ptr, int win, int half, int max_pos,
+                                       const float* cos_tab, const float* sin_tab, int* idx,
+                                       long long* row, float* cosv, float* sinv) {
+  pdl_wait();
+  pdl_trigger();
+  const int r = blockIdx.x;
+  const int start = *start_ptr;
+  int pos = start + r;
+  if (pos < 0) pos = 0;
+  if (pos >= max_pos) pos = max_pos - 1;
+  for (int i = threadIdx.x; i < win; i += blockDim.x) {
+    const int q = pos >= win - 1 ? pos - win + 1 + i : (i <= pos ? i : -1);
+    idx[static_cast<size_t>(r) * win + i] = q < 0 ? -1 : (q >= start ? win + (q - start) : q % win);
+  }
+  for (int i = threadIdx.x; i < half; i += blockDim.x) {
+    cosv[static_cast<size_t>(r) * half + i] = cos_tab[static_cast<size_t>(pos) * half + i];
+    sinv[static_cast<size_t>(r) * half + i] = sin_tab[static_cast<size_t>(pos) * half + i];
+  }
+  if (threadIdx.x == 0) row[r] = win + r;
 }
 
 // HC mixes, partial sums: CTA b covers columns [b * kMixThreads, ...) of the
@@ -387,7 +417,32 @@ struct HcFusedArgs {
   float* xs;                    // [hid / 128] its scales
   double* part;                 // [gridDim.x][32]
   unsigned int* ticket;         // zero between launches
+  // verify steps (gridDim.y rows): row r's buffers follow row 0's at these
+  // strides - state mult*hid, branch/out hid, post kHcMultMax, comb
+  // kHcMultMax^2, mix kMixMax, xq xq_ld (xs xq_ld / 128), part part_rs,
+  // ticket 1
+  int xq_ld;
+  size_t part_rs;
 };
+
+template <int M>
+__device__ __forceinline__ HcFusedArgs hc_row(HcFusedArgs a, int r) {
+  if (r == 0) return a;
+  const size_t hid = static_cast<size_t>(a.hid);
+  a.state += r * M * hid;
+  if (a.branch) a.branch += r * hid;
+  a.post_in += r * kHcMultMax;
+  a.comb_in += r * kHcMultMax * kHcMultMax;
+  a.mix_out += r * kMixMax;
+  a.out += r * hid;
+  if (a.xq) {
+    a.xq += static_cast<size_t>(r) * a.xq_ld;
+    a.xs += static_cast<size_t>(r) * (a.xq_ld / 128);
+  }
+  a.part += r * a.part_rs;
+  a.ticket += r;
+  return a;
+}
 
 constexpr int kHcfThreads = 256;
 constexpr int kHcfMaxCtas = 128;  // hid <= 8192 at 64 columns per CTA
@@ -574,7 +629,8 @@ __device__ void hc_tail(const HcFusedArgs& a, int n_units, double* pall) {
 }
 
 template <int M>
-__global__ void __launch_bounds__(kHcfThreads) hc_fused_kernel(const HcFusedArgs a) {
+__global__ void __launch_bounds__(kHcfThreads) hc_fused_kernel(const HcFusedArgs a0) {
+  const HcFusedArgs a = hc_row<M>(a0, blockIdx.y);
   __shared__ double red[kHcfThreads / 32][32];
   __shared__ double pall[kHcfMaxCtas * 32];
   __shared__ int last;
@@ -598,10 +654,15 @@ __global__ void __launch_bounds__(kHcfThreads) hc_fused_kernel(const HcFusedArgs
 // The Sinkhorn split of a layer boundary's mixes (dsv4_hc_split,
 // src/dsv4/dsv4_ops.c:412-460) into the post weights and the comb matrix
 // the next boundary's post step applies. One warp.
+// CTA r splits row r's mixes (verify steps: one CTA per row, the hc_row
+// strides).
 template <int M>
 __global__ void hc_sinkhorn_kernel(const float* mix, const float* scale, const float* base, int iters,
                                    float eps, float* post, float* comb) {
   __shared__ float pre_s[kHcMultMax], post_s[kHcMultMax], comb_s[kHcMultMax * kHcMultMax];
+  mix += blockIdx.x * kMixMax;
+  post += blockIdx.x * kHcMultMax;
+  comb += blockIdx.x * kHcMultMax * kHcMultMax;
   hc_split_warp<M>(mix, scale, base, iters, eps, pre_s, post_s, comb_s);
   __syncwarp();
   const int lane = threadIdx.x;
@@ -633,10 +694,33 @@ struct NormTailArgs {
   uint16_t* win;          // [n_win][nope + rope]
   const int* idx;         // [n_win]
   int n_win;
+  // verify steps (gridDim.y rows): row r reads x + r x_rs, quantises into
+  // xq + r xq_ld (xs + r xq_ld / 128), takes cos/sin + r cs_rs, writes
+  // ring row row[r] and stages into win + r n_win d from idx + r n_win
+  int x_rs, xq_ld, cs_rs;
 };
 
+__device__ __forceinline__ NormTailArgs norm_row(NormTailArgs a, int r) {
+  if (r == 0) return a;
+  a.x += static_cast<size_t>(r) * a.x_rs;
+  if (a.xq) {
+    a.xq += static_cast<size_t>(r) * a.xq_ld;
+    a.xs += static_cast<size_t>(r) * (a.xq_ld / 128);
+  }
+  if (a.cosv) {
+    a.cosv += static_cast<size_t>(r) * a.cs_rs;
+    a.sinv += static_cast<size_t>(r) * a.cs_rs;
+  }
+  if (a.row) a.row += r;
+  if (a.idx) a.idx += static_cast<size_t>(r) * a.n_win;
+  if (a.win) a.win += static_cast<size_t>(r) * a.n_win * (a.cache.nope + a.cache.rope_dim);
+  return a;
+}
+
 // Rows [t0, t1) of the window into win (warp = row, lane = 16 dims), all
-// but the ring row `skip` (being rewritten by CTA 0).
+// but the ring row `skip` (being rewritten by CTA 0; kNoSkipRow: none).
+// Padding keys (idx -1) are staged as zeros.
+constexpr long long kNoSkipRow = -2;
 __device__ void stage_window_rows(const NormTailArgs& a, long long skip, int cta, int n_cta) {
   const Fp8KvCache& c = a.cache;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
@@ -789,17 +873,28 @@ __device__ void norm_tail_run(const NormTailArgs& a, float* ys, Wait wait) {
 }
 
 // CTA 0 runs `a0`; CTA 1 runs `a1` when a1.x is set (two independent
-// norms in one launch); the remaining CTAs stage a0's window.
+// norms in one launch); the remaining CTAs stage a0's window. blockIdx.y
+// selects the row of a verify step (norm_row).
 __global__ void __launch_bounds__(256) norm_tail_kernel(const NormTailArgs a0, const NormTailArgs a1) {
   extern __shared__ float ys[];  // [n]
   pdl_trigger();
   const int n_norm = a1.x ? 2 : 1;
   if (static_cast<int>(blockIdx.x) >= n_norm) {
     pdl_wait();
-    stage_window_rows(a0, *a0.row, blockIdx.x - n_norm, gridDim.x - n_norm);
+    const NormTailArgs a = norm_row(a0, blockIdx.y);
+    stage_window_rows(a, *a.row, blockIdx.x - n_norm, gridDim.x - n_norm);
     return;
   }
-  norm_tail_run(blockIdx.x == 0 ? a0 : a1, ys, [] { pdl_wait(); });
+  norm_tail_run(norm_row(blockIdx.x == 0 ? a0 : a1, blockIdx.y), ys, [] { pdl_wait(); });
+}
+
+// A verify step's window staging, after every row's latent is in the cache
+// (the rows' windows include the other verify rows' scratch rows):
+// blockIdx.y = row, the CTAs along x share its window.
+__global__ void __launch_bounds__(256) stage_rows_kernel(const NormTailArgs a0) {
+  pdl_wait();
+  pdl_trigger();
+  stage_window_rows(norm_row(a0, blockIdx.y), kNoSkipRow, blockIdx.x, gridDim.x);
 }
 
 // Per-head RMS of q and its RoPE (src/dsv4/dsv4_model.c:5283-5291), one CTA
@@ -872,6 +967,8 @@ struct WinAttnArgs {
   // (q_head_kernel's step, done by the head's CTA) when q_raw is set
   int q_raw;
   float q_eps;
+  // win_head_kernel on a verify step (gridDim.y rows): row r's q, out at
+  // + r H d, idx + r n, cos/sin + r rope_dim / 2, staged window + r n d
 };
 
 __device__ __forceinline__ float cache_value(const Fp8KvCache& c, long long r, int i) {
@@ -1171,11 +1268,19 @@ __device__ void win_head_run(const WinAttnArgs& a, const uint16_t* win, unsigned
   }
 }
 
-__global__ void __launch_bounds__(kWhThreads) win_head_kernel(const WinAttnArgs a, const uint16_t* win,
+__global__ void __launch_bounds__(kWhThreads) win_head_kernel(const WinAttnArgs a0, const uint16_t* win,
                                                               unsigned int* err) {
   extern __shared__ __align__(16) unsigned char wsm[];
   pdl_trigger();
-  win_head_run(a, win, err, blockIdx.x, wsm, [] { pdl_wait(); });
+  const size_t r = blockIdx.y;
+  const size_t hd = static_cast<size_t>(a0.H) * a0.d;
+  WinAttnArgs a = a0;
+  a.q = a0.q + r * hd;
+  a.out = a0.out + r * hd;
+  a.idx = a0.idx + r * a0.n;
+  a.cosv = a0.cosv + r * (a0.rope_dim / 2);
+  a.sinv = a0.sinv + r * (a0.rope_dim / 2);
+  win_head_run(a, win + r * a0.n * a0.d, err, blockIdx.x, wsm, [] { pdl_wait(); });
 }
 
 // Greedy token: argmax_logits (src/cli/dsv4_run.c:355; first maximum, strict
@@ -1183,12 +1288,17 @@ __global__ void __launch_bounds__(kWhThreads) win_head_kernel(const WinAttnArgs 
 // takes the chunks' results in chunk order with the same strict >. For
 // finite logits this is the sequential scan's answer.
 constexpr int kArgmaxCtas = 148;
+// blockIdx.y = row of a verify step's logits [rows][n] (its chunk results
+// at + row gridDim.x).
 __global__ void __launch_bounds__(256) argmax_chunks_kernel(const float* x, int n, float* cv,
                                                             int* ci) {
   __shared__ float sv[8];
   __shared__ int si[8];
   pdl_wait();
   pdl_trigger();
+  x += static_cast<size_t>(blockIdx.y) * n;
+  cv += blockIdx.y * gridDim.x;
+  ci += blockIdx.y * gridDim.x;
   const int chunk = (n + gridDim.x - 1) / gridDim.x;
   const int b = blockIdx.x * chunk, e = min(n, b + chunk);
   float bv = -INFINITY;
@@ -1213,10 +1323,14 @@ __global__ void __launch_bounds__(256) argmax_chunks_kernel(const float* x, int 
   }
 }
 
+// CTA r: row r's chunks.
 __global__ void argmax_final_kernel(const float* cv, const int* ci, int chunks, int* out) {
   pdl_wait();
   pdl_trigger();
   if (threadIdx.x != 0) return;
+  cv += blockIdx.x * chunks;
+  ci += blockIdx.x * chunks;
+  out += blockIdx.x;
   int best = 0;
   for (int c = 1; c < chunks; ++c)
     if (cv[c] > cv[best]) best = c;
@@ -1253,6 +1367,66 @@ __global__ void fp8_to_bf16_kernel(const uint8_t* codes, const uint8_t* scales, 
                               e8m0_decode(scales[static_cast<size_t>(r / 128) * scols + c / 128]));
     out[i] = static_cast<uint16_t>(__float_as_uint(bf16_round(v)) >> 16);
   }
+}
+
+// Greedy acceptance of a verify step (the reference CLI's chain,
+// src/cli/dsv4_run.c:951-1043 at temperature 0): rows [pending, d1 .. dk]
+// with targets argmax[r]; d(a+1) is accepted while it equals argmax[a].
+// Emits the accepted drafts and the bonus argmax[a] (a + 1 tokens), keeps
+// rows 0 .. a (the commit), and sets the next step up on the device: the
+// bonus becomes the pending row, the start advances by a + 1. stats[0] +=
+// tokens emitted, stats[1] += drafts accepted, stats[2] += verify steps.
+__global__ void verify_accept_kernel(int* tok, const int* argmax, int n, int* start, int* from,
+                                     int* count, long long* stats) {
+  pdl_wait();
+  pdl_trigger();
+  if (threadIdx.x != 0) return;
+  int a = 0;
+  while (a < n - 1 && tok[a + 1] == argmax[a]) ++a;
+  const int s0 = *start;
+  *from = s0;
+  *count = a + 1;
+  *start = s0 + a + 1;
+  tok[0] = argmax[a];
+  stats[0] += a + 1;
+  stats[1] += a;
+  stats[2] += 1;
+}
+
+// Commit of a verify step: the first *count rows' latents move from their
+// scratch rows (win + j) into the ring rows of their positions
+// ((*from + j) % win), in every layer's cache. CTA (layer, j).
+__global__ void verify_commit_kernel(const Fp8KvCache* caches, int win, const int* from,
+                                     const int* count) {
+  pdl_wait();
+  pdl_trigger();
+  const int j = blockIdx.y;
+  if (j >= *count) return;
+  const Fp8KvCache c = caches[blockIdx.x];
+  const long long src = win + j, dst = (*from + j) % win;
+  for (int i = threadIdx.x; i < c.nope; i += blockDim.x)
+    c.codes[dst * c.nope + i] = c.codes[src * c.nope + i];
+  for (int i = threadIdx.x; i < kKvScaleSlots; i += blockDim.x)
+    c.scales[dst * kKvScaleSlots + i] = c.scales[src * kKvScaleSlots + i];
+  for (int i = threadIdx.x; i < c.rope_dim; i += blockDim.x)
+    c.rope[dst * c.rope_dim + i] = c.rope[src * c.rope_dim + i];
+}
+
+// Uniform random draft ids for rows 1 .. n - 1 (the verify benchmark's
+// drafts): xorshift64 (the reference CLI's rng_next, src/cli/dsv4_run.c:
+// 248-254) modulo the vocabulary, one state advanced in row order.
+__global__ void draft_random_kernel(unsigned long long* state, int* tok, int n, int vocab) {
+  pdl_wait();
+  pdl_trigger();
+  if (threadIdx.x != 0) return;
+  unsigned long long x = *state;
+  for (int r = 1; r < n; ++r) {
+    x ^= x << 13;
+    x ^= x >> 7;
+    x ^= x << 17;
+    tok[r] = static_cast<int>(x % static_cast<unsigned long long>(vocab));
+  }
+  *state = x;
 }
 
 // ------------------------------------------------------- host side ----
@@ -1325,6 +1499,42 @@ struct dsv4cuda_decoder {
   cudaStream_t graph_stream = nullptr;
   bool stepped = false;
   std::string err;
+  // speculative verify (dsv4cuda_decoder_verify*): up to
+  // DSV4CUDA_VERIFY_MAX_ROWS rows per step, each row's buffers at the
+  // single-token size apart
+  struct Verify {
+    int* tok = nullptr;            // [V] row tokens: pending, then drafts
+    int* start = nullptr;          // [1] position of row 0
+    int* from = nullptr;           // [1] the last accepted step's start
+    int* count = nullptr;          // [1] its rows to commit
+    long long* stats = nullptr;    // [3] emitted, accepted, steps
+    unsigned long long* rng = nullptr;  // [1] draft generator state
+    float* state = nullptr;        // [V][mult][hid]
+    double* part = nullptr;        // [V][part_rs]
+    size_t part_rs = 0;
+    unsigned int* ticket = nullptr;  // [V]
+    float* mix = nullptr;          // [V][kMixMax]
+    float *post = nullptr, *comb = nullptr;  // [V][kHcMultMax], [V][kHcMultMax^2]
+    float* x = nullptr;            // [V][hid]
+    __half* xq = nullptr;          // [V][ld]
+    float* xs = nullptr;           // [V][ld / 128]
+    float *qr = nullptr, *q = nullptr, *kv = nullptr, *o = nullptr;  // [V][q_lora], [V][H d], [V][d], [V][H d]
+    float *oall = nullptr, *branch = nullptr;  // [V][G o_lora], [V][hid]
+    uint16_t* kvwin = nullptr;     // [V][window][d]
+    int* idx = nullptr;            // [V][window]
+    long long* row = nullptr;      // [V]
+    float *cosv = nullptr, *sinv = nullptr;  // [V][rope / 2]
+    float* logits = nullptr;       // [V][vocab]
+    int* argmax = nullptr;         // [V]
+    float* am_v = nullptr;         // [V][kArgmaxCtas]
+    int* am_i = nullptr;
+    dsv4::GemvItem* items = nullptr;    // [V]: item n - 1 maps rows 0 .. n - 1
+    dsv4::GemvItem* items_g = nullptr;  // [V][G]: the grouped wo_a's items for n rows
+    int* n_one = nullptr;
+    int* n_groups = nullptr;
+    dsv4::Fp8KvCache* caches = nullptr;  // [n_layers] for the commit kernel
+    dsv4::MoeWorkspace moe_ws{};
+  } v;
 };
 
 namespace {
@@ -1443,19 +1653,46 @@ cudaError_t fp8_gemv2(const uint8_t* W0, const uint8_t* S0, int rows0, float* y0
 }
 
 
-cudaError_t hc_pre(dsv4cuda_decoder* D, const float* fn, const float* scale, const float* base,
-                   const uint16_t* norm, int head, cudaStream_t st) {
+// The buffers one hyper-connection boundary works on: the single-token
+// step's, or a verify step's n rows (row r's buffers at the hc_row strides).
+struct HcRows {
+  float* state;
+  double* part;
+  size_t part_rs;
+  unsigned int* ticket;
+  float* mix;
+  float* post;
+  float* comb;
+  float* x;
+  const float* branch;
+  int n;
+};
+
+HcRows hc_single(dsv4cuda_decoder* D) {
+  return HcRows{D->state, D->part, 0, D->hc_ticket, D->mix, D->post, D->comb, D->x, D->branch, 1};
+}
+
+HcRows hc_verify(dsv4cuda_decoder* D, int n) {
+  auto& v = D->v;
+  return HcRows{v.state, v.part, v.part_rs, v.ticket, v.mix, v.post, v.comb, v.x, v.branch, n};
+}
+
+// The exact mode's hc_pre of row r (one launch pair per row).
+cudaError_t hc_pre(dsv4cuda_decoder* D, const HcRows& R, int r, const float* fn, const float* scale,
+                   const float* base, const uint16_t* norm, int head, cudaStream_t st) {
   const auto& c = D->cfg;
   const int n = c.hc_mult * c.hidden;
   const int rows = head ? c.hc_mult : (2 + c.hc_mult) * c.hc_mult;
+  const float* state = R.state + static_cast<size_t>(r) * n;
+  double* part = R.part + r * R.part_rs;
   if (c.hc_exact)
-    DEC_CHECK(dsv4::launch_pdl(dsv4::hc_mix_exact_kernel, dim3(1), dim3(32), 0, st, fn, rows,
-                               static_cast<const float*>(D->state), n, D->part));
+    DEC_CHECK(dsv4::launch_pdl(dsv4::hc_mix_exact_kernel, dim3(1), dim3(32), 0, st, fn, rows, state,
+                               n, part));
   else
     DEC_CHECK(dsv4::launch_pdl(dsv4::hc_mix_partial_kernel, dim3(D->nblk), dim3(dsv4::kMixThreads),
-                               0, st, fn, rows, static_cast<const float*>(D->state), n, D->part));
+                               0, st, fn, rows, state, n, part));
   dsv4::HcReduceArgs a{};
-  a.part = D->part;
+  a.part = part;
   a.nblk = c.hc_exact ? 1 : D->nblk;
   a.rows = rows;
   a.head = head;
@@ -1466,43 +1703,47 @@ cudaError_t hc_pre(dsv4cuda_decoder* D, const float* fn, const float* scale, con
   a.iters = c.hc_iters;
   a.hc_eps = c.hc_eps;
   a.rms_eps = c.rms_eps;
-  a.state = D->state;
+  a.state = state;
   a.norm = norm;
-  a.post = D->post;
-  a.comb = D->comb;
-  a.out = D->x;
+  a.post = R.post + r * dsv4::kHcMultMax;
+  a.comb = R.comb + r * dsv4::kHcMultMax * dsv4::kHcMultMax;
+  a.out = R.x + static_cast<size_t>(r) * c.hidden;
   return dsv4::launch_pdl(dsv4::hc_reduce_kernel, dim3(1), dim3(dsv4::kHcThreads), 0, st, a);
 }
 
-cudaError_t hc_post(dsv4cuda_decoder* D, cudaStream_t st) {
+cudaError_t hc_post(dsv4cuda_decoder* D, const HcRows& R, int r, cudaStream_t st) {
   const int hid = D->cfg.hidden;
   return dsv4::launch_pdl(dsv4::hc_post_kernel, dim3((hid + 255) / 256), dim3(256), 0, st,
-                          D->state, static_cast<const float*>(D->branch),
-                          static_cast<const float*>(D->post), static_cast<const float*>(D->comb),
+                          R.state + static_cast<size_t>(r) * D->cfg.hc_mult * hid,
+                          R.branch + static_cast<size_t>(r) * hid,
+                          static_cast<const float*>(R.post + r * dsv4::kHcMultMax),
+                          static_cast<const float*>(R.comb + r * dsv4::kHcMultMax * dsv4::kHcMultMax),
                           D->cfg.hc_mult, hid);
 }
 
-// One hyper-connection boundary: hc_post of D->branch (when `post`), then
-// hc_pre of the next branch into D->x, and when xq is set its FP8 quant into
-// xq / xs. The fast mode runs it as one launch, with a layer boundary's
-// Sinkhorn split forked onto D->hc_side (joined by hc_join before the next
-// boundary); the exact mode keeps the sequential mix chains in launches of
-// their own.
-cudaError_t hc_boundary(dsv4cuda_decoder* D, bool post, const float* fn, const float* scale,
-                        const float* base, const uint16_t* norm, int head, __half* xq,
-                        float* xs, cudaStream_t st) {
+// One hyper-connection boundary over R's rows: hc_post of R.branch (when
+// `post`), then hc_pre of the next branch into R.x, and when xq is set its
+// FP8 quant into xq / xs (row r at + r xq_ld). The fast mode runs it as one
+// launch (CTA row blockIdx.y = row), with a layer boundary's Sinkhorn split
+// forked onto D->hc_side (joined by hc_join before the next boundary); the
+// exact mode keeps the sequential mix chains in launches of their own.
+cudaError_t hc_boundary(dsv4cuda_decoder* D, const HcRows& R, bool post, const float* fn,
+                        const float* scale, const float* base, const uint16_t* norm, int head,
+                        __half* xq, float* xs, int xq_ld, cudaStream_t st) {
   const auto& c = D->cfg;
   if (c.hc_exact) {
-    if (post) DEC_CHECK(hc_post(D, st));
-    DEC_CHECK(hc_pre(D, fn, scale, base, norm, head, st));
-    return xq ? dsv4::launch_quant_fp8(D->x, c.hidden, c.hidden, 1, xq, xs, c.hidden, st)
+    for (int r = 0; r < R.n; ++r) {
+      if (post) DEC_CHECK(hc_post(D, R, r, st));
+      DEC_CHECK(hc_pre(D, R, r, fn, scale, base, norm, head, st));
+    }
+    return xq ? dsv4::launch_quant_fp8(R.x, c.hidden, c.hidden, R.n, xq, xs, xq_ld, st)
               : cudaSuccess;
   }
   dsv4::HcFusedArgs a{};
-  a.state = D->state;
-  a.branch = post ? D->branch : nullptr;
-  a.post_in = D->post;
-  a.comb_in = D->comb;
+  a.state = R.state;
+  a.branch = post ? R.branch : nullptr;
+  a.post_in = R.post;
+  a.comb_in = R.comb;
   a.fn = fn;
   a.rows = head ? c.hc_mult : (2 + c.hc_mult) * c.hc_mult;
   a.head = head;
@@ -1512,14 +1753,16 @@ cudaError_t hc_boundary(dsv4cuda_decoder* D, bool post, const float* fn, const f
   a.hc_eps = c.hc_eps;
   a.rms_eps = c.rms_eps;
   a.norm = norm;
-  a.mix_out = D->mix;
-  a.out = D->x;
+  a.mix_out = R.mix;
+  a.out = R.x;
   a.xq = xq;
   a.xs = xs;
-  a.part = D->part;
-  a.ticket = D->hc_ticket;
+  a.part = R.part;
+  a.ticket = R.ticket;
+  a.xq_ld = xq_ld;
+  a.part_rs = R.part_rs;
   const int cols = dsv4::kHcfThreads / c.hc_mult;
-  const dim3 grid((c.hidden + cols - 1) / cols), block(dsv4::kHcfThreads);
+  const dim3 grid((c.hidden + cols - 1) / cols, R.n), block(dsv4::kHcfThreads);
   cudaError_t e;
   switch (c.hc_mult) {
     case 1: e = dsv4::launch_pdl(dsv4::hc_fused_kernel<1>, grid, block, 0, st, a); break;
@@ -1531,12 +1774,12 @@ cudaError_t hc_boundary(dsv4cuda_decoder* D, bool post, const float* fn, const f
   // the split of the post / comb mixes beside the branch
   DEC_CHECK(cudaEventRecord(D->hc_fork, st));
   DEC_CHECK(cudaStreamWaitEvent(D->hc_side, D->hc_fork, 0));
-  const float* mx = D->mix;
+  const float* mx = R.mix;
   switch (c.hc_mult) {
-    case 1: dsv4::hc_sinkhorn_kernel<1><<<1, 32, 0, D->hc_side>>>(mx, scale, base, c.hc_iters, c.hc_eps, D->post, D->comb); break;
-    case 2: dsv4::hc_sinkhorn_kernel<2><<<1, 32, 0, D->hc_side>>>(mx, scale, base, c.hc_iters, c.hc_eps, D->post, D->comb); break;
-    case 3: dsv4::hc_sinkhorn_kernel<3><<<1, 32, 0, D->hc_side>>>(mx, scale, base, c.hc_iters, c.hc_eps, D->post, D->comb); break;
-    default: dsv4::hc_sinkhorn_kernel<4><<<1, 32, 0, D->hc_side>>>(mx, scale, base, c.hc_iters, c.hc_eps, D->post, D->comb); break;
+    case 1: dsv4::hc_sinkhorn_kernel<1><<<R.n, 32, 0, D->hc_side>>>(mx, scale, base, c.hc_iters, c.hc_eps, R.post, R.comb); break;
+    case 2: dsv4::hc_sinkhorn_kernel<2><<<R.n, 32, 0, D->hc_side>>>(mx, scale, base, c.hc_iters, c.hc_eps, R.post, R.comb); break;
+    case 3: dsv4::hc_sinkhorn_kernel<3><<<R.n, 32, 0, D->hc_side>>>(mx, scale, base, c.hc_iters, c.hc_eps, R.post, R.comb); break;
+    default: dsv4::hc_sinkhorn_kernel<4><<<R.n, 32, 0, D->hc_side>>>(mx, scale, base, c.hc_iters, c.hc_eps, R.post, R.comb); break;
   }
   DEC_CHECK(cudaGetLastError());
   return cudaEventRecord(D->hc_join, D->hc_side);
@@ -1669,14 +1912,15 @@ cudaError_t step(dsv4cuda_decoder* D, cudaStream_t st) {
   for (size_t li = 0; li < D->layers.size(); ++li) {
     auto& L = D->layers[li];
     const auto& w = L.w;
-    DEC_CHECK(hc_boundary(D, li > 0, w.hc_attn_fn, w.hc_attn_scale, w.hc_attn_base, w.attn_norm,
-                          0, D->xq, D->xs, st));
+    DEC_CHECK(hc_boundary(D, hc_single(D), li > 0, w.hc_attn_fn, w.hc_attn_scale, w.hc_attn_base,
+                          w.attn_norm, 0, D->xq, D->xs, D->ld, st));
     DEC_CHECK(attention(D, L, st));
     // the MoE layer's input quant comes out of the boundary kernel (its
     // shared-expert item for the one token was written at create)
     const bool local = D->ep.empty();
-    DEC_CHECK(hc_boundary(D, true, w.hc_ffn_fn, w.hc_ffn_scale, w.hc_ffn_base, w.ffn_norm, 0,
-                          local ? D->moe_ws.xq : nullptr, local ? D->moe_ws.xs : nullptr, st));
+    DEC_CHECK(hc_boundary(D, hc_single(D), true, w.hc_ffn_fn, w.hc_ffn_scale, w.hc_ffn_base,
+                          w.ffn_norm, 0, local ? D->moe_ws.xq : nullptr,
+                          local ? D->moe_ws.xs : nullptr, c.hidden, st));
     if (!local) {
       if (dsv4cuda_moe_forward_ep_tokens(D->ep[li], D->x, 1, D->branch, st) != 0)
         return cudaErrorLaunchFailure;
@@ -1687,8 +1931,8 @@ cudaError_t step(dsv4cuda_decoder* D, cudaStream_t st) {
   }
   // the last layer's hc_post, model_head + head_logits (src/dsv4/dsv4_model.c:
   // 7755-7760), argmax
-  DEC_CHECK(hc_boundary(D, true, D->g.hc_head_fn, D->g.hc_head_scale, D->g.hc_head_base,
-                        D->g.norm, 1, nullptr, nullptr, st));
+  DEC_CHECK(hc_boundary(D, hc_single(D), true, D->g.hc_head_fn, D->g.hc_head_scale,
+                        D->g.hc_head_base, D->g.norm, 1, nullptr, nullptr, 0, st));
   dsv4::Bf16GemvArgs ha{};
   ha.W = D->g.head;
   ha.in = hid;
@@ -1708,6 +1952,255 @@ cudaError_t step(dsv4cuda_decoder* D, cudaStream_t st) {
   return dsv4::launch_pdl(dsv4::argmax_final_kernel, dim3(1), dim3(32), 0, st,
                           static_cast<const float*>(D->am_v), static_cast<const int*>(D->am_i),
                           chunks, D->argmax);
+}
+
+// The verify step's buffers (DSV4CUDA_VERIFY_MAX_ROWS rows), its GEMV items
+// for every row count, the layer caches for the commit kernel and a MoE
+// workspace for that many tokens. Called by create after the layers exist.
+bool verify_alloc(dsv4cuda_decoder* D) {
+  const auto& c = D->cfg;
+  auto& v = D->v;
+  constexpr int V = DSV4CUDA_VERIFY_MAX_ROWS;
+  const int H = c.n_heads, d = c.head_dim, half = c.rope_dim / 2, G = c.o_groups;
+  const size_t hid = c.hidden, hd = static_cast<size_t>(H) * d;
+  bool ok = true;
+  auto chk = [&](const void* p) { ok = ok && p != nullptr; };
+  chk(v.tok = dalloc<int>(D, V));
+  chk(v.start = dalloc<int>(D, 1));
+  chk(v.from = dalloc<int>(D, 1));
+  chk(v.count = dalloc<int>(D, 1));
+  chk(v.stats = dalloc<long long>(D, 3));
+  chk(v.rng = dalloc<unsigned long long>(D, 1));
+  chk(v.state = dalloc<float>(D, V * c.hc_mult * hid));
+  v.part_rs = std::max(static_cast<size_t>(D->nblk) * (dsv4::kMixMax + 1),
+                       static_cast<size_t>(dsv4::kHcfMaxCtas) * 32);
+  chk(v.part = dalloc<double>(D, V * v.part_rs));
+  chk(v.ticket = dalloc<unsigned int>(D, V));
+  chk(v.mix = dalloc<float>(D, V * dsv4::kMixMax));
+  chk(v.post = dalloc<float>(D, V * dsv4::kHcMultMax));
+  chk(v.comb = dalloc<float>(D, V * dsv4::kHcMultMax * dsv4::kHcMultMax));
+  chk(v.x = dalloc<float>(D, V * hid));
+  chk(v.xq = dalloc<__half>(D, static_cast<size_t>(V) * D->ld));
+  chk(v.xs = dalloc<float>(D, static_cast<size_t>(V) * D->ld / 128));
+  chk(v.qr = dalloc<float>(D, static_cast<size_t>(V) * c.q_lora));
+  chk(v.q = dalloc<float>(D, V * hd));
+  chk(v.kv = dalloc<float>(D, static_cast<size_t>(V) * d));
+  chk(v.o = dalloc<float>(D, V * hd));
+  chk(v.oall = dalloc<float>(D, static_cast<size_t>(V) * G * c.o_lora));
+  chk(v.branch = dalloc<float>(D, V * hid));
+  if (D->win_staged) chk(v.kvwin = dalloc<uint16_t>(D, static_cast<size_t>(V) * c.window * d));
+  chk(v.idx = dalloc<int>(D, static_cast<size_t>(V) * c.window));
+  chk(v.row = dalloc<long long>(D, V));
+  chk(v.cosv = dalloc<float>(D, static_cast<size_t>(V) * half));
+  chk(v.sinv = dalloc<float>(D, static_cast<size_t>(V) * half));
+  chk(v.logits = dalloc<float>(D, static_cast<size_t>(V) * c.vocab));
+  chk(v.argmax = dalloc<int>(D, V));
+  chk(v.am_v = dalloc<float>(D, static_cast<size_t>(V) * dsv4::kArgmaxCtas));
+  chk(v.am_i = dalloc<int>(D, static_cast<size_t>(V) * dsv4::kArgmaxCtas));
+  chk(v.items = dalloc<dsv4::GemvItem>(D, V));
+  chk(v.items_g = dalloc<dsv4::GemvItem>(D, static_cast<size_t>(V) * G));
+  chk(v.n_one = dalloc<int>(D, 1));
+  chk(v.n_groups = dalloc<int>(D, 1));
+  chk(v.caches = dalloc<dsv4::Fp8KvCache>(D, D->layers.size()));
+  if (!ok) return false;
+  std::vector<dsv4::GemvItem> it(V), itg(static_cast<size_t>(V) * G);
+  for (int n = 1; n <= V; ++n) {
+    auto& a = it[n - 1];
+    a = dsv4::GemvItem{};
+    a.mat = 0;
+    a.ntok = n;
+    for (int t = 0; t < n; ++t) a.tok[t] = dsv4::TokMap{t, t};
+    for (int g = 0; g < G; ++g) {
+      auto& b = itg[static_cast<size_t>(n - 1) * G + g];
+      b = dsv4::GemvItem{};
+      b.mat = g;
+      b.ntok = n;
+      for (int t = 0; t < n; ++t) b.tok[t] = dsv4::TokMap{t * G + g, t * G + g};
+    }
+  }
+  std::vector<dsv4::Fp8KvCache> caches;
+  for (const auto& L : D->layers) caches.push_back(L.cache);
+  const int one = 1;
+  const unsigned long long seed = 0x9E3779B97F4A7C15ull;
+  if (cudaMemcpy(v.items, it.data(), sizeof(dsv4::GemvItem) * it.size(), cudaMemcpyHostToDevice) != cudaSuccess ||
+      cudaMemcpy(v.items_g, itg.data(), sizeof(dsv4::GemvItem) * itg.size(), cudaMemcpyHostToDevice) != cudaSuccess ||
+      cudaMemcpy(v.n_one, &one, sizeof(int), cudaMemcpyHostToDevice) != cudaSuccess ||
+      cudaMemcpy(v.n_groups, &G, sizeof(int), cudaMemcpyHostToDevice) != cudaSuccess ||
+      cudaMemcpy(v.rng, &seed, sizeof(seed), cudaMemcpyHostToDevice) != cudaSuccess ||
+      cudaMemcpy(v.caches, caches.data(), sizeof(dsv4::Fp8KvCache) * caches.size(),
+                 cudaMemcpyHostToDevice) != cudaSuccess)
+    return false;
+  dsv4::MoeConfig mc = D->layers[0].mc;
+  mc.hash_vocab = 0;
+  char* base = dalloc<char>(D, dsv4::moe_workspace_bytes(mc, V));
+  if (!base) return false;
+  dsv4::moe_workspace_carve(&v.moe_ws, mc, V, base);
+  return true;
+}
+
+// attention_forward_batch_projected (src/dsv4/dsv4_model.c:5449-5572) for a
+// verify step's n rows: every projection one GEMV over the n rows (the
+// weights stream once), each row's latent into its scratch cache row, then
+// every row's sparse_attn over its own window (which holds the earlier
+// verify rows' latents, as the reference's row-by-row pass sees them).
+// v.x arrives with its FP8 quant in v.xq / v.xs; the branch goes to v.branch.
+cudaError_t verify_attention(dsv4cuda_decoder* D, dsv4::Layer& L, int n, cudaStream_t st) {
+  const auto& c = D->cfg;
+  auto& v = D->v;
+  const auto& w = L.w;
+  const int H = c.n_heads, d = c.head_dim, ql = c.q_lora, half = c.rope_dim / 2;
+  const int G = c.o_groups, ol = c.o_lora, hid = c.hidden;
+  auto gemv8 = [&](const uint8_t* W, const uint8_t* S, int in, int rows, float* y) {
+    dsv4::Fp8GemvArgs a{};
+    a.W[0] = W;
+    a.S[0] = S;
+    a.in = in;
+    a.rows = rows;
+    a.round_out = 1;
+    a.act = dsv4::QAct{v.xq, v.xs, D->ld, nullptr};
+    a.Y[0] = y;
+    a.items = v.items + (n - 1);
+    a.n_items = v.n_one;
+    a.max_items = 1;
+    return dsv4::launch_fp8_gemv(a, false, n, st);
+  };
+  DEC_CHECK(gemv8(w.wq_a, w.wq_a_s, hid, ql, v.qr));
+  DEC_CHECK(gemv8(w.wkv, w.wkv_s, hid, d, v.kv));
+  // per row: kv_norm + RoPE + KV write into the scratch row; q_norm + quant
+  dsv4::NormTailArgs kt{};
+  kt.x = v.kv;
+  kt.n = d;
+  kt.w = w.kv_norm;
+  kt.eps = c.rms_eps;
+  kt.half = half;
+  kt.cosv = v.cosv;
+  kt.sinv = v.sinv;
+  kt.cache = L.cache;
+  kt.row = v.row;
+  kt.x_rs = d;
+  kt.cs_rs = half;
+  dsv4::NormTailArgs qt{};
+  qt.x = v.qr;
+  qt.n = ql;
+  qt.w = w.q_norm;
+  qt.eps = c.rms_eps;
+  qt.xq = v.xq;
+  qt.xs = v.xs;
+  qt.x_rs = ql;
+  qt.xq_ld = D->ld;
+  DEC_CHECK(dsv4::launch_pdl(dsv4::norm_tail_kernel, dim3(2, n), dim3(256),
+                             sizeof(float) * std::max(d, ql), st, kt, qt));
+  // every row's window as BF16, now that all the rows' latents are cached
+  dsv4::NormTailArgs sa = kt;
+  sa.win = v.kvwin;
+  sa.idx = v.idx;
+  sa.n_win = c.window;
+  DEC_CHECK(dsv4::launch_pdl(dsv4::stage_rows_kernel, dim3((c.window + 7) / 8, n), dim3(256), 0,
+                             st, sa));
+  DEC_CHECK(gemv8(w.wq_b, w.wq_b_s, ql, H * d, v.q));
+  dsv4::WinAttnArgs wa{};
+  wa.q = v.q;
+  wa.cache = L.cache;
+  wa.idx = v.idx;
+  wa.sink = w.attn_sink;
+  wa.cosv = v.cosv;
+  wa.sinv = v.sinv;
+  wa.H = H;
+  wa.d = d;
+  wa.n = c.window;
+  wa.rope_dim = c.rope_dim;
+  wa.scale = 1.0f / sqrtf(static_cast<float>(d));
+  wa.out = v.o;
+  wa.q_raw = 1;
+  wa.q_eps = c.rms_eps;
+  DEC_CHECK(hc_join(D, st));
+  DEC_CHECK(dsv4::launch_pdl(dsv4::win_head_kernel, dim3(H, n), dim3(dsv4::kWhThreads),
+                             dsv4::win_head_smem(c.window, d), st, wa,
+                             static_cast<const uint16_t*>(v.kvwin), dsv4::device_error_word()));
+  // grouped BF16 wo_a over the rows, quant, FP8 wo_b
+  dsv4::Bf16GemvArgs ga{};
+  ga.W = L.wo_a;
+  ga.w_stride = static_cast<size_t>(ol) * (H * d / G);
+  ga.in = H * d / G;
+  ga.rows = ol;
+  ga.round_out = 1;
+  ga.x = v.o;
+  ga.ldx = H * d / G;
+  ga.Y = v.oall;
+  ga.items = v.items_g + static_cast<size_t>(n - 1) * G;
+  ga.n_items = v.n_groups;
+  ga.max_items = G;
+  ga.static_items = 1;
+  DEC_CHECK(dsv4::launch_bf16_gemv(ga, n, st));
+  DEC_CHECK(dsv4::launch_quant_fp8(v.oall, G * ol, G * ol, n, v.xq, v.xs, D->ld, st));
+  return gemv8(w.wo_b, w.wo_b_s, G * ol, hid, v.branch);
+}
+
+// dsv4_prefill_capture with all_logits (src/dsv4/dsv4_model.c:8434-8529):
+// rows v.tok[0 .. n) at positions *v.start + r through every layer
+// layer-major (forward_loaded_layer_batch, :7577-7753), then the HC head,
+// the vocab head of every row (compute_logits_batch, :7784) and each row's
+// argmax. The ring is not written; the rows' latents wait in the scratch
+// rows for a commit.
+cudaError_t verify(dsv4cuda_decoder* D, int n, cudaStream_t st) {
+  const auto& c = D->cfg;
+  auto& v = D->v;
+  const int hid = c.hidden, half = c.rope_dim / 2;
+  DEC_CHECK(dsv4::launch_pdl(dsv4::embed_kernel, dim3((hid + 255) / 256, n), dim3(256), 0, st,
+                             D->g.embed, static_cast<const int*>(v.tok), c.vocab, hid, c.hc_mult,
+                             v.state));
+  DEC_CHECK(dsv4::launch_pdl(dsv4::verify_position_kernel, dim3(n), dim3(128), 0, st,
+                             static_cast<const int*>(v.start), c.window, half, c.max_context,
+                             static_cast<const float*>(D->cos_tab),
+                             static_cast<const float*>(D->sin_tab), v.idx, v.row, v.cosv, v.sinv));
+  const HcRows R = hc_verify(D, n);
+  dsv4::MoeExecOptions opt;
+  if (!c.hc_exact) opt.join = D->hc_join;  // the FFN boundary's split, before the combine
+  for (size_t li = 0; li < D->layers.size(); ++li) {
+    auto& L = D->layers[li];
+    const auto& w = L.w;
+    DEC_CHECK(hc_boundary(D, R, li > 0, w.hc_attn_fn, w.hc_attn_scale, w.hc_attn_base,
+                          w.attn_norm, 0, v.xq, v.xs, D->ld, st));
+    DEC_CHECK(verify_attention(D, L, n, st));
+    DEC_CHECK(hc_boundary(D, R, true, w.hc_ffn_fn, w.hc_ffn_scale, w.hc_ffn_base, w.ffn_norm, 0,
+                          nullptr, nullptr, 0, st));
+    DEC_CHECK(dsv4::moe_forward(L.mc, L.mw, v.moe_ws, v.x, v.tok, n, v.branch, st, opt));
+  }
+  DEC_CHECK(hc_boundary(D, R, true, D->g.hc_head_fn, D->g.hc_head_scale, D->g.hc_head_base,
+                        D->g.norm, 1, nullptr, nullptr, 0, st));
+  dsv4::Bf16GemvArgs ha{};
+  ha.W = D->g.head;
+  ha.in = hid;
+  ha.rows = c.vocab;
+  ha.round_out = 0;
+  ha.x = v.x;
+  ha.ldx = hid;
+  ha.Y = v.logits;
+  ha.items = v.items + (n - 1);
+  ha.n_items = v.n_one;
+  ha.max_items = 1;
+  ha.static_items = 1;
+  DEC_CHECK(dsv4::launch_bf16_gemv(ha, n, st));
+  const int chunks = std::min(dsv4::kArgmaxCtas, c.vocab);
+  DEC_CHECK(dsv4::launch_pdl(dsv4::argmax_chunks_kernel, dim3(chunks, n), dim3(256), 0, st,
+                             static_cast<const float*>(v.logits), c.vocab, v.am_v, v.am_i));
+  return dsv4::launch_pdl(dsv4::argmax_final_kernel, dim3(n), dim3(32), 0, st,
+                          static_cast<const float*>(v.am_v), static_cast<const int*>(v.am_i),
+                          chunks, v.argmax);
+}
+
+cudaError_t verify_commit(dsv4cuda_decoder* D, const int* from, cudaStream_t st) {
+  return dsv4::launch_pdl(dsv4::verify_commit_kernel,
+                          dim3(static_cast<unsigned>(D->layers.size()), DSV4CUDA_VERIFY_MAX_ROWS),
+                          dim3(128), 0, st, static_cast<const dsv4::Fp8KvCache*>(D->v.caches),
+                          D->cfg.window, from, static_cast<const int*>(D->v.count));
+}
+
+const char* verify_unsupported(const dsv4cuda_decoder* D, int n) {
+  if (n < 1 || n > DSV4CUDA_VERIFY_MAX_ROWS) return "n_rows must be 1 .. DSV4CUDA_VERIFY_MAX_ROWS";
+  if (!D->ep.empty()) return "the verify step runs the local MoE layers (no expert parallelism)";
+  if (!D->win_staged || !D->v.kvwin) return "the window does not fit the one-launch attention";
+  return nullptr;
 }
 
 bool cfg_ok(const dsv4cuda_decoder_config* c) {
@@ -1854,10 +2347,12 @@ DSV4_API int dsv4cuda_decoder_create(dsv4cuda_decoder** out, const dsv4cuda_deco
     }
     L.cache.nope = nope;
     L.cache.rope_dim = c.rope_dim;
-    L.cache.rows = c.window;
-    L.cache.codes = dalloc<uint8_t>(D, static_cast<size_t>(c.window) * nope);
-    L.cache.scales = dalloc<uint8_t>(D, static_cast<size_t>(c.window) * dsv4::kKvScaleSlots);
-    L.cache.rope = dalloc<uint16_t>(D, static_cast<size_t>(c.window) * c.rope_dim);
+    // rows [0, window): the ring; [window, window + V): a verify step's rows
+    const size_t crows = static_cast<size_t>(c.window) + DSV4CUDA_VERIFY_MAX_ROWS;
+    L.cache.rows = static_cast<long long>(crows);
+    L.cache.codes = dalloc<uint8_t>(D, crows * nope);
+    L.cache.scales = dalloc<uint8_t>(D, crows * dsv4::kKvScaleSlots);
+    L.cache.rope = dalloc<uint16_t>(D, crows * c.rope_dim);
     const int rows = c.o_groups * c.o_lora, cols = H * d / c.o_groups;
     if (w.wo_a) {
       L.wo_a = const_cast<uint16_t*>(w.wo_a);
@@ -1883,6 +2378,10 @@ DSV4_API int dsv4cuda_decoder_create(dsv4cuda_decoder** out, const dsv4cuda_deco
     L.mw = dsv4::MoeWeights{m.gate_w, m.bias, m.tid2eid, m.w1, m.s1, m.w3, m.s3, m.w2, m.s2,
                             m.sh1, m.sh1s, m.sh3, m.sh3s, m.sh2, m.sh2s};
     D->layers.push_back(L);
+  }
+  if (!verify_alloc(D)) {
+    dsv4cuda_decoder_destroy(D);
+    return fail("dsv4cuda_decoder_create: out of device memory (verify buffers)");
   }
   // one MoE workspace serves every layer (their forwards run in stream order)
   {
@@ -1943,9 +2442,10 @@ DSV4_API int dsv4cuda_decoder_reset(dsv4cuda_decoder* D, void* stream) {
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const auto& c = D->cfg;
   for (auto& L : D->layers) {
-    cudaMemsetAsync(L.cache.codes, 0, static_cast<size_t>(c.window) * L.cache.nope, st);
-    cudaMemsetAsync(L.cache.scales, 0, static_cast<size_t>(c.window) * dsv4::kKvScaleSlots, st);
-    cudaMemsetAsync(L.cache.rope, 0, static_cast<size_t>(c.window) * c.rope_dim * 2, st);
+    const size_t rows = static_cast<size_t>(L.cache.rows);
+    cudaMemsetAsync(L.cache.codes, 0, rows * L.cache.nope, st);
+    cudaMemsetAsync(L.cache.scales, 0, rows * dsv4::kKvScaleSlots, st);
+    cudaMemsetAsync(L.cache.rope, 0, rows * c.rope_dim * 2, st);
   }
   const cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? 0 : fail("dsv4cuda_decoder_reset: %s", cudaGetErrorString(e));
@@ -2053,7 +2553,7 @@ DSV4_API int dsv4cuda_decoder_cache(dsv4cuda_decoder* D, int layer, dsv4cuda_kv_
   out->rope = c.rope;
   out->nope = c.nope;
   out->rope_dim = c.rope_dim;
-  out->rows = c.rows;
+  out->rows = D->cfg.window;  // the ring (a verify step's scratch rows follow it)
   return 0;
 }
 
@@ -2066,3 +2566,89 @@ DSV4_API int dsv4cuda_decoder_step(dsv4cuda_decoder* D, void* stream) {
   const cudaError_t e = step(D, static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? 0 : fail("dsv4cuda_decoder_step: %s", cudaGetErrorString(e));
 }
+
+DSV4_API int dsv4cuda_decoder_verify_device(dsv4cuda_decoder* D, int n_rows, void* stream) {
+  if (!D) return fail("dsv4cuda_decoder_verify_device: null decoder");
+  if (const char* why = verify_unsupported(D, n_rows))
+    return fail("dsv4cuda_decoder_verify_device: %s", why);
+  const cudaError_t e = verify(D, n_rows, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? 0 : fail("dsv4cuda_decoder_verify_device: %s", cudaGetErrorString(e));
+}
+
+DSV4_API int dsv4cuda_decoder_verify(dsv4cuda_decoder* D, const int* tokens, int n_rows,
+                                     int start_position, float* all_logits, int* argmax) {
+  if (!D || !tokens) return fail("dsv4cuda_decoder_verify: bad arguments");
+  if (const char* why = verify_unsupported(D, n_rows))
+    return fail("dsv4cuda_decoder_verify: %s", why);
+  if (start_position < 0 || start_position + n_rows > D->cfg.max_context)
+    return fail("dsv4cuda_decoder_verify: positions out of range");
+  for (int r = 0; r < n_rows; ++r)
+    if (tokens[r] < 0 || tokens[r] >= D->cfg.vocab)
+      return fail("dsv4cuda_decoder_verify: token out of range");
+  cudaError_t e = cudaSuccess;
+  if (!D->graph_stream) e = cudaStreamCreateWithFlags(&D->graph_stream, cudaStreamNonBlocking);
+  cudaStream_t st = D->graph_stream;
+  if (e == cudaSuccess)
+    e = cudaMemcpyAsync(D->v.tok, tokens, sizeof(int) * n_rows, cudaMemcpyHostToDevice, st);
+  if (e == cudaSuccess)
+    e = cudaMemcpyAsync(D->v.start, &start_position, sizeof(int), cudaMemcpyHostToDevice, st);
+  if (e == cudaSuccess) e = verify(D, n_rows, st);
+  if (e == cudaSuccess && all_logits)
+    e = cudaMemcpyAsync(all_logits, D->v.logits, sizeof(float) * n_rows * D->cfg.vocab,
+                        cudaMemcpyDeviceToHost, st);
+  if (e == cudaSuccess && argmax)
+    e = cudaMemcpyAsync(argmax, D->v.argmax, sizeof(int) * n_rows, cudaMemcpyDeviceToHost, st);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+  return e == cudaSuccess ? 0 : fail("dsv4cuda_decoder_verify: %s", cudaGetErrorString(e));
+}
+
+DSV4_API int dsv4cuda_decoder_commit(dsv4cuda_decoder* D, int n_keep, void* stream) {
+  if (!D || n_keep < 0 || n_keep > DSV4CUDA_VERIFY_MAX_ROWS)
+    return fail("dsv4cuda_decoder_commit: bad arguments");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  cudaError_t e = cudaMemcpyAsync(D->v.count, &n_keep, sizeof(int), cudaMemcpyHostToDevice, st);
+  if (e == cudaSuccess) e = verify_commit(D, D->v.start, st);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+  return e == cudaSuccess ? 0 : fail("dsv4cuda_decoder_commit: %s", cudaGetErrorString(e));
+}
+
+DSV4_API int dsv4cuda_decoder_accept_greedy(dsv4cuda_decoder* D, int n_rows, void* stream) {
+  if (!D || n_rows < 1 || n_rows > DSV4CUDA_VERIFY_MAX_ROWS)
+    return fail("dsv4cuda_decoder_accept_greedy: bad arguments");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  auto& v = D->v;
+  cudaError_t e = dsv4::launch_pdl(dsv4::verify_accept_kernel, dim3(1), dim3(32), 0, st, v.tok,
+                                   static_cast<const int*>(v.argmax), n_rows, v.start, v.from,
+                                   v.count, v.stats);
+  if (e == cudaSuccess) e = verify_commit(D, v.from, st);
+  return e == cudaSuccess ? 0 : fail("dsv4cuda_decoder_accept_greedy: %s", cudaGetErrorString(e));
+}
+
+DSV4_API int dsv4cuda_decoder_draft_random(dsv4cuda_decoder* D, int n_rows, void* stream) {
+  if (!D || n_rows < 1 || n_rows > DSV4CUDA_VERIFY_MAX_ROWS)
+    return fail("dsv4cuda_decoder_draft_random: bad arguments");
+  const cudaError_t e = dsv4::launch_pdl(dsv4::draft_random_kernel, dim3(1), dim3(32), 0,
+                                         static_cast<cudaStream_t>(stream), D->v.rng, D->v.tok,
+                                         n_rows, D->cfg.vocab);
+  return e == cudaSuccess ? 0 : fail("dsv4cuda_decoder_draft_random: %s", cudaGetErrorString(e));
+}
+
+DSV4_API int dsv4cuda_decoder_verify_stats(dsv4cuda_decoder* D, long long* stats3) {
+  if (!D || !stats3) return fail("dsv4cuda_decoder_verify_stats: bad arguments");
+  cudaError_t e = cudaDeviceSynchronize();
+  if (e == cudaSuccess) e = cudaMemcpy(stats3, D->v.stats, 3 * sizeof(long long), cudaMemcpyDeviceToHost);
+  return e == cudaSuccess ? 0 : fail("dsv4cuda_decoder_verify_stats: %s", cudaGetErrorString(e));
+}
+
+DSV4_API int dsv4cuda_decoder_verify_pending(dsv4cuda_decoder* D, int* token, int* position) {
+  if (!D || !token || !position) return fail("dsv4cuda_decoder_verify_pending: bad arguments");
+  cudaError_t e = cudaDeviceSynchronize();
+  if (e == cudaSuccess) e = cudaMemcpy(token, D->v.tok, sizeof(int), cudaMemcpyDeviceToHost);
+  if (e == cudaSuccess) e = cudaMemcpy(position, D->v.start, sizeof(int), cudaMemcpyDeviceToHost);
+  return e == cudaSuccess ? 0 : fail("dsv4cuda_decoder_verify_pending: %s", cudaGetErrorString(e));
+}
+
+DSV4_API int* dsv4cuda_decoder_verify_tokens(dsv4cuda_decoder* D) { return D ? D->v.tok : nullptr; }
+DSV4_API int* dsv4cuda_decoder_verify_start(dsv4cuda_decoder* D) { return D ? D->v.start : nullptr; }
+DSV4_API float* dsv4cuda_decoder_verify_logits(dsv4cuda_decoder* D) { return D ? D->v.logits : nullptr; }
+DSV4_API int* dsv4cuda_decoder_verify_argmax(dsv4cuda_decoder* D) { return D ? D->v.argmax : nullptr; }

@@ -787,7 +787,18 @@ for _n, _r, _a in (("dsv4cuda_decoder_create", C.c_int, [vp, vp, vp, vp]),
                    ("dsv4cuda_decoder_read", C.c_int, [vp, vp, vp]),
                    ("dsv4cuda_decoder_cache", C.c_int, [vp, C.c_int, vp]),
                    ("dsv4cuda_decoder_step_kernels", C.c_int, [vp]),
-                   ("dsv4cuda_decoder_set_moe_layers", C.c_int, [vp, vp, C.c_int])):
+                   ("dsv4cuda_decoder_set_moe_layers", C.c_int, [vp, vp, C.c_int]),
+                   ("dsv4cuda_decoder_verify", C.c_int, [vp, vp, C.c_int, C.c_int, vp, vp]),
+                   ("dsv4cuda_decoder_verify_device", C.c_int, [vp, C.c_int, vp]),
+                   ("dsv4cuda_decoder_commit", C.c_int, [vp, C.c_int, vp]),
+                   ("dsv4cuda_decoder_accept_greedy", C.c_int, [vp, C.c_int, vp]),
+                   ("dsv4cuda_decoder_draft_random", C.c_int, [vp, C.c_int, vp]),
+                   ("dsv4cuda_decoder_verify_stats", C.c_int, [vp, vp]),
+                   ("dsv4cuda_decoder_verify_pending", C.c_int, [vp, vp, vp]),
+                   ("dsv4cuda_decoder_verify_tokens", C.c_void_p, [vp]),
+                   ("dsv4cuda_decoder_verify_start", C.c_void_p, [vp]),
+                   ("dsv4cuda_decoder_verify_logits", C.c_void_p, [vp]),
+                   ("dsv4cuda_decoder_verify_argmax", C.c_void_p, [vp])):
     getattr(lib, _n).restype = _r
     getattr(lib, _n).argtypes = _a
 
@@ -836,6 +847,59 @@ class Decoder:
         if lib.dsv4cuda_decoder_step_device(self.handle, token.data_ptr(), position.data_ptr(),
                                             _stream(stream)) != 0:
             raise Dsv4CudaError(lib.dsv4cuda_decoder_last_error().decode())
+
+    VERIFY_MAX_ROWS = 8
+
+    def verify(self, tokens, start_position):
+        """dsv4_prefill_capture with all_logits: (logits [n][vocab] float32,
+        argmax [n] int32) of the rows `tokens` at positions start_position..;
+        the ring is untouched until commit()."""
+        t = np.ascontiguousarray(tokens, np.int32)
+        n = len(t)
+        logits = np.empty((n, self.vocab), np.float32)
+        am = np.empty(n, np.int32)
+        if lib.dsv4cuda_decoder_verify(self.handle, t.ctypes.data, n, int(start_position),
+                                       logits.ctypes.data, am.ctypes.data) != 0:
+            raise Dsv4CudaError(lib.dsv4cuda_decoder_last_error().decode())
+        return logits, am
+
+    def commit(self, n_keep, stream=None):
+        """Keeps the last verify's rows 0 .. n_keep - 1 (into the ring)."""
+        if lib.dsv4cuda_decoder_commit(self.handle, int(n_keep), _stream(stream)) != 0:
+            raise Dsv4CudaError(lib.dsv4cuda_decoder_last_error().decode())
+
+    def verify_device(self, n_rows, stream=None):
+        if lib.dsv4cuda_decoder_verify_device(self.handle, int(n_rows), _stream(stream)) != 0:
+            raise Dsv4CudaError(lib.dsv4cuda_decoder_last_error().decode())
+
+    def accept_greedy(self, n_rows, stream=None):
+        if lib.dsv4cuda_decoder_accept_greedy(self.handle, int(n_rows), _stream(stream)) != 0:
+            raise Dsv4CudaError(lib.dsv4cuda_decoder_last_error().decode())
+
+    def draft_random(self, n_rows, stream=None):
+        if lib.dsv4cuda_decoder_draft_random(self.handle, int(n_rows), _stream(stream)) != 0:
+            raise Dsv4CudaError(lib.dsv4cuda_decoder_last_error().decode())
+
+    def verify_stats(self):
+        """(tokens emitted, drafts accepted, verify steps) of accept_greedy."""
+        st = np.zeros(3, np.int64)
+        if lib.dsv4cuda_decoder_verify_stats(self.handle, st.ctypes.data) != 0:
+            raise Dsv4CudaError(lib.dsv4cuda_decoder_last_error().decode())
+        return tuple(int(x) for x in st)
+
+    def verify_pending(self):
+        """(pending token, its position) that accept_greedy left for the next step."""
+        t, p = C.c_int(), C.c_int()
+        if lib.dsv4cuda_decoder_verify_pending(self.handle, C.byref(t), C.byref(p)) != 0:
+            raise Dsv4CudaError(lib.dsv4cuda_decoder_last_error().decode())
+        return t.value, p.value
+
+    def verify_slots(self):
+        """Device addresses: (row tokens [8], start position, logits [8][vocab], argmax [8])."""
+        return (lib.dsv4cuda_decoder_verify_tokens(self.handle),
+                lib.dsv4cuda_decoder_verify_start(self.handle),
+                lib.dsv4cuda_decoder_verify_logits(self.handle),
+                lib.dsv4cuda_decoder_verify_argmax(self.handle))
 
     def set_moe_layers(self, moe_layers):
         """Expert parallelism: one EP-attached MoeLayer per decoder layer."""

@@ -595,6 +595,52 @@ int *dsv4cuda_decoder_position_slot(dsv4cuda_decoder *D);
 float *dsv4cuda_decoder_logits(dsv4cuda_decoder *D);
 int *dsv4cuda_decoder_argmax(dsv4cuda_decoder *D);
 
+/* Speculative verify on the decoder: dsv4_prefill_capture with all_logits
+ * (src/dsv4/dsv4_model.c:8434-8529, include/dsv4/dsv4_internal.h:296),
+ * i.e. n_rows tokens [pending, d1 .. dk] at positions start .. start +
+ * n_rows - 1 through every layer layer-major (forward_loaded_layer_batch
+ * :7577): each projection and expert GEMV streams its weights once for all
+ * rows, each row attends to the window of its own position (the earlier
+ * rows' latents included), and every row's logits come out
+ * (compute_logits_batch :7784). The rows' latents go to scratch rows beside
+ * each layer's ring, which is left untouched: nothing needs undoing when
+ * drafts are rejected, and a commit moves the kept rows into the ring
+ * (the reference's snapshot take / commit_prefix, :2842-3056, reduced to a
+ * row copy because these layers keep no other per-position state).
+ * Layers with the local MoE weights only (no expert parallelism). */
+#define DSV4CUDA_VERIFY_MAX_ROWS 8
+/* Host form: tokens[n_rows] and start_position in; all_logits
+ * [n_rows][vocab] and argmax[n_rows] (either may be NULL) out; synchronous. */
+int dsv4cuda_decoder_verify(dsv4cuda_decoder *D, const int *tokens, int n_rows,
+                            int start_position, float *all_logits, int *argmax);
+/* Device form: rows from dsv4cuda_decoder_verify_tokens, row 0's position
+ * from dsv4cuda_decoder_verify_start; logits and argmax stay in device memory
+ * (dsv4cuda_decoder_verify_logits / _argmax). Async, graph-capturable. */
+int dsv4cuda_decoder_verify_device(dsv4cuda_decoder *D, int n_rows, void *stream);
+/* Keep rows 0 .. n_keep - 1 of the last verify (positions start .. start +
+ * n_keep - 1): their latents move into the ring. Synchronous on stream. */
+int dsv4cuda_decoder_commit(dsv4cuda_decoder *D, int n_keep, void *stream);
+/* Greedy acceptance on the device (the reference CLI's chain at temperature
+ * 0, src/cli/dsv4_run.c:951-1043): accepts drafts while they equal the
+ * previous row's argmax, commits the pending row and the accepted drafts,
+ * makes the bonus token the next pending row and advances the start; the
+ * totals of tokens emitted, drafts accepted and steps accumulate in
+ * dsv4cuda_decoder_verify_stats. Async, graph-capturable. */
+int dsv4cuda_decoder_accept_greedy(dsv4cuda_decoder *D, int n_rows, void *stream);
+/* Uniform random drafts for rows 1 .. n_rows - 1 (the reference CLI's
+ * xorshift64 rng_next modulo the vocabulary, a decoder-owned seed).
+ * Async, graph-capturable. */
+int dsv4cuda_decoder_draft_random(dsv4cuda_decoder *D, int n_rows, void *stream);
+/* Waits for the device, then reads the totals (stats3: tokens emitted,
+ * drafts accepted, verify steps) and the pending token / its position that
+ * accept_greedy left for the next step. */
+int dsv4cuda_decoder_verify_stats(dsv4cuda_decoder *D, long long *stats3);
+int dsv4cuda_decoder_verify_pending(dsv4cuda_decoder *D, int *token, int *position);
+int *dsv4cuda_decoder_verify_tokens(dsv4cuda_decoder *D);
+int *dsv4cuda_decoder_verify_start(dsv4cuda_decoder *D);
+float *dsv4cuda_decoder_verify_logits(dsv4cuda_decoder *D);
+int *dsv4cuda_decoder_verify_argmax(dsv4cuda_decoder *D);
+
 #ifdef __cplusplus
 }
 #endif
