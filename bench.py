@@ -88,6 +88,11 @@ def parse():
     ap.add_argument("--decode-layers", type=int, default=43)
     ap.add_argument("--attn-batch", type=int, default=32)
     ap.add_argument("--attn-ctx", type=int, default=32768)
+    ap.add_argument("--no-spec", action="store_true",
+                    help="decode: skip the speculation-on measurement (verify steps of a "
+                         "k = 5 draft chain)")
+    ap.add_argument("--spec-rows", type=int, default=6,
+                    help="decode: rows per verify step (the pending token + k drafts)")
     ap.add_argument("--no-attn-sweep", action="store_true",
                     help="skip the config 3 attention sweep attached to the MoE line")
     return ap.parse_args()
@@ -1132,12 +1137,15 @@ def main_decode(args, rank, world, local):
                  hc_head_scale=torch.ones(1, device=dev))
     prompt, gen = 2048, args.steps
     n_e2e = max(8, args.steps // 4)  # host-call tokens after the timed graph replays
+    spec_steps = 0 if (args.no_spec or world > 1) else max(10, args.steps // 4)
+    spec_warm = 3
     cfg = dict(hidden=c["hidden"], n_layers=n_layers, vocab=c["vocab"], n_heads=c["n_heads"],
                head_dim=c["head_dim"], rope_dim=c["rope_dim"], q_lora=c["q_lora"],
                o_groups=c["o_groups"], o_lora=c["o_lora"], window=c["window"],
                hc_mult=c["hc_mult"], hc_iters=c["hc_iters"], rms_eps=c["rms_eps"],
                hc_eps=c["hc_eps"], rope_theta=c["rope_theta"],
-               max_context=prompt + gen + args.warmup + n_e2e + 16,
+               max_context=prompt + gen + args.warmup + n_e2e + 16 +
+               (spec_steps + spec_warm + 1) * args.spec_rows,
                moe=dict(hidden=c["hidden"], moe_inter=c["inter"], n_experts=c["experts"],
                         topk=c["topk"], swiglu_limit=10, route_scale=1.5,
                         shared_kind=dsv4cuda.SHARED_FP8, hash_vocab=0))
@@ -1235,6 +1243,60 @@ def main_decode(args, rank, world, local):
             dist.all_reduce(tt, op=dist.ReduceOp.MAX)
             el = float(tt.item())
         e2e = world * n_e2e / el
+    # speculation on: verify steps of a draft chain (config 4's form: the
+    # pending token plus k uniform random drafts), each one CUDA graph of
+    # draft_random -> verify (all rows layer-major) -> greedy acceptance +
+    # commit, the next step's pending token and position left on the device
+    spec = None
+    if spec_steps:
+        n_rows = args.spec_rows
+        p_now = int(pos.item()) if e2e is None else p0 + 2 + n_e2e
+        _, pend = dec.read()  # the last step's greedy token is the pending row
+        first = [pend] + [1] * (n_rows - 1)
+        dec.verify(first, p_now)  # eager: fills the verify slots, one-time set-up
+        dec.accept_greedy(n_rows, stream.cuda_stream)
+        stream.synchronize()
+        sgraph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(sgraph, stream=stream):
+            cs = torch.cuda.current_stream().cuda_stream
+            dec.draft_random(n_rows, cs)
+            dec.verify_device(n_rows, cs)
+            dec.accept_greedy(n_rows, cs)
+        with torch.cuda.stream(stream):
+            for _ in range(spec_warm):
+                sgraph.replay()
+        torch.cuda.synchronize()
+        st0 = dec.verify_stats()
+        clocks_s = ClockSampler(local)
+        clocks_s.start()
+        time.sleep(0.2)
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
+            e0.record(stream)
+            for _ in range(spec_steps):
+                sgraph.replay()
+            e1.record(stream)
+        torch.cuda.synchronize()
+        sms = e0.elapsed_time(e1)
+        clk_s = clocks_s.stop()
+        st1 = dec.verify_stats()
+        emitted, accepted, vsteps = (st1[i] - st0[i] for i in range(3))
+        sgraph.reset()
+        spec = {"metric": "decode tok/s, batch 1, speculation on (config 4 form: pending token "
+                          f"+ {n_rows - 1} uniform random drafts per verify step, greedy "
+                          "acceptance, config 5 model)",
+                "value": emitted / (sms * 1e-3), "unit": "tok/s",
+                "ms_per_verify_step": sms / vsteps, "verify_steps": vsteps,
+                "rows_per_step": n_rows, "tokens_per_step": emitted / vsteps,
+                "drafts_accepted_per_step": accepted / vsteps,
+                "verified_rows_per_s": n_rows * vsteps / (sms * 1e-3),
+                "tok_s_if_every_draft_accepted": n_rows * vsteps / (sms * 1e-3),
+                "verify_vs_decode_step_cost": (sms / vsteps) / ms_tok,
+                "break_even_accepted_drafts": (sms / vsteps) / ms_tok - 1.0,
+                "clocks": clk_s,
+                "note": "uniform random drafts are almost never accepted, so this is the "
+                        "floor; a drafter's gain is tokens_per_step x this step rate"}
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
         try:
@@ -1294,6 +1356,7 @@ def main_decode(args, rank, world, local):
             "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": 8,
                     "d2h_bytes_per_step": c["vocab"] * 4 + 4},
             "gpu_launches": kernels * args.steps, "clocks": clk,
+            "spec_on": spec,
             "expert_gemv_config2": moe_sub,
         }
         print(json.dumps(line), flush=True)

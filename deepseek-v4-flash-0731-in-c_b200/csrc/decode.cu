@@ -1533,6 +1533,8 @@ struct dsv4cuda_decoder {
     int* n_one = nullptr;
     int* n_groups = nullptr;
     dsv4::Fp8KvCache* caches = nullptr;  // [n_layers] for the commit kernel
+    float* mt_part = nullptr;      // the multi-token FP8 GEMVs' block partials
+    size_t mt_part_floats = 0;
     dsv4::MoeWorkspace moe_ws{};
   } v;
 };
@@ -2002,6 +2004,12 @@ bool verify_alloc(dsv4cuda_decoder* D) {
   chk(v.n_one = dalloc<int>(D, 1));
   chk(v.n_groups = dalloc<int>(D, 1));
   chk(v.caches = dalloc<dsv4::Fp8KvCache>(D, D->layers.size()));
+  {
+    // [V][in / 128][rows] for the largest projection (wq_a + wkv, wq_b, wo_b)
+    const size_t ql = c.q_lora, go = static_cast<size_t>(G) * c.o_lora;
+    v.mt_part_floats = V * std::max(std::max(hid / 128 * (ql + d), ql / 128 * hd), go / 128 * hid);
+    chk(v.mt_part = dalloc<float>(D, v.mt_part_floats));
+  }
   if (!ok) return false;
   std::vector<dsv4::GemvItem> it(V), itg(static_cast<size_t>(V) * G);
   for (int n = 1; n <= V; ++n) {
@@ -2038,6 +2046,13 @@ bool verify_alloc(dsv4cuda_decoder* D) {
   return true;
 }
 
+// A BF16 GEMV over a verify step's n rows: the (row, token)-lane kernel, or
+// the item kernel when the shape does not fit it.
+cudaError_t bf16_rows(const dsv4::Bf16GemvArgs& a, int n, cudaStream_t st) {
+  const cudaError_t e = n > 1 ? dsv4::launch_bf16_gemv_mt(a, n, st) : cudaErrorNotSupported;
+  return e == cudaErrorNotSupported ? dsv4::launch_bf16_gemv(a, n, st) : e;
+}
+
 // attention_forward_batch_projected (src/dsv4/dsv4_model.c:5449-5572) for a
 // verify step's n rows: every projection one GEMV over the n rows (the
 // weights stream once), each row's latent into its scratch cache row, then
@@ -2050,10 +2065,18 @@ cudaError_t verify_attention(dsv4cuda_decoder* D, dsv4::Layer& L, int n, cudaStr
   const auto& w = L.w;
   const int H = c.n_heads, d = c.head_dim, ql = c.q_lora, half = c.rope_dim / 2;
   const int G = c.o_groups, ol = c.o_lora, hid = c.hidden;
-  auto gemv8 = [&](const uint8_t* W, const uint8_t* S, int in, int rows, float* y) {
+  // one matrix (or two on the same input) over the n rows: the split-K
+  // multi-token kernels, else the item GEMVs
+  auto gemv8 = [&](const uint8_t* W, const uint8_t* S, int in, int rows, float* y,
+                   const uint8_t* W1 = nullptr, const uint8_t* S1 = nullptr, int rows1 = 0,
+                   float* y1 = nullptr) -> cudaError_t {
     dsv4::Fp8GemvArgs a{};
     a.W[0] = W;
     a.S[0] = S;
+    a.W[1] = W1;
+    a.S[1] = S1;
+    a.rows1 = rows1;
+    a.Y[1] = y1;
     a.in = in;
     a.rows = rows;
     a.round_out = 1;
@@ -2062,10 +2085,17 @@ cudaError_t verify_attention(dsv4cuda_decoder* D, dsv4::Layer& L, int n, cudaStr
     a.items = v.items + (n - 1);
     a.n_items = v.n_one;
     a.max_items = 1;
+    if (dsv4::fp8_gemv_mt_part_floats(a, n) <= v.mt_part_floats) {
+      const cudaError_t e = dsv4::launch_fp8_gemv_mt(a, n, v.mt_part, st);
+      if (e != cudaErrorNotSupported) return e;
+    }
+    if (W1) return cudaErrorNotSupported;
     return dsv4::launch_fp8_gemv(a, false, n, st);
   };
-  DEC_CHECK(gemv8(w.wq_a, w.wq_a_s, hid, ql, v.qr));
-  DEC_CHECK(gemv8(w.wkv, w.wkv_s, hid, d, v.kv));
+  if (gemv8(w.wq_a, w.wq_a_s, hid, ql, v.qr, w.wkv, w.wkv_s, d, v.kv) == cudaErrorNotSupported) {
+    DEC_CHECK(gemv8(w.wq_a, w.wq_a_s, hid, ql, v.qr));
+    DEC_CHECK(gemv8(w.wkv, w.wkv_s, hid, d, v.kv));
+  }
   // per row: kv_norm + RoPE + KV write into the scratch row; q_norm + quant
   dsv4::NormTailArgs kt{};
   kt.x = v.kv;
@@ -2131,7 +2161,7 @@ cudaError_t verify_attention(dsv4cuda_decoder* D, dsv4::Layer& L, int n, cudaStr
   ga.n_items = v.n_groups;
   ga.max_items = G;
   ga.static_items = 1;
-  DEC_CHECK(dsv4::launch_bf16_gemv(ga, n, st));
+  DEC_CHECK(bf16_rows(ga, n, st));
   DEC_CHECK(dsv4::launch_quant_fp8(v.oall, G * ol, G * ol, n, v.xq, v.xs, D->ld, st));
   return gemv8(w.wo_b, w.wo_b_s, G * ol, hid, v.branch);
 }
@@ -2156,6 +2186,8 @@ cudaError_t verify(dsv4cuda_decoder* D, int n, cudaStream_t st) {
   const HcRows R = hc_verify(D, n);
   dsv4::MoeExecOptions opt;
   if (!c.hc_exact) opt.join = D->hc_join;  // the FFN boundary's split, before the combine
+  opt.mt_part = v.mt_part;  // the shared expert over the rows, split-K
+  opt.mt_part_floats = v.mt_part_floats;
   for (size_t li = 0; li < D->layers.size(); ++li) {
     auto& L = D->layers[li];
     const auto& w = L.w;
@@ -2180,7 +2212,7 @@ cudaError_t verify(dsv4cuda_decoder* D, int n, cudaStream_t st) {
   ha.n_items = v.n_one;
   ha.max_items = 1;
   ha.static_items = 1;
-  DEC_CHECK(dsv4::launch_bf16_gemv(ha, n, st));
+  DEC_CHECK(bf16_rows(ha, n, st));
   const int chunks = std::min(dsv4::kArgmaxCtas, c.vocab);
   DEC_CHECK(dsv4::launch_pdl(dsv4::argmax_chunks_kernel, dim3(chunks, n), dim3(256), 0, st,
                              static_cast<const float*>(v.logits), c.vocab, v.am_v, v.am_i));

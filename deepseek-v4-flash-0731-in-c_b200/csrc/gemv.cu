@@ -1832,4 +1832,308 @@ cudaError_t launch_f32_to_f16(const float* x, __half* y, size_t n, cudaStream_t 
   return cudaGetLastError();
 }
 
+// ------------------------------------------- multi-token (verify rows) ----
+// The verify step's projections run 2..8 token rows through one matrix. The
+// one-token kernels keep a warp per 32 output rows, which leaves most SMs
+// idle when there are few row tiles and the per-byte work is several
+// tokens' FMAs. These two forms spread the work the other way while keeping
+// each output's reference order.
+//
+// FP8 (dsv4_gemv_fp8_batch_q, src/dsv4/dsv4_model.c:678): every 128-column
+// block's partial is an independent sequential chain, so a warp takes 32
+// rows x `bps` blocks, converts each block's weights to f16 once, and runs
+// the block's chain for every token (part[t][block][row]); the fold then
+// sums each (token, row) over the blocks in block order,
+// acc = fmaf(partial, qscale * ws, acc), NaN-scaled blocks skipped. W[1] /
+// rows1 is an optional second matrix on the same input (wq_a beside wkv).
+template <int NT>
+__global__ void __launch_bounds__(128) fp8_mt_partials_kernel(const Fp8GemvArgs a, int ntok,
+                                                              int bps, float* part) {
+  pdl_trigger();
+  const int lane = threadIdx.x & 31;
+  const long long gw = (blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x) >> 5;
+  const int CB = a.in / 128, total = a.rows + a.rows1;
+  const int nseg = (CB + bps - 1) / bps;
+  if (gw >= static_cast<long long>(total / 32) * nseg) return;
+  const int tile = static_cast<int>(gw / nseg), seg = static_cast<int>(gw % nseg);
+  const int row = tile * 32 + lane;
+  const int mat = row >= a.rows;
+  const uint8_t* wr = a.W[mat] + static_cast<size_t>(mat ? row - a.rows : row) * a.in;
+  const int b0 = seg * bps, b1 = min(CB, b0 + bps);
+  U8x32 w[4];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) w[k] = ldg32(wr + static_cast<size_t>(b0) * 128 + 32 * k);
+  pdl_wait();
+  const GemvItem& it = a.items[0];
+  for (int b = b0; b < b1; ++b) {
+    uint32_t wh[64];  // the block's 128 codes as f16 pairs, in column order
+#pragma unroll
+    for (int k = 0; k < 4; ++k)
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        wh[k * 16 + 2 * i] = e4m3x2_to_f16x2(w[k].w[i] & 0xFFFFu);
+        wh[k * 16 + 2 * i + 1] = e4m3x2_to_f16x2(w[k].w[i] >> 16);
+      }
+    if (b + 1 < b1) {
+#pragma unroll
+      for (int k = 0; k < 4; ++k) w[k] = ldg32(wr + static_cast<size_t>(b + 1) * 128 + 32 * k);
+    }
+#pragma unroll
+    for (int t = 0; t < NT; ++t) {
+      if (t >= ntok) break;
+      const __half* xr = a.act.x + static_cast<size_t>(it.tok[t].x) * a.act.ld + b * 128;
+      float p = 0.0f;
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const U8x32 x0 = ldg32_l1(xr + 32 * k);
+        const U8x32 x1 = ldg32_l1(xr + 32 * k + 16);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const uint32_t xv = i < 8 ? x0.w[i] : x1.w[i - 8];
+          p = fma_h_lo(wh[k * 16 + i], xv, p);
+          p = fma_h_hi(wh[k * 16 + i], xv, p);
+        }
+      }
+      part[(static_cast<size_t>(t) * CB + b) * total + row] = p;
+    }
+  }
+}
+
+__global__ void __launch_bounds__(128) fp8_mt_fold_kernel(const Fp8GemvArgs a, int ntok,
+                                                          const float* part) {
+  pdl_trigger();
+  pdl_wait();
+  const int total = a.rows + a.rows1;
+  const long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x;
+  if (i >= static_cast<long long>(ntok) * total) return;
+  const int t = static_cast<int>(i / total), row = static_cast<int>(i % total);
+  const int mat = row >= a.rows;
+  const int lrow = mat ? row - a.rows : row;
+  const int CB = a.in / 128;
+  const GemvItem& it = a.items[0];
+  const float* qs = a.act.s + static_cast<size_t>(it.tok[t].x) * (a.act.ld / 128);
+  const uint8_t* sr = a.S[mat] + static_cast<size_t>(lrow / 128) * ((a.in + 127) / 128);
+  const float* pp = part + static_cast<size_t>(t) * CB * total + row;
+  float acc = 0.0f;
+  for (int b0 = 0; b0 < CB; b0 += 8) {
+    float pv[8], sv[8];
+    uint32_t code[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int b = b0 + j < CB ? b0 + j : CB - 1;
+      pv[j] = pp[static_cast<size_t>(b) * total];
+      sv[j] = qs[b];
+      code[j] = sr[b];
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      if (b0 + j >= CB) break;
+      const float ws = e8m0_decode(code[j]);
+      if (!isnan(ws)) acc = fmaf(pv[j], sv[j] * ws, acc);
+    }
+  }
+  const int rows_m = mat ? a.rows1 : a.rows;
+  a.Y[mat][static_cast<size_t>(it.tok[t].y) * rows_m + lrow] = a.round_out ? bf16_round(acc) : acc;
+}
+
+// BF16 (dsv4_gemv_bf16_batch, :308; the grouped wo_a :371): one fmaf chain
+// per (row, token) over all columns in column order, so the columns cannot
+// be split. The streaming form of the one-token kernel (a warp owns 32 rows,
+// lane = row, 256-column chunks of four swizzled [32 rows x 128 B] TMA
+// boxes through a ring of shared-memory stages) with the chunk's
+// activations of every token beside the weights: each weight is widened
+// once and feeds NT independent chains, which also hide the FMA latency.
+template <int NT>
+__host__ __device__ constexpr int bf16_mt_stage() { return kBW + NT * kBCols * 4; }
+
+template <int STAGES, int NT>
+__device__ void bf16_stream_mt_warp(const CUtensorMap* wmapp, const Bf16GemvArgs& a, int ntok,
+                                    long long first, long long nwarps, unsigned char* wbase,
+                                    uint64_t* bars, unsigned int* err) {
+  constexpr int kStage = bf16_mt_stage<NT>();
+  const CUtensorMap& wmap = *wmapp;
+  const int lane = threadIdx.x & 31;
+  const int n_items = load_n_items(a.n_items, a.max_items);
+  const int rblocks = a.rows / 32;
+  const long long tiles = static_cast<long long>(n_items) * rblocks;
+  const int CPT = a.in / kBCols;
+  const long long my_tiles = tiles > first ? (tiles - first + nwarps - 1) / nwarps : 0;
+  const long long jobs = my_tiles * CPT;
+  const uint32_t bytes = kBW + static_cast<uint32_t>(ntok) * kBCols * 4;
+  auto issue = [&](long long j, int q) {
+    if (lane != 0) return;
+    const long long tile = first + (j / CPT) * nwarps;
+    const int chunk = static_cast<int>(j % CPT);
+    const int item = static_cast<int>(tile / rblocks);
+    const int rb = static_cast<int>(tile - static_cast<long long>(item) * rblocks);
+    const GemvItem& it = a.items[item];
+    unsigned char* st = wbase + q * kStage;
+    mbar_arrive_expect_tx(&bars[q], bytes);
+    const int y = it.mat * a.rows + rb * 32;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) tma_load_2d(st + k * 4096, &wmap, chunk * 512 + k * 128, y, &bars[q]);
+    for (int t = 0; t < ntok; ++t)
+      bulk_g2s(st + kBW + t * kBCols * 4,
+               a.x + static_cast<size_t>(it.tok[t].x) * a.ldx + chunk * kBCols, kBCols * 4, &bars[q]);
+  };
+  for (long long j = 0; j < jobs && j < STAGES; ++j) issue(j, static_cast<int>(j));
+  __syncwarp();
+  float acc[NT];
+#pragma unroll
+  for (int t = 0; t < NT; ++t) acc[t] = 0.0f;
+  int q = 0;
+  uint32_t phase = 0;
+  long long j = 0;
+  bool ok = true;
+  const int sw = lane & 7;
+  for (; j < jobs; ++j) {
+    if (!mbar_wait(&bars[q], phase, err)) { ok = false; break; }
+    const unsigned char* st = wbase + q * kStage;
+    const float4* xs = reinterpret_cast<const float4*>(st + kBW);
+#pragma unroll 4
+    for (int p = 0; p < 32; ++p) {
+      const uint4 w8 = *reinterpret_cast<const uint4*>(st + (p >> 3) * 4096 + lane * 128 +
+                                                       (((p & 7) ^ sw) << 4));
+      const float wf[8] = {__uint_as_float(w8.x << 16), __uint_as_float(w8.x & 0xFFFF0000u),
+                           __uint_as_float(w8.y << 16), __uint_as_float(w8.y & 0xFFFF0000u),
+                           __uint_as_float(w8.z << 16), __uint_as_float(w8.z & 0xFFFF0000u),
+                           __uint_as_float(w8.w << 16), __uint_as_float(w8.w & 0xFFFF0000u)};
+#pragma unroll
+      for (int t = 0; t < NT; ++t) {
+        const float4 x0 = xs[t * (kBCols / 4) + 2 * p], x1 = xs[t * (kBCols / 4) + 2 * p + 1];
+        acc[t] = fmaf(wf[0], x0.x, acc[t]);
+        acc[t] = fmaf(wf[1], x0.y, acc[t]);
+        acc[t] = fmaf(wf[2], x0.z, acc[t]);
+        acc[t] = fmaf(wf[3], x0.w, acc[t]);
+        acc[t] = fmaf(wf[4], x1.x, acc[t]);
+        acc[t] = fmaf(wf[5], x1.y, acc[t]);
+        acc[t] = fmaf(wf[6], x1.z, acc[t]);
+        acc[t] = fmaf(wf[7], x1.w, acc[t]);
+      }
+    }
+    if (j % CPT == CPT - 1) {
+      const long long tile = first + (j / CPT) * nwarps;
+      const int item = static_cast<int>(tile / rblocks);
+      const int rb = static_cast<int>(tile - static_cast<long long>(item) * rblocks);
+      const GemvItem& it = a.items[item];
+#pragma unroll
+      for (int t = 0; t < NT; ++t) {
+        if (t < ntok)
+          a.Y[static_cast<size_t>(it.tok[t].y) * a.rows + rb * 32 + lane] =
+              a.round_out ? bf16_round(acc[t]) : acc[t];
+        acc[t] = 0.0f;
+      }
+    }
+    __syncwarp();  // every lane is done with stage q before it is refilled
+    if (j + STAGES < jobs) issue(j + STAGES, q);
+    __syncwarp();
+    if (++q == STAGES) {
+      q = 0;
+      phase ^= 1u;
+    }
+  }
+  if (!ok) {
+    // drain this warp's copies still in flight before the CTA exits
+    mbar_wait(&bars[q], phase, err);
+    uint32_t ph = phase;
+    int k = q;
+    for (long long r = j + 1; r < jobs && r < j + STAGES; ++r) {
+      if (++k == STAGES) { k = 0; ph ^= 1u; }
+      mbar_wait(&bars[k], ph, err);
+    }
+  }
+}
+
+template <int WARPS, int STAGES, int NT>
+__global__ void __launch_bounds__(WARPS * 32, 1)
+    bf16_stream_mt_kernel(const __grid_constant__ CUtensorMap wmap, const Bf16GemvArgs a, int ntok,
+                          unsigned int* err) {
+  extern __shared__ __align__(1024) unsigned char smem[];
+  __shared__ uint64_t bars_all[WARPS][STAGES];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  unsigned char* const sbase = smem + ((1024u - (smem_addr(smem) & 1023u)) & 1023u);
+  uint64_t* bars = bars_all[warp];
+  if (lane == 0) {
+#pragma unroll
+    for (int q = 0; q < STAGES; ++q) mbar_init(&bars[q], 1);
+    mbar_fence_init();
+    if (warp == 0) tma_prefetch_desc(&wmap);
+  }
+  __syncthreads();
+  pdl_trigger();
+  pdl_wait();
+  bf16_stream_mt_warp<STAGES, NT>(&wmap, a, ntok, static_cast<long long>(warp) * gridDim.x + blockIdx.x,
+                                  static_cast<long long>(gridDim.x) * WARPS,
+                                  sbase + static_cast<size_t>(warp) * STAGES * bf16_mt_stage<NT>(),
+                                  bars, err);
+}
+
+int fp8_mt_bps(const Fp8GemvArgs& a) {
+  const int total = a.rows + a.rows1, CB = a.in / 128;
+  const long long target = 16LL * sm_count();
+  const long long units = static_cast<long long>(total / 32) * CB;
+  return static_cast<int>(std::min<long long>(CB, std::max<long long>(1, (units + target - 1) / target)));
+}
+
+size_t fp8_gemv_mt_part_floats(const Fp8GemvArgs& a, int ntok) {
+  return static_cast<size_t>(ntok) * (a.in / 128) * (a.rows + a.rows1);
+}
+
+cudaError_t launch_fp8_gemv_mt(const Fp8GemvArgs& a, int ntok, float* part, cudaStream_t st) {
+  if (ntok < 1 || ntok > kItemTok || a.rows <= 0) return cudaErrorInvalidValue;
+  if (a.rows % 32 != 0 || a.rows1 % 32 != 0 || a.in % 128 != 0 || a.act.ld % 128 != 0 ||
+      a.act.x32 || !aligned(a.W[0], 32) || !aligned(a.act.x, 32) ||
+      (a.rows1 > 0 && !aligned(a.W[1], 32)))
+    return cudaErrorNotSupported;
+  const int bps = fp8_mt_bps(a);
+  const int CB = a.in / 128, total = a.rows + a.rows1;
+  const long long warps = static_cast<long long>(total / 32) * ((CB + bps - 1) / bps);
+  const dim3 grid(static_cast<unsigned>((warps + 3) / 4));
+  cudaError_t e;
+  if (ntok <= 2) e = launch_pdl(fp8_mt_partials_kernel<2>, grid, dim3(128), 0, st, a, ntok, bps, part);
+  else if (ntok <= 4) e = launch_pdl(fp8_mt_partials_kernel<4>, grid, dim3(128), 0, st, a, ntok, bps, part);
+  else if (ntok <= 6) e = launch_pdl(fp8_mt_partials_kernel<6>, grid, dim3(128), 0, st, a, ntok, bps, part);
+  else e = launch_pdl(fp8_mt_partials_kernel<8>, grid, dim3(128), 0, st, a, ntok, bps, part);
+  if (e != cudaSuccess) return e;
+  const long long n = static_cast<long long>(ntok) * total;
+  return launch_pdl(fp8_mt_fold_kernel, dim3(static_cast<unsigned>((n + 127) / 128)), dim3(128), 0,
+                    st, a, ntok, static_cast<const float*>(part));
+}
+
+cudaError_t launch_bf16_gemv_mt(const Bf16GemvArgs& a, int ntok, cudaStream_t st) {
+  if (ntok < 1 || ntok > kItemTok || a.rows <= 0 || a.max_items <= 0) return cudaErrorInvalidValue;
+  const long long n_mats = a.w_stride ? a.max_items : 1;
+  if (a.rows % 32 != 0 || a.in % kBCols != 0 || !aligned(a.W, 16) || !aligned(a.x, 16) ||
+      a.ldx % 4 != 0 || (a.w_stride != 0 && a.w_stride != static_cast<size_t>(a.rows) * a.in))
+    return cudaErrorNotSupported;
+  CUtensorMap wmap;
+  if (!make_tma_map_u8(&wmap, a.W, static_cast<uint64_t>(a.in) * 2,
+                       static_cast<uint64_t>(n_mats) * a.rows, 128, 32, true))
+    return cudaErrorNotSupported;
+  const long long tiles = static_cast<long long>(a.max_items) * (a.rows / 32);
+  auto run = [&](auto kern, int warps, int stages, int stage_bytes) -> cudaError_t {
+    const size_t smem = static_cast<size_t>(warps) * stages * stage_bytes + 1024;
+    cudaError_t e = set_max_dynamic_smem(reinterpret_cast<const void*>(kern), static_cast<int>(smem));
+    if (e != cudaSuccess) return e;
+    const int grid = static_cast<int>(std::max<long long>(
+        1, std::min<long long>(sm_count(), (tiles + warps - 1) / warps)));
+    return launch_pdl(kern, dim3(grid), dim3(warps * 32), smem, st, wmap, a, ntok,
+                      device_error_word());
+  };
+  // few tiles (grouped wo_a): two warps per SM with a deep ring; many tiles
+  // (the vocab head): four warps, two stages
+  const bool few = tiles <= 2LL * sm_count();
+  if (ntok <= 2)
+    return few ? run(bf16_stream_mt_kernel<2, 4, 2>, 2, 4, bf16_mt_stage<2>())
+               : run(bf16_stream_mt_kernel<4, 2, 2>, 4, 2, bf16_mt_stage<2>());
+  if (ntok <= 4)
+    return few ? run(bf16_stream_mt_kernel<2, 4, 4>, 2, 4, bf16_mt_stage<4>())
+               : run(bf16_stream_mt_kernel<4, 2, 4>, 4, 2, bf16_mt_stage<4>());
+  if (ntok <= 6)
+    return few ? run(bf16_stream_mt_kernel<2, 4, 6>, 2, 4, bf16_mt_stage<6>())
+               : run(bf16_stream_mt_kernel<4, 2, 6>, 4, 2, bf16_mt_stage<6>());
+  return few ? run(bf16_stream_mt_kernel<2, 4, 8>, 2, 4, bf16_mt_stage<8>())
+             : run(bf16_stream_mt_kernel<4, 2, 8>, 4, 2, bf16_mt_stage<8>());
+}
+
 }  // namespace dsv4

@@ -107,6 +107,16 @@ int device_sm_count();
 cudaError_t launch_fp8_gemv_splitk(const Fp8GemvArgs& a, float* part, cudaStream_t st,
                                    unsigned int* tile_cnt = nullptr);
 
+// Multi-token forms for 1..kItemTok token rows through one matrix (the
+// verify step), each output in the reference's order. FP8: split over
+// 128-column blocks, items[0] names the tokens, W[1] / rows1 an optional
+// second matrix on the same input; part holds fp8_gemv_mt_part_floats
+// floats. BF16: one lane per (row, token) chain; items as launch_bf16_gemv.
+// cudaErrorNotSupported when the shape or alignment does not fit.
+size_t fp8_gemv_mt_part_floats(const Fp8GemvArgs& a, int ntok);
+cudaError_t launch_fp8_gemv_mt(const Fp8GemvArgs& a, int ntok, float* part, cudaStream_t st);
+cudaError_t launch_bf16_gemv_mt(const Bf16GemvArgs& a, int ntok, cudaStream_t st);
+
 // x [rows][n] fp32 -> E4M3 grid (f16) + per-128 scales (dsv4_quant_fp8_codes).
 cudaError_t launch_quant_fp8(const float* x, int ldx, int n, int rows, __half* qx,
                              float* qs, int ld_out, cudaStream_t st);

@@ -1110,7 +1110,33 @@ cudaError_t moe_forward_local(const MoeConfig& c, const MoeWeights& w, const Moe
     const QAct sact{ws.sh_qy, ws.sh_qys, I, nullptr};
     const size_t so = static_cast<size_t>(sh_t0) * I;  // first shared row
     const size_t sq = static_cast<size_t>(sh_t0) * ((I + 127) / 128);
-    if (c.shared_kind == kSharedFp8) {
+    // two or more tokens with scratch: the split-K multi-token kernels (the
+    // items' one-warp-per-32-rows form leaves most SMs idle at this size)
+    bool shared_done = false;
+    if (c.shared_kind == kSharedFp8 && opt.mt_part && sh_n >= 2 && sh_n <= kItemTok) {
+      Fp8GemvArgs g{};
+      g.W[0] = w.sh1; g.S[0] = w.sh1s; g.W[1] = w.sh3; g.S[1] = w.sh3s; g.rows1 = I;
+      g.in = H; g.rows = I; g.round_out = 1; g.act = act;
+      g.Y[0] = ws.sh_gate; g.Y[1] = ws.sh_up;
+      g.items = ws.items_sh; g.n_items = ws.counters + 3; g.max_items = 1;
+      Fp8GemvArgs d{};
+      d.W[0] = w.sh2; d.S[0] = w.sh2s;
+      d.in = I; d.rows = H; d.round_out = 1; d.act = sact;
+      d.Y[0] = ws.shared;
+      d.items = ws.items_sh; d.n_items = ws.counters + 3; d.max_items = 1;
+      if (fp8_gemv_mt_part_floats(g, sh_n) <= opt.mt_part_floats &&
+          fp8_gemv_mt_part_floats(d, sh_n) <= opt.mt_part_floats) {
+        err = launch_fp8_gemv_mt(g, sh_n, opt.mt_part, sst);
+        if (err == cudaSuccess)
+          err = launch_swiglu_quant(ws.sh_gate + so, ws.sh_up + so, I, sh_n, nullptr,
+                                    c.swiglu_limit, ws.sh_qy + so, ws.sh_qys + sq, nullptr, sst);
+        if (err == cudaSuccess) err = launch_fp8_gemv_mt(d, sh_n, opt.mt_part, sst);
+        if (err != cudaSuccess && err != cudaErrorNotSupported) return err;
+        shared_done = err == cudaSuccess;
+      }
+    }
+    if (shared_done) {
+    } else if (c.shared_kind == kSharedFp8) {
       Fp8GemvArgs g{};
       g.W[0] = w.sh1; g.S[0] = w.sh1s; g.W[1] = w.sh3; g.S[1] = w.sh3s;
       g.in = H; g.rows = I; g.round_out = 1; g.act = act;

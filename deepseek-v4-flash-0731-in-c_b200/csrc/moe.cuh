@@ -99,6 +99,11 @@ struct MoeExecOptions {
   // an event `st` also waits on before the combine (work forked by the
   // caller that must finish before the layer's output is consumed)
   cudaEvent_t join = nullptr;
+  // scratch for the multi-token split-K FP8 kernels (mt_part_floats
+  // floats): with it, an FP8 shared expert over two or more tokens runs
+  // split over its 128-column blocks (the verify step's rows)
+  float* mt_part = nullptr;
+  size_t mt_part_floats = 0;
 };
 
 cudaError_t moe_forward(const MoeConfig& c, const MoeWeights& w, const MoeWorkspace& ws,
