@@ -91,6 +91,8 @@ def parse():
     ap.add_argument("--no-spec", action="store_true",
                     help="decode: skip the speculation-on measurement (verify steps of a "
                          "k = 5 draft chain)")
+    ap.add_argument("--no-batch1", action="store_true",
+                    help="decode, N > 1: skip the batch-1 (replicated-token) measurement")
     ap.add_argument("--spec-rows", type=int, default=6,
                     help="decode: rows per verify step (the pending token + k drafts)")
     ap.add_argument("--no-attn-sweep", action="store_true",
@@ -341,8 +343,7 @@ def run_reference_arm(args, rank, world):
             "ms_per_step": 1e3 / tps, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "fp4e2m1/fp8e4m3 weights, bf16 activations, f32 accumulate",
             "data": "synthetic (random-init weights with the checkpoint's formats)",
-            "config": {"workload": "config 5 batch-1 greedy decode, speculation off",
-                       "layers": args.decode_layers},
+            "config": decode_config(args, world),
             "cpu_baseline": {"value": tps, "unit": "tok/s", "cores": cores, "kind": "reference",
                              "sample": sample, "extrapolated": True},
             "e2e": {"value": tps, "unit": "tok/s", "h2d_bytes_per_step": 0,
@@ -988,6 +989,25 @@ DECODE_METRIC = ("decode tok/s, batch 1, speculation off (config 5: DSV4-Flash s
                  "43 layers, 256+1 experts top-6, FP4 experts / FP8 attention)")
 
 
+def decode_config(args, world):
+    """The `config` of the decode line, the same in both arms."""
+    c, n_layers = C5, args.decode_layers
+    return {"workload": "config 5 batch-1 greedy decode, speculation off",
+            "layers": n_layers, "hidden": c["hidden"], "vocab": c["vocab"],
+            "heads": c["n_heads"], "head_dim": c["head_dim"],
+            "experts": c["experts"], "topk": c["topk"], "moe_inter": c["inter"],
+            "attention": "sliding window of 128 on every layer (compress ratio "
+                         "0; the compressor/indexer path is not built)",
+            "prompt_positions": 2048,
+            "weight_sets": f"{n_layers} layers cycle {args.decode_sets} distinct "
+                           "random-init layer weight sets of ~3.6 GB; every token "
+                           "reads a whole model's bytes, none of it L2-resident",
+            "graph": "one CUDA graph per token (argmax fed back on the device)",
+            "parallelism": (f"ep{world} (token-parallel: one sequence per GPU, "
+                            "experts split, slots exchanged over peer memory)"
+                            if world > 1 else "ep1")}
+
+
 def decode_bytes_per_token(c, n_layers):
     """Algorithmic HBM bytes one greedy token reads: every layer's dense
     weights (FP8 projections with their [128x128] scales, BF16 wo_a, the HC
@@ -1243,6 +1263,80 @@ def main_decode(args, rank, world, local):
             dist.all_reduce(tt, op=dist.ReduceOp.MAX)
             el = float(tt.item())
         e2e = world * n_e2e / el
+    # batch 1 at N GPUs (strong scaling): every rank decodes the same
+    # sequence from cleared rings; each rank routes the token, runs its own
+    # experts and the slots are exchanged (a second set of EP layers with
+    # their own exchange buffers)
+    batch1 = None
+    rep_own, rep_peers, moe_rep = [], [], []
+    if ep and not args.no_batch1:
+        moe_rep = [dsv4cuda.MoeLayer(st_["moe"], max_tokens=world, device=True,
+                                     expert_range=erange) for st_ in sets]
+        handles = []
+        for L in moe_rep:
+            addr, hnd = dsv4cuda.ipc_alloc(L.ep_buffer_bytes())
+            rep_own.append(addr)
+            handles.append(hnd)
+        all_h = [None] * world
+        dist.all_gather_object(all_h, handles)
+        for li, L in enumerate(moe_rep):
+            addrs = []
+            for r in range(world):
+                if r == rank:
+                    addrs.append(rep_own[li])
+                else:
+                    a_ = dsv4cuda.ipc_open(all_h[r][li])
+                    rep_peers.append(a_)
+                    addrs.append(a_)
+            L.ep_attach(rank, world, addrs)
+        dist.barrier()
+        dec.set_moe_layers([moe_rep[i % len(moe_rep)] for i in range(n_layers)])
+        dec.set_ep_replicated(True)
+        dec.reset(stream.cuda_stream)
+        pos.fill_(prompt - args.warmup - 1)
+        tok.fill_(1)
+        torch.cuda.synchronize()
+        with torch.cuda.stream(stream):
+            dec.step_device(tok, pos, stream.cuda_stream)
+            pos.add_(1)
+        stream.synchronize()
+        rgraph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(rgraph, stream=stream):
+            cs = torch.cuda.current_stream()
+            if lib.dsv4cuda_decoder_step_device(h, C.c_void_p(am_slot), C.c_void_p(pos.data_ptr()),
+                                                C.c_void_p(cs.cuda_stream)) != 0:
+                raise RuntimeError(lib.dsv4cuda_decoder_last_error().decode())
+            pos.add_(1)
+        with torch.cuda.stream(stream):
+            for _ in range(args.warmup):
+                rgraph.replay()
+        torch.cuda.synchronize()
+        dist.barrier()
+        torch.cuda.synchronize()
+        r0 = torch.cuda.Event(enable_timing=True)
+        r1 = torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
+            r0.record(stream)
+            for _ in range(args.steps):
+                rgraph.replay()
+            r1.record(stream)
+        torch.cuda.synchronize()
+        dist.barrier()
+        t = torch.tensor([r0.elapsed_time(r1)], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        rms = float(t.item()) / args.steps
+        last = torch.tensor([int(dec.read()[1])], device=dev)
+        lo, hi = last.clone(), last.clone()
+        dist.all_reduce(lo, op=dist.ReduceOp.MIN)
+        dist.all_reduce(hi, op=dist.ReduceOp.MAX)
+        batch1 = {"metric": "decode tok/s, batch 1, speculation off (one sequence on all "
+                            f"{world} GPUs: experts split, attention and dense layers "
+                            "replicated, slots exchanged over peer memory)",
+                  "value": 1e3 / rms, "unit": "tok/s", "ms_per_step": rms,
+                  "scaling": "strong", "steps": args.steps,
+                  "ranks_agree_on_last_token": bool(int(lo.item()) == int(hi.item()))}
+        torch.cuda.synchronize()
+        rgraph.reset()
     # speculation on: verify steps of a draft chain (config 4's form: the
     # pending token plus k uniform random drafts), each one CUDA graph of
     # draft_random -> verify (all rows layer-major) -> greedy acceptance +
@@ -1333,20 +1427,7 @@ def main_decode(args, rank, world, local):
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "fp4e2m1/fp8e4m3 weights, bf16 activations, f32 accumulate",
             "data": "synthetic (random-init weights with the checkpoint's formats)",
-            "config": {"workload": "config 5 batch-1 greedy decode, speculation off",
-                       "layers": n_layers, "hidden": c["hidden"], "vocab": c["vocab"],
-                       "heads": c["n_heads"], "head_dim": c["head_dim"],
-                       "experts": c["experts"], "topk": c["topk"], "moe_inter": c["inter"],
-                       "attention": "sliding window of 128 on every layer (compress ratio "
-                                    "0; the compressor/indexer path is not built)",
-                       "positions": f"{prompt - args.warmup}..{prompt + args.steps}",
-                       "weight_sets": f"{n_layers} layers cycle {len(sets)} distinct "
-                                      "random-init layer weight sets of ~3.6 GB; every token "
-                                      "reads a whole model's bytes, none of it L2-resident",
-                       "graph": "one CUDA graph per token (argmax fed back on the device)",
-                       "parallelism": (f"ep{world} (token-parallel: one sequence per GPU, "
-                                       "experts split, slots exchanged over peer memory)"
-                                       if ep else "ep1")},
+            "config": decode_config(args, world),
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
                          "frac": achieved / hbm, "traffic": None,
                          "alg_bytes_per_token": alg, "peak_source": src,
@@ -1357,6 +1438,7 @@ def main_decode(args, rank, world, local):
                     "d2h_bytes_per_step": c["vocab"] * 4 + 4},
             "gpu_launches": kernels * args.steps, "clocks": clk,
             "spec_on": spec,
+            "batch1_strong_scaling": batch1,
             "expert_gemv_config2": moe_sub,
         }
         print(json.dumps(line), flush=True)
@@ -1366,12 +1448,12 @@ def main_decode(args, rank, world, local):
     if ep:
         # every rank stops touching peer memory before any buffer is unmapped
         dist.barrier()
-        for a_ in ipc_peers:
+        for a_ in ipc_peers + rep_peers:
             dsv4cuda.ipc_close(a_)
         dist.barrier()
-        for a_ in ipc_own:
+        for a_ in ipc_own + rep_own:
             dsv4cuda.ipc_free(a_)
-        for L in moe_ep:
+        for L in moe_ep + moe_rep:
             L.close()
     if dist:
         dist.barrier()

@@ -1449,6 +1449,7 @@ struct dsv4cuda_decoder {
   // expert parallelism: per layer an EP-attached MoE layer (token-parallel
   // exchange over peer memory); empty = every expert on this device
   std::vector<dsv4cuda_moe_layer*> ep;
+  bool ep_replicated = false;  // every rank decodes the same token (batch-1 strong scaling)
   std::vector<void*> owned;  // device allocations to free
   // per-step buffers
   int* d_token = nullptr;
@@ -1924,8 +1925,10 @@ cudaError_t step(dsv4cuda_decoder* D, cudaStream_t st) {
                           w.ffn_norm, 0, local ? D->moe_ws.xq : nullptr,
                           local ? D->moe_ws.xs : nullptr, c.hidden, st));
     if (!local) {
-      if (dsv4cuda_moe_forward_ep_tokens(D->ep[li], D->x, 1, D->branch, st) != 0)
-        return cudaErrorLaunchFailure;
+      const int rc = D->ep_replicated
+                         ? dsv4cuda_moe_forward_ep(D->ep[li], D->x, D->d_token, 1, D->branch, st)
+                         : dsv4cuda_moe_forward_ep_tokens(D->ep[li], D->x, 1, D->branch, st);
+      if (rc != 0) return cudaErrorLaunchFailure;
       DEC_CHECK(hc_join(D, st));
     } else {
       DEC_CHECK(dsv4::moe_forward(L.mc, L.mw, D->moe_ws, D->x, D->d_token, 1, D->branch, st, opt));
@@ -2463,6 +2466,16 @@ DSV4_API int dsv4cuda_decoder_set_moe_layers(dsv4cuda_decoder* D, dsv4cuda_moe_l
   for (auto* L : D->ep)
     if (!L) return fail("dsv4cuda_decoder_set_moe_layers: null layer");
   if (D->graph) {  // the captured step called the previous MoE path
+    cudaGraphExecDestroy(D->graph);
+    D->graph = nullptr;
+  }
+  return 0;
+}
+
+DSV4_API int dsv4cuda_decoder_set_ep_replicated(dsv4cuda_decoder* D, int replicated) {
+  if (!D) return fail("dsv4cuda_decoder_set_ep_replicated: null decoder");
+  D->ep_replicated = replicated != 0;
+  if (D->graph) {  // the captured step called the other exchange
     cudaGraphExecDestroy(D->graph);
     D->graph = nullptr;
   }

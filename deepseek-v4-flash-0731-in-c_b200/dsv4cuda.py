@@ -788,6 +788,7 @@ for _n, _r, _a in (("dsv4cuda_decoder_create", C.c_int, [vp, vp, vp, vp]),
                    ("dsv4cuda_decoder_cache", C.c_int, [vp, C.c_int, vp]),
                    ("dsv4cuda_decoder_step_kernels", C.c_int, [vp]),
                    ("dsv4cuda_decoder_set_moe_layers", C.c_int, [vp, vp, C.c_int]),
+                   ("dsv4cuda_decoder_set_ep_replicated", C.c_int, [vp, C.c_int]),
                    ("dsv4cuda_decoder_verify", C.c_int, [vp, vp, C.c_int, C.c_int, vp, vp]),
                    ("dsv4cuda_decoder_verify_device", C.c_int, [vp, C.c_int, vp]),
                    ("dsv4cuda_decoder_commit", C.c_int, [vp, C.c_int, vp]),
@@ -906,6 +907,11 @@ class Decoder:
         arr = (vp * max(len(moe_layers), 1))(*[m.handle for m in moe_layers])
         self._ep = list(moe_layers)
         if lib.dsv4cuda_decoder_set_moe_layers(self.handle, arr, len(moe_layers)) != 0:
+            raise Dsv4CudaError(lib.dsv4cuda_decoder_last_error().decode())
+
+    def set_ep_replicated(self, on):
+        """Batch-1 expert parallelism: every rank decodes the same token."""
+        if lib.dsv4cuda_decoder_set_ep_replicated(self.handle, 1 if on else 0) != 0:
             raise Dsv4CudaError(lib.dsv4cuda_decoder_last_error().decode())
 
     def read(self):

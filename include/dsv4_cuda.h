@@ -566,6 +566,11 @@ const char *dsv4cuda_decoder_last_error(void);
  * its token's owner over peer memory (dsv4cuda_moe_forward_ep_tokens). All
  * ranks step in lockstep. n == 0 returns to the local MoE weights. */
 int dsv4cuda_decoder_set_moe_layers(dsv4cuda_decoder *D, dsv4cuda_moe_layer *const *layers, int n);
+/* replicated = 1: every rank decodes the same token (batch-1 decode over
+ * the ranks' experts, dsv4cuda_moe_forward_ep: each rank routes the token,
+ * computes its own experts' slots and exchanges them); 0 (default): the
+ * token-parallel exchange above. */
+int dsv4cuda_decoder_set_ep_replicated(dsv4cuda_decoder *D, int replicated);
 /* Clears the latent rings (dsv4_model_reset_context). Async on stream. */
 int dsv4cuda_decoder_reset(dsv4cuda_decoder *D, void *stream);
 /* dsv4_forward_token: host token/position in, host logits[vocab] (may be
