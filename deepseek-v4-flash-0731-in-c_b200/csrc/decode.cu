@@ -101,7 +101,8 @@ __global__ void embed_kernel(const uint16_t* embed, const int* token, int vocab,
 // new latent goes to (pos % win, :5304) and the RoPE cos/sin of the position.
 __global__ void position_kernel(const int* pos_ptr, int win, int half, int max_pos,
                                 const float* cos_tab, const float* sin_tab, int* idx,
-                                long long* row, float* cosv, float* sinv) {
+                                long long* row, float* cosv, float* sinv, const float* cos_tab_c,
+                                const float* sin_tab_c, float* cosv_c, float* sinv_c) {
   pdl_wait();
   pdl_trigger();
   int pos = *pos_ptr;
@@ -114,6 +115,10 @@ __global__ void position_kernel(const int* pos_ptr, int win, int half, int max_p
   for (int i = threadIdx.x; i < half; i += blockDim.x) {
     cosv[i] = cos_tab[static_cast<size_t>(pos) * half + i];
     sinv[i] = sin_tab[static_cast<size_t>(pos) * half + i];
+    if (cosv_c) {  // the compressed layers' table (YaRN)
+      cosv_c[i] = cos_tab_c[static_cast<size_t>(pos) * half + i];
+      sinv_c[i] = sin_tab_c[static_cast<size_t>(pos) * half + i];
+    }
   }
   if (threadIdx.x == 0) *row = pos % win;
 }
@@ -1283,6 +1288,165 @@ __global__ void __launch_bounds__(kWhThreads) win_head_kernel(const WinAttnArgs 
   win_head_run(a, win + r * a0.n * a0.d, err, blockIdx.x, wsm, [] { pdl_wait(); });
 }
 
+// The same attention over a longer key list (a compressed layer's window
+// plus its compressed rows, n keys, -1 = padding) than shared memory holds:
+// one CTA per head streams the staged BF16 rows in chunks of kWideKeys
+// twice - the scores (every key's dot in dimension order) for the softmax
+// over all keys, then the values (every dimension pair's chain in key order,
+// carried across chunks) - with the head's q kept in shared memory.
+constexpr int kWideKeys = 64;
+
+__host__ __device__ inline size_t wide_head_smem(int n, int d) {
+  return static_cast<size_t>(kWideKeys) * (d + 8) * 2 + static_cast<size_t>(d) * 4 +
+         static_cast<size_t>(3) * n * 4 + 16;
+}
+
+__global__ void __launch_bounds__(kWhThreads) wide_head_kernel(const WinAttnArgs a,
+                                                               const uint16_t* win,
+                                                               unsigned int* err) {
+  extern __shared__ __align__(16) unsigned char wsm[];
+  __shared__ uint64_t bar;
+  __shared__ float den_s;
+  pdl_trigger();
+  const int h = blockIdx.x;
+  const int n = a.n, d = a.d, ldk = d + 8;
+  uint16_t* ks = reinterpret_cast<uint16_t*>(wsm);                                  // [KC][d + 8]
+  float* qs = reinterpret_cast<float*>(wsm + static_cast<size_t>(kWideKeys) * ldk * 2);  // [d]
+  float* ss = qs + d;                                                                // [n]
+  float* ws = ss + n;                                                                // [n]
+  int* sidx = reinterpret_cast<int*>(ws + n);                                        // [n]
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int nth = blockDim.x;
+  if (tid == 0) {
+    mbar_init(&bar, 1);
+    mbar_fence_init();
+  }
+  __syncthreads();
+  pdl_wait();
+  for (int t = tid; t < n; t += nth) sidx[t] = a.idx[t];
+  for (int i = tid; i < d / 4; i += nth)
+    reinterpret_cast<float4*>(qs)[i] = reinterpret_cast<const float4*>(a.q + static_cast<size_t>(h) * d)[i];
+  if (a.q_raw) {
+    __shared__ double qred[32];
+    __syncthreads();
+    double sq = 0.0;
+    for (int i = tid; i < d; i += nth) sq += static_cast<double>(qs[i]) * qs[i];
+    sq = block_sum_d(sq, qred);
+    const float rr = rms_factor(sq, d, a.q_eps);
+    for (int i = tid; i < d; i += nth) qs[i] = bf16_round(__fmul_rn(qs[i], rr));
+    __syncthreads();
+    const int half = a.rope_dim / 2, start = d - a.rope_dim;
+    for (int i = tid; i < half; i += nth) {
+      const float x0 = qs[start + 2 * i], x1 = qs[start + 2 * i + 1];
+      const float c = a.cosv[i], sn = a.sinv[i];
+      qs[start + 2 * i] = bf16_round(__fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, sn)));
+      qs[start + 2 * i + 1] = bf16_round(__fadd_rn(__fmul_rn(x0, sn), __fmul_rn(x1, c)));
+    }
+  }
+  const uint32_t row_bytes = static_cast<uint32_t>(d) * 2;
+  uint32_t phase = 0;
+  // one chunk of staged rows into ks; false (every thread) when the copy
+  // did not land within the bounded wait
+  auto load_chunk = [&](int c0, int nk) -> bool {
+    __syncthreads();  // every thread is done with the previous chunk
+    if (tid == 0) mbar_arrive_expect_tx(&bar, row_bytes * static_cast<uint32_t>(nk));
+    __syncthreads();
+    for (int t = tid; t < nk; t += nth)
+      bulk_g2s(ks + static_cast<size_t>(t) * ldk, win + static_cast<size_t>(c0 + t) * d, row_bytes, &bar);
+    bool ok = mbar_wait(&bar, phase, err);
+    if (!__syncthreads_and(ok)) {
+      if (!ok) mbar_wait(&bar, phase, err);  // the copies in flight land before the CTA exits
+      return false;
+    }
+    phase ^= 1u;
+    return true;
+  };
+  for (int c0 = 0; c0 < n; c0 += kWideKeys) {
+    const int nk = min(kWideKeys, n - c0);
+    if (!load_chunk(c0, nk)) return;
+    for (int t = tid; t < nk; t += nth) {
+      const int r = sidx[c0 + t];
+      float st = -INFINITY;
+      if (r >= 0 && r < a.cache.rows) {
+        const uint16_t* kr = ks + static_cast<size_t>(t) * ldk;
+        float dot = 0.0f;
+#pragma unroll 4
+        for (int i = 0; i < d; i += 8) {
+          float kf[8];
+          bf16x8_to_f32(*reinterpret_cast<const uint4*>(kr + i), kf);
+          const float4 q0 = *reinterpret_cast<const float4*>(qs + i);
+          const float4 q1 = *reinterpret_cast<const float4*>(qs + i + 4);
+          dot = fmaf(q0.x, kf[0], dot);
+          dot = fmaf(q0.y, kf[1], dot);
+          dot = fmaf(q0.z, kf[2], dot);
+          dot = fmaf(q0.w, kf[3], dot);
+          dot = fmaf(q1.x, kf[4], dot);
+          dot = fmaf(q1.y, kf[5], dot);
+          dot = fmaf(q1.z, kf[6], dot);
+          dot = fmaf(q1.w, kf[7], dot);
+        }
+        st = __fmul_rn(dot, a.scale);
+      }
+      ss[c0 + t] = st;
+    }
+  }
+  __syncthreads();
+  if (warp == 0) {
+    float mx = -INFINITY;
+    for (int t = lane; t < n; t += 32) mx = fmaxf(mx, ss[t]);
+    mx = warp_max(mx);
+    for (int t = lane; t < n; t += 32) {
+      const float st = ss[t];
+      ws[t] = st != -INFINITY ? expf_r1(st - mx) : 0.0f;
+    }
+    __syncwarp();
+    if (lane == 0) {
+      float sum = expf_r1(a.sink[h] - mx);
+      for (int t = 0; t < n; ++t)
+        if (ss[t] != -INFINITY) sum += ws[t];
+      den_s = sum;
+    }
+    __syncwarp();
+    for (int t = lane; t < n; t += 32) ws[t] = bf16_round(ws[t]);
+  }
+  __syncthreads();
+  const float den = den_s;
+  // d / 2 dimension pairs, two per thread (d <= 4 * blockDim.x)
+  const int p0 = tid, p1 = tid + nth;
+  const bool has0 = p0 < d / 2, has1 = p1 < d / 2;
+  float o[2][2] = {{0.f, 0.f}, {0.f, 0.f}};
+  for (int c0 = 0; c0 < n; c0 += kWideKeys) {
+    const int nk = min(kWideKeys, n - c0);
+    if (!load_chunk(c0, nk)) return;
+    for (int t = 0; t < nk; ++t) {
+      const float wt = ws[c0 + t];
+      const uint16_t* vr = ks + static_cast<size_t>(t) * ldk;
+      const uint32_t v0 = has0 ? *reinterpret_cast<const uint32_t*>(vr + 2 * p0) : 0u;
+      const uint32_t v1 = has1 ? *reinterpret_cast<const uint32_t*>(vr + 2 * p1) : 0u;
+      o[0][0] = fmaf(wt, __uint_as_float(v0 << 16), o[0][0]);
+      o[0][1] = fmaf(wt, __uint_as_float(v0 & 0xFFFF0000u), o[0][1]);
+      o[1][0] = fmaf(wt, __uint_as_float(v1 << 16), o[1][0]);
+      o[1][1] = fmaf(wt, __uint_as_float(v1 & 0xFFFF0000u), o[1][1]);
+    }
+  }
+  const int start = d - a.rope_dim;
+#pragma unroll
+  for (int u = 0; u < 2; ++u) {
+    if (!(u ? has1 : has0)) continue;
+    const int i = 2 * (u ? p1 : p0);
+    float x0 = bf16_round(o[u][0] / den), x1 = bf16_round(o[u][1] / den);
+    if (a.cosv && i >= start) {
+      const int k = (i - start) / 2;
+      const float cs = a.cosv[k], sn = a.sinv[k];
+      const float y0 = bf16_round(__fadd_rn(__fmul_rn(x0, cs), __fmul_rn(x1, sn)));
+      const float y1 = bf16_round(__fadd_rn(__fmul_rn(-x0, sn), __fmul_rn(x1, cs)));
+      x0 = y0;
+      x1 = y1;
+    }
+    *reinterpret_cast<float2*>(a.out + static_cast<size_t>(h) * d + i) = make_float2(x0, x1);
+  }
+}
+
 // Greedy token: argmax_logits (src/cli/dsv4_run.c:355; first maximum, strict
 // >) in two stages - each CTA finds its chunk's first maximum, then one warp
 // takes the chunks' results in chunk order with the same strict >. For
@@ -1354,6 +1518,12 @@ __global__ void hc_post_kernel(float* state, const float* branch, const float* p
   }
 }
 
+__global__ void fill_f32_kernel(float* p, size_t n, float v) {
+  for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<size_t>(gridDim.x) * blockDim.x)
+    p[i] = v;
+}
+
 // wo_a decode at load (src/dsv4/dsv4_model.c:1927-1936): BF16 of the E4M3
 // code times its [128x128] block's E8M0 scale.
 __global__ void fp8_to_bf16_kernel(const uint8_t* codes, const uint8_t* scales, int rows, int cols,
@@ -1366,6 +1536,304 @@ __global__ void fp8_to_bf16_kernel(const uint8_t* codes, const uint8_t* scales, 
     const float v = __fmul_rn(e4m3_decode(codes[i]),
                               e8m0_decode(scales[static_cast<size_t>(r / 128) * scols + c / 128]));
     out[i] = static_cast<uint16_t>(__float_as_uint(bf16_round(v)) >> 16);
+  }
+}
+
+// ---- compressed attention state (compress ratio 4 / 128 layers) ----
+
+// 2^ceil(log2(r)) for a positive normal r, frexp's rule as the reference
+// writes it (m == 0.5 -> one binade down).
+__device__ __forceinline__ float pow2_ceil(float r) {
+  const uint32_t u = __float_as_uint(r);
+  int e = static_cast<int>((u >> 23) & 0xFFu) - 126;
+  if ((u & 0x7FFFFFu) == 0u) e -= 1;
+  return __uint_as_float(static_cast<uint32_t>(e + 127) << 23);
+}
+
+// dsv4_hadamard_inplace (src/dsv4/dsv4_model.c:1454-1468) on x[0..n) in
+// shared memory, n a power of two: the butterfly stages (each pair's sum and
+// difference in fp32), then x * (1 / sqrtf(n)) rounded to BF16. Every
+// thread of the CTA calls it.
+__device__ void hadamard_smem(float* x, int n) {
+  for (int len = 1; len < n; len <<= 1) {
+    __syncthreads();
+    for (int k = threadIdx.x; k < n / 2; k += blockDim.x) {
+      const int i = (k / len) * 2 * len + (k % len);
+      const float a = x[i], b = x[i + len];
+      x[i] = __fadd_rn(a, b);
+      x[i + len] = __fsub_rn(a, b);
+    }
+  }
+  __syncthreads();
+  const float inv = 1.0f / sqrtf(static_cast<float>(n));
+  for (int i = threadIdx.x; i < n; i += blockDim.x) x[i] = bf16_round(__fmul_rn(x[i], inv));
+  __syncthreads();
+}
+
+// dsv4_fp4_act_quant_inplace (:1417-1452, mode 0) on x[0..n) in shared
+// memory: per 32 values the power-of-two scale of amax / 6 (floor 6 *
+// 2^-126), each value to the nearest E2M1 magnitude (ties to the even
+// code, the reference's scan), times the scale, BF16. Warp = group.
+__device__ void fp4_quant_smem(float* x, int n) {
+  const float mags[8] = {0.0f, 0.5f, 1.0f, 1.5f, 2.0f, 3.0f, 4.0f, 6.0f};
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  __syncthreads();
+  for (int g = warp; g * 32 < n; g += nw) {
+    const int i = g * 32 + lane;
+    const float v = i < n ? x[i] : 0.0f;
+    float amax = warp_max(fabsf(v));
+    const float floor6 = 6.0f * __uint_as_float(1u << 23);  // 6 * 2^-126
+    if (amax < floor6) amax = floor6;
+    const float scale = pow2_ceil(__fmul_rn(amax, 1.0f / 6.0f));
+    const float inv = 1.0f / scale;
+    if (i < n) {
+      float q = __fmul_rn(v, inv);
+      q = q > 6.0f ? 6.0f : (q < -6.0f ? -6.0f : q);
+      const float aq = fabsf(q);
+      int idx = 0;
+      float best = aq;
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const float dd = fabsf(__fsub_rn(aq, mags[k]));
+        if (dd < best) { best = dd; idx = k; }
+        else if (dd == best && (k & 1) == 0) idx = k;
+      }
+      x[i] = bf16_round(__fmul_rn(q < 0.0f ? -mags[idx] : mags[idx], scale));
+    }
+  }
+  __syncthreads();
+}
+
+// compressor_update (src/dsv4/dsv4_model.c:5100-5236) for one token, after
+// its two BF16 projections kv, sc [coff * d] (fp32, as the reference keeps
+// them): score += ape[pos % ratio], both into the state slot; at a block's
+// last position the block's rows are pooled per channel (softmax of the
+// scores over the rows, fmaf-weighted sum of the kv rows in row order),
+// rounded to BF16, RMSNorm with the gain, RoPE of the compressed table at
+// the block's first position, then the FP8 QAT of the KV cache (the row goes
+// to cache row row0 + count) or, for the indexer (rotate), Hadamard + FP4
+// QAT (the row goes to out[count][d]). One CTA, any multiple of 32 threads.
+struct CompStepArgs {
+  const float* kv;        // [coff * d]
+  const float* sc;        // [coff * d]
+  const float* ape;       // [ratio][coff * d]
+  float* kvs;             // state [coff * ratio][coff * d], zeros at reset
+  float* scs;             // state, -inf at reset
+  const uint16_t* norm;   // [d] BF16 gain
+  int d, ratio, coff, rotate, rope_dim;
+  float eps;
+  const int* pos;
+  int* count;
+  int max_count;
+  const float* cos_tab;   // compressed-layer RoPE [max_pos][rope_dim / 2]
+  const float* sin_tab;
+  int max_pos;
+  Fp8KvCache cache;       // main compressor: the cache and its first compressed row
+  long long row0;
+  float* out;             // indexer: [max_count][d]
+  unsigned int* err;
+};
+
+__global__ void comp_step_kernel(const CompStepArgs a) {
+  extern __shared__ float csm[];  // [d]
+  __shared__ double red[32];
+  pdl_trigger();
+  pdl_wait();
+  const int tid = threadIdx.x, nt = blockDim.x, lane = tid & 31, warp = tid >> 5;
+  const int pos = *a.pos;
+  const int cd = a.coff * a.d;
+  const int r = pos % a.ratio;
+  const int slot = r + (a.coff == 2 ? a.ratio : 0);
+  for (int i = tid; i < cd; i += nt) {
+    a.kvs[static_cast<size_t>(slot) * cd + i] = a.kv[i];
+    a.scs[static_cast<size_t>(slot) * cd + i] = __fadd_rn(a.sc[i], a.ape[static_cast<size_t>(r) * cd + i]);
+  }
+  if ((pos + 1) % a.ratio != 0) return;  // uniform over the CTA
+  __syncthreads();
+  const int rows = a.ratio * a.coff;
+  for (int ch = tid; ch < a.d; ch += nt) {
+    // row i of the block: the previous block's first half, then this
+    // block's second half (coff 2), or this block (coff 1)
+    auto at = [&](int i) {
+      return static_cast<size_t>(i) * cd + ((a.coff == 2 && i >= a.ratio) ? a.d : 0) + ch;
+    };
+    float mx = a.scs[at(0)];
+    for (int i = 1; i < rows; ++i) {
+      const float b = a.scs[at(i)];
+      if (b > mx) mx = b;
+    }
+    float sum = 0.0f;
+    for (int i = 0; i < rows; ++i) sum = __fadd_rn(sum, expf_r1(__fsub_rn(a.scs[at(i)], mx)));
+    const float inv = 1.0f / sum;
+    float acc = 0.0f;
+    for (int i = 0; i < rows; ++i)
+      acc = fmaf(__fmul_rn(expf_r1(__fsub_rn(a.scs[at(i)], mx)), inv), a.kvs[at(i)], acc);
+    csm[ch] = bf16_round(acc);
+  }
+  __syncthreads();
+  if (a.coff == 2) {
+    // kv_state[:ratio] = kv_state[ratio:] (the halves do not overlap)
+    for (int i = tid; i < a.ratio * cd; i += nt) {
+      a.kvs[i] = a.kvs[static_cast<size_t>(a.ratio) * cd + i];
+      a.scs[i] = a.scs[static_cast<size_t>(a.ratio) * cd + i];
+    }
+  }
+  // RMSNorm with the gain (rmsnorm_bf16, :4934)
+  double ss = 0.0;
+  for (int ch = tid; ch < a.d; ch += nt) ss += static_cast<double>(csm[ch]) * csm[ch];
+  ss = block_sum_d(ss, red);
+  const float rr = rms_factor(ss, a.d, a.eps);
+  for (int ch = tid; ch < a.d; ch += nt)
+    csm[ch] = bf16_round(__fmul_rn(__fmul_rn(csm[ch], rr), bf16_widen(a.norm[ch])));
+  __syncthreads();
+  // RoPE at the block start (dsv4_rope_apply_buf, :1547-1558)
+  if (a.d >= a.rope_dim) {
+    int blk = pos + 1 - a.ratio;
+    if (blk < 0) blk = 0;
+    if (blk >= a.max_pos) blk = a.max_pos - 1;
+    const int half = a.rope_dim / 2, start = a.d - a.rope_dim;
+    for (int i = tid; i < half; i += nt) {
+      const float x0 = csm[start + 2 * i], x1 = csm[start + 2 * i + 1];
+      const float c = a.cos_tab[static_cast<size_t>(blk) * half + i];
+      const float sn = a.sin_tab[static_cast<size_t>(blk) * half + i];
+      csm[start + 2 * i] = bf16_round(__fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, sn)));
+      csm[start + 2 * i + 1] = bf16_round(__fadd_rn(__fmul_rn(x0, sn), __fmul_rn(x1, c)));
+    }
+  }
+  __syncthreads();
+  const int cnt = *a.count;
+  if (cnt >= a.max_count) {
+    if (tid == 0) atomicOr(a.err, 16u);  // more compressed rows than the decoder holds
+    return;
+  }
+  if (a.rotate) {
+    hadamard_smem(csm, a.d);
+    fp4_quant_smem(csm, a.d);
+    for (int ch = tid; ch < a.d; ch += nt) a.out[static_cast<size_t>(cnt) * a.d + ch] = csm[ch];
+  } else {
+    const long long row = a.row0 + cnt;
+    for (int g = warp; g < a.cache.nope / 64; g += nt >> 5)
+      kv_quant_group(a.cache, row, g, csm[g * 64 + lane], csm[g * 64 + 32 + lane], lane);
+    for (int i = tid; i < a.cache.rope_dim; i += nt)
+      a.cache.rope[row * a.cache.rope_dim + i] =
+          static_cast<uint16_t>(__float_as_uint(bf16_round(csm[a.cache.nope + i])) >> 16);
+  }
+  __syncthreads();
+  if (tid == 0) *a.count = cnt + 1;
+}
+
+// The indexer's query (indexer_forward, :5699-5712): per head (CTA) the
+// BF16 output of idx_wq_b, RoPE of the compressed table at the position on
+// the head's last rope_dim dims, Hadamard, FP4 QAT; in place.
+__global__ void idx_query_kernel(float* q, int id, int rope_dim, const float* cosv,
+                                 const float* sinv) {
+  extern __shared__ float qsm[];  // [id]
+  pdl_trigger();
+  pdl_wait();
+  float* qh = q + static_cast<size_t>(blockIdx.x) * id;
+  for (int i = threadIdx.x; i < id; i += blockDim.x) qsm[i] = qh[i];
+  __syncthreads();
+  const int half = rope_dim / 2, start = id - rope_dim;
+  for (int i = threadIdx.x; i < half; i += blockDim.x) {
+    const float x0 = qsm[start + 2 * i], x1 = qsm[start + 2 * i + 1];
+    const float c = cosv[i], sn = sinv[i];
+    qsm[start + 2 * i] = bf16_round(__fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, sn)));
+    qsm[start + 2 * i + 1] = bf16_round(__fadd_rn(__fmul_rn(x0, sn), __fmul_rn(x1, c)));
+  }
+  hadamard_smem(qsm, id);
+  fp4_quant_smem(qsm, id);
+  for (int i = threadIdx.x; i < id; i += blockDim.x) qh[i] = qsm[i];
+}
+
+// Index scores (:5733-5747): score[t] = sum over heads h in order of
+// fmaf(relu(q_h . k_t), w_h, acc), the dot one fmaf chain over the head's
+// dims; w_h = bf16(proj_h * (id^-1/2 * ih^-1/2)). CTA = kIdxT compressed
+// rows x ih heads (thread = (row, head) dot), t < min(count, (pos + 1) / 4).
+constexpr int kIdxT = 8;
+__global__ void idx_score_kernel(const float* q, const float* keys, const float* wproj, int ih,
+                                 int id, const int* count, const int* pos, float* score) {
+  extern __shared__ float dots[];  // [kIdxT][ih]
+  pdl_trigger();
+  pdl_wait();
+  int nt = *count;
+  const int maxc = (*pos + 1) / 4;
+  if (nt > maxc) nt = maxc;
+  const int tl = threadIdx.x / ih, h = threadIdx.x % ih;
+  const int t = blockIdx.x * kIdxT + tl;
+  if (tl < kIdxT && t < nt) {
+    const float* qh = q + static_cast<size_t>(h) * id;
+    const float* kp = keys + static_cast<size_t>(t) * id;
+    float dot = 0.0f;
+    for (int dd = 0; dd < id; ++dd) dot = fmaf(qh[dd], kp[dd], dot);
+    if (dot < 0.0f) dot = 0.0f;
+    dots[tl * ih + h] = dot;
+  }
+  __syncthreads();
+  if (h == 0 && tl < kIdxT && t < nt) {
+    const float s = __fmul_rn(1.0f / sqrtf(static_cast<float>(id)), 1.0f / sqrtf(static_cast<float>(ih)));
+    float acc = 0.0f;
+    for (int k = 0; k < ih; ++k) acc = fmaf(dots[tl * ih + k], bf16_round(__fmul_rn(wproj[k], s)), acc);
+    score[t] = acc;
+  }
+}
+
+// The attention key list of a compressed layer: the window's list (as the
+// window-only layers use it, -1 padded), then the compressed rows - the
+// indexer's top-k for ratio 4 (dsv4_indexer_select_topk, :5636-5679: score
+// descending, lower index first, k = min(index_topk, n)) or every compressed
+// row in order for ratio 128 (:5330-5336) - then -1 padding to n_max. Rows
+// are row0 + compressed index. One CTA; the ratio-4 selection sorts the
+// scores (bitonic, n2 a power of two >= the most compressed rows) in shared
+// memory.
+__global__ void comp_list_kernel(const int* win_idx, int win, const float* score, const int* count,
+                                 const int* pos, int ratio, int topk, long long row0, int n2,
+                                 int n_max, int* out) {
+  extern __shared__ unsigned char lsm[];
+  float* ks = reinterpret_cast<float*>(lsm);
+  int* ki = reinterpret_cast<int*>(ks + n2);
+  pdl_trigger();
+  pdl_wait();
+  const int tid = threadIdx.x, nt = blockDim.x;
+  for (int i = tid; i < win; i += nt) out[i] = win_idx[i];
+  int n = *count;
+  int k = n;
+  if (ratio == 4) {
+    const int maxc = (*pos + 1) / 4;
+    if (n > maxc) n = maxc;
+    k = topk < n ? topk : n;
+    for (int i = tid; i < n2; i += nt) {
+      ks[i] = i < n ? score[i] : 0.0f;
+      ki[i] = i < n ? i : -1;  // -1: padding, after every real row
+    }
+    // "a before b": real before padding; higher score first; lower index first
+    auto before = [&](int i, int j) {
+      if (ki[j] < 0) return ki[i] >= 0;
+      if (ki[i] < 0) return false;
+      if (ks[i] > ks[j]) return true;
+      if (ks[i] < ks[j]) return false;
+      return ki[i] < ki[j];
+    };
+    for (int size = 2; size <= n2; size <<= 1)
+      for (int stride = size >> 1; stride > 0; stride >>= 1) {
+        __syncthreads();
+        for (int i = tid; i < n2; i += nt) {
+          const int j = i ^ stride;
+          if (j > i) {
+            const bool up = (i & size) == 0;
+            const bool swap = up ? before(j, i) : before(i, j);
+            if (swap) {
+              const float tf = ks[i]; ks[i] = ks[j]; ks[j] = tf;
+              const int ti = ki[i]; ki[i] = ki[j]; ki[j] = ti;
+            }
+          }
+        }
+      }
+    __syncthreads();
+  }
+  for (int i = tid; i < n_max - win; i += nt) {
+    int v = -1;
+    if (i < k) v = static_cast<int>(row0 + (ratio == 4 ? ki[i] : i));
+    out[win + i] = v;
   }
 }
 
@@ -1437,6 +1905,15 @@ struct Layer {
   MoeWeights mw;
   Fp8KvCache cache;
   uint16_t* wo_a = nullptr;  // BF16, decoded at create when given as FP8
+  // compress ratio 4 / 128: the compressor's state, its rows in the cache
+  // (from comp_row0) and, for ratio 4, the indexer's state and rows
+  int ratio = 0, coff = 1;
+  float *kvs = nullptr, *scs = nullptr;
+  int* count = nullptr;
+  int max_count = 0;
+  long long comp_row0 = 0;
+  float *idx_kvs = nullptr, *idx_scs = nullptr, *idx_rows = nullptr;
+  int* idx_count = nullptr;
 };
 
 }  // namespace
@@ -1490,6 +1967,18 @@ struct dsv4cuda_decoder {
   long long* row = nullptr;   // [1]
   float *cosv = nullptr, *sinv = nullptr;      // [rope/2] of the current position
   float *cos_tab = nullptr, *sin_tab = nullptr;  // [max_context][rope/2]
+  // compressed layers: their RoPE (YaRN table), scratch of the compressor
+  // and indexer, the key list and its staged rows
+  bool any_comp = false;
+  int n_max = 0;                   // keys of the longest list
+  float *cosv_c = nullptr, *sinv_c = nullptr;
+  float *cos_tab_c = nullptr, *sin_tab_c = nullptr;
+  float *comp_kv = nullptr, *comp_sc = nullptr;  // [2 * head_dim]
+  float *idx_q = nullptr, *idx_w = nullptr;      // [index_heads * index_dim], [index_heads]
+  float* idx_score = nullptr;      // [most compressed rows]
+  int idx_n2 = 0;                  // its sort width (a power of two)
+  int* idx_full = nullptr;         // [n_max]
+  uint16_t* kvwin_full = nullptr;  // [n_max][head_dim]
   dsv4::GemvItem* item1 = nullptr;   // one (x row 0 -> y row 0) item
   dsv4::GemvItem* items_g = nullptr; // o_groups items (group g: matrix g, rows g)
   int* n_one = nullptr;
@@ -1576,6 +2065,45 @@ void rope_tables(const dsv4cuda_decoder_config& c, std::vector<float>& cs, std::
   for (int i = 0; i < half; ++i) {
     volatile float expo = static_cast<float>(2 * i) / static_cast<float>(c.rope_dim);
     inv[i] = 1.0f / powf(c.rope_theta, expo);
+  }
+  for (int p = 0; p < c.max_context; ++p)
+    for (int i = 0; i < half; ++i) {
+      volatile float angle = static_cast<float>(p) * inv[i];
+      cs[static_cast<size_t>(p) * half + i] = cosf(angle);
+      sn[static_cast<size_t>(p) * half + i] = sinf(angle);
+    }
+}
+
+// The compressed layers' RoPE table: rope_freqs_fill (src/dsv4/dsv4_model.c:
+// 1475-1503) with YaRN on and compress_rope_theta, host libm as the
+// reference.
+void rope_tables_yarn(const dsv4cuda_decoder_config& c, std::vector<float>& cs,
+                      std::vector<float>& sn) {
+  const int half = c.rope_dim / 2;
+  cs.resize(static_cast<size_t>(c.max_context) * half);
+  sn.resize(cs.size());
+  const float theta = c.compress_rope_theta;
+  const float rd = static_cast<float>(c.rope_dim);
+  const float pi = static_cast<float>(M_PI);
+  volatile float lnum = logf(static_cast<float>(c.original_position) / (c.beta_fast * 2.0f * pi));
+  volatile float lden = 2.0f * logf(theta);
+  float low = floorf(rd * lnum / lden);
+  volatile float hnum = logf(static_cast<float>(c.original_position) / (c.beta_slow * 2.0f * pi));
+  float high = ceilf(rd * hnum / lden);
+  if (low < 0) low = 0;
+  if (high > rd - 1.0f) high = rd - 1.0f;
+  if (high == low) high += 0.001f;
+  std::vector<float> inv(half);
+  for (int i = 0; i < half; ++i) {
+    volatile float expo = static_cast<float>(2 * i) / rd;
+    volatile float base = 1.0f / powf(theta, expo);
+    float ramp = (static_cast<float>(i) - low) / (high - low);
+    if (ramp < 0.0f) ramp = 0.0f;
+    if (ramp > 1.0f) ramp = 1.0f;
+    volatile float interp = base / c.rope_factor;
+    volatile float a = interp * ramp;
+    volatile float b = base * (1.0f - ramp);
+    inv[i] = a + b;
   }
   for (int p = 0; p < c.max_context; ++p)
     for (int i = 0; i < half; ++i) {
@@ -1796,7 +2324,10 @@ cudaError_t hc_join(dsv4cuda_decoder* D, cudaStream_t st) {
 // attention_forward_impl for a compress-ratio-0 layer (src/dsv4/dsv4_model.c:
 // 5241-5429): writes the branch output [hid] into D->branch.
 // D->x arrives with its FP8 quant in D->xq / D->xs.
+cudaError_t attention_comp(dsv4cuda_decoder* D, dsv4::Layer& L, cudaStream_t st);
+
 cudaError_t attention(dsv4cuda_decoder* D, dsv4::Layer& L, cudaStream_t st) {
+  if (L.ratio) return attention_comp(D, L, st);
   const auto& c = D->cfg;
   const auto& w = L.w;
   const int H = c.n_heads, d = c.head_dim, ql = c.q_lora, half = c.rope_dim / 2;
@@ -1897,6 +2428,180 @@ cudaError_t attention(dsv4cuda_decoder* D, dsv4::Layer& L, cudaStream_t st) {
                   D->n_one, D->fp8_part, D->tile_cnt, st, D->oall);
 }
 
+// A BF16 projection of the layer input D->x (one token) into y.
+cudaError_t bf16_x(dsv4cuda_decoder* D, const uint16_t* W, int rows, int round_out, float* y,
+                   cudaStream_t st) {
+  dsv4::Bf16GemvArgs a{};
+  a.W = W;
+  a.in = D->cfg.hidden;
+  a.rows = rows;
+  a.round_out = round_out;
+  a.x = D->x;
+  a.ldx = D->cfg.hidden;
+  a.Y = y;
+  a.items = D->item1;
+  a.n_items = D->n_one;
+  a.max_items = 1;
+  a.static_items = 1;
+  return dsv4::launch_bf16_gemv(a, 1, st);
+}
+
+cudaError_t comp_step(dsv4cuda_decoder* D, dsv4::Layer& L, bool indexer, const float* ape,
+                      const uint16_t* norm, cudaStream_t st) {
+  const auto& c = D->cfg;
+  dsv4::CompStepArgs a{};
+  a.kv = D->comp_kv;
+  a.sc = D->comp_sc;
+  a.ape = ape;
+  a.norm = norm;
+  a.rope_dim = c.rope_dim;
+  a.eps = c.rms_eps;
+  a.pos = D->d_pos;
+  a.max_count = L.max_count;
+  a.cos_tab = D->cos_tab_c;
+  a.sin_tab = D->sin_tab_c;
+  a.max_pos = c.max_context;
+  a.err = dsv4::device_error_word();
+  if (indexer) {
+    a.kvs = L.idx_kvs;
+    a.scs = L.idx_scs;
+    a.d = c.index_dim;
+    a.ratio = 4;
+    a.coff = 2;
+    a.rotate = 1;
+    a.count = L.idx_count;
+    a.out = L.idx_rows;
+  } else {
+    a.kvs = L.kvs;
+    a.scs = L.scs;
+    a.d = c.head_dim;
+    a.ratio = L.ratio;
+    a.coff = L.coff;
+    a.count = L.count;
+    a.cache = L.cache;
+    a.row0 = L.comp_row0;
+  }
+  const int threads = std::min(1024, std::max(32, (a.d + 31) / 32 * 32));
+  return dsv4::launch_pdl(dsv4::comp_step_kernel, dim3(1), dim3(threads), sizeof(float) * a.d, st, a);
+}
+
+// attention_forward_impl for a compress-ratio-4 or -128 layer (src/dsv4/
+// dsv4_model.c:5241-5429): the window layer's projections (the q / kv RoPE
+// from the compressed table), then compressor_update (:5319), for ratio 4
+// indexer_forward (:5685: its query, its own compressor, the scores and the
+// top-k), the key list window + compressed rows, sparse_attn over it and the
+// output projections. D->x arrives with its FP8 quant in D->xq / D->xs.
+cudaError_t attention_comp(dsv4cuda_decoder* D, dsv4::Layer& L, cudaStream_t st) {
+  const auto& c = D->cfg;
+  const auto& w = L.w;
+  const int H = c.n_heads, d = c.head_dim, ql = c.q_lora, half = c.rope_dim / 2;
+  const int G = c.o_groups, ol = c.o_lora, hid = c.hidden;
+  DEC_CHECK(fp8_gemv2(w.wq_a, w.wq_a_s, ql, D->qr, w.wkv, w.wkv_s, d, D->kv, hid, D->xq, D->xs,
+                      D->ld, D->item1, D->n_one, D->fp8_part, D->tile_cnt, st));
+  dsv4::NormTailArgs kt{};
+  kt.x = D->kv;
+  kt.n = d;
+  kt.w = w.kv_norm;
+  kt.eps = c.rms_eps;
+  kt.half = half;
+  kt.cosv = D->cosv_c;
+  kt.sinv = D->sinv_c;
+  kt.cache = L.cache;
+  kt.row = D->row;
+  dsv4::NormTailArgs qt{};
+  qt.x = D->qr;
+  qt.n = ql;
+  qt.w = w.q_norm;
+  qt.eps = c.rms_eps;
+  qt.xq = D->xq;
+  qt.xs = D->xs;
+  DEC_CHECK(dsv4::launch_pdl(dsv4::norm_tail_kernel, dim3(2), dim3(256),
+                             sizeof(float) * std::max(d, ql), st, kt, qt));
+  // compressor_update of the main compressor (its row into the cache)
+  DEC_CHECK(bf16_x(D, w.comp_wkv, L.coff * d, 0, D->comp_kv, st));
+  DEC_CHECK(bf16_x(D, w.comp_wgate, L.coff * d, 0, D->comp_sc, st));
+  DEC_CHECK(comp_step(D, L, false, w.comp_ape, w.comp_norm, st));
+  DEC_CHECK(fp8_gemv(w.wq_b, w.wq_b_s, ql, H * d, D->xq, D->xs, D->ld, D->q, D->item1, D->n_one,
+                     D->fp8_part, D->tile_cnt, st));
+  const int* win_idx = D->idx;
+  if (L.ratio == 4) {
+    const int ih = c.index_heads, id = c.index_dim;
+    // the indexer's query from the quantised q latent (still in D->xq)
+    DEC_CHECK(fp8_gemv(w.idx_wq_b, w.idx_wq_b_s, ql, ih * id, D->xq, D->xs, D->ld, D->idx_q,
+                       D->item1, D->n_one, D->fp8_part, D->tile_cnt, st));
+    DEC_CHECK(bf16_x(D, w.idx_comp_wkv, 2 * id, 0, D->comp_kv, st));
+    DEC_CHECK(bf16_x(D, w.idx_comp_wgate, 2 * id, 0, D->comp_sc, st));
+    DEC_CHECK(comp_step(D, L, true, w.idx_ape, w.idx_comp_norm, st));
+    DEC_CHECK(bf16_x(D, w.idx_weights_proj, ih, 1, D->idx_w, st));
+    DEC_CHECK(dsv4::launch_pdl(dsv4::idx_query_kernel, dim3(ih), dim3(std::max(32, std::min(1024, id))),
+                               sizeof(float) * id, st, D->idx_q, id, c.rope_dim,
+                               static_cast<const float*>(D->cosv_c),
+                               static_cast<const float*>(D->sinv_c)));
+    DEC_CHECK(dsv4::launch_pdl(dsv4::idx_score_kernel,
+                               dim3((L.max_count + dsv4::kIdxT - 1) / dsv4::kIdxT),
+                               dim3(dsv4::kIdxT * ih), sizeof(float) * dsv4::kIdxT * ih, st,
+                               static_cast<const float*>(D->idx_q),
+                               static_cast<const float*>(L.idx_rows),
+                               static_cast<const float*>(D->idx_w), ih, id,
+                               static_cast<const int*>(L.idx_count),
+                               static_cast<const int*>(D->d_pos), D->idx_score));
+    DEC_CHECK(dsv4::launch_pdl(dsv4::comp_list_kernel, dim3(1), dim3(1024),
+                               sizeof(float) * 2 * D->idx_n2, st, win_idx, c.window,
+                               static_cast<const float*>(D->idx_score),
+                               static_cast<const int*>(L.idx_count),
+                               static_cast<const int*>(D->d_pos), 4, c.index_topk, L.comp_row0,
+                               D->idx_n2, D->n_max, D->idx_full));
+  } else {
+    DEC_CHECK(dsv4::launch_pdl(dsv4::comp_list_kernel, dim3(1), dim3(1024), 0, st, win_idx,
+                               c.window, static_cast<const float*>(nullptr),
+                               static_cast<const int*>(L.count),
+                               static_cast<const int*>(D->d_pos), L.ratio, 0, L.comp_row0, 0,
+                               D->n_max, D->idx_full));
+  }
+  // the listed rows as BF16, then sparse_attn over them with the inverse RoPE
+  dsv4::NormTailArgs sa = kt;
+  sa.win = D->kvwin_full;
+  sa.idx = D->idx_full;
+  sa.n_win = D->n_max;
+  DEC_CHECK(dsv4::launch_pdl(dsv4::stage_rows_kernel, dim3((D->n_max + 7) / 8, 1), dim3(256), 0,
+                             st, sa));
+  dsv4::WinAttnArgs wa{};
+  wa.q = D->q;
+  wa.cache = L.cache;
+  wa.idx = D->idx_full;
+  wa.sink = w.attn_sink;
+  wa.cosv = D->cosv_c;
+  wa.sinv = D->sinv_c;
+  wa.H = H;
+  wa.d = d;
+  wa.n = D->n_max;
+  wa.rope_dim = c.rope_dim;
+  wa.scale = 1.0f / sqrtf(static_cast<float>(d));
+  wa.out = D->o;
+  wa.q_raw = 1;
+  wa.q_eps = c.rms_eps;
+  DEC_CHECK(hc_join(D, st));
+  DEC_CHECK(dsv4::launch_pdl(dsv4::wide_head_kernel, dim3(H), dim3(dsv4::kWhThreads),
+                             dsv4::wide_head_smem(D->n_max, d), st, wa,
+                             static_cast<const uint16_t*>(D->kvwin_full), dsv4::device_error_word()));
+  dsv4::Bf16GemvArgs ga{};
+  ga.W = L.wo_a;
+  ga.w_stride = static_cast<size_t>(ol) * (H * d / G);
+  ga.in = H * d / G;
+  ga.rows = ol;
+  ga.round_out = 1;
+  ga.x = D->o;
+  ga.ldx = H * d / G;
+  ga.Y = D->oall;
+  ga.items = D->items_g;
+  ga.n_items = D->n_groups;
+  ga.max_items = G;
+  ga.static_items = 1;
+  DEC_CHECK(dsv4::launch_bf16_gemv(ga, 1, st));
+  return fp8_gemv(w.wo_b, w.wo_b_s, G * ol, hid, D->xq, D->xs, D->ld, D->branch, D->item1,
+                  D->n_one, D->fp8_part, D->tile_cnt, st, D->oall);
+}
+
 // One decode step from device token/position into logits + argmax.
 cudaError_t step(dsv4cuda_decoder* D, cudaStream_t st) {
   const auto& c = D->cfg;
@@ -1908,7 +2613,8 @@ cudaError_t step(dsv4cuda_decoder* D, cudaStream_t st) {
                              static_cast<const int*>(D->d_pos), c.window, half, c.max_context,
                              static_cast<const float*>(D->cos_tab),
                              static_cast<const float*>(D->sin_tab), D->idx, D->row, D->cosv,
-                             D->sinv));
+                             D->sinv, static_cast<const float*>(D->cos_tab_c),
+                             static_cast<const float*>(D->sin_tab_c), D->cosv_c, D->sinv_c));
   dsv4::MoeExecOptions opt;
   opt.x_quantized = true;
   if (!c.hc_exact) opt.join = D->hc_join;  // the FFN boundary's split, before the combine
@@ -1957,6 +2663,76 @@ cudaError_t step(dsv4cuda_decoder* D, cudaStream_t st) {
   return dsv4::launch_pdl(dsv4::argmax_final_kernel, dim3(1), dim3(32), 0, st,
                           static_cast<const float*>(D->am_v), static_cast<const int*>(D->am_i),
                           chunks, D->argmax);
+}
+
+// The compressor / indexer state of every compressed layer to its start:
+// kv state zeros, score state -inf, no compressed rows (as the reference's
+// layer run state, src/dsv4/dsv4_model.c:2423-2432, 2693-2700).
+cudaError_t comp_reset(dsv4cuda_decoder* D, cudaStream_t st) {
+  const auto& c = D->cfg;
+  for (auto& L : D->layers) {
+    if (!L.ratio) continue;
+    const size_t nst = static_cast<size_t>(L.coff) * L.ratio * L.coff * c.head_dim;
+    DEC_CHECK(cudaMemsetAsync(L.kvs, 0, nst * sizeof(float), st));
+    dsv4::fill_f32_kernel<<<64, 256, 0, st>>>(L.scs, nst, -INFINITY);
+    DEC_CHECK(cudaGetLastError());
+    DEC_CHECK(cudaMemsetAsync(L.count, 0, sizeof(int), st));
+    if (L.ratio == 4) {
+      const size_t nidx = 16 * static_cast<size_t>(c.index_dim);
+      DEC_CHECK(cudaMemsetAsync(L.idx_kvs, 0, nidx * sizeof(float), st));
+      dsv4::fill_f32_kernel<<<16, 256, 0, st>>>(L.idx_scs, nidx, -INFINITY);
+      DEC_CHECK(cudaGetLastError());
+      DEC_CHECK(cudaMemsetAsync(L.idx_count, 0, sizeof(int), st));
+    }
+  }
+  return cudaSuccess;
+}
+
+// Buffers shared by the compressed layers, the YaRN RoPE table, the kernels'
+// shared-memory limits, and every layer's state at its start. D->err says
+// what failed.
+bool comp_alloc(dsv4cuda_decoder* D) {
+  const auto& c = D->cfg;
+  const int half = c.rope_dim / 2;
+  if (c.index_heads <= 0 || c.index_dim < 32 || (c.index_dim & (c.index_dim - 1)) ||
+      c.index_dim % 32 || c.index_dim < c.rope_dim || c.index_heads * dsv4::kIdxT > 1024 ||
+      c.index_topk <= 0 || c.compress_rope_theta <= 0.f || c.rope_factor <= 0.f ||
+      c.original_position <= 0 || c.head_dim > 4 * dsv4::kWhThreads || D->idx_n2 > 8192) {
+    D->err = "index heads / dim (a power of two >= 32 and >= rope_dim) / top-k or the YaRN "
+             "parameters out of range, or max_context too long for the top-k sort";
+    return false;
+  }
+  bool ok = true;
+  auto chk = [&](const void* p) { ok = ok && p != nullptr; };
+  chk(D->cosv_c = dalloc<float>(D, half));
+  chk(D->sinv_c = dalloc<float>(D, half));
+  chk(D->cos_tab_c = dalloc<float>(D, static_cast<size_t>(c.max_context) * half));
+  chk(D->sin_tab_c = dalloc<float>(D, static_cast<size_t>(c.max_context) * half));
+  const size_t cdmax = 2 * static_cast<size_t>(std::max(c.head_dim, c.index_dim));
+  chk(D->comp_kv = dalloc<float>(D, cdmax));
+  chk(D->comp_sc = dalloc<float>(D, cdmax));
+  chk(D->idx_q = dalloc<float>(D, static_cast<size_t>(c.index_heads) * c.index_dim));
+  chk(D->idx_w = dalloc<float>(D, c.index_heads));
+  chk(D->idx_score = dalloc<float>(D, std::max(D->idx_n2, 1)));
+  chk(D->idx_full = dalloc<int>(D, D->n_max));
+  chk(D->kvwin_full = dalloc<uint16_t>(D, static_cast<size_t>(D->n_max) * c.head_dim));
+  if (!ok) {
+    D->err = "out of device memory";
+    return false;
+  }
+  std::vector<float> cs, sn;
+  rope_tables_yarn(c, cs, sn);
+  if (cudaMemcpy(D->cos_tab_c, cs.data(), cs.size() * sizeof(float), cudaMemcpyHostToDevice) != cudaSuccess ||
+      cudaMemcpy(D->sin_tab_c, sn.data(), sn.size() * sizeof(float), cudaMemcpyHostToDevice) != cudaSuccess ||
+      dsv4::set_max_dynamic_smem(reinterpret_cast<const void*>(dsv4::wide_head_kernel),
+                                 static_cast<int>(dsv4::wide_head_smem(D->n_max, c.head_dim))) != cudaSuccess ||
+      dsv4::set_max_dynamic_smem(reinterpret_cast<const void*>(dsv4::comp_list_kernel),
+                                 static_cast<int>(sizeof(float) * 2 * std::max(D->idx_n2, 1))) != cudaSuccess ||
+      comp_reset(D, nullptr) != cudaSuccess) {
+    D->err = "set-up failed";
+    return false;
+  }
+  return true;
 }
 
 // The verify step's buffers (DSV4CUDA_VERIFY_MAX_ROWS rows), its GEMV items
@@ -2234,6 +3010,7 @@ cudaError_t verify_commit(dsv4cuda_decoder* D, const int* from, cudaStream_t st)
 const char* verify_unsupported(const dsv4cuda_decoder* D, int n) {
   if (n < 1 || n > DSV4CUDA_VERIFY_MAX_ROWS) return "n_rows must be 1 .. DSV4CUDA_VERIFY_MAX_ROWS";
   if (!D->ep.empty()) return "the verify step runs the local MoE layers (no expert parallelism)";
+  if (D->any_comp) return "layers of compress ratio 4 / 128 decode one token at a time";
   if (!D->win_staged || !D->v.kvwin) return "the window does not fit the one-launch attention";
   return nullptr;
 }
@@ -2382,8 +3159,24 @@ DSV4_API int dsv4cuda_decoder_create(dsv4cuda_decoder** out, const dsv4cuda_deco
     }
     L.cache.nope = nope;
     L.cache.rope_dim = c.rope_dim;
-    // rows [0, window): the ring; [window, window + V): a verify step's rows
-    const size_t crows = static_cast<size_t>(c.window) + DSV4CUDA_VERIFY_MAX_ROWS;
+    // rows [0, window): the ring; [window, window + V): a verify step's rows;
+    // then a compressed layer's compressed rows
+    L.ratio = w.compress_ratio;
+    if (L.ratio != 0 && L.ratio != 4 && L.ratio != 128) {
+      dsv4cuda_decoder_destroy(D);
+      return fail("dsv4cuda_decoder_create: layer %d: compress ratio %d (0, 4 or 128)", li, L.ratio);
+    }
+    if (L.ratio && (!w.comp_wkv || !w.comp_wgate || !w.comp_ape || !w.comp_norm ||
+                    (L.ratio == 4 && (!w.idx_wq_b || !w.idx_wq_b_s || !w.idx_weights_proj ||
+                                      !w.idx_comp_wkv || !w.idx_comp_wgate || !w.idx_ape ||
+                                      !w.idx_comp_norm)))) {
+      dsv4cuda_decoder_destroy(D);
+      return fail("dsv4cuda_decoder_create: layer %d misses a compressor / indexer weight", li);
+    }
+    L.coff = L.ratio == 4 ? 2 : 1;
+    L.max_count = L.ratio ? c.max_context / L.ratio + 1 : 0;
+    L.comp_row0 = static_cast<long long>(c.window) + DSV4CUDA_VERIFY_MAX_ROWS;
+    const size_t crows = static_cast<size_t>(c.window) + DSV4CUDA_VERIFY_MAX_ROWS + L.max_count;
     L.cache.rows = static_cast<long long>(crows);
     L.cache.codes = dalloc<uint8_t>(D, crows * nope);
     L.cache.scales = dalloc<uint8_t>(D, crows * dsv4::kKvScaleSlots);
@@ -2395,6 +3188,33 @@ DSV4_API int dsv4cuda_decoder_create(dsv4cuda_decoder** out, const dsv4cuda_deco
       L.wo_a = dalloc<uint16_t>(D, static_cast<size_t>(rows) * cols);
       if (L.wo_a)
         dsv4::fp8_to_bf16_kernel<<<1024, 256>>>(w.wo_a_fp8, w.wo_a_fp8_s, rows, cols, L.wo_a);
+    }
+    if (L.ratio) {
+      const size_t cd = static_cast<size_t>(L.coff) * d, nst = static_cast<size_t>(L.coff) * L.ratio * cd;
+      L.kvs = dalloc<float>(D, nst);
+      L.scs = dalloc<float>(D, nst);
+      L.count = dalloc<int>(D, 1);
+      bool okc = L.kvs && L.scs && L.count;
+      if (L.ratio == 4) {
+        const size_t icd = 2 * static_cast<size_t>(c.index_dim);
+        L.idx_kvs = dalloc<float>(D, 8 * icd);
+        L.idx_scs = dalloc<float>(D, 8 * icd);
+        L.idx_rows = dalloc<float>(D, static_cast<size_t>(L.max_count) * c.index_dim);
+        L.idx_count = dalloc<int>(D, 1);
+        okc = okc && L.idx_kvs && L.idx_scs && L.idx_rows && L.idx_count;
+      }
+      if (!okc) {
+        dsv4cuda_decoder_destroy(D);
+        return fail("dsv4cuda_decoder_create: out of device memory (layer %d state)", li);
+      }
+      D->any_comp = true;
+      const int keys = L.ratio == 4 ? std::min(c.index_topk, L.max_count) : L.max_count;
+      D->n_max = std::max(D->n_max, c.window + keys);
+      if (L.ratio == 4) {
+        int n2 = 1;
+        while (n2 < L.max_count) n2 <<= 1;
+        D->idx_n2 = std::max(D->idx_n2, n2);
+      }
     }
     if (!L.cache.codes || !L.cache.scales || !L.cache.rope || !L.wo_a) {
       dsv4cuda_decoder_destroy(D);
@@ -2417,6 +3237,10 @@ DSV4_API int dsv4cuda_decoder_create(dsv4cuda_decoder** out, const dsv4cuda_deco
   if (!verify_alloc(D)) {
     dsv4cuda_decoder_destroy(D);
     return fail("dsv4cuda_decoder_create: out of device memory (verify buffers)");
+  }
+  if (D->any_comp && !comp_alloc(D)) {
+    dsv4cuda_decoder_destroy(D);
+    return fail("dsv4cuda_decoder_create: compressed layers: %s", D->err.c_str());
   }
   // one MoE workspace serves every layer (their forwards run in stream order)
   {
@@ -2492,6 +3316,7 @@ DSV4_API int dsv4cuda_decoder_reset(dsv4cuda_decoder* D, void* stream) {
     cudaMemsetAsync(L.cache.scales, 0, rows * dsv4::kKvScaleSlots, st);
     cudaMemsetAsync(L.cache.rope, 0, rows * c.rope_dim * 2, st);
   }
+  if (D->any_comp) comp_reset(D, st);
   const cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? 0 : fail("dsv4cuda_decoder_reset: %s", cudaGetErrorString(e));
 }

@@ -757,7 +757,10 @@ class DecoderConfig(C.Structure):
                                        "rope_dim", "q_lora", "o_groups", "o_lora", "window",
                                        "hc_mult", "hc_iters")] + \
         [("rms_eps", C.c_float), ("hc_eps", C.c_float), ("rope_theta", C.c_float),
-         ("max_context", C.c_int), ("moe", MoeConfig), ("hc_exact", C.c_int)]
+         ("max_context", C.c_int), ("moe", MoeConfig), ("hc_exact", C.c_int),
+         ("index_heads", C.c_int), ("index_dim", C.c_int), ("index_topk", C.c_int),
+         ("compress_rope_theta", C.c_float), ("rope_factor", C.c_float),
+         ("beta_fast", C.c_float), ("beta_slow", C.c_float), ("original_position", C.c_int)]
 
 
 class ModelWeights(C.Structure):
@@ -770,7 +773,10 @@ class LayerWeights(C.Structure):
         "attn_norm", "ffn_norm", "hc_attn_fn", "hc_attn_scale", "hc_attn_base",
         "hc_ffn_fn", "hc_ffn_scale", "hc_ffn_base", "attn_sink", "wq_a", "wq_a_s", "q_norm",
         "wq_b", "wq_b_s", "wkv", "wkv_s", "kv_norm", "wo_a", "wo_a_fp8", "wo_a_fp8_s",
-        "wo_b", "wo_b_s")] + [("moe", MoeWeights)]
+        "wo_b", "wo_b_s")] + [("moe", MoeWeights), ("compress_ratio", C.c_int)] + \
+        [(n, vp) for n in ("comp_wkv", "comp_wgate", "comp_ape", "comp_norm", "idx_wq_b",
+                           "idx_wq_b_s", "idx_weights_proj", "idx_comp_wkv", "idx_comp_wgate",
+                           "idx_ape", "idx_comp_norm")]
 
 
 for _n, _r, _a in (("dsv4cuda_decoder_create", C.c_int, [vp, vp, vp, vp]),
@@ -827,6 +833,8 @@ class Decoder:
                 if name == "moe":
                     _, w = _moe_structs(L["moe"])
                     lws[i].moe = w
+                elif name == "compress_ratio":
+                    lws[i].compress_ratio = int(L.get("compress_ratio", 0))
                 else:
                     setattr(lws[i], name, _addr(L.get(name)))
         h = vp()
@@ -979,7 +987,8 @@ def decoder_from_checkpoint(ckpt_dir, max_context, device="cuda", hc_exact=False
     """Weight ingest for the device decoder: reads a checkpoint directory in
     the reference's format (config.json + one safetensors file), stacks the
     routed experts expert-major and uploads everything to `device`.
-    Returns a Decoder. Layers must be of compress ratio 0."""
+    Returns a Decoder. Layers of compress ratio 4 / 128 bring their
+    compressor (and for ratio 4 indexer) tensors."""
     import json
     import torch
     with open(os.path.join(ckpt_dir, "config.json")) as f:
@@ -988,8 +997,8 @@ def decoder_from_checkpoint(ckpt_dir, max_context, device="cuda", hc_exact=False
     t = {}
     for fn in files:
         t.update(read_safetensors(os.path.join(ckpt_dir, fn)))
-    if any(cj["compress_ratios"][:cj["num_hidden_layers"]]):
-        raise ValueError("the device decoder covers compress-ratio-0 layers only")
+    ratios = list(cj["compress_ratios"][:cj["num_hidden_layers"]])
+    ys = cj.get("rope_scaling") or {}
 
     def dev(a):
         return torch.from_numpy(np.ascontiguousarray(a)).to(device)
@@ -1003,6 +1012,12 @@ def decoder_from_checkpoint(ckpt_dir, max_context, device="cuda", hc_exact=False
                hc_iters=cj["hc_sinkhorn_iters"], rms_eps=cj["rms_norm_eps"],
                hc_eps=cj["hc_eps"], rope_theta=cj["rope_theta"], max_context=max_context,
                hc_exact=1 if hc_exact else 0,
+               index_heads=cj.get("index_n_heads", 0), index_dim=cj.get("index_head_dim", 0),
+               index_topk=cj.get("index_topk", 0),
+               compress_rope_theta=cj.get("compress_rope_theta", cj["rope_theta"]),
+               rope_factor=ys.get("factor", 1.0), beta_fast=ys.get("beta_fast", 32.0),
+               beta_slow=ys.get("beta_slow", 1.0),
+               original_position=ys.get("original_max_position_embeddings", 4096),
                moe=dict(hidden=cj["hidden_size"], moe_inter=cj["moe_intermediate_size"],
                         n_experts=E, topk=cj["num_experts_per_tok"],
                         swiglu_limit=int(cj["swiglu_limit"]),
@@ -1043,5 +1058,19 @@ def decoder_from_checkpoint(ckpt_dir, max_context, device="cuda", hc_exact=False
             wkv=dev(t[a + "wkv.weight"]), wkv_s=dev(t[a + "wkv.scale"]),
             kv_norm=dev(t[a + "kv_norm.weight"]),
             wo_a_fp8=dev(t[a + "wo_a.weight"]), wo_a_fp8_s=dev(t[a + "wo_a.scale"]),
-            wo_b=dev(t[a + "wo_b.weight"]), wo_b_s=dev(t[a + "wo_b.scale"]), moe=moe))
+            wo_b=dev(t[a + "wo_b.weight"]), wo_b_s=dev(t[a + "wo_b.scale"]), moe=moe,
+            compress_ratio=ratios[L]))
+        if ratios[L]:
+            cp, ip = a + "compressor.", a + "indexer."
+            layers[-1].update(comp_wkv=dev(t[cp + "wkv.weight"]),
+                              comp_wgate=dev(t[cp + "wgate.weight"]),
+                              comp_ape=dev(t[cp + "ape"]), comp_norm=dev(t[cp + "norm.weight"]))
+            if ratios[L] == 4:
+                layers[-1].update(idx_wq_b=dev(t[ip + "wq_b.weight"]),
+                                  idx_wq_b_s=dev(t[ip + "wq_b.scale"]),
+                                  idx_weights_proj=dev(t[ip + "weights_proj.weight"]),
+                                  idx_comp_wkv=dev(t[ip + "compressor.wkv.weight"]),
+                                  idx_comp_wgate=dev(t[ip + "compressor.wgate.weight"]),
+                                  idx_ape=dev(t[ip + "compressor.ape"]),
+                                  idx_comp_norm=dev(t[ip + "compressor.norm.weight"]))
     return Decoder(cfg, model, layers)

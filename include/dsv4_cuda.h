@@ -497,9 +497,10 @@ int dsv4cuda_kv_copy_rows(const dsv4cuda_kv_cache *cache, const long long *src_r
 /* ---------------------------------------------------------------------
  * Whole-model decode on the device: dsv4_forward_token
  * (src/dsv4/dsv4_model.c:8388, public API include/dsv4/dsv4.h:161) with
- * every weight resident in HBM, for layers of compress ratio 0 (the
- * sliding-window attention; the compressor and indexer of ratio-4/128
- * layers are not part of this path). One call per token: embedding, per
+ * every weight resident in HBM. Layers of compress ratio 0 attend to the
+ * sliding window; ratio-4 and ratio-128 layers also run the compressor
+ * (and for ratio 4 the indexer and its top-k) and attend to the window plus
+ * the selected compressed rows, in the reference's order. One call per token: embedding, per
  * layer hyper-connection pre, RMSNorm, attention (FP8 projections, norms,
  * RoPE, FP8 latent ring, sparse attention over the window, inverse RoPE,
  * grouped wo_a, wo_b), HC post, HC pre, RMSNorm, MoE layer, HC post; then
@@ -518,6 +519,13 @@ typedef struct {
      * last-ulp expf differences; 0: the mixes are summed in double in
      * parallel (fast, within the chains' rounding of the reference). */
     int hc_exact;
+    /* Layers of compress ratio 4 / 128 (dsv4cuda_layer_weights.compress_ratio):
+     * the indexer's heads, head dim and top-k, and the RoPE of compressed
+     * layers (YaRN, rope_freqs_fill src/dsv4/dsv4_model.c:1475-1503). Unused
+     * when every layer has ratio 0. */
+    int index_heads, index_dim, index_topk;
+    float compress_rope_theta, rope_factor, beta_fast, beta_slow;
+    int original_position;
 } dsv4cuda_decoder_config;
 
 typedef struct {
@@ -544,6 +552,19 @@ typedef struct {
                                               as the reference does at load (:1927-1936) */
     const uint8_t *wo_b, *wo_b_s;     /* FP8 [hidden][o_groups*o_lora] */
     dsv4cuda_moe_weights moe;         /* expert-major routed FP4 + shared expert */
+    /* compress ratio 0 (sliding window only), 4 (compressor with overlapping
+     * blocks + indexer top-k) or 128 (compressor, every compressed row
+     * attended): compressor_update / indexer_forward, src/dsv4/dsv4_model.c:
+     * 5100-5236, :5685-5760. coff = 2 for ratio 4, else 1. */
+    int compress_ratio;
+    const uint16_t *comp_wkv, *comp_wgate;      /* BF16 [coff*head_dim][hidden] */
+    const float *comp_ape;                      /* [ratio][coff*head_dim] */
+    const uint16_t *comp_norm;                  /* [head_dim] BF16 */
+    const uint8_t *idx_wq_b, *idx_wq_b_s;       /* FP8 [index_heads*index_dim][q_lora] */
+    const uint16_t *idx_weights_proj;           /* BF16 [index_heads][hidden] */
+    const uint16_t *idx_comp_wkv, *idx_comp_wgate;  /* BF16 [2*index_dim][hidden] */
+    const float *idx_ape;                       /* [4][2*index_dim] */
+    const uint16_t *idx_comp_norm;              /* [index_dim] BF16 */
 } dsv4cuda_layer_weights;
 
 typedef struct dsv4cuda_decoder dsv4cuda_decoder;

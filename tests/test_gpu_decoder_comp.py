@@ -1,0 +1,77 @@
+"""The device decoder on DeepSeek-V4 compressed-attention layers (compress
+ratio 4 with the indexer, ratio 128) against the reference engine's
+dsv4_prefill + dsv4_forward_token on the same checkpoint.
+
+The checkpoint is T1 (tests/golden/make_tiny_t1.py, random weights) with
+layer 0 of ratio 4 (compressor with overlapping blocks, indexer: 4 heads x
+32 dims, top-8 of the compressed rows) and layer 1 of ratio 128 (every
+compressed row attended), a 16-position window and a latent of 80 dims. A
+prompt of 140 tokens makes the ratio-4 layer compress 35 blocks (so the
+indexer's top-k selects) and the ratio-128 layer one block; then 8 greedy
+steps. The reference runs its own host code (oracle/_ref/tiny_decode); the
+device decodes token by token, fed the reference's tokens.
+
+Exact mode (hc_exact = 1): the compressor (projections, per-channel
+softmax pooling, RMSNorm, YaRN RoPE at the block start, FP8 / Hadamard +
+FP4 QAT), the indexer (its query, scores, ordered top-k) and the attention
+over the window plus the selected rows follow the reference's operations in
+its order, so every step's logits must be bit-identical. Fast mode (the HC
+mixes summed in double, the only difference): within 5e-2 relative L2 per
+step - these random weights make the HC split sensitive, as on the
+config-5-shaped layer of test_gpu_decoder.py - and greedy tokens equal
+where the reference's top-two margin exceeds that.
+"""
+import os
+import sys
+
+import numpy as np
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+sys.path.insert(0, os.path.join(ROOT, "tests"))
+sys.path.insert(0, os.path.join(ROOT, "tests", "golden"))
+
+from test_gpu_decoder import compare_decode, reference_steps  # noqa: E402
+
+pytestmark = pytest.mark.gpu
+N_PROMPT, N_GEN = 140, 8
+
+
+@pytest.mark.parametrize("exact", [True, False], ids=["exact", "fast"])
+def test_decoder_compressed_layers_vs_reference(cuda, tmp_path, exact):
+    import make_tiny_t1
+    cfg = dict(make_tiny_t1.CFG, ratios=[4, 128], head_dim=80)
+    ckpt = make_tiny_t1.write(str(tmp_path / "t1c"), seed=5, c=cfg)
+    ids = make_tiny_t1.prompt_ids(seed=5, n=N_PROMPT)
+    want = reference_steps(ckpt, ids, N_GEN)
+    dec = cuda.decoder_from_checkpoint(ckpt, max_context=N_PROMPT + N_GEN + 8, hc_exact=exact)
+    tol = 0.0 if exact else 5e-2
+    try:
+        same, worst, agree, near = compare_decode(dec, ids, want, tol)
+        print(f"decoder T1 ratios 4/128 ({'exact' if exact else 'fast'}): {same}/{N_GEN} steps "
+              f"bit-identical, worst rel L2 {worst:.2e}, greedy {agree}/{N_GEN}, near {near}")
+        if exact:
+            assert same == N_GEN and agree == N_GEN
+    finally:
+        dec.close()
+
+
+def test_decoder_compressed_reset_replays(cuda, tmp_path):
+    """dsv4cuda_decoder_reset returns the compressor and indexer state to
+    its start (kv state zeros, scores -inf, no compressed rows): a second
+    pass over the same tokens gives the same logits bit for bit."""
+    import make_tiny_t1
+    cfg = dict(make_tiny_t1.CFG, ratios=[4, 128], head_dim=80)
+    ckpt = make_tiny_t1.write(str(tmp_path / "t1r"), seed=6, c=cfg)
+    ids = make_tiny_t1.prompt_ids(seed=6, n=40)
+    dec = cuda.decoder_from_checkpoint(ckpt, max_context=48)
+    try:
+        first = [dec.forward_token(t, p)[0] for p, t in enumerate(ids)]
+        import torch
+        dec.reset()
+        torch.cuda.synchronize()
+        second = [dec.forward_token(t, p)[0] for p, t in enumerate(ids)]
+        for p, (a, b) in enumerate(zip(first, second)):
+            assert np.array_equal(a.view(np.uint32), b.view(np.uint32)), p
+    finally:
+        dec.close()
