@@ -86,6 +86,9 @@ def parse():
                     help="decode: distinct random-init layer weight sets the 43 layers cycle "
                          "through (each ~3.6 GB; L2 never holds a layer between uses)")
     ap.add_argument("--decode-layers", type=int, default=43)
+    ap.add_argument("--decode-ratios", default="dsv4", choices=["dsv4", "window"],
+                    help="decode: DeepSeek-V4-Flash's compress ratios (two window layers, then "
+                         "ratio 4 / 128 alternating) or every layer a sliding-window layer")
     ap.add_argument("--attn-batch", type=int, default=32)
     ap.add_argument("--attn-ctx", type=int, default=32768)
     ap.add_argument("--no-spec", action="store_true",
@@ -331,7 +334,7 @@ def run_reference_arm(args, rank, world):
     if rank != 0:
         return
     if args.workload == "decode":
-        res = cpu_reference_decode(args.decode_layers)
+        res = cpu_reference_decode(args.decode_layers, kinds_mode=args.decode_ratios)
         if res is None:
             print(json.dumps({"impl": "reference", "unavailable":
                               "oracle/_ref/ref_decode_bench was not built (reference sources absent)"}))
@@ -984,7 +987,15 @@ def main_attn(args, rank, world, local):
 # ------------------------------------------ config 5: whole-model decode ----
 C5 = dict(hidden=4096, vocab=129280, n_heads=64, head_dim=512, rope_dim=64, q_lora=1024,
           o_groups=8, o_lora=1024, window=128, hc_mult=4, hc_iters=20, rms_eps=1e-6,
-          hc_eps=1e-6, rope_theta=10000.0, experts=256, topk=6, inter=2048)
+          hc_eps=1e-6, rope_theta=10000.0, experts=256, topk=6, inter=2048,
+          index_heads=64, index_dim=128, index_topk=512, compress_rope_theta=160000.0,
+          rope_factor=16.0, beta_fast=32.0, beta_slow=1.0, original_position=65536)
+
+
+def c5_ratios(n_layers):
+    """DeepSeek-V4-Flash's compress ratios: two sliding-window layers, then
+    ratio 4 and ratio 128 alternating (21 and 20 of the 43 layers)."""
+    return [0 if i < 2 else (4 if (i - 2) % 2 == 0 else 128) for i in range(n_layers)]
 DECODE_METRIC = ("decode tok/s, batch 1, speculation off (config 5: DSV4-Flash shapes, "
                  "43 layers, 256+1 experts top-6, FP4 experts / FP8 attention)")
 
@@ -996,24 +1007,32 @@ def decode_config(args, world):
             "layers": n_layers, "hidden": c["hidden"], "vocab": c["vocab"],
             "heads": c["n_heads"], "head_dim": c["head_dim"],
             "experts": c["experts"], "topk": c["topk"], "moe_inter": c["inter"],
-            "attention": "sliding window of 128 on every layer (compress ratio "
-                         "0; the compressor/indexer path is not built)",
+            "attention": ("DeepSeek-V4-Flash compress ratios: layers 0-1 sliding window "
+                          "of 128, then ratio 4 (compressor + indexer, 64 heads x 128, "
+                          "top-512 of the compressed rows) and ratio 128 alternating"
+                          if args.decode_ratios == "dsv4" else
+                          "sliding window of 128 on every layer (compress ratio 0)"),
             "prompt_positions": 2048,
-            "weight_sets": f"{n_layers} layers cycle {args.decode_sets} distinct "
-                           "random-init layer weight sets of ~3.6 GB; every token "
-                           "reads a whole model's bytes, none of it L2-resident",
+            "context": "a 2048-token greedy prompt decoded through the same graph before "
+                       "timing (rings, compressor state and compressed rows in place)",
+            "weight_sets": f"{n_layers} layers cycle distinct random-init layer weight sets "
+                           "of ~3.6 GB (two per kind of layer); every token reads a whole "
+                           "model's bytes, none of it L2-resident",
             "graph": "one CUDA graph per token (argmax fed back on the device)",
             "parallelism": (f"ep{world} (token-parallel: one sequence per GPU, "
                             "experts split, slots exchanged over peer memory)"
                             if world > 1 else "ep1")}
 
 
-def decode_bytes_per_token(c, n_layers):
+def decode_bytes_per_token(c, n_layers, context=2048):
     """Algorithmic HBM bytes one greedy token reads: every layer's dense
     weights (FP8 projections with their [128x128] scales, BF16 wo_a, the HC
     mixes, the BF16 router), the shared expert, topk routed FP4 experts
-    (codes + per-32 scales), the latent ring, then the HC head and the BF16
-    vocab head."""
+    (codes + per-32 scales), the latent ring; a compressed layer's
+    compressor projections (and for ratio 4 the indexer's query, weights and
+    compressor projections, its compressed keys at `context` and the
+    selected latent rows; for ratio 128 every compressed row); then the HC
+    head and the BF16 vocab head."""
     H, I, hd, nh = c["hidden"], c["inter"], c["head_dim"], c["n_heads"]
     fp8 = lambda r, k: r * k + ((r + 127) // 128) * ((k + 127) // 128)  # noqa: E731
     mult = c["hc_mult"]
@@ -1024,10 +1043,17 @@ def decode_bytes_per_token(c, n_layers):
              3 * fp8(I, H) + c["window"] * 584)
     expert = 3 * (I * H // 2 + I * H // 32)
     per_layer = dense + c["topk"] * expert
-    return n_layers * per_layer + c["vocab"] * H * 2 + mult * mult * H * 4 + H * 2
+    ih, idim = c["index_heads"], c["index_dim"]
+    comp = {0: 0,
+            4: 2 * (2 * hd) * H * 2 + fp8(ih * idim, c["q_lora"]) + ih * H * 2 +
+            2 * (2 * idim) * H * 2 + (context // 4) * idim * 4 +
+            min(c["index_topk"], context // 4) * 584,
+            128: 2 * hd * H * 2 + (context // 128) * 584}
+    extra = sum(comp[r] for r in c5_ratios(n_layers))
+    return n_layers * per_layer + extra + c["vocab"] * H * 2 + mult * mult * H * 4 + H * 2
 
 
-def make_decode_set(torch, seed, dev, c, expert_range=None):
+def make_decode_set(torch, seed, dev, c, expert_range=None, ratio=0):
     """One random-init layer weight set at config-5 shapes (distributions as
     config 2: FP4 codes uniform, E8M0 lognormal(0, 0.5) rounded to powers of
     two, FP8 codes uniform over the finite values, BF16 N(0, 0.02), RMSNorm
@@ -1071,7 +1097,18 @@ def make_decode_set(torch, seed, dev, c, expert_range=None):
                s3=e8m0(n, I, H // 32), w2=u8(n, H, I // 2), s2=e8m0(n, H, I // 32),
                shared=dict(fp8=True, **sh))
     ones3 = torch.ones(3, device=dev)
-    return dict(attn_norm=bf16(H, mean=1.0), ffn_norm=bf16(H, mean=1.0),
+    comp = {"compress_ratio": ratio}
+    if ratio:
+        coff = 2 if ratio == 4 else 1
+        comp.update(comp_wkv=bf16(coff * hd, H), comp_wgate=bf16(coff * hd, H),
+                    comp_ape=f32(ratio, coff * hd), comp_norm=bf16(hd, mean=1.0))
+        if ratio == 4:
+            ih, idim = c["index_heads"], c["index_dim"]
+            iw, iws = fp8(ih * idim, c["q_lora"])
+            comp.update(idx_wq_b=iw, idx_wq_b_s=iws, idx_weights_proj=bf16(ih, H),
+                        idx_comp_wkv=bf16(2 * idim, H), idx_comp_wgate=bf16(2 * idim, H),
+                        idx_ape=f32(4, 2 * idim), idx_comp_norm=bf16(idim, mean=1.0))
+    return dict(**comp, attn_norm=bf16(H, mean=1.0), ffn_norm=bf16(H, mean=1.0),
                 hc_attn_fn=f32(mix, mult * H), hc_attn_scale=ones3, hc_attn_base=f32(mix),
                 hc_ffn_fn=f32(mix, mult * H), hc_ffn_scale=ones3.clone(), hc_ffn_base=f32(mix),
                 attn_sink=f32(nh), wq_a=wq_a, wq_a_s=wq_a_s, q_norm=bf16(c["q_lora"], mean=1.0),
@@ -1080,15 +1117,38 @@ def make_decode_set(torch, seed, dev, c, expert_range=None):
                 wo_b=wo_b, wo_b_s=wo_b_s, moe=moe)
 
 
-def cpu_reference_decode(n_layers=43, threads=None, warm=8, timed=8):
+def cpu_reference_decode(n_layers=43, threads=None, warm=8, timed=8, kinds_mode="dsv4"):
+    """Per kind of layer in the model (compress ratio 0 / 4 / 128), the
+    reference's decode of a one-layer checkpoint of that kind
+    (cpu_reference_decode_one); per token = sum over the model's layers of
+    their kind's layer time + the vocab head and the embedding. Returns
+    (tok/s, threads, sample description) or None."""
+    ratios = c5_ratios(n_layers) if kinds_mode == "dsv4" else [0] * n_layers
+    per_kind, head_emb, samples, cores = {}, None, [], None
+    for r in sorted(set(ratios)):
+        res = cpu_reference_decode_one(threads, warm, timed, ratio=r)
+        if res is None:
+            return None
+        layer, he, cores, sample = res
+        per_kind[r] = layer
+        head_emb = he
+        samples.append(f"ratio {r}: {layer * 1e3:.1f} ms per layer")
+    per_token = sum(per_kind[r] for r in ratios) + head_emb
+    return 1.0 / per_token, cores, (
+        f"dsv4_forward_token on one-layer config-5 random checkpoints in RAM (one per kind of "
+        f"layer), {timed} timed tokens after {warm} warm-up from position 0, {cores} thread(s): "
+        f"{'; '.join(samples)}; {head_emb * 1e3:.1f} ms head + embedding; per token extrapolated "
+        f"to the {n_layers}-layer pattern ({per_token:.2f} s)")
+
+
+def cpu_reference_decode_one(threads=None, warm=8, timed=8, ratio=0):
     """The reference engine's own decode step on the host cores
     (oracle/_ref/ref_decode_bench: dsv4_forward_token over a config-5-shaped
-    random checkpoint of ONE layer, written to RAM). A 43-layer checkpoint
-    (~156 GB) does not fit the host, so the per-token time is extrapolated:
-    43 x (one layer) + the vocab head + the embedding, the head and the
-    embedding split off with the engine's own profile counters. Returns
-    (tok/s, threads, sample description) or None when the reference was not
-    built here."""
+    random checkpoint of ONE layer of compress ratio `ratio`, written to
+    RAM; a 43-layer checkpoint, ~156 GB, does not fit the host). Returns
+    (seconds per layer, seconds of head + embedding per token, threads,
+    None) - the head and the embedding split off with the engine's own
+    profile counters - or None when the reference was not built here."""
     import shutil
     import tempfile
     exe = os.path.join(ROOT, "oracle", "_ref", "ref_decode_bench")
@@ -1100,7 +1160,7 @@ def cpu_reference_decode(n_layers=43, threads=None, warm=8, timed=8):
     base = "/dev/shm" if os.path.isdir("/dev/shm") else None
     d = tempfile.mkdtemp(prefix="dsv4_c5_", dir=base)
     try:
-        random_checkpoint.write(d, 1)
+        random_checkpoint.write(d, 1, c=dict(random_checkpoint.CONFIG5, ratios=[ratio]))
         r = subprocess.run([exe, d, str(warm), str(timed), str(threads)], capture_output=True,
                            text=True, timeout=1800)
         line = [ln for ln in r.stdout.splitlines() if ln.startswith("RESULT")]
@@ -1108,13 +1168,7 @@ def cpu_reference_decode(n_layers=43, threads=None, warm=8, timed=8):
             raise RuntimeError(r.stderr[-500:])
         f = line[-1].split()
         tok, total, head, emb = int(f[4]), float(f[6]), float(f[8]), float(f[10])
-        layer = (total - head - emb) / tok
-        per_token = n_layers * layer + (head + emb) / tok
-        return 1.0 / per_token, threads, (
-            f"dsv4_forward_token on a 1-layer config-5 random checkpoint in RAM, {tok} timed "
-            f"tokens after {warm} warm-up, {threads} thread(s): {layer * 1e3:.1f} ms per layer, "
-            f"{head / tok * 1e3:.1f} ms head; per token extrapolated to {n_layers} layers "
-            f"({per_token:.2f} s)")
+        return (total - head - emb) / tok, (head + emb) / tok, threads, None
     finally:
         shutil.rmtree(d, ignore_errors=True)
 
@@ -1142,7 +1196,19 @@ def main_decode(args, rank, world, local):
     n_layers = args.decode_layers
     ep = world > 1
     erange = (rank * c["experts"] // world, (rank + 1) * c["experts"] // world) if ep else None
-    sets = [make_decode_set(torch, 500 + i, dev, c, erange) for i in range(args.decode_sets)]
+    # distinct random-init layer weight sets per kind of layer, cycled so that
+    # consecutive layers never share weights
+    ratios = c5_ratios(n_layers) if args.decode_ratios == "dsv4" else [0] * n_layers
+    kinds = sorted(set(ratios))
+    per_kind = max(2, args.decode_sets // max(1, len(kinds)))
+    sets_by = {r: [make_decode_set(torch, 500 + 10 * r + i, dev, c, erange, ratio=r)
+                   for i in range(per_kind)] for r in kinds}
+    sets = [st_ for r in kinds for st_ in sets_by[r]]
+    seen = {r: 0 for r in kinds}
+    layers = []
+    for r in ratios:
+        layers.append(sets_by[r][seen[r] % per_kind])
+        seen[r] += 1
     g = torch.Generator(device=dev)
     g.manual_seed(7)
     model = dict(embed=(torch.randn(c["vocab"], c["hidden"], device=dev, generator=g) * 0.02)
@@ -1164,12 +1230,15 @@ def main_decode(args, rank, world, local):
                o_groups=c["o_groups"], o_lora=c["o_lora"], window=c["window"],
                hc_mult=c["hc_mult"], hc_iters=c["hc_iters"], rms_eps=c["rms_eps"],
                hc_eps=c["hc_eps"], rope_theta=c["rope_theta"],
-               max_context=prompt + gen + args.warmup + n_e2e + 16 +
+               max_context=prompt + 2 * (gen + args.warmup) + n_e2e + 32 +
                (spec_steps + spec_warm + 1) * args.spec_rows,
+               index_heads=c["index_heads"], index_dim=c["index_dim"],
+               index_topk=c["index_topk"], compress_rope_theta=c["compress_rope_theta"],
+               rope_factor=c["rope_factor"], beta_fast=c["beta_fast"], beta_slow=c["beta_slow"],
+               original_position=c["original_position"],
                moe=dict(hidden=c["hidden"], moe_inter=c["inter"], n_experts=c["experts"],
                         topk=c["topk"], swiglu_limit=10, route_scale=1.5,
                         shared_kind=dsv4cuda.SHARED_FP8, hash_vocab=0))
-    layers = [sets[i % len(sets)] for i in range(n_layers)]
     dec = dsv4cuda.Decoder(cfg, model, layers)
     ipc_own, ipc_peers, moe_ep = [], [], []
     if ep:
@@ -1195,11 +1264,11 @@ def main_decode(args, rank, world, local):
                     addrs.append(a_)
             L.ep_attach(rank, world, addrs)
         dist.barrier()
-        dec.set_moe_layers([moe_ep[i % len(moe_ep)] for i in range(n_layers)])
+        dec.set_moe_layers([moe_ep[sets.index(L)] for L in layers])
     lib = dsv4cuda.lib
     h = dec.handle
     _, _, _, am_slot = dec.slots()
-    pos = torch.full((1,), prompt - args.warmup - 1, dtype=torch.int32, device=dev)
+    pos = torch.full((1,), 0, dtype=torch.int32, device=dev)
     tok = torch.full((1,), 1, dtype=torch.int32, device=dev)
     stream = torch.cuda.Stream(device=dev)
     with torch.cuda.stream(stream):  # one eager step: its argmax seeds the greedy chain
@@ -1213,9 +1282,13 @@ def main_decode(args, rank, world, local):
                                             C.c_void_p(cs.cuda_stream)) != 0:
             raise RuntimeError(lib.dsv4cuda_decoder_last_error().decode())
         pos.add_(1)
+    # the context: a greedy prompt through the same graph up to position
+    # prompt - warmup (every ring, compressor state, compressed row and
+    # indexer key of a 2048-token context is in place), then the warm-up
     with torch.cuda.stream(stream):
-        for _ in range(args.warmup):
+        for _ in range(prompt - 1):
             graph.replay()
+    torch.cuda.synchronize()
     torch.cuda.synchronize()
     clocks = ClockSampler(local)
     clocks.start()
@@ -1268,6 +1341,7 @@ def main_decode(args, rank, world, local):
     # experts and the slots are exchanged (a second set of EP layers with
     # their own exchange buffers)
     batch1 = None
+    p_next = (p0 + 2 + n_e2e) if e2e is not None else int(pos.item())
     rep_own, rep_peers, moe_rep = [], [], []
     if ep and not args.no_batch1:
         moe_rep = [dsv4cuda.MoeLayer(st_["moe"], max_tokens=world, device=True,
@@ -1290,10 +1364,11 @@ def main_decode(args, rank, world, local):
                     addrs.append(a_)
             L.ep_attach(rank, world, addrs)
         dist.barrier()
-        dec.set_moe_layers([moe_rep[i % len(moe_rep)] for i in range(n_layers)])
+        dec.set_moe_layers([moe_rep[sets.index(L)] for L in layers])
         dec.set_ep_replicated(True)
-        dec.reset(stream.cuda_stream)
-        pos.fill_(prompt - args.warmup - 1)
+        # every rank already holds the same context (same weights, the same
+        # greedy tokens); continue after the positions used so far
+        pos.fill_(p_next)
         tok.fill_(1)
         torch.cuda.synchronize()
         with torch.cuda.stream(stream):
@@ -1344,23 +1419,56 @@ def main_decode(args, rank, world, local):
     spec = None
     if spec_steps:
         n_rows = args.spec_rows
-        p_now = int(pos.item()) if e2e is None else p0 + 2 + n_e2e
-        _, pend = dec.read()  # the last step's greedy token is the pending row
+        # the batched verify runs sliding-window layers; with compressed
+        # layers in the model it is measured on a decoder of the same shapes
+        # whose layers are all window layers (the window weight sets), and
+        # compared with that decoder's own one-token step
+        window_only = not any(ratios)
+        sdec, ms_ref = dec, ms_tok
+        if not window_only:
+            wsets = sets_by.get(0) or [make_decode_set(torch, 900, dev, c, erange)]
+            sdec = dsv4cuda.Decoder(cfg, model, [wsets[i % len(wsets)] for i in range(n_layers)])
+            p_now, pend = prompt, 1
+            wtok = torch.full((1,), 1, dtype=torch.int32, device=dev)
+            wpos = torch.full((1,), prompt, dtype=torch.int32, device=dev)
+            with torch.cuda.stream(stream):
+                sdec.step_device(wtok, wpos, stream.cuda_stream)
+            stream.synchronize()
+            wgraph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(wgraph, stream=stream):
+                sdec.step_device(wtok, wpos, torch.cuda.current_stream().cuda_stream)
+            with torch.cuda.stream(stream):
+                for _ in range(args.warmup):
+                    wgraph.replay()
+            torch.cuda.synchronize()
+            w0 = torch.cuda.Event(enable_timing=True)
+            w1 = torch.cuda.Event(enable_timing=True)
+            with torch.cuda.stream(stream):
+                w0.record(stream)
+                for _ in range(spec_steps):
+                    wgraph.replay()
+                w1.record(stream)
+            torch.cuda.synchronize()
+            ms_ref = w0.elapsed_time(w1) / spec_steps
+            wgraph.reset()
+        else:
+            p_now = p_next + (2 * args.steps + args.warmup + 2 if batch1 is not None else 0)
+            _, pend = dec.read()  # the last step's greedy token is the pending row
         first = [pend] + [1] * (n_rows - 1)
-        dec.verify(first, p_now)  # eager: fills the verify slots, one-time set-up
-        dec.accept_greedy(n_rows, stream.cuda_stream)
+        sdec.verify(first, p_now)  # eager: fills the verify slots, one-time set-up
+        sdec.accept_greedy(n_rows, stream.cuda_stream)
         stream.synchronize()
         sgraph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(sgraph, stream=stream):
             cs = torch.cuda.current_stream().cuda_stream
-            dec.draft_random(n_rows, cs)
-            dec.verify_device(n_rows, cs)
-            dec.accept_greedy(n_rows, cs)
+            sdec.draft_random(n_rows, cs)
+            sdec.verify_device(n_rows, cs)
+            sdec.accept_greedy(n_rows, cs)
         with torch.cuda.stream(stream):
             for _ in range(spec_warm):
                 sgraph.replay()
         torch.cuda.synchronize()
-        st0 = dec.verify_stats()
+        st0 = sdec.verify_stats()
         clocks_s = ClockSampler(local)
         clocks_s.start()
         time.sleep(0.2)
@@ -1374,9 +1482,11 @@ def main_decode(args, rank, world, local):
         torch.cuda.synchronize()
         sms = e0.elapsed_time(e1)
         clk_s = clocks_s.stop()
-        st1 = dec.verify_stats()
+        st1 = sdec.verify_stats()
         emitted, accepted, vsteps = (st1[i] - st0[i] for i in range(3))
         sgraph.reset()
+        if sdec is not dec:
+            sdec.close()
         spec = {"metric": "decode tok/s, batch 1, speculation on (config 4 form: pending token "
                           f"+ {n_rows - 1} uniform random drafts per verify step, greedy "
                           "acceptance, config 5 model)",
@@ -1386,15 +1496,20 @@ def main_decode(args, rank, world, local):
                 "drafts_accepted_per_step": accepted / vsteps,
                 "verified_rows_per_s": n_rows * vsteps / (sms * 1e-3),
                 "tok_s_if_every_draft_accepted": n_rows * vsteps / (sms * 1e-3),
-                "verify_vs_decode_step_cost": (sms / vsteps) / ms_tok,
-                "break_even_accepted_drafts": (sms / vsteps) / ms_tok - 1.0,
+                "decode_step_ms_same_layers": ms_ref,
+                "verify_vs_decode_step_cost": (sms / vsteps) / ms_ref,
+                "break_even_accepted_drafts": (sms / vsteps) / ms_ref - 1.0,
+                "layers": ("the benchmark's layers" if window_only else
+                           "every layer a sliding-window layer (the batched verify covers "
+                           "compress-ratio-0 layers); the costs compare with that decoder's "
+                           "own one-token step (decode_step_ms_same_layers)"),
                 "clocks": clk_s,
                 "note": "uniform random drafts are almost never accepted, so this is the "
                         "floor; a drafter's gain is tokens_per_step x this step rate"}
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
         try:
-            res = cpu_reference_decode(n_layers)
+            res = cpu_reference_decode(n_layers, kinds_mode=args.decode_ratios)
             if res:
                 cpu = {"value": res[0], "unit": "tok/s", "cores": res[1], "kind": "reference",
                        "sample": res[2], "extrapolated": True}

@@ -1294,10 +1294,10 @@ __global__ void __launch_bounds__(kWhThreads) win_head_kernel(const WinAttnArgs 
 // twice - the scores (every key's dot in dimension order) for the softmax
 // over all keys, then the values (every dimension pair's chain in key order,
 // carried across chunks) - with the head's q kept in shared memory.
-constexpr int kWideKeys = 64;
+constexpr int kWideKeys = 96;  // two buffers of 96 rows x 1040 B fit with d = 512
 
 __host__ __device__ inline size_t wide_head_smem(int n, int d) {
-  return static_cast<size_t>(kWideKeys) * (d + 8) * 2 + static_cast<size_t>(d) * 4 +
+  return static_cast<size_t>(2) * kWideKeys * (d + 8) * 2 + static_cast<size_t>(d) * 4 +
          static_cast<size_t>(3) * n * 4 + 16;
 }
 
@@ -1305,20 +1305,22 @@ __global__ void __launch_bounds__(kWhThreads) wide_head_kernel(const WinAttnArgs
                                                                const uint16_t* win,
                                                                unsigned int* err) {
   extern __shared__ __align__(16) unsigned char wsm[];
-  __shared__ uint64_t bar;
+  __shared__ uint64_t bars[2];
   __shared__ float den_s;
   pdl_trigger();
   const int h = blockIdx.x;
   const int n = a.n, d = a.d, ldk = d + 8;
-  uint16_t* ks = reinterpret_cast<uint16_t*>(wsm);                                  // [KC][d + 8]
-  float* qs = reinterpret_cast<float*>(wsm + static_cast<size_t>(kWideKeys) * ldk * 2);  // [d]
-  float* ss = qs + d;                                                                // [n]
-  float* ws = ss + n;                                                                // [n]
-  int* sidx = reinterpret_cast<int*>(ws + n);                                        // [n]
+  uint16_t* kbuf[2] = {reinterpret_cast<uint16_t*>(wsm),
+                       reinterpret_cast<uint16_t*>(wsm) + static_cast<size_t>(kWideKeys) * ldk};
+  float* qs = reinterpret_cast<float*>(wsm + static_cast<size_t>(2) * kWideKeys * ldk * 2);  // [d]
+  float* ss = qs + d;                                                                      // [n]
+  float* ws = ss + n;                                                                      // [n]
+  int* sidx = reinterpret_cast<int*>(ws + n);                                              // [n]
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int nth = blockDim.x;
   if (tid == 0) {
-    mbar_init(&bar, 1);
+    mbar_init(&bars[0], 1);
+    mbar_init(&bars[1], 1);
     mbar_fence_init();
   }
   __syncthreads();
@@ -1326,6 +1328,19 @@ __global__ void __launch_bounds__(kWhThreads) wide_head_kernel(const WinAttnArgs
   for (int t = tid; t < n; t += nth) sidx[t] = a.idx[t];
   for (int i = tid; i < d / 4; i += nth)
     reinterpret_cast<float4*>(qs)[i] = reinterpret_cast<const float4*>(a.q + static_cast<size_t>(h) * d)[i];
+  const uint32_t row_bytes = static_cast<uint32_t>(d) * 2;
+  const int nch = (n + kWideKeys - 1) / kWideKeys;
+  const int total = 2 * nch;  // every chunk twice: scores, then values
+  // chunk g (of key chunk g % nch) into buffer g & 1; every thread calls it
+  auto issue = [&](int g) {
+    const int c0 = (g % nch) * kWideKeys, nk = min(kWideKeys, n - c0), bi = g & 1;
+    if (tid == 0) mbar_arrive_expect_tx(&bars[bi], row_bytes * static_cast<uint32_t>(nk));
+    __syncthreads();
+    for (int t = tid; t < nk; t += nth)
+      bulk_g2s(kbuf[bi] + static_cast<size_t>(t) * ldk, win + static_cast<size_t>(c0 + t) * d,
+               row_bytes, &bars[bi]);
+  };
+  issue(0);
   if (a.q_raw) {
     __shared__ double qred[32];
     __syncthreads();
@@ -1343,81 +1358,76 @@ __global__ void __launch_bounds__(kWhThreads) wide_head_kernel(const WinAttnArgs
       qs[start + 2 * i + 1] = bf16_round(__fadd_rn(__fmul_rn(x0, sn), __fmul_rn(x1, c)));
     }
   }
-  const uint32_t row_bytes = static_cast<uint32_t>(d) * 2;
-  uint32_t phase = 0;
-  // one chunk of staged rows into ks; false (every thread) when the copy
-  // did not land within the bounded wait
-  auto load_chunk = [&](int c0, int nk) -> bool {
-    __syncthreads();  // every thread is done with the previous chunk
-    if (tid == 0) mbar_arrive_expect_tx(&bar, row_bytes * static_cast<uint32_t>(nk));
-    __syncthreads();
-    for (int t = tid; t < nk; t += nth)
-      bulk_g2s(ks + static_cast<size_t>(t) * ldk, win + static_cast<size_t>(c0 + t) * d, row_bytes, &bar);
-    bool ok = mbar_wait(&bar, phase, err);
-    if (!__syncthreads_and(ok)) {
-      if (!ok) mbar_wait(&bar, phase, err);  // the copies in flight land before the CTA exits
-      return false;
-    }
-    phase ^= 1u;
-    return true;
-  };
-  for (int c0 = 0; c0 < n; c0 += kWideKeys) {
-    const int nk = min(kWideKeys, n - c0);
-    if (!load_chunk(c0, nk)) return;
-    for (int t = tid; t < nk; t += nth) {
-      const int r = sidx[c0 + t];
-      float st = -INFINITY;
-      if (r >= 0 && r < a.cache.rows) {
-        const uint16_t* kr = ks + static_cast<size_t>(t) * ldk;
-        float dot = 0.0f;
-#pragma unroll 4
-        for (int i = 0; i < d; i += 8) {
-          float kf[8];
-          bf16x8_to_f32(*reinterpret_cast<const uint4*>(kr + i), kf);
-          const float4 q0 = *reinterpret_cast<const float4*>(qs + i);
-          const float4 q1 = *reinterpret_cast<const float4*>(qs + i + 4);
-          dot = fmaf(q0.x, kf[0], dot);
-          dot = fmaf(q0.y, kf[1], dot);
-          dot = fmaf(q0.z, kf[2], dot);
-          dot = fmaf(q0.w, kf[3], dot);
-          dot = fmaf(q1.x, kf[4], dot);
-          dot = fmaf(q1.y, kf[5], dot);
-          dot = fmaf(q1.z, kf[6], dot);
-          dot = fmaf(q1.w, kf[7], dot);
-        }
-        st = __fmul_rn(dot, a.scale);
-      }
-      ss[c0 + t] = st;
-    }
-  }
-  __syncthreads();
-  if (warp == 0) {
-    float mx = -INFINITY;
-    for (int t = lane; t < n; t += 32) mx = fmaxf(mx, ss[t]);
-    mx = warp_max(mx);
-    for (int t = lane; t < n; t += 32) {
-      const float st = ss[t];
-      ws[t] = st != -INFINITY ? expf_r1(st - mx) : 0.0f;
-    }
-    __syncwarp();
-    if (lane == 0) {
-      float sum = expf_r1(a.sink[h] - mx);
-      for (int t = 0; t < n; ++t)
-        if (ss[t] != -INFINITY) sum += ws[t];
-      den_s = sum;
-    }
-    __syncwarp();
-    for (int t = lane; t < n; t += 32) ws[t] = bf16_round(ws[t]);
-  }
-  __syncthreads();
-  const float den = den_s;
   // d / 2 dimension pairs, two per thread (d <= 4 * blockDim.x)
   const int p0 = tid, p1 = tid + nth;
   const bool has0 = p0 < d / 2, has1 = p1 < d / 2;
   float o[2][2] = {{0.f, 0.f}, {0.f, 0.f}};
-  for (int c0 = 0; c0 < n; c0 += kWideKeys) {
-    const int nk = min(kWideKeys, n - c0);
-    if (!load_chunk(c0, nk)) return;
+  float den = 0.0f;
+  for (int g = 0; g < total; ++g) {
+    __syncthreads();  // the buffer issue(g + 1) refills was last read in step g - 1
+    if (g + 1 < total) issue(g + 1);
+    const int bi = g & 1;
+    bool ok = mbar_wait(&bars[bi], static_cast<uint32_t>((g >> 1) & 1), err);
+    if (!__syncthreads_and(ok)) {
+      // the copies in flight land before the CTA exits
+      if (!ok) mbar_wait(&bars[bi], static_cast<uint32_t>((g >> 1) & 1), err);
+      if (g + 1 < total) mbar_wait(&bars[bi ^ 1], static_cast<uint32_t>(((g + 1) >> 1) & 1), err);
+      return;
+    }
+    const uint16_t* ks = kbuf[bi];
+    const int c0 = (g % nch) * kWideKeys, nk = min(kWideKeys, n - c0);
+    if (g < nch) {
+      for (int t = tid; t < nk; t += nth) {
+        const int r = sidx[c0 + t];
+        float st = -INFINITY;
+        if (r >= 0 && r < a.cache.rows) {
+          const uint16_t* kr = ks + static_cast<size_t>(t) * ldk;
+          float dot = 0.0f;
+#pragma unroll 4
+          for (int i = 0; i < d; i += 8) {
+            float kf[8];
+            bf16x8_to_f32(*reinterpret_cast<const uint4*>(kr + i), kf);
+            const float4 q0 = *reinterpret_cast<const float4*>(qs + i);
+            const float4 q1 = *reinterpret_cast<const float4*>(qs + i + 4);
+            dot = fmaf(q0.x, kf[0], dot);
+            dot = fmaf(q0.y, kf[1], dot);
+            dot = fmaf(q0.z, kf[2], dot);
+            dot = fmaf(q0.w, kf[3], dot);
+            dot = fmaf(q1.x, kf[4], dot);
+            dot = fmaf(q1.y, kf[5], dot);
+            dot = fmaf(q1.z, kf[6], dot);
+            dot = fmaf(q1.w, kf[7], dot);
+          }
+          st = __fmul_rn(dot, a.scale);
+        }
+        ss[c0 + t] = st;
+      }
+      continue;
+    }
+    if (g == nch) {
+      // every score is in: the softmax over all keys
+      __syncthreads();
+      if (warp == 0) {
+        float mx = -INFINITY;
+        for (int t = lane; t < n; t += 32) mx = fmaxf(mx, ss[t]);
+        mx = warp_max(mx);
+        for (int t = lane; t < n; t += 32) {
+          const float st = ss[t];
+          ws[t] = st != -INFINITY ? expf_r1(st - mx) : 0.0f;
+        }
+        __syncwarp();
+        if (lane == 0) {
+          float sum = expf_r1(a.sink[h] - mx);
+          for (int t = 0; t < n; ++t)
+            if (ss[t] != -INFINITY) sum += ws[t];
+          den_s = sum;
+        }
+        __syncwarp();
+        for (int t = lane; t < n; t += 32) ws[t] = bf16_round(ws[t]);
+      }
+      __syncthreads();
+      den = den_s;
+    }
     for (int t = 0; t < nk; ++t) {
       const float wt = ws[c0 + t];
       const uint16_t* vr = ks + static_cast<size_t>(t) * ldk;
@@ -1772,7 +1782,10 @@ __global__ void idx_score_kernel(const float* q, const float* keys, const float*
   if (h == 0 && tl < kIdxT && t < nt) {
     const float s = __fmul_rn(1.0f / sqrtf(static_cast<float>(id)), 1.0f / sqrtf(static_cast<float>(ih)));
     float acc = 0.0f;
-    for (int k = 0; k < ih; ++k) acc = fmaf(dots[tl * ih + k], bf16_round(__fmul_rn(wproj[k], s)), acc);
+    // wproj: the BF16 GEMV's fp32 sums; the reference rounds them to BF16
+    // (round_out = 1) before the scale
+    for (int k = 0; k < ih; ++k)
+      acc = fmaf(dots[tl * ih + k], bf16_round(__fmul_rn(bf16_round(wproj[k]), s)), acc);
     score[t] = acc;
   }
 }
@@ -1914,6 +1927,12 @@ struct Layer {
   long long comp_row0 = 0;
   float *idx_kvs = nullptr, *idx_scs = nullptr, *idx_rows = nullptr;
   int* idx_count = nullptr;
+  int n_keys = 0;                 // its attention list: window + compressed rows
+  // the BF16 projections of the layer input, stacked: compressor wkv and
+  // wgate, then (ratio 4) the indexer compressor's wkv, wgate and the
+  // indexer weights
+  uint16_t* comp_w = nullptr;
+  int comp_rows = 0;
 };
 
 }  // namespace
@@ -1971,10 +1990,13 @@ struct dsv4cuda_decoder {
   // and indexer, the key list and its staged rows
   bool any_comp = false;
   int n_max = 0;                   // keys of the longest list
+  int comp_rows_max = 0;           // rows of the largest stacked projection
   float *cosv_c = nullptr, *sinv_c = nullptr;
   float *cos_tab_c = nullptr, *sin_tab_c = nullptr;
-  float *comp_kv = nullptr, *comp_sc = nullptr;  // [2 * head_dim]
-  float *idx_q = nullptr, *idx_w = nullptr;      // [index_heads * index_dim], [index_heads]
+  float* comp_proj = nullptr;      // the stacked projections' outputs
+  cudaStream_t comp_side = nullptr;    // they run beside the q / kv path
+  cudaEvent_t comp_fork = nullptr, comp_join = nullptr;
+  float* idx_q = nullptr;          // [index_heads * index_dim]
   float* idx_score = nullptr;      // [most compressed rows]
   int idx_n2 = 0;                  // its sort width (a power of two)
   int* idx_full = nullptr;         // [n_max]
@@ -2447,11 +2469,11 @@ cudaError_t bf16_x(dsv4cuda_decoder* D, const uint16_t* W, int rows, int round_o
 }
 
 cudaError_t comp_step(dsv4cuda_decoder* D, dsv4::Layer& L, bool indexer, const float* ape,
-                      const uint16_t* norm, cudaStream_t st) {
+                      const uint16_t* norm, const float* kv, const float* sc, cudaStream_t st) {
   const auto& c = D->cfg;
   dsv4::CompStepArgs a{};
-  a.kv = D->comp_kv;
-  a.sc = D->comp_sc;
+  a.kv = kv;
+  a.sc = sc;
   a.ape = ape;
   a.norm = norm;
   a.rope_dim = c.rope_dim;
@@ -2496,6 +2518,17 @@ cudaError_t attention_comp(dsv4cuda_decoder* D, dsv4::Layer& L, cudaStream_t st)
   const auto& w = L.w;
   const int H = c.n_heads, d = c.head_dim, ql = c.q_lora, half = c.rope_dim / 2;
   const int G = c.o_groups, ol = c.o_lora, hid = c.hidden;
+  // the stacked BF16 projections of x (compressor, indexer compressor,
+  // indexer weights) beside the q / kv path
+  DEC_CHECK(cudaEventRecord(D->comp_fork, st));
+  DEC_CHECK(cudaStreamWaitEvent(D->comp_side, D->comp_fork, 0));
+  DEC_CHECK(bf16_x(D, L.comp_w, L.comp_rows, 0, D->comp_proj, D->comp_side));
+  DEC_CHECK(cudaEventRecord(D->comp_join, D->comp_side));
+  const float* p_kv = D->comp_proj;
+  const float* p_sc = p_kv + L.coff * d;
+  const float* p_ikv = p_sc + L.coff * d;
+  const float* p_isc = p_ikv + 2 * c.index_dim;
+  const float* p_iw = p_isc + 2 * c.index_dim;
   DEC_CHECK(fp8_gemv2(w.wq_a, w.wq_a_s, ql, D->qr, w.wkv, w.wkv_s, d, D->kv, hid, D->xq, D->xs,
                       D->ld, D->item1, D->n_one, D->fp8_part, D->tile_cnt, st));
   dsv4::NormTailArgs kt{};
@@ -2517,22 +2550,18 @@ cudaError_t attention_comp(dsv4cuda_decoder* D, dsv4::Layer& L, cudaStream_t st)
   qt.xs = D->xs;
   DEC_CHECK(dsv4::launch_pdl(dsv4::norm_tail_kernel, dim3(2), dim3(256),
                              sizeof(float) * std::max(d, ql), st, kt, qt));
-  // compressor_update of the main compressor (its row into the cache)
-  DEC_CHECK(bf16_x(D, w.comp_wkv, L.coff * d, 0, D->comp_kv, st));
-  DEC_CHECK(bf16_x(D, w.comp_wgate, L.coff * d, 0, D->comp_sc, st));
-  DEC_CHECK(comp_step(D, L, false, w.comp_ape, w.comp_norm, st));
   DEC_CHECK(fp8_gemv(w.wq_b, w.wq_b_s, ql, H * d, D->xq, D->xs, D->ld, D->q, D->item1, D->n_one,
                      D->fp8_part, D->tile_cnt, st));
+  // compressor_update of the main compressor (its row into the cache)
+  DEC_CHECK(cudaStreamWaitEvent(st, D->comp_join, 0));
+  DEC_CHECK(comp_step(D, L, false, w.comp_ape, w.comp_norm, p_kv, p_sc, st));
   const int* win_idx = D->idx;
   if (L.ratio == 4) {
     const int ih = c.index_heads, id = c.index_dim;
     // the indexer's query from the quantised q latent (still in D->xq)
     DEC_CHECK(fp8_gemv(w.idx_wq_b, w.idx_wq_b_s, ql, ih * id, D->xq, D->xs, D->ld, D->idx_q,
                        D->item1, D->n_one, D->fp8_part, D->tile_cnt, st));
-    DEC_CHECK(bf16_x(D, w.idx_comp_wkv, 2 * id, 0, D->comp_kv, st));
-    DEC_CHECK(bf16_x(D, w.idx_comp_wgate, 2 * id, 0, D->comp_sc, st));
-    DEC_CHECK(comp_step(D, L, true, w.idx_ape, w.idx_comp_norm, st));
-    DEC_CHECK(bf16_x(D, w.idx_weights_proj, ih, 1, D->idx_w, st));
+    DEC_CHECK(comp_step(D, L, true, w.idx_ape, w.idx_comp_norm, p_ikv, p_isc, st));
     DEC_CHECK(dsv4::launch_pdl(dsv4::idx_query_kernel, dim3(ih), dim3(std::max(32, std::min(1024, id))),
                                sizeof(float) * id, st, D->idx_q, id, c.rope_dim,
                                static_cast<const float*>(D->cosv_c),
@@ -2541,8 +2570,7 @@ cudaError_t attention_comp(dsv4cuda_decoder* D, dsv4::Layer& L, cudaStream_t st)
                                dim3((L.max_count + dsv4::kIdxT - 1) / dsv4::kIdxT),
                                dim3(dsv4::kIdxT * ih), sizeof(float) * dsv4::kIdxT * ih, st,
                                static_cast<const float*>(D->idx_q),
-                               static_cast<const float*>(L.idx_rows),
-                               static_cast<const float*>(D->idx_w), ih, id,
+                               static_cast<const float*>(L.idx_rows), p_iw, ih, id,
                                static_cast<const int*>(L.idx_count),
                                static_cast<const int*>(D->d_pos), D->idx_score));
     DEC_CHECK(dsv4::launch_pdl(dsv4::comp_list_kernel, dim3(1), dim3(1024),
@@ -2550,20 +2578,20 @@ cudaError_t attention_comp(dsv4cuda_decoder* D, dsv4::Layer& L, cudaStream_t st)
                                static_cast<const float*>(D->idx_score),
                                static_cast<const int*>(L.idx_count),
                                static_cast<const int*>(D->d_pos), 4, c.index_topk, L.comp_row0,
-                               D->idx_n2, D->n_max, D->idx_full));
+                               D->idx_n2, L.n_keys, D->idx_full));
   } else {
     DEC_CHECK(dsv4::launch_pdl(dsv4::comp_list_kernel, dim3(1), dim3(1024), 0, st, win_idx,
                                c.window, static_cast<const float*>(nullptr),
                                static_cast<const int*>(L.count),
                                static_cast<const int*>(D->d_pos), L.ratio, 0, L.comp_row0, 0,
-                               D->n_max, D->idx_full));
+                               L.n_keys, D->idx_full));
   }
   // the listed rows as BF16, then sparse_attn over them with the inverse RoPE
   dsv4::NormTailArgs sa = kt;
   sa.win = D->kvwin_full;
   sa.idx = D->idx_full;
-  sa.n_win = D->n_max;
-  DEC_CHECK(dsv4::launch_pdl(dsv4::stage_rows_kernel, dim3((D->n_max + 7) / 8, 1), dim3(256), 0,
+  sa.n_win = L.n_keys;
+  DEC_CHECK(dsv4::launch_pdl(dsv4::stage_rows_kernel, dim3((L.n_keys + 7) / 8, 1), dim3(256), 0,
                              st, sa));
   dsv4::WinAttnArgs wa{};
   wa.q = D->q;
@@ -2574,7 +2602,7 @@ cudaError_t attention_comp(dsv4cuda_decoder* D, dsv4::Layer& L, cudaStream_t st)
   wa.sinv = D->sinv_c;
   wa.H = H;
   wa.d = d;
-  wa.n = D->n_max;
+  wa.n = L.n_keys;
   wa.rope_dim = c.rope_dim;
   wa.scale = 1.0f / sqrtf(static_cast<float>(d));
   wa.out = D->o;
@@ -2582,7 +2610,7 @@ cudaError_t attention_comp(dsv4cuda_decoder* D, dsv4::Layer& L, cudaStream_t st)
   wa.q_eps = c.rms_eps;
   DEC_CHECK(hc_join(D, st));
   DEC_CHECK(dsv4::launch_pdl(dsv4::wide_head_kernel, dim3(H), dim3(dsv4::kWhThreads),
-                             dsv4::wide_head_smem(D->n_max, d), st, wa,
+                             dsv4::wide_head_smem(L.n_keys, d), st, wa,
                              static_cast<const uint16_t*>(D->kvwin_full), dsv4::device_error_word()));
   dsv4::Bf16GemvArgs ga{};
   ga.W = L.wo_a;
@@ -2708,16 +2736,19 @@ bool comp_alloc(dsv4cuda_decoder* D) {
   chk(D->sinv_c = dalloc<float>(D, half));
   chk(D->cos_tab_c = dalloc<float>(D, static_cast<size_t>(c.max_context) * half));
   chk(D->sin_tab_c = dalloc<float>(D, static_cast<size_t>(c.max_context) * half));
-  const size_t cdmax = 2 * static_cast<size_t>(std::max(c.head_dim, c.index_dim));
-  chk(D->comp_kv = dalloc<float>(D, cdmax));
-  chk(D->comp_sc = dalloc<float>(D, cdmax));
+  chk(D->comp_proj = dalloc<float>(D, D->comp_rows_max));
   chk(D->idx_q = dalloc<float>(D, static_cast<size_t>(c.index_heads) * c.index_dim));
-  chk(D->idx_w = dalloc<float>(D, c.index_heads));
   chk(D->idx_score = dalloc<float>(D, std::max(D->idx_n2, 1)));
   chk(D->idx_full = dalloc<int>(D, D->n_max));
   chk(D->kvwin_full = dalloc<uint16_t>(D, static_cast<size_t>(D->n_max) * c.head_dim));
   if (!ok) {
     D->err = "out of device memory";
+    return false;
+  }
+  if (cudaStreamCreateWithFlags(&D->comp_side, cudaStreamNonBlocking) != cudaSuccess ||
+      cudaEventCreateWithFlags(&D->comp_fork, cudaEventDisableTiming) != cudaSuccess ||
+      cudaEventCreateWithFlags(&D->comp_join, cudaEventDisableTiming) != cudaSuccess) {
+    D->err = "stream / event creation failed";
     return false;
   }
   std::vector<float> cs, sn;
@@ -3209,7 +3240,32 @@ DSV4_API int dsv4cuda_decoder_create(dsv4cuda_decoder** out, const dsv4cuda_deco
       }
       D->any_comp = true;
       const int keys = L.ratio == 4 ? std::min(c.index_topk, L.max_count) : L.max_count;
-      D->n_max = std::max(D->n_max, c.window + keys);
+      L.n_keys = c.window + keys;
+      D->n_max = std::max(D->n_max, L.n_keys);
+      {
+        const size_t H = c.hidden;
+        std::vector<std::pair<const uint16_t*, int>> parts = {{w.comp_wkv, L.coff * d},
+                                                              {w.comp_wgate, L.coff * d}};
+        if (L.ratio == 4) {
+          parts.push_back({w.idx_comp_wkv, 2 * c.index_dim});
+          parts.push_back({w.idx_comp_wgate, 2 * c.index_dim});
+          parts.push_back({w.idx_weights_proj, c.index_heads});
+        }
+        for (const auto& pr : parts) L.comp_rows += pr.second;
+        L.comp_w = dalloc<uint16_t>(D, static_cast<size_t>(L.comp_rows) * H);
+        size_t off = 0;
+        for (const auto& pr : parts) {
+          if (L.comp_w && cudaMemcpy(L.comp_w + off, pr.first, static_cast<size_t>(pr.second) * H * 2,
+                                     cudaMemcpyDeviceToDevice) != cudaSuccess)
+            L.comp_w = nullptr;
+          off += static_cast<size_t>(pr.second) * H;
+        }
+        if (!L.comp_w) {
+          dsv4cuda_decoder_destroy(D);
+          return fail("dsv4cuda_decoder_create: out of device memory (layer %d projections)", li);
+        }
+        D->comp_rows_max = std::max(D->comp_rows_max, L.comp_rows);
+      }
       if (L.ratio == 4) {
         int n2 = 1;
         while (n2 < L.max_count) n2 <<= 1;
@@ -3278,6 +3334,9 @@ DSV4_API void dsv4cuda_decoder_destroy(dsv4cuda_decoder* D) {
   if (D->hc_side) cudaStreamDestroy(D->hc_side);
   if (D->hc_fork) cudaEventDestroy(D->hc_fork);
   if (D->hc_join) cudaEventDestroy(D->hc_join);
+  if (D->comp_side) cudaStreamDestroy(D->comp_side);
+  if (D->comp_fork) cudaEventDestroy(D->comp_fork);
+  if (D->comp_join) cudaEventDestroy(D->comp_join);
   for (void* p : D->owned) cudaFree(p);
   delete D;
 }

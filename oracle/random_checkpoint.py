@@ -9,8 +9,10 @@ project). Values are drawn directly in their storage formats so that a
 multi-GB checkpoint is written in seconds: FP4 / FP8 codes uniform over the
 finite codes, E8M0 scales 127 + round(N(0, 0.5 / ln 2)) (lognormal(0, 0.5)
 rounded to a power of two), BF16 N(0, 0.02), RMSNorm gains 1 + N(0, 0.02),
-hyper-connection parameters N(0, 0.02) with unit scales. Every layer has
-compress ratio 0 (sliding-window attention).
+hyper-connection parameters N(0, 0.02) with unit scales, compressor APE
+N(0, 0.02). Layer L has compress ratio c["ratios"][L] (default 0,
+sliding-window attention); ratio-4 / ratio-128 layers carry the compressor
+and, for ratio 4, the indexer tensors of the same contract.
 """
 import json
 import os
@@ -37,9 +39,15 @@ def config_json(c, n_layers):
         "compress_rope_theta": 160000.0,
         "rope_scaling": {"factor": 16.0, "beta_fast": 32.0, "beta_slow": 1.0,
                          "original_max_position_embeddings": 65536, "type": "yarn"},
-        "index_n_heads": 64, "index_head_dim": 128, "index_topk": 512,
-        "compress_ratios": [0] * n_layers,
+        "index_n_heads": c.get("index_heads", 64), "index_head_dim": c.get("index_dim", 128),
+        "index_topk": c.get("index_topk", 512),
+        "compress_ratios": ratios(c, n_layers),
     }
+
+
+def ratios(c, n_layers):
+    r = list(c.get("ratios", []))[:n_layers]
+    return r + [0] * (n_layers - len(r))
 
 
 def tensor_specs(c, n_layers):
@@ -71,6 +79,23 @@ def tensor_specs(c, n_layers):
         sp.append((p + "attn.kv_norm.weight", "BF16", [hd], "norm"))
         fp8(p + "attn.wo_a", G * ol, nh * hd // G)
         fp8(p + "attn.wo_b", H, G * ol)
+        ratio = ratios(c, n_layers)[L]
+        if ratio:
+            coff = 2 if ratio == 4 else 1
+            cp = p + "attn.compressor."
+            sp += [(cp + "ape", "F32", [ratio, coff * hd], "w"),
+                   (cp + "wkv.weight", "BF16", [coff * hd, H], "w"),
+                   (cp + "wgate.weight", "BF16", [coff * hd, H], "w"),
+                   (cp + "norm.weight", "BF16", [hd], "norm")]
+            if ratio == 4:
+                ih, idim = c.get("index_heads", 64), c.get("index_dim", 128)
+                ip = p + "attn.indexer."
+                fp8(ip + "wq_b", ih * idim, ql)
+                sp += [(ip + "weights_proj.weight", "BF16", [ih, H], "w"),
+                       (ip + "compressor.ape", "F32", [ratio, coff * idim], "w"),
+                       (ip + "compressor.wkv.weight", "BF16", [coff * idim, H], "w"),
+                       (ip + "compressor.wgate.weight", "BF16", [coff * idim, H], "w"),
+                       (ip + "compressor.norm.weight", "BF16", [idim], "norm")]
         sp += [(p + "ffn.gate.weight", "BF16", [E, H], "w"), (p + "ffn.gate.bias", "F32", [E], "w")]
         fp8(p + "ffn.shared_experts.w1", I, H)
         fp8(p + "ffn.shared_experts.w3", I, H)
