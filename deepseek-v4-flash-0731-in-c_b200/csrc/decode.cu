@@ -1094,7 +1094,8 @@ __global__ void __launch_bounds__(64) win_values_kernel(const WinAttnArgs a) {
        p += blockDim.x) {
     const int i = 2 * p;
     float o0 = 0.0f, o1 = 0.0f;
-#pragma unroll 8
+    // 32 keys' rows requested ahead of their fmaf (the chains wait on L2)
+#pragma unroll 32
     for (int t = 0; t < a.n; ++t) {
       const float2 kv = *reinterpret_cast<const float2*>(a.kvdec + static_cast<size_t>(t) * a.d + i);
       o0 = fmaf(ws[t], kv.x, o0);
@@ -1286,175 +1287,6 @@ __global__ void __launch_bounds__(kWhThreads) win_head_kernel(const WinAttnArgs 
   a.cosv = a0.cosv + r * (a0.rope_dim / 2);
   a.sinv = a0.sinv + r * (a0.rope_dim / 2);
   win_head_run(a, win + r * a0.n * a0.d, err, blockIdx.x, wsm, [] { pdl_wait(); });
-}
-
-// The same attention over a longer key list (a compressed layer's window
-// plus its compressed rows, n keys, -1 = padding) than shared memory holds:
-// one CTA per head streams the staged BF16 rows in chunks of kWideKeys
-// twice - the scores (every key's dot in dimension order) for the softmax
-// over all keys, then the values (every dimension pair's chain in key order,
-// carried across chunks) - with the head's q kept in shared memory.
-constexpr int kWideKeys = 96;  // two buffers of 96 rows x 1040 B fit with d = 512
-
-__host__ __device__ inline size_t wide_head_smem(int n, int d) {
-  return static_cast<size_t>(2) * kWideKeys * (d + 8) * 2 + static_cast<size_t>(d) * 4 +
-         static_cast<size_t>(3) * n * 4 + 16;
-}
-
-__global__ void __launch_bounds__(kWhThreads) wide_head_kernel(const WinAttnArgs a,
-                                                               const uint16_t* win,
-                                                               unsigned int* err) {
-  extern __shared__ __align__(16) unsigned char wsm[];
-  __shared__ uint64_t bars[2];
-  __shared__ float den_s;
-  pdl_trigger();
-  const int h = blockIdx.x;
-  const int n = a.n, d = a.d, ldk = d + 8;
-  uint16_t* kbuf[2] = {reinterpret_cast<uint16_t*>(wsm),
-                       reinterpret_cast<uint16_t*>(wsm) + static_cast<size_t>(kWideKeys) * ldk};
-  float* qs = reinterpret_cast<float*>(wsm + static_cast<size_t>(2) * kWideKeys * ldk * 2);  // [d]
-  float* ss = qs + d;                                                                      // [n]
-  float* ws = ss + n;                                                                      // [n]
-  int* sidx = reinterpret_cast<int*>(ws + n);                                              // [n]
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int nth = blockDim.x;
-  if (tid == 0) {
-    mbar_init(&bars[0], 1);
-    mbar_init(&bars[1], 1);
-    mbar_fence_init();
-  }
-  __syncthreads();
-  pdl_wait();
-  for (int t = tid; t < n; t += nth) sidx[t] = a.idx[t];
-  for (int i = tid; i < d / 4; i += nth)
-    reinterpret_cast<float4*>(qs)[i] = reinterpret_cast<const float4*>(a.q + static_cast<size_t>(h) * d)[i];
-  const uint32_t row_bytes = static_cast<uint32_t>(d) * 2;
-  const int nch = (n + kWideKeys - 1) / kWideKeys;
-  const int total = 2 * nch;  // every chunk twice: scores, then values
-  // chunk g (of key chunk g % nch) into buffer g & 1; every thread calls it
-  auto issue = [&](int g) {
-    const int c0 = (g % nch) * kWideKeys, nk = min(kWideKeys, n - c0), bi = g & 1;
-    if (tid == 0) mbar_arrive_expect_tx(&bars[bi], row_bytes * static_cast<uint32_t>(nk));
-    __syncthreads();
-    for (int t = tid; t < nk; t += nth)
-      bulk_g2s(kbuf[bi] + static_cast<size_t>(t) * ldk, win + static_cast<size_t>(c0 + t) * d,
-               row_bytes, &bars[bi]);
-  };
-  issue(0);
-  if (a.q_raw) {
-    __shared__ double qred[32];
-    __syncthreads();
-    double sq = 0.0;
-    for (int i = tid; i < d; i += nth) sq += static_cast<double>(qs[i]) * qs[i];
-    sq = block_sum_d(sq, qred);
-    const float rr = rms_factor(sq, d, a.q_eps);
-    for (int i = tid; i < d; i += nth) qs[i] = bf16_round(__fmul_rn(qs[i], rr));
-    __syncthreads();
-    const int half = a.rope_dim / 2, start = d - a.rope_dim;
-    for (int i = tid; i < half; i += nth) {
-      const float x0 = qs[start + 2 * i], x1 = qs[start + 2 * i + 1];
-      const float c = a.cosv[i], sn = a.sinv[i];
-      qs[start + 2 * i] = bf16_round(__fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, sn)));
-      qs[start + 2 * i + 1] = bf16_round(__fadd_rn(__fmul_rn(x0, sn), __fmul_rn(x1, c)));
-    }
-  }
-  // d / 2 dimension pairs, two per thread (d <= 4 * blockDim.x)
-  const int p0 = tid, p1 = tid + nth;
-  const bool has0 = p0 < d / 2, has1 = p1 < d / 2;
-  float o[2][2] = {{0.f, 0.f}, {0.f, 0.f}};
-  float den = 0.0f;
-  for (int g = 0; g < total; ++g) {
-    __syncthreads();  // the buffer issue(g + 1) refills was last read in step g - 1
-    if (g + 1 < total) issue(g + 1);
-    const int bi = g & 1;
-    bool ok = mbar_wait(&bars[bi], static_cast<uint32_t>((g >> 1) & 1), err);
-    if (!__syncthreads_and(ok)) {
-      // the copies in flight land before the CTA exits
-      if (!ok) mbar_wait(&bars[bi], static_cast<uint32_t>((g >> 1) & 1), err);
-      if (g + 1 < total) mbar_wait(&bars[bi ^ 1], static_cast<uint32_t>(((g + 1) >> 1) & 1), err);
-      return;
-    }
-    const uint16_t* ks = kbuf[bi];
-    const int c0 = (g % nch) * kWideKeys, nk = min(kWideKeys, n - c0);
-    if (g < nch) {
-      for (int t = tid; t < nk; t += nth) {
-        const int r = sidx[c0 + t];
-        float st = -INFINITY;
-        if (r >= 0 && r < a.cache.rows) {
-          const uint16_t* kr = ks + static_cast<size_t>(t) * ldk;
-          float dot = 0.0f;
-#pragma unroll 4
-          for (int i = 0; i < d; i += 8) {
-            float kf[8];
-            bf16x8_to_f32(*reinterpret_cast<const uint4*>(kr + i), kf);
-            const float4 q0 = *reinterpret_cast<const float4*>(qs + i);
-            const float4 q1 = *reinterpret_cast<const float4*>(qs + i + 4);
-            dot = fmaf(q0.x, kf[0], dot);
-            dot = fmaf(q0.y, kf[1], dot);
-            dot = fmaf(q0.z, kf[2], dot);
-            dot = fmaf(q0.w, kf[3], dot);
-            dot = fmaf(q1.x, kf[4], dot);
-            dot = fmaf(q1.y, kf[5], dot);
-            dot = fmaf(q1.z, kf[6], dot);
-            dot = fmaf(q1.w, kf[7], dot);
-          }
-          st = __fmul_rn(dot, a.scale);
-        }
-        ss[c0 + t] = st;
-      }
-      continue;
-    }
-    if (g == nch) {
-      // every score is in: the softmax over all keys
-      __syncthreads();
-      if (warp == 0) {
-        float mx = -INFINITY;
-        for (int t = lane; t < n; t += 32) mx = fmaxf(mx, ss[t]);
-        mx = warp_max(mx);
-        for (int t = lane; t < n; t += 32) {
-          const float st = ss[t];
-          ws[t] = st != -INFINITY ? expf_r1(st - mx) : 0.0f;
-        }
-        __syncwarp();
-        if (lane == 0) {
-          float sum = expf_r1(a.sink[h] - mx);
-          for (int t = 0; t < n; ++t)
-            if (ss[t] != -INFINITY) sum += ws[t];
-          den_s = sum;
-        }
-        __syncwarp();
-        for (int t = lane; t < n; t += 32) ws[t] = bf16_round(ws[t]);
-      }
-      __syncthreads();
-      den = den_s;
-    }
-    for (int t = 0; t < nk; ++t) {
-      const float wt = ws[c0 + t];
-      const uint16_t* vr = ks + static_cast<size_t>(t) * ldk;
-      const uint32_t v0 = has0 ? *reinterpret_cast<const uint32_t*>(vr + 2 * p0) : 0u;
-      const uint32_t v1 = has1 ? *reinterpret_cast<const uint32_t*>(vr + 2 * p1) : 0u;
-      o[0][0] = fmaf(wt, __uint_as_float(v0 << 16), o[0][0]);
-      o[0][1] = fmaf(wt, __uint_as_float(v0 & 0xFFFF0000u), o[0][1]);
-      o[1][0] = fmaf(wt, __uint_as_float(v1 << 16), o[1][0]);
-      o[1][1] = fmaf(wt, __uint_as_float(v1 & 0xFFFF0000u), o[1][1]);
-    }
-  }
-  const int start = d - a.rope_dim;
-#pragma unroll
-  for (int u = 0; u < 2; ++u) {
-    if (!(u ? has1 : has0)) continue;
-    const int i = 2 * (u ? p1 : p0);
-    float x0 = bf16_round(o[u][0] / den), x1 = bf16_round(o[u][1] / den);
-    if (a.cosv && i >= start) {
-      const int k = (i - start) / 2;
-      const float cs = a.cosv[k], sn = a.sinv[k];
-      const float y0 = bf16_round(__fadd_rn(__fmul_rn(x0, cs), __fmul_rn(x1, sn)));
-      const float y1 = bf16_round(__fadd_rn(__fmul_rn(-x0, sn), __fmul_rn(x1, cs)));
-      x0 = y0;
-      x1 = y1;
-    }
-    *reinterpret_cast<float2*>(a.out + static_cast<size_t>(h) * d + i) = make_float2(x0, x1);
-  }
 }
 
 // Greedy token: argmax_logits (src/cli/dsv4_run.c:355; first maximum, strict
@@ -1757,24 +1589,41 @@ __global__ void idx_query_kernel(float* q, int id, int rope_dim, const float* co
 
 // Index scores (:5733-5747): score[t] = sum over heads h in order of
 // fmaf(relu(q_h . k_t), w_h, acc), the dot one fmaf chain over the head's
-// dims; w_h = bf16(proj_h * (id^-1/2 * ih^-1/2)). CTA = kIdxT compressed
-// rows x ih heads (thread = (row, head) dot), t < min(count, (pos + 1) / 4).
-constexpr int kIdxT = 8;
+// dims; w_h = bf16(bf16(proj_h) * (id^-1/2 * ih^-1/2)). CTA = kIdxT
+// compressed rows x ih heads (thread = (row, head) dot) with the query
+// transposed in shared memory ([dim][head]: a warp's heads on distinct
+// banks) and the CTA's keys beside it (broadcast), t < min(count, (pos+1)/4).
+constexpr int kIdxT = 16;
 __global__ void idx_score_kernel(const float* q, const float* keys, const float* wproj, int ih,
                                  int id, const int* count, const int* pos, float* score) {
-  extern __shared__ float dots[];  // [kIdxT][ih]
+  extern __shared__ float ism[];
+  float* qt = ism;                   // [id][ih]
+  float* kt = qt + id * ih;          // [kIdxT][id]
+  float* dots = kt + kIdxT * id;     // [kIdxT][ih]
   pdl_trigger();
   pdl_wait();
   int nt = *count;
   const int maxc = (*pos + 1) / 4;
   if (nt > maxc) nt = maxc;
+  const int t0 = blockIdx.x * kIdxT;
+  if (t0 >= nt) return;  // uniform over the CTA
+  const int nth = blockDim.x;
+  for (int i = threadIdx.x; i < ih * id; i += nth) {
+    const int h = i / id, dd = i % id;
+    qt[dd * ih + h] = q[i];
+  }
+  for (int i = threadIdx.x; i < kIdxT * id; i += nth) {
+    const int tl = i / id;
+    kt[i] = t0 + tl < nt ? keys[static_cast<size_t>(t0) * id + i] : 0.0f;
+  }
+  __syncthreads();
   const int tl = threadIdx.x / ih, h = threadIdx.x % ih;
-  const int t = blockIdx.x * kIdxT + tl;
+  const int t = t0 + tl;
   if (tl < kIdxT && t < nt) {
-    const float* qh = q + static_cast<size_t>(h) * id;
-    const float* kp = keys + static_cast<size_t>(t) * id;
+    const float* kr = kt + tl * id;
     float dot = 0.0f;
-    for (int dd = 0; dd < id; ++dd) dot = fmaf(qh[dd], kp[dd], dot);
+#pragma unroll 8
+    for (int dd = 0; dd < id; ++dd) dot = fmaf(qt[dd * ih + h], kr[dd], dot);
     if (dot < 0.0f) dot = 0.0f;
     dots[tl * ih + h] = dot;
   }
@@ -2000,7 +1849,8 @@ struct dsv4cuda_decoder {
   float* idx_score = nullptr;      // [most compressed rows]
   int idx_n2 = 0;                  // its sort width (a power of two)
   int* idx_full = nullptr;         // [n_max]
-  uint16_t* kvwin_full = nullptr;  // [n_max][head_dim]
+  float *c_kvdec = nullptr, *c_kvt = nullptr;    // [n_max][head_dim], transposed
+  float *c_att_s = nullptr, *c_att_w = nullptr;  // [n_heads][n_max]
   dsv4::GemvItem* item1 = nullptr;   // one (x row 0 -> y row 0) item
   dsv4::GemvItem* items_g = nullptr; // o_groups items (group g: matrix g, rows g)
   int* n_one = nullptr;
@@ -2450,6 +2300,12 @@ cudaError_t attention(dsv4cuda_decoder* D, dsv4::Layer& L, cudaStream_t st) {
                   D->n_one, D->fp8_part, D->tile_cnt, st, D->oall);
 }
 
+size_t idx_score_smem(const dsv4cuda_decoder_config& c) {
+  return sizeof(float) * (static_cast<size_t>(c.index_dim) * c.index_heads +
+                          static_cast<size_t>(dsv4::kIdxT) * c.index_dim +
+                          static_cast<size_t>(dsv4::kIdxT) * c.index_heads);
+}
+
 // A BF16 projection of the layer input D->x (one token) into y.
 cudaError_t bf16_x(dsv4cuda_decoder* D, const uint16_t* W, int rows, int round_out, float* y,
                    cudaStream_t st) {
@@ -2568,7 +2424,7 @@ cudaError_t attention_comp(dsv4cuda_decoder* D, dsv4::Layer& L, cudaStream_t st)
                                static_cast<const float*>(D->sinv_c)));
     DEC_CHECK(dsv4::launch_pdl(dsv4::idx_score_kernel,
                                dim3((L.max_count + dsv4::kIdxT - 1) / dsv4::kIdxT),
-                               dim3(dsv4::kIdxT * ih), sizeof(float) * dsv4::kIdxT * ih, st,
+                               dim3(dsv4::kIdxT * ih), idx_score_smem(c), st,
                                static_cast<const float*>(D->idx_q),
                                static_cast<const float*>(L.idx_rows), p_iw, ih, id,
                                static_cast<const int*>(L.idx_count),
@@ -2586,13 +2442,13 @@ cudaError_t attention_comp(dsv4cuda_decoder* D, dsv4::Layer& L, cudaStream_t st)
                                static_cast<const int*>(D->d_pos), L.ratio, 0, L.comp_row0, 0,
                                L.n_keys, D->idx_full));
   }
-  // the listed rows as BF16, then sparse_attn over them with the inverse RoPE
-  dsv4::NormTailArgs sa = kt;
-  sa.win = D->kvwin_full;
-  sa.idx = D->idx_full;
-  sa.n_win = L.n_keys;
-  DEC_CHECK(dsv4::launch_pdl(dsv4::stage_rows_kernel, dim3((L.n_keys + 7) / 8, 1), dim3(256), 0,
-                             st, sa));
+  // sparse_attn over the list with the inverse RoPE, in the reference's
+  // order: the rows decoded, every (head, key) score, per head the softmax
+  // and the key-order denominator, per (head, dimension pair) the key-order
+  // value chains
+  DEC_CHECK(dsv4::launch_pdl(dsv4::q_head_kernel, dim3(H), dim3(128), 0, st, D->q, d, c.rms_eps,
+                             half, static_cast<const float*>(D->cosv_c),
+                             static_cast<const float*>(D->sinv_c)));
   dsv4::WinAttnArgs wa{};
   wa.q = D->q;
   wa.cache = L.cache;
@@ -2605,13 +2461,22 @@ cudaError_t attention_comp(dsv4cuda_decoder* D, dsv4::Layer& L, cudaStream_t st)
   wa.n = L.n_keys;
   wa.rope_dim = c.rope_dim;
   wa.scale = 1.0f / sqrtf(static_cast<float>(d));
+  wa.kvdec = D->c_kvdec;
+  wa.kvt = D->c_kvt;
+  wa.s = D->c_att_s;
+  wa.w = D->c_att_w;
+  wa.den = D->att_den;
   wa.out = D->o;
-  wa.q_raw = 1;
-  wa.q_eps = c.rms_eps;
   DEC_CHECK(hc_join(D, st));
-  DEC_CHECK(dsv4::launch_pdl(dsv4::wide_head_kernel, dim3(H), dim3(dsv4::kWhThreads),
-                             dsv4::wide_head_smem(L.n_keys, d), st, wa,
-                             static_cast<const uint16_t*>(D->kvwin_full), dsv4::device_error_word()));
+  DEC_CHECK(dsv4::launch_pdl(dsv4::win_decode_kernel, dim3(L.n_keys), dim3(128), 0, st, wa));
+  DEC_CHECK(dsv4::launch_pdl(
+      dsv4::win_scores_kernel,
+      dim3((H + dsv4::kWinHeads - 1) / dsv4::kWinHeads, (L.n_keys + dsv4::kWinKeys - 1) / dsv4::kWinKeys),
+      dim3(dsv4::kWinHeads * 32), sizeof(float) * (dsv4::kWinHeads + dsv4::kWinKeys) * d, st, wa));
+  DEC_CHECK(dsv4::launch_pdl(dsv4::win_softmax_kernel, dim3(H), dim3(256),
+                             sizeof(float) * L.n_keys, st, wa));
+  DEC_CHECK(dsv4::launch_pdl(dsv4::win_values_kernel, dim3(H, (d / 2 + 63) / 64), dim3(64),
+                             sizeof(float) * L.n_keys, st, wa));
   dsv4::Bf16GemvArgs ga{};
   ga.W = L.wo_a;
   ga.w_stride = static_cast<size_t>(ol) * (H * d / G);
@@ -2725,7 +2590,8 @@ bool comp_alloc(dsv4cuda_decoder* D) {
   if (c.index_heads <= 0 || c.index_dim < 32 || (c.index_dim & (c.index_dim - 1)) ||
       c.index_dim % 32 || c.index_dim < c.rope_dim || c.index_heads * dsv4::kIdxT > 1024 ||
       c.index_topk <= 0 || c.compress_rope_theta <= 0.f || c.rope_factor <= 0.f ||
-      c.original_position <= 0 || c.head_dim > 4 * dsv4::kWhThreads || D->idx_n2 > 8192) {
+      c.original_position <= 0 || D->idx_n2 > 8192 ||
+      idx_score_smem(c) > 200 * 1024) {
     D->err = "index heads / dim (a power of two >= 32 and >= rope_dim) / top-k or the YaRN "
              "parameters out of range, or max_context too long for the top-k sort";
     return false;
@@ -2740,7 +2606,10 @@ bool comp_alloc(dsv4cuda_decoder* D) {
   chk(D->idx_q = dalloc<float>(D, static_cast<size_t>(c.index_heads) * c.index_dim));
   chk(D->idx_score = dalloc<float>(D, std::max(D->idx_n2, 1)));
   chk(D->idx_full = dalloc<int>(D, D->n_max));
-  chk(D->kvwin_full = dalloc<uint16_t>(D, static_cast<size_t>(D->n_max) * c.head_dim));
+  chk(D->c_kvdec = dalloc<float>(D, static_cast<size_t>(D->n_max) * c.head_dim));
+  chk(D->c_kvt = dalloc<float>(D, static_cast<size_t>(D->n_max) * c.head_dim));
+  chk(D->c_att_s = dalloc<float>(D, static_cast<size_t>(D->n_max) * c.n_heads));
+  chk(D->c_att_w = dalloc<float>(D, static_cast<size_t>(D->n_max) * c.n_heads));
   if (!ok) {
     D->err = "out of device memory";
     return false;
@@ -2755,10 +2624,13 @@ bool comp_alloc(dsv4cuda_decoder* D) {
   rope_tables_yarn(c, cs, sn);
   if (cudaMemcpy(D->cos_tab_c, cs.data(), cs.size() * sizeof(float), cudaMemcpyHostToDevice) != cudaSuccess ||
       cudaMemcpy(D->sin_tab_c, sn.data(), sn.size() * sizeof(float), cudaMemcpyHostToDevice) != cudaSuccess ||
-      dsv4::set_max_dynamic_smem(reinterpret_cast<const void*>(dsv4::wide_head_kernel),
-                                 static_cast<int>(dsv4::wide_head_smem(D->n_max, c.head_dim))) != cudaSuccess ||
+      dsv4::set_max_dynamic_smem(reinterpret_cast<const void*>(dsv4::win_scores_kernel),
+                                 static_cast<int>(sizeof(float) * (dsv4::kWinHeads + dsv4::kWinKeys) *
+                                                  c.head_dim)) != cudaSuccess ||
       dsv4::set_max_dynamic_smem(reinterpret_cast<const void*>(dsv4::comp_list_kernel),
                                  static_cast<int>(sizeof(float) * 2 * std::max(D->idx_n2, 1))) != cudaSuccess ||
+      dsv4::set_max_dynamic_smem(reinterpret_cast<const void*>(dsv4::idx_score_kernel),
+                                 static_cast<int>(idx_score_smem(c))) != cudaSuccess ||
       comp_reset(D, nullptr) != cudaSuccess) {
     D->err = "set-up failed";
     return false;
@@ -3240,7 +3112,7 @@ DSV4_API int dsv4cuda_decoder_create(dsv4cuda_decoder** out, const dsv4cuda_deco
       }
       D->any_comp = true;
       const int keys = L.ratio == 4 ? std::min(c.index_topk, L.max_count) : L.max_count;
-      L.n_keys = c.window + keys;
+      L.n_keys = (c.window + keys + 3) / 4 * 4;  // the scores kernel takes keys in fours
       D->n_max = std::max(D->n_max, L.n_keys);
       {
         const size_t H = c.hidden;
