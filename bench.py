@@ -86,6 +86,9 @@ def parse():
                     help="decode: distinct random-init layer weight sets the 43 layers cycle "
                          "through (each ~3.6 GB; L2 never holds a layer between uses)")
     ap.add_argument("--decode-layers", type=int, default=43)
+    ap.add_argument("--decode-prompt", type=int, default=2048,
+                    help="decode: context positions decoded before timing (2048: the "
+                         "benchmark's; fewer only for profiling captures)")
     ap.add_argument("--decode-ratios", default="dsv4", choices=["dsv4", "window"],
                     help="decode: DeepSeek-V4-Flash's compress ratios (two window layers, then "
                          "ratio 4 / 128 alternating) or every layer a sliding-window layer")
@@ -1012,9 +1015,10 @@ def decode_config(args, world):
                           "top-512 of the compressed rows) and ratio 128 alternating"
                           if args.decode_ratios == "dsv4" else
                           "sliding window of 128 on every layer (compress ratio 0)"),
-            "prompt_positions": 2048,
-            "context": "a 2048-token greedy prompt decoded through the same graph before "
-                       "timing (rings, compressor state and compressed rows in place)",
+            "prompt_positions": args.decode_prompt,
+            "context": f"a {args.decode_prompt}-token greedy prompt decoded through the same "
+                       "graph before timing (rings, compressor state and compressed rows in "
+                       "place)",
             "weight_sets": f"{n_layers} layers cycle distinct random-init layer weight sets "
                            "of ~3.6 GB (two per kind of layer); every token reads a whole "
                            "model's bytes, none of it L2-resident",
@@ -1205,9 +1209,11 @@ def main_decode(args, rank, world, local):
                    for i in range(per_kind)] for r in kinds}
     sets = [st_ for r in kinds for st_ in sets_by[r]]
     seen = {r: 0 for r in kinds}
-    layers = []
+    layers, set_of = [], []  # layer i runs weight set sets[set_of[i]]
     for r in ratios:
-        layers.append(sets_by[r][seen[r] % per_kind])
+        st_ = sets_by[r][seen[r] % per_kind]
+        layers.append(st_)
+        set_of.append(next(k for k, x in enumerate(sets) if x is st_))
         seen[r] += 1
     g = torch.Generator(device=dev)
     g.manual_seed(7)
@@ -1221,8 +1227,8 @@ def main_decode(args, rank, world, local):
                                         generator=g) * 0.02,
                  hc_head_base=torch.randn(c["hc_mult"], device=dev, generator=g) * 0.02,
                  hc_head_scale=torch.ones(1, device=dev))
-    prompt, gen = 2048, args.steps
-    n_e2e = max(8, args.steps // 4)  # host-call tokens after the timed graph replays
+    prompt, gen = args.decode_prompt, args.steps
+    n_e2e = max(32, args.steps // 2)  # host-call tokens after the timed graph replays
     spec_steps = 0 if (args.no_spec or world > 1) else max(10, args.steps // 4)
     spec_warm = 3
     cfg = dict(hidden=c["hidden"], n_layers=n_layers, vocab=c["vocab"], n_heads=c["n_heads"],
@@ -1264,7 +1270,7 @@ def main_decode(args, rank, world, local):
                     addrs.append(a_)
             L.ep_attach(rank, world, addrs)
         dist.barrier()
-        dec.set_moe_layers([moe_ep[sets.index(L)] for L in layers])
+        dec.set_moe_layers([moe_ep[set_of[i]] for i in range(n_layers)])
     lib = dsv4cuda.lib
     h = dec.handle
     _, _, _, am_slot = dec.slots()
@@ -1364,7 +1370,7 @@ def main_decode(args, rank, world, local):
                     addrs.append(a_)
             L.ep_attach(rank, world, addrs)
         dist.barrier()
-        dec.set_moe_layers([moe_rep[sets.index(L)] for L in layers])
+        dec.set_moe_layers([moe_rep[set_of[i]] for i in range(n_layers)])
         dec.set_ep_replicated(True)
         # every rank already holds the same context (same weights, the same
         # greedy tokens); continue after the positions used so far
