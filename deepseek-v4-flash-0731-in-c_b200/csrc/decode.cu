@@ -1118,6 +1118,76 @@ __global__ void __launch_bounds__(64) win_values_kernel(const WinAttnArgs a) {
   }
 }
 
+// The value pass for long key lists (a compressed layer's window +
+// compressed rows): CTA (head, 256-dim block), thread = dimension pair, the
+// two chains over the keys in key order as win_values_kernel, with the keys'
+// rows streamed through shared memory in chunks of kValKeys (coalesced
+// loads; the next chunk held in registers while this one is consumed).
+constexpr int kValKeys = 32;
+constexpr int kValThreads = 128;  // 256 dims per CTA
+__global__ void __launch_bounds__(kValThreads) win_values_long_kernel(const WinAttnArgs a) {
+  extern __shared__ __align__(16) float vsm[];  // ws [n] | rows [kValKeys][2 * kValThreads]
+  pdl_wait();
+  pdl_trigger();
+  const int h = blockIdx.x, tid = threadIdx.x;
+  const int n = a.n, d = a.d;
+  const int cols = 2 * kValThreads;
+  const int col0 = blockIdx.y * cols;
+  float* ws = vsm;
+  float* rows = vsm + ((n + 3) & ~3);
+  for (int t = tid; t < n; t += kValThreads) ws[t] = a.w[static_cast<size_t>(h) * n + t];
+  // each thread moves kValKeys * cols / 4 / kValThreads float4 per chunk
+  constexpr int kPer = kValKeys * 2 * kValThreads / 4 / kValThreads;  // 16
+  float4 buf[kPer];
+  auto fetch = [&](int c0) {
+#pragma unroll
+    for (int k = 0; k < kPer; ++k) {
+      const int e = k * kValThreads + tid;      // float4 index within the chunk
+      const int t = e / (cols / 4), c4 = e - t * (cols / 4);
+      const int col = col0 + 4 * c4;
+      buf[k] = (c0 + t < n && col < d)
+                   ? *reinterpret_cast<const float4*>(a.kvdec + static_cast<size_t>(c0 + t) * d + col)
+                   : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+  };
+  fetch(0);
+  const int p = col0 / 2 + tid;  // this thread's dimension pair
+  const bool live = 2 * p < d;
+  float o0 = 0.0f, o1 = 0.0f;
+  for (int c0 = 0; c0 < n; c0 += kValKeys) {
+    __syncthreads();  // the previous chunk is consumed (and ws is in)
+#pragma unroll
+    for (int k = 0; k < kPer; ++k)
+      reinterpret_cast<float4*>(rows)[k * kValThreads + tid] = buf[k];
+    __syncthreads();
+    if (c0 + kValKeys < n) fetch(c0 + kValKeys);
+    const int nk = min(kValKeys, n - c0);
+#pragma unroll 8
+    for (int t = 0; t < nk; ++t) {
+      const float2 kv = reinterpret_cast<const float2*>(rows + t * cols)[tid];
+      const float wt = ws[c0 + t];
+      o0 = fmaf(wt, kv.x, o0);
+      o1 = fmaf(wt, kv.y, o1);
+    }
+  }
+  if (!live) return;
+  const int i = 2 * p;
+  const float den = a.den[h];
+  float x0 = bf16_round(o0 / den), x1 = bf16_round(o1 / den);
+  const int start = d - a.rope_dim;
+  if (a.cosv && i >= start) {
+    const int k = (i - start) / 2;
+    const float c = a.cosv[k], sn = a.sinv[k];
+    const float y0 = bf16_round(__fadd_rn(__fmul_rn(x0, c), __fmul_rn(x1, sn)));
+    const float y1 = bf16_round(__fadd_rn(__fmul_rn(-x0, sn), __fmul_rn(x1, c)));
+    x0 = y0;
+    x1 = y1;
+  }
+  float* oh = a.out + static_cast<size_t>(h) * d;
+  oh[i] = x0;
+  oh[i + 1] = x1;
+}
+
 __device__ __forceinline__ void bf16x8_to_f32(const uint4 u, float (&f)[8]) {
   const uint32_t w[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
@@ -2475,8 +2545,10 @@ cudaError_t attention_comp(dsv4cuda_decoder* D, dsv4::Layer& L, cudaStream_t st)
       dim3(dsv4::kWinHeads * 32), sizeof(float) * (dsv4::kWinHeads + dsv4::kWinKeys) * d, st, wa));
   DEC_CHECK(dsv4::launch_pdl(dsv4::win_softmax_kernel, dim3(H), dim3(256),
                              sizeof(float) * L.n_keys, st, wa));
-  DEC_CHECK(dsv4::launch_pdl(dsv4::win_values_kernel, dim3(H, (d / 2 + 63) / 64), dim3(64),
-                             sizeof(float) * L.n_keys, st, wa));
+  DEC_CHECK(dsv4::launch_pdl(
+      dsv4::win_values_long_kernel, dim3(H, (d + 2 * dsv4::kValThreads - 1) / (2 * dsv4::kValThreads)),
+      dim3(dsv4::kValThreads),
+      sizeof(float) * (((L.n_keys + 3) & ~3) + dsv4::kValKeys * 2 * dsv4::kValThreads), st, wa));
   dsv4::Bf16GemvArgs ga{};
   ga.W = L.wo_a;
   ga.w_stride = static_cast<size_t>(ol) * (H * d / G);
