@@ -1236,7 +1236,7 @@ def main_decode(args, rank, world, local):
                o_groups=c["o_groups"], o_lora=c["o_lora"], window=c["window"],
                hc_mult=c["hc_mult"], hc_iters=c["hc_iters"], rms_eps=c["rms_eps"],
                hc_eps=c["hc_eps"], rope_theta=c["rope_theta"],
-               max_context=prompt + 2 * (gen + args.warmup) + n_e2e + 32 +
+               max_context=prompt + 4 * (gen + args.warmup) + n_e2e + 32 +
                (spec_steps + spec_warm + 1) * args.spec_rows,
                index_heads=c["index_heads"], index_dim=c["index_dim"],
                index_topk=c["index_topk"], compress_rope_theta=c["compress_rope_theta"],
@@ -1299,25 +1299,33 @@ def main_decode(args, rank, world, local):
     clocks = ClockSampler(local)
     clocks.start()
     time.sleep(0.3)
-    if dist:
-        dist.barrier()
-    torch.cuda.synchronize()
-    ev0 = torch.cuda.Event(enable_timing=True)
-    ev1 = torch.cuda.Event(enable_timing=True)
-    with torch.cuda.stream(stream):
-        ev0.record(stream)
-        for _ in range(args.steps):
-            graph.replay()
-        ev1.record(stream)
-    torch.cuda.synchronize()
-    if dist:
-        dist.barrier()
-    ms = ev0.elapsed_time(ev1)
+    def decode_window():
+        """K greedy steps between a barrier + synchronize on both sides; the
+        device time, max over ranks."""
+        if dist:
+            dist.barrier()
+        torch.cuda.synchronize()
+        ev0 = torch.cuda.Event(enable_timing=True)
+        ev1 = torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
+            ev0.record(stream)
+            for _ in range(args.steps):
+                graph.replay()
+            ev1.record(stream)
+        torch.cuda.synchronize()
+        if dist:
+            dist.barrier()
+        w = ev0.elapsed_time(ev1)
+        if dist:
+            t = torch.tensor([w], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            w = float(t.item())
+        return w
+
+    # the reported window is the first; two more give the spread
+    windows = [decode_window() for _ in range(3)]
     clk = clocks.stop()
-    if dist:
-        t = torch.tensor([ms], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
+    ms = windows[0]
     ms_tok = ms / args.steps
     value = world * 1e3 / ms_tok
     # e2e: the public host-argument call, greedy on the host, logits to host
@@ -1558,6 +1566,9 @@ def main_decode(args, rank, world, local):
             "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": 8,
                     "d2h_bytes_per_step": c["vocab"] * 4 + 4},
             "gpu_launches": kernels * args.steps, "clocks": clk,
+            "repeat_windows": {"n": len(windows), "steps_each": args.steps,
+                               "tok_s": [world * 1e3 * args.steps / w for w in windows],
+                               "spread_pct": 100.0 * (max(windows) - min(windows)) / min(windows)},
             "spec_on": spec,
             "batch1_strong_scaling": batch1,
             "expert_gemv_config2": moe_sub,
