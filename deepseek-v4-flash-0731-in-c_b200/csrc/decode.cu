@@ -1118,24 +1118,51 @@ __global__ void __launch_bounds__(64) win_values_kernel(const WinAttnArgs a) {
   }
 }
 
-// The value pass for long key lists (a compressed layer's window +
-// compressed rows): CTA (head, 256-dim block), thread = dimension pair, the
-// two chains over the keys in key order as win_values_kernel, with the keys'
-// rows streamed through shared memory in chunks of kValKeys (coalesced
-// loads; the next chunk held in registers while this one is consumed).
+// The softmax and value pass for long key lists (a compressed layer's
+// window + compressed rows), one launch: CTA (head, 256-dim block). Each
+// CTA takes its head's max over the scores, the exponentials (ex) and
+// their BF16 weights into shared memory, as win_softmax_kernel; then thread
+// = dimension pair, the two value chains over the keys in key order with
+// the keys' rows streamed through shared memory in chunks of kValKeys
+// (coalesced loads; the next chunk held in registers while this one is
+// consumed). Warp 0 adds the denominator expf(sink - m) + ex[0] + ex[1] ...
+// in key order beside its chains (a dead key's ex is +0, which leaves the
+// sum as the reference's skip does: the sum starts positive or +0).
 constexpr int kValKeys = 32;
 constexpr int kValThreads = 128;  // 256 dims per CTA
+size_t win_values_long_smem(int n) {
+  return sizeof(float) * (2 * ((static_cast<size_t>(n) + 3) & ~static_cast<size_t>(3)) +
+                          kValKeys * 2 * kValThreads);
+}
 __global__ void __launch_bounds__(kValThreads) win_values_long_kernel(const WinAttnArgs a) {
-  extern __shared__ __align__(16) float vsm[];  // ws [n] | rows [kValKeys][2 * kValThreads]
+  extern __shared__ __align__(16) float vsm[];  // ws [n4] | ex [n4] | rows [kValKeys][256]
+  __shared__ float red[kValThreads / 32];
   pdl_wait();
   pdl_trigger();
-  const int h = blockIdx.x, tid = threadIdx.x;
-  const int n = a.n, d = a.d;
+  const int h = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int n = a.n, d = a.d, n4 = (n + 3) & ~3;
   const int cols = 2 * kValThreads;
   const int col0 = blockIdx.y * cols;
   float* ws = vsm;
-  float* rows = vsm + ((n + 3) & ~3);
-  for (int t = tid; t < n; t += kValThreads) ws[t] = a.w[static_cast<size_t>(h) * n + t];
+  float* ex = vsm + n4;
+  float* rows = ex + n4;
+  const float* sh = a.s + static_cast<size_t>(h) * n;
+  float mxl = -INFINITY;
+  for (int t = tid; t < n; t += kValThreads) mxl = fmaxf(mxl, sh[t]);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) mxl = fmaxf(mxl, __shfl_xor_sync(0xffffffffu, mxl, o));
+  if (lane == 0) red[warp] = mxl;
+  __syncthreads();
+  float mx = red[0];
+#pragma unroll
+  for (int w = 1; w < kValThreads / 32; ++w) mx = fmaxf(mx, red[w]);
+  for (int t = tid; t < n; t += kValThreads) {
+    const float st = sh[t];
+    const bool live = st != -INFINITY;
+    const float e = live ? expf_r1(st - mx) : 0.0f;
+    ex[t] = e;
+    ws[t] = live ? bf16_round(e) : 0.0f;
+  }
   // each thread moves kValKeys * cols / 4 / kValThreads float4 per chunk
   constexpr int kPer = kValKeys * 2 * kValThreads / 4 / kValThreads;  // 16
   float4 buf[kPer];
@@ -1154,25 +1181,40 @@ __global__ void __launch_bounds__(kValThreads) win_values_long_kernel(const WinA
   const int p = col0 / 2 + tid;  // this thread's dimension pair
   const bool live = 2 * p < d;
   float o0 = 0.0f, o1 = 0.0f;
+  float den = expf_r1(a.sink[h] - mx);
   for (int c0 = 0; c0 < n; c0 += kValKeys) {
-    __syncthreads();  // the previous chunk is consumed (and ws is in)
+    __syncthreads();  // the previous chunk is consumed (and ws, ex are in)
 #pragma unroll
     for (int k = 0; k < kPer; ++k)
       reinterpret_cast<float4*>(rows)[k * kValThreads + tid] = buf[k];
     __syncthreads();
     if (c0 + kValKeys < n) fetch(c0 + kValKeys);
     const int nk = min(kValKeys, n - c0);
+    if (warp == 0) {
 #pragma unroll 8
-    for (int t = 0; t < nk; ++t) {
-      const float2 kv = reinterpret_cast<const float2*>(rows + t * cols)[tid];
-      const float wt = ws[c0 + t];
-      o0 = fmaf(wt, kv.x, o0);
-      o1 = fmaf(wt, kv.y, o1);
+      for (int t = 0; t < nk; ++t) {
+        const float2 kv = reinterpret_cast<const float2*>(rows + t * cols)[tid];
+        const float wt = ws[c0 + t];
+        o0 = fmaf(wt, kv.x, o0);
+        o1 = fmaf(wt, kv.y, o1);
+        den = __fadd_rn(den, ex[c0 + t]);
+      }
+    } else {
+#pragma unroll 8
+      for (int t = 0; t < nk; ++t) {
+        const float2 kv = reinterpret_cast<const float2*>(rows + t * cols)[tid];
+        const float wt = ws[c0 + t];
+        o0 = fmaf(wt, kv.x, o0);
+        o1 = fmaf(wt, kv.y, o1);
+      }
     }
   }
+  if (warp == 0 && lane == 0) red[0] = den;
+  __syncthreads();
+  den = red[0];
+  if (blockIdx.y == 0 && tid == 0) a.den[h] = den;
   if (!live) return;
   const int i = 2 * p;
-  const float den = a.den[h];
   float x0 = bf16_round(o0 / den), x1 = bf16_round(o1 / den);
   const int start = d - a.rope_dim;
   if (a.cosv && i >= start) {
@@ -1634,42 +1676,26 @@ __global__ void comp_step_kernel(const CompStepArgs a) {
   if (tid == 0) *a.count = cnt + 1;
 }
 
-// The indexer's query (indexer_forward, :5699-5712): per head (CTA) the
-// BF16 output of idx_wq_b, RoPE of the compressed table at the position on
-// the head's last rope_dim dims, Hadamard, FP4 QAT; in place.
-__global__ void idx_query_kernel(float* q, int id, int rope_dim, const float* cosv,
-                                 const float* sinv) {
-  extern __shared__ float qsm[];  // [id]
-  pdl_trigger();
-  pdl_wait();
-  float* qh = q + static_cast<size_t>(blockIdx.x) * id;
-  for (int i = threadIdx.x; i < id; i += blockDim.x) qsm[i] = qh[i];
-  __syncthreads();
-  const int half = rope_dim / 2, start = id - rope_dim;
-  for (int i = threadIdx.x; i < half; i += blockDim.x) {
-    const float x0 = qsm[start + 2 * i], x1 = qsm[start + 2 * i + 1];
-    const float c = cosv[i], sn = sinv[i];
-    qsm[start + 2 * i] = bf16_round(__fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, sn)));
-    qsm[start + 2 * i + 1] = bf16_round(__fadd_rn(__fmul_rn(x0, sn), __fmul_rn(x1, c)));
-  }
-  hadamard_smem(qsm, id);
-  fp4_quant_smem(qsm, id);
-  for (int i = threadIdx.x; i < id; i += blockDim.x) qh[i] = qsm[i];
-}
-
-// Index scores (:5733-5747): score[t] = sum over heads h in order of
-// fmaf(relu(q_h . k_t), w_h, acc), the dot one fmaf chain over the head's
-// dims; w_h = bf16(bf16(proj_h) * (id^-1/2 * ih^-1/2)). CTA = kIdxT
-// compressed rows x ih heads (thread = (row, head) dot) with the query
-// transposed in shared memory ([dim][head]: a warp's heads on distinct
-// banks) and the CTA's keys beside it (broadcast), t < min(count, (pos+1)/4).
+// Index scores (indexer_forward, :5699-5747), one launch. Each CTA first
+// builds the indexer's query from the BF16 output of idx_wq_b: per head
+// the RoPE of the compressed table at the position on the head's last
+// rope_dim dims, the Hadamard transform and the FP4 QAT (the reference's
+// operations per element, every head at once; rows padded to id + 1 floats
+// so a warp's heads sit on distinct banks). Then score[t] = sum over heads h
+// in order of fmaf(relu(q_h . k_t), w_h, acc), the dot one fmaf chain over
+// the head's dims; w_h = bf16(bf16(proj_h) * (id^-1/2 * ih^-1/2)). CTA =
+// kIdxT compressed rows x ih heads (thread = (row, head) dot), the CTA's keys
+// in shared memory beside the query, t < min(count, (pos+1)/4).
 constexpr int kIdxT = 16;
 __global__ void idx_score_kernel(const float* q, const float* keys, const float* wproj, int ih,
-                                 int id, const int* count, const int* pos, float* score) {
+                                 int id, int rope_dim, const float* cosv, const float* sinv,
+                                 const int* count, const int* pos, float* score) {
   extern __shared__ float ism[];
-  float* qt = ism;                   // [id][ih]
-  float* kt = qt + id * ih;          // [kIdxT][id]
+  const int ld = id + 1;
+  float* qs = ism;                   // [ih][id + 1]
+  float* kt = qs + ih * ld;          // [kIdxT][id]
   float* dots = kt + kIdxT * id;     // [kIdxT][ih]
+  float* wh = dots + kIdxT * ih;     // [ih]
   pdl_trigger();
   pdl_wait();
   int nt = *count;
@@ -1677,34 +1703,96 @@ __global__ void idx_score_kernel(const float* q, const float* keys, const float*
   if (nt > maxc) nt = maxc;
   const int t0 = blockIdx.x * kIdxT;
   if (t0 >= nt) return;  // uniform over the CTA
-  const int nth = blockDim.x;
-  for (int i = threadIdx.x; i < ih * id; i += nth) {
-    const int h = i / id, dd = i % id;
-    qt[dd * ih + h] = q[i];
+  const int tid = threadIdx.x, nth = blockDim.x;
+  const int lane = tid & 31, warp = tid >> 5, nw = nth >> 5;
+  for (int i = tid; i < ih * id; i += nth) {
+    const int h = i / id, dd = i - h * id;
+    qs[h * ld + dd] = q[i];
   }
-  for (int i = threadIdx.x; i < kIdxT * id; i += nth) {
+  for (int i = tid; i < kIdxT * id; i += nth) {
     const int tl = i / id;
     kt[i] = t0 + tl < nt ? keys[static_cast<size_t>(t0) * id + i] : 0.0f;
   }
+  const float s = __fmul_rn(1.0f / sqrtf(static_cast<float>(id)), 1.0f / sqrtf(static_cast<float>(ih)));
+  // wproj: the BF16 GEMV's fp32 sums; the reference rounds them to BF16
+  // (round_out = 1) before the scale
+  for (int k = tid; k < ih; k += nth) wh[k] = bf16_round(__fmul_rn(bf16_round(wproj[k]), s));
   __syncthreads();
-  const int tl = threadIdx.x / ih, h = threadIdx.x % ih;
+  // RoPE (:5703)
+  const int half = rope_dim / 2, start = id - rope_dim;
+  for (int e = tid; e < ih * half; e += nth) {
+    const int h = e / half, i = e - h * half;
+    float* x = qs + h * ld + start + 2 * i;
+    const float x0 = x[0], x1 = x[1];
+    const float c = cosv[i], sn = sinv[i];
+    x[0] = bf16_round(__fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, sn)));
+    x[1] = bf16_round(__fadd_rn(__fmul_rn(x0, sn), __fmul_rn(x1, c)));
+  }
+  // Hadamard (dsv4_hadamard_inplace): the butterflies stage by stage, then
+  // x / sqrt(id) to BF16
+  const int hb = id / 2;
+  for (int len = 1; len < id; len <<= 1) {
+    __syncthreads();
+    for (int e = tid; e < ih * hb; e += nth) {
+      const int h = e / hb, k = e - h * hb;
+      const int i = (k / len) * 2 * len + (k % len);
+      float* x = qs + h * ld;
+      const float u = x[i], v = x[i + len];
+      x[i] = __fadd_rn(u, v);
+      x[i + len] = __fsub_rn(u, v);
+    }
+  }
+  __syncthreads();
+  const float inv = 1.0f / sqrtf(static_cast<float>(id));
+  for (int e = tid; e < ih * id; e += nth) {
+    const int h = e / id, i = e - h * id;
+    qs[h * ld + i] = bf16_round(__fmul_rn(qs[h * ld + i], inv));
+  }
+  __syncthreads();
+  // FP4 QAT (dsv4_fp4_act_quant_inplace, mode 0): warp = a group of 32
+  {
+    const float mags[8] = {0.0f, 0.5f, 1.0f, 1.5f, 2.0f, 3.0f, 4.0f, 6.0f};
+    const int gph = id / 32;
+    for (int g = warp; g < ih * gph; g += nw) {
+      const int h = g / gph, j = (g - h * gph) * 32 + lane;
+      float* x = qs + h * ld + j;
+      const float v = *x;
+      float amax = warp_max(fabsf(v));
+      const float floor6 = 6.0f * __uint_as_float(1u << 23);  // 6 * 2^-126
+      if (amax < floor6) amax = floor6;
+      const float scale = pow2_ceil(__fmul_rn(amax, 1.0f / 6.0f));
+      const float rs = 1.0f / scale;
+      float qv = __fmul_rn(v, rs);
+      qv = qv > 6.0f ? 6.0f : (qv < -6.0f ? -6.0f : qv);
+      const float aq = fabsf(qv);
+      int idx = 0;
+      float best = aq;
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const float dd = fabsf(__fsub_rn(aq, mags[k]));
+        if (dd < best) { best = dd; idx = k; }
+        else if (dd == best && (k & 1) == 0) idx = k;
+      }
+      *x = bf16_round(__fmul_rn(qv < 0.0f ? -mags[idx] : mags[idx], scale));
+    }
+  }
+  __syncthreads();
+  const int tl = tid / ih, h = tid % ih;
   const int t = t0 + tl;
   if (tl < kIdxT && t < nt) {
     const float* kr = kt + tl * id;
+    const float* qh = qs + h * ld;
     float dot = 0.0f;
 #pragma unroll 8
-    for (int dd = 0; dd < id; ++dd) dot = fmaf(qt[dd * ih + h], kr[dd], dot);
+    for (int dd = 0; dd < id; ++dd) dot = fmaf(qh[dd], kr[dd], dot);
     if (dot < 0.0f) dot = 0.0f;
     dots[tl * ih + h] = dot;
   }
   __syncthreads();
   if (h == 0 && tl < kIdxT && t < nt) {
-    const float s = __fmul_rn(1.0f / sqrtf(static_cast<float>(id)), 1.0f / sqrtf(static_cast<float>(ih)));
     float acc = 0.0f;
-    // wproj: the BF16 GEMV's fp32 sums; the reference rounds them to BF16
-    // (round_out = 1) before the scale
-    for (int k = 0; k < ih; ++k)
-      acc = fmaf(dots[tl * ih + k], bf16_round(__fmul_rn(bf16_round(wproj[k]), s)), acc);
+#pragma unroll 8
+    for (int k = 0; k < ih; ++k) acc = fmaf(dots[tl * ih + k], wh[k], acc);
     score[t] = acc;
   }
 }
@@ -1714,59 +1802,105 @@ __global__ void idx_score_kernel(const float* q, const float* keys, const float*
 // indexer's top-k for ratio 4 (dsv4_indexer_select_topk, :5636-5679: score
 // descending, lower index first, k = min(index_topk, n)) or every compressed
 // row in order for ratio 128 (:5330-5336) - then -1 padding to n_max. Rows
-// are row0 + compressed index. One CTA; the ratio-4 selection sorts the
-// scores (bitonic, n2 a power of two >= the most compressed rows) in shared
-// memory.
-__global__ void comp_list_kernel(const int* win_idx, int win, const float* score, const int* count,
-                                 const int* pos, int ratio, int topk, long long row0, int n2,
-                                 int n_max, int* out) {
+// are row0 + compressed index. One CTA of kListThreads; the ratio-4
+// selection sorts the n scores with a bitonic network over the next power of
+// two >= n: while that fits the CTA, one key per thread in registers
+// (partners within a warp by shuffle, farther ones through a double-buffered
+// shared array, one barrier per stage); beyond it, in shared memory over n2
+// (a power of two >= the most compressed rows). The order is a strict total
+// order on the keys (indices are distinct), so both forms give the order.
+constexpr int kListThreads = 1024;
+size_t comp_list_smem(int n2) {
+  return sizeof(float) * std::max(2 * n2, 4 * kListThreads);
+}
+__device__ __forceinline__ bool topk_before(float sa, int ia, float sb, int ib) {
+  // real before padding (-1); higher score first; lower index first
+  if (ib < 0) return ia >= 0;
+  if (ia < 0) return false;
+  if (sa > sb) return true;
+  if (sa < sb) return false;
+  return ia < ib;
+}
+__global__ void __launch_bounds__(kListThreads)
+comp_list_kernel(const int* win_idx, int win, const float* score, const int* count, const int* pos,
+                 int ratio, int topk, long long row0, int n2, int n_max, int* out) {
   extern __shared__ unsigned char lsm[];
-  float* ks = reinterpret_cast<float*>(lsm);
-  int* ki = reinterpret_cast<int*>(ks + n2);
   pdl_trigger();
   pdl_wait();
   const int tid = threadIdx.x, nt = blockDim.x;
   for (int i = tid; i < win; i += nt) out[i] = win_idx[i];
   int n = *count;
   int k = n;
-  if (ratio == 4) {
-    const int maxc = (*pos + 1) / 4;
-    if (n > maxc) n = maxc;
-    k = topk < n ? topk : n;
-    for (int i = tid; i < n2; i += nt) {
-      ks[i] = i < n ? score[i] : 0.0f;
-      ki[i] = i < n ? i : -1;  // -1: padding, after every real row
-    }
-    // "a before b": real before padding; higher score first; lower index first
-    auto before = [&](int i, int j) {
-      if (ki[j] < 0) return ki[i] >= 0;
-      if (ki[i] < 0) return false;
-      if (ks[i] > ks[j]) return true;
-      if (ks[i] < ks[j]) return false;
-      return ki[i] < ki[j];
-    };
-    for (int size = 2; size <= n2; size <<= 1)
+  if (ratio != 4) {
+    for (int i = tid; i < n_max - win; i += nt) out[win + i] = i < k ? static_cast<int>(row0 + i) : -1;
+    return;
+  }
+  const int maxc = (*pos + 1) / 4;
+  if (n > maxc) n = maxc;
+  k = topk < n ? topk : n;
+  int m2 = 32;
+  while (m2 < n) m2 <<= 1;
+  if (m2 <= nt) {
+    float* bs = reinterpret_cast<float*>(lsm);        // [2][nt]
+    int* bi = reinterpret_cast<int*>(bs + 2 * nt);     // [2][nt]
+    float sv = tid < n ? score[tid] : 0.0f;
+    int iv = tid < n ? tid : -1;
+    int stage = 0;
+    for (int size = 2; size <= m2; size <<= 1)
       for (int stride = size >> 1; stride > 0; stride >>= 1) {
-        __syncthreads();
-        for (int i = tid; i < n2; i += nt) {
-          const int j = i ^ stride;
-          if (j > i) {
-            const bool up = (i & size) == 0;
-            const bool swap = up ? before(j, i) : before(i, j);
-            if (swap) {
-              const float tf = ks[i]; ks[i] = ks[j]; ks[j] = tf;
-              const int ti = ki[i]; ki[i] = ki[j]; ki[j] = ti;
-            }
+        float so;
+        int io;
+        if (stride >= 32) {
+          float* ws_ = bs + (stage & 1) * nt;
+          int* wi_ = bi + (stage & 1) * nt;
+          ws_[tid] = sv;
+          wi_[tid] = iv;
+          __syncthreads();
+          so = ws_[tid ^ stride];
+          io = wi_[tid ^ stride];
+          ++stage;
+        } else {
+          so = __shfl_xor_sync(0xffffffffu, sv, stride);
+          io = __shfl_xor_sync(0xffffffffu, iv, stride);
+        }
+        if (tid < m2) {
+          const bool up = (tid & size) == 0, lower = (tid & stride) == 0;
+          const bool mine_first = topk_before(sv, iv, so, io);
+          if (lower == up ? !mine_first : mine_first) {
+            sv = so;
+            iv = io;
           }
         }
       }
-    __syncthreads();
+    for (int i = tid; i < n_max - win; i += nt)
+      out[win + i] = i < k ? static_cast<int>(row0 + (i == tid ? iv : 0)) : -1;
+    return;
   }
-  for (int i = tid; i < n_max - win; i += nt) {
-    int v = -1;
-    if (i < k) v = static_cast<int>(row0 + (ratio == 4 ? ki[i] : i));
-    out[win + i] = v;
+  float* ks = reinterpret_cast<float*>(lsm);
+  int* ki = reinterpret_cast<int*>(ks + n2);
+  for (int i = tid; i < n2; i += nt) {
+    ks[i] = i < n ? score[i] : 0.0f;
+    ki[i] = i < n ? i : -1;  // -1: padding, after every real row
   }
+  for (int size = 2; size <= n2; size <<= 1)
+    for (int stride = size >> 1; stride > 0; stride >>= 1) {
+      __syncthreads();
+      for (int i = tid; i < n2; i += nt) {
+        const int j = i ^ stride;
+        if (j > i) {
+          const bool up = (i & size) == 0;
+          const bool swap = up ? topk_before(ks[j], ki[j], ks[i], ki[i])
+                               : topk_before(ks[i], ki[i], ks[j], ki[j]);
+          if (swap) {
+            const float tf = ks[i]; ks[i] = ks[j]; ks[j] = tf;
+            const int ti = ki[i]; ki[i] = ki[j]; ki[j] = ti;
+          }
+        }
+      }
+    }
+  __syncthreads();
+  for (int i = tid; i < n_max - win; i += nt)
+    out[win + i] = i < k ? static_cast<int>(row0 + ki[i]) : -1;
 }
 
 // Greedy acceptance of a verify step (the reference CLI's chain,
@@ -2371,9 +2505,9 @@ cudaError_t attention(dsv4cuda_decoder* D, dsv4::Layer& L, cudaStream_t st) {
 }
 
 size_t idx_score_smem(const dsv4cuda_decoder_config& c) {
-  return sizeof(float) * (static_cast<size_t>(c.index_dim) * c.index_heads +
+  return sizeof(float) * (static_cast<size_t>(c.index_dim + 1) * c.index_heads +
                           static_cast<size_t>(dsv4::kIdxT) * c.index_dim +
-                          static_cast<size_t>(dsv4::kIdxT) * c.index_heads);
+                          static_cast<size_t>(dsv4::kIdxT) * c.index_heads + c.index_heads);
 }
 
 // A BF16 projection of the layer input D->x (one token) into y.
@@ -2476,37 +2610,39 @@ cudaError_t attention_comp(dsv4cuda_decoder* D, dsv4::Layer& L, cudaStream_t st)
   qt.xs = D->xs;
   DEC_CHECK(dsv4::launch_pdl(dsv4::norm_tail_kernel, dim3(2), dim3(256),
                              sizeof(float) * std::max(d, ql), st, kt, qt));
-  DEC_CHECK(fp8_gemv(w.wq_b, w.wq_b_s, ql, H * d, D->xq, D->xs, D->ld, D->q, D->item1, D->n_one,
-                     D->fp8_part, D->tile_cnt, st));
+  // wq_b, and for ratio 4 the indexer's query projection of the same
+  // quantised q latent, in one split-K launch
+  if (L.ratio == 4)
+    DEC_CHECK(fp8_gemv2(w.wq_b, w.wq_b_s, H * d, D->q, w.idx_wq_b, w.idx_wq_b_s,
+                        c.index_heads * c.index_dim, D->idx_q, ql, D->xq, D->xs, D->ld, D->item1,
+                        D->n_one, D->fp8_part, D->tile_cnt, st));
+  else
+    DEC_CHECK(fp8_gemv(w.wq_b, w.wq_b_s, ql, H * d, D->xq, D->xs, D->ld, D->q, D->item1, D->n_one,
+                       D->fp8_part, D->tile_cnt, st));
   // compressor_update of the main compressor (its row into the cache)
   DEC_CHECK(cudaStreamWaitEvent(st, D->comp_join, 0));
   DEC_CHECK(comp_step(D, L, false, w.comp_ape, w.comp_norm, p_kv, p_sc, st));
   const int* win_idx = D->idx;
   if (L.ratio == 4) {
     const int ih = c.index_heads, id = c.index_dim;
-    // the indexer's query from the quantised q latent (still in D->xq)
-    DEC_CHECK(fp8_gemv(w.idx_wq_b, w.idx_wq_b_s, ql, ih * id, D->xq, D->xs, D->ld, D->idx_q,
-                       D->item1, D->n_one, D->fp8_part, D->tile_cnt, st));
     DEC_CHECK(comp_step(D, L, true, w.idx_ape, w.idx_comp_norm, p_ikv, p_isc, st));
-    DEC_CHECK(dsv4::launch_pdl(dsv4::idx_query_kernel, dim3(ih), dim3(std::max(32, std::min(1024, id))),
-                               sizeof(float) * id, st, D->idx_q, id, c.rope_dim,
-                               static_cast<const float*>(D->cosv_c),
-                               static_cast<const float*>(D->sinv_c)));
     DEC_CHECK(dsv4::launch_pdl(dsv4::idx_score_kernel,
                                dim3((L.max_count + dsv4::kIdxT - 1) / dsv4::kIdxT),
                                dim3(dsv4::kIdxT * ih), idx_score_smem(c), st,
                                static_cast<const float*>(D->idx_q),
-                               static_cast<const float*>(L.idx_rows), p_iw, ih, id,
+                               static_cast<const float*>(L.idx_rows), p_iw, ih, id, c.rope_dim,
+                               static_cast<const float*>(D->cosv_c),
+                               static_cast<const float*>(D->sinv_c),
                                static_cast<const int*>(L.idx_count),
                                static_cast<const int*>(D->d_pos), D->idx_score));
-    DEC_CHECK(dsv4::launch_pdl(dsv4::comp_list_kernel, dim3(1), dim3(1024),
-                               sizeof(float) * 2 * D->idx_n2, st, win_idx, c.window,
+    DEC_CHECK(dsv4::launch_pdl(dsv4::comp_list_kernel, dim3(1), dim3(dsv4::kListThreads),
+                               dsv4::comp_list_smem(D->idx_n2), st, win_idx, c.window,
                                static_cast<const float*>(D->idx_score),
                                static_cast<const int*>(L.idx_count),
                                static_cast<const int*>(D->d_pos), 4, c.index_topk, L.comp_row0,
                                D->idx_n2, L.n_keys, D->idx_full));
   } else {
-    DEC_CHECK(dsv4::launch_pdl(dsv4::comp_list_kernel, dim3(1), dim3(1024), 0, st, win_idx,
+    DEC_CHECK(dsv4::launch_pdl(dsv4::comp_list_kernel, dim3(1), dim3(dsv4::kListThreads), 0, st, win_idx,
                                c.window, static_cast<const float*>(nullptr),
                                static_cast<const int*>(L.count),
                                static_cast<const int*>(D->d_pos), L.ratio, 0, L.comp_row0, 0,
@@ -2543,12 +2679,9 @@ cudaError_t attention_comp(dsv4cuda_decoder* D, dsv4::Layer& L, cudaStream_t st)
       dsv4::win_scores_kernel,
       dim3((H + dsv4::kWinHeads - 1) / dsv4::kWinHeads, (L.n_keys + dsv4::kWinKeys - 1) / dsv4::kWinKeys),
       dim3(dsv4::kWinHeads * 32), sizeof(float) * (dsv4::kWinHeads + dsv4::kWinKeys) * d, st, wa));
-  DEC_CHECK(dsv4::launch_pdl(dsv4::win_softmax_kernel, dim3(H), dim3(256),
-                             sizeof(float) * L.n_keys, st, wa));
   DEC_CHECK(dsv4::launch_pdl(
       dsv4::win_values_long_kernel, dim3(H, (d + 2 * dsv4::kValThreads - 1) / (2 * dsv4::kValThreads)),
-      dim3(dsv4::kValThreads),
-      sizeof(float) * (((L.n_keys + 3) & ~3) + dsv4::kValKeys * 2 * dsv4::kValThreads), st, wa));
+      dim3(dsv4::kValThreads), dsv4::win_values_long_smem(L.n_keys), st, wa));
   dsv4::Bf16GemvArgs ga{};
   ga.W = L.wo_a;
   ga.w_stride = static_cast<size_t>(ol) * (H * d / G);
@@ -2700,9 +2833,11 @@ bool comp_alloc(dsv4cuda_decoder* D) {
                                  static_cast<int>(sizeof(float) * (dsv4::kWinHeads + dsv4::kWinKeys) *
                                                   c.head_dim)) != cudaSuccess ||
       dsv4::set_max_dynamic_smem(reinterpret_cast<const void*>(dsv4::comp_list_kernel),
-                                 static_cast<int>(sizeof(float) * 2 * std::max(D->idx_n2, 1))) != cudaSuccess ||
+                                 static_cast<int>(dsv4::comp_list_smem(D->idx_n2))) != cudaSuccess ||
       dsv4::set_max_dynamic_smem(reinterpret_cast<const void*>(dsv4::idx_score_kernel),
                                  static_cast<int>(idx_score_smem(c))) != cudaSuccess ||
+      dsv4::set_max_dynamic_smem(reinterpret_cast<const void*>(dsv4::win_values_long_kernel),
+                                 static_cast<int>(dsv4::win_values_long_smem(D->n_max))) != cudaSuccess ||
       comp_reset(D, nullptr) != cudaSuccess) {
     D->err = "set-up failed";
     return false;
@@ -3049,7 +3184,10 @@ DSV4_API int dsv4cuda_decoder_create(dsv4cuda_decoder** out, const dsv4cuda_deco
   chk(D->kvdec = dalloc<float>(D, static_cast<size_t>(c.window) * d));
   chk(D->kvt = dalloc<float>(D, static_cast<size_t>(c.window) * d));
   {
-    const size_t hid = c.hidden, ql = c.q_lora, hd = static_cast<size_t>(H) * d;
+    const size_t hid = c.hidden, ql = c.q_lora;
+    // wq_b's rows, with the indexer's query projection stacked after them
+    const size_t hd = static_cast<size_t>(H) * d +
+                      static_cast<size_t>(std::max(0, c.index_heads)) * std::max(0, c.index_dim);
     const size_t go = static_cast<size_t>(c.o_groups) * c.o_lora;
     const size_t np = std::max(std::max((hid + 127) / 128 * (ql + d), (ql + 127) / 128 * hd),
                                (go + 127) / 128 * hid);
