@@ -1230,6 +1230,151 @@ __global__ void __launch_bounds__(kValThreads) win_values_long_kernel(const WinA
   oh[i + 1] = x1;
 }
 
+// 16-byte global -> shared copies that bypass the registers (cp.async,
+// L2 only), and the wait for every copy this thread issued.
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+  const unsigned sa = static_cast<unsigned>(__cvta_generic_to_shared(dst));
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(sa), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+  asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
+}
+
+// Scores for long key lists (a compressed layer's window + compressed
+// rows): CTA = kWinHeads heads (warps) x kWinKeys keys (lanes), as
+// win_scores_kernel, with the heads' q rows and the keys' decoded rows
+// (kvdec [n][d], rows padded to d + 4 floats: a quarter-warp's 16-byte reads
+// of 8 rows hit distinct banks) copied to shared memory by cp.async, all in
+// flight together. Each thread runs its (head, key) dot as one fmaf chain in
+// dimension order, four dimensions per pair of shared-memory reads, times
+// the scale. Needs d % 4 == 0.
+size_t win_scores_rows_smem(int d) {
+  return sizeof(float) * (static_cast<size_t>(kWinHeads) * d + static_cast<size_t>(kWinKeys) * (d + 4));
+}
+__global__ void __launch_bounds__(kWinHeads * 32) win_scores_rows_kernel(const WinAttnArgs a) {
+  extern __shared__ __align__(16) float rsm[];  // q [kWinHeads][d] | k [kWinKeys][d + 4]
+  pdl_wait();
+  pdl_trigger();
+  const int h0 = blockIdx.x * kWinHeads, t0 = blockIdx.y * kWinKeys;
+  const int d = a.d, kd = d + 4, d4 = d / 4;
+  float* qs = rsm;
+  float* ks = rsm + kWinHeads * d;
+  const int nh = min(kWinHeads, a.H - h0), nk = min(kWinKeys, a.n - t0);
+  for (int e = threadIdx.x; e < nh * d4; e += blockDim.x) {
+    const int hh = e / d4, i4 = e - hh * d4;
+    cp_async16(qs + hh * d + 4 * i4, a.q + static_cast<size_t>(h0 + hh) * d + 4 * i4);
+  }
+  for (int e = threadIdx.x; e < nk * d4; e += blockDim.x) {
+    const int tl = e / d4, i4 = e - tl * d4;
+    cp_async16(ks + tl * kd + 4 * i4, a.kvdec + static_cast<size_t>(t0 + tl) * d + 4 * i4);
+  }
+  cp_async_wait_all();
+  __syncthreads();
+  const int lane = threadIdx.x & 31, hw = threadIdx.x >> 5;
+  const int h = h0 + hw, t = t0 + lane;
+  if (hw >= nh || lane >= nk) return;
+  float st = -INFINITY;
+  const int r = a.idx[t];
+  if (r >= 0 && r < a.cache.rows) {
+    const float4* q4 = reinterpret_cast<const float4*>(qs + hw * d);
+    const float4* k4 = reinterpret_cast<const float4*>(ks + lane * kd);
+    float dot = 0.0f;
+#pragma unroll 8
+    for (int i = 0; i < d4; ++i) {
+      const float4 qv = q4[i], kv = k4[i];
+      dot = fmaf(qv.x, kv.x, dot);
+      dot = fmaf(qv.y, kv.y, dot);
+      dot = fmaf(qv.z, kv.z, dot);
+      dot = fmaf(qv.w, kv.w, dot);
+    }
+    st = __fmul_rn(dot, a.scale);
+  }
+  a.s[static_cast<size_t>(h) * a.n + t] = st;
+}
+
+// The same softmax and value pass with several heads per CTA, for key lists
+// that fit shared memory: CTA (kVhHeads heads, kVhCols dims). The keys'
+// kVhCols-column slice of kvdec [n][d] is copied to shared memory once
+// (cp.async, every copy in flight together) and serves the CTA's heads, so
+// L2 delivers each key row slice once per head group instead of once per
+// head. While the copies land, warp w takes heads w, w + 4, ...: the max,
+// the exponentials (ex) and the BF16 weights (ws), as win_softmax_kernel.
+// Then thread = (head, dimension pair): the two value chains over the keys
+// in key order and the head's denominator expf(sink - m) + ex[0] + ... in
+// key order (a dead key's ex is +0, which leaves the sum unchanged, as the
+// reference's skip does), the division, BF16, the inverse RoPE.
+constexpr int kVhHeads = 8, kVhCols = 32;
+constexpr int kVhThreads = kVhHeads * kVhCols / 2;  // 128
+size_t win_values_mh_smem(int n) {
+  const size_t n4 = (static_cast<size_t>(n) + 3) & ~static_cast<size_t>(3);
+  return sizeof(float) * (n4 * kVhCols + 2 * kVhHeads * (n4 + 1));
+}
+__global__ void __launch_bounds__(kVhThreads) win_values_mh_kernel(const WinAttnArgs a) {
+  extern __shared__ __align__(16) float msm[];  // kv [n4][kVhCols] | ws [kVhHeads][n4 + 1] | ex
+  __shared__ float mxs[kVhHeads];
+  pdl_wait();
+  pdl_trigger();
+  const int n = a.n, d = a.d, n4 = (n + 3) & ~3, ns = n4 + 1;
+  const int h0 = blockIdx.x * kVhHeads, col0 = blockIdx.y * kVhCols;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  float* kv = msm;
+  float* ws = kv + static_cast<size_t>(n4) * kVhCols;
+  float* ex = ws + kVhHeads * ns;
+  for (int e = tid; e < n * (kVhCols / 4); e += kVhThreads) {
+    const int t = e / (kVhCols / 4), c4 = e - t * (kVhCols / 4);
+    cp_async16(kv + t * kVhCols + 4 * c4, a.kvdec + static_cast<size_t>(t) * d + col0 + 4 * c4);
+  }
+  for (int hh = warp; hh < kVhHeads; hh += kVhThreads / 32) {
+    const int h = h0 + hh;
+    if (h >= a.H) continue;
+    const float* sh = a.s + static_cast<size_t>(h) * n;
+    float mx = -INFINITY;
+    for (int t = lane; t < n; t += 32) mx = fmaxf(mx, sh[t]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    for (int t = lane; t < n; t += 32) {
+      const float st = sh[t];
+      const bool live = st != -INFINITY;
+      const float e = live ? expf_r1(st - mx) : 0.0f;
+      ex[hh * ns + t] = e;
+      ws[hh * ns + t] = live ? bf16_round(e) : 0.0f;
+    }
+    if (lane == 0) mxs[hh] = mx;
+  }
+  cp_async_wait_all();
+  __syncthreads();
+  const int hh = tid / (kVhCols / 2), p = tid - hh * (kVhCols / 2);
+  const int h = h0 + hh;
+  if (h >= a.H) return;
+  const float* wr = ws + hh * ns;
+  const float* er = ex + hh * ns;
+  float o0 = 0.0f, o1 = 0.0f;
+  float den = expf_r1(a.sink[h] - mxs[hh]);
+#pragma unroll 4
+  for (int t = 0; t < n; ++t) {
+    const float2 v = *reinterpret_cast<const float2*>(kv + t * kVhCols + 2 * p);
+    const float wt = wr[t];
+    o0 = fmaf(wt, v.x, o0);
+    o1 = fmaf(wt, v.y, o1);
+    den = __fadd_rn(den, er[t]);
+  }
+  if (blockIdx.y == 0 && p == 0) a.den[h] = den;
+  const int i = col0 + 2 * p;
+  float x0 = bf16_round(o0 / den), x1 = bf16_round(o1 / den);
+  const int start = d - a.rope_dim;
+  if (a.cosv && i >= start) {
+    const int k = (i - start) / 2;
+    const float c = a.cosv[k], sn = a.sinv[k];
+    const float y0 = bf16_round(__fadd_rn(__fmul_rn(x0, c), __fmul_rn(x1, sn)));
+    const float y1 = bf16_round(__fadd_rn(__fmul_rn(-x0, sn), __fmul_rn(x1, c)));
+    x0 = y0;
+    x1 = y1;
+  }
+  float* oh = a.out + static_cast<size_t>(h) * d;
+  oh[i] = x0;
+  oh[i + 1] = x1;
+}
+
 __device__ __forceinline__ void bf16x8_to_f32(const uint4 u, float (&f)[8]) {
   const uint32_t w[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
@@ -1676,16 +1821,100 @@ __global__ void comp_step_kernel(const CompStepArgs a) {
   if (tid == 0) *a.count = cnt + 1;
 }
 
+// The indexer's query of one head (indexer_forward, :5699-5712) built by
+// one warp in registers: lane holds values lane * V .. lane * V + V - 1 of
+// the head's id = 32 V. The RoPE of the compressed table at the position on
+// the last rope_dim dims (pairs inside a lane, or across a lane pair for
+// V = 1), the Hadamard butterflies stage by stage (partners inside a lane
+// while the stride is below V, else by shuffle), x / sqrt(id) to BF16, and
+// the FP4 QAT per 32 values (32 / V lanes per group): the reference's
+// operations per element. The result goes to out[0 .. id).
+template <int V>
+__device__ __forceinline__ void idx_query_warp(const float* src, float* out, int id, int rope_dim,
+                                               const float* cosv, const float* sinv, int lane) {
+  float x[V];
+#pragma unroll
+  for (int r = 0; r < V; ++r) x[r] = src[lane * V + r];
+  const int start = id - rope_dim;
+  if constexpr (V >= 2) {
+#pragma unroll
+    for (int r = 0; r < V; r += 2) {
+      const int j = lane * V + r;
+      if (j >= start) {
+        const int i = (j - start) >> 1;
+        const float x0 = x[r], x1 = x[r + 1], c = cosv[i], sn = sinv[i];
+        x[r] = bf16_round(__fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, sn)));
+        x[r + 1] = bf16_round(__fadd_rn(__fmul_rn(x0, sn), __fmul_rn(x1, c)));
+      }
+    }
+  } else {
+    const float other = __shfl_xor_sync(0xffffffffu, x[0], 1);
+    if (lane >= start) {
+      const int i = (lane - start) >> 1;
+      const bool odd = lane & 1;
+      const float x0 = odd ? other : x[0], x1 = odd ? x[0] : other;
+      const float c = cosv[i], sn = sinv[i];
+      x[0] = odd ? bf16_round(__fadd_rn(__fmul_rn(x0, sn), __fmul_rn(x1, c)))
+                 : bf16_round(__fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, sn)));
+    }
+  }
+#pragma unroll
+  for (int len = 1; len < V; len <<= 1)
+#pragma unroll
+    for (int r = 0; r < V; ++r)
+      if ((r & len) == 0) {
+        const float u = x[r], v = x[r + len];
+        x[r] = __fadd_rn(u, v);
+        x[r + len] = __fsub_rn(u, v);
+      }
+  for (int lm = 1; lm < 32; lm <<= 1) {  // lane stride lm = len / V
+    const bool upper = (lane & lm) != 0;
+#pragma unroll
+    for (int r = 0; r < V; ++r) {
+      const float o = __shfl_xor_sync(0xffffffffu, x[r], lm);
+      x[r] = upper ? __fsub_rn(o, x[r]) : __fadd_rn(x[r], o);
+    }
+  }
+  const float inv = 1.0f / sqrtf(static_cast<float>(id));
+  float amax = 0.0f;
+#pragma unroll
+  for (int r = 0; r < V; ++r) {
+    x[r] = bf16_round(__fmul_rn(x[r], inv));
+    amax = fmaxf(amax, fabsf(x[r]));
+  }
+#pragma unroll
+  for (int o = 1; o < 32 / V; o <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+  const float floor6 = 6.0f * __uint_as_float(1u << 23);  // 6 * 2^-126
+  if (amax < floor6) amax = floor6;
+  const float scale = pow2_ceil(__fmul_rn(amax, 1.0f / 6.0f));
+  const float rs = 1.0f / scale;
+  const float mags[8] = {0.0f, 0.5f, 1.0f, 1.5f, 2.0f, 3.0f, 4.0f, 6.0f};
+#pragma unroll
+  for (int r = 0; r < V; ++r) {
+    float qv = __fmul_rn(x[r], rs);
+    qv = qv > 6.0f ? 6.0f : (qv < -6.0f ? -6.0f : qv);
+    const float aq = fabsf(qv);
+    int idx = 0;
+    float best = aq;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const float dd = fabsf(__fsub_rn(aq, mags[k]));
+      if (dd < best) { best = dd; idx = k; }
+      else if (dd == best && (k & 1) == 0) idx = k;
+    }
+    out[lane * V + r] = bf16_round(__fmul_rn(qv < 0.0f ? -mags[idx] : mags[idx], scale));
+  }
+}
+
 // Index scores (indexer_forward, :5699-5747), one launch. Each CTA first
-// builds the indexer's query from the BF16 output of idx_wq_b: per head
-// the RoPE of the compressed table at the position on the head's last
-// rope_dim dims, the Hadamard transform and the FP4 QAT (the reference's
-// operations per element, every head at once; rows padded to id + 1 floats
-// so a warp's heads sit on distinct banks). Then score[t] = sum over heads h
-// in order of fmaf(relu(q_h . k_t), w_h, acc), the dot one fmaf chain over
-// the head's dims; w_h = bf16(bf16(proj_h) * (id^-1/2 * ih^-1/2)). CTA =
-// kIdxT compressed rows x ih heads (thread = (row, head) dot), the CTA's keys
-// in shared memory beside the query, t < min(count, (pos+1)/4).
+// builds the indexer's query from the BF16 output of idx_wq_b (a warp per
+// head, idx_query_warp) into shared memory, rows padded to id + 1 floats so
+// a warp's heads sit on distinct banks. Then score[t] = sum over heads h in
+// order of fmaf(relu(q_h . k_t), w_h, acc), the dot one fmaf chain over the
+// head's dims; w_h = bf16(bf16(proj_h) * (id^-1/2 * ih^-1/2)). CTA = kIdxT
+// compressed rows x ih heads (thread = (row, head) dot), the CTA's keys in
+// shared memory beside the query, t < min(count, (pos+1)/4). id = 32 V with
+// V in {1, 2, 4, 8}.
 constexpr int kIdxT = 16;
 __global__ void idx_score_kernel(const float* q, const float* keys, const float* wproj, int ih,
                                  int id, int rope_dim, const float* cosv, const float* sinv,
@@ -1705,10 +1934,6 @@ __global__ void idx_score_kernel(const float* q, const float* keys, const float*
   if (t0 >= nt) return;  // uniform over the CTA
   const int tid = threadIdx.x, nth = blockDim.x;
   const int lane = tid & 31, warp = tid >> 5, nw = nth >> 5;
-  for (int i = tid; i < ih * id; i += nth) {
-    const int h = i / id, dd = i - h * id;
-    qs[h * ld + dd] = q[i];
-  }
   for (int i = tid; i < kIdxT * id; i += nth) {
     const int tl = i / id;
     kt[i] = t0 + tl < nt ? keys[static_cast<size_t>(t0) * id + i] : 0.0f;
@@ -1717,63 +1942,14 @@ __global__ void idx_score_kernel(const float* q, const float* keys, const float*
   // wproj: the BF16 GEMV's fp32 sums; the reference rounds them to BF16
   // (round_out = 1) before the scale
   for (int k = tid; k < ih; k += nth) wh[k] = bf16_round(__fmul_rn(bf16_round(wproj[k]), s));
-  __syncthreads();
-  // RoPE (:5703)
-  const int half = rope_dim / 2, start = id - rope_dim;
-  for (int e = tid; e < ih * half; e += nth) {
-    const int h = e / half, i = e - h * half;
-    float* x = qs + h * ld + start + 2 * i;
-    const float x0 = x[0], x1 = x[1];
-    const float c = cosv[i], sn = sinv[i];
-    x[0] = bf16_round(__fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, sn)));
-    x[1] = bf16_round(__fadd_rn(__fmul_rn(x0, sn), __fmul_rn(x1, c)));
-  }
-  // Hadamard (dsv4_hadamard_inplace): the butterflies stage by stage, then
-  // x / sqrt(id) to BF16
-  const int hb = id / 2;
-  for (int len = 1; len < id; len <<= 1) {
-    __syncthreads();
-    for (int e = tid; e < ih * hb; e += nth) {
-      const int h = e / hb, k = e - h * hb;
-      const int i = (k / len) * 2 * len + (k % len);
-      float* x = qs + h * ld;
-      const float u = x[i], v = x[i + len];
-      x[i] = __fadd_rn(u, v);
-      x[i + len] = __fsub_rn(u, v);
-    }
-  }
-  __syncthreads();
-  const float inv = 1.0f / sqrtf(static_cast<float>(id));
-  for (int e = tid; e < ih * id; e += nth) {
-    const int h = e / id, i = e - h * id;
-    qs[h * ld + i] = bf16_round(__fmul_rn(qs[h * ld + i], inv));
-  }
-  __syncthreads();
-  // FP4 QAT (dsv4_fp4_act_quant_inplace, mode 0): warp = a group of 32
-  {
-    const float mags[8] = {0.0f, 0.5f, 1.0f, 1.5f, 2.0f, 3.0f, 4.0f, 6.0f};
-    const int gph = id / 32;
-    for (int g = warp; g < ih * gph; g += nw) {
-      const int h = g / gph, j = (g - h * gph) * 32 + lane;
-      float* x = qs + h * ld + j;
-      const float v = *x;
-      float amax = warp_max(fabsf(v));
-      const float floor6 = 6.0f * __uint_as_float(1u << 23);  // 6 * 2^-126
-      if (amax < floor6) amax = floor6;
-      const float scale = pow2_ceil(__fmul_rn(amax, 1.0f / 6.0f));
-      const float rs = 1.0f / scale;
-      float qv = __fmul_rn(v, rs);
-      qv = qv > 6.0f ? 6.0f : (qv < -6.0f ? -6.0f : qv);
-      const float aq = fabsf(qv);
-      int idx = 0;
-      float best = aq;
-#pragma unroll
-      for (int k = 0; k < 8; ++k) {
-        const float dd = fabsf(__fsub_rn(aq, mags[k]));
-        if (dd < best) { best = dd; idx = k; }
-        else if (dd == best && (k & 1) == 0) idx = k;
-      }
-      *x = bf16_round(__fmul_rn(qv < 0.0f ? -mags[idx] : mags[idx], scale));
+  for (int h = warp; h < ih; h += nw) {
+    const float* src = q + static_cast<size_t>(h) * id;
+    float* dst = qs + h * ld;
+    switch (id >> 5) {
+      case 1: idx_query_warp<1>(src, dst, id, rope_dim, cosv, sinv, lane); break;
+      case 2: idx_query_warp<2>(src, dst, id, rope_dim, cosv, sinv, lane); break;
+      case 4: idx_query_warp<4>(src, dst, id, rope_dim, cosv, sinv, lane); break;
+      default: idx_query_warp<8>(src, dst, id, rope_dim, cosv, sinv, lane); break;
     }
   }
   __syncthreads();
@@ -2043,6 +2219,7 @@ struct dsv4cuda_decoder {
   // and indexer, the key list and its staged rows
   bool any_comp = false;
   int n_max = 0;                   // keys of the longest list
+  size_t vmh_smem = 0;             // win_values_mh_kernel's shared memory limit (0: not used)
   int comp_rows_max = 0;           // rows of the largest stacked projection
   float *cosv_c = nullptr, *sinv_c = nullptr;
   float *cos_tab_c = nullptr, *sin_tab_c = nullptr;
@@ -2676,12 +2853,17 @@ cudaError_t attention_comp(dsv4cuda_decoder* D, dsv4::Layer& L, cudaStream_t st)
   DEC_CHECK(hc_join(D, st));
   DEC_CHECK(dsv4::launch_pdl(dsv4::win_decode_kernel, dim3(L.n_keys), dim3(128), 0, st, wa));
   DEC_CHECK(dsv4::launch_pdl(
-      dsv4::win_scores_kernel,
+      dsv4::win_scores_rows_kernel,
       dim3((H + dsv4::kWinHeads - 1) / dsv4::kWinHeads, (L.n_keys + dsv4::kWinKeys - 1) / dsv4::kWinKeys),
-      dim3(dsv4::kWinHeads * 32), sizeof(float) * (dsv4::kWinHeads + dsv4::kWinKeys) * d, st, wa));
-  DEC_CHECK(dsv4::launch_pdl(
-      dsv4::win_values_long_kernel, dim3(H, (d + 2 * dsv4::kValThreads - 1) / (2 * dsv4::kValThreads)),
-      dim3(dsv4::kValThreads), dsv4::win_values_long_smem(L.n_keys), st, wa));
+      dim3(dsv4::kWinHeads * 32), dsv4::win_scores_rows_smem(d), st, wa));
+  if (D->vmh_smem && dsv4::win_values_mh_smem(L.n_keys) <= D->vmh_smem)
+    DEC_CHECK(dsv4::launch_pdl(dsv4::win_values_mh_kernel,
+                               dim3((H + dsv4::kVhHeads - 1) / dsv4::kVhHeads, d / dsv4::kVhCols),
+                               dim3(dsv4::kVhThreads), dsv4::win_values_mh_smem(L.n_keys), st, wa));
+  else
+    DEC_CHECK(dsv4::launch_pdl(
+        dsv4::win_values_long_kernel, dim3(H, (d + 2 * dsv4::kValThreads - 1) / (2 * dsv4::kValThreads)),
+        dim3(dsv4::kValThreads), dsv4::win_values_long_smem(L.n_keys), st, wa));
   dsv4::Bf16GemvArgs ga{};
   ga.W = L.wo_a;
   ga.w_stride = static_cast<size_t>(ol) * (H * d / G);
@@ -2792,12 +2974,13 @@ cudaError_t comp_reset(dsv4cuda_decoder* D, cudaStream_t st) {
 bool comp_alloc(dsv4cuda_decoder* D) {
   const auto& c = D->cfg;
   const int half = c.rope_dim / 2;
-  if (c.index_heads <= 0 || c.index_dim < 32 || (c.index_dim & (c.index_dim - 1)) ||
-      c.index_dim % 32 || c.index_dim < c.rope_dim || c.index_heads * dsv4::kIdxT > 1024 ||
+  if (c.index_heads <= 0 || c.index_dim < 32 || c.index_dim > 256 ||
+      (c.index_dim & (c.index_dim - 1)) || c.index_dim < c.rope_dim ||
+      c.index_heads * dsv4::kIdxT > 1024 ||
       c.index_topk <= 0 || c.compress_rope_theta <= 0.f || c.rope_factor <= 0.f ||
       c.original_position <= 0 || D->idx_n2 > 8192 ||
       idx_score_smem(c) > 200 * 1024) {
-    D->err = "index heads / dim (a power of two >= 32 and >= rope_dim) / top-k or the YaRN "
+    D->err = "index heads / dim (a power of two in [32, 256], >= rope_dim) / top-k or the YaRN "
              "parameters out of range, or max_context too long for the top-k sort";
     return false;
   }
@@ -2819,6 +3002,11 @@ bool comp_alloc(dsv4cuda_decoder* D) {
     D->err = "out of device memory";
     return false;
   }
+  // the multi-head value pass while its shared-memory slice of the longest
+  // list fits 200 KB (the longer lists of ratio-128 layers at long contexts
+  // take win_values_long_kernel)
+  if (c.head_dim % dsv4::kVhCols == 0)
+    D->vmh_smem = std::min<size_t>(dsv4::win_values_mh_smem(D->n_max), 200 * 1024);
   if (cudaStreamCreateWithFlags(&D->comp_side, cudaStreamNonBlocking) != cudaSuccess ||
       cudaEventCreateWithFlags(&D->comp_fork, cudaEventDisableTiming) != cudaSuccess ||
       cudaEventCreateWithFlags(&D->comp_join, cudaEventDisableTiming) != cudaSuccess) {
@@ -2836,8 +3024,12 @@ bool comp_alloc(dsv4cuda_decoder* D) {
                                  static_cast<int>(dsv4::comp_list_smem(D->idx_n2))) != cudaSuccess ||
       dsv4::set_max_dynamic_smem(reinterpret_cast<const void*>(dsv4::idx_score_kernel),
                                  static_cast<int>(idx_score_smem(c))) != cudaSuccess ||
+      dsv4::set_max_dynamic_smem(reinterpret_cast<const void*>(dsv4::win_scores_rows_kernel),
+                                 static_cast<int>(dsv4::win_scores_rows_smem(c.head_dim))) != cudaSuccess ||
       dsv4::set_max_dynamic_smem(reinterpret_cast<const void*>(dsv4::win_values_long_kernel),
                                  static_cast<int>(dsv4::win_values_long_smem(D->n_max))) != cudaSuccess ||
+      (D->vmh_smem && dsv4::set_max_dynamic_smem(reinterpret_cast<const void*>(dsv4::win_values_mh_kernel),
+                                                 static_cast<int>(D->vmh_smem)) != cudaSuccess) ||
       comp_reset(D, nullptr) != cudaSuccess) {
     D->err = "set-up failed";
     return false;

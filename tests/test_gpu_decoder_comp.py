@@ -34,16 +34,28 @@ pytestmark = pytest.mark.gpu
 N_PROMPT, N_GEN = 140, 8
 
 
-def test_decoder_compressed_layers_vs_reference(cuda, tmp_path):
+# "t1": the latent of 80 dims and a 4 x 32 indexer (one query value per lane
+# in the score kernel; the single-head value pass). "dims128": a latent of
+# 128 dims with 64 RoPE dims and an 8 x 128 indexer, the benchmark's
+# per-head shapes in small (four query values per lane; the multi-head value
+# pass, whose 32-dim slices need a latent dim divisible by 32).
+SHAPES = {
+    "t1": dict(ratios=[4, 128], head_dim=80),
+    "dims128": dict(ratios=[4, 128], head_dim=128, rope=64, index_dim=128, index_heads=8),
+}
+
+
+@pytest.mark.parametrize("shape", sorted(SHAPES))
+def test_decoder_compressed_layers_vs_reference(cuda, tmp_path, shape):
     import make_tiny_t1
-    cfg = dict(make_tiny_t1.CFG, ratios=[4, 128], head_dim=80)
+    cfg = dict(make_tiny_t1.CFG, **SHAPES[shape])
     ckpt = make_tiny_t1.write(str(tmp_path / "t1c"), seed=5, c=cfg)
     ids = make_tiny_t1.prompt_ids(seed=5, n=N_PROMPT)
     want = reference_steps(ckpt, ids, N_GEN)
     dec = cuda.decoder_from_checkpoint(ckpt, max_context=N_PROMPT + N_GEN + 8, hc_exact=True)
     try:
         same, worst, agree, near = compare_decode(dec, ids, want, 0.0)
-        print(f"decoder T1 ratios 4/128 (exact): {same}/{N_GEN} steps bit-identical, "
+        print(f"decoder {shape} ratios 4/128 (exact): {same}/{N_GEN} steps bit-identical, "
               f"worst rel L2 {worst:.2e}, greedy {agree}/{N_GEN}")
         assert same == N_GEN and agree == N_GEN
     finally:
