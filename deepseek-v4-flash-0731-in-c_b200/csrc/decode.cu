@@ -1297,8 +1297,9 @@ __global__ void __launch_bounds__(kWinHeads * 32) win_scores_rows_kernel(const W
 // kVhCols-column slice of kvdec [n][d] is copied to shared memory once
 // (cp.async, every copy in flight together) and serves the CTA's heads, so
 // L2 delivers each key row slice once per head group instead of once per
-// head. While the copies land, warp w takes heads w, w + 4, ...: the max,
-// the exponentials (ex) and the BF16 weights (ws), as win_softmax_kernel.
+// head; the heads' scores [kVhHeads][n] come in beside them. Then warp w
+// takes heads w, w + 4, ...: the max, the exponentials (ex) and the BF16
+// weights (ws), as win_softmax_kernel.
 // Then thread = (head, dimension pair): the two value chains over the keys
 // in key order and the head's denominator expf(sink - m) + ex[0] + ... in
 // key order (a dead key's ex is +0, which leaves the sum unchanged, as the
@@ -1307,27 +1308,35 @@ constexpr int kVhHeads = 8, kVhCols = 32;
 constexpr int kVhThreads = kVhHeads * kVhCols / 2;  // 128
 size_t win_values_mh_smem(int n) {
   const size_t n4 = (static_cast<size_t>(n) + 3) & ~static_cast<size_t>(3);
-  return sizeof(float) * (n4 * kVhCols + 2 * kVhHeads * (n4 + 1));
+  return sizeof(float) * (n4 * kVhCols + 2 * kVhHeads * (n4 + 1) + kVhHeads * n4);
 }
 __global__ void __launch_bounds__(kVhThreads) win_values_mh_kernel(const WinAttnArgs a) {
-  extern __shared__ __align__(16) float msm[];  // kv [n4][kVhCols] | ws [kVhHeads][n4 + 1] | ex
+  // kv [n4][kVhCols] | sc [kVhHeads][n4] | ws [kVhHeads][n4 + 1] | ex [kVhHeads][n4 + 1]
+  extern __shared__ __align__(16) float msm[];
   __shared__ float mxs[kVhHeads];
   pdl_wait();
   pdl_trigger();
   const int n = a.n, d = a.d, n4 = (n + 3) & ~3, ns = n4 + 1;
   const int h0 = blockIdx.x * kVhHeads, col0 = blockIdx.y * kVhCols;
+  const int nh = min(kVhHeads, a.H - h0);
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   float* kv = msm;
-  float* ws = kv + static_cast<size_t>(n4) * kVhCols;
+  float* sc = kv + static_cast<size_t>(n4) * kVhCols;
+  float* ws = sc + kVhHeads * n4;
   float* ex = ws + kVhHeads * ns;
   for (int e = tid; e < n * (kVhCols / 4); e += kVhThreads) {
     const int t = e / (kVhCols / 4), c4 = e - t * (kVhCols / 4);
     cp_async16(kv + t * kVhCols + 4 * c4, a.kvdec + static_cast<size_t>(t) * d + col0 + 4 * c4);
   }
-  for (int hh = warp; hh < kVhHeads; hh += kVhThreads / 32) {
-    const int h = h0 + hh;
-    if (h >= a.H) continue;
-    const float* sh = a.s + static_cast<size_t>(h) * n;
+  // the scores rows (n is a multiple of 4: every row starts 16-byte aligned)
+  for (int e = tid; e < nh * (n / 4); e += kVhThreads) {
+    const int hh = e / (n / 4), t4 = e - hh * (n / 4);
+    cp_async16(sc + hh * n4 + 4 * t4, a.s + static_cast<size_t>(h0 + hh) * n + 4 * t4);
+  }
+  cp_async_wait_all();
+  __syncthreads();
+  for (int hh = warp; hh < nh; hh += kVhThreads / 32) {
+    const float* sh = sc + hh * n4;
     float mx = -INFINITY;
     for (int t = lane; t < n; t += 32) mx = fmaxf(mx, sh[t]);
 #pragma unroll
@@ -1341,7 +1350,6 @@ __global__ void __launch_bounds__(kVhThreads) win_values_mh_kernel(const WinAttn
     }
     if (lane == 0) mxs[hh] = mx;
   }
-  cp_async_wait_all();
   __syncthreads();
   const int hh = tid / (kVhCols / 2), p = tid - hh * (kVhCols / 2);
   const int h = h0 + hh;
@@ -1915,7 +1923,9 @@ __device__ __forceinline__ void idx_query_warp(const float* src, float* out, int
 // compressed rows x ih heads (thread = (row, head) dot), the CTA's keys in
 // shared memory beside the query, t < min(count, (pos+1)/4). id = 32 V with
 // V in {1, 2, 4, 8}.
-constexpr int kIdxT = 16;
+// 8 rows: 512-thread CTAs at 64 heads (a 1024-thread CTA, which needs an
+// SM's registers nearly to itself, was measured slower to start in the chain)
+constexpr int kIdxT = 8;
 __global__ void idx_score_kernel(const float* q, const float* keys, const float* wproj, int ih,
                                  int id, int rope_dim, const float* cosv, const float* sinv,
                                  const int* count, const int* pos, float* score) {
