@@ -1324,16 +1324,18 @@ __global__ void __launch_bounds__(kVhThreads) win_values_mh_kernel(const WinAttn
   float* sc = kv + static_cast<size_t>(n4) * kVhCols;
   float* ws = sc + kVhHeads * n4;
   float* ex = ws + kVhHeads * ns;
-  for (int e = tid; e < n * (kVhCols / 4); e += kVhThreads) {
-    const int t = e / (kVhCols / 4), c4 = e - t * (kVhCols / 4);
-    cp_async16(kv + t * kVhCols + 4 * c4, a.kvdec + static_cast<size_t>(t) * d + col0 + 4 * c4);
-  }
-  // the scores rows (n is a multiple of 4: every row starts 16-byte aligned)
+  // the scores rows first (n is a multiple of 4: every row starts 16-byte
+  // aligned), then the key slice: the softmax waits for the first group only
   for (int e = tid; e < nh * (n / 4); e += kVhThreads) {
     const int hh = e / (n / 4), t4 = e - hh * (n / 4);
     cp_async16(sc + hh * n4 + 4 * t4, a.s + static_cast<size_t>(h0 + hh) * n + 4 * t4);
   }
-  cp_async_wait_all();
+  asm volatile("cp.async.commit_group;" ::: "memory");
+  for (int e = tid; e < n * (kVhCols / 4); e += kVhThreads) {
+    const int t = e / (kVhCols / 4), c4 = e - t * (kVhCols / 4);
+    cp_async16(kv + t * kVhCols + 4 * c4, a.kvdec + static_cast<size_t>(t) * d + col0 + 4 * c4);
+  }
+  asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 1;" ::: "memory");
   __syncthreads();
   for (int hh = warp; hh < nh; hh += kVhThreads / 32) {
     const float* sh = sc + hh * n4;
@@ -1350,6 +1352,7 @@ __global__ void __launch_bounds__(kVhThreads) win_values_mh_kernel(const WinAttn
     }
     if (lane == 0) mxs[hh] = mx;
   }
+  asm volatile("cp.async.wait_group 0;" ::: "memory");
   __syncthreads();
   const int hh = tid / (kVhCols / 2), p = tid - hh * (kVhCols / 2);
   const int h = h0 + hh;
@@ -1952,8 +1955,14 @@ __global__ void idx_score_kernel(const float* q, const float* keys, const float*
   // wproj: the BF16 GEMV's fp32 sums; the reference rounds them to BF16
   // (round_out = 1) before the scale
   for (int k = tid; k < ih; k += nth) wh[k] = bf16_round(__fmul_rn(bf16_round(wproj[k]), s));
+  {
+    const int sh = __ffs(id) - 1;  // id is a power of two
+#pragma unroll 4
+    for (int i = tid; i < ih * id; i += nth) qs[(i >> sh) * ld + (i & (id - 1))] = q[i];
+  }
+  __syncthreads();
   for (int h = warp; h < ih; h += nw) {
-    const float* src = q + static_cast<size_t>(h) * id;
+    const float* src = qs + h * ld;
     float* dst = qs + h * ld;
     switch (id >> 5) {
       case 1: idx_query_warp<1>(src, dst, id, rope_dim, cosv, sinv, lane); break;
@@ -2806,6 +2815,11 @@ cudaError_t attention_comp(dsv4cuda_decoder* D, dsv4::Layer& L, cudaStream_t st)
   else
     DEC_CHECK(fp8_gemv(w.wq_b, w.wq_b_s, ql, H * d, D->xq, D->xs, D->ld, D->q, D->item1, D->n_one,
                        D->fp8_part, D->tile_cnt, st));
+  // the per-head RMS + RoPE of q needs only wq_b: it runs while the side
+  // stream's compressor projections finish
+  DEC_CHECK(dsv4::launch_pdl(dsv4::q_head_kernel, dim3(H), dim3(128), 0, st, D->q, d, c.rms_eps,
+                             half, static_cast<const float*>(D->cosv_c),
+                             static_cast<const float*>(D->sinv_c)));
   // compressor_update of the main compressor (its row into the cache)
   DEC_CHECK(cudaStreamWaitEvent(st, D->comp_join, 0));
   DEC_CHECK(comp_step(D, L, false, w.comp_ape, w.comp_norm, p_kv, p_sc, st));
@@ -2838,10 +2852,7 @@ cudaError_t attention_comp(dsv4cuda_decoder* D, dsv4::Layer& L, cudaStream_t st)
   // sparse_attn over the list with the inverse RoPE, in the reference's
   // order: the rows decoded, every (head, key) score, per head the softmax
   // and the key-order denominator, per (head, dimension pair) the key-order
-  // value chains
-  DEC_CHECK(dsv4::launch_pdl(dsv4::q_head_kernel, dim3(H), dim3(128), 0, st, D->q, d, c.rms_eps,
-                             half, static_cast<const float*>(D->cosv_c),
-                             static_cast<const float*>(D->sinv_c)));
+  // value chains (q's per-head RMS + RoPE ran before the side stream's join)
   dsv4::WinAttnArgs wa{};
   wa.q = D->q;
   wa.cache = L.cache;
