@@ -1722,7 +1722,8 @@ __device__ void fp4_quant_smem(float* x, int n) {
 // rounded to BF16, RMSNorm with the gain, RoPE of the compressed table at
 // the block's first position, then the FP8 QAT of the KV cache (the row goes
 // to cache row row0 + count) or, for the indexer (rotate), Hadamard + FP4
-// QAT (the row goes to out[count][d]). One CTA, any multiple of 32 threads.
+// QAT (the row goes to out[count][d]). One CTA per step (any multiple of 32
+// threads).
 struct CompStepArgs {
   const float* kv;        // [coff * d]
   const float* sc;        // [coff * d]
@@ -1744,11 +1745,17 @@ struct CompStepArgs {
   unsigned int* err;
 };
 
-__global__ void comp_step_kernel(const CompStepArgs a) {
+// CTA i runs step a[i]: a compress-ratio-4 layer's main compressor and its
+// indexer's compressor in one launch (independent state, rows and outputs).
+struct CompStepPair {
+  CompStepArgs a[2];
+};
+__global__ void comp_step_kernel(const __grid_constant__ CompStepPair p) {
   extern __shared__ float csm[];  // [d]
   __shared__ double red[32];
   pdl_trigger();
   pdl_wait();
+  const CompStepArgs& a = p.a[blockIdx.x];
   const int tid = threadIdx.x, nt = blockDim.x, lane = tid & 31, warp = tid >> 5;
   const int pos = *a.pos;
   const int cd = a.coff * a.d;
@@ -2724,8 +2731,8 @@ cudaError_t bf16_x(dsv4cuda_decoder* D, const uint16_t* W, int rows, int round_o
   return dsv4::launch_bf16_gemv(a, 1, st);
 }
 
-cudaError_t comp_step(dsv4cuda_decoder* D, dsv4::Layer& L, bool indexer, const float* ape,
-                      const uint16_t* norm, const float* kv, const float* sc, cudaStream_t st) {
+dsv4::CompStepArgs comp_args(dsv4cuda_decoder* D, dsv4::Layer& L, bool indexer, const float* ape,
+                             const uint16_t* norm, const float* kv, const float* sc) {
   const auto& c = D->cfg;
   dsv4::CompStepArgs a{};
   a.kv = kv;
@@ -2759,8 +2766,20 @@ cudaError_t comp_step(dsv4cuda_decoder* D, dsv4::Layer& L, bool indexer, const f
     a.cache = L.cache;
     a.row0 = L.comp_row0;
   }
-  const int threads = std::min(1024, std::max(32, (a.d + 31) / 32 * 32));
-  return dsv4::launch_pdl(dsv4::comp_step_kernel, dim3(1), dim3(threads), sizeof(float) * a.d, st, a);
+  return a;
+}
+
+// One launch of n (1 or 2) compressor steps, CTA i = step i; the block
+// fits the widest.
+cudaError_t comp_steps(const dsv4::CompStepArgs* a, int n, cudaStream_t st) {
+  dsv4::CompStepPair p{};
+  int d = 0;
+  for (int i = 0; i < n; ++i) {
+    p.a[i] = a[i];
+    d = std::max(d, a[i].d);
+  }
+  const int threads = std::min(1024, std::max(32, (d + 31) / 32 * 32));
+  return dsv4::launch_pdl(dsv4::comp_step_kernel, dim3(n), dim3(threads), sizeof(float) * d, st, p);
 }
 
 // attention_forward_impl for a compress-ratio-4 or -128 layer (src/dsv4/
@@ -2820,13 +2839,17 @@ cudaError_t attention_comp(dsv4cuda_decoder* D, dsv4::Layer& L, cudaStream_t st)
   DEC_CHECK(dsv4::launch_pdl(dsv4::q_head_kernel, dim3(H), dim3(128), 0, st, D->q, d, c.rms_eps,
                              half, static_cast<const float*>(D->cosv_c),
                              static_cast<const float*>(D->sinv_c)));
-  // compressor_update of the main compressor (its row into the cache)
   DEC_CHECK(cudaStreamWaitEvent(st, D->comp_join, 0));
-  DEC_CHECK(comp_step(D, L, false, w.comp_ape, w.comp_norm, p_kv, p_sc, st));
+  {
+    // the main compressor's step (its row into the cache) and, for ratio 4,
+    // the indexer's compressor step (its row into the indexer's keys)
+    dsv4::CompStepArgs ca[2] = {comp_args(D, L, false, w.comp_ape, w.comp_norm, p_kv, p_sc), {}};
+    if (L.ratio == 4) ca[1] = comp_args(D, L, true, w.idx_ape, w.idx_comp_norm, p_ikv, p_isc);
+    DEC_CHECK(comp_steps(ca, L.ratio == 4 ? 2 : 1, st));
+  }
   const int* win_idx = D->idx;
   if (L.ratio == 4) {
     const int ih = c.index_heads, id = c.index_dim;
-    DEC_CHECK(comp_step(D, L, true, w.idx_ape, w.idx_comp_norm, p_ikv, p_isc, st));
     DEC_CHECK(dsv4::launch_pdl(dsv4::idx_score_kernel,
                                dim3((L.max_count + dsv4::kIdxT - 1) / dsv4::kIdxT),
                                dim3(dsv4::kIdxT * ih), idx_score_smem(c), st,
