@@ -1747,15 +1747,33 @@ struct CompStepArgs {
 
 // CTA i runs step a[i]: a compress-ratio-4 layer's main compressor and its
 // indexer's compressor in one launch (independent state, rows and outputs).
+// With list set (a ratio-128 layer, one step), CTA 0 then writes the layer's
+// attention key list as comp_list_kernel does for ratio 128: the window's
+// list, every compressed row in order (row0 + i, i < the count after the
+// step), -1 padding to n_list.
 struct CompStepPair {
   CompStepArgs a[2];
+  const int* win_idx;
+  int win;
+  int* list;
+  int n_list;
 };
+__device__ void comp_step_body(const CompStepArgs& a, float* csm, double* red);
 __global__ void comp_step_kernel(const __grid_constant__ CompStepPair p) {
   extern __shared__ float csm[];  // [d]
   __shared__ double red[32];
   pdl_trigger();
   pdl_wait();
   const CompStepArgs& a = p.a[blockIdx.x];
+  comp_step_body(a, csm, red);
+  if (!p.list) return;
+  __syncthreads();  // the count the step wrote is visible to the CTA
+  const int k = *a.count;
+  for (int i = threadIdx.x; i < p.win; i += blockDim.x) p.list[i] = p.win_idx[i];
+  for (int i = threadIdx.x; i < p.n_list - p.win; i += blockDim.x)
+    p.list[p.win + i] = i < k ? static_cast<int>(a.row0 + i) : -1;
+}
+__device__ void comp_step_body(const CompStepArgs& a, float* csm, double* red) {
   const int tid = threadIdx.x, nt = blockDim.x, lane = tid & 31, warp = tid >> 5;
   const int pos = *a.pos;
   const int cd = a.coff * a.d;
@@ -2770,9 +2788,15 @@ dsv4::CompStepArgs comp_args(dsv4cuda_decoder* D, dsv4::Layer& L, bool indexer, 
 }
 
 // One launch of n (1 or 2) compressor steps, CTA i = step i; the block
-// fits the widest.
-cudaError_t comp_steps(const dsv4::CompStepArgs* a, int n, cudaStream_t st) {
+// fits the widest. With list: a ratio-128 layer's key list after its step.
+cudaError_t comp_steps(const dsv4::CompStepArgs* a, int n, cudaStream_t st,
+                       const int* win_idx = nullptr, int win = 0, int* list = nullptr,
+                       int n_list = 0) {
   dsv4::CompStepPair p{};
+  p.win_idx = win_idx;
+  p.win = win;
+  p.list = list;
+  p.n_list = n_list;
   int d = 0;
   for (int i = 0; i < n; ++i) {
     p.a[i] = a[i];
@@ -2844,8 +2868,12 @@ cudaError_t attention_comp(dsv4cuda_decoder* D, dsv4::Layer& L, cudaStream_t st)
     // the main compressor's step (its row into the cache) and, for ratio 4,
     // the indexer's compressor step (its row into the indexer's keys)
     dsv4::CompStepArgs ca[2] = {comp_args(D, L, false, w.comp_ape, w.comp_norm, p_kv, p_sc), {}};
-    if (L.ratio == 4) ca[1] = comp_args(D, L, true, w.idx_ape, w.idx_comp_norm, p_ikv, p_isc);
-    DEC_CHECK(comp_steps(ca, L.ratio == 4 ? 2 : 1, st));
+    if (L.ratio == 4) {
+      ca[1] = comp_args(D, L, true, w.idx_ape, w.idx_comp_norm, p_ikv, p_isc);
+      DEC_CHECK(comp_steps(ca, 2, st));
+    } else {  // ratio 128: every compressed row is a key; the list in the same launch
+      DEC_CHECK(comp_steps(ca, 1, st, D->idx, c.window, D->idx_full, L.n_keys));
+    }
   }
   const int* win_idx = D->idx;
   if (L.ratio == 4) {
@@ -2865,12 +2893,6 @@ cudaError_t attention_comp(dsv4cuda_decoder* D, dsv4::Layer& L, cudaStream_t st)
                                static_cast<const int*>(L.idx_count),
                                static_cast<const int*>(D->d_pos), 4, c.index_topk, L.comp_row0,
                                D->idx_n2, L.n_keys, D->idx_full));
-  } else {
-    DEC_CHECK(dsv4::launch_pdl(dsv4::comp_list_kernel, dim3(1), dim3(dsv4::kListThreads), 0, st, win_idx,
-                               c.window, static_cast<const float*>(nullptr),
-                               static_cast<const int*>(L.count),
-                               static_cast<const int*>(D->d_pos), L.ratio, 0, L.comp_row0, 0,
-                               L.n_keys, D->idx_full));
   }
   // sparse_attn over the list with the inverse RoPE, in the reference's
   // order: the rows decoded, every (head, key) score, per head the softmax
