@@ -342,7 +342,7 @@ def run_reference_arm(args, rank, world):
             print(json.dumps({"impl": "reference", "unavailable":
                               "oracle/_ref/ref_decode_bench was not built (reference sources absent)"}))
             return
-        tps, cores, sample = res
+        tps, cores, sample, _ = res
         print(json.dumps({
             "impl": "reference", "metric": DECODE_METRIC, "value": tps, "unit": "tok/s",
             "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
@@ -1121,38 +1121,54 @@ def make_decode_set(torch, seed, dev, c, expert_range=None, ratio=0):
                 wo_b=wo_b, wo_b_s=wo_b_s, moe=moe)
 
 
-def cpu_reference_decode(n_layers=43, threads=None, warm=8, timed=8, kinds_mode="dsv4"):
+def cpu_reference_decode(n_layers=43, threads=None, warm=8, timed=8, kinds_mode="dsv4",
+                         one_thread=None):
     """Per kind of layer in the model (compress ratio 0 / 4 / 128), the
     reference's decode of a one-layer checkpoint of that kind
     (cpu_reference_decode_one); per token = sum over the model's layers of
     their kind's layer time + the vocab head and the embedding. Returns
-    (tok/s, threads, sample description) or None."""
+    (tok/s, threads, sample description, one-thread line or None) or None.
+    one_thread = (warm, timed) also times every kind on one thread."""
     ratios = c5_ratios(n_layers) if kinds_mode == "dsv4" else [0] * n_layers
     per_kind, head_emb, samples, cores = {}, None, [], None
+    per_kind1, head_emb1, samples1 = {}, None, []
     for r in sorted(set(ratios)):
-        res = cpu_reference_decode_one(threads, warm, timed, ratio=r)
+        res = cpu_reference_decode_one(threads, warm, timed, ratio=r, one_thread=one_thread)
         if res is None:
             return None
-        layer, he, cores, sample = res
+        layer, he, cores, one = res
         per_kind[r] = layer
         head_emb = he
         samples.append(f"ratio {r}: {layer * 1e3:.1f} ms per layer")
+        if one:
+            per_kind1[r], head_emb1 = one
+            samples1.append(f"ratio {r}: {one[0] * 1e3:.1f} ms per layer")
     per_token = sum(per_kind[r] for r in ratios) + head_emb
+    line1 = None
+    if one_thread:
+        pt1 = sum(per_kind1[r] for r in ratios) + head_emb1
+        line1 = {"value": 1.0 / pt1, "unit": "tok/s", "cores": 1,
+                 "sample": (f"the same checkpoints, {one_thread[1]} timed tokens after "
+                            f"{one_thread[0]} warm-up, 1 thread: {'; '.join(samples1)}; "
+                            f"{head_emb1 * 1e3:.1f} ms head + embedding; per token "
+                            f"extrapolated ({pt1:.2f} s)")}
     return 1.0 / per_token, cores, (
         f"dsv4_forward_token on one-layer config-5 random checkpoints in RAM (one per kind of "
         f"layer), {timed} timed tokens after {warm} warm-up from position 0, {cores} thread(s): "
         f"{'; '.join(samples)}; {head_emb * 1e3:.1f} ms head + embedding; per token extrapolated "
-        f"to the {n_layers}-layer pattern ({per_token:.2f} s)")
+        f"to the {n_layers}-layer pattern ({per_token:.2f} s)"), line1
 
 
-def cpu_reference_decode_one(threads=None, warm=8, timed=8, ratio=0):
+def cpu_reference_decode_one(threads=None, warm=8, timed=8, ratio=0, one_thread=None):
     """The reference engine's own decode step on the host cores
     (oracle/_ref/ref_decode_bench: dsv4_forward_token over a config-5-shaped
     random checkpoint of ONE layer of compress ratio `ratio`, written to
     RAM; a 43-layer checkpoint, ~156 GB, does not fit the host). Returns
     (seconds per layer, seconds of head + embedding per token, threads,
-    None) - the head and the embedding split off with the engine's own
-    profile counters - or None when the reference was not built here."""
+    one) - the head and the embedding split off with the engine's own
+    profile counters; one = the same pair on one thread when one_thread =
+    (warm, timed) is given, on the same checkpoint, else None - or None when
+    the reference was not built here."""
     import shutil
     import tempfile
     exe = os.path.join(ROOT, "oracle", "_ref", "ref_decode_bench")
@@ -1165,14 +1181,20 @@ def cpu_reference_decode_one(threads=None, warm=8, timed=8, ratio=0):
     d = tempfile.mkdtemp(prefix="dsv4_c5_", dir=base)
     try:
         random_checkpoint.write(d, 1, c=dict(random_checkpoint.CONFIG5, ratios=[ratio]))
-        r = subprocess.run([exe, d, str(warm), str(timed), str(threads)], capture_output=True,
-                           text=True, timeout=1800)
-        line = [ln for ln in r.stdout.splitlines() if ln.startswith("RESULT")]
-        if r.returncode != 0 or not line:
-            raise RuntimeError(r.stderr[-500:])
-        f = line[-1].split()
-        tok, total, head, emb = int(f[4]), float(f[6]), float(f[8]), float(f[10])
-        return (total - head - emb) / tok, (head + emb) / tok, threads, None
+
+        def run(w, t, th):
+            r = subprocess.run([exe, d, str(w), str(t), str(th)], capture_output=True,
+                               text=True, timeout=1800)
+            line = [ln for ln in r.stdout.splitlines() if ln.startswith("RESULT")]
+            if r.returncode != 0 or not line:
+                raise RuntimeError(r.stderr[-500:])
+            f = line[-1].split()
+            tok, total, head, emb = int(f[4]), float(f[6]), float(f[8]), float(f[10])
+            return (total - head - emb) / tok, (head + emb) / tok
+
+        layer, he = run(warm, timed, threads)
+        one = run(one_thread[0], one_thread[1], 1) if one_thread else None
+        return layer, he, threads, one
     finally:
         shutil.rmtree(d, ignore_errors=True)
 
@@ -1523,10 +1545,11 @@ def main_decode(args, rank, world, local):
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
         try:
-            res = cpu_reference_decode(n_layers, kinds_mode=args.decode_ratios)
+            res = cpu_reference_decode(n_layers, kinds_mode=args.decode_ratios,
+                                       one_thread=(2, 4))
             if res:
                 cpu = {"value": res[0], "unit": "tok/s", "cores": res[1], "kind": "reference",
-                       "sample": res[2], "extrapolated": True}
+                       "sample": res[2], "extrapolated": True, "one_thread": res[3]}
         except Exception as exc:  # report, do not hide
             cpu = {"value": None, "unit": "tok/s", "cores": 0, "kind": "reference",
                    "sample": f"failed: {exc}"}
