@@ -1748,9 +1748,9 @@ struct CompStepArgs {
 // CTA i runs step a[i]: a compress-ratio-4 layer's main compressor and its
 // indexer's compressor in one launch (independent state, rows and outputs).
 // With list set (a ratio-128 layer, one step), CTA 0 then writes the layer's
-// attention key list as comp_list_kernel does for ratio 128: the window's
-// list, every compressed row in order (row0 + i, i < the count after the
-// step), -1 padding to n_list.
+// attention key list: the window's list, every compressed row in order
+// (row0 + i, i < the count after the step; src/dsv4/dsv4_model.c:5330-5336),
+// -1 padding to n_list.
 struct CompStepPair {
   CompStepArgs a[2];
   const int* win_idx;
@@ -2017,18 +2017,19 @@ __global__ void idx_score_kernel(const float* q, const float* keys, const float*
   }
 }
 
-// The attention key list of a compressed layer: the window's list (as the
-// window-only layers use it, -1 padded), then the compressed rows - the
-// indexer's top-k for ratio 4 (dsv4_indexer_select_topk, :5636-5679: score
-// descending, lower index first, k = min(index_topk, n)) or every compressed
-// row in order for ratio 128 (:5330-5336) - then -1 padding to n_max. Rows
-// are row0 + compressed index. One CTA of kListThreads; the ratio-4
-// selection sorts the n scores with a bitonic network over the next power of
-// two >= n: while that fits the CTA, one key per thread in registers
-// (partners within a warp by shuffle, farther ones through a double-buffered
-// shared array, one barrier per stage); beyond it, in shared memory over n2
-// (a power of two >= the most compressed rows). The order is a strict total
-// order on the keys (indices are distinct), so both forms give the order.
+// The attention key list of a compress-ratio-4 layer: the window's list (as
+// the window-only layers use it, -1 padded), then the indexer's top-k of the
+// compressed rows (dsv4_indexer_select_topk, :5636-5679: score descending,
+// lower index first, k = min(index_topk, n)), then -1 padding to n_max. Rows
+// are row0 + compressed index. (A ratio-128 layer lists every compressed row
+// in order, :5330-5336, written by its compressor-step launch.) One CTA of
+// kListThreads; the selection sorts the n scores with a bitonic network
+// over the next power of two >= n: while that fits the CTA, one key per
+// thread in registers (partners within a warp by shuffle, farther ones
+// through a double-buffered shared array, one barrier per stage); beyond
+// it, in shared memory over n2 (a power of two >= the most compressed rows).
+// The order is a strict total order on the keys (indices are distinct), so
+// both forms give the order.
 constexpr int kListThreads = 1024;
 size_t comp_list_smem(int n2) {
   return sizeof(float) * std::max(2 * n2, 4 * kListThreads);
@@ -2043,21 +2044,16 @@ __device__ __forceinline__ bool topk_before(float sa, int ia, float sb, int ib) 
 }
 __global__ void __launch_bounds__(kListThreads)
 comp_list_kernel(const int* win_idx, int win, const float* score, const int* count, const int* pos,
-                 int ratio, int topk, long long row0, int n2, int n_max, int* out) {
+                 int topk, long long row0, int n2, int n_max, int* out) {
   extern __shared__ unsigned char lsm[];
   pdl_trigger();
   pdl_wait();
   const int tid = threadIdx.x, nt = blockDim.x;
   for (int i = tid; i < win; i += nt) out[i] = win_idx[i];
   int n = *count;
-  int k = n;
-  if (ratio != 4) {
-    for (int i = tid; i < n_max - win; i += nt) out[win + i] = i < k ? static_cast<int>(row0 + i) : -1;
-    return;
-  }
   const int maxc = (*pos + 1) / 4;
   if (n > maxc) n = maxc;
-  k = topk < n ? topk : n;
+  const int k = topk < n ? topk : n;
   int m2 = 32;
   while (m2 < n) m2 <<= 1;
   if (m2 <= nt) {
@@ -2891,7 +2887,7 @@ cudaError_t attention_comp(dsv4cuda_decoder* D, dsv4::Layer& L, cudaStream_t st)
                                dsv4::comp_list_smem(D->idx_n2), st, win_idx, c.window,
                                static_cast<const float*>(D->idx_score),
                                static_cast<const int*>(L.idx_count),
-                               static_cast<const int*>(D->d_pos), 4, c.index_topk, L.comp_row0,
+                               static_cast<const int*>(D->d_pos), c.index_topk, L.comp_row0,
                                D->idx_n2, L.n_keys, D->idx_full));
   }
   // sparse_attn over the list with the inverse RoPE, in the reference's
